@@ -1,0 +1,83 @@
+"""Variable-length (packed) non-causal attention.
+
+Replaces the reference's FlashAttention-4 wrappers (pan/utils/flash_attention.py:18-243): the packed
+training path attends within each ``cu_seqlens`` segment, returns the output and the per-row
+log-sum-exp, and its backward gives ``dq, dk, dv``.  ``q, k, v`` are ``[L, H, D]`` bf16; the output
+is ``[L, H, D]``.  Rows beyond the last boundary are padding: their output is zero and they
+contribute nothing.
+
+CUDA tensors run the tcgen05 kernels of ``csrc/attention_sm100.cu``; CPU tensors run PyTorch's
+math attention per segment.
+"""
+from __future__ import annotations
+
+import math
+from typing import Optional, Sequence
+
+import torch
+import torch.nn.functional as F
+
+from ._ext import ext
+
+
+class _VarlenAttnCUDA(torch.autograd.Function):
+    @staticmethod
+    def forward(ctx, q, k, v, cu_seqlens, max_seqlen, scale):
+        o, lse = ext().attn_fwd(q, k, v, cu_seqlens, max_seqlen, scale)
+        ctx.save_for_backward(q, k, v, o, lse, cu_seqlens)
+        ctx.max_seqlen, ctx.scale = max_seqlen, scale
+        return o
+
+    @staticmethod
+    def backward(ctx, do):
+        q, k, v, o, lse, cu = ctx.saved_tensors
+        dq, dk, dv = ext().attn_bwd(do.contiguous(), q, k, v, o, lse, cu, ctx.max_seqlen, ctx.scale)
+        return dq, dk, dv, None, None, None
+
+
+def varlen_attention(q: torch.Tensor, k: torch.Tensor, v: torch.Tensor, cu_seqlens: torch.Tensor,
+                     lens: Sequence[int], max_seqlen: Optional[int] = None,
+                     scale: Optional[float] = None) -> torch.Tensor:
+    """Attention within each segment of ``cu_seqlens``; ``lens`` are the host segment lengths."""
+    D = q.shape[-1]
+    scale = 1.0 / math.sqrt(D) if scale is None else scale
+    max_seqlen = int(max(lens)) if max_seqlen is None else int(max_seqlen)
+    if q.is_cuda:
+        return _VarlenAttnCUDA.apply(q.contiguous(), k.contiguous(), v.contiguous(),
+                                     cu_seqlens.to(torch.int32), max_seqlen, float(scale))
+    out = torch.zeros_like(q)
+    pieces = []
+    start = 0
+    for n in lens:
+        n = int(n)
+        if n == 0:
+            continue
+        qs, ks, vs = (t[start:start + n].transpose(0, 1).unsqueeze(0) for t in (q, k, v))
+        o = F.scaled_dot_product_attention(qs.float(), ks.float(), vs.float(), scale=scale)
+        pieces.append((start, n, o[0].transpose(0, 1).to(q.dtype)))
+        start += n
+    if not pieces:
+        return out
+    rows = [p[2] for p in pieces]
+    tail = q.shape[0] - start
+    if tail:
+        rows.append(q.new_zeros(tail, *q.shape[1:]))
+    return torch.cat(rows, 0)
+
+
+def dense_attention(q: torch.Tensor, k: torch.Tensor, v: torch.Tensor,
+                    mask: Optional[torch.Tensor] = None) -> torch.Tensor:
+    """Self-attention over ``[B, S, H, D]`` where ``mask`` (``[B, S]``, True = valid) gates both
+    queries and keys; masked query rows return zeros (reference attention.py:27-53)."""
+    B, S, H, D = q.shape
+    if mask is None:
+        mask = torch.ones(B, S, dtype=torch.bool, device=q.device)
+    mask = mask.to(device=q.device, dtype=torch.bool)
+    idx = torch.nonzero(mask.flatten(), as_tuple=False).flatten()
+    lens = mask.sum(-1).tolist()
+    cu = torch.tensor([0] + torch.tensor(lens).cumsum(0).tolist(), dtype=torch.int32, device=q.device)
+    qf, kf, vf = (t.reshape(B * S, H, D).index_select(0, idx) for t in (q, k, v))
+    o = varlen_attention(qf, kf, vf, cu, lens)
+    out = q.new_zeros(B * S, H, D)
+    out.index_copy_(0, idx, o[: idx.numel()])
+    return out.view(B, S, H, D)
