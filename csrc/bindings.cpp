@@ -1,0 +1,356 @@
+// Python bindings of the sm_100a kernels: tensor validation, output allocation and stream
+// selection.  This is the only translation unit that includes torch headers.
+#include <torch/extension.h>
+#include <ATen/cuda/CUDAContext.h>
+#include <c10/cuda/CUDAGuard.h>
+
+#include "launchers.h"
+
+namespace pan {
+
+const char* launch_qkv_post_fwd(const void* raw, const float* qw, const float* kw, const float* cos_t,
+                                const float* sin_t, const int* itc, int nv, int na, int L, int H, int D, float eps,
+                                void* q, void* k, void* v, cudaStream_t s);
+const char* launch_qkv_post_bwd(const void* dq, const void* dk, const void* dv, const void* raw, const float* qw,
+                                const float* kw, const float* cos_t, const float* sin_t, const int* itc, int nv,
+                                int na, int L, int H, int D, float eps, void* draw, float* dqw, float* dkw,
+                                cudaStream_t s);
+
+namespace {
+
+cudaStream_t stream() { return at::cuda::getCurrentCUDAStream(); }
+
+void check_launch(const char* err, const char* what) {
+  TORCH_CHECK(err == nullptr, what, ": ", err ? err : "");
+  cudaError_t e = cudaGetLastError();
+  TORCH_CHECK(e == cudaSuccess, what, ": ", cudaGetErrorString(e));
+}
+
+void check_rows(const torch::Tensor& t, const char* name) {
+  TORCH_CHECK(t.is_cuda() && t.scalar_type() == torch::kBFloat16 && t.dim() == 2 && t.is_contiguous(), name,
+              " must be a contiguous bf16 CUDA [L, C] tensor");
+  TORCH_CHECK(t.size(1) % 256 == 0, name, ": C must be a multiple of 256");
+}
+
+void check_bf16(const torch::Tensor& t, const char* name) {
+  TORCH_CHECK(t.is_cuda() && t.scalar_type() == torch::kBFloat16 && t.is_contiguous(), name,
+              " must be a contiguous bf16 CUDA tensor");
+}
+
+void check_i32(const torch::Tensor& t, const char* name) {
+  TORCH_CHECK(t.is_cuda() && t.scalar_type() == torch::kInt32 && t.is_contiguous(), name,
+              " must be a contiguous int32 CUDA tensor");
+}
+
+}  // namespace
+
+// ------------------------------------------------------------------ packed elementwise ops
+torch::Tensor ln_modulate_fwd(torch::Tensor x, torch::Tensor stats, torch::Tensor shift, torch::Tensor scale,
+                              torch::Tensor bounds, int64_t n_seg) {
+  const at::cuda::CUDAGuard guard(x.device());
+  check_rows(x, "x");
+  check_bf16(shift, "shift");
+  check_bf16(scale, "scale");
+  check_i32(bounds, "bounds");
+  TORCH_CHECK(stats.scalar_type() == torch::kFloat32 && stats.is_contiguous(), "stats must be fp32 [L, 2]");
+  TORCH_CHECK(n_seg <= 64 && shift.size(0) >= n_seg && scale.size(0) >= n_seg, "bad segment count");
+  auto y = torch::empty_like(x);
+  launch_ln_modulate_fwd(x.data_ptr(), stats.data_ptr<float>(), shift.data_ptr(), scale.data_ptr(),
+                         bounds.data_ptr<int>(), n_seg, x.size(0), x.size(1), y.data_ptr(), stream());
+  check_launch(nullptr, "ln_modulate_fwd");
+  return y;
+}
+
+std::vector<torch::Tensor> ln_modulate_bwd(torch::Tensor g, torch::Tensor x, torch::Tensor stats, torch::Tensor scale,
+                                           torch::Tensor bounds, int64_t n_seg) {
+  const at::cuda::CUDAGuard guard(x.device());
+  check_rows(g, "grad");
+  check_rows(x, "x");
+  check_bf16(scale, "scale");
+  auto dx = torch::empty_like(x);
+  auto opts = x.options().dtype(torch::kFloat32);
+  auto dshift = torch::zeros({scale.size(0), x.size(1)}, opts);
+  auto dscale = torch::zeros({scale.size(0), x.size(1)}, opts);
+  launch_ln_modulate_bwd(g.data_ptr(), x.data_ptr(), stats.data_ptr<float>(), scale.data_ptr(), bounds.data_ptr<int>(),
+                         n_seg, x.size(0), x.size(1), dx.data_ptr(), dshift.data_ptr<float>(),
+                         dscale.data_ptr<float>(), stream());
+  check_launch(nullptr, "ln_modulate_bwd");
+  return {dx, dshift, dscale};
+}
+
+std::vector<torch::Tensor> gate_residual_fwd(torch::Tensor y, torch::Tensor gate, torch::Tensor res,
+                                             torch::Tensor bounds, int64_t n_seg) {
+  const at::cuda::CUDAGuard guard(y.device());
+  check_rows(y, "y");
+  check_rows(res, "residual");
+  check_bf16(gate, "gate");
+  auto out = torch::empty_like(res);
+  auto stats = torch::empty({y.size(0), 2}, y.options().dtype(torch::kFloat32));
+  launch_gate_residual_fwd(y.data_ptr(), gate.data_ptr(), res.data_ptr(), bounds.data_ptr<int>(), n_seg, y.size(0),
+                           y.size(1), out.data_ptr(), stats.data_ptr<float>(), stream());
+  check_launch(nullptr, "gate_residual_fwd");
+  return {out, stats};
+}
+
+std::vector<torch::Tensor> gate_bwd(torch::Tensor g, torch::Tensor y, torch::Tensor gate, torch::Tensor bounds,
+                                    int64_t n_seg) {
+  const at::cuda::CUDAGuard guard(g.device());
+  check_rows(g, "grad");
+  check_rows(y, "y");
+  auto dy = torch::empty_like(g);
+  auto dgate = torch::zeros({gate.size(0), g.size(1)}, g.options().dtype(torch::kFloat32));
+  launch_gate_bwd(g.data_ptr(), y.data_ptr(), gate.data_ptr(), bounds.data_ptr<int>(), n_seg, g.size(0), g.size(1),
+                  dy.data_ptr(), dgate.data_ptr<float>(), stream());
+  check_launch(nullptr, "gate_bwd");
+  return {dy, dgate};
+}
+
+std::vector<torch::Tensor> simple_concat_fwd(torch::Tensor vid, torch::Tensor txt, c10::optional<torch::Tensor> ttv,
+                                             int64_t total) {
+  const at::cuda::CUDAGuard guard(vid.device());
+  check_rows(vid, "video");
+  check_rows(txt, "text");
+  const int nv = vid.size(0), nt = txt.size(0);
+  TORCH_CHECK(total >= nv + nt, "total rows smaller than video + text");
+  auto out = torch::empty({total, vid.size(1)}, vid.options());
+  auto stats = torch::empty({total, 2}, vid.options().dtype(torch::kFloat32));
+  const void* tp = ttv.has_value() ? ttv.value().data_ptr() : nullptr;
+  launch_concat_fwd(vid.data_ptr(), txt.data_ptr(), tp, nv, nt, total, vid.size(1), out.data_ptr(),
+                    stats.data_ptr<float>(), stream());
+  check_launch(nullptr, "simple_concat_fwd");
+  return {out, stats};
+}
+
+torch::Tensor segment_sum(torch::Tensor x, torch::Tensor bounds, int64_t n_seg) {
+  const at::cuda::CUDAGuard guard(x.device());
+  check_rows(x, "x");
+  check_i32(bounds, "bounds");
+  auto out = torch::zeros({n_seg, x.size(1)}, x.options().dtype(torch::kFloat32));
+  launch_segment_sum(x.data_ptr(), bounds.data_ptr<int>(), n_seg, x.size(0), x.size(1), out.data_ptr<float>(),
+                     stream());
+  check_launch(nullptr, "segment_sum");
+  return out;
+}
+
+torch::Tensor column_sum(torch::Tensor x) {
+  auto b = torch::tensor({0, (int)x.size(0)}, x.options().dtype(torch::kInt32));
+  return segment_sum(x, b, 1)[0];
+}
+
+torch::Tensor mse_fwd(torch::Tensor pred, torch::Tensor tgt, int64_t nv) {
+  const at::cuda::CUDAGuard guard(pred.device());
+  check_bf16(pred, "pred");
+  check_bf16(tgt, "target");
+  TORCH_CHECK(pred.size(1) == tgt.size(1) && tgt.size(0) >= nv && pred.size(0) >= nv, "shape mismatch");
+  const size_t n = (size_t)nv * pred.size(1);
+  TORCH_CHECK(n % 8 == 0, "element count must be a multiple of 8");
+  const int parts = 148 * 4;
+  auto partial = torch::empty({parts}, pred.options().dtype(torch::kFloat32));
+  auto out = torch::empty({2}, pred.options().dtype(torch::kFloat32));
+  launch_mse_fwd(pred.data_ptr(), tgt.data_ptr(), n, partial.data_ptr<float>(), parts, out.data_ptr<float>(),
+                 stream());
+  check_launch(nullptr, "mse_fwd");
+  return out;
+}
+
+torch::Tensor mse_bwd(torch::Tensor pred, torch::Tensor tgt, torch::Tensor gsum, int64_t nv) {
+  const at::cuda::CUDAGuard guard(pred.device());
+  auto dpred = torch::empty_like(pred);
+  launch_mse_bwd(pred.data_ptr(), tgt.data_ptr(), gsum.data_ptr<float>(), (size_t)nv * pred.size(1), pred.numel(),
+                 dpred.data_ptr(), stream());
+  check_launch(nullptr, "mse_bwd");
+  return dpred;
+}
+
+torch::Tensor gather_rows(torch::Tensor x, torch::Tensor idx) {
+  const at::cuda::CUDAGuard guard(x.device());
+  TORCH_CHECK(x.is_contiguous(), "gather_rows: x must be contiguous");
+  check_i32(idx, "idx");
+  const int rows = idx.size(0);
+  const int64_t row_bytes = x.numel() / x.size(0) * x.element_size();
+  TORCH_CHECK(row_bytes % 16 == 0, "row size must be a multiple of 16 bytes");
+  std::vector<int64_t> shape(x.sizes().begin(), x.sizes().end());
+  shape[0] = rows;
+  auto out = torch::empty(shape, x.options());
+  launch_gather_rows(x.data_ptr(), idx.data_ptr<int>(), rows, (int)(row_bytes / 16), out.data_ptr(), stream());
+  check_launch(nullptr, "gather_rows");
+  return out;
+}
+
+// ------------------------------------------------------------------ GEMM
+namespace {
+
+GemmArgs base_args(const torch::Tensor& A, bool a_kmajor, torch::Tensor& D) {
+
+  TORCH_CHECK(A.is_cuda() && A.scalar_type() == torch::kBFloat16 && A.dim() == 2 && A.stride(1) == 1,
+              "A must be a row-major bf16 CUDA matrix");
+  TORCH_CHECK(D.is_cuda() && D.dim() == 2 && D.stride(1) == 1 &&
+                  (D.scalar_type() == torch::kBFloat16 || D.scalar_type() == torch::kFloat32),
+              "D must be a row-major bf16/fp32 CUDA matrix");
+  GemmArgs a{};
+  a.A = A.data_ptr();
+  a.lda = A.stride(0);
+  a.a_mn = a_kmajor ? 0 : 1;
+  a.M = a_kmajor ? A.size(0) : A.size(1);
+  a.K = a_kmajor ? A.size(1) : A.size(0);
+  a.D = D.data_ptr();
+  a.ldd = D.stride(0);
+  a.d_fp32 = D.scalar_type() == torch::kFloat32;
+  return a;
+}
+
+void set_group(GemmArgs& a, int g, const torch::Tensor& B, bool b_kmajor, int row_begin, int row_end,
+               const c10::optional<torch::Tensor>& bias) {
+  TORCH_CHECK(B.is_cuda() && B.scalar_type() == torch::kBFloat16 && B.dim() == 2 && B.stride(1) == 1,
+              "B must be a row-major bf16 CUDA matrix");
+  GemmGroup& gr = a.groups[g];
+  gr.B = B.data_ptr();
+  gr.ldb = B.stride(0);
+  gr.n = b_kmajor ? B.size(0) : B.size(1);
+  gr.k = b_kmajor ? B.size(1) : B.size(0);
+  gr.row_begin = row_begin;
+  gr.row_end = row_end;
+  gr.bias = nullptr;
+  if (bias.has_value()) {
+    const auto& b = bias.value();
+    TORCH_CHECK(b.scalar_type() == torch::kBFloat16 && b.is_contiguous() && b.numel() >= gr.n, "bias must be bf16 [N]");
+    gr.bias = b.data_ptr();
+  }
+}
+
+}  // namespace
+
+void gemm(torch::Tensor A, torch::Tensor B, torch::Tensor D, bool a_kmajor, bool b_kmajor,
+          c10::optional<torch::Tensor> bias, c10::optional<torch::Tensor> gelu_pre, bool accumulate) {
+  const at::cuda::CUDAGuard guard(A.device());
+  GemmArgs a = base_args(A, a_kmajor, D);
+  a.b_mn = b_kmajor ? 0 : 1;
+  a.n_groups = 1;
+  set_group(a, 0, B, b_kmajor, 0, a.M, bias);
+  TORCH_CHECK(a.groups[0].k == a.K, "K mismatch");
+  TORCH_CHECK(D.size(0) >= a.M && D.size(1) >= a.groups[0].n, "D too small");
+  if (gelu_pre.has_value()) {
+    const auto& p = gelu_pre.value();
+    TORCH_CHECK(p.scalar_type() == torch::kBFloat16 && p.stride(1) == 1, "gelu_pre must be bf16 row-major");
+    a.epi = 1;
+    a.aux = p.data_ptr();
+    a.ldaux = p.stride(0);
+  }
+  a.accumulate = accumulate ? 1 : 0;
+  check_launch(launch_gemm(a, stream()), "gemm");
+}
+
+void gemm_grouped_nt(torch::Tensor A, std::vector<torch::Tensor> Bs, torch::Tensor D,
+                     std::vector<c10::optional<torch::Tensor>> biases, c10::optional<torch::Tensor> gelu_pre,
+                     std::vector<int64_t> bounds) {
+  const at::cuda::CUDAGuard guard(A.device());
+  TORCH_CHECK(bounds.size() == Bs.size() + 1, "bounds must have one more entry than weights");
+  GemmArgs a = base_args(A, true, D);
+  a.b_mn = 0;
+  int G = 0;
+  int prev_end = -1;
+  for (size_t g = 0; g + 1 < bounds.size(); ++g) {
+    if (bounds[g + 1] <= bounds[g]) continue;
+    TORCH_CHECK(G < kGemmMaxGroups, "at most 4 groups");
+    TORCH_CHECK(prev_end < 0 || prev_end == bounds[g], "row groups must be contiguous");
+    TORCH_CHECK(bounds[g + 1] <= a.M, "row bounds beyond A");
+    set_group(a, G, Bs[g], true, bounds[g], bounds[g + 1], g < biases.size() ? biases[g] : c10::nullopt);
+    TORCH_CHECK(D.size(1) >= a.groups[G].n, "D too narrow");
+    prev_end = bounds[g + 1];
+    ++G;
+  }
+  if (G == 0) return;
+  a.n_groups = G;
+  if (gelu_pre.has_value()) {
+    const auto& p = gelu_pre.value();
+    TORCH_CHECK(p.scalar_type() == torch::kBFloat16 && p.stride(1) == 1, "gelu_pre must be bf16 row-major");
+    a.epi = 1;
+    a.aux = p.data_ptr();
+    a.ldaux = p.stride(0);
+  }
+  check_launch(launch_gemm(a, stream()), "gemm_grouped_nt");
+}
+
+void gemm_dgelu(torch::Tensor dY, torch::Tensor Wd, torch::Tensor pre, torch::Tensor dpre, torch::Tensor post) {
+  const at::cuda::CUDAGuard guard(dY.device());
+  GemmArgs a = base_args(dY, true, dpre);
+  a.b_mn = 1;
+  a.n_groups = 1;
+  set_group(a, 0, Wd, false, 0, a.M, c10::nullopt);
+  TORCH_CHECK(a.groups[0].k == a.K, "K mismatch");
+  TORCH_CHECK(pre.scalar_type() == torch::kBFloat16 && pre.stride(1) == 1 && post.stride(1) == 1, "bad pre/post");
+  a.epi = 2;
+  a.aux = pre.data_ptr();
+  a.ldaux = pre.stride(0);
+  a.aux2 = post.data_ptr();
+  a.ldaux2 = post.stride(0);
+  check_launch(launch_gemm(a, stream()), "gemm_dgelu");
+}
+
+// ------------------------------------------------------------------ QKV post-processing
+std::vector<torch::Tensor> qkv_post_fwd(torch::Tensor raw, torch::Tensor qw, torch::Tensor kw, torch::Tensor cos_t,
+                                        torch::Tensor sin_t, torch::Tensor itc, int64_t nv, int64_t na, int64_t heads,
+                                        double eps) {
+  const at::cuda::CUDAGuard guard(raw.device());
+  check_bf16(raw, "raw");
+  check_i32(itc, "interleave_to_concat");
+  const int L = raw.size(0);
+  const int HD = raw.size(1) / 3;
+  const int D = HD / heads;
+  TORCH_CHECK(cos_t.scalar_type() == torch::kFloat32 && cos_t.is_contiguous() && cos_t.size(0) >= L &&
+                  cos_t.size(1) == D,
+              "cos must be fp32 [L, D]");
+  auto q = torch::empty({L, heads, D}, raw.options());
+  auto k = torch::empty({L, heads, D}, raw.options());
+  auto v = torch::empty({L, heads, D}, raw.options());
+  check_launch(launch_qkv_post_fwd(raw.data_ptr(), qw.data_ptr<float>(), kw.data_ptr<float>(), cos_t.data_ptr<float>(),
+                                   sin_t.data_ptr<float>(), itc.data_ptr<int>(), nv, na, L, heads, D, (float)eps,
+                                   q.data_ptr(), k.data_ptr(), v.data_ptr(), stream()),
+               "qkv_post_fwd");
+  return {q, k, v};
+}
+
+std::vector<torch::Tensor> qkv_post_bwd(torch::Tensor dq, torch::Tensor dk, torch::Tensor dv, torch::Tensor raw,
+                                        torch::Tensor qw, torch::Tensor kw, torch::Tensor cos_t, torch::Tensor sin_t,
+                                        torch::Tensor itc, int64_t nv, int64_t na, int64_t heads, double eps) {
+  const at::cuda::CUDAGuard guard(raw.device());
+  check_bf16(dq, "dq");
+  check_bf16(dk, "dk");
+  check_bf16(dv, "dv");
+  const int L = raw.size(0);
+  const int HD = raw.size(1) / 3;
+  const int D = HD / heads;
+  auto draw = torch::empty_like(raw);
+  auto dqw = torch::zeros({2 * D}, raw.options().dtype(torch::kFloat32));
+  auto dkw = torch::zeros({2 * D}, raw.options().dtype(torch::kFloat32));
+  check_launch(launch_qkv_post_bwd(dq.data_ptr(), dk.data_ptr(), dv.data_ptr(), raw.data_ptr(), qw.data_ptr<float>(),
+                                   kw.data_ptr<float>(), cos_t.data_ptr<float>(), sin_t.data_ptr<float>(),
+                                   itc.data_ptr<int>(), nv, na, L, heads, D, (float)eps, draw.data_ptr(),
+                                   dqw.data_ptr<float>(), dkw.data_ptr<float>(), stream()),
+               "qkv_post_bwd");
+  return {draw, dqw, dkw};
+}
+
+int error_flag(bool reset) { return gemm_error_flag(reset) | packed_ops_error_flag(reset); }
+
+}  // namespace pan
+
+PYBIND11_MODULE(TORCH_EXTENSION_NAME, m) {
+  m.doc() = "pan2_b200 sm_100a kernels";
+  m.def("ln_modulate_fwd", &pan::ln_modulate_fwd);
+  m.def("ln_modulate_bwd", &pan::ln_modulate_bwd);
+  m.def("gate_residual_fwd", &pan::gate_residual_fwd);
+  m.def("gate_bwd", &pan::gate_bwd);
+  m.def("simple_concat_fwd", &pan::simple_concat_fwd);
+  m.def("segment_sum", &pan::segment_sum);
+  m.def("column_sum", &pan::column_sum);
+  m.def("mse_fwd", &pan::mse_fwd);
+  m.def("mse_bwd", &pan::mse_bwd);
+  m.def("gather_rows", &pan::gather_rows);
+  m.def("gemm", &pan::gemm);
+  m.def("gemm_grouped_nt", &pan::gemm_grouped_nt);
+  m.def("gemm_dgelu", &pan::gemm_dgelu);
+  m.def("qkv_post_fwd", &pan::qkv_post_fwd);
+  m.def("qkv_post_bwd", &pan::qkv_post_bwd);
+  m.def("error_flag", &pan::error_flag, py::arg("reset") = true);
+}

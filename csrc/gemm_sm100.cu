@@ -1,0 +1,406 @@
+// Persistent warp-specialised bf16 GEMM for sm_100a (tcgen05 + TMEM + TMA).
+//
+//   D[M, N] (+)= A[M, K] * B[N, K]^T      fp32 accumulation in tensor memory
+//
+// A and B are each K-major (row-major, K contiguous) or MN-major (their M/N index contiguous),
+// which covers Y = X W^T (K/K), dX = dY W (K/MN) and dW = dY^T X (MN/MN) without transposes.
+// Up to four row groups share A and K but carry their own B / bias / width (the video and text
+// weights of the per-modality projections run in one launch).
+//
+// CTA = 192 threads, one CTA per SM, tiles of 128 x 256 x 64 with a 4-stage smem ring:
+//   warp 0      TMA producer (one lane): A/B tiles -> smem, completion on `full[s]`
+//   warp 1      MMA issuer (one lane): 4 x tcgen05.mma 128x256x16 per stage, commit -> `empty[s]`;
+//               owns the TMEM allocation (2 accumulators x 256 fp32 columns = 512 columns)
+//   warps 2..5  epilogue: tcgen05.ld 32 columns at a time, bias / GELU-tanh / dGELU / accumulate,
+//               bf16 or fp32 stores; releases the accumulator through `tmem_empty[acc]`
+// The epilogue of tile i overlaps the main loop of tile i+1 (double-buffered accumulators).
+// Every barrier wait is bounded (4 s): on timeout the kernel records an error code in
+// g_error_flag and unwinds, so a bad launch cannot hang the GPU.
+#include <mutex>
+
+#include "common.cuh"
+#include "launchers.h"
+#include "sm100.cuh"
+
+namespace pan {
+namespace gemm {
+using namespace sm100;
+
+constexpr int BM = 128, BN = 256, BK = 64, STAGES = 4;
+constexpr int kThreads = 192;
+constexpr int A_STAGE = BM * BK * 2;  // 16 KB
+constexpr int B_STAGE = BN * BK * 2;  // 32 KB
+constexpr int SMEM_BYTES = STAGES * (A_STAGE + B_STAGE) + 1024 /*align*/ + 256 /*barriers*/;
+constexpr int kMaxGroups = 4;
+
+enum Epi : int { EPI_PLAIN = 0, EPI_GELU = 1, EPI_DGELU = 2 };
+
+struct Params {
+  int M, N, K;            // M: total rows of A (for OOB); N: max width; K: reduction length
+  int a_mn, b_mn;         // operand majors (1 = MN-major)
+  int n_groups;
+  int row_begin[kMaxGroups], row_end[kMaxGroups], n_cols[kMaxGroups];
+  int tile_prefix[kMaxGroups + 1];
+  int m_tiles[kMaxGroups], n_tiles[kMaxGroups];
+  int k_blocks[kMaxGroups];  // per-group reduction length (groups may read a prefix of A's columns)
+  const __nv_bfloat16* bias[kMaxGroups];
+  void* D;
+  long long ldd;
+  int d_fp32;
+  __nv_bfloat16* aux;     // GELU: pre-activation out; DGELU: pre-activation in
+  long long ldaux;
+  __nv_bfloat16* aux2;    // DGELU: GELU(pre) out
+  long long ldaux2;
+  int epi;
+  int accumulate;
+};
+
+struct TmapSet {
+  CUtensorMap a;
+  CUtensorMap b[kMaxGroups];
+};
+
+__device__ __forceinline__ void tile_coords(const Params& p, int t, int& g, int& mb, int& nb) {
+  g = 0;
+  while (g + 1 < p.n_groups && t >= p.tile_prefix[g + 1]) ++g;
+  const int local = t - p.tile_prefix[g];
+  const int mt = p.m_tiles[g], nt = p.n_tiles[g];
+  // bands of up to 8 N-tiles: consecutive tiles share the A tile, the band's B stays in L2
+  const int band = local / (mt * 8);
+  const int width = min(8, nt - band * 8);
+  const int idx = local - band * mt * 8;
+  mb = idx / width;
+  nb = band * 8 + idx % width;
+}
+
+__device__ __forceinline__ float gelu_tanh(float x) {
+  const float k0 = 0.7978845608028654f, k1 = 0.044715f;
+  return 0.5f * x * (1.f + tanhf(k0 * (x + k1 * x * x * x)));
+}
+
+__device__ __forceinline__ float gelu_tanh_grad(float x) {
+  const float k0 = 0.7978845608028654f, k1 = 0.044715f;
+  const float t = tanhf(k0 * (x + k1 * x * x * x));
+  return 0.5f * (1.f + t) + 0.5f * x * (1.f - t * t) * k0 * (1.f + 3.f * k1 * x * x);
+}
+
+__global__ void __launch_bounds__(kThreads, 1)
+gemm_kernel(const __grid_constant__ Params p, const __grid_constant__ TmapSet maps) {
+  extern __shared__ __align__(1024) uint8_t smem_raw[];
+  uint8_t* smem = reinterpret_cast<uint8_t*>((reinterpret_cast<uintptr_t>(smem_raw) + 1023) & ~uintptr_t(1023));
+  uint8_t* smem_a = smem;
+  uint8_t* smem_b = smem + STAGES * A_STAGE;
+  uint64_t* bars = reinterpret_cast<uint64_t*>(smem_b + STAGES * B_STAGE);
+  // bars: full[S], empty[S], tmem_full[2], tmem_empty[2]; then the TMEM base address
+  uint32_t* tmem_slot = reinterpret_cast<uint32_t*>(bars + 2 * STAGES + 4);
+  __shared__ volatile int s_abort;
+
+  const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
+  const int total_tiles = p.tile_prefix[p.n_groups];
+
+  auto full_bar = [&](int s) { return smem_u32(bars + s); };
+  auto empty_bar = [&](int s) { return smem_u32(bars + STAGES + s); };
+  auto tfull_bar = [&](int a) { return smem_u32(bars + 2 * STAGES + a); };
+  auto tempty_bar = [&](int a) { return smem_u32(bars + 2 * STAGES + 2 + a); };
+
+  if (threadIdx.x == 0) {
+    s_abort = 0;
+    for (int s = 0; s < STAGES; ++s) {
+      mbar_init(full_bar(s), 1);
+      mbar_init(empty_bar(s), 1);
+    }
+    for (int a = 0; a < 2; ++a) {
+      mbar_init(tfull_bar(a), 1);
+      mbar_init(tempty_bar(a), 4);  // one arrive per epilogue warp
+    }
+    fence_barrier_init();
+    prefetch_tmap(&maps.a);
+    for (int g = 0; g < p.n_groups; ++g) prefetch_tmap(&maps.b[g]);
+  }
+  if (warp == 1) {
+    tmem_alloc(smem_u32(tmem_slot), 512);
+    tmem_relinquish();
+  }
+  tc_fence_before();
+  __syncthreads();
+  tc_fence_after();
+  const uint32_t tmem_base = *tmem_slot;
+
+  if (warp == 0) {
+    // ------------------------------------------------------------------ TMA producer
+    if (lane == 0) {
+      int stage = 0;
+      uint32_t phase = 0;
+      for (int t = blockIdx.x; t < total_tiles && !s_abort; t += gridDim.x) {
+        int g, mb, nb;
+        tile_coords(p, t, g, mb, nb);
+        const int m0 = p.row_begin[g] + mb * BM;
+        const int n0 = nb * BN;
+        const int k_blocks = p.k_blocks[g];
+        for (int kb = 0; kb < k_blocks && !s_abort; ++kb) {
+          if (!mbar_wait(empty_bar(stage), phase ^ 1, 11)) { s_abort = 1; break; }
+          const uint32_t fb = full_bar(stage);
+          mbar_expect_tx(fb, A_STAGE + B_STAGE);
+          const uint32_t sa = smem_u32(smem_a + stage * A_STAGE);
+          const uint32_t sb = smem_u32(smem_b + stage * B_STAGE);
+          const int k0 = kb * BK;
+          if (!p.a_mn) {
+            tma_load_2d(sa, &maps.a, fb, k0, m0);
+          } else {
+            tma_load_2d(sa, &maps.a, fb, m0, k0);
+            tma_load_2d(sa + 8192, &maps.a, fb, m0 + 64, k0);
+          }
+          if (!p.b_mn) {
+            tma_load_2d(sb, &maps.b[g], fb, k0, n0);
+          } else {
+#pragma unroll
+            for (int j = 0; j < 4; ++j) tma_load_2d(sb + j * 8192, &maps.b[g], fb, n0 + 64 * j, k0);
+          }
+          if (++stage == STAGES) { stage = 0; phase ^= 1; }
+        }
+      }
+    }
+  } else if (warp == 1) {
+    // ------------------------------------------------------------------ MMA issuer
+    if (lane == 0) {
+      const uint32_t idesc = idesc_bf16_f32(BM, BN, p.a_mn, p.b_mn);
+      // K-major SW128: LBO unused (16 B), SBO = 8 rows * 128 B; K step of 16 = +32 B.
+      // MN-major SW128: LBO = next 64-wide MN chunk (8 KB), SBO = next 8 k-rows (1 KB); K step = +2 KB.
+      const uint32_t a_lbo = p.a_mn ? 8192 : 16, b_lbo = p.b_mn ? 8192 : 16;
+      const uint32_t a_kstep = p.a_mn ? 2048 : 32, b_kstep = p.b_mn ? 2048 : 32;
+      int stage = 0;
+      uint32_t phase = 0;
+      int acc = 0;
+      uint32_t acc_phase = 0;
+      for (int t = blockIdx.x; t < total_tiles && !s_abort; t += gridDim.x) {
+        if (!mbar_wait(tempty_bar(acc), acc_phase ^ 1, 12)) { s_abort = 1; break; }
+        tc_fence_after();
+        int g, mb, nb;
+        tile_coords(p, t, g, mb, nb);
+        const int k_blocks = p.k_blocks[g];
+        const uint32_t d_tmem = tmem_base + acc * BN;
+        bool ok = true;
+        for (int kb = 0; kb < k_blocks; ++kb) {
+          if (!mbar_wait(full_bar(stage), phase, 13)) { ok = false; break; }
+          tc_fence_after();
+          const uint32_t sa = smem_u32(smem_a + stage * A_STAGE);
+          const uint32_t sb = smem_u32(smem_b + stage * B_STAGE);
+#pragma unroll
+          for (int kk = 0; kk < BK / 16; ++kk) {
+            const uint64_t ad = smem_desc_sw128(sa + kk * a_kstep, a_lbo, 1024);
+            const uint64_t bd = smem_desc_sw128(sb + kk * b_kstep, b_lbo, 1024);
+            mma_bf16_ss(d_tmem, ad, bd, idesc, (kb | kk) != 0);
+          }
+          mma_commit(empty_bar(stage));  // frees the smem stage when these MMAs retire
+          if (++stage == STAGES) { stage = 0; phase ^= 1; }
+        }
+        if (!ok) { s_abort = 1; break; }
+        mma_commit(tfull_bar(acc));  // accumulator ready for the epilogue
+        if (++acc == 2) { acc = 0; acc_phase ^= 1; }
+      }
+    }
+  } else {
+    // ------------------------------------------------------------------ epilogue (warps 2..5)
+    const int q = warp & 3;  // TMEM lane quarter this warp may access
+    int acc = 0;
+    uint32_t acc_phase = 0;
+    for (int t = blockIdx.x; t < total_tiles && !s_abort; t += gridDim.x) {
+      if (!mbar_wait(tfull_bar(acc), acc_phase, 14)) { s_abort = 1; break; }
+      tc_fence_after();
+      int g, mb, nb;
+      tile_coords(p, t, g, mb, nb);
+      const int row = p.row_begin[g] + mb * BM + q * 32 + lane;
+      const bool row_ok = row < p.row_end[g];
+      const int n_lim = p.n_cols[g];
+      const __nv_bfloat16* bias = p.bias[g];
+      const uint32_t t_row = tmem_base + acc * BN + ((uint32_t)(q * 32) << 16);
+      for (int ch = 0; ch < BN / 32; ++ch) {
+        const int c0 = nb * BN + ch * 32;
+        uint32_t r[32];
+        tmem_ld32(t_row + ch * 32, r);
+        tmem_ld_wait();
+        if (!row_ok || c0 >= n_lim) continue;
+#pragma unroll
+        for (int v8 = 0; v8 < 4; ++v8) {
+          const int c = c0 + v8 * 8;
+          if (c >= n_lim) break;
+          float o[8];
+#pragma unroll
+          for (int i = 0; i < 8; ++i) o[i] = __uint_as_float(r[v8 * 8 + i]);
+          if (bias != nullptr) {
+            float b[8];
+            load8(bias + c, b);
+#pragma unroll
+            for (int i = 0; i < 8; ++i) o[i] += b[i];
+          }
+          if (p.epi == EPI_GELU) {
+            float pre[8];
+#pragma unroll
+            for (int i = 0; i < 8; ++i) pre[i] = o[i];
+            store8(p.aux + (size_t)row * p.ldaux + c, pre);
+#pragma unroll
+            for (int i = 0; i < 8; ++i) o[i] = gelu_tanh(__bfloat162float(__float2bfloat16_rn(pre[i])));
+          } else if (p.epi == EPI_DGELU) {
+            float pre[8], post[8];
+            load8(p.aux + (size_t)row * p.ldaux + c, pre);
+#pragma unroll
+            for (int i = 0; i < 8; ++i) {
+              post[i] = gelu_tanh(pre[i]);
+              o[i] *= gelu_tanh_grad(pre[i]);
+            }
+            store8(p.aux2 + (size_t)row * p.ldaux2 + c, post);
+          }
+          if (p.d_fp32) {
+            float* d = reinterpret_cast<float*>(p.D) + (size_t)row * p.ldd + c;
+            if (p.accumulate) {
+              const float4 x0 = *reinterpret_cast<const float4*>(d);
+              const float4 x1 = *reinterpret_cast<const float4*>(d + 4);
+              o[0] += x0.x; o[1] += x0.y; o[2] += x0.z; o[3] += x0.w;
+              o[4] += x1.x; o[5] += x1.y; o[6] += x1.z; o[7] += x1.w;
+            }
+            *reinterpret_cast<float4*>(d) = make_float4(o[0], o[1], o[2], o[3]);
+            *reinterpret_cast<float4*>(d + 4) = make_float4(o[4], o[5], o[6], o[7]);
+          } else {
+            __nv_bfloat16* d = reinterpret_cast<__nv_bfloat16*>(p.D) + (size_t)row * p.ldd + c;
+            if (p.accumulate) {
+              float x[8];
+              load8(d, x);
+#pragma unroll
+              for (int i = 0; i < 8; ++i) o[i] += x[i];
+            }
+            store8(d, o);
+          }
+        }
+      }
+      tc_fence_before();
+      __syncwarp();
+      if (lane == 0) mbar_arrive(tempty_bar(acc));
+      if (++acc == 2) { acc = 0; acc_phase ^= 1; }
+    }
+  }
+
+  tc_fence_before();
+  __syncthreads();
+  if (warp == 1) {
+    tc_fence_after();
+    tmem_dealloc(tmem_base, 512);
+  }
+}
+
+// ---------------------------------------------------------------------------------- host side
+
+typedef CUresult (*EncodeTiledFn)(CUtensorMap*, CUtensorMapDataType, cuuint32_t, void*, const cuuint64_t*,
+                                  const cuuint64_t*, const cuuint32_t*, const cuuint32_t*, CUtensorMapInterleave,
+                                  CUtensorMapSwizzle, CUtensorMapL2promotion, CUtensorMapFloatOOBfill);
+
+EncodeTiledFn encode_fn() {
+  static EncodeTiledFn fn = nullptr;
+  static std::once_flag once;
+  std::call_once(once, [] {
+    void* ptr = nullptr;
+    cudaDriverEntryPointQueryResult q;
+    if (cudaGetDriverEntryPoint("cuTensorMapEncodeTiled", &ptr, cudaEnableDefault, &q) == cudaSuccess)
+      fn = reinterpret_cast<EncodeTiledFn>(ptr);
+  });
+  return fn;
+}
+
+// 2-D bf16 tensor map over a row-major [rows, cols] matrix (row stride `ld` elements), box
+// [box_rows, box_cols] with 128-byte swizzle (box_cols * 2 == 128).
+const char* make_map(CUtensorMap* m, const void* base, long long rows, long long cols, long long ld, int box_rows,
+                     int box_cols) {
+  if (reinterpret_cast<uintptr_t>(base) % 16 != 0) return "TMA base must be 16-byte aligned";
+  if ((ld * 2) % 16 != 0) return "TMA row stride must be a multiple of 16 bytes";
+  EncodeTiledFn fn = encode_fn();
+  if (fn == nullptr) return "cuTensorMapEncodeTiled is unavailable";
+  cuuint64_t dims[2] = {(cuuint64_t)cols, (cuuint64_t)rows};
+  cuuint64_t strides[1] = {(cuuint64_t)(ld * 2)};
+  cuuint32_t box[2] = {(cuuint32_t)box_cols, (cuuint32_t)box_rows};
+  cuuint32_t estr[2] = {1, 1};
+  CUresult r = fn(m, CU_TENSOR_MAP_DATA_TYPE_BFLOAT16, 2, const_cast<void*>(base), dims, strides, box, estr,
+                  CU_TENSOR_MAP_INTERLEAVE_NONE, CU_TENSOR_MAP_SWIZZLE_128B, CU_TENSOR_MAP_L2_PROMOTION_L2_256B,
+                  CU_TENSOR_MAP_FLOAT_OOB_FILL_NONE);
+  return r == CUDA_SUCCESS ? nullptr : "cuTensorMapEncodeTiled failed";
+}
+
+int num_sms() {
+  static int n = 0;
+  if (n == 0) {
+    int dev = 0;
+    cudaGetDevice(&dev);
+    cudaDeviceGetAttribute(&n, cudaDevAttrMultiProcessorCount, dev);
+  }
+  return n;
+}
+
+}  // namespace gemm
+
+const char* launch_gemm(const GemmArgs& a, cudaStream_t stream) {
+  using namespace gemm;
+  const int G = a.n_groups;
+  if (G < 1 || G > kMaxGroups) return "gemm: 1..4 groups";
+  if (a.lda % 8 != 0) return "gemm: A row stride must be a multiple of 8 elements";
+  if (a.ldd % 8 != 0 && !a.d_fp32) return "gemm: D row stride must be a multiple of 8 elements";
+  if (a.d_fp32 && a.ldd % 4 != 0) return "gemm: fp32 D row stride must be a multiple of 4 elements";
+  Params p{};
+  p.M = a.M;
+  p.K = a.K;
+  p.a_mn = a.a_mn;
+  p.b_mn = a.b_mn;
+  p.n_groups = G;
+  p.D = a.D;
+  p.ldd = a.ldd;
+  p.d_fp32 = a.d_fp32;
+  p.epi = a.epi;
+  p.accumulate = a.accumulate;
+  p.aux = reinterpret_cast<__nv_bfloat16*>(a.aux);
+  p.ldaux = a.ldaux;
+  p.aux2 = reinterpret_cast<__nv_bfloat16*>(a.aux2);
+  p.ldaux2 = a.ldaux2;
+  TmapSet maps;
+  const char* err = !a.a_mn ? make_map(&maps.a, a.A, a.M, a.K, a.lda, BM, BK) : make_map(&maps.a, a.A, a.K, a.M, a.lda, BK, 64);
+  if (err) return err;
+  int tiles = 0;
+  p.tile_prefix[0] = 0;
+  for (int g = 0; g < G; ++g) {
+    const GemmGroup& gr = a.groups[g];
+    if (gr.k > a.K) return "gemm: group K must be <= K";
+    if (gr.ldb % 8 != 0) return "gemm: B row stride must be a multiple of 8 elements";
+    if (gr.n % 8 != 0) return "gemm: N must be a multiple of 8";
+    err = !a.b_mn ? make_map(&maps.b[g], gr.B, gr.n, gr.k, gr.ldb, BN, BK) : make_map(&maps.b[g], gr.B, gr.k, gr.n, gr.ldb, BK, 64);
+    if (err) return err;
+    p.row_begin[g] = gr.row_begin;
+    p.row_end[g] = gr.row_end;
+    p.n_cols[g] = gr.n;
+    p.k_blocks[g] = (gr.k + BK - 1) / BK;
+    p.bias[g] = reinterpret_cast<const __nv_bfloat16*>(gr.bias);
+    const int rows = gr.row_end > gr.row_begin ? gr.row_end - gr.row_begin : 0;
+    p.m_tiles[g] = (rows + BM - 1) / BM;
+    p.n_tiles[g] = (gr.n + BN - 1) / BN;
+    tiles += p.m_tiles[g] * p.n_tiles[g];
+    p.tile_prefix[g + 1] = tiles;
+  }
+  for (int g = G; g < kMaxGroups; ++g) maps.b[g] = maps.b[0];
+  if (tiles == 0) return nullptr;
+  static bool attr_set = false;
+  if (!attr_set) {
+    if (cudaFuncSetAttribute(gemm_kernel, cudaFuncAttributeMaxDynamicSharedMemorySize, SMEM_BYTES) != cudaSuccess)
+      return "gemm: cannot set the dynamic shared memory size";
+    attr_set = true;
+  }
+  const int grid = tiles < num_sms() ? tiles : num_sms();
+  gemm_kernel<<<grid, kThreads, SMEM_BYTES, stream>>>(p, maps);
+  return cudaGetLastError() == cudaSuccess ? nullptr : "gemm: launch failed";
+}
+
+int gemm_error_flag(bool reset) {
+  int v = 0;
+  cudaMemcpyFromSymbol(&v, sm100::g_error_flag, sizeof(int));
+  if (reset) {
+    int z = 0;
+    cudaMemcpyToSymbol(sm100::g_error_flag, &z, sizeof(int));
+  }
+  return v;
+}
+
+}  // namespace pan
