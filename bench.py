@@ -1,0 +1,193 @@
+"""Headline benchmark: 29B MMDiT 720p training throughput in latent tokens/s.
+
+    python bench.py [--gpus N] [--steps K] [--warmup W] [--impl ours|reference]
+    torchrun --nnodes=1 --nproc-per-node N --master-addr 127.0.0.1 --master-port P bench.py --gpus N ...
+
+One rank per GPU.  Every rank trains the 29B architecture of config/pretrain_29B_720p.yaml (random
+init, bf16 compute, exact fp32 masters, Muon + AdamW, global-norm clipping at 1.0, full activation
+checkpointing) on its own synthetic packed batch: 5 clips x (21 x 44 x 80 Wan-2.2 latents -> 18,480
+patch tokens + 512 text tokens of dim 4096) = 94,960 joint tokens within the 110,576 budget.
+Weights are sharded over the N ranks (FSDP-style); when one replica's optimizer state does not fit
+the GPUs, master low halves and optimizer state are streamed from pinned host memory.
+
+Timing: W untimed steps, then K steps between barrier + synchronize; CUDA events on the launching
+stream; the max over ranks.  ``value`` is the device time of forward+backward+optimizer per step;
+``e2e`` is the same K steps measured around the public ``StepRunner`` call including the host->device
+copy of the step's inputs from pinned memory and the device->host read of loss and grad norm.
+Per-step activations (several GB) exceed the 126 MB L2, so no extra flush is needed.
+"""
+from __future__ import annotations
+
+import argparse
+import json
+import math
+import os
+import sys
+import time
+
+os.environ.setdefault("PYTORCH_CUDA_ALLOC_CONF", "expandable_segments:True")
+
+ROOT = os.path.dirname(os.path.abspath(__file__))
+sys.path.insert(0, ROOT)
+
+METRIC = "29B MMDiT 720p train latent tokens/s (1/2/4/8 B200, max over ranks); s/video @50 steps"
+
+
+def parse():
+    ap = argparse.ArgumentParser()
+    ap.add_argument("--gpus", type=int, default=1)
+    ap.add_argument("--steps", type=int, default=2)
+    ap.add_argument("--warmup", type=int, default=3)
+    ap.add_argument("--impl", default="ours", choices=("ours", "reference"))
+    ap.add_argument("--config", default=os.path.join(ROOT, "config", "pretrain_29B_720p.yaml"))
+    ap.add_argument("--layers", type=int, default=None, help="development only: fewer joint blocks (invalid result)")
+    ap.add_argument("--clips", type=int, default=5)
+    ap.add_argument("--frames", type=int, default=21)
+    ap.add_argument("--offload", default="auto")
+    return ap.parse_args()
+
+
+def reference_arm(args):
+    print(json.dumps({
+        "impl": "reference", "metric": METRIC,
+        "unavailable": "the reference has no setup.py/pyproject.toml (pip cannot install it) and imports "
+                       "diffusers, flash_attn.cute (FA4) and quack>=0.6.3, none of which exist in this image",
+    }), flush=True)
+
+
+def main():
+    args = parse()
+    if args.impl == "reference":
+        reference_arm(args)
+        return
+    import torch
+    import torch.distributed as dist
+    import yaml
+    from pan2_b200.data.synthetic import synthetic_packed_batch, batch_to_device, batch_bytes
+    from pan2_b200.models.transformer import translate_architecture_config
+    from pan2_b200.ops._ext import start_launch_count, stop_launch_count, ext
+    from pan2_b200.training.engine import TrainEngine, OptimConfig
+    from pan2_b200.training.step import StepRunner
+    from pan2_b200.optim.lr import lr_lambda_from_config
+    from pan2_b200.utils.clocks import ClockSampler
+
+    world = int(os.environ.get("WORLD_SIZE", "1"))
+    rank = int(os.environ.get("RANK", "0"))
+    local = int(os.environ.get("LOCAL_RANK", "0"))
+    torch.cuda.set_device(local)
+    device = torch.device("cuda", local)
+    group = None
+    if world > 1:
+        import datetime
+        dist.init_process_group("nccl", timeout=datetime.timedelta(seconds=900), device_id=device)
+        group = dist.group.WORLD
+
+    with open(args.config) as f:
+        cfg = yaml.safe_load(f)
+    arch = translate_architecture_config(cfg["model"]["transformer_config_overrides"])
+    arch["zero_init_modulation"] = bool(cfg["model"].get("zero_init_modulation", True))
+    valid = True
+    if args.layers is not None:
+        arch["num_layers"] = args.layers
+        valid = args.layers == 44
+    tr = cfg["training"]
+    optim = OptimConfig(lr=float(tr["learning_rate"]), weight_decay=float(tr.get("weight_decay", 0.05)),
+                        use_muon=bool(tr.get("use_muon", True)), max_grad_norm=float(tr["max_grad_norm"]))
+
+    # 704x1280 frames -> 44x80 latents; 21 latent frames per 5 s clip; 512 text tokens per clip
+    batch = synthetic_packed_batch(args.clips, (args.frames, 44, 80), 512, seed=1234 + rank, pin=True,
+                                   rope_axes=tuple(arch["rope_axes_dim"]), rope_theta=float(arch["rope_theta"]),
+                                   rope_scale=(float(arch["rope_temporal_scale"]), 1.0, 1.0))
+    meta = batch["packed_seq_params"]
+    assert meta.n_active <= int(cfg["data"]["packed_joint_token_budget"])
+    latent_tokens = meta.n_video
+
+    t0 = time.time()
+    engine = TrainEngine(arch, device, group=group, seed=42, optim=optim, offload=args.offload,
+                         activation_bytes_estimate=int(float(os.environ.get("PAN_ACT_RESERVE_GB", "40")) * 1e9))
+    placed = {}
+    init_s = time.time() - t0
+    runner = StepRunner(engine, lr_lambda=lr_lambda_from_config(tr))
+
+    for _ in range(args.warmup):
+        runner.train_step(batch)
+    torch.cuda.synchronize()
+    if world > 1:
+        dist.barrier()
+    torch.cuda.synchronize()
+
+    sampler = ClockSampler()
+    if local == 0:
+        sampler.start()
+    start_launch_count()
+    ev = [[torch.cuda.Event(enable_timing=True) for _ in range(3)] for _ in range(args.steps)]
+    for k in range(args.steps):
+        ev[k][0].record()
+        dev_batch = batch_to_device(batch, device, non_blocking=True)
+        ev[k][1].record()
+        metrics = runner.device_step(dev_batch)
+        ev[k][2].record()
+    torch.cuda.synchronize()
+    launches = stop_launch_count()
+    if world > 1:
+        dist.barrier()
+    torch.cuda.synchronize()
+    clocks = sampler.stop(gpus=list(range(world))) if local == 0 else None
+
+    total_ms = ev[0][0].elapsed_time(ev[-1][2])
+    compute_ms = sum(e[1].elapsed_time(e[2]) for e in ev)
+    t = torch.tensor([total_ms, compute_ms], device=device)
+    if world > 1:
+        dist.all_reduce(t, op=dist.ReduceOp.MAX)
+    total_ms, compute_ms = t.tolist()
+    ms_step = compute_ms / args.steps
+    e2e_ms = total_ms / args.steps
+    tokens_global = latent_tokens * world
+    err = ext().error_flag(True)
+    if rank == 0:
+        h2d = batch_bytes(batch)
+        out = {
+            "metric": METRIC,
+            "value": tokens_global / (ms_step / 1e3),
+            "unit": "latent tokens/s",
+            "n_gpus": world,
+            "steps": args.steps,
+            "warmup": args.warmup,
+            "ms_per_step": ms_step,
+            "higher_is_better": True,
+            "scaling": "weak",
+            "vs_baseline": None,
+            "dtype": "bf16",
+            "data": "synthetic (random Wan-2.2-shaped latents, random 4096-d text embeddings, random-init 29B weights)",
+            "config": {
+                "model": f"PAN2 MMDiT {engine.total_params / 1e9:.2f}B ({arch['num_layers']} layers)",
+                "global_batch": args.clips * world,
+                "seq_len": meta.joint_packed_length,
+                "latent_tokens_per_gpu": latent_tokens,
+                "joint_tokens_per_gpu": meta.n_active,
+                "parallelism": f"fsdp{world}" + ("+host-offload" if engine.offload else ""),
+                "optimizer": "Muon+AdamW, clip 1.0",
+                "activation_checkpointing": "every block",
+                "l2": "per-step working set (GBs) larger than L2; no extra flush",
+                "valid_full_config": valid,
+            },
+            "e2e": {"value": tokens_global / (e2e_ms / 1e3), "unit": "latent tokens/s",
+                    "h2d_bytes_per_step": h2d, "d2h_bytes_per_step": 8,
+                    "api": "pan2_b200.training.step.StepRunner (inputs copied from pinned host memory)"},
+            "gpu_launches": launches["total"],
+            "clocks": clocks,
+            "loss": metrics["loss"],
+            "grad_norm": metrics["grad_norm"],
+            "init_s": init_s,
+            "device_error_flag": err,
+            "peak_mem_gb": torch.cuda.max_memory_allocated(device) / 1e9,
+            "host_pinned_gb": engine.host_bytes_planned / 1e9,
+        }
+        print(json.dumps(out), flush=True)
+    if world > 1:
+        dist.barrier()
+        dist.destroy_process_group()
+
+
+if __name__ == "__main__":
+    main()

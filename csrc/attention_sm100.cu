@@ -1,0 +1,674 @@
+// Variable-length non-causal attention for sm_100a (tcgen05 + TMEM + TMA), head_dim 128.
+//
+// Forward (one CTA = one head x two 128-row query tiles "A" and "B" of one segment):
+//   warp 0       TMA: Q_A, Q_B once; then K_j, V_j through a 3-slot smem ring
+//   warp 1       MMA (one lane): S_X = Q_X K_j^T into TMEM, O_X += P_X V_j from smem P
+//   warps 2..5   softmax of tile A (one TMEM lane = one query row per thread)
+//   warps 6..9   softmax of tile B
+// The two tiles ping-pong: while one softmax group works, the tensor core runs the other tile's
+// GEMMs.  Online softmax in the exp2 domain with lazy rescaling: O and l are rescaled only when
+// the running max grows by more than 8 (a factor of 256), so most iterations leave O in TMEM
+// untouched.  Outputs O (bf16, [L, H, D]) and the natural-log LSE ([H, L] fp32).
+//
+// Backward is two passes of one templated kernel sharing the same skeleton:
+//   MODE_DQ  : per query tile, loop over key tiles:  S = Q K^T, dP = dO V^T,
+//              dS = P (dP - Delta),  dQ += dS K
+//   MODE_DKV : per key tile, loop over query tiles:  S^T = K Q^T, dP^T = V dO^T,
+//              dV += P^T dO,  dK += dS^T Q
+// (the FlashAttention-2 recurrences, with P recomputed from the saved LSE), so no atomics are
+// needed.  TMEM holds the two score-shaped products and up to two accumulators (4 x 128 columns).
+//
+// Smem tiles are 128 rows x 64 columns bf16 with the 128-byte swizzle, two per 128-wide operand.
+// The same bytes serve as a K-major operand (rows = M/N, e.g. K for S = Q K^T) or an MN-major one
+// (rows = K, e.g. V for O += P V).  Every barrier wait is bounded (no hangs, error flag instead).
+#include "common.cuh"
+#include "launchers.h"
+#include "sm100.cuh"
+
+namespace pan {
+namespace attn {
+using namespace sm100;
+
+constexpr int D = 128;
+constexpr int BT = 128;                    // rows per tile (queries or keys)
+constexpr int TILE_BYTES = BT * D * 2;     // 32 KB (two 16 KB swizzled halves)
+constexpr int HALF_BYTES = TILE_BYTES / 2;
+constexpr int RING = 3;
+constexpr float kLog2e = 1.4426950408889634f;
+constexpr float kLn2 = 0.6931471805599453f;
+
+struct WorkItem {
+  int seg_start;   // first row of the segment
+  int seg_len;     // rows of the segment
+  int tile_start;  // first row (relative to seg_start) of this CTA's outer tile(s)
+  int pad;
+};
+
+// K-major SW128 descriptor of a [128 rows, 128 cols] operand at k-step kk (16 columns per step).
+__device__ __forceinline__ uint64_t desc_kmajor(uint32_t base, int kk) {
+  return smem_desc_sw128(base + (kk >> 2) * HALF_BYTES + (kk & 3) * 32, 16, 1024);
+}
+// MN-major SW128 descriptor: rows are the reduction dim; k-step of 16 rows = 2 KB; the two
+// 64-wide column halves are 16 KB apart.
+__device__ __forceinline__ uint64_t desc_mnmajor(uint32_t base, int kk) {
+  return smem_desc_sw128(base + kk * 2048, HALF_BYTES, 1024);
+}
+
+// Write 32 consecutive bf16 values (16 packed words) of row `r`, columns [c0, c0+32) into a
+// swizzled [128, 128] K-major smem operand.
+__device__ __forceinline__ void store_row32_swizzled(uint8_t* tile, int r, int c0, const uint32_t (&w)[16]) {
+  uint8_t* half = tile + (c0 >> 6) * HALF_BYTES + r * 128;
+  const int u0 = (c0 & 63) >> 3;  // 16-byte unit within the 128-byte row
+#pragma unroll
+  for (int j = 0; j < 4; ++j) {
+    const int u = (u0 + j) ^ (r & 7);
+    *reinterpret_cast<uint4*>(half + u * 16) = make_uint4(w[4 * j], w[4 * j + 1], w[4 * j + 2], w[4 * j + 3]);
+  }
+}
+
+__device__ __forceinline__ uint32_t pack_bf16(float a, float b) {
+  __nv_bfloat162 h = __floats2bfloat162_rn(a, b);
+  return *reinterpret_cast<uint32_t*>(&h);
+}
+
+__device__ __forceinline__ void fence_async_smem() { asm volatile("fence.proxy.async.shared::cta;" ::: "memory"); }
+
+// ============================================================================ forward
+constexpr int FWD_THREADS = 320;
+constexpr int FWD_SMEM = 2 * TILE_BYTES /*Q*/ + RING * TILE_BYTES + 2 * TILE_BYTES /*P*/ + 1024 + 256;
+
+__global__ void __launch_bounds__(FWD_THREADS, 1)
+attn_fwd_kernel(const __grid_constant__ CUtensorMap qmap, const __grid_constant__ CUtensorMap kmap,
+                const __grid_constant__ CUtensorMap vmap, const WorkItem* __restrict__ items, int L, int H,
+                float scale_log2, __nv_bfloat16* __restrict__ out, float* __restrict__ lse) {
+  extern __shared__ uint8_t smem_raw[];
+  uint8_t* smem = reinterpret_cast<uint8_t*>((reinterpret_cast<uintptr_t>(smem_raw) + 1023) & ~uintptr_t(1023));
+  uint8_t* sQ = smem;                                 // 2 tiles
+  uint8_t* sKV = sQ + 2 * TILE_BYTES;                 // RING tiles
+  uint8_t* sP = sKV + RING * TILE_BYTES;              // 2 tiles
+  uint64_t* bars = reinterpret_cast<uint64_t*>(sP + 2 * TILE_BYTES);
+  // bars: q_full, kv_full[3], kv_empty[3], s_full[2], p_ready[2], pv_done[2]
+  uint32_t* tmem_slot = reinterpret_cast<uint32_t*>(bars + 16);
+  volatile int& s_abort = *reinterpret_cast<volatile int*>(bars + 17);
+
+  const WorkItem it = items[blockIdx.x];
+  const int h = blockIdx.y;
+  const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
+  const int n_kv = (it.seg_len + BT - 1) / BT;
+
+  const uint32_t q_full = smem_u32(bars + 0);
+  auto kv_full = [&](int s) { return smem_u32(bars + 1 + s); };
+  auto kv_empty = [&](int s) { return smem_u32(bars + 4 + s); };
+  auto s_full = [&](int x) { return smem_u32(bars + 7 + x); };
+  auto p_ready = [&](int x) { return smem_u32(bars + 9 + x); };
+  auto pv_done = [&](int x) { return smem_u32(bars + 11 + x); };
+
+  if (threadIdx.x == 0) {
+    s_abort = 0;
+    mbar_init(q_full, 1);
+    for (int s = 0; s < RING; ++s) {
+      mbar_init(kv_full(s), 1);
+      mbar_init(kv_empty(s), 1);
+    }
+    for (int x = 0; x < 2; ++x) {
+      mbar_init(s_full(x), 1);
+      mbar_init(p_ready(x), 4);
+      mbar_init(pv_done(x), 1);
+    }
+    fence_barrier_init();
+    prefetch_tmap(&qmap);
+    prefetch_tmap(&kmap);
+    prefetch_tmap(&vmap);
+  }
+  if (warp == 1) {
+    tmem_alloc(smem_u32(tmem_slot), 512);
+    tmem_relinquish();
+  }
+  tc_fence_before();
+  __syncthreads();
+  tc_fence_after();
+  const uint32_t tmem = *tmem_slot;  // S_A 0, S_B 128, O_A 256, O_B 384
+
+  const int col = h * D;
+  if (warp == 0) {
+    if (lane == 0) {
+      const int q0 = it.seg_start + it.tile_start;
+      mbar_expect_tx(q_full, 2 * TILE_BYTES);
+      for (int x = 0; x < 2; ++x) {
+        const uint32_t dst = smem_u32(sQ + x * TILE_BYTES);
+        tma_load_2d(dst, &qmap, q_full, col, q0 + x * BT);
+        tma_load_2d(dst + HALF_BYTES, &qmap, q_full, col + 64, q0 + x * BT);
+      }
+      int n = 0;
+      for (int j = 0; j < n_kv && !s_abort; ++j) {
+        for (int w = 0; w < 2; ++w, ++n) {  // K_j then V_j
+          const int slot = n % RING;
+          const uint32_t ph = (n / RING) & 1;
+          if (!mbar_wait(kv_empty(slot), ph ^ 1, 21)) { s_abort = 1; break; }
+          const uint32_t fb = kv_full(slot);
+          mbar_expect_tx(fb, TILE_BYTES);
+          const uint32_t dst = smem_u32(sKV + slot * TILE_BYTES);
+          const CUtensorMap* m = w == 0 ? &kmap : &vmap;
+          const int row = it.seg_start + j * BT;
+          tma_load_2d(dst, m, fb, col, row);
+          tma_load_2d(dst + HALF_BYTES, m, fb, col + 64, row);
+        }
+      }
+    }
+  } else if (warp == 1) {
+    if (lane == 0) {
+      const uint32_t id_s = idesc_bf16_f32(128, 128, 0, 0);   // S = Q K^T
+      const uint32_t id_pv = idesc_bf16_f32(128, 128, 0, 1);  // O += P V  (V is MN-major)
+      bool ok = mbar_wait(q_full, 0, 22);
+      tc_fence_after();
+      auto wait_slot = [&](int n) {
+        if (!ok) return 0u;
+        const int slot = n % RING;
+        ok = mbar_wait(kv_full(slot), (n / RING) & 1, 23);
+        tc_fence_after();
+        return smem_u32(sKV + slot * TILE_BYTES);
+      };
+      auto issue_s = [&](int x, uint32_t kb) {
+        const uint32_t qb = smem_u32(sQ + x * TILE_BYTES);
+#pragma unroll
+        for (int kk = 0; kk < D / 16; ++kk) mma_bf16_ss(tmem + x * 128, desc_kmajor(qb, kk), desc_kmajor(kb, kk), id_s, kk > 0);
+        mma_commit(s_full(x));
+      };
+      auto issue_pv = [&](int x, uint32_t vb, bool acc) {
+        const uint32_t pb = smem_u32(sP + x * TILE_BYTES);
+#pragma unroll
+        for (int kk = 0; kk < BT / 16; ++kk)
+          mma_bf16_ss(tmem + 256 + x * 128, desc_kmajor(pb, kk), desc_mnmajor(vb, kk), id_pv, acc || kk > 0);
+        mma_commit(pv_done(x));
+      };
+      // prologue: S_A(0), S_B(0)
+      uint32_t kb = wait_slot(0);
+      if (ok) {
+        issue_s(0, kb);
+        issue_s(1, kb);
+        mma_commit(kv_empty(0));
+      }
+      for (int j = 0; j < n_kv && ok; ++j) {
+        const int nv = 2 * j + 1, nk = 2 * j + 2;
+        const uint32_t vb = wait_slot(nv);
+        if (!ok) break;
+        if (!(ok = mbar_wait(p_ready(0), j & 1, 24))) break;
+        tc_fence_after();
+        issue_pv(0, vb, j > 0);
+        uint32_t kb2 = 0;
+        if (j + 1 < n_kv) {
+          kb2 = wait_slot(nk);
+          if (!ok) break;
+          issue_s(0, kb2);
+        }
+        if (!(ok = mbar_wait(p_ready(1), j & 1, 25))) break;
+        tc_fence_after();
+        issue_pv(1, vb, j > 0);
+        mma_commit(kv_empty(nv % RING));
+        if (j + 1 < n_kv) {
+          issue_s(1, kb2);
+          mma_commit(kv_empty(nk % RING));
+        }
+      }
+      if (!ok) s_abort = 1;
+    }
+  } else {
+    // ------------------------------------------------------------ softmax groups
+    const int x = (warp - 2) >> 2;           // 0 = tile A, 1 = tile B
+    const int quarter = warp & 3;            // TMEM lane quarter of this warp
+    const int row = quarter * 32 + lane;     // query row within the tile
+    const uint32_t lane_off = (uint32_t)(quarter * 32) << 16;
+    const uint32_t tS = tmem + x * 128 + lane_off;
+    const uint32_t tO = tmem + 256 + x * 128 + lane_off;
+    uint8_t* myP = sP + x * TILE_BYTES;
+    float m_used = -INFINITY, l = 0.f;
+    bool ok = true;
+    for (int j = 0; j < n_kv; ++j) {
+      if (!(ok = mbar_wait(s_full(x), j & 1, 26))) break;
+      tc_fence_after();
+      const int valid = min(BT, it.seg_len - j * BT);
+      float mx = -INFINITY;
+#pragma unroll
+      for (int c = 0; c < 4; ++c) {
+        uint32_t r[32];
+        tmem_ld32(tS + c * 32, r);
+        tmem_ld_wait();
+#pragma unroll
+        for (int i = 0; i < 32; ++i)
+          if (c * 32 + i < valid) mx = fmaxf(mx, __uint_as_float(r[i]));
+      }
+      const float m_new = fmaxf(m_used, mx * scale_log2);
+      const bool grow = m_new > m_used + 8.f;
+      if (j > 0) {
+        if (!(ok = mbar_wait(pv_done(x), (j - 1) & 1, 27))) break;
+        tc_fence_after();
+        if (__any_sync(0xffffffffu, grow)) {
+          const float alpha = grow ? exp2f(m_used - m_new) : 1.f;
+#pragma unroll
+          for (int c = 0; c < 4; ++c) {
+            uint32_t r[32];
+            tmem_ld32(tO + c * 32, r);
+            tmem_ld_wait();
+#pragma unroll
+            for (int i = 0; i < 32; ++i) r[i] = __float_as_uint(__uint_as_float(r[i]) * alpha);
+            tmem_st32(tO + c * 32, r);
+          }
+          tmem_st_wait();
+          l *= alpha;
+        }
+      }
+      if (grow) m_used = m_new;
+#pragma unroll
+      for (int c = 0; c < 4; ++c) {
+        uint32_t r[32];
+        tmem_ld32(tS + c * 32, r);
+        tmem_ld_wait();
+        uint32_t w[16];
+#pragma unroll
+        for (int i = 0; i < 32; i += 2) {
+          const float p0 = (c * 32 + i < valid) ? exp2f(__uint_as_float(r[i]) * scale_log2 - m_used) : 0.f;
+          const float p1 = (c * 32 + i + 1 < valid) ? exp2f(__uint_as_float(r[i + 1]) * scale_log2 - m_used) : 0.f;
+          l += p0 + p1;
+          w[i >> 1] = pack_bf16(p0, p1);
+        }
+        store_row32_swizzled(myP, row, c * 32, w);
+      }
+      fence_async_smem();
+      tc_fence_before();
+      __syncwarp();
+      if (lane == 0) mbar_arrive(p_ready(x));
+    }
+    if (ok && n_kv > 0 && mbar_wait(pv_done(x), (n_kv - 1) & 1, 28)) {
+      tc_fence_after();
+      const int qrow = it.tile_start + x * BT + row;
+      const bool store = qrow < it.seg_len;
+      const float inv_l = l > 0.f ? 1.f / l : 0.f;
+      __nv_bfloat16* dst = out + ((size_t)(it.seg_start + qrow) * H + h) * D;
+#pragma unroll
+      for (int c = 0; c < 4; ++c) {
+        uint32_t r[32];
+        tmem_ld32(tO + c * 32, r);
+        tmem_ld_wait();
+        if (store) {
+#pragma unroll
+          for (int v = 0; v < 4; ++v) {
+            float o[8];
+#pragma unroll
+            for (int i = 0; i < 8; ++i) o[i] = __uint_as_float(r[v * 8 + i]) * inv_l;
+            store8(dst + c * 32 + v * 8, o);
+          }
+        }
+      }
+      if (store) lse[(size_t)h * L + it.seg_start + qrow] = (m_used + log2f(l)) * kLn2;
+    } else {
+      s_abort = 1;
+    }
+  }
+  tc_fence_before();
+  __syncthreads();
+  if (warp == 1) {
+    tc_fence_after();
+    tmem_dealloc(tmem, 512);
+  }
+}
+
+// ============================================================================ backward
+enum { MODE_DQ = 0, MODE_DKV = 1 };
+constexpr int BWD_THREADS = 192;  // warp 0 TMA, warp 1 MMA, warps 2..5 elementwise + epilogue
+constexpr int BWD_SMEM = 2 * TILE_BYTES /*outer*/ + RING * TILE_BYTES + 2 * TILE_BYTES /*P, dS*/ + 1024 + 256 +
+                         2 * BT * 4 /*per-column LSE, Delta*/;
+
+// Outer tile (resident): DQ -> (Q, dO) of a query tile; DKV -> (K, V) of a key tile.
+// Inner tiles (streamed): DQ -> (K_j, V_j); DKV -> (Q_i, dO_i).
+// X = outer0 * inner0^T (S or S^T), Y = outer1 * inner1^T (dP or dP^T).
+template <int MODE>
+__global__ void __launch_bounds__(BWD_THREADS, 1)
+attn_bwd_kernel(const __grid_constant__ CUtensorMap qmap, const __grid_constant__ CUtensorMap kmap,
+                const __grid_constant__ CUtensorMap vmap, const __grid_constant__ CUtensorMap domap,
+                const WorkItem* __restrict__ items, int L, int H, float scale, const float* __restrict__ lse,
+                const float* __restrict__ delta, __nv_bfloat16* __restrict__ out0, __nv_bfloat16* __restrict__ out1) {
+  extern __shared__ uint8_t smem_raw[];
+  uint8_t* smem = reinterpret_cast<uint8_t*>((reinterpret_cast<uintptr_t>(smem_raw) + 1023) & ~uintptr_t(1023));
+  uint8_t* sOuter = smem;                       // 2 tiles
+  uint8_t* sIn = sOuter + 2 * TILE_BYTES;       // RING tiles
+  uint8_t* sP = sIn + RING * TILE_BYTES;        // P (or P^T)
+  uint8_t* sdS = sP + TILE_BYTES;               // dS (or dS^T)
+  uint64_t* bars = reinterpret_cast<uint64_t*>(sdS + TILE_BYTES);
+  // bars: outer_full, in_full[3], in_empty[3], xy_full, p_ready, ds_ready, mma_done
+  uint32_t* tmem_slot = reinterpret_cast<uint32_t*>(bars + 12);
+  // DKV: LSE and Delta of the current query tile (per column)
+  float (*s_vec)[BT] = reinterpret_cast<float (*)[BT]>(reinterpret_cast<uint8_t*>(bars) + 256);
+  volatile int& s_abort = *reinterpret_cast<volatile int*>(bars + 13);
+
+  const WorkItem it = items[blockIdx.x];
+  const int h = blockIdx.y;
+  const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
+  const int n_in = (it.seg_len + BT - 1) / BT;
+  const float scale_log2 = scale * kLog2e;
+
+  const uint32_t outer_full = smem_u32(bars + 0);
+  auto in_full = [&](int s) { return smem_u32(bars + 1 + s); };
+  auto in_empty = [&](int s) { return smem_u32(bars + 4 + s); };
+  const uint32_t xy_full = smem_u32(bars + 7);
+  const uint32_t p_ready = smem_u32(bars + 8);
+  const uint32_t ds_ready = smem_u32(bars + 9);
+  const uint32_t mma_done = smem_u32(bars + 10);
+
+  if (threadIdx.x == 0) {
+    s_abort = 0;
+    mbar_init(outer_full, 1);
+    for (int s = 0; s < RING; ++s) {
+      mbar_init(in_full(s), 1);
+      mbar_init(in_empty(s), 1);
+    }
+    mbar_init(xy_full, 1);
+    mbar_init(p_ready, 4);
+    mbar_init(ds_ready, 4);
+    mbar_init(mma_done, 1);
+    fence_barrier_init();
+  }
+  if (warp == 1) {
+    tmem_alloc(smem_u32(tmem_slot), 512);
+    tmem_relinquish();
+  }
+  tc_fence_before();
+  __syncthreads();
+  tc_fence_after();
+  const uint32_t tmem = *tmem_slot;  // X 0, Y 128, ACC1 256, ACC2 384
+  const int col = h * D;
+  const CUtensorMap* outer_map0 = MODE == MODE_DQ ? &qmap : &kmap;
+  const CUtensorMap* outer_map1 = MODE == MODE_DQ ? &domap : &vmap;
+  const CUtensorMap* in_map0 = MODE == MODE_DQ ? &kmap : &qmap;
+  const CUtensorMap* in_map1 = MODE == MODE_DQ ? &vmap : &domap;
+
+  if (warp == 0) {
+    if (lane == 0) {
+      const int r0 = it.seg_start + it.tile_start;
+      mbar_expect_tx(outer_full, 2 * TILE_BYTES);
+      for (int x = 0; x < 2; ++x) {
+        const uint32_t dst = smem_u32(sOuter + x * TILE_BYTES);
+        const CUtensorMap* m = x == 0 ? outer_map0 : outer_map1;
+        tma_load_2d(dst, m, outer_full, col, r0);
+        tma_load_2d(dst + HALF_BYTES, m, outer_full, col + 64, r0);
+      }
+      int n = 0;
+      for (int j = 0; j < n_in && !s_abort; ++j) {
+        for (int w = 0; w < 2; ++w, ++n) {
+          const int slot = n % RING;
+          if (!mbar_wait(in_empty(slot), ((n / RING) & 1) ^ 1, 31)) { s_abort = 1; break; }
+          const uint32_t fb = in_full(slot);
+          mbar_expect_tx(fb, TILE_BYTES);
+          const uint32_t dst = smem_u32(sIn + slot * TILE_BYTES);
+          const CUtensorMap* m = w == 0 ? in_map0 : in_map1;
+          const int row = it.seg_start + j * BT;
+          tma_load_2d(dst, m, fb, col, row);
+          tma_load_2d(dst + HALF_BYTES, m, fb, col + 64, row);
+        }
+      }
+    }
+  } else if (warp == 1) {
+    if (lane == 0) {
+      const uint32_t id_kk = idesc_bf16_f32(128, 128, 0, 0);  // X, Y: both operands K-major (over D)
+      const uint32_t id_km = idesc_bf16_f32(128, 128, 0, 1);  // acc += P/dS (K-major) * T (MN-major)
+      bool ok = mbar_wait(outer_full, 0, 32);
+      tc_fence_after();
+      const uint32_t o0 = smem_u32(sOuter), o1 = smem_u32(sOuter + TILE_BYTES);
+      const uint32_t pb = smem_u32(sP), db = smem_u32(sdS);
+      int n = 0;
+      for (int j = 0; j < n_in && ok; ++j) {
+        const int s0 = n % RING, s1 = (n + 1) % RING;
+        if (!(ok = mbar_wait(in_full(s0), (n / RING) & 1, 33))) break;
+        if (!(ok = mbar_wait(in_full(s1), ((n + 1) / RING) & 1, 33))) break;
+        tc_fence_after();
+        const uint32_t i0 = smem_u32(sIn + s0 * TILE_BYTES), i1 = smem_u32(sIn + s1 * TILE_BYTES);
+        // previous iteration's accumulate GEMMs must have read P/dS before they are rewritten;
+        // the elementwise warps wait on mma_done before writing, so X/Y may be issued now.
+#pragma unroll
+        for (int kk = 0; kk < D / 16; ++kk) mma_bf16_ss(tmem + 0, desc_kmajor(o0, kk), desc_kmajor(i0, kk), id_kk, kk > 0);
+#pragma unroll
+        for (int kk = 0; kk < D / 16; ++kk) mma_bf16_ss(tmem + 128, desc_kmajor(o1, kk), desc_kmajor(i1, kk), id_kk, kk > 0);
+        mma_commit(xy_full);
+        if (MODE == MODE_DKV) {
+          // dV += P^T dO_i   (dO_i = inner1 as MN-major B)
+          if (!(ok = mbar_wait(p_ready, j & 1, 34))) break;
+          tc_fence_after();
+#pragma unroll
+          for (int kk = 0; kk < BT / 16; ++kk)
+            mma_bf16_ss(tmem + 256, desc_kmajor(pb, kk), desc_mnmajor(i1, kk), id_km, j > 0 || kk > 0);
+        }
+        if (!(ok = mbar_wait(ds_ready, j & 1, 35))) break;
+        tc_fence_after();
+        if (MODE == MODE_DQ) {
+          // dQ += dS K_j   (K_j = inner0 as MN-major B)
+#pragma unroll
+          for (int kk = 0; kk < BT / 16; ++kk)
+            mma_bf16_ss(tmem + 256, desc_kmajor(db, kk), desc_mnmajor(i0, kk), id_km, j > 0 || kk > 0);
+        } else {
+          // dK += dS^T Q_i  (Q_i = inner0 as MN-major B)
+#pragma unroll
+          for (int kk = 0; kk < BT / 16; ++kk)
+            mma_bf16_ss(tmem + 384, desc_kmajor(db, kk), desc_mnmajor(i0, kk), id_km, j > 0 || kk > 0);
+        }
+        mma_commit(mma_done);
+        mma_commit(in_empty(s0));
+        mma_commit(in_empty(s1));
+        n += 2;
+      }
+      if (!ok) s_abort = 1;
+    }
+  } else {
+    // ------------------------------------------------------------ elementwise + epilogue
+    const int quarter = warp & 3;
+    const int row = quarter * 32 + lane;  // row of the outer tile
+    const uint32_t lane_off = (uint32_t)(quarter * 32) << 16;
+    const int orow = it.tile_start + row;  // row within the segment
+    const bool row_valid = orow < it.seg_len;
+    float row_lse = 0.f, row_delta = 0.f;
+    if (MODE == MODE_DQ && row_valid) {
+      row_lse = lse[(size_t)h * L + it.seg_start + orow] * kLog2e;
+      row_delta = delta[(size_t)h * L + it.seg_start + orow];
+    }
+    const int tid = threadIdx.x - 64;
+    bool ok = true;
+    for (int j = 0; j < n_in; ++j) {
+      const int valid_cols = min(BT, it.seg_len - j * BT);
+      if (MODE == MODE_DKV) {
+        // per-column (query) LSE and Delta of inner tile j; previous readers are done once
+        // mma_done(j-1) has been observed below
+        if (j > 0) {
+          if (!(ok = mbar_wait(mma_done, (j - 1) & 1, 36))) break;
+        }
+        asm volatile("bar.sync 1, 128;" ::: "memory");
+        if (tid < BT) {
+          const int qi = j * BT + tid;
+          s_vec[0][tid] = qi < it.seg_len ? lse[(size_t)h * L + it.seg_start + qi] * kLog2e : 0.f;
+          s_vec[1][tid] = qi < it.seg_len ? delta[(size_t)h * L + it.seg_start + qi] : 0.f;
+        }
+        asm volatile("bar.sync 1, 128;" ::: "memory");
+      } else if (j > 0) {
+        if (!(ok = mbar_wait(mma_done, (j - 1) & 1, 36))) break;
+      }
+      if (!(ok = mbar_wait(xy_full, j & 1, 37))) break;
+      tc_fence_after();
+      // P = exp2(X * scale*log2e - lse*log2e); masked columns / rows -> 0
+#pragma unroll
+      for (int c = 0; c < 4; ++c) {
+        uint32_t r[32], y[32];
+        tmem_ld32(tmem + lane_off + c * 32, r);
+        tmem_ld32(tmem + 128 + lane_off + c * 32, y);
+        tmem_ld_wait();
+        uint32_t wp[16], wd[16];
+#pragma unroll
+        for (int i = 0; i < 32; i += 2) {
+          float pv[2], dsv[2];
+#pragma unroll
+          for (int e = 0; e < 2; ++e) {
+            const int cc = c * 32 + i + e;
+            const bool ok_col = cc < valid_cols && row_valid;
+            const float lse2 = MODE == MODE_DQ ? row_lse : s_vec[0][cc];
+            const float dl = MODE == MODE_DQ ? row_delta : s_vec[1][cc];
+            const float p = ok_col ? exp2f(__uint_as_float(r[i + e]) * scale_log2 - lse2) : 0.f;
+            pv[e] = p;
+            dsv[e] = p * (__uint_as_float(y[i + e]) - dl);
+          }
+          wp[i >> 1] = pack_bf16(pv[0], pv[1]);
+          wd[i >> 1] = pack_bf16(dsv[0], dsv[1]);
+        }
+        if (MODE == MODE_DKV) store_row32_swizzled(sP, row, c * 32, wp);
+        store_row32_swizzled(sdS, row, c * 32, wd);
+      }
+      fence_async_smem();
+      tc_fence_before();
+      __syncwarp();
+      if (lane == 0) {
+        if (MODE == MODE_DKV) mbar_arrive(p_ready);
+        mbar_arrive(ds_ready);
+      }
+    }
+    if (ok && n_in > 0 && mbar_wait(mma_done, (n_in - 1) & 1, 38)) {
+      tc_fence_after();
+      const size_t grow = (size_t)(it.seg_start + orow) * H + h;
+      // DQ: out0 = dQ * scale.  DKV: out0 = dK * scale (ACC2), out1 = dV (ACC1).
+      for (int which = 0; which < (MODE == MODE_DQ ? 1 : 2); ++which) {
+        const uint32_t tacc = tmem + (MODE == MODE_DQ ? 256 : (which == 0 ? 384 : 256)) + lane_off;
+        const float mul = (which == 0) ? scale : 1.f;
+        __nv_bfloat16* dst = (which == 0 ? out0 : out1) + grow * D;
+#pragma unroll
+        for (int c = 0; c < 4; ++c) {
+          uint32_t r[32];
+          tmem_ld32(tacc + c * 32, r);
+          tmem_ld_wait();
+          if (row_valid) {
+#pragma unroll
+            for (int v = 0; v < 4; ++v) {
+              float o[8];
+#pragma unroll
+              for (int i = 0; i < 8; ++i) o[i] = __uint_as_float(r[v * 8 + i]) * mul;
+              store8(dst + c * 32 + v * 8, o);
+            }
+          }
+        }
+      }
+    } else {
+      s_abort = 1;
+    }
+  }
+  tc_fence_before();
+  __syncthreads();
+  if (warp == 1) {
+    tc_fence_after();
+    tmem_dealloc(tmem, 512);
+  }
+}
+
+// Delta[h, i] = sum_d dO[i, h, d] * O[i, h, d]  (fp32), one warp per (row, head).
+__global__ void attn_bwd_delta_kernel(const __nv_bfloat16* __restrict__ o, const __nv_bfloat16* __restrict__ dout,
+                                      int L, int H, float* __restrict__ delta) {
+  const int lane = threadIdx.x & 31;
+  const int w = (blockIdx.x * blockDim.x + threadIdx.x) >> 5;
+  if (w >= L * H) return;
+  const int row = w / H, h = w % H;
+  const size_t base = ((size_t)row * H + h) * D + lane * 4;
+  const uint2 a = *reinterpret_cast<const uint2*>(o + base);
+  const uint2 b = *reinterpret_cast<const uint2*>(dout + base);
+  const float2 a0 = __bfloat1622float2(*reinterpret_cast<const __nv_bfloat162*>(&a.x));
+  const float2 a1 = __bfloat1622float2(*reinterpret_cast<const __nv_bfloat162*>(&a.y));
+  const float2 b0 = __bfloat1622float2(*reinterpret_cast<const __nv_bfloat162*>(&b.x));
+  const float2 b1 = __bfloat1622float2(*reinterpret_cast<const __nv_bfloat162*>(&b.y));
+  float s = a0.x * b0.x + a0.y * b0.y + a1.x * b1.x + a1.y * b1.y;
+  s = warp_sum(s);
+  if (lane == 0) delta[(size_t)h * L + row] = s;
+}
+
+// ---------------------------------------------------------------------------- host helpers
+typedef CUresult (*EncodeTiledFn)(CUtensorMap*, CUtensorMapDataType, cuuint32_t, void*, const cuuint64_t*,
+                                  const cuuint64_t*, const cuuint32_t*, const cuuint32_t*, CUtensorMapInterleave,
+                                  CUtensorMapSwizzle, CUtensorMapL2promotion, CUtensorMapFloatOOBfill);
+
+const char* make_qkv_map(CUtensorMap* m, const void* base, int L, int H) {
+  static EncodeTiledFn fn = nullptr;
+  if (fn == nullptr) {
+    void* ptr = nullptr;
+    cudaDriverEntryPointQueryResult q;
+    if (cudaGetDriverEntryPoint("cuTensorMapEncodeTiled", &ptr, cudaEnableDefault, &q) != cudaSuccess || !ptr)
+      return "cuTensorMapEncodeTiled is unavailable";
+    fn = reinterpret_cast<EncodeTiledFn>(ptr);
+  }
+  if (reinterpret_cast<uintptr_t>(base) % 16) return "attention: tensor base must be 16-byte aligned";
+  cuuint64_t dims[2] = {(cuuint64_t)H * D, (cuuint64_t)L};
+  cuuint64_t strides[1] = {(cuuint64_t)H * D * 2};
+  cuuint32_t box[2] = {64, BT};
+  cuuint32_t estr[2] = {1, 1};
+  CUresult r = fn(m, CU_TENSOR_MAP_DATA_TYPE_BFLOAT16, 2, const_cast<void*>(base), dims, strides, box, estr,
+                  CU_TENSOR_MAP_INTERLEAVE_NONE, CU_TENSOR_MAP_SWIZZLE_128B, CU_TENSOR_MAP_L2_PROMOTION_L2_256B,
+                  CU_TENSOR_MAP_FLOAT_OOB_FILL_NONE);
+  return r == CUDA_SUCCESS ? nullptr : "cuTensorMapEncodeTiled failed (attention)";
+}
+
+}  // namespace attn
+
+const char* launch_attn_fwd(const void* q, const void* k, const void* v, const int* items, int n_items, int L, int H,
+                            int head_dim, float scale, void* out, float* lse, cudaStream_t s) {
+  using namespace attn;
+  if (head_dim != D) return "attention: head_dim must be 128";
+  if (n_items == 0) return nullptr;
+  CUtensorMap qm, km, vm;
+  const char* e;
+  if ((e = make_qkv_map(&qm, q, L, H)) || (e = make_qkv_map(&km, k, L, H)) || (e = make_qkv_map(&vm, v, L, H))) return e;
+  static bool attr = false;
+  if (!attr) {
+    if (cudaFuncSetAttribute(attn_fwd_kernel, cudaFuncAttributeMaxDynamicSharedMemorySize, FWD_SMEM) != cudaSuccess)
+      return "attention: cannot set smem size";
+    attr = true;
+  }
+  dim3 grid(n_items, H);
+  attn_fwd_kernel<<<grid, FWD_THREADS, FWD_SMEM, s>>>(qm, km, vm, reinterpret_cast<const WorkItem*>(items), L, H,
+                                                      scale * kLog2e, (__nv_bfloat16*)out, lse);
+  return cudaGetLastError() == cudaSuccess ? nullptr : "attention forward launch failed";
+}
+
+const char* launch_attn_bwd(const void* q, const void* k, const void* v, const void* o, const void* dout,
+                            const float* lse, const int* items_q, int n_items_q, const int* items_kv, int n_items_kv,
+                            int L, int H, int head_dim, float scale, float* delta, void* dq, void* dk, void* dv,
+                            cudaStream_t s) {
+  using namespace attn;
+  if (head_dim != D) return "attention: head_dim must be 128";
+  const int warps = L * H;
+  attn_bwd_delta_kernel<<<(warps * 32 + 255) / 256, 256, 0, s>>>((const __nv_bfloat16*)o,
+                                                                 (const __nv_bfloat16*)dout, L, H, delta);
+  CUtensorMap qm, km, vm, dom;
+  const char* e;
+  if ((e = make_qkv_map(&qm, q, L, H)) || (e = make_qkv_map(&km, k, L, H)) || (e = make_qkv_map(&vm, v, L, H)) ||
+      (e = make_qkv_map(&dom, dout, L, H)))
+    return e;
+  static bool attr = false;
+  if (!attr) {
+    if (cudaFuncSetAttribute(attn_bwd_kernel<MODE_DQ>, cudaFuncAttributeMaxDynamicSharedMemorySize, BWD_SMEM) !=
+            cudaSuccess ||
+        cudaFuncSetAttribute(attn_bwd_kernel<MODE_DKV>, cudaFuncAttributeMaxDynamicSharedMemorySize, BWD_SMEM) !=
+            cudaSuccess)
+      return "attention: cannot set smem size";
+    attr = true;
+  }
+  if (n_items_q > 0)
+    attn_bwd_kernel<MODE_DQ><<<dim3(n_items_q, H), BWD_THREADS, BWD_SMEM, s>>>(
+        qm, km, vm, dom, reinterpret_cast<const WorkItem*>(items_q), L, H, scale, lse, delta, (__nv_bfloat16*)dq,
+        nullptr);
+  if (n_items_kv > 0)
+    attn_bwd_kernel<MODE_DKV><<<dim3(n_items_kv, H), BWD_THREADS, BWD_SMEM, s>>>(
+        qm, km, vm, dom, reinterpret_cast<const WorkItem*>(items_kv), L, H, scale, lse, delta, (__nv_bfloat16*)dk,
+        (__nv_bfloat16*)dv);
+  return cudaGetLastError() == cudaSuccess ? nullptr : "attention backward launch failed";
+}
+
+int attn_error_flag(bool reset) {
+  int v = 0;
+  cudaMemcpyFromSymbol(&v, sm100::g_error_flag, sizeof(int));
+  if (reset) {
+    int z = 0;
+    cudaMemcpyToSymbol(sm100::g_error_flag, &z, sizeof(int));
+  }
+  return v;
+}
+
+}  // namespace pan

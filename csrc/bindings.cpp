@@ -16,6 +16,29 @@ const char* launch_qkv_post_bwd(const void* dq, const void* dk, const void* dv, 
                                 int na, int L, int H, int D, float eps, void* draw, float* dqw, float* dkw,
                                 cudaStream_t s);
 
+const char* launch_attn_fwd(const void* q, const void* k, const void* v, const int* items, int n_items, int L, int H,
+                            int head_dim, float scale, void* out, float* lse, cudaStream_t s);
+const char* launch_attn_bwd(const void* q, const void* k, const void* v, const void* o, const void* dout,
+                            const float* lse, const int* items_q, int n_items_q, const int* items_kv, int n_items_kv,
+                            int L, int H, int head_dim, float scale, float* delta, void* dq, void* dk, void* dv,
+                            cudaStream_t s);
+int attn_error_flag(bool reset);
+void launch_sumsq(const void* x, bool fp32, size_t n, float* partial, int n_part, cudaStream_t s);
+void launch_reduce_clip(const float* partial, int n, float max_norm, float* out, cudaStream_t s);
+void launch_muon_momentum(float* buf, const void* g, bool g_fp32, const float* clip, float mu, size_t n, void* u,
+                          cudaStream_t s);
+void launch_muon_update(void* hi, void* lo, const void* u, const float* lr, float lr_scale, float wd, size_t n,
+                        cudaStream_t s);
+void launch_adamw_update(void* hi, void* lo, const void* g, bool g_fp32, float* m, float* v, const float* clip,
+                         const float* lr, float beta1, float beta2, float eps, float wd, float bc1, float bc2_sqrt,
+                         size_t n, cudaStream_t s);
+void launch_split_master(const float* x, void* hi, void* lo, size_t n, cudaStream_t s);
+void launch_join_master(const void* hi, const void* lo, float* x, size_t n, cudaStream_t s);
+void launch_trace(const float* R, int batch, int M, float* out, cudaStream_t s);
+void launch_gram_normalize(const float* R, const float* norm2, int batch, int M, float eps, void* Rn, cudaStream_t s);
+void launch_add_diag(void* Z, int batch, int M, float a, cudaStream_t s);
+void launch_scale_by_invnorm(void* Q, const float* norm2, int batch, int M, float eps, cudaStream_t s);
+
 namespace {
 
 cudaStream_t stream() { return at::cuda::getCurrentCUDAStream(); }
@@ -123,7 +146,9 @@ std::vector<torch::Tensor> simple_concat_fwd(torch::Tensor vid, torch::Tensor tx
 
 torch::Tensor segment_sum(torch::Tensor x, torch::Tensor bounds, int64_t n_seg) {
   const at::cuda::CUDAGuard guard(x.device());
-  check_rows(x, "x");
+  TORCH_CHECK(x.is_cuda() && x.scalar_type() == torch::kBFloat16 && x.dim() == 2 && x.is_contiguous() &&
+                  x.size(1) % 8 == 0,
+              "segment_sum: x must be a contiguous bf16 [L, C] CUDA tensor with C % 8 == 0");
   check_i32(bounds, "bounds");
   auto out = torch::zeros({n_seg, x.size(1)}, x.options().dtype(torch::kFloat32));
   launch_segment_sum(x.data_ptr(), bounds.data_ptr<int>(), n_seg, x.size(0), x.size(1), out.data_ptr<float>(),
@@ -240,6 +265,58 @@ void gemm(torch::Tensor A, torch::Tensor B, torch::Tensor D, bool a_kmajor, bool
   check_launch(launch_gemm(a, stream()), "gemm");
 }
 
+// Batched D[b] = alpha * A[b] @ B[b]^T + beta * C[b] over 3-D tensors [batch, rows, cols] (row-major
+// in the last two dims); operand majors as in gemm().  C may alias D.
+void gemm_batched(torch::Tensor A, torch::Tensor B, torch::Tensor D, bool a_kmajor, bool b_kmajor, double alpha,
+                  double beta, c10::optional<torch::Tensor> C) {
+  const at::cuda::CUDAGuard guard(A.device());
+  TORCH_CHECK(A.dim() == 3 && B.dim() == 3 && D.dim() == 3, "gemm_batched expects 3-D tensors");
+  TORCH_CHECK(A.size(0) == B.size(0) && A.size(0) == D.size(0), "batch mismatch");
+  for (const auto* t : {&A, &B}) {
+    TORCH_CHECK(t->is_cuda() && t->scalar_type() == torch::kBFloat16 && t->stride(2) == 1, "operands: bf16, row-major");
+  }
+  TORCH_CHECK(D.stride(2) == 1 && (D.scalar_type() == torch::kBFloat16 || D.scalar_type() == torch::kFloat32),
+              "D must be bf16/fp32 row-major");
+  GemmArgs a{};
+  a.A = A.data_ptr();
+  a.lda = A.stride(1);
+  a.a_mn = a_kmajor ? 0 : 1;
+  a.M = a_kmajor ? A.size(1) : A.size(2);
+  a.K = a_kmajor ? A.size(2) : A.size(1);
+  a.D = D.data_ptr();
+  a.ldd = D.stride(1);
+  a.d_fp32 = D.scalar_type() == torch::kFloat32;
+  a.b_mn = b_kmajor ? 0 : 1;
+  a.n_groups = 1;
+  GemmGroup& gr = a.groups[0];
+  gr.B = B.data_ptr();
+  gr.ldb = B.stride(1);
+  gr.n = b_kmajor ? B.size(1) : B.size(2);
+  gr.k = b_kmajor ? B.size(2) : B.size(1);
+  gr.row_begin = 0;
+  gr.row_end = a.M;
+  gr.bias = nullptr;
+  TORCH_CHECK(gr.k == a.K, "K mismatch");
+  TORCH_CHECK(D.size(1) >= a.M && D.size(2) >= gr.n, "D too small");
+  a.batch = A.size(0);
+  a.a_bstride = A.stride(0);
+  a.b_bstride = B.stride(0);
+  a.d_bstride = D.stride(0);
+  a.alpha = (float)alpha;
+  a.beta = (float)beta;
+  if (C.has_value() && beta != 0.0) {
+    const auto& c = C.value();
+    TORCH_CHECK(c.dim() == 3 && c.stride(2) == 1 &&
+                    (c.scalar_type() == torch::kBFloat16 || c.scalar_type() == torch::kFloat32),
+                "C must be a row-major bf16/fp32 3-D tensor");
+    a.C = c.data_ptr();
+    a.ldc = c.stride(1);
+    a.c_bstride = c.stride(0);
+    a.c_fp32 = c.scalar_type() == torch::kFloat32;
+  }
+  check_launch(launch_gemm(a, stream()), "gemm_batched");
+}
+
 void gemm_grouped_nt(torch::Tensor A, std::vector<torch::Tensor> Bs, torch::Tensor D,
                      std::vector<c10::optional<torch::Tensor>> biases, c10::optional<torch::Tensor> gelu_pre,
                      std::vector<int64_t> bounds) {
@@ -331,7 +408,162 @@ std::vector<torch::Tensor> qkv_post_bwd(torch::Tensor dq, torch::Tensor dk, torc
   return {draw, dqw, dkw};
 }
 
-int error_flag(bool reset) { return gemm_error_flag(reset) | packed_ops_error_flag(reset); }
+// ------------------------------------------------------------------ attention
+namespace {
+void check_qkv(const torch::Tensor& t, const char* name) {
+  TORCH_CHECK(t.is_cuda() && t.scalar_type() == torch::kBFloat16 && t.dim() == 3 && t.is_contiguous(), name,
+              " must be a contiguous bf16 CUDA [L, H, D] tensor");
+}
+}  // namespace
+
+// items: int32 [n, 4] = (segment start, segment length, first row of the tile, 0)
+std::vector<torch::Tensor> attn_fwd(torch::Tensor q, torch::Tensor k, torch::Tensor v, torch::Tensor items,
+                                    int64_t n_valid, double scale) {
+  const at::cuda::CUDAGuard guard(q.device());
+  check_qkv(q, "q");
+  check_qkv(k, "k");
+  check_qkv(v, "v");
+  check_i32(items, "items");
+  const int L = q.size(0), H = q.size(1), D = q.size(2);
+  auto o = torch::empty_like(q);
+  auto lse = torch::empty({H, L}, q.options().dtype(torch::kFloat32));
+  if (n_valid < L) o.narrow(0, n_valid, L - n_valid).zero_();
+  check_launch(launch_attn_fwd(q.data_ptr(), k.data_ptr(), v.data_ptr(), items.data_ptr<int>(), items.size(0), L, H, D,
+                               (float)scale, o.data_ptr(), lse.data_ptr<float>(), stream()),
+               "attn_fwd");
+  return {o, lse};
+}
+
+std::vector<torch::Tensor> attn_bwd(torch::Tensor dout, torch::Tensor q, torch::Tensor k, torch::Tensor v,
+                                    torch::Tensor o, torch::Tensor lse, torch::Tensor items_q, torch::Tensor items_kv,
+                                    int64_t n_valid, double scale) {
+  const at::cuda::CUDAGuard guard(q.device());
+  check_qkv(dout, "dout");
+  check_qkv(q, "q");
+  check_qkv(o, "o");
+  const int L = q.size(0), H = q.size(1), D = q.size(2);
+  auto dq = torch::empty_like(q);
+  auto dk = torch::empty_like(k);
+  auto dv = torch::empty_like(v);
+  if (n_valid < L) {
+    dq.narrow(0, n_valid, L - n_valid).zero_();
+    dk.narrow(0, n_valid, L - n_valid).zero_();
+    dv.narrow(0, n_valid, L - n_valid).zero_();
+  }
+  auto delta = torch::empty({H, L}, q.options().dtype(torch::kFloat32));
+  check_launch(launch_attn_bwd(q.data_ptr(), k.data_ptr(), v.data_ptr(), o.data_ptr(), dout.data_ptr(),
+                               lse.data_ptr<float>(), items_q.data_ptr<int>(), items_q.size(0),
+                               items_kv.data_ptr<int>(), items_kv.size(0), L, H, D, (float)scale,
+                               delta.data_ptr<float>(), dq.data_ptr(), dk.data_ptr(), dv.data_ptr(), stream()),
+               "attn_bwd");
+  return {dq, dk, dv};
+}
+
+// ------------------------------------------------------------------ optimizer
+namespace {
+void check_half16(const torch::Tensor& t, const char* name) {
+  TORCH_CHECK(t.is_cuda() && t.element_size() == 2 && t.is_contiguous(), name, " must be a contiguous 16-bit CUDA tensor");
+}
+const float* opt_ptr(const c10::optional<torch::Tensor>& t) { return t.has_value() ? t.value().data_ptr<float>() : nullptr; }
+}  // namespace
+
+// partial sums of squares of x (bf16 or fp32) appended into `partial` (fp32 [n_part]).
+void sumsq_partial(torch::Tensor x, torch::Tensor partial) {
+  const at::cuda::CUDAGuard guard(x.device());
+  TORCH_CHECK(x.is_contiguous() && (x.scalar_type() == torch::kBFloat16 || x.scalar_type() == torch::kFloat32), "x");
+  TORCH_CHECK(partial.scalar_type() == torch::kFloat32 && partial.is_contiguous(), "partial must be fp32");
+  if (x.numel() == 0) {
+    partial.zero_();
+    return;
+  }
+  launch_sumsq(x.data_ptr(), x.scalar_type() == torch::kFloat32, x.numel(), partial.data_ptr<float>(),
+               partial.numel(), stream());
+  check_launch(nullptr, "sumsq");
+}
+
+// out[0] = sqrt(sum(partials)), out[1] = min(1, max_norm / (out[0] + 1e-6))
+void norm_and_clip(torch::Tensor partials, double max_norm, torch::Tensor out) {
+  const at::cuda::CUDAGuard guard(partials.device());
+  launch_reduce_clip(partials.data_ptr<float>(), partials.numel(), (float)max_norm, out.data_ptr<float>(), stream());
+  check_launch(nullptr, "norm_and_clip");
+}
+
+void muon_momentum(torch::Tensor buf, torch::Tensor g, c10::optional<torch::Tensor> clip, double mu, torch::Tensor u) {
+  const at::cuda::CUDAGuard guard(buf.device());
+  TORCH_CHECK(buf.scalar_type() == torch::kFloat32 && buf.is_contiguous() && g.is_contiguous() && u.is_contiguous(),
+              "muon_momentum: contiguous fp32 buffer");
+  TORCH_CHECK(buf.numel() == g.numel() && u.numel() == g.numel(), "muon_momentum: size mismatch");
+  launch_muon_momentum(buf.data_ptr<float>(), g.data_ptr(), g.scalar_type() == torch::kFloat32, opt_ptr(clip),
+                       (float)mu, g.numel(), u.data_ptr(), stream());
+  check_launch(nullptr, "muon_momentum");
+}
+
+void muon_update(torch::Tensor hi, torch::Tensor lo, torch::Tensor u, torch::Tensor lr, double lr_scale, double wd) {
+  const at::cuda::CUDAGuard guard(hi.device());
+  check_half16(hi, "hi");
+  check_half16(lo, "lo");
+  TORCH_CHECK(u.numel() == hi.numel() && lo.numel() == hi.numel(), "muon_update: size mismatch");
+  launch_muon_update(hi.data_ptr(), lo.data_ptr(), u.data_ptr(), lr.data_ptr<float>(), (float)lr_scale, (float)wd,
+                     hi.numel(), stream());
+  check_launch(nullptr, "muon_update");
+}
+
+void adamw_update(torch::Tensor hi, torch::Tensor lo, torch::Tensor g, torch::Tensor m, torch::Tensor v,
+                  c10::optional<torch::Tensor> clip, torch::Tensor lr, double beta1, double beta2, double eps,
+                  double wd, int64_t step) {
+  const at::cuda::CUDAGuard guard(hi.device());
+  check_half16(hi, "hi");
+  check_half16(lo, "lo");
+  TORCH_CHECK(g.numel() == hi.numel() && m.numel() == hi.numel() && v.numel() == hi.numel(), "adamw: size mismatch");
+  const double bc1 = 1.0 - std::pow(beta1, (double)step);
+  const double bc2 = 1.0 - std::pow(beta2, (double)step);
+  launch_adamw_update(hi.data_ptr(), lo.data_ptr(), g.data_ptr(), g.scalar_type() == torch::kFloat32,
+                      m.data_ptr<float>(), v.data_ptr<float>(), opt_ptr(clip), lr.data_ptr<float>(), (float)beta1,
+                      (float)beta2, (float)eps, (float)wd, (float)bc1, (float)std::sqrt(bc2), hi.numel(), stream());
+  check_launch(nullptr, "adamw_update");
+}
+
+void split_master(torch::Tensor x, torch::Tensor hi, torch::Tensor lo) {
+  const at::cuda::CUDAGuard guard(x.device());
+  TORCH_CHECK(x.scalar_type() == torch::kFloat32 && x.is_contiguous() && x.numel() == hi.numel(), "split_master");
+  launch_split_master(x.data_ptr<float>(), hi.data_ptr(), lo.data_ptr(), x.numel(), stream());
+  check_launch(nullptr, "split_master");
+}
+
+void join_master(torch::Tensor hi, torch::Tensor lo, torch::Tensor x) {
+  const at::cuda::CUDAGuard guard(x.device());
+  TORCH_CHECK(x.scalar_type() == torch::kFloat32 && x.is_contiguous() && x.numel() == hi.numel(), "join_master");
+  launch_join_master(hi.data_ptr(), lo.data_ptr(), x.data_ptr<float>(), x.numel(), stream());
+  check_launch(nullptr, "join_master");
+}
+
+// Newton-Schulz helpers over a batch of M x M Gram matrices
+void ns_trace(torch::Tensor R, torch::Tensor out) {
+  const at::cuda::CUDAGuard guard(R.device());
+  TORCH_CHECK(R.scalar_type() == torch::kFloat32 && R.dim() == 3 && R.is_contiguous(), "R must be fp32 [B, M, M]");
+  launch_trace(R.data_ptr<float>(), R.size(0), R.size(1), out.data_ptr<float>(), stream());
+  check_launch(nullptr, "ns_trace");
+}
+void ns_gram_normalize(torch::Tensor R, torch::Tensor norm2, double eps, torch::Tensor Rn) {
+  const at::cuda::CUDAGuard guard(R.device());
+  launch_gram_normalize(R.data_ptr<float>(), norm2.data_ptr<float>(), R.size(0), R.size(1), (float)eps, Rn.data_ptr(),
+                        stream());
+  check_launch(nullptr, "ns_gram_normalize");
+}
+void ns_add_diag(torch::Tensor Z, double a) {
+  const at::cuda::CUDAGuard guard(Z.device());
+  launch_add_diag(Z.data_ptr(), Z.size(0), Z.size(1), (float)a, stream());
+  check_launch(nullptr, "ns_add_diag");
+}
+void ns_scale_by_invnorm(torch::Tensor Q, torch::Tensor norm2, double eps) {
+  const at::cuda::CUDAGuard guard(Q.device());
+  launch_scale_by_invnorm(Q.data_ptr(), norm2.data_ptr<float>(), Q.size(0), Q.size(1), (float)eps, stream());
+  check_launch(nullptr, "ns_scale_by_invnorm");
+}
+
+int error_flag(bool reset) {
+  return gemm_error_flag(reset) | packed_ops_error_flag(reset) | attn_error_flag(reset);
+}
 
 }  // namespace pan
 
@@ -349,8 +581,22 @@ PYBIND11_MODULE(TORCH_EXTENSION_NAME, m) {
   m.def("gather_rows", &pan::gather_rows);
   m.def("gemm", &pan::gemm);
   m.def("gemm_grouped_nt", &pan::gemm_grouped_nt);
+  m.def("gemm_batched", &pan::gemm_batched);
   m.def("gemm_dgelu", &pan::gemm_dgelu);
   m.def("qkv_post_fwd", &pan::qkv_post_fwd);
   m.def("qkv_post_bwd", &pan::qkv_post_bwd);
+  m.def("attn_fwd", &pan::attn_fwd);
+  m.def("attn_bwd", &pan::attn_bwd);
+  m.def("sumsq_partial", &pan::sumsq_partial);
+  m.def("norm_and_clip", &pan::norm_and_clip);
+  m.def("muon_momentum", &pan::muon_momentum);
+  m.def("muon_update", &pan::muon_update);
+  m.def("adamw_update", &pan::adamw_update);
+  m.def("split_master", &pan::split_master);
+  m.def("join_master", &pan::join_master);
+  m.def("ns_trace", &pan::ns_trace);
+  m.def("ns_gram_normalize", &pan::ns_gram_normalize);
+  m.def("ns_add_diag", &pan::ns_add_diag);
+  m.def("ns_scale_by_invnorm", &pan::ns_scale_by_invnorm);
   m.def("error_flag", &pan::error_flag, py::arg("reset") = true);
 }

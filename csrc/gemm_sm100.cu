@@ -53,6 +53,15 @@ struct Params {
   long long ldaux2;
   int epi;
   int accumulate;
+  // batched GEMMs: operand z-coordinate = batch index; D/C advance by their batch strides
+  int batch;
+  int tiles_per_batch;
+  long long d_bstride;
+  // epilogue: out = alpha * acc + beta * C (+ bias); C may alias D
+  float alpha, beta;
+  const void* C;
+  long long ldc, c_bstride;
+  int c_fp32;
 };
 
 struct TmapSet {
@@ -61,6 +70,7 @@ struct TmapSet {
 };
 
 __device__ __forceinline__ void tile_coords(const Params& p, int t, int& g, int& mb, int& nb) {
+  t = t % p.tiles_per_batch;
   g = 0;
   while (g + 1 < p.n_groups && t >= p.tile_prefix[g + 1]) ++g;
   const int local = t - p.tile_prefix[g];
@@ -86,17 +96,17 @@ __device__ __forceinline__ float gelu_tanh_grad(float x) {
 
 __global__ void __launch_bounds__(kThreads, 1)
 gemm_kernel(const __grid_constant__ Params p, const __grid_constant__ TmapSet maps) {
-  extern __shared__ __align__(1024) uint8_t smem_raw[];
+  extern __shared__ uint8_t smem_raw[];
   uint8_t* smem = reinterpret_cast<uint8_t*>((reinterpret_cast<uintptr_t>(smem_raw) + 1023) & ~uintptr_t(1023));
   uint8_t* smem_a = smem;
   uint8_t* smem_b = smem + STAGES * A_STAGE;
   uint64_t* bars = reinterpret_cast<uint64_t*>(smem_b + STAGES * B_STAGE);
   // bars: full[S], empty[S], tmem_full[2], tmem_empty[2]; then the TMEM base address
   uint32_t* tmem_slot = reinterpret_cast<uint32_t*>(bars + 2 * STAGES + 4);
-  __shared__ volatile int s_abort;
+  volatile int& s_abort = *reinterpret_cast<volatile int*>(bars + 2 * STAGES + 5);
 
   const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
-  const int total_tiles = p.tile_prefix[p.n_groups];
+  const int total_tiles = p.tile_prefix[p.n_groups] * p.batch;
 
   auto full_bar = [&](int s) { return smem_u32(bars + s); };
   auto empty_bar = [&](int s) { return smem_u32(bars + STAGES + s); };
@@ -136,6 +146,7 @@ gemm_kernel(const __grid_constant__ Params p, const __grid_constant__ TmapSet ma
         tile_coords(p, t, g, mb, nb);
         const int m0 = p.row_begin[g] + mb * BM;
         const int n0 = nb * BN;
+        const int z = t / p.tiles_per_batch;
         const int k_blocks = p.k_blocks[g];
         for (int kb = 0; kb < k_blocks && !s_abort; ++kb) {
           if (!mbar_wait(empty_bar(stage), phase ^ 1, 11)) { s_abort = 1; break; }
@@ -145,16 +156,16 @@ gemm_kernel(const __grid_constant__ Params p, const __grid_constant__ TmapSet ma
           const uint32_t sb = smem_u32(smem_b + stage * B_STAGE);
           const int k0 = kb * BK;
           if (!p.a_mn) {
-            tma_load_2d(sa, &maps.a, fb, k0, m0);
+            tma_load_3d(sa, &maps.a, fb, k0, m0, z);
           } else {
-            tma_load_2d(sa, &maps.a, fb, m0, k0);
-            tma_load_2d(sa + 8192, &maps.a, fb, m0 + 64, k0);
+            tma_load_3d(sa, &maps.a, fb, m0, k0, z);
+            tma_load_3d(sa + 8192, &maps.a, fb, m0 + 64, k0, z);
           }
           if (!p.b_mn) {
-            tma_load_2d(sb, &maps.b[g], fb, k0, n0);
+            tma_load_3d(sb, &maps.b[g], fb, k0, n0, z);
           } else {
 #pragma unroll
-            for (int j = 0; j < 4; ++j) tma_load_2d(sb + j * 8192, &maps.b[g], fb, n0 + 64 * j, k0);
+            for (int j = 0; j < 4; ++j) tma_load_3d(sb + j * 8192, &maps.b[g], fb, n0 + 64 * j, k0, z);
           }
           if (++stage == STAGES) { stage = 0; phase ^= 1; }
         }
@@ -209,6 +220,7 @@ gemm_kernel(const __grid_constant__ Params p, const __grid_constant__ TmapSet ma
       tc_fence_after();
       int g, mb, nb;
       tile_coords(p, t, g, mb, nb);
+      const long long zb = t / p.tiles_per_batch;
       const int row = p.row_begin[g] + mb * BM + q * 32 + lane;
       const bool row_ok = row < p.row_end[g];
       const int n_lim = p.n_cols[g];
@@ -226,7 +238,21 @@ gemm_kernel(const __grid_constant__ Params p, const __grid_constant__ TmapSet ma
           if (c >= n_lim) break;
           float o[8];
 #pragma unroll
-          for (int i = 0; i < 8; ++i) o[i] = __uint_as_float(r[v8 * 8 + i]);
+          for (int i = 0; i < 8; ++i) o[i] = p.alpha * __uint_as_float(r[v8 * 8 + i]);
+          if (p.C != nullptr) {
+            float cv[8];
+            if (p.c_fp32) {
+              const float* cp = reinterpret_cast<const float*>(p.C) + zb * p.c_bstride + (size_t)row * p.ldc + c;
+              const float4 x0 = *reinterpret_cast<const float4*>(cp);
+              const float4 x1 = *reinterpret_cast<const float4*>(cp + 4);
+              cv[0] = x0.x; cv[1] = x0.y; cv[2] = x0.z; cv[3] = x0.w;
+              cv[4] = x1.x; cv[5] = x1.y; cv[6] = x1.z; cv[7] = x1.w;
+            } else {
+              load8(reinterpret_cast<const __nv_bfloat16*>(p.C) + zb * p.c_bstride + (size_t)row * p.ldc + c, cv);
+            }
+#pragma unroll
+            for (int i = 0; i < 8; ++i) o[i] += p.beta * cv[i];
+          }
           if (bias != nullptr) {
             float b[8];
             load8(bias + c, b);
@@ -251,7 +277,7 @@ gemm_kernel(const __grid_constant__ Params p, const __grid_constant__ TmapSet ma
             store8(p.aux2 + (size_t)row * p.ldaux2 + c, post);
           }
           if (p.d_fp32) {
-            float* d = reinterpret_cast<float*>(p.D) + (size_t)row * p.ldd + c;
+            float* d = reinterpret_cast<float*>(p.D) + zb * p.d_bstride + (size_t)row * p.ldd + c;
             if (p.accumulate) {
               const float4 x0 = *reinterpret_cast<const float4*>(d);
               const float4 x1 = *reinterpret_cast<const float4*>(d + 4);
@@ -261,7 +287,7 @@ gemm_kernel(const __grid_constant__ Params p, const __grid_constant__ TmapSet ma
             *reinterpret_cast<float4*>(d) = make_float4(o[0], o[1], o[2], o[3]);
             *reinterpret_cast<float4*>(d + 4) = make_float4(o[4], o[5], o[6], o[7]);
           } else {
-            __nv_bfloat16* d = reinterpret_cast<__nv_bfloat16*>(p.D) + (size_t)row * p.ldd + c;
+            __nv_bfloat16* d = reinterpret_cast<__nv_bfloat16*>(p.D) + zb * p.d_bstride + (size_t)row * p.ldd + c;
             if (p.accumulate) {
               float x[8];
               load8(d, x);
@@ -305,19 +331,21 @@ EncodeTiledFn encode_fn() {
   return fn;
 }
 
-// 2-D bf16 tensor map over a row-major [rows, cols] matrix (row stride `ld` elements), box
-// [box_rows, box_cols] with 128-byte swizzle (box_cols * 2 == 128).
+// 3-D bf16 tensor map over `batch` row-major [rows, cols] matrices (row stride `ld`, batch stride
+// `bstride` elements), box [1, box_rows, box_cols] with 128-byte swizzle (box_cols * 2 == 128).
 const char* make_map(CUtensorMap* m, const void* base, long long rows, long long cols, long long ld, int box_rows,
-                     int box_cols) {
+                     int box_cols, int batch = 1, long long bstride = 0) {
   if (reinterpret_cast<uintptr_t>(base) % 16 != 0) return "TMA base must be 16-byte aligned";
   if ((ld * 2) % 16 != 0) return "TMA row stride must be a multiple of 16 bytes";
+  if (batch > 1 && (bstride * 2) % 16 != 0) return "TMA batch stride must be a multiple of 16 bytes";
   EncodeTiledFn fn = encode_fn();
   if (fn == nullptr) return "cuTensorMapEncodeTiled is unavailable";
-  cuuint64_t dims[2] = {(cuuint64_t)cols, (cuuint64_t)rows};
-  cuuint64_t strides[1] = {(cuuint64_t)(ld * 2)};
-  cuuint32_t box[2] = {(cuuint32_t)box_cols, (cuuint32_t)box_rows};
-  cuuint32_t estr[2] = {1, 1};
-  CUresult r = fn(m, CU_TENSOR_MAP_DATA_TYPE_BFLOAT16, 2, const_cast<void*>(base), dims, strides, box, estr,
+  if (batch <= 1) bstride = ld * rows;
+  cuuint64_t dims[3] = {(cuuint64_t)cols, (cuuint64_t)rows, (cuuint64_t)(batch < 1 ? 1 : batch)};
+  cuuint64_t strides[2] = {(cuuint64_t)(ld * 2), (cuuint64_t)(bstride * 2)};
+  cuuint32_t box[3] = {(cuuint32_t)box_cols, (cuuint32_t)box_rows, 1};
+  cuuint32_t estr[3] = {1, 1, 1};
+  CUresult r = fn(m, CU_TENSOR_MAP_DATA_TYPE_BFLOAT16, 3, const_cast<void*>(base), dims, strides, box, estr,
                   CU_TENSOR_MAP_INTERLEAVE_NONE, CU_TENSOR_MAP_SWIZZLE_128B, CU_TENSOR_MAP_L2_PROMOTION_L2_256B,
                   CU_TENSOR_MAP_FLOAT_OOB_FILL_NONE);
   return r == CUDA_SUCCESS ? nullptr : "cuTensorMapEncodeTiled failed";
@@ -357,8 +385,25 @@ const char* launch_gemm(const GemmArgs& a, cudaStream_t stream) {
   p.ldaux = a.ldaux;
   p.aux2 = reinterpret_cast<__nv_bfloat16*>(a.aux2);
   p.ldaux2 = a.ldaux2;
+  p.batch = a.batch < 1 ? 1 : a.batch;
+  p.d_bstride = a.d_bstride;
+  p.alpha = a.alpha;
+  p.beta = a.beta;
+  p.C = a.C;
+  p.ldc = a.ldc;
+  p.c_bstride = a.c_bstride;
+  p.c_fp32 = a.c_fp32;
+  if (a.accumulate) {  // D += acc  ==  C = D, beta = 1
+    p.C = a.D;
+    p.ldc = a.ldd;
+    p.c_bstride = a.d_bstride;
+    p.c_fp32 = a.d_fp32;
+    p.beta = 1.f;
+  }
+  if (p.C != nullptr && (p.ldc % 8 != 0 && !p.c_fp32)) return "gemm: C row stride must be a multiple of 8";
   TmapSet maps;
-  const char* err = !a.a_mn ? make_map(&maps.a, a.A, a.M, a.K, a.lda, BM, BK) : make_map(&maps.a, a.A, a.K, a.M, a.lda, BK, 64);
+  const char* err = !a.a_mn ? make_map(&maps.a, a.A, a.M, a.K, a.lda, BM, BK, p.batch, a.a_bstride)
+                            : make_map(&maps.a, a.A, a.K, a.M, a.lda, BK, 64, p.batch, a.a_bstride);
   if (err) return err;
   int tiles = 0;
   p.tile_prefix[0] = 0;
@@ -367,7 +412,8 @@ const char* launch_gemm(const GemmArgs& a, cudaStream_t stream) {
     if (gr.k > a.K) return "gemm: group K must be <= K";
     if (gr.ldb % 8 != 0) return "gemm: B row stride must be a multiple of 8 elements";
     if (gr.n % 8 != 0) return "gemm: N must be a multiple of 8";
-    err = !a.b_mn ? make_map(&maps.b[g], gr.B, gr.n, gr.k, gr.ldb, BN, BK) : make_map(&maps.b[g], gr.B, gr.k, gr.n, gr.ldb, BK, 64);
+    err = !a.b_mn ? make_map(&maps.b[g], gr.B, gr.n, gr.k, gr.ldb, BN, BK, p.batch, a.b_bstride)
+                  : make_map(&maps.b[g], gr.B, gr.k, gr.n, gr.ldb, BK, 64, p.batch, a.b_bstride);
     if (err) return err;
     p.row_begin[g] = gr.row_begin;
     p.row_end[g] = gr.row_end;
@@ -381,6 +427,8 @@ const char* launch_gemm(const GemmArgs& a, cudaStream_t stream) {
     p.tile_prefix[g + 1] = tiles;
   }
   for (int g = G; g < kMaxGroups; ++g) maps.b[g] = maps.b[0];
+  p.tiles_per_batch = tiles;
+  tiles *= p.batch;
   if (tiles == 0) return nullptr;
   static bool attr_set = false;
   if (!attr_set) {

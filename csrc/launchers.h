@@ -53,7 +53,15 @@ struct GemmArgs {
   long long ldaux;
   void* aux2;
   long long ldaux2;
-  int accumulate;
+  int accumulate;        // D += ...  (same as C = D, beta = 1)
+  // batched: `batch` problems with element strides between consecutive A / B / D / C matrices
+  int batch = 1;
+  long long a_bstride = 0, b_bstride = 0, d_bstride = 0;
+  // out = alpha * acc + beta * C (+ bias)
+  float alpha = 1.f, beta = 0.f;
+  const void* C = nullptr;
+  long long ldc = 0, c_bstride = 0;
+  int c_fp32 = 0;
 };
 // Returns an error string (nullptr on success).
 const char* launch_gemm(const GemmArgs& args, cudaStream_t s);

@@ -97,5 +97,7 @@ class TimestepEncoder(nn.Module):
         self._rebuild_freqs()
 
     def forward(self, timestep: torch.Tensor) -> torch.Tensor:
+        from ..ops.gemm import linear
         sample = timestep_embedding(timestep, self.freqs).to(self.in_proj.weight.dtype)
-        return self.out_proj(self.act(self.in_proj(sample)))
+        h = self.act(linear(sample, self.in_proj.weight, self.in_proj.bias))
+        return linear(h, self.out_proj.weight, self.out_proj.bias)

@@ -20,19 +20,42 @@ import torch.nn.functional as F
 from ._ext import ext
 
 
+_ITEM_CACHE: dict = {}
+
+
+def work_items(lens: Sequence[int], rows_per_item: int, device) -> torch.Tensor:
+    """int32 ``[n, 4]`` work list ``(segment start, segment length, first tile row, 0)``: one entry
+    per ``rows_per_item`` rows of every non-empty segment.  Cached per (lens, tile, device)."""
+    key = (tuple(int(n) for n in lens), rows_per_item, str(device))
+    t = _ITEM_CACHE.get(key)
+    if t is None:
+        rows, start = [], 0
+        for n in key[0]:
+            for r0 in range(0, n, rows_per_item):
+                rows.append((start, n, r0, 0))
+            start += n
+        t = torch.tensor(rows if rows else [(0, 0, 0, 0)][:0], dtype=torch.int32).reshape(-1, 4).to(device)
+        if len(_ITEM_CACHE) > 256:
+            _ITEM_CACHE.clear()
+        _ITEM_CACHE[key] = t
+    return t
+
+
 class _VarlenAttnCUDA(torch.autograd.Function):
     @staticmethod
-    def forward(ctx, q, k, v, cu_seqlens, max_seqlen, scale):
-        o, lse = ext().attn_fwd(q, k, v, cu_seqlens, max_seqlen, scale)
-        ctx.save_for_backward(q, k, v, o, lse, cu_seqlens)
-        ctx.max_seqlen, ctx.scale = max_seqlen, scale
+    def forward(ctx, q, k, v, lens, scale):
+        n_valid = int(sum(lens))
+        o, lse = ext().attn_fwd(q, k, v, work_items(lens, 256, q.device), n_valid, scale)
+        ctx.save_for_backward(q, k, v, o, lse)
+        ctx.lens, ctx.scale, ctx.n_valid = lens, scale, n_valid
         return o
 
     @staticmethod
     def backward(ctx, do):
-        q, k, v, o, lse, cu = ctx.saved_tensors
-        dq, dk, dv = ext().attn_bwd(do.contiguous(), q, k, v, o, lse, cu, ctx.max_seqlen, ctx.scale)
-        return dq, dk, dv, None, None, None
+        q, k, v, o, lse = ctx.saved_tensors
+        items = work_items(ctx.lens, 128, q.device)
+        dq, dk, dv = ext().attn_bwd(do.contiguous(), q, k, v, o, lse, items, items, ctx.n_valid, ctx.scale)
+        return dq, dk, dv, None, None
 
 
 def varlen_attention(q: torch.Tensor, k: torch.Tensor, v: torch.Tensor, cu_seqlens: torch.Tensor,
@@ -44,7 +67,7 @@ def varlen_attention(q: torch.Tensor, k: torch.Tensor, v: torch.Tensor, cu_seqle
     max_seqlen = int(max(lens)) if max_seqlen is None else int(max_seqlen)
     if q.is_cuda:
         return _VarlenAttnCUDA.apply(q.contiguous(), k.contiguous(), v.contiguous(),
-                                     cu_seqlens.to(torch.int32), max_seqlen, float(scale))
+                                     [int(n) for n in lens], float(scale))
     out = torch.zeros_like(q)
     pieces = []
     start = 0

@@ -128,16 +128,28 @@ def grouped_mm_nt(a: torch.Tensor, w: torch.Tensor, bounds: Sequence[int], out: 
 # autograd ops
 # --------------------------------------------------------------------------------------------
 
+def _pad_k(t: torch.Tensor, k_pad: int) -> torch.Tensor:
+    """Zero-pad the last dim to ``k_pad`` (TMA needs 16-byte row strides)."""
+    if t.shape[-1] == k_pad:
+        return t.contiguous()
+    out = t.new_zeros(*t.shape[:-1], k_pad)
+    out[..., : t.shape[-1]] = t
+    return out
+
+
 class _LinearCUDA(torch.autograd.Function):
     @staticmethod
     def forward(ctx, x, w, b):
         shp = x.shape
-        x2 = x.reshape(-1, shp[-1]).contiguous()
-        wc = w.to(torch.bfloat16).contiguous()
+        K = shp[-1]
+        k_pad = (K + 7) // 8 * 8
+        x2 = _pad_k(x.reshape(-1, K), k_pad)
+        wc = _pad_k(w.to(torch.bfloat16), k_pad)
         bc = None if b is None else b.to(torch.bfloat16).contiguous()
         y = mm_nt(x2, wc, bias=bc)
         ctx.save_for_backward(x2, wc)
         ctx.shp = shp
+        ctx.K = K
         ctx.w_dtype = w.dtype
         ctx.has_b = b is not None
         ctx.b_dtype = None if b is None else b.dtype
@@ -147,8 +159,9 @@ class _LinearCUDA(torch.autograd.Function):
     def backward(ctx, gy):
         x2, wc = ctx.saved_tensors
         g2 = gy.reshape(-1, gy.shape[-1]).contiguous().to(torch.bfloat16)
-        gx = mm_nn(g2, wc).reshape(ctx.shp) if ctx.needs_input_grad[0] else None
-        gw = mm_tn(g2, x2, out_dtype=torch.float32).to(ctx.w_dtype) if ctx.needs_input_grad[1] else None
+        K = ctx.K
+        gx = mm_nn(g2, wc)[:, :K].reshape(ctx.shp) if ctx.needs_input_grad[0] else None
+        gw = mm_tn(g2, x2, out_dtype=torch.float32)[:, :K].to(ctx.w_dtype) if ctx.needs_input_grad[1] else None
         gb = segment_sum(g2, [0, g2.shape[0]])[0].to(ctx.b_dtype) if ctx.has_b and ctx.needs_input_grad[2] else None
         return gx, gw, gb
 
@@ -208,8 +221,18 @@ def grouped_linear(x: torch.Tensor, w: torch.Tensor, b: torch.Tensor, bounds: Se
     return torch.cat(parts, 0) if parts else out
 
 
+FFN_ROW_CHUNK = 16384
+
+
+def _chunks(r0: int, r1: int, size: int):
+    for a in range(r0, r1, size):
+        yield a, min(a + size, r1)
+
+
 class _GroupedFFNCUDA(torch.autograd.Function):
-    """Per-modality GELU-tanh MLP; stores the bf16 pre-activation and recomputes GELU in backward."""
+    """Per-modality GELU-tanh MLP.  Forward stores only the bf16 pre-activation; GELU is recomputed
+    in the backward's dGELU epilogue.  Rows are processed in chunks so the [rows, hidden] temporaries
+    (post-activation, its gradient) stay small at 100k-token batches."""
 
     @staticmethod
     def forward(ctx, x, bounds, *params):
@@ -221,11 +244,14 @@ class _GroupedFFNCUDA(torch.autograd.Function):
         L = x.shape[0]
         hidden = max(w.shape[0] for w in wu)
         pre = torch.empty(L, hidden, dtype=torch.bfloat16, device=x.device)
-        post = torch.empty(L, hidden, dtype=torch.bfloat16, device=x.device)
-        ext().gemm_grouped_nt(x, wu, post, bu, pre, list(bounds))
         out = torch.zeros(L, wd[0].shape[0], dtype=torch.bfloat16, device=x.device)
-        # down projection: each group reads only its first N_g hidden columns
-        ext().gemm_grouped_nt(post, wd, out, bd, None, list(bounds))
+        E = ext()
+        for g in range(G):
+            hid = wu[g].shape[0]
+            for a, b in _chunks(bounds[g], bounds[g + 1], FFN_ROW_CHUNK):
+                post = torch.empty(b - a, hid, dtype=torch.bfloat16, device=x.device)
+                E.gemm(x[a:b], wu[g], post, True, True, bu[g], pre[a:b, :hid], False)
+                E.gemm(post, wd[g], out[a:b], True, True, bd[g], None, False)
         ctx.save_for_backward(x, pre, *wu, *wd)
         ctx.bounds, ctx.G = list(bounds), G
         ctx.dtypes = [p.dtype for p in params]
@@ -240,24 +266,24 @@ class _GroupedFFNCUDA(torch.autograd.Function):
         gy = gy.contiguous()
         gx = torch.zeros_like(x)
         grads = []
+        E = ext()
+        dev = x.device
         for g in range(G):
-            r0, r1 = bounds[g], bounds[g + 1]
-            hid = wu[g].shape[0]
-            if r1 <= r0:
-                grads += [torch.zeros_like(wu[g], dtype=torch.float32), torch.zeros(hid, device=x.device),
-                          torch.zeros_like(wd[g], dtype=torch.float32), torch.zeros(wd[g].shape[0], device=x.device)]
-                continue
-            pre_g = pre[r0:r1, :hid]
-            gyg = gy[r0:r1]
-            # d post = gy @ Wd  ;  d pre = d post * gelu'(pre) (fused epilogue), post recomputed
-            dpre = torch.empty(r1 - r0, hid, dtype=torch.bfloat16, device=x.device)
-            post = torch.empty(r1 - r0, hid, dtype=torch.bfloat16, device=x.device)
-            ext().gemm_dgelu(gyg, wd[g], pre_g, dpre, post)
-            gwd = mm_tn(gyg, post, out_dtype=torch.float32)
-            gbd = segment_sum(gyg, [0, r1 - r0])[0]
-            mm_nn(dpre, wu[g], out=gx[r0:r1])
-            gwu = mm_tn(dpre, x[r0:r1], out_dtype=torch.float32)
-            gbu = segment_sum(dpre, [0, r1 - r0])[0]
+            hid, H = wu[g].shape[0], wd[g].shape[0]
+            gwu = torch.zeros(hid, x.shape[1], dtype=torch.float32, device=dev)
+            gwd = torch.zeros(H, hid, dtype=torch.float32, device=dev)
+            gbu = torch.zeros(hid, dtype=torch.float32, device=dev)
+            gbd = torch.zeros(H, dtype=torch.float32, device=dev)
+            for a, b in _chunks(bounds[g], bounds[g + 1], FFN_ROW_CHUNK):
+                gyg = gy[a:b]
+                dpre = torch.empty(b - a, hid, dtype=torch.bfloat16, device=dev)
+                post = torch.empty(b - a, hid, dtype=torch.bfloat16, device=dev)
+                E.gemm_dgelu(gyg, wd[g], pre[a:b, :hid], dpre, post)   # d pre = (gy Wd) * gelu'(pre)
+                E.gemm(gyg, post, gwd, False, False, None, None, True)  # gWd += gy^T post
+                gbd += segment_sum(gyg, [0, b - a])[0]
+                E.gemm(dpre, wu[g], gx[a:b], True, False, None, None, False)  # gx = dpre Wu
+                E.gemm(dpre, x[a:b], gwu, False, False, None, None, True)    # gWu += dpre^T x
+                gbu += segment_sum(dpre, [0, b - a])[0]
             grads += [gwu, gbu, gwd, gbd]
         grads = [gr.to(dt) for gr, dt in zip(grads, ctx.dtypes)]
         return (gx, None, *grads)

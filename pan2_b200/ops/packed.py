@@ -185,7 +185,6 @@ class _MseCUDA(torch.autograd.Function):
         sums = ext().mse_fwd(pred, target, n_video)   # [2] fp32: (sum sq, count)
         ctx.save_for_backward(pred, target)
         ctx.n_video = n_video
-        ctx.mark_non_differentiable(sums)
         return sums
 
     @staticmethod

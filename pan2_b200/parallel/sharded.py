@@ -1,0 +1,307 @@
+"""Flat sharded parameter units: the B200 replacement for FSDP2 ``fully_shard`` (train.py:788-815).
+
+Every joint block (and one root unit holding everything else) owns one flat buffer.  Within a unit,
+each parameter is split row-wise (dim 0) across the shard group exactly like FSDP2's per-parameter
+``Shard(0)``: rank ``r`` owns rows ``[r*R/N, (r+1)*R/N)`` of every parameter (rows padded to a
+multiple of N).  That keeps Muon's chunk structure local (QKV's 192 row chunks split evenly) and
+makes every rank's shard one contiguous buffer, so
+
+* the parameter all-gather is one ``all_gather_into_tensor`` of bf16 ``hi`` shards per unit, followed
+  by an unpack into the natural per-parameter layout the model reads;
+* the gradient reduce-scatter packs the unit's bf16 gradients rank-major, casts to fp32 and runs one
+  ``reduce_scatter_tensor`` (the reference reduces in fp32: ``MixedPrecisionPolicy(reduce=fp32)``).
+
+Master weights are exact fp32 values kept as two 16-bit halves (``hi``: the bf16 compute weight,
+``lo``: the low bits).  With one rank the natural and shard layouts coincide and ``hi`` *is* the
+model's weight storage.  When the planner decides the GPU cannot hold everything (29B on 1-2 GPUs),
+``lo`` and the optimizer state live in pinned host memory and the optimizer streams them per unit.
+"""
+from __future__ import annotations
+
+import math
+from dataclasses import dataclass, field
+from typing import Dict, List, Optional, Sequence, Tuple
+
+import torch
+import torch.distributed as dist
+import torch.nn as nn
+
+from ..optim.muon import use_muon_for
+
+
+@dataclass
+class ParamSlot:
+    name: str                 # name relative to the model root
+    module: nn.Module
+    attr: str
+    shape: Tuple[int, ...]
+    rows: int
+    cols: int
+    rows_pad: int
+    full_off: int             # offset in the natural (gathered) layout
+    shard_off: int            # offset in the per-rank shard layout
+    kind: str                 # "muon" | "adamw"
+    chunks: Optional[Tuple[int, int]] = None
+
+    @property
+    def numel(self) -> int:
+        return self.rows * self.cols
+
+    @property
+    def shard_rows(self) -> int:
+        return self.rows_pad // self._world
+
+    _world: int = 1
+
+
+@dataclass
+class Unit:
+    index: int
+    name: str
+    module: nn.Module
+    slots: List[ParamSlot]
+    numel_full: int
+    numel_shard: int
+    world: int
+    hi: Optional[torch.Tensor] = None          # bf16 [numel_shard] (GPU)
+    lo: Optional[torch.Tensor] = None          # int16 [numel_shard] (GPU or pinned host)
+    full_hi: Optional[torch.Tensor] = None     # bf16 [numel_full] gathered weights (alias of hi when world==1)
+    full_grad: Optional[torch.Tensor] = None   # bf16 [numel_full] unsharded gradients
+    grad_shard: Optional[torch.Tensor] = None  # fp32 [numel_shard] (world > 1)
+    state: Dict[str, torch.Tensor] = field(default_factory=dict)  # optimizer state (flat shard layout)
+    gather_event: Optional[torch.cuda.Event] = None
+
+    def slot_full(self, buf: torch.Tensor, s: ParamSlot) -> torch.Tensor:
+        return buf[s.full_off:s.full_off + s.numel].view(s.shape)
+
+    def slot_shard(self, buf: torch.Tensor, s: ParamSlot) -> torch.Tensor:
+        n = s.shard_rows * s.cols
+        return buf[s.shard_off:s.shard_off + n].view(s.shard_rows, s.cols)
+
+
+def _align(n: int, a: int) -> int:
+    return (n + a - 1) // a * a
+
+
+def build_unit(index: int, name: str, module: nn.Module, world: int, prefix: str = "") -> Unit:
+    """Lay out the parameters of ``module`` (names prefixed with ``prefix``)."""
+    from ..optim.muon import muon_chunks
+    chunk_map = muon_chunks(module)
+    slots = []
+    full_off = shard_off = 0
+    for pname, p in module.named_parameters():
+        mod_name, _, attr = pname.rpartition(".")
+        owner = module.get_submodule(mod_name) if mod_name else module
+        shape = tuple(p.shape)
+        rows = shape[0] if len(shape) >= 1 else 1
+        cols = int(math.prod(shape[1:])) if len(shape) >= 2 else 1
+        rows_pad = _align(rows, world)
+        full_name = prefix + pname
+        slot = ParamSlot(name=full_name, module=owner, attr=attr, shape=shape, rows=rows, cols=cols,
+                         rows_pad=rows_pad, full_off=full_off, shard_off=shard_off,
+                         kind="muon" if use_muon_for(full_name, shape) else "adamw",
+                         chunks=chunk_map.get(pname))
+        slot._world = world
+        slots.append(slot)
+        # 16-byte aligned offsets (8 bf16 elements) keep every view TMA-addressable
+        full_off += _align(rows * cols, 8)
+        shard_off += _align(slot.shard_rows * cols, 8)
+    return Unit(index=index, name=name, module=module, slots=slots, numel_full=full_off,
+                numel_shard=shard_off, world=world)
+
+
+class ShardedModel:
+    """Owns the units of a model and moves weights / gradients between layouts.
+
+    ``units[0..n_blocks-1]`` are the joint blocks; ``units[-1]`` is the root (everything else).
+    """
+
+    def __init__(self, units: List[Unit], group: Optional[dist.ProcessGroup], device: torch.device,
+                 offload: bool):
+        self.units = units
+        self.group = group
+        self.world = units[0].world if units else 1
+        self.rank = dist.get_rank(group) if (group is not None and self.world > 1) else 0
+        self.device = device
+        self.offload = offload
+        self.comm_stream = torch.cuda.Stream(device) if device.type == "cuda" else None
+
+    # ---------------------------------------------------------------- parameter views
+    def bind_weights(self, u: Unit, full: Optional[torch.Tensor]) -> None:
+        """Point every module parameter of ``u`` at its view of ``full`` (or an empty placeholder)."""
+        for s in u.slots:
+            p = getattr(s.module, s.attr)
+            if full is None:
+                p.data = torch.empty(0, dtype=torch.bfloat16, device=self.device)
+            else:
+                p.data = u.slot_full(full, s)
+
+    # ---------------------------------------------------------------- all-gather
+    def gather(self, u: Unit, stream: Optional[torch.cuda.Stream] = None) -> None:
+        """Make ``u.full_hi`` hold the unit's full bf16 weights and bind the module to it."""
+        if self.world == 1:
+            u.full_hi = u.hi
+            self.bind_weights(u, u.full_hi)
+            return
+        if u.full_hi is None:
+            self.prefetch(u)
+        if u.gather_event is not None:
+            torch.cuda.current_stream(self.device).wait_event(u.gather_event)
+            u.gather_event = None
+        self.bind_weights(u, u.full_hi)
+
+    def prefetch(self, u: Unit) -> None:
+        """Start the all-gather of ``u`` on the communication stream (no-op if in flight/done)."""
+        if self.world == 1 or u.full_hi is not None:
+            return
+        packed = torch.empty(self.world * u.numel_shard, dtype=torch.bfloat16, device=self.device)
+        full = torch.empty(u.numel_full, dtype=torch.bfloat16, device=self.device)
+
+        def run():
+            dist.all_gather_into_tensor(packed, u.hi, group=self.group)
+            pk = packed.view(self.world, u.numel_shard)
+            for s in u.slots:
+                n = s.shard_rows * s.cols
+                src = pk[:, s.shard_off:s.shard_off + n].reshape(self.world * s.shard_rows, s.cols)[:s.rows]
+                u.slot_full(full, s).view(s.rows, s.cols).copy_(src)
+
+        if self.comm_stream is None:
+            run()
+        else:
+            self.comm_stream.wait_stream(torch.cuda.current_stream(self.device))
+            with torch.cuda.stream(self.comm_stream):
+                run()
+                ev = torch.cuda.Event()
+                ev.record(self.comm_stream)
+            packed.record_stream(self.comm_stream)
+            full.record_stream(self.comm_stream)
+            u.gather_event = ev
+        u.full_hi = full
+
+    def release(self, u: Unit) -> None:
+        """Drop the gathered weights of ``u`` (world > 1); the module keeps an empty placeholder."""
+        if self.world == 1:
+            return
+        u.full_hi = None
+        self.bind_weights(u, None)
+
+    # ---------------------------------------------------------------- gradients
+    def attach_grads(self, u: Unit) -> None:
+        """Give every parameter of ``u`` a zeroed ``.grad`` view of the unit's flat bf16 gradient."""
+        if u.full_grad is None:
+            u.full_grad = torch.zeros(u.numel_full, dtype=torch.bfloat16, device=self.device)
+        else:
+            u.full_grad.zero_()
+        for s in u.slots:
+            getattr(s.module, s.attr).grad = u.slot_full(u.full_grad, s)
+
+    def detach_grads(self, u: Unit) -> None:
+        for s in u.slots:
+            getattr(s.module, s.attr).grad = None
+
+    def reduce_grads(self, u: Unit, accumulate: bool = False) -> None:
+        """world > 1: fp32 reduce-scatter of the unit's gradient into ``u.grad_shard`` (async on the
+        communication stream).  world == 1: the bf16 gradient stays as is."""
+        self.detach_grads(u)
+        if self.world == 1:
+            return
+        g = u.full_grad
+        u.full_grad = None
+        packed = torch.zeros(self.world * u.numel_shard, dtype=torch.float32, device=self.device)
+        out = torch.empty(u.numel_shard, dtype=torch.float32, device=self.device)
+
+        def run():
+            pk = packed.view(self.world, u.numel_shard)
+            for s in u.slots:
+                n = s.shard_rows * s.cols
+                dst = pk[:, s.shard_off:s.shard_off + n].reshape(self.world * s.shard_rows, s.cols)[:s.rows]
+                dst.copy_(u.slot_full(g, s).view(s.rows, s.cols))
+            dist.reduce_scatter_tensor(out, packed, op=dist.ReduceOp.SUM, group=self.group)
+            if u.grad_shard is None or not accumulate:
+                u.grad_shard = out
+            else:
+                u.grad_shard.add_(out)
+
+        if self.comm_stream is None:
+            run()
+            return
+        self.comm_stream.wait_stream(torch.cuda.current_stream(self.device))
+        with torch.cuda.stream(self.comm_stream):
+            run()
+        g.record_stream(self.comm_stream)
+        packed.record_stream(self.comm_stream)
+        out.record_stream(self.comm_stream)
+
+    def wait_comm(self) -> None:
+        if self.comm_stream is not None and self.world > 1:
+            torch.cuda.current_stream(self.device).wait_stream(self.comm_stream)
+
+    def grad_of(self, u: Unit) -> torch.Tensor:
+        """Gradient in the shard layout (bf16 full buffer when world == 1, fp32 shard otherwise)."""
+        return u.full_grad if self.world == 1 else u.grad_shard
+
+    # ---------------------------------------------------------------- state dict
+    def full_state_dict(self, to_cpu: bool = True) -> Dict[str, torch.Tensor]:
+        """fp32 full weights of every parameter (gathers all shards; collective when world > 1)."""
+        from ..optim.flat_ops import join_master
+        out = {}
+        for u in self.units:
+            x = join_master(u.hi, u.lo)
+            if self.world > 1:
+                full = torch.empty(self.world * u.numel_shard, dtype=torch.float32, device=self.device)
+                dist.all_gather_into_tensor(full, x, group=self.group)
+                pk = full.view(self.world, u.numel_shard)
+            else:
+                pk = x.view(1, u.numel_shard)
+            for s in u.slots:
+                n = s.shard_rows * s.cols
+                t = pk[:, s.shard_off:s.shard_off + n].reshape(self.world * s.shard_rows, s.cols)[:s.rows]
+                t = t.reshape(s.shape).clone()
+                out[s.name] = t.cpu() if to_cpu else t
+        return out
+
+    def load_full_state_dict(self, sd: Dict[str, torch.Tensor], strict: bool = False) -> List[str]:
+        """Load full fp32 weights into the local shards; unmatched parameters keep their values.
+        Returns the names that were missing from ``sd``."""
+        from ..optim.flat_ops import join_master
+        missing = []
+        for u in self.units:
+            x = join_master(u.hi, u.lo).clone()
+            for s in u.slots:
+                t = sd.get(s.name)
+                if t is None:
+                    missing.append(s.name)
+                    continue
+                t = t.reshape(s.rows, s.cols).float().cpu()
+                pad = torch.zeros(s.rows_pad, s.cols)
+                pad[:s.rows] = t
+                mine = pad[self.rank * s.shard_rows:(self.rank + 1) * s.shard_rows]
+                n = s.shard_rows * s.cols
+                x[s.shard_off:s.shard_off + n] = mine.reshape(-1).to(x.device)
+            set_master(u, x)
+            if self.world == 1:
+                self.bind_weights(u, u.hi)
+        if strict and missing:
+            raise KeyError(f"missing parameters: {missing[:8]}")
+        return missing
+
+
+def join_master_cpu(hi: torch.Tensor, lo: torch.Tensor) -> torch.Tensor:
+    h = hi.cpu().view(torch.int16).to(torch.int32) & 0xFFFF
+    l = lo.cpu().view(torch.int16).to(torch.int32) & 0xFFFF
+    return ((h << 16) | l).view(torch.float32)
+
+
+def split_master_cpu(x: torch.Tensor) -> Tuple[torch.Tensor, torch.Tensor]:
+    b = x.float().contiguous().view(torch.int32)
+    hi = ((b >> 16) & 0xFFFF).to(torch.int16).view(torch.bfloat16)
+    lo = (b & 0xFFFF).to(torch.int16)
+    return hi, lo
+
+
+def set_master(u: Unit, x: torch.Tensor) -> None:
+    """Write fp32 shard values ``x`` into ``u.hi`` / ``u.lo`` (``lo`` may live in host memory)."""
+    from ..optim.flat_ops import split_master
+    lo_dev = torch.empty(x.numel(), dtype=torch.int16, device=x.device)
+    split_master(x, u.hi, lo_dev)
+    u.lo.copy_(lo_dev)

@@ -1,0 +1,485 @@
+"""Training engine: sharded units, block-level activation checkpointing and the fused optimizer step.
+
+This is the B200 restatement of the reference trainer's model wrapping and step
+(train.py:572-1055): FSDP2 + ``checkpoint_wrapper`` + ``torch.optim.Muon``/``AdamW`` become
+
+* one :class:`~pan2_b200.parallel.sharded.Unit` per joint block plus a root unit, with exact fp32
+  masters stored as (bf16 hi, 16-bit lo) shards;
+* :class:`BlockCheckpoint`, an autograd node per block that gathers the block's weights (prefetching
+  the next block on a communication stream), runs the fused forward without saving activations,
+  and in backward re-gathers, recomputes, back-propagates into the block's flat bf16 gradient and
+  launches the fp32 reduce-scatter while the previous block computes;
+* a flat optimizer over the shards: Nesterov-momentum Muon with Gram Newton-Schulz on tcgen05
+  batched GEMMs (chunked QKV / out-projection locally, other matrices gathered to an owner rank
+  with all-to-all, as in patch_muon.py:174-268) and fused AdamW for everything else; learning rate
+  and clip coefficient stay on the device;
+* optional host offload of ``lo`` and the optimizer state (pinned memory, streamed per unit on
+  copy-engine streams), chosen automatically when the GPU cannot hold a full replica's state —
+  the 29B model on one or two B200s.
+"""
+from __future__ import annotations
+
+import math
+import os
+from dataclasses import dataclass
+from typing import Dict, List, Optional, Sequence
+
+import torch
+import torch.distributed as dist
+import torch.nn as nn
+
+from ..models.transformer import PanVideoDiffusionTransformer, JointAttentionBlock
+from ..models.packed import PackedSequenceParams
+from ..ops._ext import ext
+from ..optim import flat_ops as F
+from ..optim.muon import adjust_lr_scale, chunk_view, gram_newton_schulz
+from ..parallel.sharded import ShardedModel, Unit, build_unit, set_master, split_master_cpu
+
+
+class _Root(nn.Module):
+    """Everything outside the joint blocks, as one parameter unit (names match the model)."""
+
+    def __init__(self, model: PanVideoDiffusionTransformer):
+        super().__init__()
+        for name, child in model.named_children():
+            if name != "blocks":
+                self.add_module(name, child)
+
+
+@dataclass
+class OptimConfig:
+    lr: float = 1e-5
+    weight_decay: float = 0.05
+    use_muon: bool = True
+    momentum: float = 0.95
+    adamw_betas: tuple = (0.95, 0.95)
+    adamw_eps: float = 1e-8
+    max_grad_norm: float = 1.0
+    adjust_lr_fn: str = "match_rms_adamw"
+
+
+class BlockCheckpoint(torch.autograd.Function):
+    """Activation-checkpointed joint block driven by the engine's gather / reduce-scatter."""
+
+    @staticmethod
+    def forward(ctx, engine: "TrainEngine", idx: int, x, ln_stats, vec):
+        sm = engine.sharded
+        u = sm.units[idx]
+        sm.gather(u)
+        if idx + 1 < engine.n_blocks:
+            sm.prefetch(sm.units[idx + 1])
+        blk = engine.model.blocks[idx]
+        with torch.no_grad():
+            y, st = blk.forward_packed(x, ln_stats, vec, engine.meta)
+        sm.release(u)
+        ctx.engine, ctx.idx = engine, idx
+        stash = engine.stash_checkpoint(idx, x, ln_stats)
+        if stash is None:
+            ctx.save_for_backward(x, ln_stats, vec)
+            ctx.stash = None
+        else:
+            ctx.save_for_backward(vec)
+            ctx.stash = stash
+        ctx.mark_non_differentiable(st)
+        return y, st
+
+    @staticmethod
+    def backward(ctx, gy, _gst):
+        engine, idx = ctx.engine, ctx.idx
+        sm = engine.sharded
+        u = sm.units[idx]
+        if ctx.stash is None:
+            x, ln_stats, vec = ctx.saved_tensors
+        else:
+            (vec,) = ctx.saved_tensors
+            x, ln_stats = ctx.stash
+            ctx.stash = None
+        sm.gather(u)
+        if idx > 0:
+            sm.prefetch(sm.units[idx - 1])
+        blk = engine.model.blocks[idx]
+        x_ = x.detach().requires_grad_(True)
+        vec_ = vec.detach().requires_grad_(True)
+        sm.attach_grads(u)
+        params = [getattr(s.module, s.attr) for s in u.slots]
+        with torch.enable_grad():
+            y, _ = blk.forward_packed(x_, ln_stats, vec_, engine.meta)
+        torch.autograd.backward([y], [gy], inputs=[x_, vec_] + params)
+        sm.reduce_grads(u)
+        sm.release(u)
+        return None, None, x_.grad, None, vec_.grad
+
+
+def _host_available_bytes() -> Optional[int]:
+    try:
+        with open("/proc/meminfo") as f:
+            for line in f:
+                if line.startswith("MemAvailable:"):
+                    return int(line.split()[1]) * 1024
+    except OSError:
+        return None
+    return None
+
+
+def _local_ranks() -> int:
+    return int(os.environ.get("LOCAL_WORLD_SIZE", "1"))
+
+
+def _hbm_bytes(device) -> int:
+    if device.type != "cuda":
+        return 1 << 62
+    free, total = torch.cuda.mem_get_info(device)
+    return total
+
+
+class TrainEngine:
+    """Owns the model, its sharded units and the optimizer state; runs one training step."""
+
+    def __init__(self, arch: dict, device: torch.device, *, group: Optional[dist.ProcessGroup] = None,
+                 seed: int = 42, optim: Optional[OptimConfig] = None, offload: str = "auto",
+                 activation_bytes_estimate: int = 0):
+        self.device = device
+        self.group = group
+        self.world = dist.get_world_size(group) if (group is not None and dist.is_initialized()) else 1
+        self.rank = dist.get_rank(group) if self.world > 1 else 0
+        self.optim = optim or OptimConfig()
+        self.arch = dict(arch)
+        self.meta: Optional[PackedSequenceParams] = None
+        self.step_count = 0
+        self.host_bytes_planned = 0
+        # skeleton on the meta device, then each unit materialised on the device with its own seed
+        with torch.device("meta"):
+            model = PanVideoDiffusionTransformer(**arch)
+        self.n_blocks = len(model.blocks)
+        units: List[Unit] = []
+        blk_opts = dict(attention_backend=model.attention_backend, mlp_ratio=arch.get("mlp_ratio", 8.0),
+                        context_mlp_ratio=arch.get("context_mlp_ratio", 4.0),
+                        zero_init_modulation=arch.get("zero_init_modulation", True),
+                        text_modulation_timestep_dependent=arch.get("text_modulation_timestep_dependent", False))
+        total = sum(p.numel() for p in model.parameters())
+        self.total_params = total
+        self.offload = self._plan_offload(total, offload, activation_bytes_estimate)
+        # GPU bytes left for offloadable state (lo halves, optimizer state) after the resident
+        # weights, gradients and the activation reserve; the rest goes to pinned host memory.
+        self._gpu_budget = 0
+        if self.offload and device.type == "cuda":
+            resident = total * 2 / self.world + (total * 2 if self.world == 1 else total * 4 / self.world)
+            self._gpu_budget = int(_hbm_bytes(device) - resident - activation_bytes_estimate - 8e9)
+            from ..optim.muon import use_muon_for
+            n_muon = sum(p.numel() for n, p in model.named_parameters()
+                         if self.optim.use_muon and use_muon_for(n, tuple(p.shape)))
+            state = (total * 2 + n_muon * 4 + (total - n_muon) * 8) / self.world
+            self.host_bytes_planned = max(0, int(state - max(self._gpu_budget, 0)))
+            avail = _host_available_bytes()
+            if avail is not None and self.host_bytes_planned > 0.85 * avail / max(1, _local_ranks()):
+                raise MemoryError(
+                    f"offloaded optimizer state needs {self.host_bytes_planned / 1e9:.0f} GB of pinned host memory per "
+                    f"rank but only {avail / 1e9:.0f} GB are available on this host")
+        for i in range(self.n_blocks):
+            torch.manual_seed(seed * 1000003 + i)
+            with torch.device(device):
+                blk = JointAttentionBlock(model.hidden_size, model.num_attention_heads, **blk_opts)
+            model.blocks[i] = blk
+            units.append(self._materialise(i, f"blocks.{i}", blk, f"blocks.{i}."))
+        torch.manual_seed(seed * 1000003 + self.n_blocks)
+        with torch.device(device):
+            small = PanVideoDiffusionTransformer(**{**arch, "num_layers": 0})
+        for name, child in small.named_children():
+            if name != "blocks":
+                setattr(model, name, child)
+        root = _Root(model)
+        units.append(self._materialise(self.n_blocks, "root", root, ""))
+        self.model = model
+        self.sharded = ShardedModel(units, group, device, self.offload)
+        for u in units:
+            if self.world == 1:
+                self.sharded.bind_weights(u, u.hi)
+            else:
+                self.sharded.bind_weights(u, None)
+        self._alloc_optimizer_state()
+        self.stash_in_grads = self.world == 1
+        if self.world == 1:  # persistent gradient buffers (they also hold activation checkpoints)
+            for u in units:
+                u.full_grad = torch.zeros(u.numel_full, dtype=torch.bfloat16, device=device)
+        self.lr_t = torch.full((1,), self.optim.lr, dtype=torch.float32, device=device)
+        self.norm_clip = torch.zeros(2, dtype=torch.float32, device=device)
+        self._partials = torch.zeros(len(units) * 256, dtype=torch.float32, device=device)
+        if self.offload and device.type == "cuda":
+            self._h2d = torch.cuda.Stream(device)
+            self._d2h = torch.cuda.Stream(device)
+
+    # ---------------------------------------------------------------- construction
+    def _plan_offload(self, total: int, offload: str, act_bytes: int) -> bool:
+        if offload in (True, "on", "true", "1"):
+            return True
+        if offload in (False, "off", "false", "0") or self.device.type != "cuda":
+            return False
+        per_rank = total / self.world
+        grad_bytes = 2 if self.world == 1 else 4
+        need = per_rank * (2 + 2 + grad_bytes + 4) + act_bytes + (2 if self.world == 1 else 0) * 0
+        return need > 0.9 * _hbm_bytes(self.device)
+
+    def _materialise(self, idx: int, name: str, module: nn.Module, prefix: str) -> Unit:
+        u = build_unit(idx, name, module, self.world, prefix)
+        x = torch.zeros(u.numel_shard, dtype=torch.float32, device=self.device)
+        for s in u.slots:
+            p = getattr(s.module, s.attr).detach().float().reshape(s.rows, s.cols)
+            if s.rows_pad != s.rows:
+                p = torch.cat([p, p.new_zeros(s.rows_pad - s.rows, s.cols)], 0)
+            mine = p[self.rank * s.shard_rows:(self.rank + 1) * s.shard_rows]
+            n = s.shard_rows * s.cols
+            x[s.shard_off:s.shard_off + n] = mine.reshape(-1)
+        u.hi = torch.empty(u.numel_shard, dtype=torch.bfloat16, device=self.device)
+        u.lo = self._state_tensor(u.numel_shard, torch.int16)
+        lo_dev = torch.empty(u.numel_shard, dtype=torch.int16, device=self.device)
+        F.split_master(x, u.hi, lo_dev)
+        u.lo.copy_(lo_dev)
+        # free the fp32 initial values held by the module
+        for s in u.slots:
+            getattr(s.module, s.attr).data = torch.empty(0, dtype=torch.bfloat16, device=self.device)
+        return u
+
+    def _state_tensor(self, n: int, dtype) -> torch.Tensor:
+        """Offloadable state: on the GPU while the budget lasts, else pinned host memory."""
+        nbytes = n * torch.empty(0, dtype=dtype).element_size()
+        if not self.offload or nbytes <= self._gpu_budget:
+            self._gpu_budget -= nbytes if self.offload else 0
+            return torch.zeros(n, dtype=dtype, device=self.device)
+        return torch.zeros(n, dtype=dtype, pin_memory=True)
+
+    def _alloc_optimizer_state(self) -> None:
+        """Compact per-unit state: Muon momentum for Muon slots, AdamW (m, v) for the others."""
+        pin = self.offload
+        self._soff = {}
+        for u in self.sharded.units:
+            mo = ao = 0
+            for s in u.slots:
+                n = s.shard_rows * s.cols
+                if self._is_muon(s):
+                    self._soff[id(s)] = mo
+                    mo += n
+                else:
+                    self._soff[id(s)] = ao
+                    ao += n
+            u.state["mom"] = self._state_tensor(mo, torch.float32) if mo else None
+            u.state["m"] = self._state_tensor(ao, torch.float32) if ao else None
+            u.state["v"] = self._state_tensor(ao, torch.float32) if ao else None
+
+    def _is_muon(self, s) -> bool:
+        return self.optim.use_muon and s.kind == "muon"
+
+    # ---------------------------------------------------------------- step
+    def forward_backward(self, batch: dict) -> torch.Tensor:
+        """Forward + backward of one packed batch; returns the (global-mean) loss as a device scalar."""
+        meta: PackedSequenceParams = batch["packed_seq_params"]
+        self.meta = meta
+        model = self.model
+        sm = self.sharded
+        root = sm.units[-1]
+        sm.gather(root)
+        if self.n_blocks:
+            sm.prefetch(sm.units[0])
+        sm.attach_grads(root)
+        x, ln_stats, vec = model.embed_packed(batch["hidden_states"], batch["timestep"], batch["text_states"], meta)
+        for i in range(self.n_blocks):
+            x, ln_stats = BlockCheckpoint.apply(self, i, x, ln_stats, vec)
+        sums = model.head_and_loss(x, ln_stats, vec, batch["target"], meta)
+        glob = sums.detach().clone()
+        if self.world > 1:
+            dist.all_reduce(glob, op=dist.ReduceOp.SUM, group=self.group)
+        loss = sums[0] / glob[1]
+        loss.backward()
+        sm.reduce_grads(root)
+        sm.wait_comm()
+        if self.world > 1:
+            sm.release(root)
+        return (glob[0] / glob[1]).detach()
+
+    def stash_checkpoint(self, idx: int, x: torch.Tensor, ln_stats: torch.Tensor):
+        """Keep block ``idx``'s input inside block ``idx-1``'s gradient buffer.
+
+        With one rank every block has a persistent bf16 gradient buffer that is idle from the
+        optimizer step until that block's backward.  Block ``idx``'s backward (which needs the
+        checkpoint) always finishes before block ``idx-1``'s backward zeroes its buffer, so the
+        checkpointed activations (44 x 0.78 GB for the 29B batch) cost no extra memory.
+        """
+        if self.world != 1 or idx == 0 or not self.stash_in_grads:
+            return None
+        buf = self.sharded.units[idx - 1].full_grad
+        nx = x.numel()
+        ns = ln_stats.numel() * 2  # fp32 -> bf16-sized slots
+        if buf is None or nx + ns > buf.numel() or x.dtype != torch.bfloat16 or nx % 2:
+            return None
+        xs = buf[:nx].view(x.shape)
+        xs.copy_(x)
+        ss = buf[nx:nx + ns].view(torch.float32).view(ln_stats.shape)
+        ss.copy_(ln_stats)
+        return xs, ss
+
+    def _cur_stream(self):
+        return torch.cuda.current_stream(self.device) if self.device.type == "cuda" else None
+
+    def grad_norm(self) -> torch.Tensor:
+        """Global gradient L2 norm and clip coefficient (``self.norm_clip = [norm, clip]``)."""
+        parts = self._partials.view(len(self.sharded.units), 256)
+        for i, u in enumerate(self.sharded.units):
+            F.sumsq_partial(self.sharded.grad_of(u), parts[i])
+        if self.world > 1:
+            dist.all_reduce(self._partials, op=dist.ReduceOp.SUM, group=self.group)
+        F.norm_and_clip(self._partials, float(self.optim.max_grad_norm), self.norm_clip)
+        return self.norm_clip
+
+    def set_lr(self, lr: float) -> None:
+        self.lr_t.fill_(lr)
+
+    def optimizer_step(self) -> None:
+        self.step_count += 1
+        clip = self.norm_clip[1:2] if self.optim.max_grad_norm > 0 else None
+        units = self.sharded.units
+        if not self.offload:
+            for u in units:
+                self._step_unit(u, u.lo, u.state, clip)
+            return
+        # streamed: H2D of unit i+1 overlaps compute of unit i; D2H after compute.  Tensors that
+        # the placement kept on the GPU are used in place.
+        cur = torch.cuda.current_stream(self.device)
+        staged = {}
+
+        def on_host(t):
+            return t is not None and t.device.type == "cpu"
+
+        def stage(i):
+            u = units[i]
+            self._h2d.wait_stream(cur)
+            with torch.cuda.stream(self._h2d):
+                lo = u.lo.to(self.device, non_blocking=True) if on_host(u.lo) else u.lo
+                st = {k: (v.to(self.device, non_blocking=True) if on_host(v) else v) for k, v in u.state.items()}
+                ev = torch.cuda.Event()
+                ev.record(self._h2d)
+            staged[i] = (lo, st, ev)
+
+        stage(0)
+        for i, u in enumerate(units):
+            if i + 1 < len(units):
+                stage(i + 1)
+            lo, st, ev = staged.pop(i)
+            cur.wait_event(ev)
+            moved = [(u.lo, lo)] if on_host(u.lo) else []
+            moved += [(u.state[k], v) for k, v in st.items() if on_host(u.state[k])]
+            for _, t in moved:
+                t.record_stream(cur)
+            self._step_unit(u, lo, st, clip)
+            if moved:
+                self._d2h.wait_stream(cur)
+                with torch.cuda.stream(self._d2h):
+                    for host, dev in moved:
+                        host.copy_(dev, non_blocking=True)
+                for _, t in moved:
+                    t.record_stream(self._d2h)
+        cur.wait_stream(self._d2h)
+
+    def place_state(self, reserve_bytes: int) -> Dict[str, int]:
+        """Move offloaded ``lo`` halves / optimizer state back to the GPU while free memory minus
+        ``reserve_bytes`` allows (largest savings of PCIe traffic first: ``lo`` then momentum)."""
+        if not self.offload or self.device.type != "cuda":
+            return {}
+        free = torch.cuda.mem_get_info(self.device)[0] - reserve_bytes
+        moved = {"lo": 0, "state": 0}
+        for u in self.sharded.units:
+            nb = u.lo.numel() * 2
+            if u.lo.device.type == "cpu" and nb < free:
+                u.lo = u.lo.to(self.device)
+                free -= nb
+                moved["lo"] += nb
+        for u in self.sharded.units:
+            for k, v in list(u.state.items()):
+                if v is not None and v.device.type == "cpu" and v.numel() * 4 < free:
+                    u.state[k] = v.to(self.device)
+                    free -= v.numel() * 4
+                    moved["state"] += v.numel() * 4
+        return moved
+
+    def _step_unit(self, u: Unit, lo: torch.Tensor, st: Dict[str, torch.Tensor], clip) -> None:
+        E = F
+        o = self.optim
+        g = self.sharded.grad_of(u)
+        b1, b2 = o.adamw_betas
+        muon_work = []
+        for s in u.slots:
+            n = s.shard_rows * s.cols
+            sl = slice(s.shard_off, s.shard_off + n)
+            so = self._soff[id(s)]
+            ss = slice(so, so + n)
+            if self._is_muon(s):
+                upd = torch.empty(n, dtype=torch.bfloat16, device=self.device)
+                E.muon_momentum(st["mom"][ss], g[sl], clip, o.momentum, upd)
+                muon_work.append((s, sl, upd))
+            else:
+                E.adamw_update(u.hi[sl], lo[sl], g[sl], st["m"][ss], st["v"][ss], clip, self.lr_t, b1, b2,
+                               o.adamw_eps, o.weight_decay, self.step_count)
+        if not muon_work:
+            return
+        local, remote = [], []
+        for item in muon_work:
+            s = item[0]
+            if self.world == 1 or (s.chunks is not None and s.chunks[0] == 0 and s.chunks[1] % self.world == 0
+                                   and s.rows == s.rows_pad):
+                local.append(item)
+            else:
+                remote.append(item)
+        for s, sl, upd in local:
+            n_chunks = s.chunks[1] // self.world if s.chunks is not None and s.chunks[0] == 0 else 1
+            mat = upd.view(s.shard_rows, s.cols)
+            if n_chunks > 1:
+                orth = gram_newton_schulz(chunk_view(mat, n_chunks)).reshape(s.shard_rows, s.cols)
+                shape = (s.rows // s.chunks[1], s.cols)
+            else:
+                orth = gram_newton_schulz(mat)
+                shape = (s.rows, s.cols)
+            E.muon_update(u.hi[sl], lo[sl], orth.reshape(-1), self.lr_t, adjust_lr_scale(shape, o.adjust_lr_fn),
+                          o.weight_decay)
+        if remote:
+            self._muon_all_to_all(u, lo, remote)
+
+    def _muon_all_to_all(self, u: Unit, lo: torch.Tensor, work) -> None:
+        """Owner-rank orthogonalisation of row-sharded matrices (reference: patch_muon.py:174-268)."""
+        E = F
+        o = self.optim
+        W = self.world
+        for start in range(0, len(work), W):
+            chunk = work[start:start + W]
+            send = [chunk[j][2].view(chunk[j][0].shard_rows, chunk[j][0].cols) if j < len(chunk)
+                    else torch.empty(0, dtype=torch.bfloat16, device=self.device) for j in range(W)]
+            mine = chunk[self.rank] if self.rank < len(chunk) else None
+            if mine is not None:
+                s = mine[0]
+                full = torch.empty(W * s.shard_rows, s.cols, dtype=torch.bfloat16, device=self.device)
+                recv = list(full.split(s.shard_rows, 0))
+            else:
+                full = None
+                recv = [torch.empty(0, dtype=torch.bfloat16, device=self.device) for _ in range(W)]
+            dist.all_to_all(recv, send, group=self.group)
+            if full is not None:
+                s = mine[0]
+                real = full[:s.rows]
+                if s.chunks is not None and s.chunks[0] == 0 and s.chunks[1] > 1:
+                    orth = gram_newton_schulz(chunk_view(real, s.chunks[1])).reshape(s.rows, s.cols)
+                else:
+                    orth = gram_newton_schulz(real)
+                full[:s.rows].copy_(orth)
+                full[s.rows:].zero_()
+            dist.all_to_all(send, recv, group=self.group)
+            for s, sl, upd in chunk:
+                shape = (s.rows // s.chunks[1], s.cols) if (s.chunks and s.chunks[0] == 0) else (s.rows, s.cols)
+                E.muon_update(u.hi[sl], lo[sl], upd, self.lr_t, adjust_lr_scale(shape, o.adjust_lr_fn),
+                              o.weight_decay)
+
+    def zero_grad(self) -> None:
+        for u in self.sharded.units:
+            if self.world == 1:
+                continue
+            u.grad_shard = None
+
+    def parameters_bytes(self) -> Dict[str, int]:
+        us = self.sharded.units
+        return dict(hi=sum(u.hi.numel() * 2 for u in us), lo=sum(u.lo.numel() * 2 for u in us))

@@ -1,0 +1,67 @@
+"""One optimizer step through the engine, with the reference trainer's safety semantics.
+
+``StepRunner.train_step(host_batch)`` is the public per-step call (reference: PanVideoTrainer.train_step,
+train.py:949-1055): copy the step's inputs host->device, forward+backward, global grad norm and clip
+coefficient on the device, a host read of loss and norm, a cross-rank vote on whether the update is
+finite (every rank must agree before the optimizer runs: train.py:1000-1023), the optimizer step
+(skipped, with gradients dropped, when not finite), then the learning-rate schedule.
+"""
+from __future__ import annotations
+
+import math
+from typing import Callable, Dict, Optional
+
+import torch
+import torch.distributed as dist
+
+from ..data.synthetic import batch_to_device
+from .engine import TrainEngine
+
+
+class StepRunner:
+    def __init__(self, engine: TrainEngine, lr_lambda: Optional[Callable[[int], float]] = None,
+                 base_lr: Optional[float] = None, cpu_group=None):
+        self.engine = engine
+        self.lr_lambda = lr_lambda or (lambda step: 1.0)
+        self.base_lr = engine.optim.lr if base_lr is None else base_lr
+        self.cpu_group = cpu_group
+        self.global_step = 0
+        dev = engine.device
+        pin = dev.type == "cuda"
+        self.loss_host = torch.zeros(2, dtype=torch.float32, pin_memory=pin)
+        self.engine.set_lr(self.base_lr * self.lr_lambda(0))
+        self.skipped = 0
+
+    def device_step(self, batch_dev: Dict) -> Dict:
+        eng = self.engine
+        loss = eng.forward_backward(batch_dev)
+        norm_clip = eng.grad_norm()
+        self.loss_host[0].copy_(loss, non_blocking=True)
+        self.loss_host[1].copy_(norm_clip[0], non_blocking=True)
+        if eng.device.type == "cuda":
+            torch.cuda.current_stream(eng.device).synchronize()
+        loss_v, norm_v = float(self.loss_host[0]), float(self.loss_host[1])
+        ok = math.isfinite(loss_v) and math.isfinite(norm_v)
+        if eng.world > 1:
+            flag = torch.tensor([int(ok)], dtype=torch.int32)
+            if self.cpu_group is not None:
+                dist.all_reduce(flag, op=dist.ReduceOp.MIN, group=self.cpu_group)
+            else:
+                f = flag.to(eng.device)
+                dist.all_reduce(f, op=dist.ReduceOp.MIN, group=eng.group)
+                flag = f.cpu()
+            ok = bool(flag.item())
+        if ok:
+            eng.optimizer_step()
+        else:
+            self.skipped += 1
+        eng.zero_grad()
+        self.global_step += 1
+        lr = self.base_lr * self.lr_lambda(self.global_step)
+        eng.set_lr(lr)
+        return dict(loss=loss_v, grad_norm=norm_v, lr=lr, step_skipped=not ok)
+
+    def train_step(self, host_batch: Dict) -> Dict:
+        """Host batch in (pinned CPU tensors), metrics out (host floats)."""
+        dev_batch = batch_to_device(host_batch, self.engine.device, non_blocking=True)
+        return self.device_step(dev_batch)
