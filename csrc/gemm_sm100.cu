@@ -52,7 +52,7 @@ struct Params {
   __nv_bfloat16* aux2;    // DGELU: GELU(pre) out
   long long ldaux2;
   int epi;
-  int accumulate;
+  int accumulate;  // host-side only: folded into C = D, beta = 1
   // batched GEMMs: operand z-coordinate = batch index; D/C advance by their batch strides
   int batch;
   int tiles_per_batch;
@@ -278,22 +278,10 @@ gemm_kernel(const __grid_constant__ Params p, const __grid_constant__ TmapSet ma
           }
           if (p.d_fp32) {
             float* d = reinterpret_cast<float*>(p.D) + zb * p.d_bstride + (size_t)row * p.ldd + c;
-            if (p.accumulate) {
-              const float4 x0 = *reinterpret_cast<const float4*>(d);
-              const float4 x1 = *reinterpret_cast<const float4*>(d + 4);
-              o[0] += x0.x; o[1] += x0.y; o[2] += x0.z; o[3] += x0.w;
-              o[4] += x1.x; o[5] += x1.y; o[6] += x1.z; o[7] += x1.w;
-            }
             *reinterpret_cast<float4*>(d) = make_float4(o[0], o[1], o[2], o[3]);
             *reinterpret_cast<float4*>(d + 4) = make_float4(o[4], o[5], o[6], o[7]);
           } else {
             __nv_bfloat16* d = reinterpret_cast<__nv_bfloat16*>(p.D) + zb * p.d_bstride + (size_t)row * p.ldd + c;
-            if (p.accumulate) {
-              float x[8];
-              load8(d, x);
-#pragma unroll
-              for (int i = 0; i < 8; ++i) o[i] += x[i];
-            }
             store8(d, o);
           }
         }

@@ -211,7 +211,8 @@ class JointAttentionBlock(nn.Module):
         else:
             o = attn_fn(q, k, v, meta)
         L = x.shape[0]
-        o_concat = P.gather_rows(o.reshape(o.shape[0], -1), meta.indices_interleave_to_concat)
+        o_concat = P.permute_rows(o.reshape(o.shape[0], -1), meta.indices_interleave_to_concat,
+                                  meta.indices_concat_to_interleave)
         h = self.hidden_size
         attn_out = grouped_linear(o_concat, self.out_proj.weight.view(2, h, h), self.out_proj.bias.view(2, h),
                                   mm_bounds)

@@ -219,8 +219,28 @@ def segment_sum(x: torch.Tensor, bounds: Sequence[int], out_dtype=torch.float32)
     return torch.stack([x[bounds[s]:bounds[s + 1]].float().sum(0) for s in range(n_seg)]).to(out_dtype)
 
 
+class _PermuteRowsCUDA(torch.autograd.Function):
+    @staticmethod
+    def forward(ctx, x, index, inverse):
+        ctx.save_for_backward(inverse)
+        return ext().gather_rows(x.contiguous(), index)
+
+    @staticmethod
+    def backward(ctx, g):
+        (inverse,) = ctx.saved_tensors
+        return ext().gather_rows(g.contiguous(), inverse), None, None
+
+
+def permute_rows(x: torch.Tensor, index: torch.Tensor, inverse: torch.Tensor) -> torch.Tensor:
+    """``x[index]`` for a row permutation ``index`` whose inverse is ``inverse`` (differentiable:
+    the gradient is gathered back with the inverse permutation)."""
+    if x.is_cuda:
+        return _PermuteRowsCUDA.apply(x, index.to(torch.int32), inverse.to(torch.int32))
+    return x.index_select(0, index.long())
+
+
 def gather_rows(x: torch.Tensor, index: torch.Tensor) -> torch.Tensor:
-    """``x[index]`` for a 2-D/3-D tensor (row gather)."""
+    """``x[index]`` for a 2-D/3-D tensor (row gather, no gradient on CUDA: use permute_rows)."""
     if x.is_cuda:
         return ext().gather_rows(x.contiguous(), index)
     return x.index_select(0, index.long())

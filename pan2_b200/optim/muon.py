@@ -73,26 +73,34 @@ def adjust_lr_scale(shape: Sequence[int], fn: str = "match_rms_adamw") -> float:
 # Gram Newton-Schulz
 # ---------------------------------------------------------------------------------------------
 
-def _ns_cpu(X: torch.Tensor, coeffs, steps, eps, reset) -> torch.Tensor:
-    """Same recurrence in fp32 on the CPU (reference for tests); X is [B, M, N] with M <= N."""
+def _ns_cpu(X: torch.Tensor, coeffs, steps, eps, reset, round_bf16: bool = False) -> torch.Tensor:
+    """The same recurrence on the CPU in fp32; ``round_bf16`` rounds every product to bf16 the way
+    the tcgen05 path stores it (fp32 accumulation, one rounding per output).  X is [B, M, N], M <= N."""
     a, b, c = coeffs
-    X = X.float()
-    norm = X.flatten(1).norm(dim=1).clamp(min=eps).view(-1, 1, 1)
-    X = X / norm
-    R = X @ X.transpose(-1, -2)
+    rd = (lambda t: t.to(torch.bfloat16).float()) if round_bf16 else (lambda t: t)
+    X = rd(X.float())
+    R32 = X @ X.transpose(-1, -2)
+    n2 = torch.diagonal(R32, dim1=-2, dim2=-1).sum(-1).clamp(min=eps * eps).view(-1, 1, 1)
+    R = rd(R32 / n2)
     Q = None
+    first = True
     I = torch.eye(X.shape[1]).expand_as(R)
     for i in range(steps):
         if i == reset and Q is not None:
-            X = Q @ X
-            R = X @ X.transpose(-1, -2)
+            if first:
+                Q = rd(Q / n2.sqrt())
+                first = False
+            X = rd(Q @ X)
+            R = rd(X @ X.transpose(-1, -2))
             Q = None
-        Z = b * R + c * (R @ R)
-        Q = a * I + Z if Q is None else Q @ Z + a * Q
+        Z = rd(c * (R @ R) + b * R)
+        Q = rd(a * I + Z) if Q is None else rd(Q @ Z + a * Q)
         if i < steps - 1 and (i + 1) != reset:
-            RZ = R @ Z + a * R
-            R = Z @ RZ + a * RZ
-    return Q @ X
+            RZ = rd(R @ Z + a * R)
+            R = rd(Z @ RZ + a * RZ)
+    if first:
+        Q = rd(Q / n2.sqrt())
+    return rd(Q @ X)
 
 
 def gram_newton_schulz(G: torch.Tensor, coeffs=NS_COEFFS, steps: int = NS_STEPS, eps: float = NS_EPS,
@@ -133,7 +141,7 @@ def gram_newton_schulz(G: torch.Tensor, coeffs=NS_COEFFS, steps: int = NS_STEPS,
 
     def apply_q(Qm, Xm):
         out = torch.empty_like(Xm)
-        if transpose:   # X^T <- X^T Q   (Q symmetric)
+        if transpose:   # X^T <- X^T Q^T  (= (Q X)^T)
             E.gemm_batched(Xm, Qm, out, True, True, 1.0, 0.0, None)
         else:           # X <- Q X       (X as an MN-major B operand)
             E.gemm_batched(Qm, Xm, out, True, False, 1.0, 0.0, None)
@@ -150,17 +158,19 @@ def gram_newton_schulz(G: torch.Tensor, coeffs=NS_COEFFS, steps: int = NS_STEPS,
             else:
                 E.gemm_batched(X, X, R, True, True, 1.0, 0.0, None)
             Q = None
-        E.gemm_batched(R, R, Z, True, True, c, b, R)           # Z = c R R + b R
+        # M x M products use B as an MN-major operand (true A @ B): the Gram iterates are only
+        # symmetric up to rounding, and A @ B^T would feed that asymmetry back every step
+        E.gemm_batched(R, R, Z, True, False, c, b, R)          # Z = c R R + b R
         if Q is None:
             Q = Z.clone()
             E.ns_add_diag(Q, a)                                  # Q = a I + Z
         else:
             Qn = torch.empty_like(Q)
-            E.gemm_batched(Q, Z, Qn, True, True, 1.0, a, Q)     # Q = Q Z + a Q
+            E.gemm_batched(Q, Z, Qn, True, False, 1.0, a, Q)    # Q = Q Z + a Q
             Q = Qn
         if i < steps - 1 and (i + 1) != reset:
-            E.gemm_batched(R, Z, RZ, True, True, 1.0, a, R)     # RZ = R Z + a R
-            E.gemm_batched(Z, RZ, Rn, True, True, 1.0, a, RZ)   # R = Z RZ + a RZ
+            E.gemm_batched(R, Z, RZ, True, False, 1.0, a, R)    # RZ = R Z + a R
+            E.gemm_batched(Z, RZ, Rn, True, False, 1.0, a, RZ)  # R = Z RZ + a RZ
             R, Rn = Rn, R
     if first_segment:
         E.ns_scale_by_invnorm(Q, norm2, eps)

@@ -37,10 +37,15 @@ def test_tiny_model_packed_gpu_matches_cpu():
     rel = abs(loss_gpu.item() - loss_cpu.item()) / abs(loss_cpu.item())
     assert rel < 2e-2, (loss_gpu.item(), loss_cpu.item())
     worst = []
+    no_grad = [k for k, p in model.named_parameters() if k in g_cpu and p.grad is None]
+    assert not no_grad, no_grad
     for k, p in model.named_parameters():
         if k not in g_cpu:
             continue
         a, b = p.grad.float().cpu(), g_cpu[k]
+        if b.abs().max() == 0:  # e.g. the last block's text FFN: no path to the video loss
+            assert a.abs().max() == 0, k
+            continue
         cos = torch.nn.functional.cosine_similarity(a.flatten(), b.flatten(), dim=0).item()
         worst.append((cos, k))
     worst.sort()
