@@ -103,8 +103,10 @@ def main():
     latent_tokens = meta.n_video
 
     t0 = time.time()
+    # activation reserve: with one rank the block checkpoints live in idle gradient buffers
+    reserve_gb = float(os.environ.get("PAN_ACT_RESERVE_GB", "40" if world == 1 else "72"))
     engine = TrainEngine(arch, device, group=group, seed=42, optim=optim, offload=args.offload,
-                         activation_bytes_estimate=int(float(os.environ.get("PAN_ACT_RESERVE_GB", "40")) * 1e9))
+                         activation_bytes_estimate=int(reserve_gb * 1e9))
     placed = {}
     init_s = time.time() - t0
     runner = StepRunner(engine, lr_lambda=lr_lambda_from_config(tr))

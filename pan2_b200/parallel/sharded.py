@@ -83,6 +83,39 @@ def _align(n: int, a: int) -> int:
     return (n + a - 1) // a * a
 
 
+def pack_rows(pk: torch.Tensor, s: "ParamSlot", full: torch.Tensor, world: int) -> None:
+    """Scatter a full ``[rows, cols]`` parameter into the rank-major packed buffer ``pk``
+    (``[world, numel_shard]``): rank ``r`` gets rows ``[r*shard_rows, (r+1)*shard_rows)`` (zero padding)."""
+    n = s.shard_rows * s.cols
+    dst = pk[:, s.shard_off:s.shard_off + n].view(world, s.shard_rows, s.cols)
+    src = full.view(s.rows, s.cols)
+    if s.rows == s.rows_pad:
+        dst.copy_(src.view(world, s.shard_rows, s.cols))
+        return
+    for r in range(world):
+        a = r * s.shard_rows
+        k = max(0, min(s.shard_rows, s.rows - a))
+        if k:
+            dst[r, :k].copy_(src[a:a + k])
+        if k < s.shard_rows:
+            dst[r, k:].zero_()
+
+
+def unpack_rows(pk: torch.Tensor, s: "ParamSlot", full: torch.Tensor, world: int) -> None:
+    """Inverse of :func:`pack_rows`: gather the rank-major shards of one parameter into ``full``."""
+    n = s.shard_rows * s.cols
+    src = pk[:, s.shard_off:s.shard_off + n].view(world, s.shard_rows, s.cols)
+    dst = full.view(s.rows, s.cols)
+    if s.rows == s.rows_pad:
+        dst.view(world, s.shard_rows, s.cols).copy_(src)
+        return
+    for r in range(world):
+        a = r * s.shard_rows
+        k = max(0, min(s.shard_rows, s.rows - a))
+        if k:
+            dst[a:a + k].copy_(src[r, :k])
+
+
 def build_unit(index: int, name: str, module: nn.Module, world: int, prefix: str = "") -> Unit:
     """Lay out the parameters of ``module`` (names prefixed with ``prefix``)."""
     from ..optim.muon import muon_chunks
@@ -161,9 +194,7 @@ class ShardedModel:
             dist.all_gather_into_tensor(packed, u.hi, group=self.group)
             pk = packed.view(self.world, u.numel_shard)
             for s in u.slots:
-                n = s.shard_rows * s.cols
-                src = pk[:, s.shard_off:s.shard_off + n].reshape(self.world * s.shard_rows, s.cols)[:s.rows]
-                u.slot_full(full, s).view(s.rows, s.cols).copy_(src)
+                unpack_rows(pk, s, u.slot_full(full, s), self.world)
 
         if self.comm_stream is None:
             run()
@@ -213,9 +244,7 @@ class ShardedModel:
         def run():
             pk = packed.view(self.world, u.numel_shard)
             for s in u.slots:
-                n = s.shard_rows * s.cols
-                dst = pk[:, s.shard_off:s.shard_off + n].reshape(self.world * s.shard_rows, s.cols)[:s.rows]
-                dst.copy_(u.slot_full(g, s).view(s.rows, s.cols))
+                pack_rows(pk, s, u.slot_full(g, s), self.world)
             dist.reduce_scatter_tensor(out, packed, op=dist.ReduceOp.SUM, group=self.group)
             if u.grad_shard is None or not accumulate:
                 u.grad_shard = out
@@ -254,9 +283,8 @@ class ShardedModel:
             else:
                 pk = x.view(1, u.numel_shard)
             for s in u.slots:
-                n = s.shard_rows * s.cols
-                t = pk[:, s.shard_off:s.shard_off + n].reshape(self.world * s.shard_rows, s.cols)[:s.rows]
-                t = t.reshape(s.shape).clone()
+                t = torch.empty(s.shape, dtype=torch.float32, device=x.device)
+                unpack_rows(pk, s, t, self.world)
                 out[s.name] = t.cpu() if to_cpu else t
         return out
 

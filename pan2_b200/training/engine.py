@@ -33,6 +33,7 @@ from ..models.packed import PackedSequenceParams
 from ..ops._ext import ext
 from ..optim import flat_ops as F
 from ..optim.muon import adjust_lr_scale, chunk_view, gram_newton_schulz
+from ..parallel.collectives import all_to_all_list
 from ..parallel.sharded import ShardedModel, Unit, build_unit, set_master, split_master_cpu
 
 
@@ -428,14 +429,12 @@ class TrainEngine:
             else:
                 remote.append(item)
         for s, sl, upd in local:
-            n_chunks = s.chunks[1] // self.world if s.chunks is not None and s.chunks[0] == 0 else 1
+            chunked = s.chunks is not None and s.chunks[0] == 0
+            n_local = s.chunks[1] // self.world if chunked else 1
             mat = upd.view(s.shard_rows, s.cols)
-            if n_chunks > 1:
-                orth = gram_newton_schulz(chunk_view(mat, n_chunks)).reshape(s.shard_rows, s.cols)
-                shape = (s.rows // s.chunks[1], s.cols)
-            else:
-                orth = gram_newton_schulz(mat)
-                shape = (s.rows, s.cols)
+            orth = (gram_newton_schulz(chunk_view(mat, n_local)).reshape(s.shard_rows, s.cols) if n_local > 1
+                    else gram_newton_schulz(mat))
+            shape = (s.rows // s.chunks[1], s.cols) if chunked else (s.rows, s.cols)
             E.muon_update(u.hi[sl], lo[sl], orth.reshape(-1), self.lr_t, adjust_lr_scale(shape, o.adjust_lr_fn),
                           o.weight_decay)
         if remote:
@@ -458,7 +457,7 @@ class TrainEngine:
             else:
                 full = None
                 recv = [torch.empty(0, dtype=torch.bfloat16, device=self.device) for _ in range(W)]
-            dist.all_to_all(recv, send, group=self.group)
+            all_to_all_list(recv, send, group=self.group)
             if full is not None:
                 s = mine[0]
                 real = full[:s.rows]
@@ -468,7 +467,7 @@ class TrainEngine:
                     orth = gram_newton_schulz(real)
                 full[:s.rows].copy_(orth)
                 full[s.rows:].zero_()
-            dist.all_to_all(send, recv, group=self.group)
+            all_to_all_list(send, recv, group=self.group)
             for s, sl, upd in chunk:
                 shape = (s.rows // s.chunks[1], s.cols) if (s.chunks and s.chunks[0] == 0) else (s.rows, s.cols)
                 E.muon_update(u.hi[sl], lo[sl], upd, self.lr_t, adjust_lr_scale(shape, o.adjust_lr_fn),

@@ -1,0 +1,78 @@
+"""Sharded engine across 2 gloo ranks == the same engine on 1 rank (CPU).
+
+Both ranks train on the same batch, so the global mean loss and its gradient equal the single-rank
+ones; after one optimizer step (AdamW for 1-D/modulation tensors, Muon with local chunked NS for QKV
+and owner-rank all-to-all NS for the other matrices) the gathered fp32 masters must match."""
+import os
+import socket
+
+import pytest
+import torch
+import torch.distributed as dist
+import torch.multiprocessing as mp
+
+from tiny import TINY_ARCH, tiny_batch
+
+
+def _free_port():
+    s = socket.socket()
+    s.bind(("127.0.0.1", 0))
+    p = s.getsockname()[1]
+    s.close()
+    return p
+
+
+def _step(world, rank, port, out_q):
+    os.environ.update(MASTER_ADDR="127.0.0.1", MASTER_PORT=str(port))
+    if world > 1:
+        import datetime
+        dist.init_process_group("gloo", rank=rank, world_size=world, timeout=datetime.timedelta(seconds=120))
+    from pan2_b200.training.engine import TrainEngine, OptimConfig
+    from pan2_b200.models.transformer import PanVideoDiffusionTransformer
+    arch = dict(TINY_ARCH)
+    group = dist.group.WORLD if world > 1 else None
+    eng = TrainEngine(arch, torch.device("cpu"), group=group, seed=11,
+                      optim=OptimConfig(lr=1e-2, weight_decay=0.1, max_grad_norm=0.5), offload="off")
+    with torch.device("meta"):
+        shape_model = PanVideoDiffusionTransformer(**arch)
+    batch, _ = tiny_batch(shape_model, seed=7)
+    loss = eng.forward_backward(batch)
+    norm = eng.grad_norm().clone()
+    eng.optimizer_step()
+    sd = eng.sharded.full_state_dict()
+    if rank == 0:
+        import tempfile
+        path = os.path.join(tempfile.mkdtemp(), "sd.pt")
+        torch.save((float(loss), norm.tolist(), sd), path)
+        out_q.put(path)
+    if world > 1:
+        dist.barrier()
+        dist.destroy_process_group()
+
+
+def _run(world):
+    ctx = mp.get_context("spawn")
+    q = ctx.Queue()
+    port = _free_port()
+    procs = [ctx.Process(target=_step, args=(world, r, port, q)) for r in range(world)]
+    for p in procs:
+        p.start()
+    path = q.get(timeout=300)
+    for p in procs:
+        p.join(timeout=120)
+        assert p.exitcode == 0
+    return torch.load(path)
+
+
+@pytest.mark.timeout(900)
+def test_two_rank_step_matches_one_rank():
+    loss1, norm1, sd1 = _run(1)
+    loss2, norm2, sd2 = _run(2)
+    assert abs(loss1 - loss2) < 1e-5 * abs(loss1) + 1e-6, (loss1, loss2)
+    assert abs(norm1[0] - norm2[0]) < 1e-3 * norm1[0], (norm1, norm2)
+    worst = (0.0, "")
+    for k in sd1:
+        a, b = sd1[k].float(), sd2[k].float()
+        d = (a - b).abs().max().item() / (a.abs().max().item() + 1e-8)
+        worst = max(worst, (d, k))
+    assert worst[0] < 2e-3, worst
