@@ -183,6 +183,7 @@ def main():
             "init_s": init_s,
             "device_error_flag": err,
             "peak_mem_gb": torch.cuda.max_memory_allocated(device) / 1e9,
+            "last_step_phases_ms": runner.phase_times(),
             "host_pinned_gb": engine.host_bytes_planned / 1e9,
         }
         print(json.dumps(out), flush=True)

@@ -37,7 +37,19 @@ __device__ __forceinline__ float to_f<__nv_bfloat16>(__nv_bfloat16 g) { return _
 template <typename G>
 __global__ void sumsq_kernel(const G* __restrict__ x, size_t n, float* __restrict__ partial) {
   float acc = 0.f;
-  for (size_t i = (size_t)blockIdx.x * blockDim.x + threadIdx.x; i < n; i += (size_t)gridDim.x * blockDim.x) {
+  constexpr int V = 16 / sizeof(G);  // elements per 16-byte load
+  const size_t nv = (reinterpret_cast<uintptr_t>(x) % 16 == 0) ? n / V : 0;
+  const size_t stride = (size_t)gridDim.x * blockDim.x;
+  for (size_t i = (size_t)blockIdx.x * blockDim.x + threadIdx.x; i < nv; i += stride) {
+    const uint4 raw = reinterpret_cast<const uint4*>(x)[i];
+    const G* e = reinterpret_cast<const G*>(&raw);
+#pragma unroll
+    for (int k = 0; k < V; ++k) {
+      const float v = to_f<G>(e[k]);
+      acc += v * v;
+    }
+  }
+  for (size_t i = nv * V + (size_t)blockIdx.x * blockDim.x + threadIdx.x; i < n; i += stride) {
     const float v = to_f<G>(x[i]);
     acc += v * v;
   }

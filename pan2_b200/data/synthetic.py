@@ -44,7 +44,7 @@ def synthetic_packed_batch(n_clips: int, latent_thw: Tuple[int, int, int], text_
         if image_cond_first and i == 0:
             cond[:, :1] = x0[:, :1]
             mask[:, :1] = 1.0
-        inp = torch.cat([xt, cond, 1 - mask if image_cond_first and i == 0 else mask], 0)
+        inp = torch.cat([xt, cond, mask], 0)
         inputs.append(patchify(inp, patch_size))
         targets.append(patchify(eps - x0, patch_size).t())
     hidden = torch.cat(inputs, 1).to(dtype)[:, :, None, None].contiguous()

@@ -31,11 +31,28 @@ class StepRunner:
         self.loss_host = torch.zeros(2, dtype=torch.float32, pin_memory=pin)
         self.engine.set_lr(self.base_lr * self.lr_lambda(0))
         self.skipped = 0
+        self._events = None
+
+    def phase_times(self) -> Dict[str, float]:
+        """Device milliseconds of the last step's phases (call after a synchronize)."""
+        ev = self._events
+        if ev is None:
+            return {}
+        return {"forward_backward": ev[0].elapsed_time(ev[1]), "grad_norm": ev[1].elapsed_time(ev[2]),
+                "optimizer": ev[3].elapsed_time(ev[4])}
 
     def device_step(self, batch_dev: Dict) -> Dict:
         eng = self.engine
+        timing = eng.device.type == "cuda"
+        ev = [torch.cuda.Event(enable_timing=True) for _ in range(5)] if timing else None
+        if timing:
+            ev[0].record()
         loss = eng.forward_backward(batch_dev)
+        if timing:
+            ev[1].record()
         norm_clip = eng.grad_norm()
+        if timing:
+            ev[2].record()
         self.loss_host[0].copy_(loss, non_blocking=True)
         self.loss_host[1].copy_(norm_clip[0], non_blocking=True)
         if eng.device.type == "cuda":
@@ -51,10 +68,15 @@ class StepRunner:
                 dist.all_reduce(f, op=dist.ReduceOp.MIN, group=eng.group)
                 flag = f.cpu()
             ok = bool(flag.item())
+        if timing:
+            ev[3].record()
         if ok:
             eng.optimizer_step()
         else:
             self.skipped += 1
+        if timing:
+            ev[4].record()
+        self._events = ev
         eng.zero_grad()
         self.global_step += 1
         lr = self.base_lr * self.lr_lambda(self.global_step)
