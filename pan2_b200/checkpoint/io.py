@@ -1,0 +1,376 @@
+"""Sharded checkpoints of the flat-unit engine: streamed per unit, resharded on load.
+
+Directory layout of ``checkpoint-<step>/`` (the same folders as the reference, train.py:455-458 and
+1060-1151):
+
+* ``transformer/meta.json`` + ``transformer/<unit>.rank<r>-of-<W>.safetensors`` -- every rank writes
+  the fp32 master rows it owns of every parameter of the unit (``Shard(0)`` row ranges with
+  ``ceil(rows / W)`` rows per rank, the FSDP2 rule), keyed by the parameter's full name;
+* ``optimizer/<unit>.rank<r>-of-<W>.safetensors`` -- the same rows of ``<name>.momentum_buffer``
+  (Muon) or ``<name>.exp_avg`` / ``<name>.exp_avg_sq`` (AdamW), plus ``optimizer/meta.json``;
+* ``training_state.pt`` -- ``{"lr_schedulers": {name: state}, "global_step": N}``;
+* ``dataloader/<dp_rank>.json`` -- the packing loader's cursor;
+* ``COMPLETE`` -- written by rank 0 after every rank finished; a folder without it is unreadable and
+  resume falls back to the previous checkpoint (train.py:1256-1279).
+
+Units are written one at a time (device -> host -> file), so no rank ever holds more than one unit of
+host copies; there is no gather to one rank.  Loading reads, for every parameter, only the row range
+the loading rank owns, from whichever saved rank files hold it (``safe_open(...).get_slice``), so a
+checkpoint loads on any world size.  :func:`consolidate` writes a plain state dict (5 GB safetensors
+shards + index), the format warm starts, the converter and the inference pipeline read.
+"""
+from __future__ import annotations
+
+import glob
+import json
+import os
+import re
+import shutil
+from typing import Callable, Dict, Iterable, List, Optional, Tuple
+
+import torch
+import torch.distributed as dist
+
+FORMAT = "pan2_b200-sharded-v1"
+COMPLETE = "COMPLETE"
+
+
+def checkpoint_layout(root: str) -> Tuple[str, str, str]:
+    return os.path.join(root, "transformer"), os.path.join(root, "optimizer"), os.path.join(root, "training_state.pt")
+
+
+def _fname(unit: str, rank: int, world: int) -> str:
+    return f"{unit}.rank{rank:05d}-of-{world:05d}.safetensors"
+
+
+def rows_owned(rows: int, world: int, rank: int) -> Tuple[int, int]:
+    per = -(-rows // world)
+    a = min(rows, rank * per)
+    return a, min(rows, a + per)
+
+
+def _slot_rows(x: torch.Tensor, s, k: int) -> torch.Tensor:
+    return x[s.shard_off:s.shard_off + k * s.cols].view(k, s.cols)
+
+
+def _opt_names(engine, s) -> List[Tuple[str, str]]:
+    if engine._is_muon(s):
+        return [("mom", "momentum_buffer")]
+    return [("m", "exp_avg"), ("v", "exp_avg_sq")]
+
+
+def _state_rows(engine, u, s, key: str, k: int) -> torch.Tensor:
+    buf = u.state[key]
+    off = engine._soff[id(s)]
+    return buf[off:off + k * s.cols].view(k, s.cols)
+
+
+def _barrier(group):
+    if dist.is_initialized() and dist.get_world_size(group) > 1:
+        dist.barrier(group=group)
+
+
+def save_engine(engine, root: str, *, group=None, save_optimizer: bool = True) -> None:
+    """Every rank calls this.  Writes ``transformer/`` (and ``optimizer/``) of ``root``."""
+    from safetensors.torch import save_file
+    from ..optim.flat_ops import join_master
+    model_dir, optim_dir, _ = checkpoint_layout(root)
+    world, rank = engine.world, engine.rank
+    os.makedirs(model_dir, exist_ok=True)
+    if save_optimizer:
+        os.makedirs(optim_dir, exist_ok=True)
+    if engine.device.type == "cuda":
+        torch.cuda.synchronize(engine.device)
+    for u in engine.sharded.units:
+        x = join_master(u.hi, u.lo).cpu()
+        w, o = {}, {}
+        for s in u.slots:
+            a, b = rows_owned(s.rows, world, rank)
+            w[s.name] = _slot_rows(x, s, b - a).reshape(b - a, s.cols).clone()
+            if save_optimizer:
+                for key, label in _opt_names(engine, s):
+                    o[f"{s.name}.{label}"] = _state_rows(engine, u, s, key, b - a).float().cpu().clone()
+        save_file(w, os.path.join(model_dir, _fname(u.name, rank, world)), metadata={"format": FORMAT})
+        if save_optimizer:
+            save_file(o, os.path.join(optim_dir, _fname(u.name, rank, world)), metadata={"format": FORMAT})
+    if rank == 0:
+        meta = {"format": FORMAT, "world_size": world,
+                "units": [{"name": u.name, "params": [{"name": s.name, "shape": list(s.shape), "rows": s.rows,
+                                                       "cols": s.cols, "kind": s.kind} for s in u.slots]}
+                          for u in engine.sharded.units]}
+        with open(os.path.join(model_dir, "meta.json"), "w") as f:
+            json.dump(meta, f)
+        if save_optimizer:
+            with open(os.path.join(optim_dir, "meta.json"), "w") as f:
+                json.dump({"format": FORMAT, "world_size": world, "step": engine.step_count,
+                           "use_muon": engine.optim.use_muon}, f)
+
+
+class ShardedReader:
+    """Row-range reads of one saved folder (``transformer/`` or ``optimizer/``)."""
+
+    def __init__(self, folder: str, meta_folder: Optional[str] = None):
+        meta_path = os.path.join(meta_folder or folder, "meta.json")
+        with open(meta_path) as f:
+            meta = json.load(f)
+        if meta.get("format") != FORMAT:
+            raise ValueError(f"{meta_path}: unknown checkpoint format {meta.get('format')!r}")
+        self.folder = folder
+        self.world = int(meta["world_size"])
+        self.where: Dict[str, Tuple[str, int, int]] = {}   # param name -> (unit, rows, cols)
+        for u in meta["units"]:
+            for p in u["params"]:
+                self.where[p["name"]] = (u["name"], int(p["rows"]), int(p["cols"]))
+        self._open: Dict[str, object] = {}
+
+    def _handle(self, unit: str, q: int):
+        from safetensors import safe_open
+        fn = os.path.join(self.folder, _fname(unit, q, self.world))
+        h = self._open.get(fn)
+        if h is None:
+            if not os.path.exists(fn):
+                raise FileNotFoundError(fn)
+            h = safe_open(fn, framework="pt", device="cpu")
+            self._open[fn] = h
+        return h
+
+    def has(self, param: str) -> bool:
+        return param in self.where
+
+    def read_rows(self, param: str, a: int, b: int, suffix: str = "") -> torch.Tensor:
+        """Rows ``[a, b)`` of ``param`` (+``suffix`` for optimizer entries) as fp32 ``[b-a, cols]``."""
+        unit, rows, cols = self.where[param]
+        out = torch.empty(max(0, b - a), cols, dtype=torch.float32)
+        per = -(-rows // self.world)
+        r = a
+        while r < b:
+            q = r // per
+            qa, qb = rows_owned(rows, self.world, q)
+            hi = min(b, qb)
+            t = self._handle(unit, q).get_slice(param + suffix)[r - qa:hi - qa]
+            out[r - a:hi - a] = t.float()
+            r = hi
+        return out
+
+    def full(self, param: str, suffix: str = "") -> torch.Tensor:
+        unit, rows, cols = self.where[param]
+        return self.read_rows(param, 0, rows, suffix)
+
+
+def load_engine(engine, root: str, *, load_optimizer: bool = True, strict: bool = True) -> List[str]:
+    """Load ``root``'s transformer (and optimizer) rows this rank owns; works across world sizes.
+    Returns parameter names absent from the checkpoint (raises when ``strict``)."""
+    from ..parallel.sharded import set_master
+    from ..optim.flat_ops import join_master
+    model_dir, optim_dir, _ = checkpoint_layout(root)
+    wr = ShardedReader(model_dir)
+    orr = None
+    if load_optimizer:
+        if not os.path.isdir(optim_dir):
+            raise ValueError(f"{root} holds no optimizer state")
+        orr = ShardedReader(optim_dir, meta_folder=model_dir)
+        with open(os.path.join(optim_dir, "meta.json")) as f:
+            ometa = json.load(f)
+    world, rank = engine.world, engine.rank
+    missing = []
+    for u in engine.sharded.units:
+        x = join_master(u.hi, u.lo).cpu().clone()
+        for s in u.slots:
+            if not wr.has(s.name):
+                missing.append(s.name)
+                continue
+            a, b = rows_owned(s.rows, world, rank)
+            _slot_rows(x, s, b - a).copy_(wr.read_rows(s.name, a, b))
+            if orr is not None:
+                for key, label in _opt_names(engine, s):
+                    dst = _state_rows(engine, u, s, key, b - a)
+                    dst.copy_(orr.read_rows(s.name, a, b, "." + label).to(dst.device, dst.dtype))
+        set_master(u, x.to(engine.device))
+        if world == 1:
+            engine.sharded.bind_weights(u, u.hi)
+    if orr is not None:
+        engine.step_count = int(ometa.get("step", engine.step_count))
+    if strict and missing:
+        raise ValueError(f"{model_dir} is missing {len(missing)} transformer tensors, e.g. {missing[:5]}")
+    return missing
+
+
+# ------------------------------------------------------------------ plain state dicts
+class LazyStateDict:
+    """Read-on-demand view of a plain state dict: safetensors shards (a folder, an index json or one
+    file), a ``.pt``/``.bin`` file, or a sharded checkpoint folder.  ``get(name)`` loads one tensor."""
+
+    def __init__(self, path: str, key_map: Optional[Callable[[str], str]] = None):
+        self.key_map = key_map or (lambda k: k)
+        path = str(path)
+        self._files: Dict[str, str] = {}
+        self._eager: Optional[Dict[str, torch.Tensor]] = None
+        self._sharded: Optional[ShardedReader] = None
+        p = os.path.normpath(path)
+        if os.path.isdir(p) and os.path.exists(os.path.join(p, "transformer", "meta.json")):
+            p = os.path.join(p, "transformer")
+        if os.path.isdir(p) and os.path.exists(os.path.join(p, "meta.json")):
+            self._sharded = ShardedReader(p)
+            self._names = {self.key_map(k): k for k in self._sharded.where}
+            return
+        files = []
+        if os.path.isdir(p):
+            files = sorted(glob.glob(os.path.join(p, "*.safetensors")))
+            if not files:
+                pts = sorted(glob.glob(os.path.join(p, "*.pt")) + glob.glob(os.path.join(p, "*.bin")))
+                if pts:
+                    p = pts[0]
+        elif p.endswith(".json"):
+            with open(p) as f:
+                idx = json.load(f)["weight_map"]
+            files = sorted({os.path.join(os.path.dirname(p), v) for v in idx.values()})
+        elif p.endswith(".safetensors"):
+            files = [p]
+        if files:
+            from safetensors import safe_open
+            for fn in files:
+                with safe_open(fn, framework="pt", device="cpu") as h:
+                    for k in h.keys():
+                        self._files[k] = fn
+            self._names = {self.key_map(k): k for k in self._files}
+        else:
+            sd = torch.load(p, map_location="cpu", weights_only=True)
+            if isinstance(sd, dict) and "state_dict" in sd and isinstance(sd["state_dict"], dict):
+                sd = sd["state_dict"]
+            self._eager = {k: v for k, v in sd.items() if isinstance(v, torch.Tensor)}
+            self._names = {self.key_map(k): k for k in self._eager}
+
+    def keys(self) -> Iterable[str]:
+        return self._names.keys()
+
+    def __contains__(self, name: str) -> bool:
+        return name in self._names
+
+    def get(self, name: str, default=None):
+        raw = self._names.get(name)
+        if raw is None:
+            return default
+        if self._sharded is not None:
+            return self._sharded.full(raw)
+        if self._eager is not None:
+            return self._eager[raw]
+        from safetensors import safe_open
+        with safe_open(self._files[raw], framework="pt", device="cpu") as h:
+            return h.get_tensor(raw)
+
+
+def consolidate(src: str, out_dir: str, dtype=torch.bfloat16, max_shard_bytes: int = 5 * 1024 ** 3,
+                prefix: str = "diffusion_pytorch_model") -> List[str]:
+    """Write a sharded checkpoint (``checkpoint-N`` or its ``transformer/``) as plain safetensors
+    shards plus ``<prefix>.safetensors.index.json``; returns the shard paths."""
+    from safetensors.torch import save_file
+    sd = LazyStateDict(src)
+    os.makedirs(out_dir, exist_ok=True)
+    names = sorted(sd.keys())
+    groups, cur, size = [], [], 0
+    esize = torch.empty(0, dtype=dtype).element_size()
+    for n in names:
+        _, rows, cols = sd._sharded.where[n] if sd._sharded is not None else (None, 0, 0)
+        nbytes = rows * cols * esize if sd._sharded is not None else sd.get(n).numel() * esize
+        if cur and size + nbytes > max_shard_bytes:
+            groups.append(cur)
+            cur, size = [], 0
+        cur.append(n)
+        size += nbytes
+    if cur:
+        groups.append(cur)
+    shapes = {}
+    if sd._sharded is not None:
+        with open(os.path.join(sd._sharded.folder, "meta.json")) as f:
+            for u in json.load(f)["units"]:
+                for p in u["params"]:
+                    shapes[p["name"]] = tuple(p["shape"])
+    paths, weight_map, total = [], {}, 0
+    for i, grp in enumerate(groups):
+        fn = f"{prefix}-{i + 1:05d}-of-{len(groups):05d}.safetensors"
+        tensors = {}
+        for n in grp:
+            t = sd.get(n)
+            if n in shapes:
+                t = t.reshape(shapes[n])
+            tensors[n] = t.to(dtype).contiguous()
+            total += tensors[n].numel() * esize
+            weight_map[n] = fn
+        save_file(tensors, os.path.join(out_dir, fn), metadata={"format": "pt"})
+        paths.append(os.path.join(out_dir, fn))
+    with open(os.path.join(out_dir, f"{prefix}.safetensors.index.json"), "w") as f:
+        json.dump({"metadata": {"total_size": total}, "weight_map": weight_map}, f, indent=1)
+    return paths
+
+
+def load_plain_into_engine(engine, path: str, strict: bool = True) -> List[str]:
+    """Warm start from a plain state dict (any :class:`LazyStateDict` source), one unit at a time.
+    Legacy per-modality block keys are converted per block (``convert_legacy_block_keys``)."""
+    from .keys import convert_legacy_block_keys
+    from ..parallel.sharded import set_master
+    from ..optim.flat_ops import join_master
+    sd = LazyStateDict(path)
+    all_keys = list(sd.keys())
+    tmtd = bool(engine.arch.get("text_modulation_timestep_dependent", False))
+    missing = []
+    world, rank = engine.world, engine.rank
+    for u in engine.sharded.units:
+        if u.name.startswith("blocks."):
+            pre = u.name + "."
+            local = {k: sd.get(k) for k in all_keys if k.startswith(pre)}
+            lw = next((s for s in u.slots if s.name == pre + "text_modulation.linear.weight"), None)
+            convert_legacy_block_keys(local, pre, tmtd, torch.Size(lw.shape) if lw is not None else None)
+            getter = local.get
+        else:
+            getter = sd.get
+        x = join_master(u.hi, u.lo).cpu().clone()
+        for s in u.slots:
+            t = getter(s.name)
+            if t is None:
+                missing.append(s.name)
+                continue
+            a, b = rows_owned(s.rows, world, rank)
+            _slot_rows(x, s, b - a).copy_(t.reshape(s.rows, s.cols)[a:b].float())
+        set_master(u, x.to(engine.device))
+        if world == 1:
+            engine.sharded.bind_weights(u, u.hi)
+    if strict and missing:
+        raise ValueError(f"{path} is missing {len(missing)} transformer tensors, e.g. {missing[:5]}")
+    return missing
+
+
+# ------------------------------------------------------------------ folders
+_CKPT_RE = re.compile(r"checkpoint-(\d+)$")
+
+
+def list_checkpoints(output_dir: str) -> List[Tuple[int, str]]:
+    if not os.path.isdir(output_dir):
+        return []
+    out = []
+    for d in os.listdir(output_dir):
+        m = _CKPT_RE.match(d)
+        if m:
+            out.append((int(m.group(1)), os.path.join(output_dir, d)))
+    return sorted(out)
+
+
+def is_complete(root: str) -> bool:
+    return os.path.exists(os.path.join(root, COMPLETE))
+
+
+def mark_complete(root: str, step: int) -> None:
+    with open(os.path.join(root, COMPLETE), "w") as f:
+        f.write(f"{step}\n")
+
+
+def cleanup_old(output_dir: str, keep: int) -> List[str]:
+    """Keep the ``keep`` most recent checkpoints; returns the removed folders."""
+    if keep <= 0:
+        return []
+    ck = list_checkpoints(output_dir)
+    removed = []
+    while len(ck) > keep:
+        _, d = ck.pop(0)
+        shutil.rmtree(d, ignore_errors=True)
+        removed.append(d)
+    return removed

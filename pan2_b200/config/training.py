@@ -155,6 +155,12 @@ class TrainingConfig:
     activation_reserve_gb: float = opt(0.0, float, "GPU memory kept free for activations when planning offload "
                                                    "(0: automatic).")
     fault_injection: Optional[str] = opt(None, str, "Host-side fault injection spec, e.g. 'nan_loss@5,stall@7:2'.")
+    text_encoder: str = opt("qwen", str, "Caption embeddings: the Qwen3.5 encoder, or a deterministic hash "
+                                         "stand-in for offline smoke runs.", choices=("qwen", "hash"))
+    text_encoder_path: str = opt("Qwen/Qwen3.5-9B", str, "Hugging Face id or local folder of the text encoder.")
+    heartbeat_timeout_s: float = opt(50000.0, float, "Exit a rank whose loop made no progress for this long.")
+    process_group_timeout_s: float = opt(1800.0, float, "Collective timeout of the process groups.")
+    profile_step: int = opt(10, int, "cudaProfilerStart after this step (-1: never).")
 
     def check(self) -> None:
         """Reject inconsistent settings with an error naming the option."""

@@ -61,13 +61,17 @@ class PackedLoader:
     def __init__(self, dataset: PackingDataset, *, device, dtype=torch.bfloat16, prefetch: int = 2, seed: int = 0,
                  T: int = 1000, timestep_distribution: str = "lognorm", timestep_loc: float = 0.0,
                  timestep_scale: float = 1.0, shift: float = 1.0, shift_mode: str = "fixed",
-                 shift_kwargs: Optional[Dict] = None):
+                 shift_kwargs: Optional[Dict] = None, start_index: int = 0):
         self.dataset = dataset
         self.device = torch.device(device)
         self.dtype = dtype
         self.prefetch = prefetch
-        self.cpu_rng = torch.Generator().manual_seed(seed)
-        self.dev_rng = torch.Generator(device=self.device).manual_seed(seed + 1)
+        # every batch reseeds both generators from (seed, batch index), so a resumed run that starts
+        # at batch ``start_index`` draws exactly what the uninterrupted run drew
+        self.seed = seed
+        self.batch_index = start_index
+        self.cpu_rng = torch.Generator()
+        self.dev_rng = torch.Generator(device=self.device)
         self.T, self.dist, self.loc, self.scale = T, timestep_distribution, timestep_loc, timestep_scale
         self.shift, self.shift_mode, self.shift_kwargs = shift, shift_mode, dict(shift_kwargs or {})
         self._stop = threading.Event()
@@ -101,6 +105,9 @@ class PackedLoader:
         dev = self.device
         pt, ph, pw = self.dataset.patch_size
         n = len(plan.items)
+        self.cpu_rng.manual_seed((self.seed * 1000003 + self.batch_index) % (2 ** 62))
+        self.dev_rng.manual_seed((self.seed * 1000003 + self.batch_index + 7) % (2 ** 62))
+        self.batch_index += 1
         t = draw_timesteps(n, "cpu", self.cpu_rng, distribution=self.dist, T=self.T, loc=self.loc, scale=self.scale)
         t = shift_timesteps(t, self.T, self.shift, self.shift_mode,
                             latent_shapes=torch.tensor([list(g) for g in plan.grids], dtype=torch.float32),

@@ -44,6 +44,8 @@ class PackedSequenceParams:
     # Context parallelism (strided shard of the joint sequence).
     cp_text_index: Optional[torch.Tensor] = None
     cp_joint_total: Optional[int] = None
+    cp_caption_lens: Optional[List[int]] = None   # full per-sample caption lengths (caption encoder)
+    cp_group: Optional[object] = None             # the cp process group of this shard
 
     @property
     def num_samples(self) -> int:

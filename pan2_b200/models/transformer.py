@@ -33,6 +33,7 @@ from ..ops import packed as P
 from ..ops.gemm import linear, grouped_linear, grouped_ffn
 from ..ops.qkv import qkv_project
 from ..ops.attention import varlen_attention, dense_attention
+from ..parallel.ulysses import ulysses_attention
 
 
 # ---------------------------------------------------------------------------------------------
@@ -206,7 +207,9 @@ class JointAttentionBlock(nn.Module):
                               self.qkv_proj.bias.view(2, 3 * self.hidden_size), self.qkv_proj.q_weight,
                               self.qkv_proj.k_weight, meta.freqs_cos, meta.freqs_sin,
                               meta.indices_interleave_to_concat, mm_bounds, self.num_heads, self.qkv_proj.eps)
-        if attn_fn is None:
+        if attn_fn is None and meta.cp_group is not None:
+            o = ulysses_attention(q, k, v, meta)
+        elif attn_fn is None:
             o = varlen_attention(q, k, v, meta.joint_cu_seqlens, meta.joint_lens, meta.joint_segment_limit)
         else:
             o = attn_fn(q, k, v, meta)
@@ -391,7 +394,8 @@ class PanVideoDiffusionTransformer(nn.Module):
         vec = vec.to(hidden_states.dtype) if hidden_states.is_floating_point() else vec
         txt = linear(rms_norm(text_states, self.cap_embedder[0].weight.to(text_states.dtype), self.cap_embedder[0].eps),
                      self.cap_embedder[1].weight, self.cap_embedder[1].bias)
-        txt = self.caption_encoder(txt, cu_seqlens=meta.caption_cu_seqlens, lens=meta.caption_lens,
+        cap_lens = meta.cp_caption_lens if meta.cp_caption_lens is not None else meta.caption_lens
+        txt = self.caption_encoder(txt, cu_seqlens=meta.caption_cu_seqlens, lens=cap_lens,
                                    max_seqlen=meta.caption_segment_limit)
         if meta.cp_text_index is not None:
             txt = txt.index_select(0, meta.cp_text_index)

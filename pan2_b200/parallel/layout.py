@@ -35,6 +35,7 @@ class ParallelLayout:
     shard_group: Optional[dist.ProcessGroup] = None
     replicate_group: Optional[dist.ProcessGroup] = None
     cpu_group: Optional[dist.ProcessGroup] = None
+    cp_cpu_group: Optional[dist.ProcessGroup] = None   # gloo twin of cp_group (host metadata)
 
     @property
     def cp_enabled(self) -> bool:
@@ -109,6 +110,11 @@ def init_parallel_layout(cp: int = 1, hybrid_shard: bool = False, timeout_s: flo
         layout.cpu_group = dist.new_group(list(range(world)), backend="gloo") if world > 1 else None
     except Exception:  # pragma: no cover
         layout.cpu_group = None
+    if cp > 1:
+        for g in cp_groups:
+            pg = dist.new_group(g, backend="gloo")
+            if rank in g:
+                layout.cp_cpu_group = pg
     _LAYOUT = layout
     return layout
 

@@ -150,9 +150,13 @@ class ShardedModel:
     """
 
     def __init__(self, units: List[Unit], group: Optional[dist.ProcessGroup], device: torch.device,
-                 offload: bool):
+                 offload: bool, replicate_group: Optional[dist.ProcessGroup] = None):
         self.units = units
         self.group = group
+        # HSDP: shards are replicated across this group (one member per node); gradients are
+        # all-reduced over it after the reduce-scatter
+        self.replicate_group = (replicate_group if replicate_group is not None and dist.is_initialized()
+                                and dist.get_world_size(replicate_group) > 1 else None)
         self.world = units[0].world if units else 1
         self.rank = dist.get_rank(group) if (group is not None and self.world > 1) else 0
         self.device = device
@@ -217,11 +221,12 @@ class ShardedModel:
         self.bind_weights(u, None)
 
     # ---------------------------------------------------------------- gradients
-    def attach_grads(self, u: Unit) -> None:
-        """Give every parameter of ``u`` a zeroed ``.grad`` view of the unit's flat bf16 gradient."""
+    def attach_grads(self, u: Unit, zero: bool = True) -> None:
+        """Give every parameter of ``u`` a ``.grad`` view of the unit's flat bf16 gradient (zeroed
+        unless ``zero`` is False: gradient accumulation with one rank)."""
         if u.full_grad is None:
             u.full_grad = torch.zeros(u.numel_full, dtype=torch.bfloat16, device=self.device)
-        else:
+        elif zero:
             u.full_grad.zero_()
         for s in u.slots:
             getattr(s.module, s.attr).grad = u.slot_full(u.full_grad, s)
@@ -246,6 +251,8 @@ class ShardedModel:
             for s in u.slots:
                 pack_rows(pk, s, u.slot_full(g, s), self.world)
             dist.reduce_scatter_tensor(out, packed, op=dist.ReduceOp.SUM, group=self.group)
+            if self.replicate_group is not None:
+                dist.all_reduce(out, op=dist.ReduceOp.SUM, group=self.replicate_group)
             if u.grad_shard is None or not accumulate:
                 u.grad_shard = out
             else:

@@ -101,12 +101,12 @@ class BlockCheckpoint(torch.autograd.Function):
         blk = engine.model.blocks[idx]
         x_ = x.detach().requires_grad_(True)
         vec_ = vec.detach().requires_grad_(True)
-        sm.attach_grads(u)
+        sm.attach_grads(u, zero=not engine.accumulating)
         params = [getattr(s.module, s.attr) for s in u.slots]
         with torch.enable_grad():
             y, _ = blk.forward_packed(x_, ln_stats, vec_, engine.meta)
         torch.autograd.backward([y], [gy], inputs=[x_, vec_] + params)
-        sm.reduce_grads(u)
+        sm.reduce_grads(u, accumulate=engine.accumulating)
         sm.release(u)
         return None, None, x_.grad, None, vec_.grad
 
@@ -138,9 +138,10 @@ class TrainEngine:
 
     def __init__(self, arch: dict, device: torch.device, *, group: Optional[dist.ProcessGroup] = None,
                  seed: int = 42, optim: Optional[OptimConfig] = None, offload: str = "auto",
-                 activation_bytes_estimate: int = 0):
+                 activation_bytes_estimate: int = 0, replicate_group: Optional[dist.ProcessGroup] = None):
         self.device = device
         self.group = group
+        self.replicate_group = replicate_group
         self.world = dist.get_world_size(group) if (group is not None and dist.is_initialized()) else 1
         self.rank = dist.get_rank(group) if self.world > 1 else 0
         self.optim = optim or OptimConfig()
@@ -191,7 +192,7 @@ class TrainEngine:
         root = _Root(model)
         units.append(self._materialise(self.n_blocks, "root", root, ""))
         self.model = model
-        self.sharded = ShardedModel(units, group, device, self.offload)
+        self.sharded = ShardedModel(units, group, device, self.offload, replicate_group)
         for u in units:
             if self.world == 1:
                 self.sharded.bind_weights(u, u.hi)
@@ -199,6 +200,8 @@ class TrainEngine:
                 self.sharded.bind_weights(u, None)
         self._alloc_optimizer_state()
         self.stash_in_grads = self.world == 1
+        self.accum_steps = 1
+        self.accumulating = False
         if self.world == 1:  # persistent gradient buffers (they also hold activation checkpoints)
             for u in units:
                 u.full_grad = torch.zeros(u.numel_full, dtype=torch.bfloat16, device=device)
@@ -270,8 +273,28 @@ class TrainEngine:
         return self.optim.use_muon and s.kind == "muon"
 
     # ---------------------------------------------------------------- step
-    def forward_backward(self, batch: dict) -> torch.Tensor:
-        """Forward + backward of one packed batch; returns the (global-mean) loss as a device scalar."""
+    def set_context_parallel(self, group, size: int, rank: int) -> None:
+        """Record the Ulysses context-parallel group.  Batches split by
+        :func:`pan2_b200.data.cp_batch.strided_split` carry the group in their metadata, and the
+        joint blocks then run attention through :func:`pan2_b200.parallel.ulysses.ulysses_attention`."""
+        self.cp_group, self.cp_size, self.cp_rank = group, int(size), int(rank)
+        if self.cp_size > 1 and self.arch.get("num_attention_heads", 32) % self.cp_size:
+            raise ValueError(f"cp_size={size} must divide the {self.arch.get('num_attention_heads')} attention heads")
+
+    def set_accumulation(self, steps: int) -> None:
+        """Prepare for ``steps`` micro-batches per optimizer step.  With more than one, gradients
+        persist across micro-batches, so activation checkpoints no longer live in gradient buffers."""
+        self.accum_steps = max(1, int(steps))
+        if self.accum_steps > 1:
+            self.stash_in_grads = False
+
+    def forward_backward(self, batch: dict, micro_step: int = 0) -> torch.Tensor:
+        """Forward + backward of one packed batch; returns the (global-mean) loss as a device scalar.
+
+        With gradient accumulation the loss is divided by the number of micro-batches and
+        micro-batches after the first add into the gradients."""
+        self.accumulating = micro_step > 0
+        scale = 1.0 / self.accum_steps
         meta: PackedSequenceParams = batch["packed_seq_params"]
         self.meta = meta
         model = self.model
@@ -280,17 +303,18 @@ class TrainEngine:
         sm.gather(root)
         if self.n_blocks:
             sm.prefetch(sm.units[0])
-        sm.attach_grads(root)
+        sm.attach_grads(root, zero=not self.accumulating)
         x, ln_stats, vec = model.embed_packed(batch["hidden_states"], batch["timestep"], batch["text_states"], meta)
         for i in range(self.n_blocks):
             x, ln_stats = BlockCheckpoint.apply(self, i, x, ln_stats, vec)
         sums = model.head_and_loss(x, ln_stats, vec, batch["target"], meta)
         glob = sums.detach().clone()
-        if self.world > 1:
-            dist.all_reduce(glob, op=dist.ReduceOp.SUM, group=self.group)
-        loss = sums[0] / glob[1]
+        if dist.is_initialized() and dist.get_world_size() > 1:
+            # global mean over every rank's tokens (shard, replica and context-parallel ranks)
+            dist.all_reduce(glob, op=dist.ReduceOp.SUM)
+        loss = sums[0] * (scale / glob[1])
         loss.backward()
-        sm.reduce_grads(root)
+        sm.reduce_grads(root, accumulate=self.accumulating)
         sm.wait_comm()
         if self.world > 1:
             sm.release(root)

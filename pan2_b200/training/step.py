@@ -41,13 +41,23 @@ class StepRunner:
         return {"forward_backward": ev[0].elapsed_time(ev[1]), "grad_norm": ev[1].elapsed_time(ev[2]),
                 "optimizer": ev[3].elapsed_time(ev[4])}
 
-    def device_step(self, batch_dev: Dict) -> Dict:
+    def device_step(self, batch_dev, poison: bool = False) -> Dict:
+        """One optimizer step over ``batch_dev`` (a device batch, or a list of micro-batches for
+        gradient accumulation).  ``poison`` makes this rank vote the update non-finite (host-side
+        fault injection)."""
         eng = self.engine
+        micro = batch_dev if isinstance(batch_dev, (list, tuple)) else [batch_dev]
+        if eng.accum_steps != len(micro):
+            eng.set_accumulation(len(micro))
         timing = eng.device.type == "cuda"
         ev = [torch.cuda.Event(enable_timing=True) for _ in range(5)] if timing else None
         if timing:
             ev[0].record()
-        loss = eng.forward_backward(batch_dev)
+        loss = None
+        for k, b in enumerate(micro):
+            lk = eng.forward_backward(b, micro_step=k)
+            loss = lk if loss is None else loss + lk
+        loss = loss / len(micro)
         if timing:
             ev[1].record()
         norm_clip = eng.grad_norm()
@@ -58,7 +68,7 @@ class StepRunner:
         if eng.device.type == "cuda":
             torch.cuda.current_stream(eng.device).synchronize()
         loss_v, norm_v = float(self.loss_host[0]), float(self.loss_host[1])
-        ok = math.isfinite(loss_v) and math.isfinite(norm_v)
+        ok = math.isfinite(loss_v) and math.isfinite(norm_v) and not poison
         if eng.world > 1:
             flag = torch.tensor([int(ok)], dtype=torch.int32)
             if self.cpu_group is not None:
@@ -83,7 +93,17 @@ class StepRunner:
         eng.set_lr(lr)
         return dict(loss=loss_v, grad_norm=norm_v, lr=lr, step_skipped=not ok)
 
-    def train_step(self, host_batch: Dict) -> Dict:
-        """Host batch in (pinned CPU tensors), metrics out (host floats)."""
-        dev_batch = batch_to_device(host_batch, self.engine.device, non_blocking=True)
-        return self.device_step(dev_batch)
+    def train_step(self, host_batch) -> Dict:
+        """Host batch (or list of micro-batches) in, pinned CPU tensors; metrics out (host floats)."""
+        if isinstance(host_batch, (list, tuple)):
+            dev = [batch_to_device(b, self.engine.device, non_blocking=True) for b in host_batch]
+        else:
+            dev = batch_to_device(host_batch, self.engine.device, non_blocking=True)
+        return self.device_step(dev)
+
+    def state_dict(self) -> Dict:
+        return {"last_epoch": self.global_step}
+
+    def load_state_dict(self, sd: Dict) -> None:
+        self.global_step = int(sd["last_epoch"])
+        self.engine.set_lr(self.base_lr * self.lr_lambda(self.global_step))

@@ -1,0 +1,218 @@
+"""Trainer on CPU (tiny model, sample data): checkpoint resume is exact, non-finite updates are skipped,
+anomalies roll back to the latest checkpoint, the heartbeat fires, checkpoints reshard."""
+import json
+import os
+import socket
+import threading
+import time
+
+import pytest
+import torch
+import torch.distributed as dist
+import torch.multiprocessing as mp
+
+from pan2_b200.data.items import HashCaptionCodec
+from pan2_b200.data.make_sample_data import write_sample_data
+from pan2_b200.training.fault import AnomalyDetector, FaultInjector, Heartbeat, InjectedFault
+
+TINY_OVERRIDES = dict(hidden_size=256, num_attention_heads=4, num_layers=2, rope_axes_dim=[16, 24, 24],
+                      text_embed_dim=64)
+
+
+@pytest.fixture(scope="module")
+def data_dir(tmp_path_factory):
+    d = tmp_path_factory.mktemp("trainer_data")
+    write_sample_data(str(d), num_videos=6, num_images=4, latent_frames=3, height=8, width=12,
+                      image_grids=((8, 8), (6, 10)))
+    return d
+
+
+def _cfg(data_dir, out, **over):
+    from pan2_b200.config.training import parse_training_config
+    argv = ["--transformer_config_overrides", json.dumps(TINY_OVERRIDES),
+            "--packed_dataloader_meta_csv_path", str(data_dir / "videos.csv"),
+            "--image_tar_path", str(data_dir / "images.tar"), "--image_sample_prob", "0.3",
+            "--packed_joint_token_budget", "300", "--packed_video_token_budget", "260",
+            "--packed_caption_token_budget", "200", "--packed_joint_segment_limit", "300",
+            "--packed_caption_segment_limit", "100", "--packed_dataloader_max_num_seq", "3",
+            "--packed_dataloader_num_buffers", "2", "--packed_dataloader_num_workers", "2",
+            "--video_height", "128", "--video_width", "192",
+            "--output_dir", str(out), "--learning_rate", "1e-3", "--warmup_steps", "2", "--log_interval", "1",
+            "--text_encoder", "hash", "--optimizer_offload", "off", "--profile_step", "-1",
+            "--anomaly_detection_warmup_steps", "1000"]
+    for k, v in over.items():
+        argv += [f"--{k}", str(v)]
+    return parse_training_config(argv)
+
+
+def _train(cfg):
+    from pan2_b200.training.trainer import Trainer
+    tr = Trainer(cfg, codec=HashCaptionCodec(embed_dim=64))
+    hist = tr.train()
+    return tr, hist
+
+
+@pytest.mark.timeout(900)
+def test_resume_is_exact(data_dir, tmp_path):
+    _, full = _train(_cfg(data_dir, tmp_path / "a", max_steps=4, save_interval=2))
+    _train(_cfg(data_dir, tmp_path / "b", max_steps=2, save_interval=2))
+    assert os.path.exists(tmp_path / "b" / "checkpoint-2" / "COMPLETE")
+    assert os.path.exists(tmp_path / "b" / "checkpoint-2" / "dataloader" / "0.json")
+    assert os.path.exists(tmp_path / "b" / "save_logging" / "checkpoint_2.txt")
+    tr, rest = _train(_cfg(data_dir, tmp_path / "b", max_steps=4, save_interval=2))
+    assert [h["step"] for h in rest] == [2, 3]
+    for a, b in zip(full[2:], rest):
+        assert a["loss"] == pytest.approx(b["loss"], rel=1e-6, abs=1e-7), (a, b)
+        assert a["grad_norm"] == pytest.approx(b["grad_norm"], rel=1e-5), (a, b)
+        assert a["lr"] == b["lr"]
+
+
+@pytest.mark.timeout(900)
+def test_skip_then_recover_and_retention(data_dir, tmp_path):
+    cfg = _cfg(data_dir, tmp_path / "c", max_steps=5, save_interval=2, save_total_limit=1,
+               fault_injection="nan_loss@3", max_consecutive_skipped_steps=0)
+    tr, hist = _train(cfg)
+    steps = [h["step"] for h in hist]
+    assert hist[steps.index(3)]["step_skipped"]
+    assert tr.total_skipped == 1 and tr.recoveries == 1
+    assert steps == [0, 1, 2, 3, 2, 3, 4]  # rolled back to checkpoint-2 after the anomaly at step 3
+    kept = sorted(d for d in os.listdir(tmp_path / "c") if d.startswith("checkpoint-"))
+    assert kept == ["checkpoint-5"]
+
+
+@pytest.mark.timeout(600)
+def test_skip_without_recovery_when_budget_allows(data_dir, tmp_path):
+    cfg = _cfg(data_dir, tmp_path / "d", max_steps=3, save_interval=100, fault_injection="nan_loss@1",
+               max_consecutive_skipped_steps=5)
+    tr, hist = _train(cfg)
+    assert [h["step_skipped"] for h in hist] == [False, True, False]
+    assert tr.recoveries == 0
+
+
+@pytest.mark.timeout(600)
+def test_injected_exception_surfaces(data_dir, tmp_path):
+    cfg = _cfg(data_dir, tmp_path / "e", max_steps=3, save_interval=100, fault_injection="raise@1")
+    with pytest.raises(InjectedFault):
+        _train(cfg)
+
+
+def test_heartbeat_fires_when_stuck():
+    fired = []
+    hb = Heartbeat(rank=0, threshold_s=0.2, poll_s=0.05, on_stuck=fired.append).start()
+    hb.beat("train_step", 7)
+    time.sleep(0.6)
+    hb.stop()
+    assert fired and "stage='train_step'" in fired[0] and "step=7" in fired[0]
+    fired.clear()
+    hb = Heartbeat(rank=0, threshold_s=0.5, poll_s=0.05, on_stuck=fired.append).start()
+    for _ in range(8):
+        hb.beat()
+        time.sleep(0.1)
+    hb.stop()
+    assert not fired
+
+
+def test_anomaly_detector_rules():
+    det = AnomalyDetector(warmup_steps=3)
+    for s in range(5):
+        assert not det(s, 1.0, 0.5)
+    assert det(5, 30.0, 0.5)          # loss spike > 20x EMA
+    assert det(6, 1.0, 10.0)          # grad spike > 6x EMA
+    assert det(7, float("nan"), 0.5)
+    assert det(8, 1.0, 2e6)           # hard limit
+    early = AnomalyDetector(warmup_steps=100)
+    early(0, 1.0, 0.5)
+    assert not early(1, 30.0, 0.5)    # spikes are ignored during warmup
+    assert early(2, float("inf"), 0.5)
+
+
+def test_fault_spec_parsing():
+    f = FaultInjector("nan_loss@2,stall@3:0.01,inf_grad@4/1", rank=0)
+    assert f.poisons_update(2) and not f.poisons_update(4)
+    assert FaultInjector("inf_grad@4/1", rank=1).poisons_update(4)
+    t = time.time()
+    f.before_step(3)
+    assert time.time() - t >= 0.01
+    m = f.after_step(2, {"loss": 1.0})["loss"]
+    assert m != m  # NaN
+    assert f.after_step(2, {"loss": 1.0})["loss"] == 1.0  # one-shot
+    assert not f.poisons_update(2)
+    with pytest.raises(ValueError):
+        FaultInjector("melt@1")
+
+
+# ---------------------------------------------------------------- checkpoint resharding
+
+def _free_port():
+    s = socket.socket()
+    s.bind(("127.0.0.1", 0))
+    p = s.getsockname()[1]
+    s.close()
+    return p
+
+
+def _save_ranks(world, rank, port, root):
+    os.environ.update(MASTER_ADDR="127.0.0.1", MASTER_PORT=str(port))
+    dist.init_process_group("gloo", rank=rank, world_size=world)
+    from pan2_b200.training.engine import TrainEngine, OptimConfig
+    from pan2_b200.checkpoint.io import save_engine, mark_complete
+    import sys
+    sys.path.insert(0, os.path.dirname(__file__))
+    from tiny import TINY_ARCH, tiny_batch
+    from pan2_b200.models.transformer import PanVideoDiffusionTransformer
+    eng = TrainEngine(dict(TINY_ARCH), torch.device("cpu"), group=dist.group.WORLD, seed=4,
+                      optim=OptimConfig(lr=1e-2), offload="off")
+    with torch.device("meta"):
+        m = PanVideoDiffusionTransformer(**TINY_ARCH)
+    batch, _ = tiny_batch(m, seed=3)
+    eng.forward_backward(batch)
+    eng.grad_norm()
+    eng.optimizer_step()
+    save_engine(eng, root)
+    sd = eng.sharded.full_state_dict()
+    states = {}
+    for u in eng.sharded.units:
+        for s in u.slots:
+            if not eng._is_muon(s):
+                continue
+            st = u.state["mom"]
+            off = eng._soff[id(s)]
+            states[s.name] = st[off:off + s.shard_rows * s.cols].clone()
+            break
+    dist.barrier()
+    if rank == 0:
+        mark_complete(root, 1)
+        torch.save(sd, os.path.join(root, "expect.pt"))
+    dist.destroy_process_group()
+
+
+@pytest.mark.timeout(900)
+def test_checkpoint_reshards_and_consolidates(tmp_path):
+    root = str(tmp_path / "checkpoint-1")
+    ctx = mp.get_context("spawn")
+    port = _free_port()
+    ps = [ctx.Process(target=_save_ranks, args=(2, r, port, root)) for r in range(2)]
+    for p in ps:
+        p.start()
+    for p in ps:
+        p.join(timeout=600)
+        assert p.exitcode == 0
+    expect = torch.load(os.path.join(root, "expect.pt"))
+    from tiny import TINY_ARCH
+    from pan2_b200.training.engine import TrainEngine, OptimConfig
+    from pan2_b200.checkpoint.io import load_engine, consolidate, load_plain_into_engine
+    eng = TrainEngine(dict(TINY_ARCH), torch.device("cpu"), seed=99, optim=OptimConfig(lr=1e-2), offload="off")
+    load_engine(eng, root)
+    got = eng.sharded.full_state_dict()
+    for k, v in expect.items():
+        assert torch.equal(got[k], v), k
+    assert eng.step_count == 1
+    assert any(u.state["mom"] is not None and u.state["mom"].abs().sum() > 0 for u in eng.sharded.units)
+    out = str(tmp_path / "plain")
+    consolidate(root, out, dtype=torch.float32, max_shard_bytes=2 * 1024 ** 2)
+    assert len([f for f in os.listdir(out) if f.endswith(".safetensors")]) > 1
+    eng2 = TrainEngine(dict(TINY_ARCH), torch.device("cpu"), seed=98, optim=OptimConfig(lr=1e-2), offload="off")
+    load_plain_into_engine(eng2, out)
+    got2 = eng2.sharded.full_state_dict()
+    for k, v in expect.items():
+        assert torch.equal(got2[k], v), k
