@@ -34,42 +34,54 @@ def _strided_count(length: int, offset: int, cp: int) -> int:
     return -(-(length - offset) // cp) if offset < length else 0
 
 
-def strided_split(batch: Dict, cp: int, rank: int, group=None) -> Dict:
-    """This cp-rank's shard of a FULL batch (``packed_seq_params`` with host lengths)."""
-    P: PackedSequenceParams = batch["packed_seq_params"]
-    dev = batch["hidden_states"].device
-    vlen, clen = list(P.video_lens), list(P.caption_lens)
-    n = len(vlen)
+def shard_rows(video_lens: List[int], caption_lens: List[int], cp: int, rank: int):
+    """Rows of cp-rank ``rank``: ``(video rows, caption rows, local video lens, local caption lens)``,
+    video / caption rows indexing the full batch's concat-order video / caption blocks."""
+    n = len(video_lens)
     vcu, ccu = [0], [0]
-    for a, b in zip(vlen, clen):
+    for a, b in zip(video_lens, caption_lens):
         vcu.append(vcu[-1] + a)
         ccu.append(ccu[-1] + b)
     jcu = [a + b for a, b in zip(vcu, ccu)]
-    S = jcu[-1]
     vrows: List[int] = []
     trows: List[int] = []
     lv, lc = [], []
     for i in range(n):
         v_off = (rank - jcu[i]) % cp
-        t_off = (rank - jcu[i] - vlen[i]) % cp
+        t_off = (rank - jcu[i] - video_lens[i]) % cp
         vrows += range(vcu[i] + v_off, vcu[i + 1], cp)
         trows += range(ccu[i] + t_off, ccu[i + 1], cp)
-        lv.append(_strided_count(vlen[i], v_off, cp))
-        lc.append(_strided_count(clen[i], t_off, cp))
-    s_local = sum(lv) + sum(lc)
-    assert s_local == shard_sizes(S, cp)[rank], (s_local, S, cp, rank)
+        lv.append(_strided_count(video_lens[i], v_off, cp))
+        lc.append(_strided_count(caption_lens[i], t_off, cp))
+    assert sum(lv) + sum(lc) == shard_sizes(jcu[-1], cp)[rank], (lv, lc, jcu[-1], cp, rank)
+    return vrows, trows, lv, lc
+
+
+def local_params(P: PackedSequenceParams, cp: int, rank: int, group, device) -> Tuple[PackedSequenceParams, torch.Tensor]:
+    """Local packed metadata of cp-rank ``rank`` for the full ``P``; also returns the video row index."""
+    vlen, clen = list(P.video_lens), list(P.caption_lens)
+    vrows, trows, lv, lc = shard_rows(vlen, clen, cp, rank)
+    S = sum(vlen) + sum(clen)
     if sum(lv) == 0:
         raise ValueError(f"cp shard {rank} of a {S}-token batch holds no video tokens (cp={cp}); use a smaller cp_size")
-    idx_v = torch.tensor(vrows, dtype=torch.long, device=dev)
-    idx_t = torch.tensor(trows, dtype=torch.long, device=dev)
+    s_local = sum(lv) + sum(lc)
+    idx_v = torch.tensor(vrows, dtype=torch.long, device=device)
+    idx_t = torch.tensor(trows, dtype=torch.long, device=device)
     cos = P.freqs_cos[:S][rank::cp]
     sin = P.freqs_sin[:S][rank::cp]
     local = build_packed_params(lv, lc, s_local, cos.reshape(s_local, -1), sin.reshape(s_local, -1),
                                 joint_segment_limit=P.joint_segment_limit,
-                                caption_segment_limit=P.caption_segment_limit).to(dev, non_blocking=True)
+                                caption_segment_limit=P.caption_segment_limit).to(device, non_blocking=True)
     local = replace(local, joint_cu_seqlens=P.joint_cu_seqlens, joint_lens=list(P.joint_lens),
                     caption_cu_seqlens=P.caption_cu_seqlens, cp_caption_lens=list(clen), cp_text_index=idx_t,
                     cp_joint_total=S, cp_group=group, active_sequence_count=P.active_sequence_count)
+    return local, idx_v
+
+
+def strided_split(batch: Dict, cp: int, rank: int, group=None) -> Dict:
+    """This cp-rank's shard of a FULL batch (``packed_seq_params`` with host lengths)."""
+    dev = batch["hidden_states"].device
+    local, idx_v = local_params(batch["packed_seq_params"], cp, rank, group, dev)
     return dict(hidden_states=batch["hidden_states"].index_select(1, idx_v).contiguous(),
                 timestep=batch["timestep"], text_states=batch["text_states"],
                 target=batch["target"].index_select(0, idx_v).contiguous(), packed_seq_params=local)

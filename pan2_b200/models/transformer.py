@@ -414,6 +414,17 @@ class PanVideoDiffusionTransformer(nn.Module):
         pred = self.output_head.forward_packed(x, vec, ln_stats, [0] + _cumsum(meta.video_lens), meta.n_video)
         return P.concat_mse_sums(pred, target, meta.n_video)
 
+    def predict_packed(self, hidden_states, timestep, text_states, meta: PackedSequenceParams,
+                       skip_layers: Sequence[int] = ()) -> torch.Tensor:
+        """Inference over a packed batch: velocity rows ``[n_video, prod(patch) * C_out]`` for the video
+        tokens (concat order).  ``skip_layers`` drops joint blocks (the STG weak prediction)."""
+        x, ln_stats, vec = self.embed_packed(hidden_states, timestep, text_states, meta)
+        for i, block in enumerate(self.blocks):
+            if i in skip_layers:
+                continue
+            x, ln_stats = block.forward_packed(x, ln_stats, vec, meta)
+        return self.output_head.forward_packed(x, vec, ln_stats, [0] + _cumsum(meta.video_lens), meta.n_video)
+
     def forward(self, hidden_states: torch.Tensor, timestep: torch.Tensor, text_states: torch.Tensor,
                 text_mask: Optional[torch.Tensor] = None, freqs_cos=None, freqs_sin=None,
                 packed_seq_params: Optional[PackedSequenceParams] = None, target: Optional[torch.Tensor] = None,
