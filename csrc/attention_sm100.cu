@@ -66,11 +66,6 @@ __device__ __forceinline__ void store_row32_swizzled(uint8_t* tile, int r, int c
   }
 }
 
-__device__ __forceinline__ uint32_t pack_bf16(float a, float b) {
-  __nv_bfloat162 h = __floats2bfloat162_rn(a, b);
-  return *reinterpret_cast<uint32_t*>(&h);
-}
-
 __device__ __forceinline__ void fence_async_smem() { asm volatile("fence.proxy.async.shared::cta;" ::: "memory"); }
 
 // 2^x on the FMA pipe: x = j + f with j = round(x) (float magic-number rounding) and |f| <= 1/2;

@@ -580,6 +580,8 @@ PYBIND11_MODULE(TORCH_EXTENSION_NAME, m) {
   m.def("mse_bwd", &pan::mse_bwd);
   m.def("gather_rows", &pan::gather_rows);
   m.def("gemm", &pan::gemm);
+  m.def("gemm_force_cta_group", &pan::gemm_force_cta_group);
+  m.def("gemm_tuning", &pan::gemm_tuning);
   m.def("gemm_grouped_nt", &pan::gemm_grouped_nt);
   m.def("gemm_batched", &pan::gemm_batched);
   m.def("gemm_dgelu", &pan::gemm_dgelu);

@@ -29,6 +29,11 @@ __device__ __forceinline__ void store8(__nv_bfloat16* p, const float (&v)[8]) {
   *reinterpret_cast<bf16x8*>(p) = r;
 }
 
+__device__ __forceinline__ uint32_t pack_bf16(float a, float b) {
+  __nv_bfloat162 h = __floats2bfloat162_rn(a, b);
+  return *reinterpret_cast<uint32_t*>(&h);
+}
+
 // Round-trip through bf16 (the value a consumer reading the stored tensor sees).
 __device__ __forceinline__ void round8(float (&v)[8]) {
 #pragma unroll

@@ -26,12 +26,27 @@ namespace pan {
 namespace gemm {
 using namespace sm100;
 
-constexpr int BM = 128, BN = 256, BK = 64, STAGES = 4;
+constexpr int BM = 128, BN = 256, BK = 64;
 constexpr int kThreads = 192;
-constexpr int A_STAGE = BM * BK * 2;  // 16 KB
-constexpr int B_STAGE = BN * BK * 2;  // 32 KB
-constexpr int SMEM_BYTES = STAGES * (A_STAGE + B_STAGE) + 1024 /*align*/ + 256 /*barriers*/;
 constexpr int kMaxGroups = 4;
+
+// CG = 1: one CTA per 128 x 256 tile.  CG = 2: a (2,1,1) cluster per 256 x 256 tile; each CTA holds
+// its 128 A rows and 128 of the 256 B rows, which cuts the L2 -> SMEM bytes per FLOP by a third.
+// Epilogue staging: every epilogue warp owns two 4 KB slots; a slot holds one 32-row x 32-column
+// block of one output (bf16 with a 64-byte swizzle, fp32 with a 128-byte swizzle) that a TMA bulk
+// store writes out as whole 64/128-byte row segments.
+constexpr int EPI_SLOT = 4096;
+constexpr int EPI_BYTES = 4 * 2 * EPI_SLOT;
+
+template <int CG, int NSTAGES = (CG == 1 ? 4 : 6)>
+struct Cfg {
+  static constexpr int TILE_M = BM * CG;
+  static constexpr int B_ROWS = BN / CG;                // B rows held by one CTA
+  static constexpr int A_STAGE = BM * BK * 2;           // 16 KB
+  static constexpr int B_STAGE = B_ROWS * BK * 2;       // 32 KB (CG 1) or 16 KB (CG 2)
+  static constexpr int STAGES = NSTAGES;
+  static constexpr int SMEM_BYTES = STAGES * (A_STAGE + B_STAGE) + EPI_BYTES + 1024 /*align*/ + 256 /*barriers*/;
+};
 
 enum Epi : int { EPI_PLAIN = 0, EPI_GELU = 1, EPI_DGELU = 2 };
 
@@ -52,6 +67,8 @@ struct Params {
   __nv_bfloat16* aux2;    // DGELU: GELU(pre) out
   long long ldaux2;
   int epi;
+  int probe;  // timing experiments only: bit 0 skips the epilogue stores, bit 1 re-reads k-block 0
+  int reduce_add;  // D += acc through TMA reduce-add stores (no read of D by the kernel)
   int accumulate;  // host-side only: folded into C = D, beta = 1
   // batched GEMMs: operand z-coordinate = batch index; D/C advance by their batch strides
   int batch;
@@ -67,6 +84,10 @@ struct Params {
 struct TmapSet {
   CUtensorMap a;
   CUtensorMap b[kMaxGroups];
+  // outputs, one map per row group clipped at that group's rows / columns
+  CUtensorMap d[kMaxGroups];
+  CUtensorMap aux[kMaxGroups];
+  CUtensorMap aux2[kMaxGroups];
 };
 
 __device__ __forceinline__ void tile_coords(const Params& p, int t, int& g, int& mb, int& nb) {
@@ -94,19 +115,27 @@ __device__ __forceinline__ float gelu_tanh_grad(float x) {
   return 0.5f * (1.f + t) + 0.5f * x * (1.f - t * t) * k0 * (1.f + 3.f * k1 * x * x);
 }
 
+template <int CG, int NSTAGES>
 __global__ void __launch_bounds__(kThreads, 1)
 gemm_kernel(const __grid_constant__ Params p, const __grid_constant__ TmapSet maps) {
+  using C = Cfg<CG, NSTAGES>;
+  constexpr int STAGES = C::STAGES, A_STAGE = C::A_STAGE, B_STAGE = C::B_STAGE;
   extern __shared__ uint8_t smem_raw[];
   uint8_t* smem = reinterpret_cast<uint8_t*>((reinterpret_cast<uintptr_t>(smem_raw) + 1023) & ~uintptr_t(1023));
   uint8_t* smem_a = smem;
   uint8_t* smem_b = smem + STAGES * A_STAGE;
-  uint64_t* bars = reinterpret_cast<uint64_t*>(smem_b + STAGES * B_STAGE);
+  uint8_t* smem_epi = smem_b + STAGES * B_STAGE;
+  uint64_t* bars = reinterpret_cast<uint64_t*>(smem_epi + EPI_BYTES);
   // bars: full[S], empty[S], tmem_full[2], tmem_empty[2]; then the TMEM base address
   uint32_t* tmem_slot = reinterpret_cast<uint32_t*>(bars + 2 * STAGES + 4);
   volatile int& s_abort = *reinterpret_cast<volatile int*>(bars + 2 * STAGES + 5);
 
   const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
   const int total_tiles = p.tile_prefix[p.n_groups] * p.batch;
+  // CG 2: the pair works on one tile; `crank` selects this CTA's half, rank 0 issues the MMAs
+  const int crank = CG == 2 ? (int)cluster_ctarank() : 0;
+  const int tile0 = CG == 2 ? (int)cluster_id_x() : (int)blockIdx.x;
+  const int tile_step = CG == 2 ? (int)nclusters_x() : (int)gridDim.x;
 
   auto full_bar = [&](int s) { return smem_u32(bars + s); };
   auto empty_bar = [&](int s) { return smem_u32(bars + STAGES + s); };
@@ -121,18 +150,24 @@ gemm_kernel(const __grid_constant__ Params p, const __grid_constant__ TmapSet ma
     }
     for (int a = 0; a < 2; ++a) {
       mbar_init(tfull_bar(a), 1);
-      mbar_init(tempty_bar(a), 4);  // one arrive per epilogue warp
+      mbar_init(tempty_bar(a), 4 * CG);  // one arrive per epilogue warp of every CTA of the pair
     }
     fence_barrier_init();
     prefetch_tmap(&maps.a);
     for (int g = 0; g < p.n_groups; ++g) prefetch_tmap(&maps.b[g]);
   }
   if (warp == 1) {
-    tmem_alloc(smem_u32(tmem_slot), 512);
-    tmem_relinquish();
+    if (CG == 2) {
+      tmem_alloc_pair(smem_u32(tmem_slot), 512);
+      tmem_relinquish_pair();
+    } else {
+      tmem_alloc(smem_u32(tmem_slot), 512);
+      tmem_relinquish();
+    }
   }
   tc_fence_before();
   __syncthreads();
+  if (CG == 2) cluster_sync();  // peer barriers initialised and TMEM allocated before any remote use
   tc_fence_after();
   const uint32_t tmem_base = *tmem_slot;
 
@@ -141,40 +176,45 @@ gemm_kernel(const __grid_constant__ Params p, const __grid_constant__ TmapSet ma
     if (lane == 0) {
       int stage = 0;
       uint32_t phase = 0;
-      for (int t = blockIdx.x; t < total_tiles && !s_abort; t += gridDim.x) {
+      for (int t = tile0; t < total_tiles && !s_abort; t += tile_step) {
         int g, mb, nb;
         tile_coords(p, t, g, mb, nb);
-        const int m0 = p.row_begin[g] + mb * BM;
-        const int n0 = nb * BN;
+        const int m0 = p.row_begin[g] + mb * C::TILE_M + crank * BM;
+        const int n0 = nb * BN + crank * C::B_ROWS;
         const int z = t / p.tiles_per_batch;
         const int k_blocks = p.k_blocks[g];
         for (int kb = 0; kb < k_blocks && !s_abort; ++kb) {
           if (!mbar_wait(empty_bar(stage), phase ^ 1, 11)) { s_abort = 1; break; }
-          const uint32_t fb = full_bar(stage);
-          mbar_expect_tx(fb, A_STAGE + B_STAGE);
+          // CG 2: both CTAs' bytes complete on the leader's full barrier
+          const uint32_t fb = CG == 2 ? mapa_shared(full_bar(stage), 0) : full_bar(stage);
+          if (crank == 0) mbar_expect_tx(full_bar(stage), CG * (A_STAGE + B_STAGE));
           const uint32_t sa = smem_u32(smem_a + stage * A_STAGE);
           const uint32_t sb = smem_u32(smem_b + stage * B_STAGE);
-          const int k0 = kb * BK;
+          const int k0 = (p.probe & 2) ? 0 : kb * BK;
+          auto load = [&](uint32_t dst, const CUtensorMap* m, int c0, int c1) {
+            if (CG == 2) tma_load_3d_pair(dst, m, fb, c0, c1, z);
+            else tma_load_3d(dst, m, fb, c0, c1, z);
+          };
           if (!p.a_mn) {
-            tma_load_3d(sa, &maps.a, fb, k0, m0, z);
+            load(sa, &maps.a, k0, m0);
           } else {
-            tma_load_3d(sa, &maps.a, fb, m0, k0, z);
-            tma_load_3d(sa + 8192, &maps.a, fb, m0 + 64, k0, z);
+            load(sa, &maps.a, m0, k0);
+            load(sa + 8192, &maps.a, m0 + 64, k0);
           }
           if (!p.b_mn) {
-            tma_load_3d(sb, &maps.b[g], fb, k0, n0, z);
+            load(sb, &maps.b[g], k0, n0);
           } else {
 #pragma unroll
-            for (int j = 0; j < 4; ++j) tma_load_3d(sb + j * 8192, &maps.b[g], fb, n0 + 64 * j, k0, z);
+            for (int j = 0; j < C::B_ROWS / 64; ++j) load(sb + j * 8192, &maps.b[g], n0 + 64 * j, k0);
           }
           if (++stage == STAGES) { stage = 0; phase ^= 1; }
         }
       }
     }
   } else if (warp == 1) {
-    // ------------------------------------------------------------------ MMA issuer
-    if (lane == 0) {
-      const uint32_t idesc = idesc_bf16_f32(BM, BN, p.a_mn, p.b_mn);
+    // ------------------------------------------------------------------ MMA issuer (pair leader)
+    if (lane == 0 && crank == 0) {
+      const uint32_t idesc = idesc_bf16_f32(C::TILE_M, BN, p.a_mn, p.b_mn);
       // K-major SW128: LBO unused (16 B), SBO = 8 rows * 128 B; K step of 16 = +32 B.
       // MN-major SW128: LBO = next 64-wide MN chunk (8 KB), SBO = next 8 k-rows (1 KB); K step = +2 KB.
       const uint32_t a_lbo = p.a_mn ? 8192 : 16, b_lbo = p.b_mn ? 8192 : 16;
@@ -183,7 +223,7 @@ gemm_kernel(const __grid_constant__ Params p, const __grid_constant__ TmapSet ma
       uint32_t phase = 0;
       int acc = 0;
       uint32_t acc_phase = 0;
-      for (int t = blockIdx.x; t < total_tiles && !s_abort; t += gridDim.x) {
+      for (int t = tile0; t < total_tiles && !s_abort; t += tile_step) {
         if (!mbar_wait(tempty_bar(acc), acc_phase ^ 1, 12)) { s_abort = 1; break; }
         tc_fence_after();
         int g, mb, nb;
@@ -200,28 +240,70 @@ gemm_kernel(const __grid_constant__ Params p, const __grid_constant__ TmapSet ma
           for (int kk = 0; kk < BK / 16; ++kk) {
             const uint64_t ad = smem_desc_sw128(sa + kk * a_kstep, a_lbo, 1024);
             const uint64_t bd = smem_desc_sw128(sb + kk * b_kstep, b_lbo, 1024);
-            mma_bf16_ss(d_tmem, ad, bd, idesc, (kb | kk) != 0);
+            if (CG == 2) mma_bf16_ss_pair(d_tmem, ad, bd, idesc, (kb | kk) != 0);
+            else mma_bf16_ss(d_tmem, ad, bd, idesc, (kb | kk) != 0);
           }
-          mma_commit(empty_bar(stage));  // frees the smem stage when these MMAs retire
+          // frees the smem stage (in both CTAs of a pair) when these MMAs retire
+          if (CG == 2) mma_commit_pair(empty_bar(stage), 0x3);
+          else mma_commit(empty_bar(stage));
           if (++stage == STAGES) { stage = 0; phase ^= 1; }
         }
         if (!ok) { s_abort = 1; break; }
-        mma_commit(tfull_bar(acc));  // accumulator ready for the epilogue
+        if (CG == 2) mma_commit_pair(tfull_bar(acc), 0x3);  // accumulator ready for both epilogues
+        else mma_commit(tfull_bar(acc));
         if (++acc == 2) { acc = 0; acc_phase ^= 1; }
       }
     }
   } else {
     // ------------------------------------------------------------------ epilogue (warps 2..5)
     const int q = warp & 3;  // TMEM lane quarter this warp may access
+    uint8_t* slots = smem_epi + q * 2 * EPI_SLOT;
+    int n_used = 0;
+    // next staging slot; the bulk store that last read it (two stores ago) must have finished reading
+    auto acquire = [&]() -> uint8_t* {
+      uint8_t* b = slots + (n_used & 1) * EPI_SLOT;
+      if (n_used >= 2 && lane == 0) bulk_wait_read<1>();
+      __syncwarp();
+      ++n_used;
+      return b;
+    };
+    // this lane's row of a 32 x 32 block: bf16 rows of 64 B (64-byte swizzle), fp32 rows of 128 B
+    auto put_bf16 = [&](uint8_t* b, const float* v) {
+#pragma unroll
+      for (int j = 0; j < 4; ++j) {
+        uint4 w;
+        w.x = pack_bf16(v[8 * j + 0], v[8 * j + 1]);
+        w.y = pack_bf16(v[8 * j + 2], v[8 * j + 3]);
+        w.z = pack_bf16(v[8 * j + 4], v[8 * j + 5]);
+        w.w = pack_bf16(v[8 * j + 6], v[8 * j + 7]);
+        *reinterpret_cast<uint4*>(b + lane * 64 + ((j ^ ((lane >> 1) & 3)) << 4)) = w;
+      }
+    };
+    auto put_f32 = [&](uint8_t* b, const float* v) {
+#pragma unroll
+      for (int j = 0; j < 8; ++j)
+        *reinterpret_cast<float4*>(b + lane * 128 + ((j ^ (lane & 7)) << 4)) =
+            make_float4(v[4 * j], v[4 * j + 1], v[4 * j + 2], v[4 * j + 3]);
+    };
+    auto issue = [&](const CUtensorMap* m, uint8_t* b, int col, int row, int z, bool add = false) {
+      fence_async_shared();
+      __syncwarp();
+      if (lane == 0) {
+        if (add) tma_reduce_add_3d(m, smem_u32(b), col, row, z);
+        else tma_store_3d(m, smem_u32(b), col, row, z);
+        bulk_commit();
+      }
+    };
     int acc = 0;
     uint32_t acc_phase = 0;
-    for (int t = blockIdx.x; t < total_tiles && !s_abort; t += gridDim.x) {
+    for (int t = tile0; t < total_tiles && !s_abort; t += tile_step) {
       if (!mbar_wait(tfull_bar(acc), acc_phase, 14)) { s_abort = 1; break; }
       tc_fence_after();
       int g, mb, nb;
       tile_coords(p, t, g, mb, nb);
-      const long long zb = t / p.tiles_per_batch;
-      const int row = p.row_begin[g] + mb * BM + q * 32 + lane;
+      const int zb = t / p.tiles_per_batch;
+      const int row0 = p.row_begin[g] + mb * C::TILE_M + crank * BM + q * 32;  // first row of this warp
+      const int row = row0 + lane;
       const bool row_ok = row < p.row_end[g];
       const int n_lim = p.n_cols[g];
       const __nv_bfloat16* bias = p.bias[g];
@@ -231,15 +313,15 @@ gemm_kernel(const __grid_constant__ Params p, const __grid_constant__ TmapSet ma
         uint32_t r[32];
         tmem_ld32(t_row + ch * 32, r);
         tmem_ld_wait();
-        if (!row_ok || c0 >= n_lim) continue;
+        if (c0 >= n_lim || (p.probe & 1)) continue;
+        float o[32];
 #pragma unroll
-        for (int v8 = 0; v8 < 4; ++v8) {
-          const int c = c0 + v8 * 8;
-          if (c >= n_lim) break;
-          float o[8];
+        for (int i = 0; i < 32; ++i) o[i] = p.alpha * __uint_as_float(r[i]);
+        if (p.C != nullptr && row_ok) {
 #pragma unroll
-          for (int i = 0; i < 8; ++i) o[i] = p.alpha * __uint_as_float(r[v8 * 8 + i]);
-          if (p.C != nullptr) {
+          for (int v8 = 0; v8 < 4; ++v8) {
+            const int c = c0 + v8 * 8;
+            if (c >= n_lim) break;
             float cv[8];
             if (p.c_fp32) {
               const float* cp = reinterpret_cast<const float*>(p.C) + zb * p.c_bstride + (size_t)row * p.ldc + c;
@@ -251,53 +333,68 @@ gemm_kernel(const __grid_constant__ Params p, const __grid_constant__ TmapSet ma
               load8(reinterpret_cast<const __nv_bfloat16*>(p.C) + zb * p.c_bstride + (size_t)row * p.ldc + c, cv);
             }
 #pragma unroll
-            for (int i = 0; i < 8; ++i) o[i] += p.beta * cv[i];
+            for (int i = 0; i < 8; ++i) o[v8 * 8 + i] += p.beta * cv[i];
           }
-          if (bias != nullptr) {
+        }
+        if (bias != nullptr) {
+#pragma unroll
+          for (int v8 = 0; v8 < 4; ++v8) {
+            const int c = c0 + v8 * 8;
+            if (c >= n_lim) break;
             float b[8];
             load8(bias + c, b);
 #pragma unroll
-            for (int i = 0; i < 8; ++i) o[i] += b[i];
-          }
-          if (p.epi == EPI_GELU) {
-            float pre[8];
-#pragma unroll
-            for (int i = 0; i < 8; ++i) pre[i] = o[i];
-            store8(p.aux + (size_t)row * p.ldaux + c, pre);
-#pragma unroll
-            for (int i = 0; i < 8; ++i) o[i] = gelu_tanh(__bfloat162float(__float2bfloat16_rn(pre[i])));
-          } else if (p.epi == EPI_DGELU) {
-            float pre[8], post[8];
-            load8(p.aux + (size_t)row * p.ldaux + c, pre);
-#pragma unroll
-            for (int i = 0; i < 8; ++i) {
-              post[i] = gelu_tanh(pre[i]);
-              o[i] *= gelu_tanh_grad(pre[i]);
-            }
-            store8(p.aux2 + (size_t)row * p.ldaux2 + c, post);
-          }
-          if (p.d_fp32) {
-            float* d = reinterpret_cast<float*>(p.D) + zb * p.d_bstride + (size_t)row * p.ldd + c;
-            *reinterpret_cast<float4*>(d) = make_float4(o[0], o[1], o[2], o[3]);
-            *reinterpret_cast<float4*>(d + 4) = make_float4(o[4], o[5], o[6], o[7]);
-          } else {
-            __nv_bfloat16* d = reinterpret_cast<__nv_bfloat16*>(p.D) + zb * p.d_bstride + (size_t)row * p.ldd + c;
-            store8(d, o);
+            for (int i = 0; i < 8; ++i) o[v8 * 8 + i] += b[i];
           }
         }
+        if (p.epi == EPI_GELU) {
+          uint8_t* sb = acquire();
+          put_bf16(sb, o);  // pre-activation
+          issue(&maps.aux[g], sb, c0, row0, zb);
+#pragma unroll
+          for (int i = 0; i < 32; ++i) o[i] = gelu_tanh(__bfloat162float(__float2bfloat16_rn(o[i])));
+        } else if (p.epi == EPI_DGELU) {
+          float pre[32];
+#pragma unroll
+          for (int v8 = 0; v8 < 4; ++v8) {
+            const int c = c0 + v8 * 8;
+            float x[8] = {0.f, 0.f, 0.f, 0.f, 0.f, 0.f, 0.f, 0.f};
+            if (row_ok && c < n_lim) load8(p.aux + (size_t)row * p.ldaux + c, x);
+#pragma unroll
+            for (int i = 0; i < 8; ++i) pre[v8 * 8 + i] = x[i];
+          }
+#pragma unroll
+          for (int i = 0; i < 32; ++i) o[i] *= gelu_tanh_grad(pre[i]);
+#pragma unroll
+          for (int i = 0; i < 32; ++i) pre[i] = gelu_tanh(pre[i]);
+          uint8_t* sb = acquire();
+          put_bf16(sb, pre);  // post-activation
+          issue(&maps.aux2[g], sb, c0, row0, zb);
+        }
+        uint8_t* sb = acquire();
+        if (p.d_fp32) put_f32(sb, o);
+        else put_bf16(sb, o);
+        issue(&maps.d[g], sb, c0, row0, zb, p.reduce_add != 0);
       }
       tc_fence_before();
       __syncwarp();
-      if (lane == 0) mbar_arrive(tempty_bar(acc));
+      if (lane == 0) {
+        // the leader's MMA warp reuses the accumulator once every epilogue warp of the pair is done
+        if (CG == 2) mbar_arrive_cluster(mapa_shared(tempty_bar(acc), 0));
+        else mbar_arrive(tempty_bar(acc));
+      }
       if (++acc == 2) { acc = 0; acc_phase ^= 1; }
     }
+    if (lane == 0) bulk_wait_all();
   }
 
   tc_fence_before();
   __syncthreads();
+  if (CG == 2) cluster_sync();  // the peer's MMAs / arrivals target this CTA until both are done
   if (warp == 1) {
     tc_fence_after();
-    tmem_dealloc(tmem_base, 512);
+    if (CG == 2) tmem_dealloc_pair(tmem_base, 512);
+    else tmem_dealloc(tmem_base, 512);
   }
 }
 
@@ -319,25 +416,40 @@ EncodeTiledFn encode_fn() {
   return fn;
 }
 
-// 3-D bf16 tensor map over `batch` row-major [rows, cols] matrices (row stride `ld`, batch stride
-// `bstride` elements), box [1, box_rows, box_cols] with 128-byte swizzle (box_cols * 2 == 128).
+// 3-D tensor map over `batch` row-major [rows, cols] matrices (row stride `ld`, batch stride `bstride`
+// elements), box [1, box_rows, box_cols].  Operand maps use bf16 with a 128-byte swizzle (box_cols * 2
+// == 128); output maps use bf16 / fp32 with the swizzle matching their 64 / 128-byte box rows.
 const char* make_map(CUtensorMap* m, const void* base, long long rows, long long cols, long long ld, int box_rows,
-                     int box_cols, int batch = 1, long long bstride = 0) {
+                     int box_cols, int batch = 1, long long bstride = 0,
+                     CUtensorMapDataType dtype = CU_TENSOR_MAP_DATA_TYPE_BFLOAT16, int esize = 2,
+                     CUtensorMapSwizzle swz = CU_TENSOR_MAP_SWIZZLE_128B) {
   if (reinterpret_cast<uintptr_t>(base) % 16 != 0) return "TMA base must be 16-byte aligned";
-  if ((ld * 2) % 16 != 0) return "TMA row stride must be a multiple of 16 bytes";
-  if (batch > 1 && (bstride * 2) % 16 != 0) return "TMA batch stride must be a multiple of 16 bytes";
+  if ((ld * esize) % 16 != 0) return "TMA row stride must be a multiple of 16 bytes";
+  if (batch > 1 && (bstride * esize) % 16 != 0) return "TMA batch stride must be a multiple of 16 bytes";
   EncodeTiledFn fn = encode_fn();
   if (fn == nullptr) return "cuTensorMapEncodeTiled is unavailable";
+  if (rows < 1) rows = 1;
   if (batch <= 1) bstride = ld * rows;
   cuuint64_t dims[3] = {(cuuint64_t)cols, (cuuint64_t)rows, (cuuint64_t)(batch < 1 ? 1 : batch)};
-  cuuint64_t strides[2] = {(cuuint64_t)(ld * 2), (cuuint64_t)(bstride * 2)};
+  cuuint64_t strides[2] = {(cuuint64_t)(ld * esize), (cuuint64_t)(bstride * esize)};
   cuuint32_t box[3] = {(cuuint32_t)box_cols, (cuuint32_t)box_rows, 1};
   cuuint32_t estr[3] = {1, 1, 1};
-  CUresult r = fn(m, CU_TENSOR_MAP_DATA_TYPE_BFLOAT16, 3, const_cast<void*>(base), dims, strides, box, estr,
-                  CU_TENSOR_MAP_INTERLEAVE_NONE, CU_TENSOR_MAP_SWIZZLE_128B, CU_TENSOR_MAP_L2_PROMOTION_L2_256B,
-                  CU_TENSOR_MAP_FLOAT_OOB_FILL_NONE);
+  CUresult r = fn(m, dtype, 3, const_cast<void*>(base), dims, strides, box, estr, CU_TENSOR_MAP_INTERLEAVE_NONE, swz,
+                  CU_TENSOR_MAP_L2_PROMOTION_L2_256B, CU_TENSOR_MAP_FLOAT_OOB_FILL_NONE);
   return r == CUDA_SUCCESS ? nullptr : "cuTensorMapEncodeTiled failed";
 }
+
+// Output map of one row group: clipped at the group's last row and column, 32 x 32 boxes.
+const char* make_out_map(CUtensorMap* m, const void* base, int row_end, int n, long long ld, bool fp32, int batch,
+                         long long bstride) {
+  return make_map(m, base, row_end, n, ld, 32, 32, batch, bstride,
+                  fp32 ? CU_TENSOR_MAP_DATA_TYPE_FLOAT32 : CU_TENSOR_MAP_DATA_TYPE_BFLOAT16, fp32 ? 4 : 2,
+                  fp32 ? CU_TENSOR_MAP_SWIZZLE_128B : CU_TENSOR_MAP_SWIZZLE_64B);
+}
+
+int g_forced_cta_group = 0;  // 0: choose per launch; 1 / 2: force (tests, A/B timing)
+int g_pair_stages = 6;       // smem stages of the CTA-pair kernel (4 or 6)
+int g_probe = 0;             // Params::probe of every launch (timing experiments)
 
 int num_sms() {
   static int n = 0;
@@ -381,14 +493,33 @@ const char* launch_gemm(const GemmArgs& a, cudaStream_t stream) {
   p.ldc = a.ldc;
   p.c_bstride = a.c_bstride;
   p.c_fp32 = a.c_fp32;
-  if (a.accumulate) {  // D += acc  ==  C = D, beta = 1
-    p.C = a.D;
-    p.ldc = a.ldd;
-    p.c_bstride = a.d_bstride;
-    p.c_fp32 = a.d_fp32;
-    p.beta = 1.f;
+  if (a.accumulate) {
+    if (a.C == nullptr && a.epi == EPI_PLAIN && a.d_fp32) {
+      // D += alpha * acc (+ bias): the L2 adds through TMA reduce-add stores; D is never read
+      p.reduce_add = 1;
+    } else {  // D += acc  ==  C = D, beta = 1
+      p.C = a.D;
+      p.ldc = a.ldd;
+      p.c_bstride = a.d_bstride;
+      p.c_fp32 = a.d_fp32;
+      p.beta = 1.f;
+    }
   }
   if (p.C != nullptr && (p.ldc % 8 != 0 && !p.c_fp32)) return "gemm: C row stride must be a multiple of 8";
+  // CTA pairs for large single-batch GEMMs whose row groups fill 256-row tiles; the batched
+  // 128-row Gram products of Muon and small problems keep one CTA per tile.
+  int min_rows = 1 << 30;
+  long long pair_tiles = 0;
+  for (int g = 0; g < G; ++g) {
+    const int rows = a.groups[g].row_end > a.groups[g].row_begin ? a.groups[g].row_end - a.groups[g].row_begin : 0;
+    if (rows > 0) min_rows = rows < min_rows ? rows : min_rows;
+    pair_tiles += (long long)((rows + 255) / 256) * ((a.groups[g].n + BN - 1) / BN);
+  }
+  int cg = (p.batch == 1 && min_rows >= 256 && pair_tiles >= 16) ? 2 : 1;
+  const int forced = g_forced_cta_group;
+  if (forced == 1 || (forced == 2 && p.batch == 1)) cg = forced;
+  const int tile_m = BM * cg;
+  const int b_rows = BN / cg;
   TmapSet maps;
   const char* err = !a.a_mn ? make_map(&maps.a, a.A, a.M, a.K, a.lda, BM, BK, p.batch, a.a_bstride)
                             : make_map(&maps.a, a.A, a.K, a.M, a.lda, BK, 64, p.batch, a.a_bstride);
@@ -400,8 +531,16 @@ const char* launch_gemm(const GemmArgs& a, cudaStream_t stream) {
     if (gr.k > a.K) return "gemm: group K must be <= K";
     if (gr.ldb % 8 != 0) return "gemm: B row stride must be a multiple of 8 elements";
     if (gr.n % 8 != 0) return "gemm: N must be a multiple of 8";
-    err = !a.b_mn ? make_map(&maps.b[g], gr.B, gr.n, gr.k, gr.ldb, BN, BK, p.batch, a.b_bstride)
+    err = !a.b_mn ? make_map(&maps.b[g], gr.B, gr.n, gr.k, gr.ldb, b_rows, BK, p.batch, a.b_bstride)
                   : make_map(&maps.b[g], gr.B, gr.k, gr.n, gr.ldb, BK, 64, p.batch, a.b_bstride);
+    if (err) return err;
+    err = make_out_map(&maps.d[g], a.D, gr.row_end, gr.n, a.ldd, a.d_fp32, p.batch, a.d_bstride);
+    if (err) return err;
+    if (a.epi == EPI_GELU) err = make_out_map(&maps.aux[g], a.aux, gr.row_end, gr.n, a.ldaux, false, 1, 0);
+    else maps.aux[g] = maps.d[g];
+    if (err) return err;
+    if (a.epi == EPI_DGELU) err = make_out_map(&maps.aux2[g], a.aux2, gr.row_end, gr.n, a.ldaux2, false, 1, 0);
+    else maps.aux2[g] = maps.d[g];
     if (err) return err;
     p.row_begin[g] = gr.row_begin;
     p.row_end[g] = gr.row_end;
@@ -409,24 +548,73 @@ const char* launch_gemm(const GemmArgs& a, cudaStream_t stream) {
     p.k_blocks[g] = (gr.k + BK - 1) / BK;
     p.bias[g] = reinterpret_cast<const __nv_bfloat16*>(gr.bias);
     const int rows = gr.row_end > gr.row_begin ? gr.row_end - gr.row_begin : 0;
-    p.m_tiles[g] = (rows + BM - 1) / BM;
+    p.m_tiles[g] = (rows + tile_m - 1) / tile_m;
     p.n_tiles[g] = (gr.n + BN - 1) / BN;
     tiles += p.m_tiles[g] * p.n_tiles[g];
     p.tile_prefix[g + 1] = tiles;
   }
-  for (int g = G; g < kMaxGroups; ++g) maps.b[g] = maps.b[0];
+  for (int g = G; g < kMaxGroups; ++g) {
+    maps.b[g] = maps.b[0];
+    maps.d[g] = maps.d[0];
+    maps.aux[g] = maps.aux[0];
+    maps.aux2[g] = maps.aux2[0];
+  }
   p.tiles_per_batch = tiles;
   tiles *= p.batch;
   if (tiles == 0) return nullptr;
-  static bool attr_set = false;
-  if (!attr_set) {
-    if (cudaFuncSetAttribute(gemm_kernel, cudaFuncAttributeMaxDynamicSharedMemorySize, SMEM_BYTES) != cudaSuccess)
-      return "gemm: cannot set the dynamic shared memory size";
-    attr_set = true;
+  p.probe = g_probe;
+  if (cg == 1) {
+    static bool attr1 = false;
+    if (!attr1) {
+      if (cudaFuncSetAttribute(gemm_kernel<1, 4>, cudaFuncAttributeMaxDynamicSharedMemorySize,
+                               Cfg<1, 4>::SMEM_BYTES) != cudaSuccess)
+        return "gemm: cannot set the dynamic shared memory size";
+      attr1 = true;
+    }
+    const int grid = tiles < num_sms() ? tiles : num_sms();
+    gemm_kernel<1, 4><<<grid, kThreads, Cfg<1, 4>::SMEM_BYTES, stream>>>(p, maps);
+  } else {
+    const int clusters = tiles < num_sms() / 2 ? tiles : num_sms() / 2;
+    cudaLaunchConfig_t cfg = {};
+    cfg.gridDim = dim3(2 * clusters, 1, 1);
+    cfg.blockDim = dim3(kThreads, 1, 1);
+    cfg.stream = stream;
+    cudaLaunchAttribute attr[1];
+    attr[0].id = cudaLaunchAttributeClusterDimension;
+    attr[0].val.clusterDim.x = 2;
+    attr[0].val.clusterDim.y = 1;
+    attr[0].val.clusterDim.z = 1;
+    cfg.attrs = attr;
+    cfg.numAttrs = 1;
+    cudaError_t e;
+    switch (g_pair_stages) {
+#define PAN_PAIR_LAUNCH(S)                                                                                         \
+  case S: {                                                                                                      \
+    static bool set = false;                                                                                     \
+    if (!set) {                                                                                                  \
+      if (cudaFuncSetAttribute(gemm_kernel<2, S>, cudaFuncAttributeMaxDynamicSharedMemorySize,                   \
+                               Cfg<2, S>::SMEM_BYTES) != cudaSuccess)                                            \
+        return "gemm: cannot set the dynamic shared memory size";                                                \
+      set = true;                                                                                                \
+    }                                                                                                            \
+    cfg.dynamicSmemBytes = Cfg<2, S>::SMEM_BYTES;                                                                \
+    e = cudaLaunchKernelEx(&cfg, gemm_kernel<2, S>, p, maps);                                                    \
+    break;                                                                                                       \
   }
-  const int grid = tiles < num_sms() ? tiles : num_sms();
-  gemm_kernel<<<grid, kThreads, SMEM_BYTES, stream>>>(p, maps);
+      PAN_PAIR_LAUNCH(4)
+      default:
+      PAN_PAIR_LAUNCH(6)
+#undef PAN_PAIR_LAUNCH
+    }
+    if (e != cudaSuccess) return "gemm: pair launch failed";
+  }
   return cudaGetLastError() == cudaSuccess ? nullptr : "gemm: launch failed";
+}
+
+void gemm_force_cta_group(int cg) { gemm::g_forced_cta_group = (cg == 1 || cg == 2) ? cg : 0; }
+void gemm_tuning(int pair_stages, int probe) {
+  gemm::g_pair_stages = pair_stages == 4 ? 4 : 6;
+  gemm::g_probe = probe;
 }
 
 int gemm_error_flag(bool reset) {

@@ -66,5 +66,9 @@ struct GemmArgs {
 // Returns an error string (nullptr on success).
 const char* launch_gemm(const GemmArgs& args, cudaStream_t s);
 int gemm_error_flag(bool reset);
+// 0: CTA pairs or single CTAs chosen per launch; 1 / 2: forced.
+void gemm_force_cta_group(int cg);
+// CTA-pair smem stages (4 or 6) and timing-probe bits (0 in normal use).
+void gemm_tuning(int pair_stages, int probe);
 
 }  // namespace pan

@@ -31,8 +31,16 @@ def bf(*shape, scale=1.0):
     return (torch.randn(*shape, device="cuda") * scale).to(torch.bfloat16)
 
 
-@pytest.mark.parametrize("M,N,K", [(128, 256, 64), (300, 200, 136), (1024, 768, 512), (77, 4096, 256)])
-def test_gemm_nt(M, N, K):
+@pytest.fixture(params=[1, 2], ids=["cta1", "cta2"])
+def cta_group(request):
+    ext().gemm_force_cta_group(request.param)
+    yield request.param
+    ext().gemm_force_cta_group(0)
+
+
+@pytest.mark.parametrize("M,N,K", [(128, 256, 64), (300, 200, 136), (1024, 768, 512), (77, 4096, 256),
+                                   (2304, 2048, 1024)])
+def test_gemm_nt(M, N, K, cta_group):
     a, b = bf(M, K), bf(N, K)
     bias = bf(N)
     out = torch.empty(M, N, device="cuda", dtype=torch.bfloat16)
@@ -41,16 +49,16 @@ def test_gemm_nt(M, N, K):
     assert_close(out, ref, 1e-2, "nt")
 
 
-@pytest.mark.parametrize("M,N,K", [(256, 128, 256), (300, 200, 136), (512, 1024, 768)])
-def test_gemm_nn(M, N, K):
+@pytest.mark.parametrize("M,N,K", [(256, 128, 256), (300, 200, 136), (512, 1024, 768), (1300, 1536, 512)])
+def test_gemm_nn(M, N, K, cta_group):
     a, b = bf(M, K), bf(K, N)
     out = torch.empty(M, N, device="cuda", dtype=torch.bfloat16)
     ext().gemm(a, b, out, True, False, None, None, False)
     assert_close(out, a.float() @ b.float(), 1e-2, "nn")
 
 
-@pytest.mark.parametrize("M,N,K", [(256, 256, 128), (200, 136, 300), (768, 512, 1000)])
-def test_gemm_tn_fp32_accumulate(M, N, K):
+@pytest.mark.parametrize("M,N,K", [(256, 256, 128), (200, 136, 300), (768, 512, 1000), (1024, 2048, 640)])
+def test_gemm_tn_fp32_accumulate(M, N, K, cta_group):
     a, b = bf(K, M), bf(K, N)
     out = torch.randn(M, N, device="cuda")
     base = out.clone()
@@ -58,7 +66,7 @@ def test_gemm_tn_fp32_accumulate(M, N, K):
     assert_close(out, base + a.float().t() @ b.float(), 1e-2, "tn")
 
 
-def test_gemm_gelu_and_dgelu():
+def test_gemm_gelu_and_dgelu(cta_group):
     M, N, K = 384, 512, 256
     a, b, bias = bf(M, K), bf(N, K, scale=0.1), bf(N)
     pre = torch.empty(M, N, device="cuda", dtype=torch.bfloat16)
@@ -79,7 +87,7 @@ def test_gemm_gelu_and_dgelu():
     assert_close(post, g.detach(), 2e-2, "post")
 
 
-def test_gemm_grouped_two_weights():
+def test_gemm_grouped_two_weights(cta_group):
     L, K = 700, 256
     x = bf(L, K)
     w = [bf(384, K), bf(256, K)]
