@@ -562,7 +562,36 @@ void ns_scale_by_invnorm(torch::Tensor Q, torch::Tensor norm2, double eps) {
 }
 
 int error_flag(bool reset) {
-  return gemm_error_flag(reset) | packed_ops_error_flag(reset) | attn_error_flag(reset);
+  return gemm_error_flag(reset) | packed_ops_error_flag(reset) | attn_error_flag(reset) | comm_error_flag(reset);
+}
+
+// ---------------------------------------------------------------- peer-memory collectives
+void symm_barrier(torch::Tensor pads, int64_t rank, int64_t world, int64_t epoch, int64_t channel,
+                  int64_t timeout_ms) {
+  TORCH_CHECK(pads.is_cuda() && pads.scalar_type() == torch::kInt64 && pads.numel() >= world, "pads: int64 [world]");
+  check_launch(launch_symm_barrier(reinterpret_cast<const uint64_t*>(pads.data_ptr<int64_t>()), (int)rank, (int)world,
+                                   (uint32_t)epoch, (int)channel, (int)timeout_ms, stream()),
+               "symm_barrier");
+}
+
+// segs: int64 [n, 3] (src, dst, n elements); prefix: int64 [n] work-unit prefix; seg_peer: int32 [n]
+void peer_gather(torch::Tensor peers, torch::Tensor segs, torch::Tensor seg_peer, torch::Tensor prefix, int64_t total,
+                 torch::Tensor out) {
+  TORCH_CHECK(out.scalar_type() == torch::kBFloat16 && out.is_contiguous(), "peer_gather: bf16 contiguous output");
+  check_launch(launch_peer_gather(reinterpret_cast<const uint64_t*>(peers.data_ptr<int64_t>()), segs.data_ptr<int64_t>(),
+                                  seg_peer.data_ptr<int32_t>(), reinterpret_cast<const long long*>(prefix.data_ptr<int64_t>()),
+                                  (int)segs.size(0), total,
+                                  out.data_ptr(), stream()),
+               "peer_gather");
+}
+
+void peer_reduce(torch::Tensor peers, int64_t world, torch::Tensor segs, torch::Tensor prefix, int64_t total,
+                 double scale, torch::Tensor out) {
+  TORCH_CHECK(out.scalar_type() == torch::kFloat32 && out.is_contiguous(), "peer_reduce: fp32 contiguous output");
+  check_launch(launch_peer_reduce(reinterpret_cast<const uint64_t*>(peers.data_ptr<int64_t>()), (int)world,
+                                  segs.data_ptr<int64_t>(), reinterpret_cast<const long long*>(prefix.data_ptr<int64_t>()),
+                                  (int)segs.size(0), total, (float)scale, out.data_ptr<float>(), stream()),
+               "peer_reduce");
 }
 
 }  // namespace pan
@@ -601,4 +630,7 @@ PYBIND11_MODULE(TORCH_EXTENSION_NAME, m) {
   m.def("ns_add_diag", &pan::ns_add_diag);
   m.def("ns_scale_by_invnorm", &pan::ns_scale_by_invnorm);
   m.def("error_flag", &pan::error_flag, py::arg("reset") = true);
+  m.def("symm_barrier", &pan::symm_barrier);
+  m.def("peer_gather", &pan::peer_gather);
+  m.def("peer_reduce", &pan::peer_reduce);
 }

@@ -71,4 +71,13 @@ void gemm_force_cta_group(int cg);
 // CTA-pair smem stages (4 or 6) and timing-probe bits (0 in normal use).
 void gemm_tuning(int pair_stages, int probe);
 
+// ------------------------------------------------------------------ comm_ops.cu (peer memory)
+const char* launch_symm_barrier(const uint64_t* pads, int rank, int world, uint32_t epoch, int channel,
+                                int timeout_ms, cudaStream_t s);
+const char* launch_peer_gather(const uint64_t* peers, const void* segs, const int* seg_peer, const long long* prefix,
+                               int n_seg, long long total, void* out, cudaStream_t s);
+const char* launch_peer_reduce(const uint64_t* peers, int world, const void* segs, const long long* prefix, int n_seg,
+                               long long total, float scale, float* out, cudaStream_t s);
+int comm_error_flag(bool reset);
+
 }  // namespace pan

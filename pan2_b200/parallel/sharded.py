@@ -70,6 +70,7 @@ class Unit:
     grad_shard: Optional[torch.Tensor] = None  # fp32 [numel_shard] (world > 1)
     state: Dict[str, torch.Tensor] = field(default_factory=dict)  # optimizer state (flat shard layout)
     gather_event: Optional[torch.cuda.Event] = None
+    grad_slot: int = 0                          # peer mode: gradient ring slot of the current backward
 
     def slot_full(self, buf: torch.Tensor, s: ParamSlot) -> torch.Tensor:
         return buf[s.full_off:s.full_off + s.numel].view(s.shape)
@@ -162,6 +163,14 @@ class ShardedModel:
         self.device = device
         self.offload = offload
         self.comm_stream = torch.cuda.Stream(device) if device.type == "cuda" else None
+        # peer-memory collectives (enable_peer_memory): hi shards and a ring of gradient buffers live
+        # in symmetric memory, gathers / reductions are single kernels reading peers over NVLink
+        self.peer = False
+        self.n_reduce = 0           # gradient reductions issued so far (identical on every rank)
+        self._ring_next = 0         # block gradients attached so far
+        self._slot_last: Dict[int, int] = {}   # slot -> index of the reduction that last read it
+        self._latest: Optional[Tuple[int, torch.cuda.Event]] = None  # last reduction barrier passed
+        self._begin_event: Optional[torch.cuda.Event] = None
 
     # ---------------------------------------------------------------- parameter views
     def bind_weights(self, u: Unit, full: Optional[torch.Tensor]) -> None:
@@ -172,6 +181,58 @@ class ShardedModel:
                 p.data = torch.empty(0, dtype=torch.bfloat16, device=self.device)
             else:
                 p.data = u.slot_full(full, s)
+
+    # ---------------------------------------------------------------- peer memory
+    GRAD_SLOTS = 4  # slot 0: the root unit's gradient (alive for the whole backward); 1..3: block ring
+
+    def enable_peer_memory(self) -> bool:
+        """Move ``hi`` shards into symmetric memory and set up the fused gather / reduce plans.
+        Returns False (NCCL collectives stay in use) when peer memory is unavailable."""
+        from .symm import GatherPlan, PeerMemory, ReducePlan, peer_memory_available
+        if self.world == 1 or self.replicate_group is not None or not peer_memory_available(self.group, self.device):
+            return False
+        offs, total = [], 0
+        for u in self.units:
+            offs.append(total)
+            total += _align(u.numel_shard, 128)
+        self.hi_mem = PeerMemory(total * 2, self.group, self.device)
+        for u, off in zip(self.units, offs):
+            view = self.hi_mem.view(off * 2, u.numel_shard, torch.bfloat16)
+            view.copy_(u.hi)
+            u.hi = view
+        self.slot_elems = _align(max(u.numel_full for u in self.units), 128)
+        self.grad_mem = PeerMemory(self.GRAD_SLOTS * self.slot_elems * 2, self.group, self.device)
+        self.gather_plans = [GatherPlan(u, self.world, off, self.device) for u, off in zip(self.units, offs)]
+        self.reduce_plans = [ReducePlan(u, self.rank, self.world, self.device) for u in self.units]
+        self.slot_ptrs = [self.grad_mem.peer_ptrs(j * self.slot_elems * 2) for j in range(self.GRAD_SLOTS)]
+        torch.cuda.synchronize(self.device)
+        self.peer = True
+        return True
+
+    def begin_gathers(self) -> None:
+        """Peer mode: every rank's optimizer step (which writes ``hi``) precedes this step's gathers."""
+        if not self.peer:
+            return
+        self.comm_stream.wait_stream(torch.cuda.current_stream(self.device))
+        with torch.cuda.stream(self.comm_stream):
+            self.hi_mem.barrier(0)
+            # also: every rank finished last step's reductions (they precede this barrier in each
+            # rank's communication stream), so the root's gradient slot may be rewritten
+            self._begin_event = torch.cuda.Event()
+            self._begin_event.record(self.comm_stream)
+
+    def end_gathers(self) -> None:
+        """Peer mode: no rank still reads this rank's ``hi`` when the optimizer overwrites it."""
+        if not self.peer:
+            return
+        self.comm_stream.wait_stream(torch.cuda.current_stream(self.device))
+        with torch.cuda.stream(self.comm_stream):
+            self.hi_mem.barrier(1)
+        torch.cuda.current_stream(self.device).wait_stream(self.comm_stream)
+
+    def comm_error(self) -> int:
+        from ..ops._ext import ext
+        return ext().error_flag(False)
 
     # ---------------------------------------------------------------- all-gather
     def gather(self, u: Unit, stream: Optional[torch.cuda.Stream] = None) -> None:
@@ -190,6 +251,17 @@ class ShardedModel:
     def prefetch(self, u: Unit) -> None:
         """Start the all-gather of ``u`` on the communication stream (no-op if in flight/done)."""
         if self.world == 1 or u.full_hi is not None:
+            return
+        if self.peer:
+            full = torch.empty(u.numel_full, dtype=torch.bfloat16, device=self.device)
+            self.comm_stream.wait_stream(torch.cuda.current_stream(self.device))
+            with torch.cuda.stream(self.comm_stream):
+                self.gather_plans[u.index].run(self.hi_mem, full)
+                ev = torch.cuda.Event()
+                ev.record(self.comm_stream)
+            full.record_stream(self.comm_stream)
+            u.gather_event = ev
+            u.full_hi = full
             return
         packed = torch.empty(self.world * u.numel_shard, dtype=torch.bfloat16, device=self.device)
         full = torch.empty(u.numel_full, dtype=torch.bfloat16, device=self.device)
@@ -224,6 +296,34 @@ class ShardedModel:
     def attach_grads(self, u: Unit, zero: bool = True) -> None:
         """Give every parameter of ``u`` a ``.grad`` view of the unit's flat bf16 gradient (zeroed
         unless ``zero`` is False: gradient accumulation with one rank)."""
+        if self.peer:
+            cur = torch.cuda.current_stream(self.device)
+            if u.index == len(self.units) - 1:
+                slot = 0
+                if self._begin_event is not None:
+                    cur.wait_event(self._begin_event)
+            else:
+                slot = 1 + self._ring_next % (self.GRAD_SLOTS - 1)
+                self._ring_next += 1
+                last = self._slot_last.get(slot)
+                if last is not None:
+                    # every rank has finished reading this slot once any later reduction barrier passed
+                    if self._latest is None or self._latest[0] <= last:
+                        self.comm_stream.wait_stream(cur)
+                        with torch.cuda.stream(self.comm_stream):
+                            self.grad_mem.barrier(2)
+                            ev = torch.cuda.Event()
+                            ev.record(self.comm_stream)
+                        self._latest = (self.n_reduce, ev)
+                        self._slot_last = {k: v for k, v in self._slot_last.items() if v >= self.n_reduce}
+                    cur.wait_event(self._latest[1])
+            # always zeroed: the previous contents were already reduced into the fp32 shard
+            u.full_grad = self.grad_mem.view(slot * self.slot_elems * 2, u.numel_full, torch.bfloat16)
+            u.full_grad.zero_()
+            u.grad_slot = slot
+            for s in u.slots:
+                getattr(s.module, s.attr).grad = u.slot_full(u.full_grad, s)
+            return
         if u.full_grad is None:
             u.full_grad = torch.zeros(u.numel_full, dtype=torch.bfloat16, device=self.device)
         elif zero:
@@ -240,6 +340,25 @@ class ShardedModel:
         communication stream).  world == 1: the bf16 gradient stays as is."""
         self.detach_grads(u)
         if self.world == 1:
+            return
+        if self.peer:
+            c = self.n_reduce
+            self.n_reduce += 1
+            out = torch.zeros(u.numel_shard, dtype=torch.float32, device=self.device)
+            self.comm_stream.wait_stream(torch.cuda.current_stream(self.device))
+            with torch.cuda.stream(self.comm_stream):
+                self.grad_mem.barrier(2)  # every rank's gradient of this unit is complete
+                ev = torch.cuda.Event()
+                ev.record(self.comm_stream)
+                self._latest = (c, ev)
+                self.reduce_plans[u.index].run(self.slot_ptrs[u.grad_slot], out)
+                self._slot_last[u.grad_slot] = c
+                if u.grad_shard is None or not accumulate:
+                    u.grad_shard = out
+                else:
+                    u.grad_shard.add_(out)
+            out.record_stream(self.comm_stream)
+            u.full_grad = None
             return
         g = u.full_grad
         u.full_grad = None

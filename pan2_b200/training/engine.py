@@ -199,6 +199,10 @@ class TrainEngine:
             else:
                 self.sharded.bind_weights(u, None)
         self._alloc_optimizer_state()
+        # gathers / gradient reductions as peer-memory kernels when the shard group is one node
+        self.peer_comm = False
+        if self.world > 1 and device.type == "cuda" and os.environ.get("PAN_PEER_COMM", "1") != "0":
+            self.peer_comm = self.sharded.enable_peer_memory()
         self.stash_in_grads = self.world == 1
         self.accum_steps = 1
         self.accumulating = False
@@ -300,6 +304,7 @@ class TrainEngine:
         model = self.model
         sm = self.sharded
         root = sm.units[-1]
+        sm.begin_gathers()
         sm.gather(root)
         if self.n_blocks:
             sm.prefetch(sm.units[0])
@@ -358,6 +363,7 @@ class TrainEngine:
         self.lr_t.fill_(lr)
 
     def optimizer_step(self) -> None:
+        self.sharded.end_gathers()
         self.step_count += 1
         clip = self.norm_clip[1:2] if self.optim.max_grad_norm > 0 else None
         units = self.sharded.units
