@@ -602,6 +602,263 @@ attn_bwd_kernel(const __grid_constant__ CUtensorMap qmap, const __grid_constant_
   }
 }
 
+// ============================================================================ fused backward
+// One pass, key tiles outer (one CTA = one head x 128 keys of one segment), query tiles inner:
+//   S^T  = K Q_i^T,  dP^T = V dO_i^T                        (tcgen05, operands in smem)
+//   P^T  = exp2(S^T s log2e - lse_i),  dS^T = P^T (dP^T - Delta_i)   (E warps; lane = key)
+//   dV  += P^T dO_i,  dK += dS^T Q_i                        (A = P^T / dS^T straight from TMEM)
+//   dQ_i^T = K^T dS^T                                        (tensor core, into the S^T columns)
+//   dQ   += dQ_i  via TMA reduce-add of fp32 row blocks      (Q warps; lane = head dim)
+// so every score element is exponentiated once and five 128^3 products run per tile pair (the
+// two-pass form needs seven and two exponentials).  TMEM: S^T/P^T/dQ^T 0..127, dP^T/dS^T 128..255,
+// dV 256..383, dK 384..511.  Warps: 0 TMA, 1 MMA, 2..5 E, 6..9 Q.  dQ accumulates in an fp32
+// buffer that a final kernel scales into bf16.
+constexpr int FB_THREADS = 320;
+constexpr int FB_STAGE = 32 * D * 4;  // 32 query rows of fp32 dQ
+constexpr int FB_SMEM = 2 * TILE_BYTES /*K, V*/ + 2 * TILE_BYTES /*Q ring*/ + TILE_BYTES /*dO*/ +
+                        TILE_BYTES /*dS^T*/ + 2 * FB_STAGE + 1024 + 256 + 2 * BT * 4;
+
+__global__ void __launch_bounds__(FB_THREADS, 1)
+attn_bwd_fused_kernel(const __grid_constant__ CUtensorMap qmap, const __grid_constant__ CUtensorMap kmap,
+                      const __grid_constant__ CUtensorMap vmap, const __grid_constant__ CUtensorMap domap,
+                      const __grid_constant__ CUtensorMap dqmap, const WorkItem* __restrict__ items, int L, int H,
+                      float scale, const float* __restrict__ lse, const float* __restrict__ delta,
+                      __nv_bfloat16* __restrict__ dk_out, __nv_bfloat16* __restrict__ dv_out) {
+  extern __shared__ uint8_t smem_raw[];
+  uint8_t* smem = reinterpret_cast<uint8_t*>((reinterpret_cast<uintptr_t>(smem_raw) + 1023) & ~uintptr_t(1023));
+  uint8_t* sK = smem;
+  uint8_t* sV = sK + TILE_BYTES;
+  uint8_t* sQ = sV + TILE_BYTES;            // 2 slots
+  uint8_t* sdO = sQ + 2 * TILE_BYTES;
+  uint8_t* sdS = sdO + TILE_BYTES;          // dS^T, [keys][queries] K-major swizzled
+  uint8_t* sStage = sdS + TILE_BYTES;       // 2 x [32 q][128 d] fp32
+  uint64_t* bars = reinterpret_cast<uint64_t*>(sStage + 2 * FB_STAGE);
+  // kv_full 0, q_full 1-2, q_empty 3-4, do_full 5, do_empty 6, s_full 7, ds_ready 8, ds_free 9,
+  // pv_done 10, dq_full 11, dq_drained 12, all_done 13
+  uint32_t* tmem_slot = reinterpret_cast<uint32_t*>(bars + 14);
+  volatile int& s_abort = *reinterpret_cast<volatile int*>(bars + 15);
+  float (*s_vec)[BT] = reinterpret_cast<float (*)[BT]>(reinterpret_cast<uint8_t*>(bars) + 256);
+
+  const WorkItem it = items[blockIdx.x];
+  const int h = blockIdx.y;
+  const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
+  const int n_q = (it.seg_len + BT - 1) / BT;
+  const float scale_log2 = scale * kLog2e;
+  auto B = [&](int i) { return smem_u32(bars + i); };
+
+  if (threadIdx.x == 0) {
+    s_abort = 0;
+    for (int i = 0; i < 14; ++i) mbar_init(B(i), (i == 8 || i == 12) ? 4 : 1);  // ds_ready / dq_drained: 4 warps
+    fence_barrier_init();
+  }
+  if (warp == 1) {
+    tmem_alloc(smem_u32(tmem_slot), 512);
+    tmem_relinquish();
+  }
+  tc_fence_before();
+  __syncthreads();
+  tc_fence_after();
+  const uint32_t tmem = *tmem_slot;
+  const uint32_t T_S = tmem, T_DP = tmem + 128, T_DV = tmem + 256, T_DK = tmem + 384;
+  const int col = h * D;
+
+  if (warp == 0) {
+    if (lane == 0) {
+      const int r0 = it.seg_start + it.tile_start;
+      mbar_expect_tx(B(0), 2 * TILE_BYTES);
+      tma_load_2d(smem_u32(sK), &kmap, B(0), col, r0);
+      tma_load_2d(smem_u32(sK) + HALF_BYTES, &kmap, B(0), col + 64, r0);
+      tma_load_2d(smem_u32(sV), &vmap, B(0), col, r0);
+      tma_load_2d(smem_u32(sV) + HALF_BYTES, &vmap, B(0), col + 64, r0);
+      for (int i = 0; i < n_q && !s_abort; ++i) {
+        const int slot = i & 1;
+        const int row = it.seg_start + i * BT;
+        if (!mbar_wait(B(3 + slot), ((i >> 1) & 1) ^ 1, 41)) { s_abort = 1; break; }
+        mbar_expect_tx(B(1 + slot), TILE_BYTES);
+        const uint32_t dq = smem_u32(sQ + slot * TILE_BYTES);
+        tma_load_2d(dq, &qmap, B(1 + slot), col, row);
+        tma_load_2d(dq + HALF_BYTES, &qmap, B(1 + slot), col + 64, row);
+        if (!mbar_wait(B(6), (i & 1) ^ 1, 42)) { s_abort = 1; break; }
+        mbar_expect_tx(B(5), TILE_BYTES);
+        tma_load_2d(smem_u32(sdO), &domap, B(5), col, row);
+        tma_load_2d(smem_u32(sdO) + HALF_BYTES, &domap, B(5), col + 64, row);
+      }
+    }
+  } else if (warp == 1) {
+    if (lane == 0) {
+      const uint32_t id_kk = idesc_bf16_f32(128, 128, 0, 0);  // S^T, dP^T: both K-major over D
+      const uint32_t id_tm = idesc_bf16_f32(128, 128, 0, 1);  // dV, dK: A from TMEM, B MN-major
+      const uint32_t id_mm = idesc_bf16_f32(128, 128, 1, 1);  // dQ^T: A = K^T, B = dS^T, both MN-major
+      const uint32_t k = smem_u32(sK), v = smem_u32(sV), dO = smem_u32(sdO), dS = smem_u32(sdS);
+      bool ok = mbar_wait(B(0), 0, 43);
+      for (int i = 0; i < n_q && ok; ++i) {
+        const int slot = i & 1;
+        const uint32_t q = smem_u32(sQ + slot * TILE_BYTES);
+        if (!(ok = mbar_wait(B(1 + slot), (i >> 1) & 1, 44))) break;
+        if (!(ok = mbar_wait(B(5), i & 1, 45))) break;
+        if (i > 0 && !(ok = mbar_wait(B(12), (i - 1) & 1, 46))) break;  // dQ^T(i-1) drained
+        tc_fence_after();
+#pragma unroll
+        for (int kk = 0; kk < D / 16; ++kk) mma_bf16_ss(T_S, desc_kmajor(k, kk), desc_kmajor(q, kk), id_kk, kk > 0);
+#pragma unroll
+        for (int kk = 0; kk < D / 16; ++kk) mma_bf16_ss(T_DP, desc_kmajor(v, kk), desc_kmajor(dO, kk), id_kk, kk > 0);
+        mma_commit(B(7));
+        if (!(ok = mbar_wait(B(8), i & 1, 47))) break;  // P^T, dS^T in TMEM and dS^T in smem
+        tc_fence_after();
+        // dV += P^T dO_i ; dK += dS^T Q_i  (K = 128 queries, 8 columns of packed bf16 per step)
+#pragma unroll
+        for (int kk = 0; kk < BT / 16; ++kk)
+          mma_bf16_ts(T_DV, T_S + kk * 8, desc_mnmajor(dO, kk), id_tm, (i > 0) || (kk > 0));
+        mma_commit(B(6));  // dO slot free
+#pragma unroll
+        for (int kk = 0; kk < BT / 16; ++kk)
+          mma_bf16_ts(T_DK, T_DP + kk * 8, desc_mnmajor(q, kk), id_tm, (i > 0) || (kk > 0));
+        mma_commit(B(3 + slot));  // Q slot free
+        mma_commit(B(10));
+        if (!(ok = mbar_wait(B(10), i & 1, 48))) break;  // P^T read before dQ^T overwrites its columns
+        tc_fence_after();
+        // dQ_i^T = K^T dS^T  (M = D, N = queries, K = keys)
+#pragma unroll
+        for (int kk = 0; kk < BT / 16; ++kk) mma_bf16_ss(T_S, desc_mnmajor(k, kk), desc_mnmajor(dS, kk), id_mm, kk > 0);
+        mma_commit(B(11));
+        mma_commit(B(9));  // dS^T smem free
+      }
+      mma_commit(B(13));
+      if (!ok) s_abort = 1;
+    }
+  } else if (warp < 6) {
+    // ------------------------------------------------ E warps: P^T and dS^T (lane = key row)
+    const int quarter = warp & 3;
+    const int row = quarter * 32 + lane;
+    const uint32_t lane_off = (uint32_t)(quarter * 32) << 16;
+    const bool row_valid = it.tile_start + row < it.seg_len;
+    const int tid = threadIdx.x - 64;
+    bool ok = true;
+    for (int i = 0; i < n_q; ++i) {
+      const int valid_q = min(BT, it.seg_len - i * BT);
+      asm volatile("bar.sync 1, 128;" ::: "memory");
+      if (tid < BT) {
+        const int qi = i * BT + tid;
+        s_vec[0][tid] = qi < it.seg_len ? lse[(size_t)h * L + it.seg_start + qi] * kLog2e : 0.f;
+        s_vec[1][tid] = qi < it.seg_len ? delta[(size_t)h * L + it.seg_start + qi] : 0.f;
+      }
+      asm volatile("bar.sync 1, 128;" ::: "memory");
+      if (!(ok = mbar_wait(B(7), i & 1, 49))) break;
+      if (i > 0 && !(ok = mbar_wait(B(9), (i - 1) & 1, 50))) break;  // dQ^T(i-1) has read dS^T smem
+      tc_fence_after();
+#pragma unroll
+      for (int c = 0; c < 4; ++c) {
+        uint32_t r[32], y[32];
+        tmem_ld32(T_S + lane_off + c * 32, r);
+        tmem_ld32(T_DP + lane_off + c * 32, y);
+        tmem_ld_wait();
+        uint32_t wp[16], wd[16];
+#pragma unroll
+        for (int j = 0; j < 32; j += 2) {
+          float pv[2], dsv[2];
+#pragma unroll
+          for (int e = 0; e < 2; ++e) {
+            const int cc = c * 32 + j + e;
+            const bool on = cc < valid_q && row_valid;
+            const float p = on ? fast_exp2(__uint_as_float(r[j + e]) * scale_log2 - s_vec[0][cc]) : 0.f;
+            pv[e] = p;
+            dsv[e] = p * (__uint_as_float(y[j + e]) - s_vec[1][cc]);
+          }
+          wp[j >> 1] = pack_bf16(pv[0], pv[1]);
+          wd[j >> 1] = pack_bf16(dsv[0], dsv[1]);
+        }
+        // columns [16c, 16c + 16) were read in chunk c or earlier
+        tmem_st16(T_S + lane_off + c * 16, wp);
+        tmem_st16(T_DP + lane_off + c * 16, wd);
+        store_row32_swizzled(sdS, row, c * 32, wd);
+      }
+      tmem_st_wait();
+      fence_async_smem();
+      tc_fence_before();
+      __syncwarp();
+      if (lane == 0) mbar_arrive(B(8));
+    }
+    // dV, dK rows of this key tile
+    if (ok && n_q > 0 && mbar_wait(B(13), 0, 51)) {
+      tc_fence_after();
+      const size_t grow = (size_t)(it.seg_start + it.tile_start + row) * H + h;
+      for (int which = 0; which < 2; ++which) {
+        const uint32_t tacc = (which == 0 ? T_DK : T_DV) + lane_off;
+        const float mul = which == 0 ? scale : 1.f;
+        __nv_bfloat16* dst = (which == 0 ? dk_out : dv_out) + grow * D;
+#pragma unroll
+        for (int c = 0; c < 4; ++c) {
+          uint32_t r[32];
+          tmem_ld32(tacc + c * 32, r);
+          tmem_ld_wait();
+          if (row_valid) {
+#pragma unroll
+            for (int vv = 0; vv < 4; ++vv) {
+              float o[8];
+#pragma unroll
+              for (int e = 0; e < 8; ++e) o[e] = __uint_as_float(r[vv * 8 + e]) * mul;
+              store8(dst + c * 32 + vv * 8, o);
+            }
+          }
+        }
+      }
+    } else {
+      s_abort = 1;
+    }
+  } else {
+    // ------------------------------------------------ Q warps: dQ^T -> fp32 reduce-add (lane = d)
+    const int quarter = warp & 3;
+    const int d = quarter * 32 + lane;
+    const uint32_t lane_off = (uint32_t)(quarter * 32) << 16;
+    const int qt = threadIdx.x - 192;  // 0..127
+    int n_used = 0;
+    for (int i = 0; i < n_q; ++i) {
+      if (!mbar_wait(B(11), i & 1, 52)) { s_abort = 1; break; }
+      tc_fence_after();
+      uint32_t r[4][32];
+#pragma unroll
+      for (int c = 0; c < 4; ++c) tmem_ld32(T_S + lane_off + c * 32, r[c]);
+      tmem_ld_wait();
+      tc_fence_before();
+      __syncwarp();
+      if (lane == 0) mbar_arrive(B(12));  // the S^T columns may be rewritten
+#pragma unroll
+      for (int c = 0; c < 4; ++c) {
+        float* st = reinterpret_cast<float*>(sStage + (n_used & 1) * FB_STAGE);
+        if (n_used >= 2 && qt == 0) bulk_wait_read<1>();
+        asm volatile("bar.sync 2, 128;" ::: "memory");
+#pragma unroll
+        for (int qq = 0; qq < 32; ++qq) st[qq * D + d] = __uint_as_float(r[c][qq]);
+        fence_async_shared();
+        asm volatile("bar.sync 2, 128;" ::: "memory");
+        if (qt == 0) {
+          tma_reduce_add_2d(&dqmap, smem_u32(st), col, it.seg_start + i * BT + c * 32);
+          bulk_commit();
+        }
+        ++n_used;
+      }
+    }
+    if (qt == 0) bulk_wait_all();
+  }
+  tc_fence_before();
+  __syncthreads();
+  if (warp == 1) {
+    tc_fence_after();
+    tmem_dealloc(tmem, 512);
+  }
+}
+
+// dq = scale * dq_acc (fp32 -> bf16), 8 elements per thread
+__global__ void attn_dq_convert_kernel(const float* __restrict__ acc, size_t n8, float scale,
+                                       __nv_bfloat16* __restrict__ dq) {
+  const size_t i = (size_t)blockIdx.x * blockDim.x + threadIdx.x;
+  if (i >= n8) return;
+  const float4 a = reinterpret_cast<const float4*>(acc)[2 * i];
+  const float4 b = reinterpret_cast<const float4*>(acc)[2 * i + 1];
+  float v[8] = {a.x * scale, a.y * scale, a.z * scale, a.w * scale, b.x * scale, b.y * scale, b.z * scale, b.w * scale};
+  store8(dq + 8 * i, v);
+}
+
 // Delta[h, i] = sum_d dO[i, h, d] * O[i, h, d]  (fp32), one warp per (row, head).
 __global__ void attn_bwd_delta_kernel(const __nv_bfloat16* __restrict__ o, const __nv_bfloat16* __restrict__ dout,
                                       int L, int H, float* __restrict__ delta) {
@@ -646,7 +903,32 @@ const char* make_qkv_map(CUtensorMap* m, const void* base, int L, int H, int box
   return r == CUDA_SUCCESS ? nullptr : "cuTensorMapEncodeTiled failed (attention)";
 }
 
+// fp32 [L, H*D] accumulator map for the dQ reduce-add: boxes of 32 rows x 128 columns, no swizzle.
+const char* make_dq_map(CUtensorMap* m, const float* base, int L, int H) {
+  static EncodeTiledFn fn = nullptr;
+  if (fn == nullptr) {
+    void* ptr = nullptr;
+    cudaDriverEntryPointQueryResult q;
+    if (cudaGetDriverEntryPoint("cuTensorMapEncodeTiled", &ptr, cudaEnableDefault, &q) != cudaSuccess || !ptr)
+      return "cuTensorMapEncodeTiled is unavailable";
+    fn = reinterpret_cast<EncodeTiledFn>(ptr);
+  }
+  if (reinterpret_cast<uintptr_t>(base) % 16) return "attention: dq accumulator must be 16-byte aligned";
+  cuuint64_t dims[2] = {(cuuint64_t)H * D, (cuuint64_t)L};
+  cuuint64_t strides[1] = {(cuuint64_t)H * D * 4};
+  cuuint32_t box[2] = {(cuuint32_t)D, 32};
+  cuuint32_t estr[2] = {1, 1};
+  CUresult r = fn(m, CU_TENSOR_MAP_DATA_TYPE_FLOAT32, 2, const_cast<float*>(base), dims, strides, box, estr,
+                  CU_TENSOR_MAP_INTERLEAVE_NONE, CU_TENSOR_MAP_SWIZZLE_NONE, CU_TENSOR_MAP_L2_PROMOTION_L2_256B,
+                  CU_TENSOR_MAP_FLOAT_OOB_FILL_NONE);
+  return r == CUDA_SUCCESS ? nullptr : "cuTensorMapEncodeTiled failed (dq accumulator)";
+}
+
+int g_bwd_variant = 1;  // 1: fused single pass; 0: two passes
+
 }  // namespace attn
+
+void attn_set_backward_variant(int v) { attn::g_bwd_variant = v ? 1 : 0; }
 
 const char* launch_attn_fwd(const void* q, const void* k, const void* v, const int* items, int n_items, int L, int H,
                             int head_dim, float scale, void* out, float* lse, cudaStream_t s) {
@@ -671,7 +953,7 @@ const char* launch_attn_fwd(const void* q, const void* k, const void* v, const i
 const char* launch_attn_bwd(const void* q, const void* k, const void* v, const void* o, const void* dout,
                             const float* lse, const int* items_q, int n_items_q, const int* items_kv, int n_items_kv,
                             int L, int H, int head_dim, float scale, float* delta, void* dq, void* dk, void* dv,
-                            cudaStream_t s) {
+                            float* dq_acc, cudaStream_t s) {
   using namespace attn;
   if (head_dim != D) return "attention: head_dim must be 128";
   const int warps = L * H;
@@ -682,6 +964,25 @@ const char* launch_attn_bwd(const void* q, const void* k, const void* v, const v
   if ((e = make_qkv_map(&qm, q, L, H)) || (e = make_qkv_map(&km, k, L, H)) || (e = make_qkv_map(&vm, v, L, H)) ||
       (e = make_qkv_map(&dom, dout, L, H)))
     return e;
+  if (g_bwd_variant == 1 && dq_acc != nullptr) {
+    static bool fattr = false;
+    if (!fattr) {
+      if (cudaFuncSetAttribute(attn_bwd_fused_kernel, cudaFuncAttributeMaxDynamicSharedMemorySize, FB_SMEM) !=
+          cudaSuccess)
+        return "attention: cannot set smem size (fused backward)";
+      fattr = true;
+    }
+    CUtensorMap dqm;
+    if ((e = make_dq_map(&dqm, dq_acc, L, H))) return e;
+    if (cudaMemsetAsync(dq_acc, 0, (size_t)L * H * D * sizeof(float), s) != cudaSuccess) return "dq memset failed";
+    if (n_items_kv > 0)
+      attn_bwd_fused_kernel<<<dim3(n_items_kv, H), FB_THREADS, FB_SMEM, s>>>(
+          qm, km, vm, dom, dqm, reinterpret_cast<const WorkItem*>(items_kv), L, H, scale, lse, delta,
+          (__nv_bfloat16*)dk, (__nv_bfloat16*)dv);
+    const size_t n8 = (size_t)L * H * D / 8;
+    attn_dq_convert_kernel<<<(unsigned)((n8 + 255) / 256), 256, 0, s>>>(dq_acc, n8, scale, (__nv_bfloat16*)dq);
+    return cudaGetLastError() == cudaSuccess ? nullptr : "attention fused backward launch failed";
+  }
   static bool attr = false;
   if (!attr) {
     if (cudaFuncSetAttribute(attn_bwd_kernel<MODE_DQ>, cudaFuncAttributeMaxDynamicSharedMemorySize, BWD_SMEM) !=

@@ -21,8 +21,9 @@ const char* launch_attn_fwd(const void* q, const void* k, const void* v, const i
 const char* launch_attn_bwd(const void* q, const void* k, const void* v, const void* o, const void* dout,
                             const float* lse, const int* items_q, int n_items_q, const int* items_kv, int n_items_kv,
                             int L, int H, int head_dim, float scale, float* delta, void* dq, void* dk, void* dv,
-                            cudaStream_t s);
+                            float* dq_acc, cudaStream_t s);
 int attn_error_flag(bool reset);
+void attn_set_backward_variant(int v);
 void launch_sumsq(const void* x, bool fp32, size_t n, float* partial, int n_part, cudaStream_t s);
 void launch_reduce_clip(const float* partial, int n, float max_norm, float* out, cudaStream_t s);
 void launch_muon_momentum(float* buf, const void* g, bool g_fp32, const float* clip, float mu, size_t n, void* u,
@@ -451,10 +452,12 @@ std::vector<torch::Tensor> attn_bwd(torch::Tensor dout, torch::Tensor q, torch::
     dv.narrow(0, n_valid, L - n_valid).zero_();
   }
   auto delta = torch::empty({H, L}, q.options().dtype(torch::kFloat32));
+  auto dq_acc = torch::empty({L, H, D}, q.options().dtype(torch::kFloat32));
   check_launch(launch_attn_bwd(q.data_ptr(), k.data_ptr(), v.data_ptr(), o.data_ptr(), dout.data_ptr(),
                                lse.data_ptr<float>(), items_q.data_ptr<int>(), items_q.size(0),
                                items_kv.data_ptr<int>(), items_kv.size(0), L, H, D, (float)scale,
-                               delta.data_ptr<float>(), dq.data_ptr(), dk.data_ptr(), dv.data_ptr(), stream()),
+                               delta.data_ptr<float>(), dq.data_ptr(), dk.data_ptr(), dv.data_ptr(),
+                               dq_acc.data_ptr<float>(), stream()),
                "attn_bwd");
   return {dq, dk, dv};
 }
@@ -610,6 +613,7 @@ PYBIND11_MODULE(TORCH_EXTENSION_NAME, m) {
   m.def("gather_rows", &pan::gather_rows);
   m.def("gemm", &pan::gemm);
   m.def("gemm_force_cta_group", &pan::gemm_force_cta_group);
+  m.def("attn_set_backward_variant", &pan::attn_set_backward_variant);
   m.def("gemm_tuning", &pan::gemm_tuning);
   m.def("gemm_grouped_nt", &pan::gemm_grouped_nt);
   m.def("gemm_batched", &pan::gemm_batched);

@@ -21,8 +21,16 @@ def ref_attention(q, k, v, lens, scale):
     return out, lse
 
 
+@pytest.fixture(params=[1, 0], ids=["fused_bwd", "two_pass_bwd"])
+def bwd_variant(request):
+    from pan2_b200.ops._ext import ext
+    ext().attn_set_backward_variant(request.param)
+    yield request.param
+    ext().attn_set_backward_variant(1)
+
+
 @pytest.mark.parametrize("lens", [[128], [300, 129, 1000, 64], [2048, 5, 700]])
-def test_attention_forward_backward(lens):
+def test_attention_forward_backward(lens, bwd_variant):
     from pan2_b200.ops.attention import varlen_attention
     from pan2_b200.ops._ext import ext
     torch.manual_seed(0)
