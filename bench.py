@@ -183,6 +183,9 @@ def main():
             "init_s": init_s,
             "device_error_flag": err,
             "peak_mem_gb": torch.cuda.max_memory_allocated(device) / 1e9,
+            "allocator": {k: torch.cuda.memory_stats(device).get(k) for k in
+                          ("num_alloc_retries", "num_device_alloc", "num_device_free")},
+            "act_reserve_gb": reserve_gb,
             "last_step_phases_ms": runner.phase_times(),
             "host_pinned_gb": engine.host_bytes_planned / 1e9,
         }

@@ -93,7 +93,8 @@ __device__ __forceinline__ float fast_exp2(float x) {
 
 // ============================================================================ forward
 constexpr int FWD_THREADS = 320;
-constexpr int FWD_SMEM = 2 * TILE_BYTES /*Q*/ + RING * TILE_BYTES + 2 * TILE_BYTES /*P*/ + 1024 + 256;
+constexpr int FWD_RING = 5;  // K/V tiles in flight (P lives in TMEM, so the smem goes to the ring)
+constexpr int FWD_SMEM = 2 * TILE_BYTES /*Q*/ + FWD_RING * TILE_BYTES + 1024 + 256;
 
 __global__ void __launch_bounds__(FWD_THREADS, 1)
 attn_fwd_kernel(const __grid_constant__ CUtensorMap qmap, const __grid_constant__ CUtensorMap kmap,
@@ -102,12 +103,12 @@ attn_fwd_kernel(const __grid_constant__ CUtensorMap qmap, const __grid_constant_
   extern __shared__ uint8_t smem_raw[];
   uint8_t* smem = reinterpret_cast<uint8_t*>((reinterpret_cast<uintptr_t>(smem_raw) + 1023) & ~uintptr_t(1023));
   uint8_t* sQ = smem;                                 // 2 tiles
-  uint8_t* sKV = sQ + 2 * TILE_BYTES;                 // RING tiles
-  uint8_t* sP = sKV + RING * TILE_BYTES;              // 2 tiles
-  uint64_t* bars = reinterpret_cast<uint64_t*>(sP + 2 * TILE_BYTES);
-  // bars: q_full, kv_full[3], kv_empty[3], s_full[2], p_ready[2], pv_done[2]
-  uint32_t* tmem_slot = reinterpret_cast<uint32_t*>(bars + 16);
-  volatile int& s_abort = *reinterpret_cast<volatile int*>(bars + 17);
+  uint8_t* sKV = sQ + 2 * TILE_BYTES;                 // FWD_RING tiles
+  uint64_t* bars = reinterpret_cast<uint64_t*>(sKV + FWD_RING * TILE_BYTES);
+  // bars: q_full, kv_full[R], kv_empty[R], s_full[2], p_ready[2], pv_done[2]
+  constexpr int RB = 1 + 2 * FWD_RING;
+  uint32_t* tmem_slot = reinterpret_cast<uint32_t*>(bars + RB + 6);
+  volatile int& s_abort = *reinterpret_cast<volatile int*>(bars + RB + 7);
 
   const WorkItem it = items[blockIdx.x];
   const int h = blockIdx.y;
@@ -116,15 +117,15 @@ attn_fwd_kernel(const __grid_constant__ CUtensorMap qmap, const __grid_constant_
 
   const uint32_t q_full = smem_u32(bars + 0);
   auto kv_full = [&](int s) { return smem_u32(bars + 1 + s); };
-  auto kv_empty = [&](int s) { return smem_u32(bars + 4 + s); };
-  auto s_full = [&](int x) { return smem_u32(bars + 7 + x); };
-  auto p_ready = [&](int x) { return smem_u32(bars + 9 + x); };
-  auto pv_done = [&](int x) { return smem_u32(bars + 11 + x); };
+  auto kv_empty = [&](int s) { return smem_u32(bars + 1 + FWD_RING + s); };
+  auto s_full = [&](int x) { return smem_u32(bars + RB + x); };
+  auto p_ready = [&](int x) { return smem_u32(bars + RB + 2 + x); };
+  auto pv_done = [&](int x) { return smem_u32(bars + RB + 4 + x); };
 
   if (threadIdx.x == 0) {
     s_abort = 0;
     mbar_init(q_full, 1);
-    for (int s = 0; s < RING; ++s) {
+    for (int s = 0; s < FWD_RING; ++s) {
       mbar_init(kv_full(s), 1);
       mbar_init(kv_empty(s), 1);
     }
@@ -160,8 +161,8 @@ attn_fwd_kernel(const __grid_constant__ CUtensorMap qmap, const __grid_constant_
       int n = 0;
       for (int j = 0; j < n_kv && !s_abort; ++j) {
         for (int w = 0; w < 2; ++w, ++n) {  // K_j then V_j
-          const int slot = n % RING;
-          const uint32_t ph = (n / RING) & 1;
+          const int slot = n % FWD_RING;
+          const uint32_t ph = (n / FWD_RING) & 1;
           if (!mbar_wait(kv_empty(slot), ph ^ 1, 21)) { s_abort = 1; break; }
           const uint32_t fb = kv_full(slot);
           mbar_expect_tx(fb, TILE_BYTES);
@@ -181,8 +182,8 @@ attn_fwd_kernel(const __grid_constant__ CUtensorMap qmap, const __grid_constant_
       tc_fence_after();
       auto wait_slot = [&](int n) {
         if (!ok) return 0u;
-        const int slot = n % RING;
-        ok = mbar_wait(kv_full(slot), (n / RING) & 1, 23);
+        const int slot = n % FWD_RING;
+        ok = mbar_wait(kv_full(slot), (n / FWD_RING) & 1, 23);
         tc_fence_after();
         return smem_u32(sKV + slot * TILE_BYTES);
       };
@@ -192,11 +193,11 @@ attn_fwd_kernel(const __grid_constant__ CUtensorMap qmap, const __grid_constant_
         for (int kk = 0; kk < D / 16; ++kk) mma_bf16_ss(tmem + x * 128, desc_kmajor(qb, kk), desc_kmajor(kb, kk), id_s, kk > 0);
         mma_commit(s_full(x));
       };
+      // O_x += P_x V_j with P_x (bf16, written over the first 64 columns of S_x) as the A operand
       auto issue_pv = [&](int x, uint32_t vb, bool acc) {
-        const uint32_t pb = smem_u32(sP + x * TILE_BYTES);
 #pragma unroll
         for (int kk = 0; kk < BT / 16; ++kk)
-          mma_bf16_ss(tmem + 256 + x * 128, desc_kmajor(pb, kk), desc_mnmajor(vb, kk), id_pv, acc || kk > 0);
+          mma_bf16_ts(tmem + 256 + x * 128, tmem + x * 128 + kk * 8, desc_mnmajor(vb, kk), id_pv, acc || kk > 0);
         mma_commit(pv_done(x));
       };
       // prologue: S_A(0), S_B(0)
@@ -217,15 +218,20 @@ attn_fwd_kernel(const __grid_constant__ CUtensorMap qmap, const __grid_constant_
         if (j + 1 < n_kv) {
           kb2 = wait_slot(nk);
           if (!ok) break;
+          // S_A(j+1) overwrites the columns PV_A(j) reads P from
+          if (!(ok = mbar_wait(pv_done(0), j & 1, 29))) break;
+          tc_fence_after();
           issue_s(0, kb2);
         }
         if (!(ok = mbar_wait(p_ready(1), j & 1, 25))) break;
         tc_fence_after();
         issue_pv(1, vb, j > 0);
-        mma_commit(kv_empty(nv % RING));
+        mma_commit(kv_empty(nv % FWD_RING));
         if (j + 1 < n_kv) {
+          if (!(ok = mbar_wait(pv_done(1), j & 1, 30))) break;
+          tc_fence_after();
           issue_s(1, kb2);
-          mma_commit(kv_empty(nk % RING));
+          mma_commit(kv_empty(nk % FWD_RING));
         }
       }
       if (!ok) s_abort = 1;
@@ -238,7 +244,6 @@ attn_fwd_kernel(const __grid_constant__ CUtensorMap qmap, const __grid_constant_
     const uint32_t lane_off = (uint32_t)(quarter * 32) << 16;
     const uint32_t tS = tmem + x * 128 + lane_off;
     const uint32_t tO = tmem + 256 + x * 128 + lane_off;
-    uint8_t* myP = sP + x * TILE_BYTES;
     float m_used = -INFINITY, l = 0.f;
     bool ok = true;
     for (int j = 0; j < n_kv; ++j) {
@@ -311,10 +316,10 @@ attn_fwd_kernel(const __grid_constant__ CUtensorMap qmap, const __grid_constant_
             w[i >> 1] = pack_bf16(p0, p1);
           }
         }
-        store_row32_swizzled(myP, row, c * 32, w);
+        tmem_st16(tS + c * 16, w);  // columns [16c, 16c + 16) were read in chunk c or earlier
       }
       l += l0 + l1;
-      fence_async_smem();
+      tmem_st_wait();
       tc_fence_before();
       __syncwarp();
       if (lane == 0) mbar_arrive(p_ready(x));

@@ -285,6 +285,54 @@ gemm_kernel(const __grid_constant__ Params p, const __grid_constant__ TmapSet ma
         *reinterpret_cast<float4*>(b + lane * 128 + ((j ^ (lane & 7)) << 4)) =
             make_float4(v[4 * j], v[4 * j + 1], v[4 * j + 2], v[4 * j + 3]);
     };
+    // Coalesced read of a 32-row x 32-column block (rows row0.., columns c0..) through a staging
+    // slot: the warp loads whole 64 / 128-byte row segments, then each lane takes its own row.
+    // Rows at or past `row_lim` and columns at or past `col_lim` read as zero.
+    auto get_bf16 = [&](uint8_t* b, const __nv_bfloat16* src, long long ld, int row0_, int c0_, int row_lim,
+                        int col_lim, float* v) {
+#pragma unroll
+      for (int k = 0; k < 4; ++k) {
+        const int r = k * 8 + (lane >> 2), part = lane & 3;
+        const int rr = row0_ + r, cc = c0_ + part * 8;
+        uint4 w = make_uint4(0u, 0u, 0u, 0u);
+        if (rr < row_lim && cc < col_lim) w = *reinterpret_cast<const uint4*>(src + (size_t)rr * ld + cc);
+        *reinterpret_cast<uint4*>(b + r * 64 + ((part ^ ((r >> 1) & 3)) << 4)) = w;
+      }
+      __syncwarp();
+#pragma unroll
+      for (int j = 0; j < 4; ++j) {
+        const uint4 w = *reinterpret_cast<const uint4*>(b + lane * 64 + ((j ^ ((lane >> 1) & 3)) << 4));
+        const uint32_t u[4] = {w.x, w.y, w.z, w.w};
+#pragma unroll
+        for (int e = 0; e < 4; ++e) {
+          const float2 f = __bfloat1622float2(*reinterpret_cast<const __nv_bfloat162*>(&u[e]));
+          v[8 * j + 2 * e] = f.x;
+          v[8 * j + 2 * e + 1] = f.y;
+        }
+      }
+      __syncwarp();
+    };
+    auto get_f32 = [&](uint8_t* b, const float* src, long long ld, int row0_, int c0_, int row_lim, int col_lim,
+                       float* v) {
+#pragma unroll
+      for (int k = 0; k < 8; ++k) {
+        const int r = k * 4 + (lane >> 3), part = lane & 7;
+        const int rr = row0_ + r, cc = c0_ + part * 4;
+        float4 w = make_float4(0.f, 0.f, 0.f, 0.f);
+        if (rr < row_lim && cc < col_lim) w = *reinterpret_cast<const float4*>(src + (size_t)rr * ld + cc);
+        *reinterpret_cast<float4*>(b + r * 128 + ((part ^ (r & 7)) << 4)) = w;
+      }
+      __syncwarp();
+#pragma unroll
+      for (int j = 0; j < 8; ++j) {
+        const float4 w = *reinterpret_cast<const float4*>(b + lane * 128 + ((j ^ (lane & 7)) << 4));
+        v[4 * j] = w.x;
+        v[4 * j + 1] = w.y;
+        v[4 * j + 2] = w.z;
+        v[4 * j + 3] = w.w;
+      }
+      __syncwarp();
+    };
     auto issue = [&](const CUtensorMap* m, uint8_t* b, int col, int row, int z, bool add = false) {
       fence_async_shared();
       __syncwarp();
@@ -317,24 +365,17 @@ gemm_kernel(const __grid_constant__ Params p, const __grid_constant__ TmapSet ma
         float o[32];
 #pragma unroll
         for (int i = 0; i < 32; ++i) o[i] = p.alpha * __uint_as_float(r[i]);
-        if (p.C != nullptr && row_ok) {
+        if (p.C != nullptr) {
+          float cv[32];
+          uint8_t* sb = acquire();  // used as scratch, then released for the next output
+          if (p.c_fp32)
+            get_f32(sb, reinterpret_cast<const float*>(p.C) + zb * p.c_bstride, p.ldc, row0, c0, p.row_end[g], n_lim, cv);
+          else
+            get_bf16(sb, reinterpret_cast<const __nv_bfloat16*>(p.C) + zb * p.c_bstride, p.ldc, row0, c0, p.row_end[g],
+                     n_lim, cv);
+          --n_used;  // nothing was stored from this slot
 #pragma unroll
-          for (int v8 = 0; v8 < 4; ++v8) {
-            const int c = c0 + v8 * 8;
-            if (c >= n_lim) break;
-            float cv[8];
-            if (p.c_fp32) {
-              const float* cp = reinterpret_cast<const float*>(p.C) + zb * p.c_bstride + (size_t)row * p.ldc + c;
-              const float4 x0 = *reinterpret_cast<const float4*>(cp);
-              const float4 x1 = *reinterpret_cast<const float4*>(cp + 4);
-              cv[0] = x0.x; cv[1] = x0.y; cv[2] = x0.z; cv[3] = x0.w;
-              cv[4] = x1.x; cv[5] = x1.y; cv[6] = x1.z; cv[7] = x1.w;
-            } else {
-              load8(reinterpret_cast<const __nv_bfloat16*>(p.C) + zb * p.c_bstride + (size_t)row * p.ldc + c, cv);
-            }
-#pragma unroll
-            for (int i = 0; i < 8; ++i) o[v8 * 8 + i] += p.beta * cv[i];
-          }
+          for (int i = 0; i < 32; ++i) o[i] += p.beta * cv[i];
         }
         if (bias != nullptr) {
 #pragma unroll
@@ -355,20 +396,13 @@ gemm_kernel(const __grid_constant__ Params p, const __grid_constant__ TmapSet ma
           for (int i = 0; i < 32; ++i) o[i] = gelu_tanh(__bfloat162float(__float2bfloat16_rn(o[i])));
         } else if (p.epi == EPI_DGELU) {
           float pre[32];
-#pragma unroll
-          for (int v8 = 0; v8 < 4; ++v8) {
-            const int c = c0 + v8 * 8;
-            float x[8] = {0.f, 0.f, 0.f, 0.f, 0.f, 0.f, 0.f, 0.f};
-            if (row_ok && c < n_lim) load8(p.aux + (size_t)row * p.ldaux + c, x);
-#pragma unroll
-            for (int i = 0; i < 8; ++i) pre[v8 * 8 + i] = x[i];
-          }
+          uint8_t* sb = acquire();
+          get_bf16(sb, p.aux, p.ldaux, row0, c0, p.row_end[g], n_lim, pre);
 #pragma unroll
           for (int i = 0; i < 32; ++i) o[i] *= gelu_tanh_grad(pre[i]);
 #pragma unroll
           for (int i = 0; i < 32; ++i) pre[i] = gelu_tanh(pre[i]);
-          uint8_t* sb = acquire();
-          put_bf16(sb, pre);  // post-activation
+          put_bf16(sb, pre);  // post-activation (same slot)
           issue(&maps.aux2[g], sb, c0, row0, zb);
         }
         uint8_t* sb = acquire();

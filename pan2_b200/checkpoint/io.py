@@ -163,6 +163,10 @@ def load_engine(engine, root: str, *, load_optimizer: bool = True, strict: bool 
     from ..parallel.sharded import set_master
     from ..optim.flat_ops import join_master
     model_dir, optim_dir, _ = checkpoint_layout(root)
+    if hasattr(engine, "flush_updates"):
+        engine.flush_updates()
+    if engine.device.type == "cuda":
+        torch.cuda.synchronize(engine.device)
     wr = ShardedReader(model_dir)
     orr = None
     if load_optimizer:

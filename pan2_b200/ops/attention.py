@@ -34,7 +34,10 @@ def work_items(lens: Sequence[int], rows_per_item: int, device) -> torch.Tensor:
             for r0 in range(0, n, rows_per_item):
                 rows.append((start, n, r0, 0))
             start += n
-        t = torch.tensor(rows if rows else [(0, 0, 0, 0)][:0], dtype=torch.int32).reshape(-1, 4).to(device)
+        t = torch.tensor(rows if rows else [(0, 0, 0, 0)][:0], dtype=torch.int32).reshape(-1, 4)
+        if torch.device(device).type == "cuda":
+            t = t.pin_memory()
+        t = t.to(device, non_blocking=True)
         if len(_ITEM_CACHE) > 256:
             _ITEM_CACHE.clear()
         _ITEM_CACHE[key] = t

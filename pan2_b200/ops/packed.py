@@ -37,8 +37,23 @@ def _seg_index(bounds: Sequence[int], total: int, device) -> torch.Tensor:
     return idx
 
 
+_BOUNDS_CACHE: dict = {}
+
+
 def _bounds_tensor(bounds: Sequence[int], device) -> torch.Tensor:
-    return torch.tensor(list(bounds), dtype=torch.int32, device=device)
+    """Device int32 copy of host boundaries, cached: building it from a Python list would be a
+    pageable host-to-device copy, which synchronises the host with the GPU on every call."""
+    key = (tuple(int(b) for b in bounds), str(device))
+    t = _BOUNDS_CACHE.get(key)
+    if t is None:
+        host = torch.tensor(key[0], dtype=torch.int32)
+        if torch.device(device).type == "cuda":
+            host = host.pin_memory()
+        t = host.to(device, non_blocking=True)
+        if len(_BOUNDS_CACHE) > 4096:
+            _BOUNDS_CACHE.clear()
+        _BOUNDS_CACHE[key] = t
+    return t
 
 
 # --------------------------------------------------------------------------------------------

@@ -66,6 +66,9 @@ class BlockCheckpoint(torch.autograd.Function):
     def forward(ctx, engine: "TrainEngine", idx: int, x, ln_stats, vec):
         sm = engine.sharded
         u = sm.units[idx]
+        engine._wait_update(u)
+        if idx > 0:
+            engine._wait_update(sm.units[idx - 1])  # its gradient buffer receives this block's checkpoint
         sm.gather(u)
         if idx + 1 < engine.n_blocks:
             sm.prefetch(sm.units[idx + 1])
@@ -211,10 +214,17 @@ class TrainEngine:
                 u.full_grad = torch.zeros(u.numel_full, dtype=torch.bfloat16, device=device)
         self.lr_t = torch.full((1,), self.optim.lr, dtype=torch.float32, device=device)
         self.norm_clip = torch.zeros(2, dtype=torch.float32, device=device)
+        # deferred (overlapped) optimizer updates with host-offloaded state and one rank
+        self.defer_optimizer = device.type == "cuda" and os.environ.get("PAN_DEFER_OPTIMIZER", "0") == "1"
+        self._upd_events: Dict[int, torch.cuda.Event] = {}
+        self._lr_used = torch.zeros(1, dtype=torch.float32, device=device)
+        self._clip_used = torch.ones(1, dtype=torch.float32, device=device)
+        self._lr_override = None
         self._partials = torch.zeros(len(units) * 256, dtype=torch.float32, device=device)
         if self.offload and device.type == "cuda":
             self._h2d = torch.cuda.Stream(device)
             self._d2h = torch.cuda.Stream(device)
+            self._opt_stream = torch.cuda.Stream(device)
 
     # ---------------------------------------------------------------- construction
     def _plan_offload(self, total: int, offload: str, act_bytes: int) -> bool:
@@ -304,6 +314,7 @@ class TrainEngine:
         model = self.model
         sm = self.sharded
         root = sm.units[-1]
+        self._wait_update(root)
         sm.begin_gathers()
         sm.gather(root)
         if self.n_blocks:
@@ -362,18 +373,47 @@ class TrainEngine:
     def set_lr(self, lr: float) -> None:
         self.lr_t.fill_(lr)
 
+    def _lr(self) -> torch.Tensor:
+        return self._lr_override if self._lr_override is not None else self.lr_t
+
+    def _wait_update(self, u: Unit) -> None:
+        """Order the current stream after a deferred optimizer update of ``u`` (if one is pending)."""
+        ev = self._upd_events.pop(u.index, None)
+        if ev is not None:
+            torch.cuda.current_stream(self.device).wait_event(ev)
+
+    def flush_updates(self) -> None:
+        """Wait for every deferred optimizer update (before reading weights or optimizer state)."""
+        for u in self.sharded.units:
+            self._wait_update(u)
+
     def optimizer_step(self) -> None:
         self.sharded.end_gathers()
         self.step_count += 1
-        clip = self.norm_clip[1:2] if self.optim.max_grad_norm > 0 else None
         units = self.sharded.units
         if not self.offload:
+            clip = self.norm_clip[1:2] if self.optim.max_grad_norm > 0 else None
             for u in units:
                 self._step_unit(u, u.lo, u.state, clip)
             return
         # streamed: H2D of unit i+1 overlaps compute of unit i; D2H after compute.  Tensors that
-        # the placement kept on the GPU are used in place.
-        cur = torch.cuda.current_stream(self.device)
+        # the placement kept on the GPU are used in place.  With one rank the whole pipeline runs
+        # on side streams and overlaps the next forward, which waits per unit (root first, then the
+        # blocks in forward order) right before it reads that unit's weights.
+        launch = torch.cuda.current_stream(self.device)
+        deferred = self.defer_optimizer and self.world == 1
+        if deferred:
+            # private copies: the caller may change the learning rate right after this call
+            self._lr_used.copy_(self.lr_t)
+            self._clip_used.copy_(self.norm_clip[1:2])
+            self._opt_stream.wait_stream(launch)
+            cur = self._opt_stream
+            lr_t, clip = self._lr_used, (self._clip_used if self.optim.max_grad_norm > 0 else None)
+            units = [units[-1]] + list(units[:-1])
+        else:
+            cur = launch
+            lr_t, clip = self.lr_t, (self.norm_clip[1:2] if self.optim.max_grad_norm > 0 else None)
+        self._lr_override = lr_t
         staged = {}
 
         def on_host(t):
@@ -399,7 +439,12 @@ class TrainEngine:
             moved += [(u.state[k], v) for k, v in st.items() if on_host(u.state[k])]
             for _, t in moved:
                 t.record_stream(cur)
-            self._step_unit(u, lo, st, clip)
+            with torch.cuda.stream(cur):
+                self._step_unit(u, lo, st, clip)
+            if deferred:
+                ev = torch.cuda.Event()
+                ev.record(cur)
+                self._upd_events[u.index] = ev
             if moved:
                 self._d2h.wait_stream(cur)
                 with torch.cuda.stream(self._d2h):
@@ -407,7 +452,12 @@ class TrainEngine:
                         host.copy_(dev, non_blocking=True)
                 for _, t in moved:
                     t.record_stream(self._d2h)
-        cur.wait_stream(self._d2h)
+        self._lr_override = None
+        if deferred:
+            # the host halves of the next step's state must be written back before they are re-read
+            cur.wait_stream(self._d2h)
+        else:
+            cur.wait_stream(self._d2h)
 
     def place_state(self, reserve_bytes: int) -> Dict[str, int]:
         """Move offloaded ``lo`` halves / optimizer state back to the GPU while free memory minus
@@ -446,7 +496,7 @@ class TrainEngine:
                 E.muon_momentum(st["mom"][ss], g[sl], clip, o.momentum, upd)
                 muon_work.append((s, sl, upd))
             else:
-                E.adamw_update(u.hi[sl], lo[sl], g[sl], st["m"][ss], st["v"][ss], clip, self.lr_t, b1, b2,
+                E.adamw_update(u.hi[sl], lo[sl], g[sl], st["m"][ss], st["v"][ss], clip, self._lr(), b1, b2,
                                o.adamw_eps, o.weight_decay, self.step_count)
         if not muon_work:
             return
@@ -465,7 +515,7 @@ class TrainEngine:
             orth = (gram_newton_schulz(chunk_view(mat, n_local)).reshape(s.shard_rows, s.cols) if n_local > 1
                     else gram_newton_schulz(mat))
             shape = (s.rows // s.chunks[1], s.cols) if chunked else (s.rows, s.cols)
-            E.muon_update(u.hi[sl], lo[sl], orth.reshape(-1), self.lr_t, adjust_lr_scale(shape, o.adjust_lr_fn),
+            E.muon_update(u.hi[sl], lo[sl], orth.reshape(-1), self._lr(), adjust_lr_scale(shape, o.adjust_lr_fn),
                           o.weight_decay)
         if remote:
             self._muon_all_to_all(u, lo, remote)
@@ -500,7 +550,7 @@ class TrainEngine:
             all_to_all_list(send, recv, group=self.group)
             for s, sl, upd in chunk:
                 shape = (s.rows // s.chunks[1], s.cols) if (s.chunks and s.chunks[0] == 0) else (s.rows, s.cols)
-                E.muon_update(u.hi[sl], lo[sl], upd, self.lr_t, adjust_lr_scale(shape, o.adjust_lr_fn),
+                E.muon_update(u.hi[sl], lo[sl], upd, self._lr(), adjust_lr_scale(shape, o.adjust_lr_fn),
                               o.weight_decay)
 
     def zero_grad(self) -> None:

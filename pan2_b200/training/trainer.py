@@ -139,6 +139,14 @@ class Trainer:
         self.util: Dict[str, Optional[float]] = dict(seq=None, image=None, joint=None, video=None, caption=None)
         self.history: List[Dict] = []
         self.heartbeat: Optional[Heartbeat] = None
+        self.wandb = None
+        if cfg.report_to == "wandb" and self.is_main:
+            try:
+                import wandb
+                wandb.init(project=os.environ.get("WANDB_PROJECT", "pan2_b200"), config=vars(cfg))
+                self.wandb = wandb
+            except Exception as e:  # not installed / no credentials: keep training, say so once
+                log.warning(f"report_to=wandb but wandb is unavailable ({e}); metrics go to the log only")
         if self.is_main:
             log.info(f"model: {self.engine.total_params / 1e9:.2f}B parameters, world {self.world} "
                      f"(dp {L.dp_size} x cp {L.cp_size}, shard {L.shard_size}), device {self.device}, "
@@ -385,6 +393,9 @@ class Trainer:
                                          f"CPU Wall: {wall:.3f}s", f"(Prev Step CUDA) Data: {data_t:.3f}s",
                                          f"Train: {train_t:.3f}s", f"Elapsed: {format_duration(now - t0)}"]))
                 self.history.append(dict(step=self.global_step, **stats))
+                if self.wandb is not None and self.global_step % cfg.log_interval == 0:
+                    self.wandb.log({"train/loss": stats["loss"], "train/grad_norm": stats["grad_norm"],
+                                    "train/lr": stats["lr"]}, step=self.global_step)
                 if stats["step_skipped"]:
                     self.consecutive_skipped += 1
                     self.total_skipped += 1
@@ -426,6 +437,8 @@ class Trainer:
             if not ckpt.is_complete(self.checkpoint_dir(self.global_step)):
                 self.save_checkpoint()
             log.info(f"Training finished at step {self.global_step}")
+            if self.wandb is not None:
+                self.wandb.finish()
         finally:
             self.heartbeat.stop()
             if loader is not None:

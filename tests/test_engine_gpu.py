@@ -76,3 +76,37 @@ def test_gram_newton_schulz_matches_cpu(shape):
         assert c > 0.99, (shape, steps, c)
     s = torch.linalg.svdvals(out_gpu[0])
     assert s.max() < 1.3 and s.min() > 0.5, (shape, s.min(), s.max())
+
+
+def test_deferred_offloaded_optimizer_matches_synchronous():
+    """Host-offloaded optimizer state: updates overlapped with the next forward give the same
+    weights as the synchronous streamed optimizer."""
+    from pan2_b200.training.engine import TrainEngine, OptimConfig
+    from pan2_b200.models.transformer import PanVideoDiffusionTransformer
+    from pan2_b200.ops._ext import ext
+    with torch.device("meta"):
+        shape_model = PanVideoDiffusionTransformer(**ARCH)
+    batch, _ = tiny_batch(shape_model)
+    b = _dev(batch)
+    res = {}
+    for defer in (False, True):
+        # an activation reserve larger than the GPU puts every lo half and optimizer state on the host
+        eng = TrainEngine(ARCH, torch.device("cuda"), seed=5, optim=OptimConfig(lr=1e-3), offload="on",
+                          activation_bytes_estimate=int(1e15))
+        assert all(u.lo.device.type == "cpu" for u in eng.sharded.units)
+        eng.defer_optimizer = defer
+        losses = []
+        for step in range(3):
+            loss = eng.forward_backward(b)
+            eng.grad_norm()
+            eng.optimizer_step()
+            eng.set_lr(1e-3 * (0.5 ** (step + 1)))  # changed right after the step, as the step runner does
+            losses.append(loss.item())
+        eng.flush_updates()
+        torch.cuda.synchronize()
+        res[defer] = (losses, [u.hi.float().cpu().clone() for u in eng.sharded.units])
+        assert ext().error_flag(True) == 0
+        del eng
+    assert res[False][0] == res[True][0]
+    for a, c in zip(res[False][1], res[True][1]):
+        assert torch.equal(a, c)
