@@ -1,0 +1,214 @@
+"""Kernel micro-benchmarks of the 29B training step's hot ops, against the measured roofline.
+
+    python bench_kernels.py                       # every case at the bench shapes
+    python bench_kernels.py --case gemm --small   # one small case per kernel (for profiler captures)
+
+Each case prints one JSON line: the shape, the median device time over ``--iters`` launches (CUDA
+events on the launching stream, one pair per launch, an L2 flush of 256 MiB between launches so no
+launch reads the previous one's operands from L2), the achieved TFLOP/s or GB/s and the fraction of
+the measured peak (``MEASURED_PEAKS.json``: copy bandwidth and cuBLAS bf16 burst throughput; the
+earlier pool measurements 6650 GB/s and 1590 TFLOP/s when it is absent).  GEMM and attention cases
+also time the library kernel of the same op (cuBLAS through ``torch.matmul``, cuDNN / flash through
+``scaled_dot_product_attention``) unless ``--no-library``.
+
+Shapes are the 29B model's (hidden 4096, 32 heads of 128, FFN 32768) on the training bench's
+packed batch (5 clips of 18,992 joint tokens; 94,976 rows in total).
+"""
+from __future__ import annotations
+
+import argparse
+import json
+import math
+import os
+import re
+import statistics
+
+import torch
+
+from pan2_b200.ops._ext import ext
+from pan2_b200.ops.attention import work_items
+from pan2_b200.ops.packed import _bounds_tensor, ln_stats_of
+
+HIDDEN, HEADS, HEAD_DIM, FFN = 4096, 32, 128, 32768
+CLIPS, CLIP_TOKENS = 5, 18992
+
+
+def measured_peaks():
+    path = os.path.join(os.path.dirname(os.path.abspath(__file__)), "MEASURED_PEAKS.json")
+    try:
+        with open(path) as f:
+            d = json.load(f)
+        return float(d["hbm_gbs"]), float(d["bf16_tflops"]), "measured"
+    except (OSError, KeyError, ValueError):
+        return 6650.0, 1590.0, "fallback"
+
+
+class Timer:
+    """Median per-launch device time with an L2 flush between launches."""
+
+    def __init__(self, iters: int, warmup: int):
+        self.iters, self.warmup = iters, warmup
+        self.flush = torch.empty(256 << 20, dtype=torch.uint8, device="cuda")
+
+    def __call__(self, fn) -> float:
+        for _ in range(self.warmup):
+            fn()
+        times = []
+        torch.cuda.synchronize()
+        for _ in range(self.iters):
+            self.flush.fill_(1)
+            s, e = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+            s.record()
+            fn()
+            e.record()
+            times.append((s, e))
+        torch.cuda.synchronize()
+        return statistics.median(s.elapsed_time(e) for s, e in times)
+
+
+def gemm_cases(small: bool):
+    rows = 8192 if small else CLIPS * CLIP_TOKENS
+    # (name, M, N, K, layout): NT = x @ w^T (forward), NN = dy @ w (input grad), TN = x^T @ dy (weight grad)
+    cases = [("qkv_fwd", rows, 3 * HIDDEN, HIDDEN, "NT"), ("ffn_up_fwd", rows, FFN, HIDDEN, "NT"),
+             ("ffn_down_fwd", rows, HIDDEN, FFN, "NT"), ("ffn_down_dgrad", rows, FFN, HIDDEN, "NN"),
+             ("ffn_up_wgrad", FFN, HIDDEN, rows, "TN")]
+    return cases[:1] if small else cases
+
+
+def run_gemm(name, M, N, K, layout, timer, library, peaks):
+    E = ext()
+    dev = "cuda"
+    a = torch.randn(K, M, device=dev, dtype=torch.bfloat16) if layout == "TN" else \
+        torch.randn(M, K, device=dev, dtype=torch.bfloat16)
+    b = torch.randn(N, K, device=dev, dtype=torch.bfloat16) if layout == "NT" else \
+        torch.randn(K, N, device=dev, dtype=torch.bfloat16)
+    out = torch.empty(M, N, device=dev, dtype=torch.float32 if layout == "TN" else torch.bfloat16)
+    fn = lambda: E.gemm(a, b, out, layout != "TN", layout == "NT", None, None, False)
+    ms = timer(fn)
+    fl = 2.0 * M * N * K
+    rec = dict(case=f"gemm_{name}", shape=[M, N, K], layout=layout, out_dtype=str(out.dtype).split(".")[-1],
+               ms=round(ms, 4), tflops=round(fl / ms / 1e9, 1), frac_of_peak=round(fl / ms / 1e9 / peaks[1], 3))
+    if library:
+        ao = a.t() if layout == "TN" else a
+        bo = b.t() if layout == "NT" else b
+        lib_out = torch.empty(M, N, device=dev, dtype=torch.bfloat16)
+        ms_l = timer(lambda: torch.matmul(ao, bo, out=lib_out))
+        rec["cublas_bf16_out_ms"] = round(ms_l, 4)
+        rec["cublas_tflops"] = round(fl / ms_l / 1e9, 1)
+    rec["error_flag"] = E.error_flag(True)
+    return rec
+
+
+def run_attention(small, timer, library, peaks, which):
+    E = ext()
+    lens = [8192] if small else [CLIP_TOKENS] * CLIPS
+    L = sum(lens)
+    q, k, v = (torch.randn(L, HEADS, HEAD_DIM, device="cuda", dtype=torch.bfloat16) for _ in range(3))
+    scale = 1 / math.sqrt(HEAD_DIM)
+    it_f, it_b = work_items(lens, 256, q.device), work_items(lens, 128, q.device)
+    fl = sum(4.0 * s * s * HEAD_DIM * HEADS for s in lens)
+    out = []
+    o, lse = E.attn_fwd(q, k, v, it_f, L, scale)
+    if "fwd" in which:
+        ms = timer(lambda: E.attn_fwd(q, k, v, it_f, L, scale))
+        rec = dict(case="attn_fwd", segments=lens, heads=HEADS, head_dim=HEAD_DIM, ms=round(ms, 4),
+                   tflops=round(fl / ms / 1e9, 1), frac_of_peak=round(fl / ms / 1e9 / peaks[1], 3))
+        if library:
+            rec.update(_sdpa(q, lens, timer, fl, backward=False))
+        out.append(rec)
+    if "bwd" in which:
+        do = torch.randn_like(o)
+        ms = timer(lambda: E.attn_bwd(do, q, k, v, o, lse, it_b, it_b, L, scale))
+        flb = 2.5 * fl  # dV, dP, dQ, dK GEMMs plus the S recompute
+        rec = dict(case="attn_bwd", segments=lens, heads=HEADS, head_dim=HEAD_DIM, ms=round(ms, 4),
+                   tflops=round(flb / ms / 1e9, 1), frac_of_peak=round(flb / ms / 1e9 / peaks[1], 3))
+        if library:
+            rec.update(_sdpa(q, lens, timer, flb, backward=True))
+        out.append(rec)
+    for r in out:
+        r["error_flag"] = E.error_flag(True)
+    return out
+
+
+def _sdpa(q, lens, timer, fl, backward):
+    """The library attention on the same work: one dense call per segment (no varlen packing)."""
+    import torch.nn.functional as F
+    try:
+        segs = []
+        start = 0
+        for s in lens:
+            x = q[start:start + s].transpose(0, 1).unsqueeze(0).contiguous().requires_grad_(backward)
+            segs.append(x)
+            start += s
+        if not backward:
+            ms = timer(lambda: [F.scaled_dot_product_attention(x, x, x) for x in segs])
+            return {"sdpa_ms": round(ms, 4), "sdpa_tflops": round(fl / ms / 1e9, 1)}
+        outs = [F.scaled_dot_product_attention(x, x, x) for x in segs]
+        grads = [torch.randn_like(o) for o in outs]
+
+        def bwd():
+            for x, o, g in zip(segs, outs, grads):
+                torch.autograd.grad(o, x, g, retain_graph=True)
+        ms = timer(bwd)
+        return {"sdpa_bwd_ms": round(ms, 4), "sdpa_bwd_tflops": round(fl / ms / 1e9, 1)}
+    except RuntimeError as err:  # a backend without this shape
+        return {"sdpa_error": str(err).splitlines()[0][:200]}
+
+
+def run_elementwise(small, timer, peaks, which):
+    E = ext()
+    L = 8192 * 4 if small else CLIPS * CLIP_TOKENS
+    x = torch.randn(L, HIDDEN, device="cuda", dtype=torch.bfloat16)
+    bounds = [i * (L // CLIPS) for i in range(CLIPS)] + [L]
+    bt = _bounds_tensor(bounds, x.device)
+    shift = torch.randn(CLIPS, HIDDEN, device="cuda", dtype=torch.bfloat16)
+    scl = torch.randn(CLIPS, HIDDEN, device="cuda", dtype=torch.bfloat16)
+    stats = ln_stats_of(x)
+    out = []
+    nbytes = x.numel() * 2
+    if "ln_modulate" in which:
+        ms = timer(lambda: E.ln_modulate_fwd(x, stats, shift, scl, bt, CLIPS))
+        moved = 2 * nbytes + L * 8
+        out.append(dict(case="ln_modulate_fwd", shape=[L, HIDDEN], ms=round(ms, 4),
+                        gbs=round(moved / ms / 1e6, 1), frac_of_peak=round(moved / ms / 1e6 / peaks[0], 3)))
+    if "gate_residual" in which:
+        res = torch.randn_like(x)
+        ms = timer(lambda: E.gate_residual_fwd(x, shift, res, bt, CLIPS))
+        moved = 3 * nbytes + L * 8
+        out.append(dict(case="gate_residual_fwd", shape=[L, HIDDEN], ms=round(ms, 4),
+                        gbs=round(moved / ms / 1e6, 1), frac_of_peak=round(moved / ms / 1e6 / peaks[0], 3)))
+    for r in out:
+        r["error_flag"] = E.error_flag(True)
+    return out
+
+
+def main():
+    ap = argparse.ArgumentParser(description=__doc__.splitlines()[0])
+    ap.add_argument("--case", default=".*", help="regex over gemm, attn_fwd, attn_bwd, ln_modulate, gate_residual")
+    ap.add_argument("--small", action="store_true", help="one small case per kernel (operands still above L2)")
+    ap.add_argument("--iters", type=int, default=10)
+    ap.add_argument("--warmup", type=int, default=3)
+    ap.add_argument("--no-library", action="store_true", help="skip the cuBLAS / SDPA comparisons")
+    args = ap.parse_args()
+    pat = re.compile(args.case)
+    peaks = measured_peaks()
+    timer = Timer(args.iters, args.warmup)
+    library = not args.no_library
+    recs = []
+    if pat.search("gemm"):
+        for c in gemm_cases(args.small):
+            recs.append(run_gemm(*c, timer=timer, library=library, peaks=peaks))
+            print(json.dumps(recs[-1]), flush=True)
+    which = [w for w in ("fwd", "bwd") if pat.search("attn_" + w)]
+    if which:
+        for r in run_attention(args.small, timer, library, peaks, which):
+            print(json.dumps(r), flush=True)
+    which = [w for w in ("ln_modulate", "gate_residual") if pat.search(w)]
+    if which:
+        for r in run_elementwise(args.small, timer, peaks, which):
+            print(json.dumps(r), flush=True)
+    print(json.dumps({"peaks": {"hbm_gbs": peaks[0], "bf16_tflops": peaks[1], "source": peaks[2]}}))
+
+
+if __name__ == "__main__":
+    main()

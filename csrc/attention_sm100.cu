@@ -44,6 +44,21 @@ struct WorkItem {
   int pad;
 };
 
+// Token-sharded destination of a Ulysses context-parallel group (the reverse all-to-all folded
+// into a kernel's stores).  Attention runs on the FULL sequence for heads [head_base, head_base +
+// H); global row g belongs to cp-rank g % cp at its local row g / cp, whose [rows, H_total, D]
+// buffer starts at base[g % cp] (an address in that rank's memory, mapped over NVLink).  Only
+// plain vector stores go through these addresses.
+struct PeerRows {
+  const uint64_t* base;  // nullptr: off
+  int cp, head_base, H_total;
+};
+
+__device__ __forceinline__ __nv_bfloat16* peer_row(const PeerRows& pr, int g, int h) {
+  return reinterpret_cast<__nv_bfloat16*>(pr.base[g % pr.cp]) +
+         ((size_t)(g / pr.cp) * pr.H_total + pr.head_base + h) * D;
+}
+
 // K-major SW128 descriptor of a [128 rows, 128 cols] operand at k-step kk (16 columns per step).
 __device__ __forceinline__ uint64_t desc_kmajor(uint32_t base, int kk) {
   return smem_desc_sw128(base + (kk >> 2) * HALF_BYTES + (kk & 3) * 32, 16, 1024);
@@ -99,7 +114,7 @@ constexpr int FWD_SMEM = 2 * TILE_BYTES /*Q*/ + FWD_RING * TILE_BYTES + 1024 + 2
 __global__ void __launch_bounds__(FWD_THREADS, 1)
 attn_fwd_kernel(const __grid_constant__ CUtensorMap qmap, const __grid_constant__ CUtensorMap kmap,
                 const __grid_constant__ CUtensorMap vmap, const WorkItem* __restrict__ items, int L, int H,
-                float scale_log2, __nv_bfloat16* __restrict__ out, float* __restrict__ lse) {
+                float scale_log2, __nv_bfloat16* __restrict__ out, float* __restrict__ lse, const PeerRows o_peer) {
   extern __shared__ uint8_t smem_raw[];
   uint8_t* smem = reinterpret_cast<uint8_t*>((reinterpret_cast<uintptr_t>(smem_raw) + 1023) & ~uintptr_t(1023));
   uint8_t* sQ = smem;                                 // 2 tiles
@@ -330,6 +345,7 @@ attn_fwd_kernel(const __grid_constant__ CUtensorMap qmap, const __grid_constant_
       const bool store = qrow < it.seg_len;
       const float inv_l = l > 0.f ? 1.f / l : 0.f;
       __nv_bfloat16* dst = out + ((size_t)(it.seg_start + qrow) * H + h) * D;
+      __nv_bfloat16* pdst = (store && o_peer.base) ? peer_row(o_peer, it.seg_start + qrow, h) : nullptr;
 #pragma unroll
       for (int c = 0; c < 4; ++c) {
         uint32_t r[32];
@@ -342,6 +358,7 @@ attn_fwd_kernel(const __grid_constant__ CUtensorMap qmap, const __grid_constant_
 #pragma unroll
             for (int i = 0; i < 8; ++i) o[i] = __uint_as_float(r[v * 8 + i]) * inv_l;
             store8(dst + c * 32 + v * 8, o);
+            if (pdst) store8(pdst + c * 32 + v * 8, o);
           }
         }
       }
@@ -628,7 +645,8 @@ attn_bwd_fused_kernel(const __grid_constant__ CUtensorMap qmap, const __grid_con
                       const __grid_constant__ CUtensorMap vmap, const __grid_constant__ CUtensorMap domap,
                       const __grid_constant__ CUtensorMap dqmap, const WorkItem* __restrict__ items, int L, int H,
                       float scale, const float* __restrict__ lse, const float* __restrict__ delta,
-                      __nv_bfloat16* __restrict__ dk_out, __nv_bfloat16* __restrict__ dv_out) {
+                      __nv_bfloat16* __restrict__ dk_out, __nv_bfloat16* __restrict__ dv_out, const PeerRows dk_peer,
+                      const PeerRows dv_peer) {
   extern __shared__ uint8_t smem_raw[];
   uint8_t* smem = reinterpret_cast<uint8_t*>((reinterpret_cast<uintptr_t>(smem_raw) + 1023) & ~uintptr_t(1023));
   uint8_t* sK = smem;
@@ -786,11 +804,14 @@ attn_bwd_fused_kernel(const __grid_constant__ CUtensorMap qmap, const __grid_con
     // dV, dK rows of this key tile
     if (ok && n_q > 0 && mbar_wait(B(13), 0, 51)) {
       tc_fence_after();
-      const size_t grow = (size_t)(it.seg_start + it.tile_start + row) * H + h;
+      const int g = it.seg_start + it.tile_start + row;
+      const size_t grow = (size_t)g * H + h;
       for (int which = 0; which < 2; ++which) {
         const uint32_t tacc = (which == 0 ? T_DK : T_DV) + lane_off;
         const float mul = which == 0 ? scale : 1.f;
-        __nv_bfloat16* dst = (which == 0 ? dk_out : dv_out) + grow * D;
+        const PeerRows& pr = which == 0 ? dk_peer : dv_peer;
+        __nv_bfloat16* dst = pr.base ? (row_valid ? peer_row(pr, g, h) : nullptr)
+                                     : (which == 0 ? dk_out : dv_out) + grow * D;
 #pragma unroll
         for (int c = 0; c < 4; ++c) {
           uint32_t r[32];
@@ -854,14 +875,49 @@ attn_bwd_fused_kernel(const __grid_constant__ CUtensorMap qmap, const __grid_con
 }
 
 // dq = scale * dq_acc (fp32 -> bf16), 8 elements per thread
+// With `dq_peer` on, element (row g, head h, d) goes to its token owner instead (the reverse
+// all-to-all of dQ) and rows at or beyond n_valid are skipped (the owners zero their padding).
 __global__ void attn_dq_convert_kernel(const float* __restrict__ acc, size_t n8, float scale,
-                                       __nv_bfloat16* __restrict__ dq) {
+                                       __nv_bfloat16* __restrict__ dq, const PeerRows dq_peer, int H, int n_valid) {
   const size_t i = (size_t)blockIdx.x * blockDim.x + threadIdx.x;
   if (i >= n8) return;
   const float4 a = reinterpret_cast<const float4*>(acc)[2 * i];
   const float4 b = reinterpret_cast<const float4*>(acc)[2 * i + 1];
   float v[8] = {a.x * scale, a.y * scale, a.z * scale, a.w * scale, b.x * scale, b.y * scale, b.z * scale, b.w * scale};
-  store8(dq + 8 * i, v);
+  if (dq_peer.base == nullptr) {
+    store8(dq + 8 * i, v);
+    return;
+  }
+  const size_t e = 8 * i;
+  const int g = (int)(e / ((size_t)H * D));
+  if (g >= n_valid) return;
+  const int rem = (int)(e - (size_t)g * H * D);
+  store8(peer_row(dq_peer, g, rem / D) + (rem % D), v);
+}
+
+// Ulysses backward prologue: dO of global row g and head h (heads [head_base, head_base + H) of
+// this rank) is read from its token owner (the all-to-all of dO, peer loads) into the local
+// head-sharded dO, and Delta[h, g] = sum_d dO * O is formed on the way.  One warp per (row, head);
+// rows at or beyond n_valid are zeroed.
+__global__ void attn_bwd_gather_delta_kernel(const __nv_bfloat16* __restrict__ o, const PeerRows do_src, int L,
+                                             int H, int n_valid, __nv_bfloat16* __restrict__ dout,
+                                             float* __restrict__ delta) {
+  const int lane = threadIdx.x & 31;
+  const int w = (blockIdx.x * blockDim.x + threadIdx.x) >> 5;
+  if (w >= L * H) return;
+  const int row = w / H, h = w % H;
+  const size_t base = ((size_t)row * H + h) * D + lane * 4;
+  uint2 b = make_uint2(0u, 0u);
+  if (row < n_valid) b = *reinterpret_cast<const uint2*>(peer_row(do_src, row, h) + lane * 4);
+  *reinterpret_cast<uint2*>(dout + base) = b;
+  const uint2 a = *reinterpret_cast<const uint2*>(o + base);
+  const float2 a0 = __bfloat1622float2(*reinterpret_cast<const __nv_bfloat162*>(&a.x));
+  const float2 a1 = __bfloat1622float2(*reinterpret_cast<const __nv_bfloat162*>(&a.y));
+  const float2 b0 = __bfloat1622float2(*reinterpret_cast<const __nv_bfloat162*>(&b.x));
+  const float2 b1 = __bfloat1622float2(*reinterpret_cast<const __nv_bfloat162*>(&b.y));
+  float s = a0.x * b0.x + a0.y * b0.y + a1.x * b1.x + a1.y * b1.y;
+  s = warp_sum(s);
+  if (lane == 0) delta[(size_t)h * L + row] = s;
 }
 
 // Delta[h, i] = sum_d dO[i, h, d] * O[i, h, d]  (fp32), one warp per (row, head).
@@ -936,8 +992,11 @@ int g_bwd_variant = 1;  // 1: fused single pass; 0: two passes
 void attn_set_backward_variant(int v) { attn::g_bwd_variant = v ? 1 : 0; }
 
 const char* launch_attn_fwd(const void* q, const void* k, const void* v, const int* items, int n_items, int L, int H,
-                            int head_dim, float scale, void* out, float* lse, cudaStream_t s) {
+                            int head_dim, float scale, void* out, float* lse, cudaStream_t s, const uint64_t* o_peer,
+                            int cp, int head_base, int H_total) {
   using namespace attn;
+  const PeerRows opr{o_peer, cp, head_base, H_total};
+  if (o_peer && (cp < 1 || head_base < 0 || head_base + H > H_total)) return "attention: bad peer head range";
   if (head_dim != D) return "attention: head_dim must be 128";
   if (n_items == 0) return nullptr;
   CUtensorMap qm, km, vm;
@@ -951,7 +1010,7 @@ const char* launch_attn_fwd(const void* q, const void* k, const void* v, const i
   }
   dim3 grid(n_items, H);
   attn_fwd_kernel<<<grid, FWD_THREADS, FWD_SMEM, s>>>(qm, km, vm, reinterpret_cast<const WorkItem*>(items), L, H,
-                                                      scale * kLog2e, (__nv_bfloat16*)out, lse);
+                                                      scale * kLog2e, (__nv_bfloat16*)out, lse, opr);
   return cudaGetLastError() == cudaSuccess ? nullptr : "attention forward launch failed";
 }
 
@@ -983,9 +1042,10 @@ const char* launch_attn_bwd(const void* q, const void* k, const void* v, const v
     if (n_items_kv > 0)
       attn_bwd_fused_kernel<<<dim3(n_items_kv, H), FB_THREADS, FB_SMEM, s>>>(
           qm, km, vm, dom, dqm, reinterpret_cast<const WorkItem*>(items_kv), L, H, scale, lse, delta,
-          (__nv_bfloat16*)dk, (__nv_bfloat16*)dv);
+          (__nv_bfloat16*)dk, (__nv_bfloat16*)dv, PeerRows{nullptr, 1, 0, H}, PeerRows{nullptr, 1, 0, H});
     const size_t n8 = (size_t)L * H * D / 8;
-    attn_dq_convert_kernel<<<(unsigned)((n8 + 255) / 256), 256, 0, s>>>(dq_acc, n8, scale, (__nv_bfloat16*)dq);
+    attn_dq_convert_kernel<<<(unsigned)((n8 + 255) / 256), 256, 0, s>>>(dq_acc, n8, scale, (__nv_bfloat16*)dq,
+                                                                         PeerRows{nullptr, 1, 0, H}, H, L);
     return cudaGetLastError() == cudaSuccess ? nullptr : "attention fused backward launch failed";
   }
   static bool attr = false;
@@ -1016,6 +1076,47 @@ int attn_error_flag(bool reset) {
     cudaMemcpyToSymbol(sm100::g_error_flag, &z, sizeof(int));
   }
   return v;
+}
+
+// Ulysses context-parallel backward over the full sequence for this rank's H heads: dO is pulled
+// from its token owners while Delta is formed, the fused kernel writes dK / dV rows straight to
+// their token owners, and the dQ conversion does the same for dQ.  q/k/v/o/lse/dout_head are this
+// rank's head-sharded buffers (local memory); the *_peer tables hold every cp-rank's address of its
+// token-sharded [rows, H_total, D] buffer.
+const char* launch_attn_bwd_cp(const void* q, const void* k, const void* v, const void* o, const float* lse,
+                               const int* items_kv, int n_items_kv, int L, int H, int head_dim, float scale,
+                               int n_valid, float* delta, void* dout_head, float* dq_acc, const uint64_t* do_peer,
+                               const uint64_t* dq_peer, const uint64_t* dk_peer, const uint64_t* dv_peer, int cp,
+                               int head_base, int H_total, cudaStream_t s) {
+  using namespace attn;
+  if (head_dim != D) return "attention: head_dim must be 128";
+  if (cp < 1 || head_base < 0 || head_base + H > H_total) return "attention: bad peer head range";
+  const PeerRows dsrc{do_peer, cp, head_base, H_total};
+  const int warps = L * H;
+  attn_bwd_gather_delta_kernel<<<(warps * 32 + 255) / 256, 256, 0, s>>>((const __nv_bfloat16*)o, dsrc, L, H, n_valid,
+                                                                        (__nv_bfloat16*)dout_head, delta);
+  CUtensorMap qm, km, vm, dom, dqm;
+  const char* e;
+  if ((e = make_qkv_map(&qm, q, L, H)) || (e = make_qkv_map(&km, k, L, H)) || (e = make_qkv_map(&vm, v, L, H)) ||
+      (e = make_qkv_map(&dom, dout_head, L, H)) || (e = make_dq_map(&dqm, dq_acc, L, H)))
+    return e;
+  static bool fattr = false;
+  if (!fattr) {
+    if (cudaFuncSetAttribute(attn_bwd_fused_kernel, cudaFuncAttributeMaxDynamicSharedMemorySize, FB_SMEM) !=
+        cudaSuccess)
+      return "attention: cannot set smem size (fused backward)";
+    fattr = true;
+  }
+  if (cudaMemsetAsync(dq_acc, 0, (size_t)L * H * D * sizeof(float), s) != cudaSuccess) return "dq memset failed";
+  if (n_items_kv > 0)
+    attn_bwd_fused_kernel<<<dim3(n_items_kv, H), FB_THREADS, FB_SMEM, s>>>(
+        qm, km, vm, dom, dqm, reinterpret_cast<const WorkItem*>(items_kv), L, H, scale, lse, delta, nullptr, nullptr,
+        PeerRows{dk_peer, cp, head_base, H_total}, PeerRows{dv_peer, cp, head_base, H_total});
+  const size_t n8 = (size_t)L * H * D / 8;
+  attn_dq_convert_kernel<<<(unsigned)((n8 + 255) / 256), 256, 0, s>>>(dq_acc, n8, scale, nullptr,
+                                                                       PeerRows{dq_peer, cp, head_base, H_total}, H,
+                                                                       n_valid);
+  return cudaGetLastError() == cudaSuccess ? nullptr : "attention context-parallel backward launch failed";
 }
 
 }  // namespace pan

@@ -10,14 +10,22 @@ namespace pan {
 
 const char* launch_qkv_post_fwd(const void* raw, const float* qw, const float* kw, const float* cos_t,
                                 const float* sin_t, const int* itc, int nv, int na, int L, int H, int D, float eps,
-                                void* q, void* k, void* v, cudaStream_t s);
+                                void* q, void* k, void* v, cudaStream_t s, const uint64_t* peer_q = nullptr,
+                                const uint64_t* peer_k = nullptr, const uint64_t* peer_v = nullptr, int cp = 1,
+                                int rank = 0);
 const char* launch_qkv_post_bwd(const void* dq, const void* dk, const void* dv, const void* raw, const float* qw,
                                 const float* kw, const float* cos_t, const float* sin_t, const int* itc, int nv,
                                 int na, int L, int H, int D, float eps, void* draw, float* dqw, float* dkw,
                                 cudaStream_t s);
 
 const char* launch_attn_fwd(const void* q, const void* k, const void* v, const int* items, int n_items, int L, int H,
-                            int head_dim, float scale, void* out, float* lse, cudaStream_t s);
+                            int head_dim, float scale, void* out, float* lse, cudaStream_t s,
+                            const uint64_t* o_peer = nullptr, int cp = 1, int head_base = 0, int H_total = 0);
+const char* launch_attn_bwd_cp(const void* q, const void* k, const void* v, const void* o, const float* lse,
+                               const int* items_kv, int n_items_kv, int L, int H, int head_dim, float scale,
+                               int n_valid, float* delta, void* dout_head, float* dq_acc, const uint64_t* do_peer,
+                               const uint64_t* dq_peer, const uint64_t* dk_peer, const uint64_t* dv_peer, int cp,
+                               int head_base, int H_total, cudaStream_t s);
 const char* launch_attn_bwd(const void* q, const void* k, const void* v, const void* o, const void* dout,
                             const float* lse, const int* items_q, int n_items_q, const int* items_kv, int n_items_kv,
                             int L, int H, int head_dim, float scale, float* delta, void* dq, void* dk, void* dv,
@@ -462,6 +470,83 @@ std::vector<torch::Tensor> attn_bwd(torch::Tensor dout, torch::Tensor q, torch::
   return {dq, dk, dv};
 }
 
+// ------------------------------------------------------------------ Ulysses all-to-all fused in
+namespace {
+const uint64_t* peer_table(const torch::Tensor& t, int64_t cp, const char* name) {
+  TORCH_CHECK(t.is_cuda() && t.scalar_type() == torch::kInt64 && t.is_contiguous() && t.numel() == cp, name,
+              " must be a CUDA int64 [cp] table of peer addresses");
+  return reinterpret_cast<const uint64_t*>(t.data_ptr<int64_t>());
+}
+}  // namespace
+
+// qkv_post forward whose q/k/v rows go straight to their head owners' buffers (tables: [cp] int64).
+void qkv_post_fwd_scatter(torch::Tensor raw, torch::Tensor qw, torch::Tensor kw, torch::Tensor cos_t,
+                          torch::Tensor sin_t, torch::Tensor itc, int64_t nv, int64_t na, int64_t heads, double eps,
+                          torch::Tensor peer_q, torch::Tensor peer_k, torch::Tensor peer_v, int64_t cp, int64_t rank) {
+  const at::cuda::CUDAGuard guard(raw.device());
+  check_rows(raw, "raw");
+  check_i32(itc, "itc");
+  const int L = raw.size(0);
+  const int HD = raw.size(1) / 3;
+  const int D = HD / heads;
+  TORCH_CHECK(cos_t.scalar_type() == torch::kFloat32 && cos_t.is_contiguous() && cos_t.size(0) >= L &&
+                  cos_t.size(1) == D,
+              "cos must be fp32 [L, D]");
+  check_launch(launch_qkv_post_fwd(raw.data_ptr(), qw.data_ptr<float>(), kw.data_ptr<float>(), cos_t.data_ptr<float>(),
+                                   sin_t.data_ptr<float>(), itc.data_ptr<int>(), nv, na, L, heads, D, (float)eps,
+                                   nullptr, nullptr, nullptr, stream(), peer_table(peer_q, cp, "peer_q"),
+                                   peer_table(peer_k, cp, "peer_k"), peer_table(peer_v, cp, "peer_v"), (int)cp,
+                                   (int)rank),
+               "qkv_post_fwd_scatter");
+}
+
+// attention forward over the full sequence for this rank's heads; O is also written to its token
+// owners (o_peer: [cp] int64 addresses of each rank's [rows, H_total, D] buffer).
+std::vector<torch::Tensor> attn_fwd_cp(torch::Tensor q, torch::Tensor k, torch::Tensor v, torch::Tensor items,
+                                       int64_t n_valid, double scale, torch::Tensor o_peer, int64_t cp,
+                                       int64_t head_base, int64_t H_total) {
+  const at::cuda::CUDAGuard guard(q.device());
+  check_qkv(q, "q");
+  check_qkv(k, "k");
+  check_qkv(v, "v");
+  check_i32(items, "items");
+  const int L = q.size(0), H = q.size(1), D = q.size(2);
+  auto o = torch::empty_like(q);
+  auto lse = torch::empty({H, L}, q.options().dtype(torch::kFloat32));
+  if (n_valid < L) o.narrow(0, n_valid, L - n_valid).zero_();
+  check_launch(launch_attn_fwd(q.data_ptr(), k.data_ptr(), v.data_ptr(), items.data_ptr<int>(), items.size(0), L, H, D,
+                               (float)scale, o.data_ptr(), lse.data_ptr<float>(), stream(),
+                               peer_table(o_peer, cp, "o_peer"), (int)cp, (int)head_base, (int)H_total),
+               "attn_fwd_cp");
+  return {o, lse};
+}
+
+// attention backward over the full sequence for this rank's heads: dO is read from the token
+// owners, dQ / dK / dV are written to them.  Returns the gathered head-sharded dO.
+torch::Tensor attn_bwd_cp(torch::Tensor q, torch::Tensor k, torch::Tensor v, torch::Tensor o, torch::Tensor lse,
+                          torch::Tensor items_kv, int64_t n_valid, double scale, torch::Tensor do_peer,
+                          torch::Tensor dq_peer, torch::Tensor dk_peer, torch::Tensor dv_peer, int64_t cp,
+                          int64_t head_base, int64_t H_total) {
+  const at::cuda::CUDAGuard guard(q.device());
+  check_qkv(q, "q");
+  check_qkv(k, "k");
+  check_qkv(v, "v");
+  check_qkv(o, "o");
+  check_i32(items_kv, "items_kv");
+  const int L = q.size(0), H = q.size(1), D = q.size(2);
+  auto dout = torch::empty_like(q);
+  auto delta = torch::empty({H, L}, q.options().dtype(torch::kFloat32));
+  auto dq_acc = torch::empty({L, H, D}, q.options().dtype(torch::kFloat32));
+  check_launch(launch_attn_bwd_cp(q.data_ptr(), k.data_ptr(), v.data_ptr(), o.data_ptr(), lse.data_ptr<float>(),
+                                  items_kv.data_ptr<int>(), items_kv.size(0), L, H, D, (float)scale, (int)n_valid,
+                                  delta.data_ptr<float>(), dout.data_ptr(), dq_acc.data_ptr<float>(),
+                                  peer_table(do_peer, cp, "do_peer"), peer_table(dq_peer, cp, "dq_peer"),
+                                  peer_table(dk_peer, cp, "dk_peer"), peer_table(dv_peer, cp, "dv_peer"), (int)cp,
+                                  (int)head_base, (int)H_total, stream()),
+               "attn_bwd_cp");
+  return dout;
+}
+
 // ------------------------------------------------------------------ optimizer
 namespace {
 void check_half16(const torch::Tensor& t, const char* name) {
@@ -622,6 +707,9 @@ PYBIND11_MODULE(TORCH_EXTENSION_NAME, m) {
   m.def("qkv_post_bwd", &pan::qkv_post_bwd);
   m.def("attn_fwd", &pan::attn_fwd);
   m.def("attn_bwd", &pan::attn_bwd);
+  m.def("qkv_post_fwd_scatter", &pan::qkv_post_fwd_scatter);
+  m.def("attn_fwd_cp", &pan::attn_fwd_cp);
+  m.def("attn_bwd_cp", &pan::attn_bwd_cp);
   m.def("sumsq_partial", &pan::sumsq_partial);
   m.def("norm_and_clip", &pan::norm_and_clip);
   m.def("muon_momentum", &pan::muon_momentum);

@@ -18,6 +18,16 @@
 namespace pan {
 namespace {
 
+// Ulysses scatter of the forward outputs: when q/k/v are set they hold, per cp-rank, the address
+// of that rank's head-sharded [S, hl, D] buffer (S = cp * local rows); local interleave row t of
+// rank `rank` is global row t * cp + rank, and head h lives on rank h / hl as its head h % hl.
+struct HeadScatter {
+  const uint64_t* q;
+  const uint64_t* k;
+  const uint64_t* v;
+  int cp, rank, hl;
+};
+
 template <int EPL>
 __device__ __forceinline__ void loadv(const __nv_bfloat16* p, float (&v)[EPL]) {
   if (EPL == 4) {
@@ -48,7 +58,7 @@ __global__ void qkv_post_fwd_kernel(const __nv_bfloat16* __restrict__ raw, const
                                     const float* __restrict__ kw, const float* __restrict__ cos_t,
                                     const float* __restrict__ sin_t, const int* __restrict__ itc, int nv, int na,
                                     int L, int H, float eps, __nv_bfloat16* __restrict__ q, __nv_bfloat16* __restrict__ k,
-                                    __nv_bfloat16* __restrict__ v) {
+                                    __nv_bfloat16* __restrict__ v, const HeadScatter hs) {
   constexpr int D = EPL * 32;
   const int lane = threadIdx.x & 31;
   const int warps = blockDim.x >> 5;
@@ -56,12 +66,19 @@ __global__ void qkv_post_fwd_kernel(const __nv_bfloat16* __restrict__ raw, const
   for (int p = blockIdx.x * warps + (threadIdx.x >> 5); p < L; p += gridDim.x * warps) {
     const int dst = itc[p];
     const size_t orow = (size_t)dst * HD;
+    // destination of (this row, head h) in q / k / v: the local interleave row, or with the
+    // Ulysses scatter on, row dst * cp + rank of head owner h / hl's head-sharded buffer
+    auto out_at = [&](__nv_bfloat16* local, const uint64_t* tab, int h) -> __nv_bfloat16* {
+      if (tab == nullptr) return local + orow + h * D + lane * EPL;
+      const size_t g = (size_t)dst * hs.cp + hs.rank;
+      return reinterpret_cast<__nv_bfloat16*>(tab[h / hs.hl]) + (g * hs.hl + h % hs.hl) * D + lane * EPL;
+    };
     if (p >= na) {  // padding: zero the interleave row
       float z[EPL] = {};
       for (int h = 0; h < H; ++h) {
-        storev<EPL>(q + orow + h * D + lane * EPL, z);
-        storev<EPL>(k + orow + h * D + lane * EPL, z);
-        storev<EPL>(v + orow + h * D + lane * EPL, z);
+        storev<EPL>(out_at(q, hs.q, h), z);
+        storev<EPL>(out_at(k, hs.k, h), z);
+        storev<EPL>(out_at(v, hs.v, h), z);
       }
       continue;
     }
@@ -92,11 +109,11 @@ __global__ void qkv_post_fwd_kernel(const __nv_bfloat16* __restrict__ raw, const
           y[i] = z[i] * c[i] - z[i + 1] * s[i];
           y[i + 1] = z[i + 1] * c[i + 1] + z[i] * s[i + 1];
         }
-        storev<EPL>((which == 0 ? q : k) + orow + h * D + lane * EPL, y);
+        storev<EPL>(which == 0 ? out_at(q, hs.q, h) : out_at(k, hs.k, h), y);
       }
       float vv[EPL];
       loadv<EPL>(rr + 2 * HD + h * D + lane * EPL, vv);
-      storev<EPL>(v + orow + h * D + lane * EPL, vv);
+      storev<EPL>(out_at(v, hs.v, h), vv);
     }
   }
 }
@@ -188,18 +205,23 @@ int grid_for(int L) {
 
 const char* launch_qkv_post_fwd(const void* raw, const float* qw, const float* kw, const float* cos_t,
                                 const float* sin_t, const int* itc, int nv, int na, int L, int H, int D, float eps,
-                                void* q, void* k, void* v, cudaStream_t s) {
+                                void* q, void* k, void* v, cudaStream_t s, const uint64_t* peer_q,
+                                const uint64_t* peer_k, const uint64_t* peer_v, int cp, int rank) {
   auto R = (const __nv_bfloat16*)raw;
   auto Q = (__nv_bfloat16*)q;
   auto K = (__nv_bfloat16*)k;
   auto V = (__nv_bfloat16*)v;
+  const bool scatter = peer_q != nullptr;
+  if (scatter && (peer_k == nullptr || peer_v == nullptr || cp < 1 || H % cp || rank < 0 || rank >= cp))
+    return "qkv_post: bad Ulysses scatter arguments";
+  const HeadScatter hs{peer_q, peer_k, peer_v, scatter ? cp : 1, scatter ? rank : 0, scatter ? H / cp : H};
   if (D == 128)
-    qkv_post_fwd_kernel<4><<<grid_for(L), 256, 0, s>>>(R, qw, kw, cos_t, sin_t, itc, nv, na, L, H, eps, Q, K, V);
+    qkv_post_fwd_kernel<4><<<grid_for(L), 256, 0, s>>>(R, qw, kw, cos_t, sin_t, itc, nv, na, L, H, eps, Q, K, V, hs);
   else if (D == 64)
-    qkv_post_fwd_kernel<2><<<grid_for(L), 256, 0, s>>>(R, qw, kw, cos_t, sin_t, itc, nv, na, L, H, eps, Q, K, V);
+    qkv_post_fwd_kernel<2><<<grid_for(L), 256, 0, s>>>(R, qw, kw, cos_t, sin_t, itc, nv, na, L, H, eps, Q, K, V, hs);
   else
     return "qkv_post: head_dim must be 64 or 128";
-  return nullptr;
+  return cudaGetLastError() == cudaSuccess ? nullptr : "qkv_post: launch failed";
 }
 
 const char* launch_qkv_post_bwd(const void* dq, const void* dk, const void* dv, const void* raw, const float* qw,
