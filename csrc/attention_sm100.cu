@@ -106,6 +106,22 @@ __device__ __forceinline__ float fast_exp2(float x) {
   return y;
 }
 
+// 2^x on the FMA / integer pipes, for softmax arguments (x <= ~8; results below 2^-125 flush to
+// tiny values, which bf16 P rounds away next to a row maximum of at least 2^-8).  Range reduction
+// x = n + f with n = round(x) taken from the low mantissa bits of x + 1.5 * 2^23 and f in
+// [-0.5, 0.5]; 2^f by a degree-3 polynomial (a relative-error least-squares fit made for this
+// kernel, max relative error 7.5e-5, far below bf16's 2^-9); 2^n is added to the exponent field
+// (the magic constant's own bits vanish in the 23-bit shift).  Moving a share of the softmax
+// exponentials here relieves the MUFU unit, which otherwise needs as many cycles per score tile as
+// the tensor core (the exponential-emulation idea of FlashAttention-4).
+__device__ __forceinline__ float exp2_poly(float x) {
+  x = fmaxf(x, -125.f);
+  const float t = x + 12582912.f;
+  const float f = x - (t - 12582912.f);
+  const float p = fmaf(fmaf(fmaf(0.0551716685f, f, 0.2426111400f), f, 0.6932609677f), f, 0.9999280572f);
+  return __int_as_float(__float_as_int(p) + (__float_as_int(t) << 23));
+}
+
 // ============================================================================ forward
 constexpr int FWD_THREADS = 320;
 constexpr int FWD_RING = 5;  // K/V tiles in flight (P lives in TMEM, so the smem goes to the ring)
@@ -265,22 +281,27 @@ attn_fwd_kernel(const __grid_constant__ CUtensorMap qmap, const __grid_constant_
       if (!(ok = mbar_wait(s_full(x), j & 1, 26))) break;
       tc_fence_after();
       const int valid = min(BT, it.seg_len - j * BT);
+      // row maximum: two chunks per TMEM wait (10 warps per CTA cap registers at 168 per thread, so
+      // at most 64 scores are live at a time)
       float mx0 = -INFINITY, mx1 = -INFINITY;
 #pragma unroll
-      for (int c = 0; c < 4; ++c) {
-        uint32_t r[32];
-        tmem_ld32(tS + c * 32, r);
+      for (int h2 = 0; h2 < 2; ++h2) {
+        uint32_t ra[32], rb[32];
+        tmem_ld32(tS + h2 * 64, ra);
+        tmem_ld32(tS + h2 * 64 + 32, rb);
         tmem_ld_wait();
         if (valid == BT) {
 #pragma unroll
-          for (int i = 0; i < 32; i += 2) {
-            mx0 = fmaxf(mx0, __uint_as_float(r[i]));
-            mx1 = fmaxf(mx1, __uint_as_float(r[i + 1]));
+          for (int i = 0; i < 32; ++i) {
+            mx0 = fmaxf(mx0, __uint_as_float(ra[i]));
+            mx1 = fmaxf(mx1, __uint_as_float(rb[i]));
           }
         } else {
 #pragma unroll
-          for (int i = 0; i < 32; ++i)
-            if (c * 32 + i < valid) mx0 = fmaxf(mx0, __uint_as_float(r[i]));
+          for (int i = 0; i < 32; ++i) {
+            if (h2 * 64 + i < valid) mx0 = fmaxf(mx0, __uint_as_float(ra[i]));
+            if (h2 * 64 + 32 + i < valid) mx1 = fmaxf(mx1, __uint_as_float(rb[i]));
+          }
         }
       }
       const float m_new = fmaxf(m_used, fmaxf(mx0, mx1) * scale_log2);
@@ -292,12 +313,12 @@ attn_fwd_kernel(const __grid_constant__ CUtensorMap qmap, const __grid_constant_
           const float alpha = grow ? fast_exp2(m_used - m_new) : 1.f;  // m_used finite here (j > 0)
 #pragma unroll
           for (int c = 0; c < 4; ++c) {
-            uint32_t r[32];
-            tmem_ld32(tO + c * 32, r);
+            uint32_t o[32];
+            tmem_ld32(tO + c * 32, o);
             tmem_ld_wait();
 #pragma unroll
-            for (int i = 0; i < 32; ++i) r[i] = __float_as_uint(__uint_as_float(r[i]) * alpha);
-            tmem_st32(tO + c * 32, r);
+            for (int i = 0; i < 32; ++i) o[i] = __float_as_uint(__uint_as_float(o[i]) * alpha);
+            tmem_st32(tO + c * 32, o);
           }
           tmem_st_wait();
           l *= alpha;
@@ -305,33 +326,40 @@ attn_fwd_kernel(const __grid_constant__ CUtensorMap qmap, const __grid_constant_
       }
       if (grow) m_used = m_new;
       float l0 = 0.f, l1 = 0.f;
-#pragma unroll
-      for (int c = 0; c < 4; ++c) {
-        uint32_t r[32];
-        tmem_ld32(tS + c * 32, r);
-        tmem_ld_wait();
+      // P = exp2(S * scale - m) as bf16 pairs into the first 64 columns of S (a chunk's P columns
+      // were read as scores in an earlier or the same chunk)
+      auto softmax_chunk = [&](const uint32_t (&r)[32], int c) {
         uint32_t w[16];
-        if (valid == BT) {
 #pragma unroll
-          for (int i = 0; i < 32; i += 2) {
-            const float p0 = fast_exp2(fmaf(__uint_as_float(r[i]), scale_log2, -m_used));
-            const float p1 = fast_exp2(fmaf(__uint_as_float(r[i + 1]), scale_log2, -m_used));
-            l0 += p0;
-            l1 += p1;
-            w[i >> 1] = pack_bf16(p0, p1);
+        for (int i = 0; i < 32; i += 2) {
+          const float x0 = fmaf(__uint_as_float(r[i]), scale_log2, -m_used);
+          const float x1 = fmaf(__uint_as_float(r[i + 1]), scale_log2, -m_used);
+          float p0, p1;
+          if ((i & 6) == 6) {  // one pair in four on the FMA pipe
+            p0 = exp2_poly(x0);
+            p1 = exp2_poly(x1);
+          } else {
+            p0 = fast_exp2(x0);
+            p1 = fast_exp2(x1);
           }
-        } else {
-#pragma unroll
-          for (int i = 0; i < 32; i += 2) {
-            const float p0 = c * 32 + i < valid ? fast_exp2(fmaf(__uint_as_float(r[i]), scale_log2, -m_used)) : 0.f;
-            const float p1 =
-                c * 32 + i + 1 < valid ? fast_exp2(fmaf(__uint_as_float(r[i + 1]), scale_log2, -m_used)) : 0.f;
-            l0 += p0;
-            l1 += p1;
-            w[i >> 1] = pack_bf16(p0, p1);
+          if (valid < BT) {
+            p0 = c * 32 + i < valid ? p0 : 0.f;
+            p1 = c * 32 + i + 1 < valid ? p1 : 0.f;
           }
+          l0 += p0;
+          l1 += p1;
+          w[i >> 1] = pack_bf16(p0, p1);
         }
-        tmem_st16(tS + c * 16, w);  // columns [16c, 16c + 16) were read in chunk c or earlier
+        tmem_st16(tS + c * 16, w);
+      };
+#pragma unroll
+      for (int h2 = 0; h2 < 2; ++h2) {
+        uint32_t ra[32], rb[32];
+        tmem_ld32(tS + h2 * 64, ra);
+        tmem_ld32(tS + h2 * 64 + 32, rb);
+        tmem_ld_wait();
+        softmax_chunk(ra, 2 * h2);
+        softmax_chunk(rb, 2 * h2 + 1);
       }
       l += l0 + l1;
       tmem_st_wait();

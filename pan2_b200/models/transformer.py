@@ -34,6 +34,7 @@ from ..ops.gemm import linear, grouped_linear, grouped_ffn
 from ..ops.qkv import qkv_project
 from ..ops.attention import varlen_attention, dense_attention
 from ..parallel.ulysses import ulysses_attention
+from ..parallel.cp_fused import fused_cp_enabled, fused_qkv_ulysses_attention
 
 
 # ---------------------------------------------------------------------------------------------
@@ -203,19 +204,25 @@ class JointAttentionBlock(nn.Module):
         shift1, scale1, gate1, shift2, scale2, gate2 = mods.chunk(6, dim=-1)
         x_mod = P.ln_modulate(x, ln_stats, shift1, scale1, bounds, bt)
         mm_bounds = [0, meta.n_video, meta.n_active]
-        q, k, v = qkv_project(x_mod, self.qkv_proj.weight.view(2, 3 * self.hidden_size, self.hidden_size),
-                              self.qkv_proj.bias.view(2, 3 * self.hidden_size), self.qkv_proj.q_weight,
-                              self.qkv_proj.k_weight, meta.freqs_cos, meta.freqs_sin,
-                              meta.indices_interleave_to_concat, mm_bounds, self.num_heads, self.qkv_proj.eps)
-        if attn_fn is None and meta.cp_group is not None:
-            o = ulysses_attention(q, k, v, meta)
-        elif attn_fn is None:
-            o = varlen_attention(q, k, v, meta.joint_cu_seqlens, meta.joint_lens, meta.joint_segment_limit)
+        qkv_w = self.qkv_proj.weight.view(2, 3 * self.hidden_size, self.hidden_size)
+        qkv_b = self.qkv_proj.bias.view(2, 3 * self.hidden_size)
+        if attn_fn is None and meta.cp_group is not None and fused_cp_enabled(meta.cp_group, x.device):
+            # Ulysses all-to-alls folded into qkv_post / attention (peer memory, one node)
+            o_concat = fused_qkv_ulysses_attention(x_mod, qkv_w, qkv_b, self.qkv_proj.q_weight,
+                                                   self.qkv_proj.k_weight, meta, mm_bounds, self.num_heads,
+                                                   self.qkv_proj.eps)
         else:
-            o = attn_fn(q, k, v, meta)
-        L = x.shape[0]
-        o_concat = P.permute_rows(o.reshape(o.shape[0], -1), meta.indices_interleave_to_concat,
-                                  meta.indices_concat_to_interleave)
+            q, k, v = qkv_project(x_mod, qkv_w, qkv_b, self.qkv_proj.q_weight, self.qkv_proj.k_weight,
+                                  meta.freqs_cos, meta.freqs_sin, meta.indices_interleave_to_concat, mm_bounds,
+                                  self.num_heads, self.qkv_proj.eps)
+            if attn_fn is None and meta.cp_group is not None:
+                o = ulysses_attention(q, k, v, meta)
+            elif attn_fn is None:
+                o = varlen_attention(q, k, v, meta.joint_cu_seqlens, meta.joint_lens, meta.joint_segment_limit)
+            else:
+                o = attn_fn(q, k, v, meta)
+            o_concat = P.permute_rows(o.reshape(o.shape[0], -1), meta.indices_interleave_to_concat,
+                                      meta.indices_concat_to_interleave)
         h = self.hidden_size
         attn_out = grouped_linear(o_concat, self.out_proj.weight.view(2, h, h), self.out_proj.bias.view(2, h),
                                   mm_bounds)

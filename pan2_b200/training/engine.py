@@ -37,6 +37,10 @@ from ..parallel.collectives import all_to_all_list
 from ..parallel.sharded import ShardedModel, Unit, build_unit, set_master, split_master_cpu
 
 
+def _align256(n: int) -> int:
+    return (int(n) + 255) // 256 * 256
+
+
 class _Root(nn.Module):
     """Everything outside the joint blocks, as one parameter unit (names match the model)."""
 
@@ -225,6 +229,11 @@ class TrainEngine:
             self._h2d = torch.cuda.Stream(device)
             self._d2h = torch.cuda.Stream(device)
             self._opt_stream = torch.cuda.Stream(device)
+        # streamed optimizer state: two persistent device slots (unit i uses slot i % 2), so the
+        # per-unit staging never goes through the caching allocator; _slot_free[s] marks the end of
+        # the write-back that last read slot s
+        self._slots: List[torch.Tensor] = []
+        self._slot_free: List[Optional[torch.cuda.Event]] = [None, None]
 
     # ---------------------------------------------------------------- construction
     def _plan_offload(self, total: int, offload: str, act_bytes: int) -> bool:
@@ -419,45 +428,88 @@ class TrainEngine:
         def on_host(t):
             return t is not None and t.device.type == "cpu"
 
+        def host_parts(u):
+            parts = [("lo", None, u.lo)] if on_host(u.lo) else []
+            return parts + [("state", k, v) for k, v in u.state.items() if on_host(v)]
+
+        slots = self._staging_slots(max(sum(_align256(t.numel() * t.element_size()) for *_, t in host_parts(u))
+                                        for u in units))
+
         def stage(i):
             u = units[i]
+            parts = host_parts(u)
             self._h2d.wait_stream(cur)
+            s = i % 2
+            if parts and slots and self._slot_free[s] is not None:
+                self._h2d.wait_event(self._slot_free[s])
+            lo, st, views = u.lo, dict(u.state), []
             with torch.cuda.stream(self._h2d):
-                lo = u.lo.to(self.device, non_blocking=True) if on_host(u.lo) else u.lo
-                st = {k: (v.to(self.device, non_blocking=True) if on_host(v) else v) for k, v in u.state.items()}
+                off = 0
+                for kind, k, t in parts:
+                    nb = t.numel() * t.element_size()
+                    if slots:
+                        dev = slots[s][off:off + nb].view(t.dtype).view(t.shape)
+                        dev.copy_(t, non_blocking=True)
+                        off += _align256(nb)
+                    else:  # no room for persistent slots: allocate per unit
+                        dev = t.to(self.device, non_blocking=True)
+                    views.append(dev)
+                    if kind == "lo":
+                        lo = dev
+                    else:
+                        st[k] = dev
                 ev = torch.cuda.Event()
                 ev.record(self._h2d)
-            staged[i] = (lo, st, ev)
+            staged[i] = (lo, st, ev, parts, views)
 
         stage(0)
         for i, u in enumerate(units):
             if i + 1 < len(units):
                 stage(i + 1)
-            lo, st, ev = staged.pop(i)
+            lo, st, ev, parts, views = staged.pop(i)
             cur.wait_event(ev)
-            moved = [(u.lo, lo)] if on_host(u.lo) else []
-            moved += [(u.state[k], v) for k, v in st.items() if on_host(u.state[k])]
-            for _, t in moved:
-                t.record_stream(cur)
+            if not slots:
+                for t in views:
+                    t.record_stream(cur)
             with torch.cuda.stream(cur):
                 self._step_unit(u, lo, st, clip)
             if deferred:
                 ev = torch.cuda.Event()
                 ev.record(cur)
                 self._upd_events[u.index] = ev
-            if moved:
+            if parts:
                 self._d2h.wait_stream(cur)
                 with torch.cuda.stream(self._d2h):
-                    for host, dev in moved:
+                    for (_, _, host), dev in zip(parts, views):
                         host.copy_(dev, non_blocking=True)
-                for _, t in moved:
-                    t.record_stream(self._d2h)
+                    done = torch.cuda.Event()
+                    done.record(self._d2h)
+                self._slot_free[i % 2] = done
+                if not slots:
+                    for t in views:
+                        t.record_stream(self._d2h)
         self._lr_override = None
         if deferred:
             # the host halves of the next step's state must be written back before they are re-read
             cur.wait_stream(self._d2h)
         else:
             cur.wait_stream(self._d2h)
+
+    def _staging_slots(self, nbytes: int) -> List[torch.Tensor]:
+        """The two device slots for streamed optimizer state (grown to ``nbytes`` each); empty when
+        the GPU has no room, in which case units are staged through the caching allocator."""
+        if nbytes <= 0:
+            return []
+        if self._slots and self._slots[0].numel() >= nbytes:
+            return self._slots
+        torch.cuda.current_stream(self.device).wait_stream(self._h2d)
+        torch.cuda.current_stream(self.device).wait_stream(self._d2h)
+        self._slots, self._slot_free = [], [None, None]
+        try:
+            self._slots = [torch.empty(nbytes, dtype=torch.uint8, device=self.device) for _ in range(2)]
+        except torch.cuda.OutOfMemoryError:
+            self._slots = []
+        return self._slots
 
     def place_state(self, reserve_bytes: int) -> Dict[str, int]:
         """Move offloaded ``lo`` halves / optimizer state back to the GPU while free memory minus

@@ -94,7 +94,8 @@ def test_attention_backward_reproducible_within_tolerance():
     scale = 1 / math.sqrt(128)
     o, lse = E.attn_fwd(q, k, v, itf, sum(lens), scale)
     o2, lse2 = E.attn_fwd(q, k, v, itf, sum(lens), scale)
-    assert torch.equal(o, o2) and torch.equal(lse, lse2)
+    n = sum(lens)  # LSE columns of padding rows are never written (nothing reads them)
+    assert torch.equal(o, o2) and torch.equal(lse[:, :n], lse2[:, :n])
     g1 = E.attn_bwd(do, q, k, v, o, lse, itb, itb, sum(lens), scale)
     g2 = E.attn_bwd(do, q, k, v, o, lse, itb, itb, sum(lens), scale)
     assert E.error_flag(True) == 0
