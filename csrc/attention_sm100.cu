@@ -100,26 +100,31 @@ __device__ __forceinline__ float poly_exp2(float x) {
 }
 
 // 2^x on the SFU (PTX ex2.approx.ftz.f32, ~2 ulp); softmax probabilities are rounded to bf16 anyway.
+// Packed fp32 pair arithmetic (one instruction for two lanes' worth of FMA / add) and a 3-input
+// max: the forward softmax is bound by instruction issue, not by the MUFU exponentials.
+__device__ __forceinline__ void ffma2(float& d0, float& d1, float a0, float a1, float b0, float b1, float c0,
+                                      float c1) {
+  asm("{\n\t.reg .b64 ra, rb, rc, rd;\n\tmov.b64 ra, {%2, %3};\n\tmov.b64 rb, {%4, %5};\n\t"
+      "mov.b64 rc, {%6, %7};\n\tfma.rn.f32x2 rd, ra, rb, rc;\n\tmov.b64 {%0, %1}, rd;\n\t}"
+      : "=f"(d0), "=f"(d1)
+      : "f"(a0), "f"(a1), "f"(b0), "f"(b1), "f"(c0), "f"(c1));
+}
+__device__ __forceinline__ void fadd2(float& d0, float& d1, float a0, float a1, float b0, float b1) {
+  asm("{\n\t.reg .b64 ra, rb, rd;\n\tmov.b64 ra, {%2, %3};\n\tmov.b64 rb, {%4, %5};\n\t"
+      "add.rn.f32x2 rd, ra, rb;\n\tmov.b64 {%0, %1}, rd;\n\t}"
+      : "=f"(d0), "=f"(d1)
+      : "f"(a0), "f"(a1), "f"(b0), "f"(b1));
+}
+__device__ __forceinline__ float fmax3(float a, float b, float c) {
+  float d;
+  asm("max.f32 %0, %1, %2, %3;" : "=f"(d) : "f"(a), "f"(b), "f"(c));
+  return d;
+}
+
 __device__ __forceinline__ float fast_exp2(float x) {
   float y;
   asm("ex2.approx.ftz.f32 %0, %1;" : "=f"(y) : "f"(x));
   return y;
-}
-
-// 2^x on the FMA / integer pipes, for softmax arguments (x <= ~8; results below 2^-125 flush to
-// tiny values, which bf16 P rounds away next to a row maximum of at least 2^-8).  Range reduction
-// x = n + f with n = round(x) taken from the low mantissa bits of x + 1.5 * 2^23 and f in
-// [-0.5, 0.5]; 2^f by a degree-3 polynomial (a relative-error least-squares fit made for this
-// kernel, max relative error 7.5e-5, far below bf16's 2^-9); 2^n is added to the exponent field
-// (the magic constant's own bits vanish in the 23-bit shift).  Moving a share of the softmax
-// exponentials here relieves the MUFU unit, which otherwise needs as many cycles per score tile as
-// the tensor core (the exponential-emulation idea of FlashAttention-4).
-__device__ __forceinline__ float exp2_poly(float x) {
-  x = fmaxf(x, -125.f);
-  const float t = x + 12582912.f;
-  const float f = x - (t - 12582912.f);
-  const float p = fmaf(fmaf(fmaf(0.0551716685f, f, 0.2426111400f), f, 0.6932609677f), f, 0.9999280572f);
-  return __int_as_float(__float_as_int(p) + (__float_as_int(t) << 23));
 }
 
 // ============================================================================ forward
@@ -127,6 +132,7 @@ constexpr int FWD_THREADS = 320;
 constexpr int FWD_RING = 5;  // K/V tiles in flight (P lives in TMEM, so the smem goes to the ring)
 constexpr int FWD_SMEM = 2 * TILE_BYTES /*Q*/ + FWD_RING * TILE_BYTES + 1024 + 256;
 
+template <int PAIRED, int PACKED>
 __global__ void __launch_bounds__(FWD_THREADS, 1)
 attn_fwd_kernel(const __grid_constant__ CUtensorMap qmap, const __grid_constant__ CUtensorMap kmap,
                 const __grid_constant__ CUtensorMap vmap, const WorkItem* __restrict__ items, int L, int H,
@@ -231,6 +237,12 @@ attn_fwd_kernel(const __grid_constant__ CUtensorMap qmap, const __grid_constant_
           mma_bf16_ts(tmem + 256 + x * 128, tmem + x * 128 + kk * 8, desc_mnmajor(vb, kk), id_pv, acc || kk > 0);
         mma_commit(pv_done(x));
       };
+      // S_x(j+1) overwrites the columns PV_x(j) reads P_x(j) from: wait for PV_x(j) first
+      auto next_s = [&](int x, uint32_t kb, int j) {
+        if (!(ok = mbar_wait(pv_done(x), j & 1, 29 + x))) return;
+        tc_fence_after();
+        issue_s(x, kb);
+      };
       // prologue: S_A(0), S_B(0)
       uint32_t kb = wait_slot(0);
       if (ok) {
@@ -249,19 +261,16 @@ attn_fwd_kernel(const __grid_constant__ CUtensorMap qmap, const __grid_constant_
         if (j + 1 < n_kv) {
           kb2 = wait_slot(nk);
           if (!ok) break;
-          // S_A(j+1) overwrites the columns PV_A(j) reads P from
-          if (!(ok = mbar_wait(pv_done(0), j & 1, 29))) break;
-          tc_fence_after();
-          issue_s(0, kb2);
+          next_s(0, kb2, j);
+          if (!ok) break;
         }
         if (!(ok = mbar_wait(p_ready(1), j & 1, 25))) break;
         tc_fence_after();
         issue_pv(1, vb, j > 0);
         mma_commit(kv_empty(nv % FWD_RING));
         if (j + 1 < n_kv) {
-          if (!(ok = mbar_wait(pv_done(1), j & 1, 30))) break;
-          tc_fence_after();
-          issue_s(1, kb2);
+          next_s(1, kb2, j);
+          if (!ok) break;
           mma_commit(kv_empty(nk % FWD_RING));
         }
       }
@@ -281,27 +290,44 @@ attn_fwd_kernel(const __grid_constant__ CUtensorMap qmap, const __grid_constant_
       if (!(ok = mbar_wait(s_full(x), j & 1, 26))) break;
       tc_fence_after();
       const int valid = min(BT, it.seg_len - j * BT);
-      // row maximum: two chunks per TMEM wait (10 warps per CTA cap registers at 168 per thread, so
-      // at most 64 scores are live at a time)
+      // row maximum: PAIRED reads two chunks per TMEM wait (10 warps per CTA cap registers at 168
+      // per thread, so at most 64 scores are live at a time); otherwise one chunk per wait
       float mx0 = -INFINITY, mx1 = -INFINITY;
-#pragma unroll
-      for (int h2 = 0; h2 < 2; ++h2) {
-        uint32_t ra[32], rb[32];
-        tmem_ld32(tS + h2 * 64, ra);
-        tmem_ld32(tS + h2 * 64 + 32, rb);
-        tmem_ld_wait();
+      auto max_chunk = [&](const uint32_t (&r)[32], int c0) {
         if (valid == BT) {
 #pragma unroll
-          for (int i = 0; i < 32; ++i) {
-            mx0 = fmaxf(mx0, __uint_as_float(ra[i]));
-            mx1 = fmaxf(mx1, __uint_as_float(rb[i]));
+          for (int i = 0; i < 32; i += 4) {
+            if (PACKED) {
+              mx0 = fmax3(mx0, __uint_as_float(r[i]), __uint_as_float(r[i + 1]));
+              mx1 = fmax3(mx1, __uint_as_float(r[i + 2]), __uint_as_float(r[i + 3]));
+            } else {
+              mx0 = fmaxf(fmaxf(mx0, __uint_as_float(r[i])), __uint_as_float(r[i + 1]));
+              mx1 = fmaxf(fmaxf(mx1, __uint_as_float(r[i + 2])), __uint_as_float(r[i + 3]));
+            }
           }
         } else {
 #pragma unroll
-          for (int i = 0; i < 32; ++i) {
-            if (h2 * 64 + i < valid) mx0 = fmaxf(mx0, __uint_as_float(ra[i]));
-            if (h2 * 64 + 32 + i < valid) mx1 = fmaxf(mx1, __uint_as_float(rb[i]));
-          }
+          for (int i = 0; i < 32; ++i)
+            if (c0 + i < valid) mx0 = fmaxf(mx0, __uint_as_float(r[i]));
+        }
+      };
+      if (PAIRED) {
+#pragma unroll
+        for (int h2 = 0; h2 < 2; ++h2) {
+          uint32_t ra[32], rb[32];
+          tmem_ld32(tS + h2 * 64, ra);
+          tmem_ld32(tS + h2 * 64 + 32, rb);
+          tmem_ld_wait();
+          max_chunk(ra, h2 * 64);
+          max_chunk(rb, h2 * 64 + 32);
+        }
+      } else {
+#pragma unroll
+        for (int c = 0; c < 4; ++c) {
+          uint32_t r[32];
+          tmem_ld32(tS + c * 32, r);
+          tmem_ld_wait();
+          max_chunk(r, c * 32);
         }
       }
       const float m_new = fmaxf(m_used, fmaxf(mx0, mx1) * scale_log2);
@@ -332,34 +358,47 @@ attn_fwd_kernel(const __grid_constant__ CUtensorMap qmap, const __grid_constant_
         uint32_t w[16];
 #pragma unroll
         for (int i = 0; i < 32; i += 2) {
-          const float x0 = fmaf(__uint_as_float(r[i]), scale_log2, -m_used);
-          const float x1 = fmaf(__uint_as_float(r[i + 1]), scale_log2, -m_used);
-          float p0, p1;
-          if ((i & 6) == 6) {  // one pair in four on the FMA pipe
-            p0 = exp2_poly(x0);
-            p1 = exp2_poly(x1);
+          float x0, x1;
+          if (PACKED) {
+            ffma2(x0, x1, __uint_as_float(r[i]), __uint_as_float(r[i + 1]), scale_log2, scale_log2, -m_used, -m_used);
           } else {
-            p0 = fast_exp2(x0);
-            p1 = fast_exp2(x1);
+            x0 = fmaf(__uint_as_float(r[i]), scale_log2, -m_used);
+            x1 = fmaf(__uint_as_float(r[i + 1]), scale_log2, -m_used);
           }
+          float p0 = fast_exp2(x0);
+          float p1 = fast_exp2(x1);
           if (valid < BT) {
             p0 = c * 32 + i < valid ? p0 : 0.f;
             p1 = c * 32 + i + 1 < valid ? p1 : 0.f;
           }
-          l0 += p0;
-          l1 += p1;
+          if (PACKED) {
+            fadd2(l0, l1, l0, l1, p0, p1);
+          } else {
+            l0 += p0;
+            l1 += p1;
+          }
           w[i >> 1] = pack_bf16(p0, p1);
         }
         tmem_st16(tS + c * 16, w);
       };
+      if (PAIRED) {
 #pragma unroll
-      for (int h2 = 0; h2 < 2; ++h2) {
-        uint32_t ra[32], rb[32];
-        tmem_ld32(tS + h2 * 64, ra);
-        tmem_ld32(tS + h2 * 64 + 32, rb);
-        tmem_ld_wait();
-        softmax_chunk(ra, 2 * h2);
-        softmax_chunk(rb, 2 * h2 + 1);
+        for (int h2 = 0; h2 < 2; ++h2) {
+          uint32_t ra[32], rb[32];
+          tmem_ld32(tS + h2 * 64, ra);
+          tmem_ld32(tS + h2 * 64 + 32, rb);
+          tmem_ld_wait();
+          softmax_chunk(ra, 2 * h2);
+          softmax_chunk(rb, 2 * h2 + 1);
+        }
+      } else {
+#pragma unroll
+        for (int c = 0; c < 4; ++c) {
+          uint32_t r[32];
+          tmem_ld32(tS + c * 32, r);
+          tmem_ld_wait();
+          softmax_chunk(r, c);
+        }
       }
       l += l0 + l1;
       tmem_st_wait();
@@ -1014,10 +1053,12 @@ const char* make_dq_map(CUtensorMap* m, const float* base, int L, int H) {
 }
 
 int g_bwd_variant = 1;  // 1: fused single pass; 0: two passes
+int g_fwd_variant = 3;  // forward softmax: bit 0 two score chunks per TMEM wait, bit 1 packed fp32x2 math
 
 }  // namespace attn
 
 void attn_set_backward_variant(int v) { attn::g_bwd_variant = v ? 1 : 0; }
+void attn_set_forward_variant(int v) { attn::g_fwd_variant = v & 3; }
 
 const char* launch_attn_fwd(const void* q, const void* k, const void* v, const int* items, int n_items, int L, int H,
                             int head_dim, float scale, void* out, float* lse, cudaStream_t s, const uint64_t* o_peer,
@@ -1030,15 +1071,21 @@ const char* launch_attn_fwd(const void* q, const void* k, const void* v, const i
   CUtensorMap qm, km, vm;
   const char* e;
   if ((e = make_qkv_map(&qm, q, L, H)) || (e = make_qkv_map(&km, k, L, H)) || (e = make_qkv_map(&vm, v, L, H))) return e;
-  static bool attr = false;
-  if (!attr) {
-    if (cudaFuncSetAttribute(attn_fwd_kernel, cudaFuncAttributeMaxDynamicSharedMemorySize, FWD_SMEM) != cudaSuccess)
+  typedef void (*FwdKernel)(CUtensorMap, CUtensorMap, CUtensorMap, const WorkItem*, int, int, float, __nv_bfloat16*,
+                            float*, PeerRows);
+  static const FwdKernel variants[4] = {attn_fwd_kernel<0, 0>, attn_fwd_kernel<1, 0>, attn_fwd_kernel<0, 1>,
+                                        attn_fwd_kernel<1, 1>};
+  static bool attr[4] = {};
+  const int var = g_fwd_variant & 3;
+  if (!attr[var]) {
+    if (cudaFuncSetAttribute(variants[var], cudaFuncAttributeMaxDynamicSharedMemorySize, FWD_SMEM) != cudaSuccess)
       return "attention: cannot set smem size";
-    attr = true;
+    attr[var] = true;
   }
   dim3 grid(n_items, H);
-  attn_fwd_kernel<<<grid, FWD_THREADS, FWD_SMEM, s>>>(qm, km, vm, reinterpret_cast<const WorkItem*>(items), L, H,
-                                                      scale * kLog2e, (__nv_bfloat16*)out, lse, opr);
+  auto kern = variants[var];
+  kern<<<grid, FWD_THREADS, FWD_SMEM, s>>>(qm, km, vm, reinterpret_cast<const WorkItem*>(items), L, H, scale * kLog2e,
+                                           (__nv_bfloat16*)out, lse, opr);
   return cudaGetLastError() == cudaSuccess ? nullptr : "attention forward launch failed";
 }
 

@@ -32,6 +32,7 @@ const char* launch_attn_bwd(const void* q, const void* k, const void* v, const v
                             float* dq_acc, cudaStream_t s);
 int attn_error_flag(bool reset);
 void attn_set_backward_variant(int v);
+void attn_set_forward_variant(int v);
 void launch_sumsq(const void* x, bool fp32, size_t n, float* partial, int n_part, cudaStream_t s);
 void launch_reduce_clip(const float* partial, int n, float max_norm, float* out, cudaStream_t s);
 void launch_muon_momentum(float* buf, const void* g, bool g_fp32, const float* clip, float mu, size_t n, void* u,
@@ -596,6 +597,20 @@ void muon_update(torch::Tensor hi, torch::Tensor lo, torch::Tensor u, torch::Ten
   check_launch(nullptr, "muon_update");
 }
 
+// Muon update whose orthogonalised rows are read from `u_addr`: an address in this or another
+// rank's peer-mapped memory (distributed Muon's scatter fused into the update).
+void muon_update_peer(torch::Tensor hi, torch::Tensor lo, int64_t u_addr, torch::Tensor lr, double lr_scale,
+                      double wd) {
+  const at::cuda::CUDAGuard guard(hi.device());
+  check_half16(hi, "hi");
+  check_half16(lo, "lo");
+  TORCH_CHECK(lo.numel() == hi.numel(), "muon_update_peer: size mismatch");
+  TORCH_CHECK(u_addr != 0 && u_addr % 16 == 0, "muon_update_peer: u address must be 16-byte aligned");
+  launch_muon_update(hi.data_ptr(), lo.data_ptr(), reinterpret_cast<const void*>(u_addr), lr.data_ptr<float>(),
+                     (float)lr_scale, (float)wd, hi.numel(), stream());
+  check_launch(nullptr, "muon_update_peer");
+}
+
 void adamw_update(torch::Tensor hi, torch::Tensor lo, torch::Tensor g, torch::Tensor m, torch::Tensor v,
                   c10::optional<torch::Tensor> clip, torch::Tensor lr, double beta1, double beta2, double eps,
                   double wd, int64_t step) {
@@ -699,6 +714,7 @@ PYBIND11_MODULE(TORCH_EXTENSION_NAME, m) {
   m.def("gemm", &pan::gemm);
   m.def("gemm_force_cta_group", &pan::gemm_force_cta_group);
   m.def("attn_set_backward_variant", &pan::attn_set_backward_variant);
+  m.def("attn_set_forward_variant", &pan::attn_set_forward_variant);
   m.def("gemm_tuning", &pan::gemm_tuning);
   m.def("gemm_grouped_nt", &pan::gemm_grouped_nt);
   m.def("gemm_batched", &pan::gemm_batched);
@@ -714,6 +730,7 @@ PYBIND11_MODULE(TORCH_EXTENSION_NAME, m) {
   m.def("norm_and_clip", &pan::norm_and_clip);
   m.def("muon_momentum", &pan::muon_momentum);
   m.def("muon_update", &pan::muon_update);
+  m.def("muon_update_peer", &pan::muon_update_peer);
   m.def("adamw_update", &pan::adamw_update);
   m.def("split_master", &pan::split_master);
   m.def("join_master", &pan::join_master);

@@ -108,6 +108,32 @@ __global__ void muon_update_kernel(uint16_t* __restrict__ hi, uint16_t* __restri
   }
 }
 
+// Same update, 8 elements per thread with 16-byte loads of u (which may be another rank's memory,
+// read over NVLink: the scatter of distributed Muon's orthogonalised rows fused into the update).
+__global__ void muon_update_vec_kernel(uint16_t* __restrict__ hi, uint16_t* __restrict__ lo,
+                                       const __nv_bfloat16* __restrict__ u, const float* __restrict__ lr,
+                                       float lr_scale, float wd, size_t n8) {
+  const float l = lr[0];
+  const float decay = 1.f - l * wd;
+  const float step = l * lr_scale;
+  for (size_t i = (size_t)blockIdx.x * blockDim.x + threadIdx.x; i < n8; i += (size_t)gridDim.x * blockDim.x) {
+    const uint4 uv = reinterpret_cast<const uint4*>(u)[i];
+    uint4 hv = reinterpret_cast<const uint4*>(hi)[i];
+    uint4 lv = reinterpret_cast<const uint4*>(lo)[i];
+    const __nv_bfloat16* ub = reinterpret_cast<const __nv_bfloat16*>(&uv);
+    uint16_t* hb = reinterpret_cast<uint16_t*>(&hv);
+    uint16_t* lb = reinterpret_cast<uint16_t*>(&lv);
+#pragma unroll
+    for (int e = 0; e < 8; ++e) {
+      float p = join_master(hb[e], lb[e]);
+      p = p * decay - step * __bfloat162float(ub[e]);
+      split_master(p, hb[e], lb[e]);
+    }
+    reinterpret_cast<uint4*>(hi)[i] = hv;
+    reinterpret_cast<uint4*>(lo)[i] = lv;
+  }
+}
+
 template <typename G>
 __global__ void adamw_update_kernel(uint16_t* __restrict__ hi, uint16_t* __restrict__ lo, const G* __restrict__ g,
                                     float* __restrict__ m, float* __restrict__ v, const float* __restrict__ clip,
@@ -211,8 +237,14 @@ void launch_muon_momentum(float* buf, const void* g, bool g_fp32, const float* c
 }
 void launch_muon_update(void* hi, void* lo, const void* u, const float* lr, float lr_scale, float wd, size_t n,
                         cudaStream_t s) {
-  muon_update_kernel<<<grid_for(n), 256, 0, s>>>((uint16_t*)hi, (uint16_t*)lo, (const __nv_bfloat16*)u, lr, lr_scale,
-                                                 wd, n);
+  const bool vec = n % 8 == 0 && ((reinterpret_cast<uintptr_t>(hi) | reinterpret_cast<uintptr_t>(lo) |
+                                   reinterpret_cast<uintptr_t>(u)) & 15) == 0;
+  if (vec)
+    muon_update_vec_kernel<<<grid_for(n / 8), 256, 0, s>>>((uint16_t*)hi, (uint16_t*)lo, (const __nv_bfloat16*)u, lr,
+                                                           lr_scale, wd, n / 8);
+  else
+    muon_update_kernel<<<grid_for(n), 256, 0, s>>>((uint16_t*)hi, (uint16_t*)lo, (const __nv_bfloat16*)u, lr,
+                                                   lr_scale, wd, n);
 }
 void launch_adamw_update(void* hi, void* lo, const void* g, bool g_fp32, float* m, float* v, const float* clip,
                          const float* lr, float beta1, float beta2, float eps, float wd, float bc1, float bc2_sqrt,

@@ -210,6 +210,8 @@ class TrainEngine:
         self.peer_comm = False
         if self.world > 1 and device.type == "cuda" and os.environ.get("PAN_PEER_COMM", "1") != "0":
             self.peer_comm = self.sharded.enable_peer_memory()
+        self._muon_pm = None  # peer-mapped exchange / result regions of distributed Muon
+        self._muon_layouts: Dict[int, dict] = {}
         self.stash_in_grads = self.world == 1
         self.accum_steps = 1
         self.accumulating = False
@@ -538,13 +540,20 @@ class TrainEngine:
         g = self.sharded.grad_of(u)
         b1, b2 = o.adamw_betas
         muon_work = []
+        lay = self._muon_layout(u) if self._peer_muon() else None
+        n_remote = 0
         for s in u.slots:
             n = s.shard_rows * s.cols
             sl = slice(s.shard_off, s.shard_off + n)
             so = self._soff[id(s)]
             ss = slice(so, so + n)
             if self._is_muon(s):
-                upd = torch.empty(n, dtype=torch.bfloat16, device=self.device)
+                if lay is not None and not self._muon_local(s):
+                    # straight into this rank's exchange region, where the matrix owner reads it
+                    upd = self._muon_pm.view(lay["xoff"][n_remote], n, torch.bfloat16)
+                    n_remote += 1
+                else:
+                    upd = torch.empty(n, dtype=torch.bfloat16, device=self.device)
                 E.muon_momentum(st["mom"][ss], g[sl], clip, o.momentum, upd)
                 muon_work.append((s, sl, upd))
             else:
@@ -554,12 +563,7 @@ class TrainEngine:
             return
         local, remote = [], []
         for item in muon_work:
-            s = item[0]
-            if self.world == 1 or (s.chunks is not None and s.chunks[0] == 0 and s.chunks[1] % self.world == 0
-                                   and s.rows == s.rows_pad):
-                local.append(item)
-            else:
-                remote.append(item)
+            (local if self._muon_local(item[0]) else remote).append(item)
         for s, sl, upd in local:
             chunked = s.chunks is not None and s.chunks[0] == 0
             n_local = s.chunks[1] // self.world if chunked else 1
@@ -570,7 +574,85 @@ class TrainEngine:
             E.muon_update(u.hi[sl], lo[sl], orth.reshape(-1), self._lr(), adjust_lr_scale(shape, o.adjust_lr_fn),
                           o.weight_decay)
         if remote:
-            self._muon_all_to_all(u, lo, remote)
+            if lay is not None:
+                self._muon_peer(u, lo, remote, lay)
+            else:
+                self._muon_all_to_all(u, lo, remote)
+
+    def _muon_local(self, s) -> bool:
+        """A Muon matrix each rank can orthogonalise alone: its row shard is a whole number of the
+        independent row chunks (or there is one rank)."""
+        return self.world == 1 or (s.chunks is not None and s.chunks[0] == 0 and s.chunks[1] % self.world == 0
+                                   and s.rows == s.rows_pad)
+
+    def _peer_muon(self) -> bool:
+        return self.peer_comm and self.world > 1 and os.environ.get("PAN_PEER_MUON", "1") != "0"
+
+    def _muon_layout(self, u: Unit) -> dict:
+        """Byte offsets of unit ``u``'s distributed-Muon buffers, identical on every rank: the
+        exchange region holds each remote matrix's momentum rows of this rank; matrix j of the unit
+        belongs to owner j % world, whose result region holds the full orthogonalised matrix.
+        The peer-mapped buffer is allocated at the first call for the largest unit."""
+        lay = self._muon_layouts.get(u.index)
+        if lay is not None:
+            return lay
+        from ..parallel.symm import PeerMemory
+        W = self.world
+        for unit in self.sharded.units:
+            remote = [s for s in unit.slots if self._is_muon(s) and not self._muon_local(s)]
+            xoff, off = [], 0
+            for s in remote:
+                xoff.append(off)
+                off += _align256(s.shard_rows * s.cols * 2)
+            roff, per_owner = [], [0] * W
+            for j, s in enumerate(remote):
+                roff.append(per_owner[j % W])
+                per_owner[j % W] += _align256(s.rows_pad * s.cols * 2)
+            self._muon_layouts[unit.index] = dict(xoff=xoff, x_bytes=off, roff=roff, r_bytes=max(per_owner),
+                                                  plans={})
+        x_max = max(l["x_bytes"] for l in self._muon_layouts.values())
+        r_max = max(l["r_bytes"] for l in self._muon_layouts.values())
+        for l in self._muon_layouts.values():
+            l["rbase"] = x_max
+        self._muon_pm = PeerMemory(max(256, x_max + r_max), self.group, self.device)
+        return self._muon_layouts[u.index]
+
+    def _muon_peer(self, u: Unit, lo: torch.Tensor, work, lay: dict) -> None:
+        """Distributed Muon over peer memory (reference: patch_muon.py:174-268, which moves the rows
+        with two NCCL all-to-alls): the momentum kernel already wrote this rank's rows of every
+        remote matrix into its exchange region; each owner gathers its matrices' rows from all ranks
+        with peer loads straight into its result region, orthogonalises them in place, and every
+        rank's update kernel reads its own rows from the owner's result region over NVLink."""
+        from ..parallel.symm import _pack
+        E = F
+        o = self.optim
+        W, me, pm = self.world, self.rank, self._muon_pm
+        pm.barrier(0)  # every rank's momentum rows are in its exchange region
+        for j, (s, sl, upd) in enumerate(work):
+            if j % W != me:
+                continue
+            n = s.shard_rows * s.cols
+            plan = lay["plans"].get(j)
+            if plan is None:
+                segs = [(lay["xoff"][j] // 2, r * n, n) for r in range(W)]
+                plan = lay["plans"][j] = _pack(segs, list(range(W)), self.device)
+            full = pm.view(lay["rbase"] + lay["roff"][j], s.rows_pad * s.cols, torch.bfloat16).view(s.rows_pad, s.cols)
+            seg_t, prefix, total, seg_peer = plan
+            ext().peer_gather(pm.peers, seg_t, seg_peer, prefix, total, full)
+            real = full[:s.rows]
+            if s.chunks is not None and s.chunks[0] == 0 and s.chunks[1] > 1:
+                orth = gram_newton_schulz(chunk_view(real, s.chunks[1])).reshape(s.rows, s.cols)
+            else:
+                orth = gram_newton_schulz(real)
+            real.copy_(orth)
+            full[s.rows:].zero_()
+        pm.barrier(1)  # every owner's orthogonalised matrices are ready
+        ptrs = pm.handle.buffer_ptrs
+        for j, (s, sl, upd) in enumerate(work):
+            addr = ptrs[j % W] + lay["rbase"] + lay["roff"][j] + me * s.shard_rows * s.cols * 2
+            shape = (s.rows // s.chunks[1], s.cols) if (s.chunks and s.chunks[0] == 0) else (s.rows, s.cols)
+            ext().muon_update_peer(u.hi[sl], lo[sl], int(addr), self._lr(), adjust_lr_scale(shape, o.adjust_lr_fn),
+                                   o.weight_decay)
 
     def _muon_all_to_all(self, u: Unit, lo: torch.Tensor, work) -> None:
         """Owner-rank orthogonalisation of row-sharded matrices (reference: patch_muon.py:174-268)."""

@@ -45,14 +45,17 @@ def _engine_step(rank, world, port, path):
                           optim=OptimConfig(lr=1e-3), offload="off")
         assert eng.peer_comm == (mode == "1")
         batch = batch_to_device(synthetic_packed_batch(2, (3, 16, 16), 40, rope_axes=(32, 48, 48), seed=rank), "cuda")
+        hi0 = [u.hi.float().clone() for u in eng.sharded.units]
         loss = eng.forward_backward(batch)
         grads = [u.grad_shard.clone() for u in eng.sharded.units]
         norm = eng.grad_norm().clone()
         eng.optimizer_step()
+        delta = [(u.hi.float() - h0).cpu() for u, h0 in zip(eng.sharded.units, hi0)]
         loss2 = eng.forward_backward(batch)  # second step: exercises the barriers and the gradient ring again
         torch.cuda.synchronize()
         out[mode] = dict(loss=loss.item(), loss2=loss2.item(), norm=norm.tolist(), grads=[g.cpu() for g in grads],
-                         hi=[u.hi.float().cpu() for u in eng.sharded.units], err=ext().error_flag(True))
+                         hi=[u.hi.float().cpu() for u in eng.sharded.units], delta=delta,
+                         err=ext().error_flag(True))
         del eng
         torch.cuda.empty_cache()
     if rank == 0:
@@ -101,6 +104,9 @@ def test_peer_memory_engine_matches_nccl(tmp_path):
         assert (ga - gb).abs().max().item() <= 1e-5 * (ga.abs().max().item() + 1e-12)
     for ha, hb in zip(a["hi"], b["hi"]):
         assert (ha - hb).abs().max().item() <= 1e-2 * (ha.abs().max().item() + 1e-12)
+    # the optimizer's change of every parameter (Muon over peer memory vs NCCL all-to-all, AdamW)
+    for da, db in zip(a["delta"], b["delta"]):
+        assert (da - db).abs().max().item() <= 5e-2 * (da.abs().max().item() + 1e-12)
     assert abs(a["loss2"] - b["loss2"]) < 1e-3 * abs(a["loss2"])
 
 
