@@ -236,6 +236,8 @@ class TrainEngine:
         # the write-back that last read slot s
         self._slots: List[torch.Tensor] = []
         self._slot_free: List[Optional[torch.cuda.Event]] = [None, None]
+        if self._peer_muon() and self.sharded.units:
+            self._muon_layout(self.sharded.units[0])  # allocate now, before memory placement
 
     # ---------------------------------------------------------------- construction
     def _plan_offload(self, total: int, offload: str, act_bytes: int) -> bool:
