@@ -115,12 +115,6 @@ __device__ __forceinline__ void fadd2(float& d0, float& d1, float a0, float a1, 
       : "=f"(d0), "=f"(d1)
       : "f"(a0), "f"(a1), "f"(b0), "f"(b1));
 }
-__device__ __forceinline__ void fmul2(float& d0, float& d1, float a0, float a1, float b0, float b1) {
-  asm("{\n\t.reg .b64 ra, rb, rd;\n\tmov.b64 ra, {%2, %3};\n\tmov.b64 rb, {%4, %5};\n\t"
-      "mul.rn.f32x2 rd, ra, rb;\n\tmov.b64 {%0, %1}, rd;\n\t}"
-      : "=f"(d0), "=f"(d1)
-      : "f"(a0), "f"(a1), "f"(b0), "f"(b1));
-}
 __device__ __forceinline__ float fmax3(float a, float b, float c) {
   float d;
   asm("max.f32 %0, %1, %2, %3;" : "=f"(d) : "f"(a), "f"(b), "f"(c));
@@ -713,7 +707,6 @@ constexpr int FB_STAGE = 32 * D * 4;  // 32 query rows of fp32 dQ
 constexpr int FB_SMEM = 2 * TILE_BYTES /*K, V*/ + 2 * TILE_BYTES /*Q ring*/ + TILE_BYTES /*dO*/ +
                         TILE_BYTES /*dS^T*/ + 2 * FB_STAGE + 1024 + 256 + 2 * BT * 4;
 
-template <int FAST>
 __global__ void __launch_bounds__(FB_THREADS, 1)
 attn_bwd_fused_kernel(const __grid_constant__ CUtensorMap qmap, const __grid_constant__ CUtensorMap kmap,
                       const __grid_constant__ CUtensorMap vmap, const __grid_constant__ CUtensorMap domap,
@@ -843,7 +836,6 @@ attn_bwd_fused_kernel(const __grid_constant__ CUtensorMap qmap, const __grid_con
       if (!(ok = mbar_wait(B(7), i & 1, 49))) break;
       if (i > 0 && !(ok = mbar_wait(B(9), (i - 1) & 1, 50))) break;  // dQ^T(i-1) has read dS^T smem
       tc_fence_after();
-      const bool full = FAST && valid_q == BT && row_valid;
 #pragma unroll
       for (int c = 0; c < 4; ++c) {
         uint32_t r[32], y[32];
@@ -851,40 +843,19 @@ attn_bwd_fused_kernel(const __grid_constant__ CUtensorMap qmap, const __grid_con
         tmem_ld32(T_DP + lane_off + c * 32, y);
         tmem_ld_wait();
         uint32_t wp[16], wd[16];
-        if (full) {
-          // whole tile valid: no masks, LSE / Delta read four at a time, packed fp32x2 math
 #pragma unroll
-          for (int j = 0; j < 32; j += 4) {
-            const float4 lv = *reinterpret_cast<const float4*>(&s_vec[0][c * 32 + j]);
-            const float4 dv = *reinterpret_cast<const float4*>(&s_vec[1][c * 32 + j]);
-            float x0, x1, x2, x3, t0, t1, t2, t3;
-            ffma2(x0, x1, __uint_as_float(r[j]), __uint_as_float(r[j + 1]), scale_log2, scale_log2, -lv.x, -lv.y);
-            ffma2(x2, x3, __uint_as_float(r[j + 2]), __uint_as_float(r[j + 3]), scale_log2, scale_log2, -lv.z, -lv.w);
-            const float p0 = fast_exp2(x0), p1 = fast_exp2(x1), p2 = fast_exp2(x2), p3 = fast_exp2(x3);
-            fadd2(t0, t1, __uint_as_float(y[j]), __uint_as_float(y[j + 1]), -dv.x, -dv.y);
-            fadd2(t2, t3, __uint_as_float(y[j + 2]), __uint_as_float(y[j + 3]), -dv.z, -dv.w);
-            fmul2(t0, t1, t0, t1, p0, p1);
-            fmul2(t2, t3, t2, t3, p2, p3);
-            wp[j >> 1] = pack_bf16(p0, p1);
-            wp[(j >> 1) + 1] = pack_bf16(p2, p3);
-            wd[j >> 1] = pack_bf16(t0, t1);
-            wd[(j >> 1) + 1] = pack_bf16(t2, t3);
+        for (int j = 0; j < 32; j += 2) {
+          float pv[2], dsv[2];
+#pragma unroll
+          for (int e = 0; e < 2; ++e) {
+            const int cc = c * 32 + j + e;
+            const bool on = cc < valid_q && row_valid;
+            const float p = on ? fast_exp2(__uint_as_float(r[j + e]) * scale_log2 - s_vec[0][cc]) : 0.f;
+            pv[e] = p;
+            dsv[e] = p * (__uint_as_float(y[j + e]) - s_vec[1][cc]);
           }
-        } else {
-#pragma unroll
-          for (int j = 0; j < 32; j += 2) {
-            float pv[2], dsv[2];
-#pragma unroll
-            for (int e = 0; e < 2; ++e) {
-              const int cc = c * 32 + j + e;
-              const bool on = cc < valid_q && row_valid;
-              const float p = on ? fast_exp2(__uint_as_float(r[j + e]) * scale_log2 - s_vec[0][cc]) : 0.f;
-              pv[e] = p;
-              dsv[e] = p * (__uint_as_float(y[j + e]) - s_vec[1][cc]);
-            }
-            wp[j >> 1] = pack_bf16(pv[0], pv[1]);
-            wd[j >> 1] = pack_bf16(dsv[0], dsv[1]);
-          }
+          wp[j >> 1] = pack_bf16(pv[0], pv[1]);
+          wd[j >> 1] = pack_bf16(dsv[0], dsv[1]);
         }
         // columns [16c, 16c + 16) were read in chunk c or earlier
         tmem_st16(T_S + lane_off + c * 16, wp);
@@ -1082,15 +1053,11 @@ const char* make_dq_map(CUtensorMap* m, const float* base, int L, int H) {
 }
 
 int g_bwd_variant = 1;  // 1: fused single pass; 0: two passes
-int g_bwd_fast = 1;     // fused backward: unmasked packed-math path for full tiles
 int g_fwd_variant = 3;  // forward softmax: bit 0 two score chunks per TMEM wait, bit 1 packed fp32x2 math
 
 }  // namespace attn
 
-void attn_set_backward_variant(int v) {
-  attn::g_bwd_variant = v ? 1 : 0;
-  attn::g_bwd_fast = v == 1;  // 2: fused without the full-tile fast path (A/B timing)
-}
+void attn_set_backward_variant(int v) { attn::g_bwd_variant = v ? 1 : 0; }
 void attn_set_forward_variant(int v) { attn::g_fwd_variant = v & 3; }
 
 const char* launch_attn_fwd(const void* q, const void* k, const void* v, const int* items, int n_items, int L, int H,
@@ -1139,9 +1106,7 @@ const char* launch_attn_bwd(const void* q, const void* k, const void* v, const v
   if (g_bwd_variant == 1 && dq_acc != nullptr) {
     static bool fattr = false;
     if (!fattr) {
-      if (cudaFuncSetAttribute(attn_bwd_fused_kernel<0>, cudaFuncAttributeMaxDynamicSharedMemorySize, FB_SMEM) !=
-              cudaSuccess ||
-          cudaFuncSetAttribute(attn_bwd_fused_kernel<1>, cudaFuncAttributeMaxDynamicSharedMemorySize, FB_SMEM) !=
+      if (cudaFuncSetAttribute(attn_bwd_fused_kernel, cudaFuncAttributeMaxDynamicSharedMemorySize, FB_SMEM) !=
           cudaSuccess)
         return "attention: cannot set smem size (fused backward)";
       fattr = true;
@@ -1150,7 +1115,7 @@ const char* launch_attn_bwd(const void* q, const void* k, const void* v, const v
     if ((e = make_dq_map(&dqm, dq_acc, L, H))) return e;
     if (cudaMemsetAsync(dq_acc, 0, (size_t)L * H * D * sizeof(float), s) != cudaSuccess) return "dq memset failed";
     if (n_items_kv > 0)
-      (g_bwd_fast ? attn_bwd_fused_kernel<1> : attn_bwd_fused_kernel<0>)<<<dim3(n_items_kv, H), FB_THREADS, FB_SMEM, s>>>(
+      attn_bwd_fused_kernel<<<dim3(n_items_kv, H), FB_THREADS, FB_SMEM, s>>>(
           qm, km, vm, dom, dqm, reinterpret_cast<const WorkItem*>(items_kv), L, H, scale, lse, delta,
           (__nv_bfloat16*)dk, (__nv_bfloat16*)dv, PeerRows{nullptr, 1, 0, H}, PeerRows{nullptr, 1, 0, H});
     const size_t n8 = (size_t)L * H * D / 8;
@@ -1212,16 +1177,14 @@ const char* launch_attn_bwd_cp(const void* q, const void* k, const void* v, cons
     return e;
   static bool fattr = false;
   if (!fattr) {
-    if (cudaFuncSetAttribute(attn_bwd_fused_kernel<0>, cudaFuncAttributeMaxDynamicSharedMemorySize, FB_SMEM) !=
-            cudaSuccess ||
-        cudaFuncSetAttribute(attn_bwd_fused_kernel<1>, cudaFuncAttributeMaxDynamicSharedMemorySize, FB_SMEM) !=
+    if (cudaFuncSetAttribute(attn_bwd_fused_kernel, cudaFuncAttributeMaxDynamicSharedMemorySize, FB_SMEM) !=
         cudaSuccess)
       return "attention: cannot set smem size (fused backward)";
     fattr = true;
   }
   if (cudaMemsetAsync(dq_acc, 0, (size_t)L * H * D * sizeof(float), s) != cudaSuccess) return "dq memset failed";
   if (n_items_kv > 0)
-    (g_bwd_fast ? attn_bwd_fused_kernel<1> : attn_bwd_fused_kernel<0>)<<<dim3(n_items_kv, H), FB_THREADS, FB_SMEM, s>>>(
+    attn_bwd_fused_kernel<<<dim3(n_items_kv, H), FB_THREADS, FB_SMEM, s>>>(
         qm, km, vm, dom, dqm, reinterpret_cast<const WorkItem*>(items_kv), L, H, scale, lse, delta, nullptr, nullptr,
         PeerRows{dk_peer, cp, head_base, H_total}, PeerRows{dv_peer, cp, head_base, H_total});
   const size_t n8 = (size_t)L * H * D / 8;
