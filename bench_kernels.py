@@ -189,8 +189,12 @@ def main():
     ap.add_argument("--iters", type=int, default=10)
     ap.add_argument("--warmup", type=int, default=3)
     ap.add_argument("--no-library", action="store_true", help="skip the cuBLAS / SDPA comparisons")
+    ap.add_argument("--attn-bwd-variant", type=int, default=None,
+                    help="attention backward: 0 two passes, 1 fused single pass, 2 pipelined single pass")
     args = ap.parse_args()
     pat = re.compile(args.case)
+    if args.attn_bwd_variant is not None:
+        ext().attn_set_backward_variant(args.attn_bwd_variant)
     peaks = measured_peaks()
     timer = Timer(args.iters, args.warmup)
     library = not args.no_library

@@ -941,6 +941,302 @@ attn_bwd_fused_kernel(const __grid_constant__ CUtensorMap qmap, const __grid_con
   }
 }
 
+// ---------------------------------------------------------------------------------------------
+// Pipelined fused backward.  Same recurrences as attn_bwd_fused_kernel, but each key tile walks
+// 64-query sub-tiles with TWO TMEM buffer sets, so the tensor core works on one sub-tile while the
+// elementwise warps and the dQ drain work on the other:
+//   buffer b (128 columns): S^T (64 cols; later P^T in its first 32, later dQ^T in all 64) and
+//                           dP^T (64 cols; later dS^T in its first 32);  dV, dK: 256 columns.
+// The MMA thread schedules from readiness instead of a fixed order: it issues a sub-tile's
+// S^T / dP^T as soon as a buffer is free (its previous dQ^T drained) and its Q / dO are loaded, and
+// a sub-tile's dV / dK / dQ^T as soon as its P^T / dS^T are written.  Q and dO sub-tiles arrive
+// through a 3-slot ring.  Barriers (index): kv_full 0, slot_full 1-3, slot_empty 4-6, s_full 7-8,
+// ds_ready 9-10, pv_done 11-12, dq_full 13-14, dq_drained 15-16, dsm_free 17-18, all_done 19.
+constexpr int BQ = 64;                          // queries per sub-tile
+constexpr int SUB_BYTES = BQ * D * 2;           // 16 KB: two [64 x 64] swizzled halves
+constexpr int SUB_HALF = SUB_BYTES / 2;
+constexpr int PB_SLOTS = 3;
+constexpr int PB_DS = BT * BQ * 2;              // dS^T [128 keys][64 queries] bf16
+constexpr int PB_STAGE = 32 * D * 4;            // 32 query rows of fp32 dQ
+constexpr int PB_SMEM = 2 * TILE_BYTES + PB_SLOTS * 2 * SUB_BYTES + 2 * PB_DS + 2 * PB_STAGE + 1024 + 256 +
+                        2 * BQ * 4;
+
+// K-major descriptor of a [64 rows, 128 cols] sub-tile at k-step kk (two 8 KB halves)
+__device__ __forceinline__ uint64_t desc_kmajor64(uint32_t base, int kk) {
+  return smem_desc_sw128(base + (kk >> 2) * SUB_HALF + (kk & 3) * 32, 16, 1024);
+}
+// the same sub-tile as an MN-major operand whose reduction dim is its 64 rows
+__device__ __forceinline__ uint64_t desc_mnmajor64(uint32_t base, int kk) {
+  return smem_desc_sw128(base + kk * 2048, SUB_HALF, 1024);
+}
+
+__global__ void __launch_bounds__(FB_THREADS, 1)
+attn_bwd_pipe_kernel(const __grid_constant__ CUtensorMap qmap, const __grid_constant__ CUtensorMap kmap,
+                     const __grid_constant__ CUtensorMap vmap, const __grid_constant__ CUtensorMap domap,
+                     const __grid_constant__ CUtensorMap dqmap, const WorkItem* __restrict__ items, int L, int H,
+                     float scale, const float* __restrict__ lse, const float* __restrict__ delta,
+                     __nv_bfloat16* __restrict__ dk_out, __nv_bfloat16* __restrict__ dv_out, const PeerRows dk_peer,
+                     const PeerRows dv_peer) {
+  extern __shared__ uint8_t smem_raw[];
+  uint8_t* smem = reinterpret_cast<uint8_t*>((reinterpret_cast<uintptr_t>(smem_raw) + 1023) & ~uintptr_t(1023));
+  uint8_t* sK = smem;
+  uint8_t* sV = sK + TILE_BYTES;
+  uint8_t* sQ = sV + TILE_BYTES;                 // PB_SLOTS sub-tiles
+  uint8_t* sdO = sQ + PB_SLOTS * SUB_BYTES;      // PB_SLOTS sub-tiles
+  uint8_t* sdS = sdO + PB_SLOTS * SUB_BYTES;     // 2 x dS^T
+  uint8_t* sStage = sdS + 2 * PB_DS;             // 2 x [32 q][128 d] fp32
+  uint64_t* bars = reinterpret_cast<uint64_t*>(sStage + 2 * PB_STAGE);
+  uint32_t* tmem_slot = reinterpret_cast<uint32_t*>(bars + 20);
+  volatile int& s_abort = *reinterpret_cast<volatile int*>(bars + 21);
+  float (*s_vec)[BQ] = reinterpret_cast<float (*)[BQ]>(reinterpret_cast<uint8_t*>(bars) + 256);
+
+  const WorkItem it = items[blockIdx.x];
+  const int h = blockIdx.y;
+  const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
+  const int n_q = (it.seg_len + BQ - 1) / BQ;
+  const float scale_log2 = scale * kLog2e;
+  auto B = [&](int i) { return smem_u32(bars + i); };
+  auto slot_full = [&](int s) { return B(1 + s); };
+  auto slot_empty = [&](int s) { return B(4 + s); };
+  auto s_full = [&](int b) { return B(7 + b); };
+  auto ds_ready = [&](int b) { return B(9 + b); };
+  auto pv_done = [&](int b) { return B(11 + b); };
+  auto dq_full = [&](int b) { return B(13 + b); };
+  auto dq_drained = [&](int b) { return B(15 + b); };
+  auto dsm_free = [&](int b) { return B(17 + b); };
+
+  if (threadIdx.x == 0) {
+    s_abort = 0;
+    for (int i = 0; i < 20; ++i) {
+      const bool four = (i == 9 || i == 10 || i == 15 || i == 16);  // arrivals of 4 warps
+      mbar_init(B(i), four ? 4 : 1);
+    }
+    fence_barrier_init();
+  }
+  if (warp == 1) {
+    tmem_alloc(smem_u32(tmem_slot), 512);
+    tmem_relinquish();
+  }
+  tc_fence_before();
+  __syncthreads();
+  tc_fence_after();
+  const uint32_t tmem = *tmem_slot;
+  auto T_S = [&](int b) { return tmem + b * 128; };
+  auto T_DP = [&](int b) { return tmem + b * 128 + 64; };
+  const uint32_t T_DV = tmem + 256, T_DK = tmem + 384;
+  const int col = h * D;
+
+  if (warp == 0) {
+    if (lane == 0) {
+      const int r0 = it.seg_start + it.tile_start;
+      mbar_expect_tx(B(0), 2 * TILE_BYTES);
+      tma_load_2d(smem_u32(sK), &kmap, B(0), col, r0);
+      tma_load_2d(smem_u32(sK) + HALF_BYTES, &kmap, B(0), col + 64, r0);
+      tma_load_2d(smem_u32(sV), &vmap, B(0), col, r0);
+      tma_load_2d(smem_u32(sV) + HALF_BYTES, &vmap, B(0), col + 64, r0);
+      for (int j = 0; j < n_q && !s_abort; ++j) {
+        const int sl = j % PB_SLOTS;
+        const int row = it.seg_start + j * BQ;
+        if (!mbar_wait(slot_empty(sl), ((j / PB_SLOTS) & 1) ^ 1, 61)) { s_abort = 1; break; }
+        mbar_expect_tx(slot_full(sl), 2 * SUB_BYTES);
+        const uint32_t q = smem_u32(sQ + sl * SUB_BYTES), o = smem_u32(sdO + sl * SUB_BYTES);
+        tma_load_2d(q, &qmap, slot_full(sl), col, row);
+        tma_load_2d(q + SUB_HALF, &qmap, slot_full(sl), col + 64, row);
+        tma_load_2d(o, &domap, slot_full(sl), col, row);
+        tma_load_2d(o + SUB_HALF, &domap, slot_full(sl), col + 64, row);
+      }
+    }
+  } else if (warp == 1) {
+    if (lane == 0) {
+      const uint32_t id_kk = idesc_bf16_f32(128, BQ, 0, 0);   // S^T, dP^T: K-major over D
+      const uint32_t id_tm = idesc_bf16_f32(128, 128, 0, 1);  // dV, dK: A from TMEM, B MN-major
+      const uint32_t id_mm = idesc_bf16_f32(128, BQ, 1, 1);   // dQ^T: A = K^T, B = dS^T, both MN-major
+      const uint32_t k = smem_u32(sK), v = smem_u32(sV);
+      bool ok = mbar_wait(B(0), 0, 62);
+      int ns = 0, ng = 0;  // next sub-tile for S^T / dP^T, next for the gradients
+      uint64_t t_last = global_timer_ns();
+      while (ok && ng < n_q) {
+        bool progress = false;
+        if (ns < n_q && ns - ng < 2) {
+          const int b = ns & 1, sl = ns % PB_SLOTS;
+          if ((ns < 2 || mbar_try_wait(dq_drained(b), ((ns - 2) >> 1) & 1)) &&
+              mbar_try_wait(slot_full(sl), (ns / PB_SLOTS) & 1)) {
+            tc_fence_after();
+            const uint32_t q = smem_u32(sQ + sl * SUB_BYTES), o = smem_u32(sdO + sl * SUB_BYTES);
+#pragma unroll
+            for (int kk = 0; kk < D / 16; ++kk)
+              mma_bf16_ss(T_S(b), desc_kmajor(k, kk), desc_kmajor64(q, kk), id_kk, kk > 0);
+#pragma unroll
+            for (int kk = 0; kk < D / 16; ++kk)
+              mma_bf16_ss(T_DP(b), desc_kmajor(v, kk), desc_kmajor64(o, kk), id_kk, kk > 0);
+            mma_commit(s_full(b));
+            ++ns;
+            progress = true;
+          }
+        }
+        if (!progress && ng < ns && mbar_try_wait(ds_ready(ng & 1), (ng >> 1) & 1)) {
+          const int b = ng & 1, sl = ng % PB_SLOTS;
+          tc_fence_after();
+          const uint32_t q = smem_u32(sQ + sl * SUB_BYTES), o = smem_u32(sdO + sl * SUB_BYTES);
+          // dV += P^T dO ; dK += dS^T Q  (K = 64 queries)
+#pragma unroll
+          for (int kk = 0; kk < BQ / 16; ++kk)
+            mma_bf16_ts(T_DV, T_S(b) + kk * 8, desc_mnmajor64(o, kk), id_tm, (ng > 0) || (kk > 0));
+#pragma unroll
+          for (int kk = 0; kk < BQ / 16; ++kk)
+            mma_bf16_ts(T_DK, T_DP(b) + kk * 8, desc_mnmajor64(q, kk), id_tm, (ng > 0) || (kk > 0));
+          mma_commit(slot_empty(sl));
+          mma_commit(pv_done(b));
+          // dQ^T overwrites the columns P^T is read from: wait until dV has consumed them
+          if (!(ok = mbar_wait(pv_done(b), (ng >> 1) & 1, 63))) break;
+          tc_fence_after();
+          const uint32_t ds = smem_u32(sdS + b * PB_DS);
+#pragma unroll
+          for (int kk = 0; kk < BT / 16; ++kk)
+            mma_bf16_ss(T_S(b), desc_mnmajor(k, kk), smem_desc_sw128(ds + kk * 2048, SUB_HALF, 1024), id_mm, kk > 0);
+          mma_commit(dq_full(b));
+          mma_commit(dsm_free(b));
+          ++ng;
+          progress = true;
+        }
+        if (progress) {
+          t_last = global_timer_ns();
+        } else if (global_timer_ns() - t_last > 4000000000ull) {
+          atomicCAS(&g_error_flag, 0, 64);
+          ok = false;
+        }
+      }
+      mma_commit(B(19));
+      if (!ok) s_abort = 1;
+    }
+  } else if (warp < 6) {
+    // ------------------------------------------------ E warps: P^T and dS^T (lane = key row)
+    const int quarter = warp & 3;
+    const int row = quarter * 32 + lane;
+    const uint32_t lane_off = (uint32_t)(quarter * 32) << 16;
+    const bool row_valid = it.tile_start + row < it.seg_len;
+    const int tid = threadIdx.x - 64;
+    bool ok = true;
+    for (int i = 0; i < n_q; ++i) {
+      const int b = i & 1;
+      const int valid_q = min(BQ, it.seg_len - i * BQ);
+      asm volatile("bar.sync 1, 128;" ::: "memory");
+      if (tid < BQ) {
+        const int qi = i * BQ + tid;
+        s_vec[0][tid] = qi < it.seg_len ? lse[(size_t)h * L + it.seg_start + qi] * kLog2e : 0.f;
+        s_vec[1][tid] = qi < it.seg_len ? delta[(size_t)h * L + it.seg_start + qi] : 0.f;
+      }
+      asm volatile("bar.sync 1, 128;" ::: "memory");
+      if (!(ok = mbar_wait(s_full(b), (i >> 1) & 1, 65))) break;
+      if (i >= 2 && !(ok = mbar_wait(dsm_free(b), ((i - 2) >> 1) & 1, 66))) break;  // dQ^T(i-2) read sdS[b]
+      tc_fence_after();
+      uint8_t* dsb = sdS + b * PB_DS;
+#pragma unroll
+      for (int c = 0; c < 2; ++c) {
+        uint32_t r[32], y[32];
+        tmem_ld32(T_S(b) + lane_off + c * 32, r);
+        tmem_ld32(T_DP(b) + lane_off + c * 32, y);
+        tmem_ld_wait();
+        uint32_t wp[16], wd[16];
+#pragma unroll
+        for (int j = 0; j < 32; j += 2) {
+          float pv[2], dsv[2];
+#pragma unroll
+          for (int e = 0; e < 2; ++e) {
+            const int cc = c * 32 + j + e;
+            const bool on = cc < valid_q && row_valid;
+            const float p = on ? fast_exp2(__uint_as_float(r[j + e]) * scale_log2 - s_vec[0][cc]) : 0.f;
+            pv[e] = p;
+            dsv[e] = p * (__uint_as_float(y[j + e]) - s_vec[1][cc]);
+          }
+          wp[j >> 1] = pack_bf16(pv[0], pv[1]);
+          wd[j >> 1] = pack_bf16(dsv[0], dsv[1]);
+        }
+        // packed columns [16c, 16c + 16) lie in score columns already read
+        tmem_st16(T_S(b) + lane_off + c * 16, wp);
+        tmem_st16(T_DP(b) + lane_off + c * 16, wd);
+        store_row32_swizzled(dsb, row, c * 32, wd);
+      }
+      tmem_st_wait();
+      fence_async_smem();
+      tc_fence_before();
+      __syncwarp();
+      if (lane == 0) mbar_arrive(ds_ready(b));
+    }
+    // dV, dK rows of this key tile
+    if (ok && n_q > 0 && mbar_wait(B(19), 0, 67)) {
+      tc_fence_after();
+      const int g = it.seg_start + it.tile_start + row;
+      const size_t grow = (size_t)g * H + h;
+      for (int which = 0; which < 2; ++which) {
+        const uint32_t tacc = (which == 0 ? T_DK : T_DV) + lane_off;
+        const float mul = which == 0 ? scale : 1.f;
+        const PeerRows& pr = which == 0 ? dk_peer : dv_peer;
+        __nv_bfloat16* dst = pr.base ? (row_valid ? peer_row(pr, g, h) : nullptr)
+                                     : (which == 0 ? dk_out : dv_out) + grow * D;
+#pragma unroll
+        for (int c = 0; c < 4; ++c) {
+          uint32_t r[32];
+          tmem_ld32(tacc + c * 32, r);
+          tmem_ld_wait();
+          if (row_valid) {
+#pragma unroll
+            for (int vv = 0; vv < 4; ++vv) {
+              float o[8];
+#pragma unroll
+              for (int e = 0; e < 8; ++e) o[e] = __uint_as_float(r[vv * 8 + e]) * mul;
+              store8(dst + c * 32 + vv * 8, o);
+            }
+          }
+        }
+      }
+    } else {
+      s_abort = 1;
+    }
+  } else {
+    // ------------------------------------------------ Q warps: dQ^T -> fp32 reduce-add (lane = d)
+    const int quarter = warp & 3;
+    const int d = quarter * 32 + lane;
+    const uint32_t lane_off = (uint32_t)(quarter * 32) << 16;
+    const int qt = threadIdx.x - 192;  // 0..127
+    int n_used = 0;
+    for (int i = 0; i < n_q; ++i) {
+      const int b = i & 1;
+      if (!mbar_wait(dq_full(b), (i >> 1) & 1, 68)) { s_abort = 1; break; }
+      tc_fence_after();
+      uint32_t r[2][32];
+#pragma unroll
+      for (int c = 0; c < 2; ++c) tmem_ld32(T_S(b) + lane_off + c * 32, r[c]);
+      tmem_ld_wait();
+      tc_fence_before();
+      __syncwarp();
+      if (lane == 0) mbar_arrive(dq_drained(b));  // buffer b may be reused
+#pragma unroll
+      for (int c = 0; c < 2; ++c) {
+        float* st = reinterpret_cast<float*>(sStage + (n_used & 1) * PB_STAGE);
+        if (n_used >= 2 && qt == 0) bulk_wait_read<1>();
+        asm volatile("bar.sync 2, 128;" ::: "memory");
+#pragma unroll
+        for (int qq = 0; qq < 32; ++qq) st[qq * D + d] = __uint_as_float(r[c][qq]);
+        fence_async_shared();
+        asm volatile("bar.sync 2, 128;" ::: "memory");
+        if (qt == 0) {
+          tma_reduce_add_2d(&dqmap, smem_u32(st), col, it.seg_start + i * BQ + c * 32);
+          bulk_commit();
+        }
+        ++n_used;
+      }
+    }
+    if (qt == 0) bulk_wait_all();
+  }
+  tc_fence_before();
+  __syncthreads();
+  if (warp == 1) {
+    tc_fence_after();
+    tmem_dealloc(tmem, 512);
+  }
+}
+
 // dq = scale * dq_acc (fp32 -> bf16), 8 elements per thread
 // With `dq_peer` on, element (row g, head h, d) goes to its token owner instead (the reverse
 // all-to-all of dQ) and rows at or beyond n_valid are skipped (the owners zero their padding).
@@ -1052,12 +1348,50 @@ const char* make_dq_map(CUtensorMap* m, const float* base, int L, int H) {
   return r == CUDA_SUCCESS ? nullptr : "cuTensorMapEncodeTiled failed (dq accumulator)";
 }
 
-int g_bwd_variant = 1;  // 1: fused single pass; 0: two passes
+// Key-tile-outer backward (fused or pipelined, per g_bwd_variant) into dq_acc / dk / dv.
+int g_bwd_variant = 1;  // 2: pipelined single pass; 1: fused single pass; 0: two passes
+
+const char* run_bwd_single_pass(const void* q, const void* k, const void* v, const void* dout, const float* lse,
+                                const float* delta, const int* items_kv, int n_items_kv, int L, int H, float scale,
+                                float* dq_acc, __nv_bfloat16* dk, __nv_bfloat16* dv, const PeerRows& dk_peer,
+                                const PeerRows& dv_peer, cudaStream_t s) {
+  const bool pipe = g_bwd_variant == 2;
+  const int qrows = pipe ? BQ : BT;
+  CUtensorMap qm, km, vm, dom, dqm;
+  const char* e;
+  if ((e = make_qkv_map(&qm, q, L, H, qrows)) || (e = make_qkv_map(&km, k, L, H)) || (e = make_qkv_map(&vm, v, L, H)) ||
+      (e = make_qkv_map(&dom, dout, L, H, qrows)) || (e = make_dq_map(&dqm, dq_acc, L, H)))
+    return e;
+  static bool attr_f = false, attr_p = false;
+  if (!pipe && !attr_f) {
+    if (cudaFuncSetAttribute(attn_bwd_fused_kernel, cudaFuncAttributeMaxDynamicSharedMemorySize, FB_SMEM) !=
+        cudaSuccess)
+      return "attention: cannot set smem size (fused backward)";
+    attr_f = true;
+  }
+  if (pipe && !attr_p) {
+    if (cudaFuncSetAttribute(attn_bwd_pipe_kernel, cudaFuncAttributeMaxDynamicSharedMemorySize, PB_SMEM) !=
+        cudaSuccess)
+      return "attention: cannot set smem size (pipelined backward)";
+    attr_p = true;
+  }
+  if (cudaMemsetAsync(dq_acc, 0, (size_t)L * H * D * sizeof(float), s) != cudaSuccess) return "dq memset failed";
+  if (n_items_kv > 0) {
+    const WorkItem* it = reinterpret_cast<const WorkItem*>(items_kv);
+    if (pipe)
+      attn_bwd_pipe_kernel<<<dim3(n_items_kv, H), FB_THREADS, PB_SMEM, s>>>(qm, km, vm, dom, dqm, it, L, H, scale, lse,
+                                                                           delta, dk, dv, dk_peer, dv_peer);
+    else
+      attn_bwd_fused_kernel<<<dim3(n_items_kv, H), FB_THREADS, FB_SMEM, s>>>(qm, km, vm, dom, dqm, it, L, H, scale, lse,
+                                                                            delta, dk, dv, dk_peer, dv_peer);
+  }
+  return cudaGetLastError() == cudaSuccess ? nullptr : "attention single-pass backward launch failed";
+}
 int g_fwd_variant = 3;  // forward softmax: bit 0 two score chunks per TMEM wait, bit 1 packed fp32x2 math
 
 }  // namespace attn
 
-void attn_set_backward_variant(int v) { attn::g_bwd_variant = v ? 1 : 0; }
+void attn_set_backward_variant(int v) { attn::g_bwd_variant = v < 0 ? 0 : (v > 2 ? 2 : v); }
 void attn_set_forward_variant(int v) { attn::g_fwd_variant = v & 3; }
 
 const char* launch_attn_fwd(const void* q, const void* k, const void* v, const int* items, int n_items, int L, int H,
@@ -1103,21 +1437,11 @@ const char* launch_attn_bwd(const void* q, const void* k, const void* v, const v
   if ((e = make_qkv_map(&qm, q, L, H)) || (e = make_qkv_map(&km, k, L, H)) || (e = make_qkv_map(&vm, v, L, H)) ||
       (e = make_qkv_map(&dom, dout, L, H)))
     return e;
-  if (g_bwd_variant == 1 && dq_acc != nullptr) {
-    static bool fattr = false;
-    if (!fattr) {
-      if (cudaFuncSetAttribute(attn_bwd_fused_kernel, cudaFuncAttributeMaxDynamicSharedMemorySize, FB_SMEM) !=
-          cudaSuccess)
-        return "attention: cannot set smem size (fused backward)";
-      fattr = true;
-    }
-    CUtensorMap dqm;
-    if ((e = make_dq_map(&dqm, dq_acc, L, H))) return e;
-    if (cudaMemsetAsync(dq_acc, 0, (size_t)L * H * D * sizeof(float), s) != cudaSuccess) return "dq memset failed";
-    if (n_items_kv > 0)
-      attn_bwd_fused_kernel<<<dim3(n_items_kv, H), FB_THREADS, FB_SMEM, s>>>(
-          qm, km, vm, dom, dqm, reinterpret_cast<const WorkItem*>(items_kv), L, H, scale, lse, delta,
-          (__nv_bfloat16*)dk, (__nv_bfloat16*)dv, PeerRows{nullptr, 1, 0, H}, PeerRows{nullptr, 1, 0, H});
+  if (g_bwd_variant >= 1 && dq_acc != nullptr) {
+    if ((e = run_bwd_single_pass(q, k, v, dout, lse, delta, items_kv, n_items_kv, L, H, scale, dq_acc,
+                                 (__nv_bfloat16*)dk, (__nv_bfloat16*)dv, PeerRows{nullptr, 1, 0, H},
+                                 PeerRows{nullptr, 1, 0, H}, s)))
+      return e;
     const size_t n8 = (size_t)L * H * D / 8;
     attn_dq_convert_kernel<<<(unsigned)((n8 + 255) / 256), 256, 0, s>>>(dq_acc, n8, scale, (__nv_bfloat16*)dq,
                                                                          PeerRows{nullptr, 1, 0, H}, H, L);
@@ -1170,23 +1494,10 @@ const char* launch_attn_bwd_cp(const void* q, const void* k, const void* v, cons
   const int warps = L * H;
   attn_bwd_gather_delta_kernel<<<(warps * 32 + 255) / 256, 256, 0, s>>>((const __nv_bfloat16*)o, dsrc, L, H, n_valid,
                                                                         (__nv_bfloat16*)dout_head, delta);
-  CUtensorMap qm, km, vm, dom, dqm;
-  const char* e;
-  if ((e = make_qkv_map(&qm, q, L, H)) || (e = make_qkv_map(&km, k, L, H)) || (e = make_qkv_map(&vm, v, L, H)) ||
-      (e = make_qkv_map(&dom, dout_head, L, H)) || (e = make_dq_map(&dqm, dq_acc, L, H)))
-    return e;
-  static bool fattr = false;
-  if (!fattr) {
-    if (cudaFuncSetAttribute(attn_bwd_fused_kernel, cudaFuncAttributeMaxDynamicSharedMemorySize, FB_SMEM) !=
-        cudaSuccess)
-      return "attention: cannot set smem size (fused backward)";
-    fattr = true;
-  }
-  if (cudaMemsetAsync(dq_acc, 0, (size_t)L * H * D * sizeof(float), s) != cudaSuccess) return "dq memset failed";
-  if (n_items_kv > 0)
-    attn_bwd_fused_kernel<<<dim3(n_items_kv, H), FB_THREADS, FB_SMEM, s>>>(
-        qm, km, vm, dom, dqm, reinterpret_cast<const WorkItem*>(items_kv), L, H, scale, lse, delta, nullptr, nullptr,
-        PeerRows{dk_peer, cp, head_base, H_total}, PeerRows{dv_peer, cp, head_base, H_total});
+  const char* e = run_bwd_single_pass(q, k, v, dout_head, lse, delta, items_kv, n_items_kv, L, H, scale, dq_acc,
+                                      nullptr, nullptr, PeerRows{dk_peer, cp, head_base, H_total},
+                                      PeerRows{dv_peer, cp, head_base, H_total}, s);
+  if (e) return e;
   const size_t n8 = (size_t)L * H * D / 8;
   attn_dq_convert_kernel<<<(unsigned)((n8 + 255) / 256), 256, 0, s>>>(dq_acc, n8, scale, nullptr,
                                                                        PeerRows{dq_peer, cp, head_base, H_total}, H,

@@ -21,7 +21,7 @@ def ref_attention(q, k, v, lens, scale):
     return out, lse
 
 
-@pytest.fixture(params=[1, 0], ids=["fused_bwd", "two_pass_bwd"])
+@pytest.fixture(params=[1, 2, 0], ids=["fused_bwd", "pipelined_bwd", "two_pass_bwd"])
 def bwd_variant(request):
     from pan2_b200.ops._ext import ext
     ext().attn_set_backward_variant(request.param)
