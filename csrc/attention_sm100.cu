@@ -824,15 +824,23 @@ attn_bwd_fused_kernel(const __grid_constant__ CUtensorMap qmap, const __grid_con
     const bool row_valid = it.tile_start + row < it.seg_len;
     const int tid = threadIdx.x - 64;
     bool ok = true;
+    // LSE / Delta of query tile i are loaded from global memory one tile ahead (registers), so their
+    // latency overlaps the previous tile's work instead of stalling every tile
+    auto fetch = [&](int i, float& lv, float& dv) {
+      const int qi = i * BT + tid;
+      const bool in = i < n_q && qi < it.seg_len;
+      lv = in ? lse[(size_t)h * L + it.seg_start + qi] * kLog2e : 0.f;
+      dv = in ? delta[(size_t)h * L + it.seg_start + qi] : 0.f;
+    };
+    float next_l, next_d;
+    fetch(0, next_l, next_d);
     for (int i = 0; i < n_q; ++i) {
       const int valid_q = min(BT, it.seg_len - i * BT);
       asm volatile("bar.sync 1, 128;" ::: "memory");
-      if (tid < BT) {
-        const int qi = i * BT + tid;
-        s_vec[0][tid] = qi < it.seg_len ? lse[(size_t)h * L + it.seg_start + qi] * kLog2e : 0.f;
-        s_vec[1][tid] = qi < it.seg_len ? delta[(size_t)h * L + it.seg_start + qi] : 0.f;
-      }
+      s_vec[0][tid] = next_l;
+      s_vec[1][tid] = next_d;
       asm volatile("bar.sync 1, 128;" ::: "memory");
+      fetch(i + 1, next_l, next_d);
       if (!(ok = mbar_wait(B(7), i & 1, 49))) break;
       if (i > 0 && !(ok = mbar_wait(B(9), (i - 1) & 1, 50))) break;  // dQ^T(i-1) has read dS^T smem
       tc_fence_after();
@@ -1117,16 +1125,24 @@ attn_bwd_pipe_kernel(const __grid_constant__ CUtensorMap qmap, const __grid_cons
     const bool row_valid = it.tile_start + row < it.seg_len;
     const int tid = threadIdx.x - 64;
     bool ok = true;
+    auto fetch = [&](int i, float& lv, float& dv) {  // one sub-tile ahead, as in the fused kernel
+      const int qi = i * BQ + tid;
+      const bool in = tid < BQ && i < n_q && qi < it.seg_len;
+      lv = in ? lse[(size_t)h * L + it.seg_start + qi] * kLog2e : 0.f;
+      dv = in ? delta[(size_t)h * L + it.seg_start + qi] : 0.f;
+    };
+    float next_l, next_d;
+    fetch(0, next_l, next_d);
     for (int i = 0; i < n_q; ++i) {
       const int b = i & 1;
       const int valid_q = min(BQ, it.seg_len - i * BQ);
       asm volatile("bar.sync 1, 128;" ::: "memory");
       if (tid < BQ) {
-        const int qi = i * BQ + tid;
-        s_vec[0][tid] = qi < it.seg_len ? lse[(size_t)h * L + it.seg_start + qi] * kLog2e : 0.f;
-        s_vec[1][tid] = qi < it.seg_len ? delta[(size_t)h * L + it.seg_start + qi] : 0.f;
+        s_vec[0][tid] = next_l;
+        s_vec[1][tid] = next_d;
       }
       asm volatile("bar.sync 1, 128;" ::: "memory");
+      fetch(i + 1, next_l, next_d);
       if (!(ok = mbar_wait(s_full(b), (i >> 1) & 1, 65))) break;
       if (i >= 2 && !(ok = mbar_wait(dsm_free(b), ((i - 2) >> 1) & 1, 66))) break;  // dQ^T(i-2) read sdS[b]
       tc_fence_after();

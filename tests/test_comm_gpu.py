@@ -81,6 +81,11 @@ def _barrier_timeout(rank, world, port, path):
     dist.destroy_process_group()
 
 
+def gpu_world() -> int:
+    """Ranks for the multi-GPU tests: 2, or ``PAN_TEST_WORLD`` (capped by the visible GPUs)."""
+    return max(2, min(torch.cuda.device_count(), int(os.environ.get("PAN_TEST_WORLD", "2"))))
+
+
 def _spawn(fn, world, path):
     ctx = mp.get_context("spawn")
     port = _port()
@@ -95,7 +100,7 @@ def _spawn(fn, world, path):
 
 @pytest.mark.skipif(torch.cuda.device_count() < 2, reason="needs two GPUs of one node")
 def test_peer_memory_engine_matches_nccl(tmp_path):
-    r = _spawn(_engine_step, 2, str(tmp_path / "r.pt"))
+    r = _spawn(_engine_step, gpu_world(), str(tmp_path / "r.pt"))
     a, b = r["0"], r["1"]
     assert a["err"] == 0 and b["err"] == 0
     assert abs(a["loss"] - b["loss"]) < 1e-6 * abs(a["loss"]) + 1e-7

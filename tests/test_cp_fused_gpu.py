@@ -5,7 +5,7 @@ import os
 import pytest
 import torch
 
-from test_comm_gpu import _spawn
+from test_comm_gpu import _spawn, gpu_world
 
 pytestmark = pytest.mark.gpu
 
@@ -54,7 +54,7 @@ def _cp_step(rank, world, port, path):
 
 @pytest.mark.skipif(torch.cuda.device_count() < 2, reason="needs two GPUs of one node")
 def test_fused_ulysses_matches_nccl_all_to_all(tmp_path):
-    r = _spawn(_cp_step, 2, str(tmp_path / "cp.pt"))
+    r = _spawn(_cp_step, gpu_world(), str(tmp_path / "cp.pt"))
     a, b = r["0"], r["1"]
     assert a["err"] == 0 and b["err"] == 0
     assert abs(a["loss"] - b["loss"]) < 1e-6 * abs(a["loss"]) + 1e-7, (a["loss"], b["loss"])
