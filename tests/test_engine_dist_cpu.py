@@ -1,4 +1,4 @@
-"""Sharded engine across 2 gloo ranks == the same engine on 1 rank (CPU).
+"""Sharded engine across 2 or 4 gloo ranks == the same engine on 1 rank (CPU).
 
 Both ranks train on the same batch, so the global mean loss and its gradient equal the single-rank
 ones; after one optimizer step (AdamW for 1-D/modulation tensors, Muon with local chunked NS for QKV
@@ -65,9 +65,10 @@ def _run(world):
 
 
 @pytest.mark.timeout(900)
-def test_two_rank_step_matches_one_rank():
+@pytest.mark.parametrize("world", [2, 4])
+def test_multi_rank_step_matches_one_rank(world):
     loss1, norm1, sd1 = _run(1)
-    loss2, norm2, sd2 = _run(2)
+    loss2, norm2, sd2 = _run(world)
     assert abs(loss1 - loss2) < 1e-5 * abs(loss1) + 1e-6, (loss1, loss2)
     assert abs(norm1[0] - norm2[0]) < 1e-3 * norm1[0], (norm1, norm2)
     worst = (0.0, "")

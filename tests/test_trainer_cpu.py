@@ -96,6 +96,57 @@ def test_injected_exception_surfaces(data_dir, tmp_path):
         _train(cfg)
 
 
+@pytest.mark.timeout(900)
+def test_corrupt_latest_checkpoint_falls_back(data_dir, tmp_path):
+    _train(_cfg(data_dir, tmp_path / "f", max_steps=4, save_interval=2))
+    tdir = tmp_path / "f" / "checkpoint-4" / "transformer"
+    shards = [f for f in os.listdir(tdir) if f.endswith(".safetensors")]
+    assert shards
+    for f in shards:
+        with open(tdir / f, "wb") as fh:
+            fh.write(b"not a safetensors file")
+    tr, rest = _train(_cfg(data_dir, tmp_path / "f", max_steps=5, save_interval=100))
+    assert [h["step"] for h in rest] == [2, 3, 4]  # resumed from checkpoint-2
+
+
+def _dead_peer(rank, port, path):
+    from pan2_b200.parallel.layout import init_parallel_layout
+    os.environ.update(MASTER_ADDR="127.0.0.1", MASTER_PORT=str(port), RANK=str(rank), WORLD_SIZE="2")
+    init_parallel_layout(cp=1, backend="gloo", timeout_s=5)
+    t = torch.ones(4)
+    dist.all_reduce(t)  # both ranks alive
+    if rank == 1:
+        os._exit(0)  # leaves between steps, with nothing in flight
+    t0 = time.time()
+    err = None
+    try:
+        dist.all_reduce(t)  # the peer never joins
+    except Exception as e:  # noqa: BLE001 - the collective must fail, whatever the error type
+        err = type(e).__name__
+    with open(path, "w") as f:
+        json.dump(dict(err=err, waited=time.time() - t0), f)
+    os._exit(0)
+
+
+@pytest.mark.timeout(300)
+def test_lost_rank_ends_next_collective_with_error(tmp_path):
+    s = socket.socket()
+    s.bind(("127.0.0.1", 0))
+    port = s.getsockname()[1]
+    s.close()
+    path = str(tmp_path / "dead.json")
+    ctx = mp.get_context("spawn")
+    ps = [ctx.Process(target=_dead_peer, args=(r, port, path)) for r in range(2)]
+    for p in ps:
+        p.start()
+    for p in ps:
+        p.join(timeout=120)
+    with open(path) as f:
+        r = json.load(f)
+    assert r["err"] is not None, r
+    assert r["waited"] < 60, r
+
+
 def test_heartbeat_fires_when_stuck():
     fired = []
     hb = Heartbeat(rank=0, threshold_s=0.2, poll_s=0.05, on_stuck=fired.append).start()
