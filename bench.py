@@ -31,6 +31,10 @@ ROOT = os.path.dirname(os.path.abspath(__file__))
 sys.path.insert(0, ROOT)
 
 METRIC = "29B MMDiT 720p train latent tokens/s (1/2/4/8 B200, max over ranks); s/video @50 steps"
+WORKLOAD_METRICS = {
+    "longctx": "29B MMDiT long-context (one 121-frame 720p clip, Ulysses CP) train latent tokens/s",
+    "sft": "29B MMDiT SFT mixed image+video packing (CP=2) train latent tokens/s",
+}
 
 
 def parse():
@@ -44,6 +48,11 @@ def parse():
     ap.add_argument("--clips", type=int, default=5)
     ap.add_argument("--frames", type=int, default=21)
     ap.add_argument("--offload", default="auto")
+    ap.add_argument("--workload", default="pretrain", choices=("pretrain", "longctx", "sft"),
+                    help="pretrain: the headline (5 x 5 s clips per GPU, FSDP); longctx: one 121-frame 720p "
+                         "clip (~107k tokens) with Ulysses CP over all ranks; sft: mixed images + videos of "
+                         "random lengths filling the SFT budget, CP=2")
+    ap.add_argument("--cp", type=int, default=None, help="context-parallel size (longctx: all ranks, sft: 2)")
     return ap.parse_args()
 
 
@@ -63,7 +72,8 @@ def main():
     import torch
     import torch.distributed as dist
     import yaml
-    from pan2_b200.data.synthetic import synthetic_packed_batch, batch_to_device, batch_bytes
+    from pan2_b200.data.synthetic import (batch_bytes, batch_to_device, pin_batch, sft_mix_items,
+                                          synthetic_items_batch, synthetic_packed_batch)
     from pan2_b200.models.transformer import translate_architecture_config
     from pan2_b200.ops._ext import start_launch_count, stop_launch_count, ext
     from pan2_b200.training.engine import TrainEngine, OptimConfig
@@ -77,7 +87,20 @@ def main():
     torch.cuda.set_device(local)
     device = torch.device("cuda", local)
     group = None
-    if world > 1:
+    if args.workload == "longctx":
+        cp = args.cp or world
+    elif args.workload == "sft":
+        cp = args.cp or (2 if world % 2 == 0 else 1)
+    else:
+        cp = 1
+    if world % cp:
+        raise SystemExit(f"--cp {cp} does not divide {world} ranks")
+    layout = None
+    if world > 1 and cp > 1:
+        from pan2_b200.parallel.layout import init_parallel_layout
+        layout = init_parallel_layout(cp=cp, backend="cpu:gloo,cuda:nccl", timeout_s=900)
+        group = layout.shard_group
+    elif world > 1:
         import datetime
         dist.init_process_group("nccl", timeout=datetime.timedelta(seconds=900), device_id=device)
         group = dist.group.WORLD
@@ -95,19 +118,38 @@ def main():
                         use_muon=bool(tr.get("use_muon", True)), max_grad_norm=float(tr["max_grad_norm"]))
 
     # 704x1280 frames -> 44x80 latents; 21 latent frames per 5 s clip; 512 text tokens per clip
-    batch = synthetic_packed_batch(args.clips, (args.frames, 44, 80), 512, seed=1234 + rank, pin=True,
-                                   rope_axes=tuple(arch["rope_axes_dim"]), rope_theta=float(arch["rope_theta"]),
-                                   rope_scale=(float(arch["rope_temporal_scale"]), 1.0, 1.0))
+    rope = dict(rope_axes=tuple(arch["rope_axes_dim"]), rope_theta=float(arch["rope_theta"]),
+                rope_scale=(float(arch["rope_temporal_scale"]), 1.0, 1.0))
+    dp_rank = rank // cp
+    data = cfg["data"]
+    if args.workload == "pretrain":
+        batch = synthetic_packed_batch(args.clips, (args.frames, 44, 80), 512, seed=1234 + rank, pin=True, **rope)
+    else:
+        if args.workload == "longctx":  # 121 latent frames (~20 s) of 704x1280 in one sequence
+            items = [((121, 44, 80), True)]
+        else:
+            items = sft_mix_items(int(data["packed_video_token_budget"]), int(data["packed_joint_token_budget"]),
+                                  int(data["packed_dataloader_max_num_seq"]), 512, seed=1234 + dp_rank)
+        batch = synthetic_items_batch(items, [512] * len(items), seed=1234 + dp_rank, **rope)
     meta = batch["packed_seq_params"]
-    assert meta.n_active <= int(cfg["data"]["packed_joint_token_budget"])
-    latent_tokens = meta.n_video
+    assert meta.n_active <= int(data["packed_joint_token_budget"])
+    latent_tokens = meta.n_video  # per cp group
 
     t0 = time.time()
     # activation reserve: with one rank the block checkpoints live in idle gradient buffers
     reserve_gb = float(os.environ.get("PAN_ACT_RESERVE_GB", "40" if world == 1 else "72"))
     engine = TrainEngine(arch, device, group=group, seed=42, optim=optim, offload=args.offload,
                          activation_bytes_estimate=int(reserve_gb * 1e9))
-    placed = {}
+    if cp > 1:
+        # every cp rank trains its strided shard of the cp group's sequence
+        from pan2_b200.data.cp_batch import broadcast_and_split
+        engine.set_context_parallel(layout.cp_group, cp, layout.cp_rank)
+        src = batch_to_device(batch, device) if layout.cp_rank == 0 else None
+        local, _ = broadcast_and_split(src, None, layout, device)
+        torch.cuda.synchronize()
+        batch = pin_batch({k: (v.cpu() if isinstance(v, torch.Tensor) else v) for k, v in local.items()})
+    elif args.workload != "pretrain":
+        batch = pin_batch(batch)
     init_s = time.time() - t0
     runner = StepRunner(engine, lr_lambda=lr_lambda_from_config(tr))
 
@@ -144,12 +186,12 @@ def main():
     total_ms, compute_ms = t.tolist()
     ms_step = compute_ms / args.steps
     e2e_ms = total_ms / args.steps
-    tokens_global = latent_tokens * world
+    tokens_global = latent_tokens * (world // cp)
     err = ext().error_flag(True)
     if rank == 0:
         h2d = batch_bytes(batch)
         out = {
-            "metric": METRIC,
+            "metric": WORKLOAD_METRICS.get(args.workload, METRIC),
             "value": tokens_global / (ms_step / 1e3),
             "unit": "latent tokens/s",
             "n_gpus": world,
@@ -157,17 +199,18 @@ def main():
             "warmup": args.warmup,
             "ms_per_step": ms_step,
             "higher_is_better": True,
-            "scaling": "weak",
+            "scaling": "strong" if args.workload == "longctx" else "weak",
             "vs_baseline": None,
             "dtype": "bf16",
             "data": "synthetic (random Wan-2.2-shaped latents, random 4096-d text embeddings, random-init 29B weights)",
             "config": {
                 "model": f"PAN2 MMDiT {engine.total_params / 1e9:.2f}B ({arch['num_layers']} layers)",
-                "global_batch": args.clips * world,
+                "global_batch": (args.clips if args.workload == "pretrain" else meta.num_samples) * (world // cp),
                 "seq_len": meta.joint_packed_length,
-                "latent_tokens_per_gpu": latent_tokens,
-                "joint_tokens_per_gpu": meta.n_active,
-                "parallelism": f"fsdp{world}" + ("+host-offload" if engine.offload else ""),
+                "latent_tokens_per_gpu": latent_tokens * (world // cp) // world,
+                "joint_tokens_per_gpu": meta.n_active * (world // cp) // world,
+                "parallelism": f"fsdp{world}" + (f"+cp{cp}" if cp > 1 else "") + ("+host-offload" if engine.offload else ""),
+                "workload": args.workload,
                 "optimizer": "Muon+AdamW, clip 1.0",
                 "activation_checkpointing": "every block",
                 "l2": "per-step working set (GBs) larger than L2; no extra flush",

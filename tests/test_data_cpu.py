@@ -106,3 +106,28 @@ def test_loader_assembly_feeds_model(sample_dir):
     model = tiny_model(text_embed_dim=64, hidden_size=128, rope_axes_dim=(8, 12, 12))
     loss = model(**batch)
     assert torch.isfinite(loss) and loss.item() > 0
+
+
+def test_synthetic_workload_batches_fit_their_budgets():
+    from pan2_b200.data.cp_batch import strided_split
+    from pan2_b200.data.synthetic import sft_mix_items, synthetic_items_batch, synthetic_packed_batch
+    items = sft_mix_items(109142, 110576, 8, 512, seed=3)
+    n_video = sum(t * (h // 2) * (w // 2) for (t, h, w), _ in items)
+    assert len(items) <= 8 and n_video <= 109142 and n_video + 512 * len(items) <= 110576
+    assert sum(1 for (t, _, _), _ in items if t == 1) == 4  # single-frame image items
+    small = [((3, 8, 8), True), ((1, 8, 8), False), ((5, 8, 8), False)]
+    b = synthetic_items_batch(small, [16, 8, 12], text_dim=64, rope_axes=(16, 24, 24), seed=5)
+    m = b["packed_seq_params"]
+    assert m.video_lens == [48, 16, 80] and m.caption_lens == [16, 8, 12]
+    assert b["hidden_states"].shape[1] == sum(m.video_lens)
+    # the same generator behind the fixed-shape helper: identical clips for identical seeds
+    a1 = synthetic_packed_batch(2, (3, 8, 8), 8, text_dim=64, rope_axes=(16, 24, 24), seed=9)
+    a2 = synthetic_items_batch([((3, 8, 8), True), ((3, 8, 8), False)], [8, 8], text_dim=64,
+                               rope_axes=(16, 24, 24), seed=9)
+    assert torch.equal(a1["hidden_states"], a2["hidden_states"])
+    # a long single clip splits into strided CP shards that cover every video row once
+    long = synthetic_items_batch([((9, 8, 8), True)], [16], text_dim=64, rope_axes=(16, 24, 24), seed=1)
+    rows = 0
+    for r in range(4):
+        rows += strided_split(long, 4, r)["hidden_states"].shape[1]
+    assert rows == long["hidden_states"].shape[1]
