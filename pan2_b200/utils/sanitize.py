@@ -20,32 +20,38 @@ from typing import Callable, Dict
 import torch
 
 
-def poison_free_memory(byte: int = 0xFF, device=None, headroom: int = 2 << 30,
+def poison_free_memory(byte: int = 0xFF, device=None, headroom: int = 2 << 30, chunk: int = 4 << 30,
                        small_blocks: int = 512) -> int:
     """Fill the caching allocator's free memory on ``device`` with ``byte``; returns bytes filled.
 
-    Large-pool memory is poisoned by allocating one block of (free device memory - ``headroom``),
-    filling it and freeing it back to the cache, so that later allocations are carved from it.  The
-    small pool (requests up to 1 MiB, served from 2 MiB segments) is poisoned with ``small_blocks``
-    1 MiB tensors.
+    Large-pool memory is poisoned by allocating blocks of ``chunk`` bytes (halving the block size
+    when one does not fit) until all but ``headroom`` bytes of the device's free memory are taken,
+    filling them and freeing them back to the cache, so that later allocations are carved from
+    poisoned blocks.  The small pool (requests up to 1 MiB, served from 2 MiB segments) is
+    poisoned with ``small_blocks`` 1 MiB tensors.
     """
     dev = torch.device(device if device is not None else torch.cuda.current_device())
     torch.cuda.synchronize(dev)
     free, _ = torch.cuda.mem_get_info(dev)
-    cached_free = torch.cuda.memory_reserved(dev) - torch.cuda.memory_allocated(dev)
-    nbytes = max(0, free + cached_free - headroom)
-    filled = 0
-    if nbytes > 0:
-        big = torch.empty(nbytes, dtype=torch.uint8, device=dev)
-        big.fill_(byte)
-        filled += nbytes
-        del big
+    remaining = max(0, free - headroom)
+    blocks, filled = [], 0
+    while remaining >= (64 << 20) and chunk >= (64 << 20):
+        size = min(chunk, remaining)
+        try:
+            t = torch.empty(size, dtype=torch.uint8, device=dev)
+        except torch.cuda.OutOfMemoryError:
+            chunk //= 2
+            continue
+        t.fill_(byte)
+        blocks.append(t)
+        filled += size
+        remaining -= size
     smalls = [torch.empty(1 << 20, dtype=torch.uint8, device=dev) for _ in range(small_blocks)]
-    for s in smalls:
-        s.fill_(byte)
+    for t in smalls:
+        t.fill_(byte)
     filled += small_blocks << 20
-    del smalls
     torch.cuda.synchronize(dev)
+    del blocks, smalls
     return filled
 
 
