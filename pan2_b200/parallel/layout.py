@@ -119,6 +119,10 @@ def init_parallel_layout(cp: int = 1, hybrid_shard: bool = False, timeout_s: flo
     return layout
 
 
-def reset_parallel_layout() -> None:
+def reset_parallel_layout(destroy: bool = False) -> None:
+    """Forget the layout; with ``destroy`` also tear down the default process group (and with it
+    every subgroup), e.g. when a process that trained in-process exits cleanly."""
     global _LAYOUT
     _LAYOUT = ParallelLayout()
+    if destroy and dist.is_initialized():
+        dist.destroy_process_group()
