@@ -1,4 +1,4 @@
-"""Headline benchmark: 29B MMDiT 720p training throughput in latent tokens/s.
+"""Headline benchmark: 29B MMDiT 720p training throughput in latent tokens/s (pretraining, FSDP, no CP).
 
     python bench.py [--gpus N] [--steps K] [--warmup W] [--impl ours|reference]
     torchrun --nnodes=1 --nproc-per-node N --master-addr 127.0.0.1 --master-port P bench.py --gpus N ...

@@ -1,4 +1,4 @@
-"""Inference benchmark: seconds per video for 50-step sampling of the 29B MMDiT.
+"""Inference benchmark: seconds per video for 50-step sampling of the 29B MMDiT (720p i2v, CFG, SP).
 
     python bench_inference.py [--gpus N] [--steps 50] [--warmup 3]
     torchrun --nnodes=1 --nproc-per-node N --master-addr 127.0.0.1 --master-port P bench_inference.py --gpus N

@@ -1,4 +1,4 @@
-"""Tiny-model fixtures shared by the tests (BASELINE config 1 shapes)."""
+"""Tiny-model fixtures shared by the tests (2 blocks, hidden 256, two packed 48x5x8x8 videos)."""
 from __future__ import annotations
 
 import torch
