@@ -160,8 +160,8 @@ def main():
         dist.barrier()
     torch.cuda.synchronize()
 
-    sampler = ClockSampler()
-    if local == 0:
+    sampler = ClockSampler()  # sampled by the rank that prints (every GPU of this node is queried)
+    if rank == 0:
         sampler.start()
     start_launch_count()
     ev = [[torch.cuda.Event(enable_timing=True) for _ in range(3)] for _ in range(args.steps)]
@@ -176,7 +176,7 @@ def main():
     if world > 1:
         dist.barrier()
     torch.cuda.synchronize()
-    clocks = sampler.stop(gpus=list(range(world))) if local == 0 else None
+    clocks = sampler.stop(gpus=list(range(world))) if rank == 0 else None
 
     total_ms = ev[0][0].elapsed_time(ev[-1][2])
     compute_ms = sum(e[1].elapsed_time(e[2]) for e in ev)
