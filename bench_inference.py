@@ -87,8 +87,8 @@ def main():
     if world > 1:
         dist.barrier()
     torch.cuda.synchronize()
-    sampler = ClockSampler()
-    if local == 0:
+    sampler = ClockSampler()  # sampled by the rank that prints
+    if rank == 0:
         sampler.start()
     start_launch_count()
     e0, e1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
@@ -101,7 +101,7 @@ def main():
     if world > 1:
         dist.barrier()
     torch.cuda.synchronize()
-    clocks = sampler.stop(gpus=list(range(world))) if local == 0 else None
+    clocks = sampler.stop(gpus=list(range(world))) if rank == 0 else None
     total_ms = e0.elapsed_time(e1)
     steps_ms = sum(out.step_ms)
     t = torch.tensor([total_ms, steps_ms], device=device)
