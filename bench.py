@@ -170,6 +170,10 @@ def main():
         dev_batch = batch_to_device(batch, device, non_blocking=True)
         ev[k][1].record()
         metrics = runner.device_step(dev_batch)
+        if k == args.steps - 1:
+            # deferred optimizer updates (one rank) finish inside the timed region: the last step's
+            # update is waited for here, the earlier ones by the next step's forward
+            engine.flush_updates()
         ev[k][2].record()
     torch.cuda.synchronize()
     launches = stop_launch_count()
