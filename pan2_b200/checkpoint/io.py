@@ -318,6 +318,10 @@ def load_plain_into_engine(engine, path: str, strict: bool = True) -> List[str]:
     tmtd = bool(engine.arch.get("text_modulation_timestep_dependent", False))
     missing = []
     world, rank = engine.world, engine.rank
+    if hasattr(engine, "flush_updates"):
+        engine.flush_updates()
+    if engine.device.type == "cuda":
+        torch.cuda.synchronize(engine.device)
     for u in engine.sharded.units:
         if u.name.startswith("blocks."):
             pre = u.name + "."

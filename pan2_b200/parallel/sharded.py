@@ -154,6 +154,8 @@ class ShardedModel:
                  offload: bool, replicate_group: Optional[dist.ProcessGroup] = None):
         self.units = units
         self.group = group
+        # called before the weights are read outside a step (the engine waits for deferred updates)
+        self.before_read = None
         # HSDP: shards are replicated across this group (one member per node); gradients are
         # all-reduced over it after the reduce-scatter
         self.replicate_group = (replicate_group if replicate_group is not None and dist.is_initialized()
@@ -399,6 +401,8 @@ class ShardedModel:
     def full_state_dict(self, to_cpu: bool = True) -> Dict[str, torch.Tensor]:
         """fp32 full weights of every parameter (gathers all shards; collective when world > 1)."""
         from ..optim.flat_ops import join_master
+        if self.before_read is not None:
+            self.before_read()
         out = {}
         for u in self.units:
             x = join_master(u.hi, u.lo)

@@ -200,6 +200,7 @@ class TrainEngine:
         units.append(self._materialise(self.n_blocks, "root", root, ""))
         self.model = model
         self.sharded = ShardedModel(units, group, device, self.offload, replicate_group)
+        self.sharded.before_read = self.flush_updates
         for u in units:
             if self.world == 1:
                 self.sharded.bind_weights(u, u.hi)
