@@ -222,7 +222,7 @@ class TrainEngine:
         self.lr_t = torch.full((1,), self.optim.lr, dtype=torch.float32, device=device)
         self.norm_clip = torch.zeros(2, dtype=torch.float32, device=device)
         # deferred (overlapped) optimizer updates with host-offloaded state and one rank
-        self.defer_optimizer = device.type == "cuda" and os.environ.get("PAN_DEFER_OPTIMIZER", "1") != "0"
+        self.defer_optimizer = device.type == "cuda" and os.environ.get("PAN_DEFER_OPTIMIZER", "0") == "1"
         self._upd_events: Dict[int, torch.cuda.Event] = {}
         self._lr_used = torch.zeros(1, dtype=torch.float32, device=device)
         self._clip_used = torch.ones(1, dtype=torch.float32, device=device)
