@@ -41,6 +41,24 @@ def _align256(n: int) -> int:
     return (int(n) + 255) // 256 * 256
 
 
+def muon_exchange_layout(remote, world: int) -> dict:
+    """Byte offsets of one unit's distributed-Muon buffers (identical on every rank).
+
+    ``remote`` lists the unit's Muon matrices that need the whole matrix on one rank, in slot order;
+    matrix j belongs to owner ``j % world``.  The exchange region holds, per matrix, this rank's
+    ``shard_rows x cols`` bf16 momentum rows at ``xoff[j]``; an owner's result region holds each
+    of its matrices whole (``rows_pad x cols`` bf16) at ``roff[j]``.  Offsets are 256-byte aligned."""
+    xoff, off = [], 0
+    for s in remote:
+        xoff.append(off)
+        off += _align256(s.shard_rows * s.cols * 2)
+    roff, per_owner = [], [0] * world
+    for j, s in enumerate(remote):
+        roff.append(per_owner[j % world])
+        per_owner[j % world] += _align256(s.rows_pad * s.cols * 2)
+    return dict(xoff=xoff, x_bytes=off, roff=roff, r_bytes=max(per_owner) if per_owner else 0, plans={})
+
+
 class _Root(nn.Module):
     """Everything outside the joint blocks, as one parameter unit (names match the model)."""
 
@@ -600,19 +618,9 @@ class TrainEngine:
         if lay is not None:
             return lay
         from ..parallel.symm import PeerMemory
-        W = self.world
         for unit in self.sharded.units:
             remote = [s for s in unit.slots if self._is_muon(s) and not self._muon_local(s)]
-            xoff, off = [], 0
-            for s in remote:
-                xoff.append(off)
-                off += _align256(s.shard_rows * s.cols * 2)
-            roff, per_owner = [], [0] * W
-            for j, s in enumerate(remote):
-                roff.append(per_owner[j % W])
-                per_owner[j % W] += _align256(s.rows_pad * s.cols * 2)
-            self._muon_layouts[unit.index] = dict(xoff=xoff, x_bytes=off, roff=roff, r_bytes=max(per_owner),
-                                                  plans={})
+            self._muon_layouts[unit.index] = muon_exchange_layout(remote, self.world)
         x_max = max(l["x_bytes"] for l in self._muon_layouts.values())
         r_max = max(l["r_bytes"] for l in self._muon_layouts.values())
         for l in self._muon_layouts.values():
