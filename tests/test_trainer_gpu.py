@@ -31,15 +31,7 @@ def _cfg(data, out, **over):
     return parse_training_config(argv)
 
 
-@pytest.fixture
-def clean_process_group():
-    yield
-    from pan2_b200.parallel.layout import reset_parallel_layout
-    torch.cuda.synchronize()
-    reset_parallel_layout(destroy=True)
-
-
-def test_trainer_gpu_resume_exact(tmp_path, clean_process_group):
+def test_trainer_gpu_resume_exact(tmp_path):
     from pan2_b200.training.trainer import Trainer
     from pan2_b200.ops._ext import ext
     data = tmp_path / "data"
