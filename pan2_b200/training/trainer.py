@@ -85,9 +85,11 @@ def nvtx(name: str):
         yield
 
 
-def build_caption_codec(cfg: TrainingConfig, device) -> CaptionCodec:
+def build_caption_codec(cfg: TrainingConfig, device, embed_dim: int = 4096) -> CaptionCodec:
+    """``hash``: the offline stand-in, with the model's caption embedding width; otherwise the Qwen
+    caption encoder at ``text_encoder_path``."""
     if cfg.text_encoder == "hash":
-        return HashCaptionCodec()
+        return HashCaptionCodec(embed_dim=int(embed_dim))
     from ..models.text_encoder import QwenCaptionCodec
     return QwenCaptionCodec(cfg.text_encoder_path, device=device,
                             hidden_state_skip_layer=cfg.text_encoder_hidden_state_skip_layer)
@@ -180,7 +182,7 @@ class Trainer:
                           caption_segment=cfg.packed_caption_segment_limit,
                           max_num_seq=cfg.packed_dataloader_max_num_seq)
         if self.codec is None:
-            self.codec = build_caption_codec(cfg, self.device)
+            self.codec = build_caption_codec(cfg, self.device, embed_dim=self.arch["text_embed_dim"])
         return PackingDataset(csvs, self.codec, budgets, patch_size=self.arch["patch_size"],
                               rope_axes=tuple(self.arch["rope_axes_dim"]), rope_theta=float(self.arch["rope_theta"]),
                               rope_scale=(float(self.arch["rope_temporal_scale"]), 1.0, 1.0),

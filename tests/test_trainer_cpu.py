@@ -267,3 +267,37 @@ def test_checkpoint_reshards_and_consolidates(tmp_path):
     got2 = eng2.sharded.full_state_dict()
     for k, v in expect.items():
         assert torch.equal(got2[k], v), k
+
+
+@pytest.mark.timeout(600)
+def test_train_cli_runs_and_writes_checkpoint(data_dir, tmp_path):
+    """``python train.py`` end to end on CPU (one process, hash captions) for two steps."""
+    import subprocess
+    import sys
+    root = os.path.dirname(os.path.dirname(os.path.abspath(__file__)))
+    out = tmp_path / "cli"
+    argv = ["--transformer_config_overrides", json.dumps(TINY_OVERRIDES),
+            "--packed_dataloader_meta_csv_path", str(data_dir / "videos.csv"),
+            "--image_tar_path", str(data_dir / "images.tar"), "--image_sample_prob", "0.3",
+            "--packed_joint_token_budget", "300", "--packed_video_token_budget", "260",
+            "--packed_caption_token_budget", "200", "--packed_joint_segment_limit", "300",
+            "--packed_caption_segment_limit", "100", "--packed_dataloader_max_num_seq", "3",
+            "--packed_dataloader_num_buffers", "2", "--packed_dataloader_num_workers", "2",
+            "--video_height", "128", "--video_width", "192", "--output_dir", str(out),
+            "--learning_rate", "1e-3", "--warmup_steps", "2", "--log_interval", "1",
+            "--text_encoder", "hash", "--optimizer_offload", "off", "--profile_step", "-1",
+            "--max_steps", "2", "--save_interval", "2"]
+    env = dict(os.environ, CUDA_VISIBLE_DEVICES="")
+    r = subprocess.run([sys.executable, os.path.join(root, "train.py")] + argv, cwd=root, env=env,
+                       capture_output=True, text=True, timeout=500)
+    assert r.returncode == 0, r.stderr[-2000:]
+    assert os.path.exists(out / "checkpoint-2" / "COMPLETE")
+    assert "Step 2/2" in (r.stdout + r.stderr) or "Step 1/2" in (r.stdout + r.stderr)
+
+
+def test_launch_scripts_parse():
+    import subprocess
+    root = os.path.dirname(os.path.dirname(os.path.abspath(__file__)))
+    for name in ("train.sh", "generate.sh"):
+        r = subprocess.run(["bash", "-n", os.path.join(root, "launch", name)], capture_output=True, text=True)
+        assert r.returncode == 0, (name, r.stderr)
