@@ -1,0 +1,22 @@
+"""Every command-line entry point imports and parses its arguments (``--help``) without a GPU."""
+import os
+import subprocess
+import sys
+
+import pytest
+
+ROOT = os.path.dirname(os.path.dirname(os.path.abspath(__file__)))
+ENTRY_POINTS = [
+    ["train.py"], ["generate.py"], ["bench.py"], ["bench_inference.py"], ["bench_kernels.py"],
+    ["-m", "pan2_b200.checkpoint.convert"], ["-m", "pan2_b200.inference.prompt_rewriter"],
+    ["-m", "pan2_b200.data.make_sample_data"],
+]
+
+
+@pytest.mark.parametrize("cmd", ENTRY_POINTS, ids=[" ".join(c) for c in ENTRY_POINTS])
+def test_entry_point_help(cmd):
+    env = dict(os.environ, CUDA_VISIBLE_DEVICES="")
+    r = subprocess.run([sys.executable] + cmd + ["--help"], cwd=ROOT, env=env, capture_output=True, text=True,
+                       timeout=300)
+    assert r.returncode == 0, r.stderr[-2000:]
+    assert "usage" in r.stdout.lower()
