@@ -22,17 +22,28 @@ def _free_port():
     return p
 
 
-def _step(world, rank, port, out_q):
+def _step(world, rank, port, out_q, hsdp_local=0):
     os.environ.update(MASTER_ADDR="127.0.0.1", MASTER_PORT=str(port))
-    if world > 1:
+    replicate = None
+    if world > 1 and hsdp_local:
+        # HSDP: shards within groups of `hsdp_local` ranks (one "node"), replicated across them
+        os.environ.update(RANK=str(rank), WORLD_SIZE=str(world), LOCAL_WORLD_SIZE=str(hsdp_local))
+        from pan2_b200.parallel.layout import init_parallel_layout
+        L = init_parallel_layout(cp=1, hybrid_shard=True, backend="gloo", timeout_s=120)
+        assert L.shard_size == hsdp_local and L.replicate_size == world // hsdp_local
+        group, replicate = L.shard_group, L.replicate_group
+    elif world > 1:
         import datetime
         dist.init_process_group("gloo", rank=rank, world_size=world, timeout=datetime.timedelta(seconds=120))
+        group = dist.group.WORLD
+    else:
+        group = None
     from pan2_b200.training.engine import TrainEngine, OptimConfig
     from pan2_b200.models.transformer import PanVideoDiffusionTransformer
     arch = dict(TINY_ARCH)
-    group = dist.group.WORLD if world > 1 else None
     eng = TrainEngine(arch, torch.device("cpu"), group=group, seed=11,
-                      optim=OptimConfig(lr=1e-2, weight_decay=0.1, max_grad_norm=0.5), offload="off")
+                      optim=OptimConfig(lr=1e-2, weight_decay=0.1, max_grad_norm=0.5), offload="off",
+                      replicate_group=replicate)
     with torch.device("meta"):
         shape_model = PanVideoDiffusionTransformer(**arch)
     batch, _ = tiny_batch(shape_model, seed=7)
@@ -50,11 +61,11 @@ def _step(world, rank, port, out_q):
         dist.destroy_process_group()
 
 
-def _run(world):
+def _run(world, hsdp_local=0):
     ctx = mp.get_context("spawn")
     q = ctx.Queue()
     port = _free_port()
-    procs = [ctx.Process(target=_step, args=(world, r, port, q)) for r in range(world)]
+    procs = [ctx.Process(target=_step, args=(world, r, port, q, hsdp_local)) for r in range(world)]
     for p in procs:
         p.start()
     path = q.get(timeout=300)
@@ -65,10 +76,10 @@ def _run(world):
 
 
 @pytest.mark.timeout(900)
-@pytest.mark.parametrize("world", [2, 4])
-def test_multi_rank_step_matches_one_rank(world):
+@pytest.mark.parametrize("world,hsdp_local", [(2, 0), (4, 0), (4, 2)], ids=["fsdp2", "fsdp4", "hsdp2x2"])
+def test_multi_rank_step_matches_one_rank(world, hsdp_local):
     loss1, norm1, sd1 = _run(1)
-    loss2, norm2, sd2 = _run(world)
+    loss2, norm2, sd2 = _run(world, hsdp_local)
     assert abs(loss1 - loss2) < 1e-5 * abs(loss1) + 1e-6, (loss1, loss2)
     assert abs(norm1[0] - norm2[0]) < 1e-3 * norm1[0], (norm1, norm2)
     worst = (0.0, "")
