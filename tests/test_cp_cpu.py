@@ -80,11 +80,12 @@ def _run(world, cp, tmp):
 
 
 @pytest.mark.timeout(900)
-def test_ulysses_cp2_matches_single_rank(tmp_path):
+@pytest.mark.parametrize("world,cp", [(2, 2), (4, 2)], ids=["cp2", "dp2xcp2"])
+def test_ulysses_cp_matches_single_rank(tmp_path, world, cp):
     # gradients, not updated weights: the one-rank gradients are bf16, and AdamW's first step turns
     # near-zero gradient elements into full +-lr updates, which bf16 rounding can flip
     loss1, norm1, g1 = _run(1, 1, str(tmp_path))
-    loss2, norm2, g2 = _run(2, 2, str(tmp_path))
+    loss2, norm2, g2 = _run(world, cp, str(tmp_path))
     assert abs(loss1 - loss2) < 1e-5 * abs(loss1) + 1e-6, (loss1, loss2)
     assert abs(norm1[0] - norm2[0]) < 1e-3 * norm1[0], (norm1, norm2)
     worst = (0.0, "")
