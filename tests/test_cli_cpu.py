@@ -20,3 +20,11 @@ def test_entry_point_help(cmd):
                        timeout=300)
     assert r.returncode == 0, r.stderr[-2000:]
     assert "usage" in r.stdout.lower()
+
+
+def test_graft_entry_imports_built_extension():
+    if not any(f.startswith("_C.") and f.endswith(".so") for f in os.listdir(os.path.join(ROOT, "pan2_b200"))):
+        pytest.skip("extension not built")
+    r = subprocess.run([sys.executable, "-c", "import __graft_entry__ as g; g.import_package(); print('ok')"],
+                       cwd=ROOT, capture_output=True, text=True, timeout=300)
+    assert r.returncode == 0 and "ok" in r.stdout, r.stderr[-2000:]
