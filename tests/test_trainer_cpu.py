@@ -267,6 +267,16 @@ def test_checkpoint_reshards_and_consolidates(tmp_path):
     got2 = eng2.sharded.full_state_dict()
     for k, v in expect.items():
         assert torch.equal(got2[k], v), k
+    # the reference's checkpoint converter reads a directory of safetensors shards by merging their
+    # key -> tensor maps: the consolidated folder must give every parameter whole, by its name
+    import glob
+    from safetensors.torch import load_file
+    merged = {}
+    for shard in sorted(glob.glob(os.path.join(out, "*.safetensors"))):
+        merged |= load_file(shard)
+    assert set(merged) == set(expect)
+    for k, v in expect.items():
+        assert torch.equal(merged[k], v.reshape(merged[k].shape)), k
 
 
 @pytest.mark.timeout(600)
