@@ -200,22 +200,47 @@ def load_engine(engine, root: str, *, load_optimizer: bool = True, strict: bool 
 
 
 # ------------------------------------------------------------------ plain state dicts
+def strip_wrapper_prefix(name: str) -> str:
+    """Parameter name without the ``module.`` / ``model.`` prefixes that DDP / FSDP wrappers and
+    trainer state dicts add (the reference's loaders strip the same two)."""
+    for pre in ("module.", "model."):
+        if name.startswith(pre):
+            name = name[len(pre):]
+    return name
+
+
 class LazyStateDict:
     """Read-on-demand view of a plain state dict: safetensors shards (a folder, an index json or one
-    file), a ``.pt``/``.bin`` file, or a sharded checkpoint folder.  ``get(name)`` loads one tensor."""
+    file), a ``.pt``/``.bin`` file, a torch distributed checkpoint (DCP) folder -- the reference
+    trainer's ``checkpoint-N/transformer`` -- or this framework's sharded checkpoint folder.
+    ``get(name)`` loads one tensor.  Names are reported without ``module.`` / ``model.`` prefixes
+    unless ``key_map`` says otherwise."""
 
     def __init__(self, path: str, key_map: Optional[Callable[[str], str]] = None):
-        self.key_map = key_map or (lambda k: k)
+        self.key_map = key_map or strip_wrapper_prefix
         path = str(path)
         self._files: Dict[str, str] = {}
         self._eager: Optional[Dict[str, torch.Tensor]] = None
         self._sharded: Optional[ShardedReader] = None
+        self._dcp = None
         p = os.path.normpath(path)
         if os.path.isdir(p) and os.path.exists(os.path.join(p, "transformer", "meta.json")):
             p = os.path.join(p, "transformer")
         if os.path.isdir(p) and os.path.exists(os.path.join(p, "meta.json")):
             self._sharded = ShardedReader(p)
             self._names = {self.key_map(k): k for k in self._sharded.where}
+            return
+        if os.path.isdir(p) and not os.path.exists(os.path.join(p, ".metadata")) and \
+                os.path.exists(os.path.join(p, "transformer", ".metadata")):
+            p = os.path.join(p, "transformer")
+        if os.path.isdir(p) and os.path.exists(os.path.join(p, ".metadata")):
+            import torch.distributed.checkpoint as dcp
+            from torch.distributed.checkpoint.metadata import TensorStorageMetadata
+            reader = dcp.FileSystemReader(p)
+            meta = reader.read_metadata()
+            self._dcp = (p, {k: (tuple(m.size), m.properties.dtype) for k, m in meta.state_dict_metadata.items()
+                             if isinstance(m, TensorStorageMetadata)})
+            self._names = {self.key_map(k): k for k in self._dcp[1]}
             return
         files = []
         if os.path.isdir(p):
@@ -239,8 +264,9 @@ class LazyStateDict:
             self._names = {self.key_map(k): k for k in self._files}
         else:
             sd = torch.load(p, map_location="cpu", weights_only=True)
-            if isinstance(sd, dict) and "state_dict" in sd and isinstance(sd["state_dict"], dict):
-                sd = sd["state_dict"]
+            for wrapper in ("state_dict", "model"):
+                if isinstance(sd, dict) and isinstance(sd.get(wrapper), dict):
+                    sd = sd[wrapper]
             self._eager = {k: v for k, v in sd.items() if isinstance(v, torch.Tensor)}
             self._names = {self.key_map(k): k for k in self._eager}
 
@@ -256,6 +282,13 @@ class LazyStateDict:
             return default
         if self._sharded is not None:
             return self._sharded.full(raw)
+        if self._dcp is not None:
+            import torch.distributed.checkpoint as dcp
+            folder, specs = self._dcp
+            size, dtype = specs[raw]
+            out = {raw: torch.empty(size, dtype=dtype)}
+            dcp.load(out, storage_reader=dcp.FileSystemReader(folder), no_dist=True)
+            return out[raw]
         if self._eager is not None:
             return self._eager[raw]
         from safetensors import safe_open

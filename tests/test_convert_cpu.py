@@ -40,3 +40,24 @@ def test_round_trip_and_layout(tmp_path):
         assert torch.equal(r.get(k).to(v.dtype), v), k
     m2 = tiny_model(seed=9)
     m2.load_state_dict({k: r.get(k) for k in r.keys()})
+
+
+def test_reference_style_dcp_checkpoint_loads(tmp_path):
+    """A torch distributed checkpoint with ``model.``-prefixed keys (the reference trainer's
+    ``checkpoint-N/transformer``) loads into the model by name, tensor by tensor."""
+    import torch.distributed.checkpoint as dcp
+    from pan2_b200.checkpoint.io import LazyStateDict
+    from pan2_b200.pipelines.video import load_transformer_weights
+    from tiny import tiny_model
+    src = tiny_model(seed=3)
+    ck = tmp_path / "checkpoint-7" / "transformer"
+    sd = {"model." + k: v.clone() for k, v in src.state_dict().items()}
+    dcp.save(sd, storage_writer=dcp.FileSystemWriter(str(ck)), no_dist=True)
+    lazy = LazyStateDict(str(tmp_path / "checkpoint-7"))
+    assert set(lazy.keys()) == set(src.state_dict())
+    dst = tiny_model(seed=4)
+    load_transformer_weights(dst, str(ck))
+    for k, v in src.state_dict().items():
+        if k.endswith("freqs"):
+            continue
+        assert torch.equal(dst.state_dict()[k], v), k
