@@ -42,7 +42,7 @@ NEG=()
 mkdir -p "$OUTPUT_DIR" logs
 export PYTORCH_CUDA_ALLOC_CONF=${PYTORCH_CUDA_ALLOC_CONF:-expandable_segments:True}
 export HF_HUB_OFFLINE=${HF_HUB_OFFLINE:-1}
-python -c "import pan2_b200._C" 2>/dev/null || python setup.py build_ext --inplace
+python -c "import torch, pan2_b200._C" 2>/dev/null || python setup.py build_ext --inplace
 
 torchrun --standalone --local-addr 127.0.0.1 --nnodes=1 --nproc-per-node="$GPUS" generate.py \
     --task "$TASK" --prompt_json "$PROMPTS_JSON" --output_dir "$OUTPUT_DIR" --sp_size "$SP_SIZE" \

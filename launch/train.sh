@@ -31,7 +31,7 @@ export PYTORCH_CUDA_ALLOC_CONF=${PYTORCH_CUDA_ALLOC_CONF:-expandable_segments:Tr
 export HF_HUB_OFFLINE=${HF_HUB_OFFLINE:-1}
 export TORCH_NCCL_ASYNC_ERROR_HANDLING=${TORCH_NCCL_ASYNC_ERROR_HANDLING:-1}
 # the CUDA extension is built in-tree once; every rank imports the same .so
-python -c "import pan2_b200._C" 2>/dev/null || python setup.py build_ext --inplace
+python -c "import torch, pan2_b200._C" 2>/dev/null || python setup.py build_ext --inplace
 
 GPUS_PER_NODE=${GPUS_PER_NODE:-$(nvidia-smi -L 2>/dev/null | wc -l)}
 if [[ -n ${SLURM_JOB_ID:-} && ${SLURM_NNODES:-1} -gt 1 ]]; then
