@@ -14,7 +14,8 @@ encoder ``qkv`` into ``to_q/k/v``, per-modality q/k norm weights into ``norm_q/k
 is a constant rebuilt on load.
 
 Inputs of ``to-diffusers`` are anything :class:`~pan2_b200.checkpoint.io.LazyStateDict` reads (this
-framework's sharded ``checkpoint-N``, consolidated or single safetensors, ``.pt``); tensors are read
+framework's sharded ``checkpoint-N``, consolidated or single safetensors, ``.pt``, torch distributed
+checkpoints); tensors are read
 per block, so host memory holds one block at a time.  Outputs are 5 GB safetensors shards with an
 index (and ``config.json`` for diffusers).
 """
