@@ -415,3 +415,24 @@ def cleanup_old(output_dir: str, keep: int) -> List[str]:
         shutil.rmtree(d, ignore_errors=True)
         removed.append(d)
     return removed
+
+
+def main(argv=None) -> None:
+    """``python -m pan2_b200.checkpoint.io consolidate --input checkpoint-N --output DIR [--dtype]``:
+    write a checkpoint (any form :class:`LazyStateDict` reads) as one plain safetensors state dict."""
+    import argparse
+    ap = argparse.ArgumentParser(description="Checkpoint tools")
+    sub = ap.add_subparsers(dest="cmd", required=True)
+    c = sub.add_parser("consolidate", help="sharded / distributed checkpoint -> plain safetensors shards + index")
+    c.add_argument("--input", required=True, help="checkpoint-N, its transformer/ folder, or any state dict")
+    c.add_argument("--output", required=True)
+    c.add_argument("--dtype", default="bf16", choices=("bf16", "fp32"))
+    c.add_argument("--max_shard_gb", type=float, default=5.0)
+    args = ap.parse_args(argv)
+    dtype = torch.bfloat16 if args.dtype == "bf16" else torch.float32
+    paths = consolidate(args.input, args.output, dtype=dtype, max_shard_bytes=int(args.max_shard_gb * 1024 ** 3))
+    print(f"wrote {len(paths)} shard(s) to {args.output}")
+
+
+if __name__ == "__main__":
+    main()

@@ -9,7 +9,7 @@ ROOT = os.path.dirname(os.path.dirname(os.path.abspath(__file__)))
 ENTRY_POINTS = [
     ["train.py"], ["generate.py"], ["bench.py"], ["bench_inference.py"], ["bench_kernels.py"],
     ["-m", "pan2_b200.checkpoint.convert"], ["-m", "pan2_b200.inference.prompt_rewriter"],
-    ["-m", "pan2_b200.data.make_sample_data"],
+    ["-m", "pan2_b200.data.make_sample_data"], ["-m", "pan2_b200.checkpoint.io"],
 ]
 
 
