@@ -311,3 +311,24 @@ def test_launch_scripts_parse():
     for name in ("train.sh", "generate.sh"):
         r = subprocess.run(["bash", "-n", os.path.join(root, "launch", name)], capture_output=True, text=True)
         assert r.returncode == 0, (name, r.stderr)
+
+
+@pytest.mark.timeout(600)
+def test_wandb_reporting_with_a_stand_in_module(data_dir, tmp_path, monkeypatch):
+    import sys
+    import types
+    calls = {"init": [], "log": [], "finish": 0}
+    fake = types.ModuleType("wandb")
+    fake.init = lambda **kw: calls["init"].append(kw)
+    fake.log = lambda d, step=None: calls["log"].append((dict(d), step))
+
+    def finish():
+        calls["finish"] += 1
+    fake.finish = finish
+    monkeypatch.setitem(sys.modules, "wandb", fake)
+    _train(_cfg(data_dir, tmp_path / "w", max_steps=2, save_interval=100, report_to="wandb"))
+    assert len(calls["init"]) == 1 and "learning_rate" in calls["init"][0]["config"]
+    assert len(calls["log"]) == 2
+    for d, _ in calls["log"]:
+        assert {"train/loss", "train/grad_norm"} <= set(d)
+    assert calls["finish"] == 1
