@@ -145,9 +145,9 @@ def main():
         from pan2_b200.data.cp_batch import broadcast_and_split
         engine.set_context_parallel(layout.cp_group, cp, layout.cp_rank)
         src = batch_to_device(batch, device) if layout.cp_rank == 0 else None
-        local, _ = broadcast_and_split(src, None, layout, device)
+        shard, _ = broadcast_and_split(src, None, layout, device)
         torch.cuda.synchronize()
-        batch = pin_batch({k: (v.cpu() if isinstance(v, torch.Tensor) else v) for k, v in local.items()})
+        batch = pin_batch({k: (v.cpu() if isinstance(v, torch.Tensor) else v) for k, v in shard.items()})
     elif args.workload != "pretrain":
         batch = pin_batch(batch)
     init_s = time.time() - t0
