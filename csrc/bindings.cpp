@@ -31,6 +31,7 @@ const char* launch_attn_bwd(const void* q, const void* k, const void* v, const v
                             int L, int H, int head_dim, float scale, float* delta, void* dq, void* dk, void* dv,
                             float* dq_acc, cudaStream_t s);
 int attn_error_flag(bool reset);
+int qkv_bounds_error(bool reset);
 void attn_set_backward_variant(int v);
 void attn_set_forward_variant(int v);
 void launch_sumsq(const void* x, bool fp32, size_t n, float* partial, int n_part, cudaStream_t s);
@@ -665,7 +666,8 @@ void ns_scale_by_invnorm(torch::Tensor Q, torch::Tensor norm2, double eps) {
 }
 
 int error_flag(bool reset) {
-  return gemm_error_flag(reset) | packed_ops_error_flag(reset) | attn_error_flag(reset) | comm_error_flag(reset);
+  return gemm_error_flag(reset) | packed_ops_error_flag(reset) | attn_error_flag(reset) | comm_error_flag(reset) |
+         qkv_bounds_error(reset);
 }
 
 // ---------------------------------------------------------------- peer-memory collectives

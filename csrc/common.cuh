@@ -7,6 +7,25 @@
 
 namespace pan {
 
+// Bounds-checked debug build (compile with -DPAN_DEBUG_BOUNDS, e.g. PAN_DEBUG_BOUNDS=1 python setup.py
+// build_ext --inplace): PAN_IDX(i, n, code) checks a data-driven index against its bound, records
+// `code` in the device error flag read by error_flag() when it is out of range, and substitutes 0 so
+// the access stays in bounds.  In the normal build the macro is the bare index expression, so the
+// production kernels compile exactly as written.
+#ifdef PAN_DEBUG_BOUNDS
+static __device__ int g_bounds_error = 0;  // one per translation unit; each file exposes a reader
+__device__ __forceinline__ int pan_checked_index(int i, int n, int code) {
+  if (i < 0 || i >= n) {
+    atomicCAS(&g_bounds_error, 0, code);
+    return 0;
+  }
+  return i;
+}
+#define PAN_IDX(i, n, code) ::pan::pan_checked_index((i), (n), (code))
+#else
+#define PAN_IDX(i, n, code) (i)
+#endif
+
 // 8 x bf16 = 16 bytes, the unit of every vectorised row access.
 struct __align__(16) bf16x8 {
   __nv_bfloat162 h[4];

@@ -64,7 +64,7 @@ __global__ void qkv_post_fwd_kernel(const __nv_bfloat16* __restrict__ raw, const
   const int warps = blockDim.x >> 5;
   const int HD = H * D;
   for (int p = blockIdx.x * warps + (threadIdx.x >> 5); p < L; p += gridDim.x * warps) {
-    const int dst = itc[p];
+    const int dst = PAN_IDX(itc[p], L, 201);
     const size_t orow = (size_t)dst * HD;
     // destination of (this row, head h) in q / k / v: the local interleave row, or with the
     // Ulysses scatter on, row dst * cp + rank of head owner h / hl's head-sharded buffer
@@ -139,7 +139,7 @@ __global__ void qkv_post_bwd_kernel(const __nv_bfloat16* __restrict__ dq, const 
       for (int j = 0; j < 3 * H; ++j) storev<EPL>(dr + j * D + lane * EPL, z);
       continue;
     }
-    const int src = itc[p];
+    const int src = PAN_IDX(itc[p], L, 202);
     const size_t irow = (size_t)src * HD;
     const int mod = p < nv ? 0 : 1;
     float c[EPL], s[EPL], wq[EPL], wk[EPL];
@@ -238,6 +238,22 @@ const char* launch_qkv_post_bwd(const void* dq, const void* dk, const void* dv, 
   else
     return "qkv_post: head_dim must be 64 or 128";
   return nullptr;
+}
+
+// Index errors recorded by the bounds-checked debug build in this file's kernels (0 otherwise).
+int qkv_bounds_error(bool reset) {
+#ifdef PAN_DEBUG_BOUNDS
+  int v = 0;
+  cudaMemcpyFromSymbol(&v, g_bounds_error, sizeof(int));
+  if (reset) {
+    int z = 0;
+    cudaMemcpyToSymbol(g_bounds_error, &z, sizeof(int));
+  }
+  return v;
+#else
+  (void)reset;
+  return 0;
+#endif
 }
 
 }  // namespace pan

@@ -14,6 +14,10 @@ NVCC_FLAGS = [
     "-Xptxas", "-v",
 ]
 
+if os.environ.get("PAN_DEBUG_BOUNDS", "0") == "1":
+    # bounds-checked debug build: data-driven indices are checked and recorded in error_flag()
+    NVCC_FLAGS.append("-DPAN_DEBUG_BOUNDS")
+
 sources = ["csrc/bindings.cpp"] + sorted(glob.glob("csrc/*.cu"))
 
 setup(
