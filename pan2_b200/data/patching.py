@@ -7,7 +7,7 @@ rotation (cos = 1, sin = 0), as in dataset/packing_dataset.py:439-442.
 """
 from __future__ import annotations
 
-from typing import List, Sequence, Tuple
+from typing import Sequence, Tuple
 
 import torch
 from einops import rearrange

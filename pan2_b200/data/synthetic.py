@@ -9,7 +9,7 @@ with identity rows for text.  All tensors are created on the CPU (pinned when re
 """
 from __future__ import annotations
 
-from typing import Dict, List, Optional, Sequence, Tuple
+from typing import Dict, List, Sequence, Tuple
 
 import torch
 

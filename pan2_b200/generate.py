@@ -25,7 +25,7 @@ import copy
 import datetime
 import json
 import sys
-from typing import List, Optional
+from typing import List
 
 import torch
 import torch.distributed as dist

@@ -21,7 +21,7 @@ import json
 import re
 from decimal import ROUND_CEILING, Decimal, InvalidOperation
 from pathlib import Path, PurePosixPath
-from typing import Dict, List, Optional
+from typing import Dict, List
 
 GUIDANCE_KEYS = ("cfg_start_step", "cfg_end_step", "stg_scale", "stg_skip_layers")
 ROUTING_ARGS = {"prompt_json", "output_dir", "prompt_shard_index", "prompt_shard_count", "skip_existing",

@@ -16,7 +16,7 @@ interface (:class:`~pan2_b200.data.items.CaptionCodec`) and also serves generati
 from __future__ import annotations
 
 import os
-from typing import List, Optional, Sequence, Tuple
+from typing import Optional, Sequence, Tuple
 
 import torch
 import torch.nn as nn

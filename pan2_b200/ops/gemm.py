@@ -20,7 +20,7 @@ CPU tensors take the plain PyTorch path with identical semantics.
 """
 from __future__ import annotations
 
-from typing import List, Optional, Sequence
+from typing import Optional, Sequence
 
 import torch
 import torch.nn.functional as F

@@ -20,7 +20,7 @@ tensors run plain PyTorch with the same math.
 """
 from __future__ import annotations
 
-from typing import List, Optional, Sequence, Tuple
+from typing import Optional, Sequence, Tuple
 
 import torch
 

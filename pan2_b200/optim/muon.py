@@ -19,7 +19,7 @@ MN-major operands, so nothing is transposed in memory.
 from __future__ import annotations
 
 import math
-from typing import Dict, List, Sequence, Tuple
+from typing import Dict, Sequence, Tuple
 
 import torch
 

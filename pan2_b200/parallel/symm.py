@@ -17,7 +17,7 @@ layout makes every parameter's rank slice one run in both layouts).
 """
 from __future__ import annotations
 
-from typing import List, Optional, Sequence, Tuple
+from typing import List, Optional, Tuple
 
 import torch
 import torch.distributed as dist

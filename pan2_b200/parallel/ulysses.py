@@ -16,7 +16,7 @@ Transport: NCCL ``all_to_all_single`` over NVLink (gloo point-to-point on CPU te
 from __future__ import annotations
 
 import functools
-from typing import List, Sequence, Tuple
+from typing import Sequence, Tuple
 
 import torch
 import torch.distributed as dist

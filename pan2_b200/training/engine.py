@@ -19,7 +19,6 @@ This is the B200 restatement of the reference trainer's model wrapping and step
 """
 from __future__ import annotations
 
-import math
 import os
 from dataclasses import dataclass
 from typing import Dict, List, Optional, Sequence
@@ -34,7 +33,7 @@ from ..ops._ext import ext
 from ..optim import flat_ops as F
 from ..optim.muon import adjust_lr_scale, chunk_view, gram_newton_schulz
 from ..parallel.collectives import all_to_all_list
-from ..parallel.sharded import ShardedModel, Unit, build_unit, set_master, split_master_cpu
+from ..parallel.sharded import ShardedModel, Unit, build_unit
 
 
 def _align256(n: int) -> int:

@@ -26,7 +26,6 @@ from __future__ import annotations
 import glob
 import json
 import logging
-import math
 import os
 import random
 import sys
