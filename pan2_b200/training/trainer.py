@@ -291,6 +291,15 @@ class Trainer:
             ckpt.load_plain_into_engine(self.engine, path, strict=True)
         log.info(f"warm start from {path}: transformer weights only")
 
+    def _check_device_errors(self) -> None:
+        """Stop the run when a kernel gave up a bounded wait (a peer that never arrived, a copy
+        that never landed): its outputs are incomplete, so continuing would train on them."""
+        from ..ops._ext import ext
+        flag = int(ext().error_flag(True))
+        if flag:
+            raise RuntimeError(f"device error code {flag} after step {self.global_step - 1}: a kernel stopped "
+                               "waiting (peer rank gone or stalled, or a transfer that never completed)")
+
     def recover(self) -> None:
         log.warning("recovering from the latest checkpoint")
         used = self.load_checkpoint(load_dataloader_state=False)
@@ -378,6 +387,8 @@ class Trainer:
                 with nvtx("train_step"):
                     stats = self.runner.device_step(batches, poison=self.injector.poisons_update(self.global_step))
                 stats = self.injector.after_step(self.global_step, stats)
+                if cuda and (self.global_step - 1) % max(1, cfg.log_interval) == 0:
+                    self._check_device_errors()
                 if meta is not None:
                     self._update_util(meta)
                 if cuda:
