@@ -174,6 +174,9 @@ class CsvStream:
         epoch = last.epoch_index if last else 0
         gidx = (last.global_index + 1) if last else 0
         resume = last
+        # a whole pass that starts at the first file and yields nothing means every CSV is empty:
+        # fail instead of cycling through empty files forever
+        full_pass, yielded = resume is None and csv_i == 0, 0
         while True:
             with open(self.paths[csv_i], "rb") as f:
                 header = _parse_record(_read_record(f))
@@ -195,10 +198,14 @@ class CsvStream:
                                        epoch_index=epoch)
                     gidx += 1
                     local += 1
+                    yielded += 1
             csv_i += 1
             if csv_i == len(self.paths):
+                if full_pass and yielded == 0:
+                    raise ValueError(f"the video CSVs ({len(self.paths)} file(s)) contain no rows")
                 csv_i = 0
                 epoch += 1
+                full_pass, yielded = True, 0
 
 
 class PackingDataset:

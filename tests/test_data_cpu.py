@@ -131,3 +131,18 @@ def test_synthetic_workload_batches_fit_their_budgets():
     for r in range(4):
         rows += strided_split(long, 4, r)["hidden_states"].shape[1]
     assert rows == long["hidden_states"].shape[1]
+
+
+def test_loader_inputs_fail_fast(tmp_path):
+    from pan2_b200.data.packing import CsvStream
+    with pytest.raises(ValueError):
+        CsvStream([])  # no video CSV files
+    empty = tmp_path / "empty.csv"
+    empty.write_text("latent_path,caption\n")
+    with pytest.raises(ValueError, match="contain no rows"):
+        next(iter(CsvStream([str(empty), str(empty)]).rows(None)))
+    one = tmp_path / "one.csv"
+    one.write_text("latent_path,caption\na.safetensors,hello\n")
+    rows = CsvStream([str(empty), str(one)]).rows(None)
+    first = [next(rows)[0]["caption"] for _ in range(3)]  # cycles through the non-empty file
+    assert first == ["hello"] * 3
