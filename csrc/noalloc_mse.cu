@@ -1,10 +1,10 @@
 // Allocation-free entry point for the flow-matching loss sums.
 //
 // This file has no counterpart in the reference project.  It exists for callers that cannot call
-// cudaMalloc or any allocating library routine: code running while a CUDA graph is being built
-// around it by someone else, custom allocators or runtimes that forbid hidden device allocations,
-// and C/C++ hosts that link this library without PyTorch and so have no caching allocator to borrow
-// scratch space from.
+// cudaMalloc or any allocating library routine: runtimes and custom allocators that own every
+// device allocation and forbid hidden ones, and C/C++ hosts that link this library without PyTorch
+// and so have no caching allocator to borrow scratch space from.  The C declarations are in
+// noalloc_mse.h:
 //
 //   int pan2_mse_sums_noalloc(const void* pred, const void* target, long long n, float* out,
 //                             void* stream);
@@ -33,6 +33,7 @@
 #include <mutex>
 
 #include "common.cuh"
+#include "noalloc_mse.h"
 
 constexpr int kMaxPartials = 16384;
 

@@ -1,8 +1,8 @@
 """The allocation-free loss entry point, called through its exported C symbol.
 
-``pan2_mse_sums_noalloc`` serves callers that cannot allocate device memory (for example code
-running under someone else's graph capture, or a C/C++ host without a caching allocator): its
-scratch is a fixed device array inside the library.  This test calls it through ctypes twice in a
+``pan2_mse_sums_noalloc`` serves callers that cannot allocate device memory (runtimes or allocators
+that forbid hidden device allocations, or a C/C++ host that has no caching allocator to borrow
+from): its scratch is a fixed device array inside the library.  This test calls it through ctypes twice in a
 row and compares each result with the allocating ``mse_fwd`` binding.  It lives in its own file,
 collected last, so a failure here never hides the results of the other tests.
 """
