@@ -245,12 +245,20 @@ class PackingDataset:
 
     def _image_stream(self, cur: ImageCursor):
         shard, sample, cycle = cur.shard_index % len(self.tars), cur.sample_index, cur.cycle
+        # shards read from their first sample in a row that yielded nothing; once that covers every
+        # tar, all of them are empty: fail instead of cycling through empty tars forever
+        empty_run = 0
         while True:
+            yielded = 0
             for idx, key, raw, text in iter_tar_samples(self.tars[shard]):
                 if idx < sample:
                     continue
+                yielded += 1
                 ref = ItemRef(global_index=-1, modality="image", shard_index=shard, sample_index=idx, cycle=cycle)
                 yield raw, text, ref, ImageCursor(shard, idx + 1, cycle)
+            empty_run = empty_run + 1 if (yielded == 0 and sample == 0) else 0
+            if empty_run == len(self.tars):
+                raise ValueError(f"the image tars ({len(self.tars)} file(s)) contain no complete samples")
             shard, sample = shard + 1, 0
             if shard == len(self.tars):
                 shard, cycle = 0, cycle + 1

@@ -146,3 +146,23 @@ def test_loader_inputs_fail_fast(tmp_path):
     rows = CsvStream([str(empty), str(one)]).rows(None)
     first = [next(rows)[0]["caption"] for _ in range(3)]  # cycles through the non-empty file
     assert first == ["hello"] * 3
+
+
+def test_image_stream_fails_fast_on_empty_tars(tmp_path, sample_dir):
+    import tarfile
+    from pan2_b200.data.packing import ImageCursor
+    empty = tmp_path / "empty.tar"
+    with tarfile.open(empty, "w"):
+        pass
+    ds = _dataset(sample_dir, image_tars=[str(empty), str(empty)])
+    with pytest.raises(ValueError, match="no complete samples"):
+        next(ds._image_stream(ImageCursor()))
+    # an empty tar beside a real one: the stream keeps cycling through the real one's samples
+    ds = _dataset(sample_dir, image_tars=[str(empty), str(sample_dir / "images.tar")])
+    it = ds._image_stream(ImageCursor())
+    got = [next(it)[2] for _ in range(14)]
+    assert {r.shard_index for r in got} == {1}
+    assert [r.sample_index for r in got[:7]] == list(range(6)) + [0] and got[6].cycle == 1
+    # resuming past the last sample of the only real tar is not mistaken for an empty pass
+    it = ds._image_stream(ImageCursor(1, 6, 0))
+    assert next(it)[2].sample_index == 0
