@@ -41,17 +41,22 @@ def _producer(it: Iterator[PackedPlan], q: "queue.Queue", stop: threading.Event)
             if torch.cuda.is_available():
                 for item in plan.items:
                     item.latent = item.latent.pin_memory()
-            while not stop.is_set():
-                try:
-                    q.put(plan, timeout=0.5)
-                    break
-                except queue.Full:
-                    continue
-            if stop.is_set():
+            if not _put_until_stopped(q, plan, stop):
                 return
-        q.put(None)
+        _put_until_stopped(q, None, stop)
     except BaseException as e:  # surfaced on the consumer side
-        q.put(e)
+        _put_until_stopped(q, e, stop)
+
+
+def _put_until_stopped(q: "queue.Queue", obj, stop: threading.Event) -> bool:
+    """Put ``obj`` into ``q``, giving up once ``stop`` is set; True when it was put."""
+    while not stop.is_set():
+        try:
+            q.put(obj, timeout=0.5)
+            return True
+        except queue.Full:
+            continue
+    return False
 
 
 class PackedLoader:
@@ -79,8 +84,11 @@ class PackedLoader:
         self._q = None
 
     def __iter__(self):
+        # a second iter() stops the previous producer first (each producer gets its own stop event,
+        # so the old one cannot keep filling a queue that nobody reads)
+        self.close()
         self._q = queue.Queue(maxsize=self.prefetch)
-        self._stop.clear()
+        self._stop = threading.Event()
         self._thread = threading.Thread(target=_producer, args=(iter(self.dataset), self._q, self._stop), daemon=True)
         self._thread.start()
         return self

@@ -166,3 +166,25 @@ def test_image_stream_fails_fast_on_empty_tars(tmp_path, sample_dir):
     # resuming past the last sample of the only real tar is not mistaken for an empty pass
     it = ds._image_stream(ImageCursor(1, 6, 0))
     assert next(it)[2].sample_index == 0
+
+
+def test_loader_reiteration_stops_previous_producer(sample_dir):
+    loader = PackedLoader(_dataset(sample_dir, image_prob=0.0), device="cpu", dtype=torch.float32, seed=0)
+    next(iter(loader))
+    first = loader._thread
+    next(iter(loader))  # restarts: the first producer must end instead of filling its old queue forever
+    first.join(timeout=10)
+    assert not first.is_alive()
+    loader.close()
+    assert not loader._thread.is_alive()
+
+
+def test_loader_surfaces_producer_errors():
+    class Broken:
+        def __iter__(self):
+            raise OSError("disk gone")
+            yield  # pragma: no cover
+    loader = PackedLoader(Broken(), device="cpu")
+    with pytest.raises(OSError, match="disk gone"):
+        next(iter(loader))
+    loader.close()
