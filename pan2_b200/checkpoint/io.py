@@ -404,14 +404,33 @@ def mark_complete(root: str, step: int) -> None:
         f.write(f"{step}\n")
 
 
+def clear_complete(root: str) -> None:
+    """Drop the marker before a folder is rewritten, so an interrupted rewrite reads as incomplete."""
+    try:
+        os.remove(os.path.join(root, COMPLETE))
+    except FileNotFoundError:
+        pass
+
+
 def cleanup_old(output_dir: str, keep: int) -> List[str]:
-    """Keep the ``keep`` most recent checkpoints; returns the removed folders."""
+    """Keep the ``keep`` most recent complete checkpoints; returns the removed folders.
+
+    Only complete checkpoints count toward ``keep``.  Incomplete folders older than the newest
+    complete one (left by interrupted saves) are removed too; incomplete folders newer than it (an
+    interrupted save of a run that was rolled back to an earlier step) are left in place, since a
+    resumed run skips them and rewrites them when it reaches their step again."""
     if keep <= 0:
         return []
     ck = list_checkpoints(output_dir)
+    complete = [(s, d) for s, d in ck if is_complete(d)]
+    if not complete:
+        return []
+    kept = {d for _, d in complete[-keep:]}
+    newest = complete[-1][0]
     removed = []
-    while len(ck) > keep:
-        _, d = ck.pop(0)
+    for s, d in ck:
+        if d in kept or s > newest:
+            continue
         shutil.rmtree(d, ignore_errors=True)
         removed.append(d)
     return removed

@@ -217,6 +217,7 @@ class Trainer:
         root = self.checkpoint_dir(step)
         if self.is_main:
             os.makedirs(root, exist_ok=True)
+            ckpt.clear_complete(root)  # a folder being rewritten (after a rollback) is incomplete until done
         self._barrier()
         ckpt.save_engine(self.engine, root)
         _, _, state_file = ckpt.checkpoint_layout(root)
@@ -262,8 +263,15 @@ class Trainer:
 
     def load_checkpoint(self, load_dataloader_state: bool = True) -> Optional[str]:
         """Resume from the latest complete checkpoint, falling back to the one before it."""
-        cks = ckpt.list_checkpoints(self.cfg.output_dir)
+        every = ckpt.list_checkpoints(self.cfg.output_dir)
+        cks = [(s, d) for s, d in every if ckpt.is_complete(d)]
+        skipped = [d for s, d in every if not ckpt.is_complete(d) and (not cks or s > cks[-1][0])]
+        if skipped:
+            log.warning(f"skipping incomplete checkpoint folder(s) {skipped} (interrupted saves)")
         if not cks:
+            if every:
+                raise ValueError(f"no complete checkpoint in {self.cfg.output_dir}: {[d for _, d in every]} "
+                                 f"all lack the {ckpt.COMPLETE} marker")
             return None
         last = cks[-1][1]
         prev = cks[-2][1] if len(cks) > 1 else None

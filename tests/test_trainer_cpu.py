@@ -109,6 +109,39 @@ def test_corrupt_latest_checkpoint_falls_back(data_dir, tmp_path):
     assert [h["step"] for h in rest] == [2, 3, 4]  # resumed from checkpoint-2
 
 
+
+def test_checkpoint_retention_counts_complete_folders_only(tmp_path):
+    from pan2_b200.checkpoint import io as ckpt
+    out = tmp_path / "r"
+
+    def folder(step, complete):
+        d = out / f"checkpoint-{step}"
+        d.mkdir(parents=True)
+        if complete:
+            ckpt.mark_complete(str(d), step)
+        return d
+    folder(1, True)
+    folder(2, False)  # interrupted save older than the newest complete one: garbage
+    folder(3, True)
+    folder(9, False)  # interrupted save of a run that was later rolled back to step 3
+    folder(5, True)   # the save that just finished
+    removed = ckpt.cleanup_old(str(out), keep=1)
+    assert sorted(os.path.basename(d) for d in removed) == ["checkpoint-1", "checkpoint-2", "checkpoint-3"]
+    assert sorted(os.listdir(out)) == ["checkpoint-5", "checkpoint-9"]
+    # a rewrite drops the marker first, so an interrupted rewrite reads as incomplete
+    ckpt.clear_complete(str(out / "checkpoint-5"))
+    assert not ckpt.is_complete(str(out / "checkpoint-5"))
+    ckpt.clear_complete(str(out / "checkpoint-5"))  # no marker: nothing to do
+
+
+@pytest.mark.timeout(900)
+def test_resume_skips_incomplete_newer_folder(data_dir, tmp_path):
+    _train(_cfg(data_dir, tmp_path / "g", max_steps=2, save_interval=2))
+    (tmp_path / "g" / "checkpoint-7" / "transformer").mkdir(parents=True)  # an interrupted save
+    tr, rest = _train(_cfg(data_dir, tmp_path / "g", max_steps=3, save_interval=100))
+    assert [h["step"] for h in rest] == [2]  # resumed from checkpoint-2, not the incomplete checkpoint-7
+
+
 def _dead_peer(rank, port, path):
     from pan2_b200.parallel.layout import init_parallel_layout
     os.environ.update(MASTER_ADDR="127.0.0.1", MASTER_PORT=str(port), RANK=str(rank), WORLD_SIZE="2")
