@@ -63,8 +63,13 @@ def write_video(video: torch.Tensor, path: str, fps: float = 24, crf=None, prese
         for i, f in enumerate(frames):
             Image.fromarray(f).save(os.path.join(folder, f"{i:05d}.png"))
         return folder
+    # written under a temporary name and renamed, so an interrupted write never leaves a truncated
+    # file under the final name (the resume check treats a present, non-empty file as finished)
+    stem, ext = os.path.splitext(path)
+    tmp = f"{stem}.partial{ext}"
     if frames.shape[0] == 1:
-        imageio.imwrite(path, frames[0])
+        imageio.imwrite(tmp, frames[0])
+        os.replace(tmp, path)
         return path
     opts, params = {}, []
     if crf is not None:
@@ -76,7 +81,8 @@ def write_video(video: torch.Tensor, path: str, fps: float = 24, crf=None, prese
         opts["ffmpeg_params"] = params
     if pix_fmt is not None:
         opts["pixelformat"] = pix_fmt
-    imageio.mimwrite(path, frames, fps=fps, **opts)
+    imageio.mimwrite(tmp, frames, fps=fps, **opts)
+    os.replace(tmp, path)
     return path
 
 
@@ -90,8 +96,9 @@ def save_settings(args, video_path: str, task: str) -> str:
     doc = {"model": MODEL_LABEL, "task": task, "video": video_path, "written_at": datetime.datetime.now().isoformat(),
            "arguments": {k: plain(v) for k, v in vars(args).items() if not k.startswith("_") and not callable(v)}}
     out = os.path.splitext(video_path)[0] + "_config.json"
-    with open(out, "w", encoding="utf-8") as f:
+    with open(out + ".partial", "w", encoding="utf-8") as f:
         json.dump(doc, f, indent=2, ensure_ascii=False)
+    os.replace(out + ".partial", out)
     return out
 
 
@@ -232,9 +239,11 @@ def generate(args, sp_group=None, sp_rank: int = 0) -> List[str]:
         else:
             from safetensors.torch import save_file
             target = os.path.splitext(path)[0] + ".latent.safetensors"
-            save_file({"latent": out.latents[0].contiguous()}, target)
-            with open(path, "wb") as f:  # placeholder so resume checks see a finished output
+            save_file({"latent": out.latents[0].contiguous()}, target + ".partial")
+            os.replace(target + ".partial", target)
+            with open(path + ".partial", "wb") as f:  # placeholder so resume checks see a finished output
                 f.write(b"latent-only output; see " + os.path.basename(target).encode())
+            os.replace(path + ".partial", path)
         if args.save_settings:
             job.output_path = path
             save_settings(job, path, job.task)

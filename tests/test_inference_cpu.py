@@ -214,4 +214,24 @@ def test_generate_cli_latent_output_and_skip(tmp_path):
     assert lat.shape == (48, 2, 4, 4) and torch.isfinite(lat).all()
     cfg = json.loads((tmp_path / "out" / "t2v_one_config.json").read_text())
     assert cfg["arguments"]["seed"] == 42
+    assert not [f for f in os.listdir(tmp_path / "out") if ".partial" in f]  # every file renamed into place
     assert main(argv + ["--skip_existing"]) == []
+
+
+def test_write_video_renames_a_finished_file_into_place(tmp_path, monkeypatch):
+    import sys
+    import types
+    from pan2_b200.generate import write_video
+    seen = []
+
+    def mimwrite(path, frames, fps, **opts):
+        seen.append(path)
+        assert not os.path.exists(tmp_path / "v.mp4")  # the final name appears only once the write is done
+        with open(path, "wb") as f:
+            f.write(b"x" * len(frames))
+    fake = types.SimpleNamespace(mimwrite=mimwrite, imwrite=lambda path, frame: open(path, "wb").write(b"y"))
+    monkeypatch.setitem(sys.modules, "imageio", types.ModuleType("imageio"))
+    sys.modules["imageio"].__dict__.update(vars(fake))
+    out = write_video(torch.rand(3, 4, 8, 8), str(tmp_path / "v.mp4"))
+    assert out == str(tmp_path / "v.mp4") and seen == [str(tmp_path / "v.partial.mp4")]
+    assert os.listdir(tmp_path) == ["v.mp4"] and (tmp_path / "v.mp4").read_bytes() == b"xxxx"
