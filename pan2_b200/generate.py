@@ -185,10 +185,16 @@ def prepare_jobs(args, task: str) -> List[argparse.Namespace]:
 def build_pipeline(args, sp_group=None):
     from .models.text_encoder import HashTextEncoder, QwenCaptionCodec
     from .pipelines.video import PanVideoPipeline, build_inference_model, load_transformer_weights
+    from .inference.offload import choose_offload
     dev = torch.device("cuda", torch.cuda.current_device()) if torch.cuda.is_available() else torch.device("cpu")
     arch = architecture(args.transformer_config_overrides)
     dtype = {"bf16": torch.bfloat16, "fp32": torch.float32}[args.dtype]
-    model = build_inference_model(arch, dev, dtype=dtype, seed=0)
+    offload = choose_offload(args.offload, dit_bytes(arch, dtype), dev)
+    if args.compile:
+        _log("--compile has no effect: the transformer blocks run hand-written kernels")
+    # with offloading the models are built on the CPU and moved to the GPU while they run
+    home = dev if offload == "none" else torch.device("cpu")
+    model = build_inference_model(arch, home, dtype=dtype, seed=0)
     if args.checkpoint_path:
         load_transformer_weights(model, args.checkpoint_path)
         _log(f"transformer weights loaded from {args.checkpoint_path}")
@@ -196,13 +202,24 @@ def build_pipeline(args, sp_group=None):
     if args.text_encoder == "hash":
         te = HashTextEncoder(embed_dim=int(arch.get("text_embed_dim", 4096)), max_caption_tokens=max_len)
     else:
-        te = QwenCaptionCodec(args.text_encoder_path, device=dev, hidden_state_skip_layer=args.text_encoder_hidden_state_skip_layer,
+        te = QwenCaptionCodec(args.text_encoder_path, device=home, hidden_state_skip_layer=args.text_encoder_hidden_state_skip_layer,
                               max_caption_tokens=max_len)
     vae = None
     if args.output_type == "video":
         from .models.vae import WanVAE
-        vae = WanVAE(args.wan_vae_checkpoint, device=dev)
-    return PanVideoPipeline(model, te, vae, device=dev, sp_group=sp_group)
+        vae = WanVAE(args.wan_vae_checkpoint, device=home)
+    pipe = PanVideoPipeline(model, te, vae, device=dev, sp_group=sp_group)
+    pipe.configure_runtime(offload=offload, prefetch=args.offload_prefetch)
+    _log(f"offload={offload} prefetch={args.offload_prefetch}")
+    return pipe
+
+
+def dit_bytes(arch: dict, dtype) -> int:
+    """Bytes of the DiT's weights in ``dtype`` (counted on the meta device, nothing allocated)."""
+    from .models.transformer import PanVideoDiffusionTransformer
+    with torch.device("meta"):
+        m = PanVideoDiffusionTransformer(**arch)
+    return sum(p.numel() for p in m.parameters()) * torch.empty(0, dtype=dtype).element_size()
 
 
 def generate(args, sp_group=None, sp_rank: int = 0) -> List[str]:
@@ -285,8 +302,15 @@ def build_arg_parser() -> argparse.ArgumentParser:
     p.add_argument("--num_inference_steps", default=None, type=int)
     p.add_argument("--video_length", default=241, type=int)
     p.add_argument("--fps", default=24.0, type=float)
-    p.add_argument("--offload", default="none", choices=("none", "auto"),
-                   help="kept for command-line compatibility: the bf16 29B model (58 GB) always fits a B200")
+    p.add_argument("--offload", default="auto", choices=("auto", "none", "models", "blocks"),
+                   help="none: every model on the GPU; models: text encoder, DiT and VAE wait on the CPU between "
+                        "uses; blocks: also stream the DiT's blocks to the GPU while it runs; auto (default): blocks "
+                        "only when the DiT's weights do not fit in free GPU memory, else none")
+    p.add_argument("--offload_prefetch", default=True, type=str_to_bool, nargs="?", const=True,
+                   help="with --offload blocks: copy the next block on a side stream while the current one runs")
+    p.add_argument("--compile", default=False, type=str_to_bool, nargs="?", const=True,
+                   help="accepted for command-line compatibility; the blocks already run hand-written kernels, "
+                        "so there is nothing to compile")
     p.add_argument("--dtype", default="bf16", choices=["bf16", "fp32"])
     p.add_argument("--seed", default=42, type=int)
     p.add_argument("--image_path", default=None, type=str, nargs="+")

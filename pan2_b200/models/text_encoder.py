@@ -73,6 +73,11 @@ class QwenCaptionCodec(CaptionCodec):
         self._prefix: Optional[int] = None
         self.embed_dim = embed_dim or int(getattr(getattr(self.model, "config", None), "hidden_size", 4096))
 
+    def to(self, device) -> "QwenCaptionCodec":
+        """Move the language model (generation offloading parks it on the CPU between prompts)."""
+        self.model.to(device)
+        return self
+
     # ---- tokens
     def _ids(self, caption: str, max_length: Optional[int]) -> torch.Tensor:
         out = self.tokenizer.apply_chat_template(chat_for(caption), add_generation_prompt=True, tokenize=True,

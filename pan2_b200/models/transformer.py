@@ -426,9 +426,10 @@ class PanVideoDiffusionTransformer(nn.Module):
         """Inference over a packed batch: velocity rows ``[n_video, prod(patch) * C_out]`` for the video
         tokens (concat order).  ``skip_layers`` drops joint blocks (the STG weak prediction)."""
         x, ln_stats, vec = self.embed_packed(hidden_states, timestep, text_states, meta)
-        for i, block in enumerate(self.blocks):
-            if i in skip_layers:
-                continue
+        order = [i for i in range(len(self.blocks)) if i not in skip_layers]
+        streamer = getattr(self, "block_streamer", None)  # set when the blocks live in host memory
+        blocks = streamer.run(self.blocks, order) if streamer is not None else ((i, self.blocks[i]) for i in order)
+        for _, block in blocks:
             x, ln_stats = block.forward_packed(x, ln_stats, vec, meta)
         return self.output_head.forward_packed(x, vec, ln_stats, [0] + _cumsum(meta.video_lens), meta.n_video)
 

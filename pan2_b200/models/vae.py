@@ -34,6 +34,13 @@ class WanVAE:
         self.mean = torch.tensor(cfg.latents_mean, device=self.device, dtype=dtype).view(1, -1, 1, 1, 1)
         self.std = torch.tensor(cfg.latents_std, device=self.device, dtype=dtype).view(1, -1, 1, 1, 1)
 
+    def to(self, device) -> "WanVAE":
+        """Move the VAE and its latent statistics (generation offloading parks it on the CPU)."""
+        self.device = torch.device(device)
+        self.vae.to(self.device)
+        self.mean, self.std = self.mean.to(self.device), self.std.to(self.device)
+        return self
+
     @torch.no_grad()
     def encode_image(self, image, height: int, width: int) -> torch.Tensor:
         import torchvision.transforms.functional as TF

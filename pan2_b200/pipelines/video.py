@@ -155,6 +155,34 @@ class PanVideoPipeline:
         self.runner = PackedDiTRunner(transformer, self.device, sp_group)
         self.defaults = dict(flow_shift=flow_shift, guidance_scale=guidance_scale,
                              num_inference_steps=num_inference_steps)
+        self.offload = "none"
+        self._dit = transformer   # what moves between host and device in the models / blocks modes
+
+    def configure_runtime(self, offload: str = "none", prefetch: bool = True) -> None:
+        """Offloading, set once after construction (reference: pan_video_pipeline.py:111-158).
+
+        ``none``: every model stays on the device.  ``models``: the text encoder, the DiT and the VAE
+        wait on the CPU and each moves to the device only while it runs.  ``blocks``: as ``models``,
+        and the DiT's blocks stay in host memory and are streamed to the device block by block
+        while it runs (:class:`~pan2_b200.inference.offload.BlockStreamer`; ``prefetch`` overlaps
+        the copy of the next block with the current one on a side stream)."""
+        from ..inference.offload import OFFLOAD_MODES, NonBlockParts, enable_block_streaming
+        if offload not in OFFLOAD_MODES:
+            raise ValueError(f"offload must be one of {OFFLOAD_MODES}, got {offload!r}")
+        if self.offload != "none":
+            raise ValueError("configure_runtime runs once per pipeline")
+        self.offload = offload
+        if offload == "blocks":
+            enable_block_streaming(self.transformer, self.device, prefetch=prefetch)
+            self._dit = NonBlockParts(self.transformer)
+        if offload != "none":  # every model waits on the CPU until it runs
+            for m in (self.text_encoder, self._dit, self.vae):
+                if m is not None and hasattr(m, "to"):
+                    m.to(torch.device("cpu"))
+
+    def _resident(self, *models):
+        from ..inference.offload import resident
+        return resident(self.offload != "none", self.device, *models)
 
     # ------------------------------------------------------------------ inputs
     def _caption_rows(self, texts: List[str]) -> List[torch.Tensor]:
@@ -215,24 +243,26 @@ class PanVideoPipeline:
         use_cfg = guidance_scale > 1
 
         # ---- text
-        if prompt_embeds is not None:
-            pos = [t.to(self.device) for t in prompt_embeds]
-        else:
-            prompts = [prompt] if isinstance(prompt, str) else list(prompt)
-            pos = self._caption_rows(prompts)
-        B = len(pos)
-        neg = []
-        if use_cfg:
-            if negative_prompt_embeds is not None:
-                neg = [t.to(self.device) for t in negative_prompt_embeds]
+        encode = prompt_embeds is None or (use_cfg and negative_prompt_embeds is None)
+        with self._resident(self.text_encoder if encode else None):
+            if prompt_embeds is not None:
+                pos = [t.to(self.device) for t in prompt_embeds]
             else:
-                negs = (list(negative_prompt) if isinstance(negative_prompt, (list, tuple))
-                        else [negative_prompt or ""] * B)
-                if len(negs) != B:
-                    raise ValueError(f"got {len(negs)} negative prompts for {B} prompts")
-                neg = self._caption_rows(negs)
-            if len(neg) != B:
-                raise ValueError("one negative embedding per prompt is required")
+                prompts = [prompt] if isinstance(prompt, str) else list(prompt)
+                pos = self._caption_rows(prompts)
+            B = len(pos)
+            neg = []
+            if use_cfg:
+                if negative_prompt_embeds is not None:
+                    neg = [t.to(self.device) for t in negative_prompt_embeds]
+                else:
+                    negs = (list(negative_prompt) if isinstance(negative_prompt, (list, tuple))
+                            else [negative_prompt or ""] * B)
+                    if len(negs) != B:
+                        raise ValueError(f"got {len(negs)} negative prompts for {B} prompts")
+                    neg = self._caption_rows(negs)
+                if len(neg) != B:
+                    raise ValueError("one negative embedding per prompt is required")
         samples = neg + pos
         dt = self.runner.dtype
         text_rows = torch.cat([t.to(dt) for t in samples], 0)
@@ -260,7 +290,8 @@ class PanVideoPipeline:
         if reference_image is not None and reference_latents is None:
             if self.vae is None:
                 raise ValueError("image conditioning needs a VAE (or pass reference_latents)")
-            reference_latents = self.vae.encode_image(reference_image, video_height, video_width)
+            with self._resident(self.vae):
+                reference_latents = self.vae.encode_image(reference_image, video_height, video_width)
         cond = self._condition(B, grid, reference_latents if i2v else None)
         runner = self.runner
         n_samp = len(samples)
@@ -269,39 +300,41 @@ class PanVideoPipeline:
         cond_all = cond.repeat(2, 1, 1) if use_cfg else cond
         frame0 = (grid[1] // ps[1]) * (grid[2] // ps[2])  # tokens of latent frame 0 (temporal patch 1)
         step_ms = []
-        for i, t in enumerate(timesteps):
-            if time_steps and self.device.type == "cuda":
-                e0, e1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
-                e0.record()
-            x_in = x.repeat(2, 1, 1) if use_cfg else x
-            tb = t.reshape(1).expand(n_samp).float()
-            v = runner.predict(p, x_in, cond_all, tb, text_rows)
-            if use_cfg:
-                v_neg, v_pos = v[:B], v[B:]
-                if guided:
-                    def weak():
-                        return runner.predict(p_pos, x, cond, tb[:B], torch.cat([r.to(dt) for r in pos]),
-                                              skip_layers=skip)
-                    v = apply_guidance(v_neg, v_pos, guidance_scale, step_index=i, plan=plan, weak_predict_fn=weak)
-                else:
-                    v = v_neg + guidance_scale * (v_pos - v_neg)
-                if i2v and i2v_skip_first_latent_cfg and plan.active(i):
-                    v = v.clone()
-                    v[:, :frame0] = v_pos[:, :frame0]
-            if i == 0 and first_step_velocity_scale != 1.0:
-                v = v * first_step_velocity_scale
-            x = sched.step(v, t, x)
-            if time_steps and self.device.type == "cuda":
-                e1.record()
-                e1.synchronize()
-                step_ms.append(e0.elapsed_time(e1))
+        with self._resident(self._dit):
+            for i, t in enumerate(timesteps):
+                if time_steps and self.device.type == "cuda":
+                    e0, e1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+                    e0.record()
+                x_in = x.repeat(2, 1, 1) if use_cfg else x
+                tb = t.reshape(1).expand(n_samp).float()
+                v = runner.predict(p, x_in, cond_all, tb, text_rows)
+                if use_cfg:
+                    v_neg, v_pos = v[:B], v[B:]
+                    if guided:
+                        def weak():
+                            return runner.predict(p_pos, x, cond, tb[:B], torch.cat([r.to(dt) for r in pos]),
+                                                  skip_layers=skip)
+                        v = apply_guidance(v_neg, v_pos, guidance_scale, step_index=i, plan=plan, weak_predict_fn=weak)
+                    else:
+                        v = v_neg + guidance_scale * (v_pos - v_neg)
+                    if i2v and i2v_skip_first_latent_cfg and plan.active(i):
+                        v = v.clone()
+                        v[:, :frame0] = v_pos[:, :frame0]
+                if i == 0 and first_step_velocity_scale != 1.0:
+                    v = v * first_step_velocity_scale
+                x = sched.step(v, t, x)
+                if time_steps and self.device.type == "cuda":
+                    e1.record()
+                    e1.synchronize()
+                    step_ms.append(e0.elapsed_time(e1))
         lat = torch.stack([unpatchify(x[b].float(), tuple(s // q for s, q in zip(grid, ps)), ps, WAN22_LATENT_CHANNELS)
                            for b in range(B)])
         videos = None
         if output_type == "video":
             if self.vae is None:
                 raise ValueError("no VAE: use output_type='latent'")
-            videos = self.vae.decode(lat)
+            with self._resident(self.vae):
+                videos = self.vae.decode(lat)
         return PipelineOutput(videos=videos, latents=lat, step_ms=step_ms, seed=int(seed))
 
 

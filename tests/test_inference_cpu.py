@@ -216,6 +216,10 @@ def test_generate_cli_latent_output_and_skip(tmp_path):
     assert cfg["arguments"]["seed"] == 42
     assert not [f for f in os.listdir(tmp_path / "out") if ".partial" in f]  # every file renamed into place
     assert main(argv + ["--skip_existing"]) == []
+    # the reference's runtime flags: block streaming (no prefetch) and --compile give the same latents
+    argv2 = [a if a != str(tmp_path / "out") else str(tmp_path / "out2") for a in argv]
+    again = main(argv2 + ["--offload", "blocks", "--offload_prefetch", "false", "--compile"])
+    assert torch.equal(load_file(again[0])["latent"], lat)
 
 
 def test_write_video_renames_a_finished_file_into_place(tmp_path, monkeypatch):
@@ -235,3 +239,82 @@ def test_write_video_renames_a_finished_file_into_place(tmp_path, monkeypatch):
     out = write_video(torch.rand(3, 4, 8, 8), str(tmp_path / "v.mp4"))
     assert out == str(tmp_path / "v.mp4") and seen == [str(tmp_path / "v.partial.mp4")]
     assert os.listdir(tmp_path) == ["v.mp4"] and (tmp_path / "v.mp4").read_bytes() == b"xxxx"
+
+
+class _CountingTextEncoder:
+    """Text encoder stand-in that records where it was when it ran (offloading moves it)."""
+
+    def __init__(self, dim=64):
+        from pan2_b200.models.text_encoder import HashTextEncoder
+        self.inner = HashTextEncoder(embed_dim=dim)
+        self.moves = []
+
+    def to(self, device):
+        self.moves.append(str(torch.device(device)))
+        return self
+
+    def encode(self, texts, device=None):
+        return self.inner.encode(texts, device)
+
+
+def _pipe_latents(offload, prefetch=True, stg=False):
+    from pan2_b200.pipelines.video import PanVideoPipeline
+    torch.manual_seed(0)
+    m = _model()
+    te = _CountingTextEncoder()
+    pipe = PanVideoPipeline(m, te, device="cpu", num_inference_steps=3)
+    if offload is not None:
+        pipe.configure_runtime(offload=offload, prefetch=prefetch)
+    extra = dict(stg_scale=0.5, stg_skip_layers=[1]) if stg else {}
+    out = pipe(prompt="a red ball", negative_prompt="blurry", video_length=9, video_height=128, video_width=128,
+               seed=3, output_type="latent", guidance_scale=4.0, **extra)
+    return out.latents, te, m
+
+
+@pytest.mark.parametrize("stg", [False, True])
+def test_offload_modes_give_identical_samples(stg):
+    base, _, _ = _pipe_latents(None, stg=stg)
+    for mode in ("none", "models", "blocks"):
+        lat, te, m = _pipe_latents(mode, stg=stg)
+        assert torch.equal(lat, base), mode
+        if mode != "none":
+            assert te.moves[0] == "cpu" and te.moves[1:] == ["cpu", "cpu"]  # parked, then in and out once
+        if mode == "blocks":
+            s = m.block_streamer
+            # after the run every block points at its host buffer again (nothing holds slot memory)
+            for i, blk in enumerate(m.blocks):
+                host = s.host[i]
+                for prm in blk.parameters():
+                    ptr = prm.data_ptr()
+                    assert host.data_ptr() <= ptr < host.data_ptr() + host.numel()
+
+
+def test_block_streamer_follows_the_run_order():
+    from pan2_b200.inference.offload import BlockStreamer
+    blocks = torch.nn.ModuleList([torch.nn.Linear(4, 4) for _ in range(4)])
+    ref = [b.weight.detach().clone() for b in blocks]
+    s = BlockStreamer(blocks, "cpu", prefetch=True)  # prefetch needs CUDA; on the CPU it copies in place
+    seen = []
+    for i, blk in s.run(blocks, [0, 2, 3]):
+        slot = s.slots[0]
+        assert slot.data_ptr() <= blk.weight.data_ptr() < slot.data_ptr() + slot.numel()
+        assert torch.equal(blk.weight, ref[i])
+        seen.append(i)
+    assert seen == [0, 2, 3]
+    with pytest.raises(RuntimeError):
+        for i, blk in s.run(blocks, [1, 2]):
+            raise RuntimeError("a block failed")
+    assert all(torch.equal(b.weight, r) for b, r in zip(blocks, ref))
+    assert all(s.host[i].data_ptr() <= b.weight.data_ptr() < s.host[i].data_ptr() + s.host[i].numel()
+               for i, b in enumerate(blocks))
+
+
+def test_choose_offload(monkeypatch):
+    from pan2_b200.inference.offload import choose_offload
+    assert choose_offload("auto", 10 ** 12, "cpu") == "none"
+    assert choose_offload("models", 1, "cpu") == "models"
+    with pytest.raises(ValueError):
+        choose_offload("disk", 1, "cpu")
+    monkeypatch.setattr(torch.cuda, "mem_get_info", lambda device=None: (100, 200))
+    assert choose_offload("auto", 99, "cuda:0") == "none"
+    assert choose_offload("auto", 100, "cuda:0") == "blocks"
