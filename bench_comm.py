@@ -259,5 +259,6 @@ def main():
         dist.barrier()
         dist.destroy_process_group()
 
+
 if __name__ == "__main__":
     main()
