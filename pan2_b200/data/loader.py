@@ -34,6 +34,9 @@ class LoaderMeta:
     dataloader_state: DataloaderState
 
 
+CONDITIONING_SCHEMAS = ("token_concat", "channel_concat")
+
+
 def _producer(it: Iterator[PackedPlan], q: "queue.Queue", stop: threading.Event):
     try:
         for plan in it:
@@ -66,7 +69,14 @@ class PackedLoader:
     def __init__(self, dataset: PackingDataset, *, device, dtype=torch.bfloat16, prefetch: int = 2, seed: int = 0,
                  T: int = 1000, timestep_distribution: str = "lognorm", timestep_loc: float = 0.0,
                  timestep_scale: float = 1.0, shift: float = 1.0, shift_mode: str = "fixed",
-                 shift_kwargs: Optional[Dict] = None, start_index: int = 0):
+                 shift_kwargs: Optional[Dict] = None, start_index: int = 0,
+                 conditioning_schema: str = "channel_concat"):
+        if conditioning_schema not in CONDITIONING_SCHEMAS:
+            raise ValueError(f"conditioning_schema must be one of {CONDITIONING_SCHEMAS}, got {conditioning_schema!r}")
+        # channel_concat: every frame noised, [clean prefix frames | prefix mask] appended as 49 extra
+        # channels (2 * 48 + 1 = 97 inputs); token_concat: the 48 noised channels alone
+        # (reference: dataset/packed_dataloader.py:388-418)
+        self.channel_concat = conditioning_schema == "channel_concat"
         self.dataset = dataset
         self.device = torch.device(device)
         self.dtype = dtype
@@ -127,12 +137,14 @@ class PackedLoader:
             noise = torch.randn(x0.shape, device=dev, generator=self.dev_rng)
             xt = interpolate(x0.unsqueeze(0), noise.unsqueeze(0), t_dev[i:i + 1], dim=0, T=self.T)[0]
             C, Tl, H, W = x0.shape
-            cond = x0.new_zeros(C + 1, Tl, H, W)
-            k = min(item.prefix_frames, Tl)
-            if k > 0:
-                cond[:C, :k] = x0[:, :k]
-                cond[C, :k] = 1.0
-            inputs.append(patchify(torch.cat([xt, cond], 0), (pt, ph, pw)))
+            if self.channel_concat:
+                cond = x0.new_zeros(C + 1, Tl, H, W)
+                k = min(item.prefix_frames, Tl)
+                if k > 0:
+                    cond[:C, :k] = x0[:, :k]
+                    cond[C, :k] = 1.0
+                xt = torch.cat([xt, cond], 0)
+            inputs.append(patchify(xt, (pt, ph, pw)))
             targets.append(patchify(noise - x0, (pt, ph, pw)).t())
         hidden = torch.cat(inputs, 1).to(self.dtype)[:, :, None, None].contiguous()
         target = torch.cat(targets, 0).to(self.dtype).contiguous()

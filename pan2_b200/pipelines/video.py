@@ -280,6 +280,11 @@ class PanVideoPipeline:
             skip = self.transformer.validate_stg_layers(stg_skip_layers)
 
         # ---- latents, condition
+        if int(self.transformer.in_channels) != 2 * WAN22_LATENT_CHANNELS + 1:
+            # the sampler feeds [noisy latent | condition | condition mask] (reference:
+            # pan_video_pipeline.py:356-359): a token_concat-trained transformer does not fit it
+            raise ValueError(f"sampling needs a {2 * WAN22_LATENT_CHANNELS + 1}-channel (channel_concat) "
+                             f"transformer, got in_channels={self.transformer.in_channels}")
         grid = latent_grid(video_length, video_height, video_width, self.transformer.patch_size)
         if seed in (None, -1):
             seed = random.randint(100000, 999999)

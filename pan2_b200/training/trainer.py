@@ -51,6 +51,7 @@ from .step import StepRunner
 
 IMAGE_TAR_SHUFFLE_SEED = 1234
 WAN22_SPATIAL_RATIO = 16
+WAN22_LATENT_CHANNELS = 48
 
 log = logging.getLogger("pan2_b200.train")
 
@@ -95,8 +96,23 @@ def build_caption_codec(cfg: TrainingConfig, device, embed_dim: int = 4096) -> C
 
 
 def architecture_from_config(cfg: TrainingConfig) -> dict:
+    """The transformer architecture of a run: the defaults, the YAML overrides, and the input /
+    output widths the conditioning schema implies (reference: train.py:572-601)."""
+    over = translate_architecture_config(cfg.transformer_config_overrides or {})
+    if "zero_init_modulation" in over and bool(over["zero_init_modulation"]) != bool(cfg.zero_init_modulation):
+        log.warning(f"transformer_config_overrides['zero_init_modulation'] ({over['zero_init_modulation']}) is "
+                    f"overridden by the config's zero_init_modulation ({cfg.zero_init_modulation})")
+    schema = getattr(cfg.conditioning_schema, "value", cfg.conditioning_schema)
+    # channel_concat: [noised (48) | clean condition (48) | mask (1)]; token_concat: the noised latent
+    expected = {"in_channels": 2 * WAN22_LATENT_CHANNELS + 1 if schema == "channel_concat" else WAN22_LATENT_CHANNELS,
+                "out_channels": WAN22_LATENT_CHANNELS}
+    for key, want in expected.items():
+        if key in over and int(over[key]) != want:
+            raise ValueError(f"{schema} conditioning with Wan 2.2 latents expects "
+                             f"transformer_config_overrides.{key}={want}, got {over[key]}")
     arch = dict(ARCH_DEFAULTS)
-    arch.update(translate_architecture_config(cfg.transformer_config_overrides or {}))
+    arch.update(over)
+    arch.update(expected)
     arch["zero_init_modulation"] = bool(cfg.zero_init_modulation)
     return arch
 
@@ -174,6 +190,10 @@ class Trainer:
                              f"spatial ratio {WAN22_SPATIAL_RATIO}")
         if pt != 1:
             raise ValueError("packed training needs a temporal patch size of 1")
+        lat_h, lat_w = cfg.video_height // WAN22_SPATIAL_RATIO, cfg.video_width // WAN22_SPATIAL_RATIO
+        if lat_h % ph or lat_w % pw:
+            raise ValueError(f"latent grid {(lat_h, lat_w)} of {cfg.video_height}x{cfg.video_width} video is not "
+                             f"divisible by the transformer patch size {tuple(self.arch['patch_size'])}")
         budgets = Budgets(joint=cfg.packed_joint_token_budget, video=cfg.packed_video_token_budget,
                           caption=cfg.packed_caption_token_budget,
                           text_encoder=cfg.packed_caption_token_budget + 64 * cfg.packed_dataloader_max_num_seq,
@@ -202,7 +222,8 @@ class Trainer:
                             timestep_loc=cfg.flow_lognorm_loc, timestep_scale=cfg.flow_lognorm_scale,
                             shift=cfg.train_timestep_shift, shift_mode=str(cfg.train_timestep_shift_mode.value),
                             shift_kwargs=dict(rescale_factor=cfg.train_timestep_rescale_factor,
-                                              max_shift=cfg.train_timestep_max_shift))
+                                              max_shift=cfg.train_timestep_max_shift),
+                            conditioning_schema=str(getattr(cfg.conditioning_schema, "value", cfg.conditioning_schema)))
 
     # ------------------------------------------------------------------ checkpoints
     def checkpoint_dir(self, step: int) -> str:

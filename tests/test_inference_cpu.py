@@ -318,3 +318,12 @@ def test_choose_offload(monkeypatch):
     monkeypatch.setattr(torch.cuda, "mem_get_info", lambda device=None: (100, 200))
     assert choose_offload("auto", 99, "cuda:0") == "none"
     assert choose_offload("auto", 100, "cuda:0") == "blocks"
+
+
+def test_sampler_rejects_a_token_concat_transformer():
+    from pan2_b200.pipelines.video import PanVideoPipeline, build_inference_model
+    m = build_inference_model(dict(ARCH, in_channels=48), "cpu", dtype=torch.float32)
+    pipe = PanVideoPipeline(m, device="cpu", num_inference_steps=2)
+    with pytest.raises(ValueError, match="channel_concat"):
+        pipe(prompt_embeds=[torch.randn(5, 64)], video_length=5, video_height=64, video_width=64,
+             output_type="latent", guidance_scale=1.0)

@@ -142,6 +142,37 @@ def test_resume_skips_incomplete_newer_folder(data_dir, tmp_path):
     assert [h["step"] for h in rest] == [2]  # resumed from checkpoint-2, not the incomplete checkpoint-7
 
 
+
+def test_conditioning_schema_sets_and_checks_the_channel_widths(data_dir, tmp_path):
+    from pan2_b200.training.trainer import architecture_from_config
+    tok = architecture_from_config(_cfg(data_dir, tmp_path / "s"))  # the option's default: token_concat
+    assert (tok["in_channels"], tok["out_channels"]) == (48, 48)
+    ch = architecture_from_config(_cfg(data_dir, tmp_path / "s", conditioning_schema="channel_concat"))
+    assert (ch["in_channels"], ch["out_channels"]) == (97, 48)
+    bad = _cfg(data_dir, tmp_path / "s", conditioning_schema="channel_concat",
+               transformer_config_overrides=json.dumps(dict(TINY_OVERRIDES, in_channels=48)))
+    with pytest.raises(ValueError, match="in_channels=97"):
+        architecture_from_config(bad)
+    with pytest.raises(ValueError, match="not divisible by the transformer patch size"):
+        _train(_cfg(data_dir, tmp_path / "s", video_width=208, max_steps=1))  # 13 latent columns, patch 2
+
+
+@pytest.mark.timeout(600)
+def test_token_concat_trains_on_the_noised_latent_alone(data_dir, tmp_path):
+    from pan2_b200.data.loader import PackedLoader
+    from pan2_b200.training.trainer import Trainer
+    for schema, width in (("token_concat", 48), ("channel_concat", 97)):
+        tr = Trainer(_cfg(data_dir, tmp_path / schema, conditioning_schema=schema, max_steps=1),
+                     codec=HashCaptionCodec(embed_dim=64))
+        loader = tr.build_loader(None)
+        batch, _ = next(iter(loader))
+        loader.close()
+        assert batch["hidden_states"].shape[0] == width * 4  # channels x (1 x 2 x 2) patch
+        assert tr.engine.model.patch_embed.proj.in_channels == width
+    with pytest.raises(ValueError, match="conditioning_schema"):
+        PackedLoader(None, device="cpu", conditioning_schema="interleave")
+
+
 def _dead_peer(rank, port, path):
     from pan2_b200.parallel.layout import init_parallel_layout
     os.environ.update(MASTER_ADDR="127.0.0.1", MASTER_PORT=str(port), RANK=str(rank), WORLD_SIZE="2")

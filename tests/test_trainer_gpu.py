@@ -25,7 +25,7 @@ def _cfg(data, out, **over):
             "--packed_dataloader_num_buffers", "2", "--packed_dataloader_num_workers", "2",
             "--video_height", "256", "--video_width", "384", "--output_dir", str(out),
             "--learning_rate", "1e-4", "--warmup_steps", "2", "--log_interval", "1", "--text_encoder", "hash",
-            "--optimizer_offload", "off", "--profile_step", "-1"]
+            "--optimizer_offload", "off", "--profile_step", "-1", "--conditioning_schema", "channel_concat"]
     for k, v in over.items():
         argv += [f"--{k}", str(v)]
     return parse_training_config(argv)
