@@ -133,7 +133,8 @@ class TrainingConfig:
     cp_size: int = opt(1, int, "Ulysses context-parallel degree.", flags=["--cp_size", "--sp_size"])
     hybrid_shard: bool = opt(False, "set", "Shard within a node, replicate across nodes.")
     enable_gradient_checkpointing: bool = opt(True, "switch", "Recompute block activations in backward.")
-    use_dedicated_gradient_checkpointing: bool = opt(False, "set", "Keep attention outputs instead of recomputing them.")
+    use_dedicated_gradient_checkpointing: bool = opt(False, "set", "Selective checkpointing: keep each block's attention "
+                                                     "output from the forward instead of recomputing it.")
     compile_text_encoder: bool = opt(False, "set", "Compile the text encoder (not used: eager CUDA kernels).")
     compile_transformer: bool = opt(False, "set", "Compile the transformer (not used: eager CUDA kernels).")
     compile_optimizer: bool = opt(False, "set", "Compile the optimizer (not used: fused CUDA kernels).")

@@ -91,6 +91,60 @@ def varlen_attention(q: torch.Tensor, k: torch.Tensor, v: torch.Tensor, cu_seqle
     return torch.cat(rows, 0)
 
 
+@torch.no_grad()
+def attention_forward(q: torch.Tensor, k: torch.Tensor, v: torch.Tensor, lens: Sequence[int],
+                      scale: Optional[float] = None):
+    """Forward only: ``(o, lse)`` of :func:`varlen_attention` (``lse`` is ``None`` on the CPU, whose
+    backward recomputes the attention).  With :func:`kept_attention` this is selective activation
+    checkpointing: the checkpointed forward keeps ``o`` / ``lse`` and the recompute before the
+    backward skips the attention forward (reference: train.py:817-845, which keeps the FA4 forward
+    outputs under ``use_dedicated_gradient_checkpointing``)."""
+    D = q.shape[-1]
+    scale = 1.0 / math.sqrt(D) if scale is None else float(scale)
+    lens = [int(n) for n in lens]
+    if q.is_cuda:
+        o, lse = ext().attn_fwd(q.contiguous(), k.contiguous(), v.contiguous(), work_items(lens, 256, q.device),
+                                int(sum(lens)), scale)
+        return o, lse
+    cu = torch.tensor([0] + list(torch.tensor(lens).cumsum(0).tolist()), dtype=torch.int32)
+    return varlen_attention(q, k, v, cu, lens, scale=scale), None
+
+
+class _KeptAttn(torch.autograd.Function):
+    """Attention whose forward output was kept: returns ``o``; the backward is the attention
+    backward of ``q, k, v`` (the fused kernel with the kept ``o`` / ``lse`` on CUDA, a recomputation
+    through the math path on the CPU)."""
+
+    @staticmethod
+    def forward(ctx, q, k, v, o, lse, lens, scale):
+        ctx.save_for_backward(q, k, v, o, *(() if lse is None else (lse,)))
+        ctx.lens, ctx.scale, ctx.has_lse = lens, scale, lse is not None
+        return o.view_as(o)
+
+    @staticmethod
+    def backward(ctx, do):
+        q, k, v, o, *rest = ctx.saved_tensors
+        if ctx.has_lse:
+            items = work_items(ctx.lens, 128, q.device)
+            dq, dk, dv = ext().attn_bwd(do.contiguous(), q, k, v, o, rest[0], items, items, int(sum(ctx.lens)),
+                                        ctx.scale)
+            return dq, dk, dv, None, None, None, None
+        cu = torch.tensor([0] + list(torch.tensor(ctx.lens).cumsum(0).tolist()), dtype=torch.int32)
+        with torch.enable_grad():
+            qd, kd, vd = (t.detach().requires_grad_(True) for t in (q, k, v))
+            out = varlen_attention(qd, kd, vd, cu, ctx.lens, scale=ctx.scale)
+            dq, dk, dv = torch.autograd.grad(out, (qd, kd, vd), do)
+        return dq, dk, dv, None, None, None, None
+
+
+def kept_attention(q: torch.Tensor, k: torch.Tensor, v: torch.Tensor, o: torch.Tensor, lse: Optional[torch.Tensor],
+                   lens: Sequence[int], scale: Optional[float] = None) -> torch.Tensor:
+    """:func:`varlen_attention` of ``q, k, v`` given its kept forward ``(o, lse)`` from
+    :func:`attention_forward` on the same inputs."""
+    scale = 1.0 / math.sqrt(q.shape[-1]) if scale is None else float(scale)
+    return _KeptAttn.apply(q.contiguous(), k.contiguous(), v.contiguous(), o, lse, [int(n) for n in lens], scale)
+
+
 def dense_attention(q: torch.Tensor, k: torch.Tensor, v: torch.Tensor,
                     mask: Optional[torch.Tensor] = None) -> torch.Tensor:
     """Self-attention over ``[B, S, H, D]`` where ``mask`` (``[B, S]``, True = valid) gates both

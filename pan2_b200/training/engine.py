@@ -95,7 +95,7 @@ class BlockCheckpoint(torch.autograd.Function):
             sm.prefetch(sm.units[idx + 1])
         blk = engine.model.blocks[idx]
         with torch.no_grad():
-            y, st = blk.forward_packed(x, ln_stats, vec, engine.meta)
+            y, st = blk.forward_packed(x, ln_stats, vec, engine.meta, attn_fn=engine._attention_keeper(idx))
         sm.release(u)
         ctx.engine, ctx.idx = engine, idx
         stash = engine.stash_checkpoint(idx, x, ln_stats)
@@ -128,7 +128,49 @@ class BlockCheckpoint(torch.autograd.Function):
         sm.attach_grads(u, zero=not engine.accumulating)
         params = [getattr(s.module, s.attr) for s in u.slots]
         with torch.enable_grad():
-            y, _ = blk.forward_packed(x_, ln_stats, vec_, engine.meta)
+            y, _ = blk.forward_packed(x_, ln_stats, vec_, engine.meta, attn_fn=engine._attention_replayer(idx))
+        torch.autograd.backward([y], [gy], inputs=[x_, vec_] + params)
+        sm.reduce_grads(u, accumulate=engine.accumulating)
+        sm.release(u)
+        return None, None, x_.grad, None, vec_.grad
+
+
+class BlockKeepGraph(torch.autograd.Function):
+    """Joint block without activation checkpointing: the forward keeps the block's autograd graph
+    (every activation, and the gathered weights it saved), the backward runs it without
+    recomputing.  Memory grows with every block, so this suits small models only."""
+
+    @staticmethod
+    def forward(ctx, engine: "TrainEngine", idx: int, x, ln_stats, vec):
+        sm = engine.sharded
+        u = sm.units[idx]
+        engine._wait_update(u)
+        sm.gather(u)
+        if idx + 1 < engine.n_blocks:
+            sm.prefetch(sm.units[idx + 1])
+        blk = engine.model.blocks[idx]
+        x_ = x.detach().requires_grad_(True)
+        vec_ = vec.detach().requires_grad_(True)
+        with torch.enable_grad():
+            y, st = blk.forward_packed(x_, ln_stats, vec_, engine.meta)
+        ctx.full = u.full_hi  # the graph holds views of these weights already; rebound in backward
+        sm.release(u)
+        ctx.engine, ctx.idx, ctx.graph = engine, idx, (x_, vec_, y)
+        ctx.mark_non_differentiable(st)
+        return y.detach(), st
+
+    @staticmethod
+    def backward(ctx, gy, _gst):
+        engine, idx = ctx.engine, ctx.idx
+        sm = engine.sharded
+        u = sm.units[idx]
+        x_, vec_, y = ctx.graph
+        ctx.graph = None
+        u.full_hi, full = ctx.full, ctx.full
+        ctx.full = None
+        sm.bind_weights(u, full)
+        sm.attach_grads(u, zero=not engine.accumulating)
+        params = [getattr(s.module, s.attr) for s in u.slots]
         torch.autograd.backward([y], [gy], inputs=[x_, vec_] + params)
         sm.reduce_grads(u, accumulate=engine.accumulating)
         sm.release(u)
@@ -231,6 +273,10 @@ class TrainEngine:
         self._muon_pm = None  # peer-mapped exchange / result regions of distributed Muon
         self._muon_layouts: Dict[int, dict] = {}
         self.stash_in_grads = self.world == 1
+        # activation checkpointing of the joint blocks (set_activation_checkpointing)
+        self.recompute_blocks = True
+        self.keep_attention = False
+        self._kept_attn: Dict[int, tuple] = {}
         self.accum_steps = 1
         self.accumulating = False
         if self.world == 1:  # persistent gradient buffers (they also hold activation checkpoints)
@@ -325,6 +371,42 @@ class TrainEngine:
         self.cp_group, self.cp_size, self.cp_rank = group, int(size), int(rank)
         if self.cp_size > 1 and self.arch.get("num_attention_heads", 32) % self.cp_size:
             raise ValueError(f"cp_size={size} must divide the {self.arch.get('num_attention_heads')} attention heads")
+        if self.cp_size > 1 and self.keep_attention:
+            raise ValueError("keeping attention outputs (use_dedicated_gradient_checkpointing) is not supported "
+                             "with context parallelism (cp_size > 1)")
+
+    def set_activation_checkpointing(self, enabled: bool = True, keep_attention: bool = False) -> None:
+        """``enabled``: recompute each joint block's forward before its backward (the default);
+        off, every block keeps its activations.  ``keep_attention``: selective checkpointing that
+        keeps each block's attention output and log-sum-exp from the forward, so the recompute skips
+        the attention forward (about 0.8 GB per block at 95k tokens of the 29B model); the QKV
+        projection is still recomputed (reference: train.py:817-845)."""
+        self.recompute_blocks = bool(enabled)
+        self.keep_attention = bool(keep_attention) and self.recompute_blocks
+        if self.keep_attention and getattr(self, "cp_size", 1) > 1:
+            raise ValueError("keeping attention outputs (use_dedicated_gradient_checkpointing) is not supported "
+                             "with context parallelism (cp_size > 1)")
+
+    def _attention_keeper(self, idx: int):
+        """Block ``idx``'s attention for the checkpointed forward: records ``(o, lse)``."""
+        if not self.keep_attention:
+            return None
+        from ..ops.attention import attention_forward
+
+        def run(q, k, v, meta):
+            o, lse = attention_forward(q, k, v, meta.joint_lens)
+            self._kept_attn[idx] = (o, lse)
+            return o
+        return run
+
+    def _attention_replayer(self, idx: int):
+        """Block ``idx``'s attention for the recompute: the kept forward, the normal backward."""
+        kept = self._kept_attn.pop(idx, None)
+        if kept is None:
+            return None
+        from ..ops.attention import kept_attention
+        o, lse = kept
+        return lambda q, k, v, meta: kept_attention(q, k, v, o, lse, meta.joint_lens)
 
     def set_accumulation(self, steps: int) -> None:
         """Prepare for ``steps`` micro-batches per optimizer step.  With more than one, gradients
@@ -352,8 +434,10 @@ class TrainEngine:
             sm.prefetch(sm.units[0])
         sm.attach_grads(root, zero=not self.accumulating)
         x, ln_stats, vec = model.embed_packed(batch["hidden_states"], batch["timestep"], batch["text_states"], meta)
+        self._kept_attn = {}
+        block_fn = BlockCheckpoint if self.recompute_blocks else BlockKeepGraph
         for i in range(self.n_blocks):
-            x, ln_stats = BlockCheckpoint.apply(self, i, x, ln_stats, vec)
+            x, ln_stats = block_fn.apply(self, i, x, ln_stats, vec)
         sums = model.head_and_loss(x, ln_stats, vec, batch["target"], meta)
         glob = sums.detach().clone()
         if dist.is_initialized() and dist.get_world_size() > 1:

@@ -139,6 +139,8 @@ class Trainer:
         self.engine = TrainEngine(self.arch, self.device, group=L.shard_group if self.world > 1 else None,
                                   seed=cfg.seed, optim=optim, offload=cfg.optimizer_offload,
                                   activation_bytes_estimate=act, replicate_group=L.replicate_group)
+        self.engine.set_activation_checkpointing(cfg.enable_gradient_checkpointing,
+                                                 cfg.use_dedicated_gradient_checkpointing)
         if cfg.cp_size > 1:
             self.engine.set_context_parallel(L.cp_group, L.cp_size, L.cp_rank)
         self.engine.set_accumulation(cfg.gradient_accumulation_steps)

@@ -88,3 +88,30 @@ def test_multi_rank_step_matches_one_rank(world, hsdp_local):
         d = (a - b).abs().max().item() / (a.abs().max().item() + 1e-8)
         worst = max(worst, (d, k))
     assert worst[0] < 2e-3, worst
+
+
+def test_checkpointing_modes_give_the_same_gradients():
+    """Recompute (default), recompute with the kept attention forward, and no recompute."""
+    from pan2_b200.models.transformer import PanVideoDiffusionTransformer
+    from pan2_b200.training.engine import OptimConfig, TrainEngine
+    arch = dict(TINY_ARCH)
+    with torch.device("meta"):
+        shape_model = PanVideoDiffusionTransformer(**arch)
+    batch, _ = tiny_batch(shape_model, seed=7)
+    res = {}
+    for mode in ((True, False), (True, True), (False, False)):
+        eng = TrainEngine(arch, torch.device("cpu"), seed=11, optim=OptimConfig(lr=1e-2), offload="off")
+        eng.set_activation_checkpointing(*mode)
+        loss = eng.forward_backward(batch)
+        assert not eng._kept_attn  # every kept attention output was consumed by its backward
+        res[mode] = (float(loss), [u.full_grad.float().clone() for u in eng.sharded.units])
+    base_loss, base = res[(True, False)]
+    for mode in ((True, True), (False, False)):
+        loss, grads = res[mode]
+        assert loss == base_loss
+        for a, b in zip(grads, base):  # bf16 gradient buffers: equal within a few ulps
+            assert (a - b).abs().max().item() <= 1e-2 * b.abs().max().item() + 1e-7, mode
+    eng = TrainEngine(arch, torch.device("cpu"), seed=11, offload="off")
+    eng.set_activation_checkpointing(True, True)
+    with pytest.raises(ValueError, match="context parallelism"):
+        eng.set_context_parallel(None, 2, 0)
