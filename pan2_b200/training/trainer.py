@@ -389,6 +389,11 @@ class Trainer:
             else:
                 log.info(f"{cfg.output_dir} already has checkpoints; resumed {resumed} instead of warm starting")
         self._barrier()
+        if self.is_main:
+            log.info(f"Training for {cfg.max_steps} steps: batch_size={cfg.batch_size} (packed batches are sized "
+                     f"by the token budgets) lr={cfg.learning_rate} weight_decay={cfg.weight_decay} "
+                     f"zero_init_modulation={cfg.zero_init_modulation} activation_checkpointing="
+                     f"{'kept-attention' if self.engine.keep_attention else cfg.enable_gradient_checkpointing}")
         loader = None
         it = None
         if not self.layout.cp_enabled or self.layout.cp_rank == 0:
