@@ -24,7 +24,7 @@ import hashlib
 import io
 import random
 from dataclasses import dataclass
-from typing import Any, Dict, Optional, Sequence, Tuple
+from typing import Any, Dict, List, Optional, Sequence, Tuple
 
 import torch
 
@@ -60,6 +60,9 @@ class ItemRef:
     shard_index: int = -1
     sample_index: int = -1
     cycle: int = 0
+    # image members' byte ranges in an uncompressed tar: [latent offset, latent size, caption
+    # offset, caption size], so a resumed loader reads a buffered image back without a tar scan
+    tar_members: Optional[List[int]] = None
 
 
 @dataclass
@@ -173,10 +176,21 @@ def finalize_item(latent: torch.Tensor, text: str, ref: ItemRef, *, prefix_frame
                 modality=modality)
 
 
+def _plain_tar(path: str) -> bool:
+    """True for an uncompressed tar, whose member data sit at fixed byte offsets of the file."""
+    with open(path, "rb") as f:
+        magic = f.read(6)
+    return not (magic[:2] == b"\x1f\x8b" or magic[:3] == b"BZh" or magic == b"\xfd7zXZ\x00")
+
+
 def iter_tar_samples(path: str):
-    """Yield ``(sample_index, key, latent_bytes, caption)`` from a WebDataset-style tar."""
+    """Yield ``(sample_index, key, latent_bytes, caption, members)`` from a WebDataset-style tar:
+    every key with a ``.safetensors`` and a ``.txt`` member is one sample, numbered in tar order.
+    ``members`` is ``[latent offset, latent size, caption offset, caption size]`` in an
+    uncompressed tar (``None`` in a compressed one); :func:`read_tar_sample` reads them back."""
     import tarfile
-    pending: Dict[str, Dict[str, bytes]] = {}
+    plain = _plain_tar(path)
+    pending: Dict[str, Dict[str, tuple]] = {}
     idx = 0
     with tarfile.open(path, "r") as tf:
         for m in tf:
@@ -184,9 +198,24 @@ def iter_tar_samples(path: str):
                 continue
             key, _, ext = m.name.rpartition(".")
             data = tf.extractfile(m).read()
-            pending.setdefault(key, {})[ext] = data
+            pending.setdefault(key, {})[ext] = (data, m.offset_data, m.size)
             entry = pending[key]
             if "safetensors" in entry and "txt" in entry:
-                yield idx, key, entry["safetensors"], entry["txt"].decode("utf-8", "ignore")
+                lat, txt = entry["safetensors"], entry["txt"]
+                members = [lat[1], lat[2], txt[1], txt[2]] if plain else None
+                yield idx, key, lat[0], txt[0].decode("utf-8", "ignore"), members
                 del pending[key]
                 idx += 1
+
+
+def read_tar_sample(path: str, members: Sequence[int]) -> Tuple[bytes, str]:
+    """``(latent_bytes, caption)`` of one sample from its member byte ranges (uncompressed tar)."""
+    lat_off, lat_n, txt_off, txt_n = (int(v) for v in members)
+    with open(path, "rb") as f:
+        f.seek(lat_off)
+        raw = f.read(lat_n)
+        f.seek(txt_off)
+        txt = f.read(txt_n)
+    if len(raw) != lat_n or len(txt) != txt_n:
+        raise ValueError(f"{path} is shorter than the recorded sample ranges {list(members)}")
+    return raw, txt.decode("utf-8", "ignore")

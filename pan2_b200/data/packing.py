@@ -23,7 +23,7 @@ from typing import Iterator, List, Optional, Sequence, Tuple
 import torch
 
 from .items import (Budgets, CaptionCodec, Item, ItemRef, decode_latent, draw_task, finalize_item, iter_tar_samples,
-                    load_latent)
+                    load_latent, read_tar_sample)
 from .patching import packed_rope_tables
 
 MIX_SALT = 0x51C3A7E1
@@ -124,16 +124,24 @@ def expand_csv_paths(paths: Sequence[str]) -> List[str]:
 
 
 def expand_tar_paths(paths: Sequence[str]) -> List[str]:
-    out = []
+    """Tar shards of ``paths``: folders (every ``.tar`` below them, recursively), ``.tar`` files,
+    and text files listing more of either, one per line; absolute, de-duplicated and sorted
+    (reference: dataset/image_item_processor.py:76-108)."""
+    out = set()
     for p in paths:
+        p = p.strip()
+        if not p:
+            continue
         if os.path.isdir(p):
-            out += sorted(glob.glob(os.path.join(p, "*.tar")))
+            out.update(os.path.abspath(t) for t in glob.glob(os.path.join(p, "**", "*.tar"), recursive=True))
         elif p.endswith(".tar"):
-            out.append(p)
+            out.add(os.path.abspath(p))
         elif os.path.isfile(p):
             with open(p) as f:
-                out += expand_tar_paths([ln.strip() for ln in f if ln.strip()])
-    return out
+                out.update(expand_tar_paths([ln.strip() for ln in f if ln.strip()]))
+        else:
+            raise ValueError(f"image tar path {p!r} is neither a folder, a .tar file nor a list file")
+    return sorted(out)
 
 
 def _read_record(f) -> bytes:
@@ -250,11 +258,12 @@ class PackingDataset:
         empty_run = 0
         while True:
             yielded = 0
-            for idx, key, raw, text in iter_tar_samples(self.tars[shard]):
+            for idx, key, raw, text, members in iter_tar_samples(self.tars[shard]):
                 if idx < sample:
                     continue
                 yielded += 1
-                ref = ItemRef(global_index=-1, modality="image", shard_index=shard, sample_index=idx, cycle=cycle)
+                ref = ItemRef(global_index=-1, modality="image", shard_index=shard, sample_index=idx, cycle=cycle,
+                              tar_members=members)
                 yield raw, text, ref, ImageCursor(shard, idx + 1, cycle)
             empty_run = empty_run + 1 if (yielded == 0 and sample == 0) else 0
             if empty_run == len(self.tars):
@@ -324,10 +333,14 @@ class PackingDataset:
                     row = read_csv_row(self.stream.paths[ref.csv_index], ref.local_file_pos)
                     it = self._video_item((row, ref))
                 elif ref.modality == "image" and self.tars:
-                    for idx, key, raw, text in iter_tar_samples(self.tars[ref.shard_index % len(self.tars)]):
-                        if idx == ref.sample_index:
-                            it = self._image_item(raw, text, ref)
-                            break
+                    tar = self.tars[ref.shard_index % len(self.tars)]
+                    if ref.tar_members is not None:  # byte ranges recorded: no scan of the tar
+                        it = self._image_item(*read_tar_sample(tar, ref.tar_members), ref)
+                    else:
+                        for idx, key, raw, text, _ in iter_tar_samples(tar):
+                            if idx == ref.sample_index:
+                                it = self._image_item(raw, text, ref)
+                                break
                 if it is not None and b.fits(it):  # items that no longer fit are dropped
                     b.add(it)
 

@@ -159,12 +159,14 @@ def test_image_stream_fails_fast_on_empty_tars(tmp_path, sample_dir):
         next(ds._image_stream(ImageCursor()))
     # an empty tar beside a real one: the stream keeps cycling through the real one's samples
     ds = _dataset(sample_dir, image_tars=[str(empty), str(sample_dir / "images.tar")])
+    real = ds.tars.index(str(sample_dir / "images.tar"))
     it = ds._image_stream(ImageCursor())
     got = [next(it)[2] for _ in range(14)]
-    assert {r.shard_index for r in got} == {1}
-    assert [r.sample_index for r in got[:7]] == list(range(6)) + [0] and got[6].cycle == 1
+    assert {r.shard_index for r in got} == {real}
+    first = got[0].cycle
+    assert [r.sample_index for r in got[:7]] == list(range(6)) + [0] and got[6].cycle == first + 1
     # resuming past the last sample of the only real tar is not mistaken for an empty pass
-    it = ds._image_stream(ImageCursor(1, 6, 0))
+    it = ds._image_stream(ImageCursor(real, 6, 0))
     assert next(it)[2].sample_index == 0
 
 
@@ -188,3 +190,40 @@ def test_loader_surfaces_producer_errors():
     with pytest.raises(OSError, match="disk gone"):
         next(iter(loader))
     loader.close()
+
+
+def test_resume_reads_buffered_images_by_byte_range(sample_dir, monkeypatch):
+    import pan2_b200.data.packing as packing
+    full = list(itertools.islice(iter(_dataset(sample_dir, image_prob=0.8)), 6))
+    k = next(i for i, p in enumerate(full[:-1]) if any(r.modality == "image" for b in p.state.buffer_items for r in b))
+    st = DataloaderState.from_json(full[k].state.to_json())
+    refs = [r for b in st.buffer_items for r in b if r.modality == "image"]
+    assert refs and all(r.tar_members is not None and len(r.tar_members) == 4 for r in refs)
+    ds = _dataset(sample_dir, resume=st, image_prob=0.8)
+    scans = []
+    real = packing.iter_tar_samples
+    monkeypatch.setattr(packing, "iter_tar_samples", lambda path: scans.append(path) or real(path))
+    from pan2_b200.data.packing import _Bin
+    bins = [_Bin(ds.budgets) for _ in range(ds.num_buffers)]
+    ds._restore_bins(bins)
+    assert scans == []  # restored from the recorded ranges, without scanning a tar
+    restored = [it for b in bins for it in b.items if it.modality == "image"]
+    assert len(restored) == len(refs)
+    # the same samples as a scan of the tar gives
+    by_idx = {idx: (raw, text) for idx, _, raw, text, _ in real(str(sample_dir / "images.tar"))}
+    for it in restored:
+        scanned = ds._image_item(*by_idx[it.ref.sample_index], it.ref)
+        assert torch.equal(it.latent, scanned.latent) and it.caption.text == scanned.caption.text
+
+
+def test_tar_paths_expand_recursively_and_deduplicate(tmp_path):
+    from pan2_b200.data.packing import expand_tar_paths
+    (tmp_path / "a" / "b").mkdir(parents=True)
+    for rel in ("a/x.tar", "a/b/y.tar", "z.tar"):
+        (tmp_path / rel).write_bytes(b"")
+    listing = tmp_path / "list.txt"
+    listing.write_text(f"{tmp_path / 'a'}\n{tmp_path / 'z.tar'}\n\n")
+    got = expand_tar_paths([str(tmp_path / "a"), str(listing), str(tmp_path / "a" / "x.tar")])
+    assert got == sorted({str(tmp_path / p) for p in ("a/x.tar", "a/b/y.tar", "z.tar")})
+    with pytest.raises(ValueError, match="neither"):
+        expand_tar_paths([str(tmp_path / "missing")])
