@@ -183,28 +183,33 @@ def _plain_tar(path: str) -> bool:
     return not (magic[:2] == b"\x1f\x8b" or magic[:3] == b"BZh" or magic == b"\xfd7zXZ\x00")
 
 
-def iter_tar_samples(path: str):
+def iter_tar_samples(path: str, start: int = 0):
     """Yield ``(sample_index, key, latent_bytes, caption, members)`` from a WebDataset-style tar:
-    every key with a ``.safetensors`` and a ``.txt`` member is one sample, numbered in tar order.
-    ``members`` is ``[latent offset, latent size, caption offset, caption size]`` in an
-    uncompressed tar (``None`` in a compressed one); :func:`read_tar_sample` reads them back."""
+    every key with a ``.safetensors`` and a ``.txt`` member is one sample, numbered in tar order,
+    from sample ``start`` on (the data of earlier samples is not read).  ``members`` is ``[latent
+    offset, latent size, caption offset, caption size]`` in an uncompressed tar (``None`` in a
+    compressed one); :func:`read_tar_sample` reads them back."""
     import tarfile
     plain = _plain_tar(path)
-    pending: Dict[str, Dict[str, tuple]] = {}
+    pending: Dict[str, Dict[str, Any]] = {}
     idx = 0
     with tarfile.open(path, "r") as tf:
         for m in tf:
             if not m.isfile():
                 continue
             key, _, ext = m.name.rpartition(".")
-            data = tf.extractfile(m).read()
-            pending.setdefault(key, {})[ext] = (data, m.offset_data, m.size)
-            entry = pending[key]
+            entry = pending.setdefault(key, {})
+            # plain tars are read at the recorded offsets once a sample is wanted; a compressed one
+            # is read as it streams past (seeking back in it would decompress from the start)
+            entry[ext] = (m, None if plain else tf.extractfile(m).read())
             if "safetensors" in entry and "txt" in entry:
-                lat, txt = entry["safetensors"], entry["txt"]
-                members = [lat[1], lat[2], txt[1], txt[2]] if plain else None
-                yield idx, key, lat[0], txt[0].decode("utf-8", "ignore"), members
+                (lat, lat_b), (txt, txt_b) = entry["safetensors"], entry["txt"]
                 del pending[key]
+                if idx >= start:
+                    if plain:
+                        lat_b, txt_b = tf.extractfile(lat).read(), tf.extractfile(txt).read()
+                    members = [lat.offset_data, lat.size, txt.offset_data, txt.size] if plain else None
+                    yield idx, key, lat_b, txt_b.decode("utf-8", "ignore"), members
                 idx += 1
 
 

@@ -258,9 +258,7 @@ class PackingDataset:
         empty_run = 0
         while True:
             yielded = 0
-            for idx, key, raw, text, members in iter_tar_samples(self.tars[shard]):
-                if idx < sample:
-                    continue
+            for idx, key, raw, text, members in iter_tar_samples(self.tars[shard], start=sample):
                 yielded += 1
                 ref = ItemRef(global_index=-1, modality="image", shard_index=shard, sample_index=idx, cycle=cycle,
                               tar_members=members)
@@ -337,10 +335,9 @@ class PackingDataset:
                     if ref.tar_members is not None:  # byte ranges recorded: no scan of the tar
                         it = self._image_item(*read_tar_sample(tar, ref.tar_members), ref)
                     else:
-                        for idx, key, raw, text, _ in iter_tar_samples(tar):
-                            if idx == ref.sample_index:
-                                it = self._image_item(raw, text, ref)
-                                break
+                        for idx, key, raw, text, _ in iter_tar_samples(tar, start=ref.sample_index):
+                            it = self._image_item(raw, text, ref)
+                            break
                 if it is not None and b.fits(it):  # items that no longer fit are dropped
                     b.add(it)
 

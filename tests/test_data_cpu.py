@@ -227,3 +227,21 @@ def test_tar_paths_expand_recursively_and_deduplicate(tmp_path):
     assert got == sorted({str(tmp_path / p) for p in ("a/x.tar", "a/b/y.tar", "z.tar")})
     with pytest.raises(ValueError, match="neither"):
         expand_tar_paths([str(tmp_path / "missing")])
+
+
+def test_tar_samples_from_a_start_index_plain_and_compressed(sample_dir, tmp_path):
+    import gzip
+    import shutil
+    from pan2_b200.data.items import iter_tar_samples, read_tar_sample
+    plain = str(sample_dir / "images.tar")
+    gz = str(tmp_path / "images.tar.gz")
+    with open(plain, "rb") as src, gzip.open(gz, "wb") as dst:
+        shutil.copyfileobj(src, dst)
+    every = list(iter_tar_samples(plain))
+    assert [s[0] for s in every] == list(range(6)) and all(s[4] is not None for s in every)
+    tail = list(iter_tar_samples(plain, start=4))
+    assert [(s[0], s[2], s[3]) for s in tail] == [(s[0], s[2], s[3]) for s in every[4:]]
+    assert read_tar_sample(plain, every[3][4]) == (every[3][2], every[3][3])
+    zipped = list(iter_tar_samples(gz, start=2))
+    assert [(s[0], s[2], s[3]) for s in zipped] == [(s[0], s[2], s[3]) for s in every[2:]]
+    assert all(s[4] is None for s in zipped)  # no byte ranges inside a compressed stream
