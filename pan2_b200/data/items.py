@@ -144,11 +144,16 @@ class Item:
 
 def draw_task(seed: int, ref: ItemRef, latent_steps: int, video_cond_prob: float, image_cond_prob: float,
               cfg_drop_prob: float) -> Tuple[int, bool]:
-    """``(prefix latent frames, drop caption)`` from an RNG seeded by the item's position."""
+    """``(prefix latent frames, drop caption)`` from an RNG seeded by the item's position: with
+    ``video_cond_prob`` a continuation prefix of 1 .. T // 2 latent frames, with ``image_cond_prob``
+    the first frame; clips of fewer than 2 latent frames get no prefix (reference:
+    dataset/video_item_processor.py:239-250)."""
     rng = random.Random(hash((seed, ref.epoch_index, ref.global_index, ref.local_index, ref.local_file_pos)))
     u = rng.random()
-    if u < video_cond_prob and latent_steps > 1:
-        prefix = rng.randint(1, latent_steps - 1)
+    if latent_steps < 2:
+        prefix = 0
+    elif u < video_cond_prob:
+        prefix = rng.randint(1, max(1, latent_steps // 2))
     elif u < video_cond_prob + image_cond_prob:
         prefix = 1
     else:

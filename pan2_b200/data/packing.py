@@ -242,6 +242,9 @@ class PackingDataset:
         text = row.get("caption")
         if not path or not isinstance(text, str) or not text.strip():
             return None
+        # lone UTF-16 surrogates (broken emoji from data preparation) cannot be encoded as UTF-8
+        # and would fail the tokenizer: drop them
+        text = text.encode("utf-8", "ignore").decode("utf-8")
         try:
             lat = load_latent(path)
         except Exception:

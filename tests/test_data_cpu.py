@@ -245,3 +245,23 @@ def test_tar_samples_from_a_start_index_plain_and_compressed(sample_dir, tmp_pat
     zipped = list(iter_tar_samples(gz, start=2))
     assert [(s[0], s[2], s[3]) for s in zipped] == [(s[0], s[2], s[3]) for s in every[2:]]
     assert all(s[4] is None for s in zipped)  # no byte ranges inside a compressed stream
+
+
+def test_task_draws_follow_the_reference_ranges():
+    from pan2_b200.data.items import ItemRef, draw_task
+    refs = [ItemRef(global_index=i, local_index=i, local_file_pos=100 * i) for i in range(200)]
+    cont = [draw_task(3, r, 21, 1.0, 0.0, 0.0)[0] for r in refs]
+    assert min(cont) == 1 and max(cont) == 10  # 1 .. T // 2
+    assert {draw_task(3, r, 21, 0.0, 1.0, 0.0)[0] for r in refs} == {1}
+    assert {draw_task(3, r, 1, 0.5, 0.5, 0.0)[0] for r in refs} == {0}  # one latent frame: no prefix
+    drops = [draw_task(3, r, 21, 0.0, 0.0, 0.3)[1] for r in refs]
+    assert 0.15 < sum(drops) / len(drops) < 0.45
+    assert draw_task(3, refs[7], 21, 0.4, 0.3, 0.1) == draw_task(3, refs[7], 21, 0.4, 0.3, 0.1)
+
+
+def test_caption_with_lone_surrogates_is_cleaned(sample_dir):
+    ds = _dataset(sample_dir)
+    row, ref = next(ds.stream.rows(None))
+    row = dict(row, caption="a cat \ud83d sits")
+    it = ds._video_item((row, ref))
+    assert it is not None and it.caption.text == "a cat  sits"
