@@ -22,11 +22,14 @@ from __future__ import annotations
 
 import hashlib
 import io
+import logging
 import random
 from dataclasses import dataclass
 from typing import Any, Dict, List, Optional, Sequence, Tuple
 
 import torch
+
+log = logging.getLogger("pan2_b200.data")
 
 
 def decode_latent(raw: bytes, where: str = "") -> torch.Tensor:
@@ -168,15 +171,24 @@ def finalize_item(latent: torch.Tensor, text: str, ref: ItemRef, *, prefix_frame
     pt, ph, pw = patch_size
     _, T, H, W = latent.shape
     if H % ph or W % pw or T % pt:
+        log.warning(f"skipping {modality} item {ref.global_index}/{ref.shard_index}:{ref.sample_index}: latent grid "
+                    f"{(T, H, W)} not divisible by patch {tuple(patch_size)}")
         return None
     grid = (T // pt, H // ph, W // pw)
     n_video = grid[0] * grid[1] * grid[2]
     cap = codec.empty(budgets.caption_segment) if drop_caption else codec.tokenize(text, budgets.caption_segment)
     c = cap.cropped_length
-    if (n_video + c > budgets.joint or cap.full_length > budgets.text_encoder or n_video > budgets.video
-            or c > budgets.caption or cap.full_length > budgets.text_encoder_segment
-            or n_video + c > budgets.joint_segment or c > budgets.caption_segment):
-        return None
+    for needed, limit, what in ((n_video + c, budgets.joint, "joint tokens (packed_joint_token_budget)"),
+                                (cap.full_length, budgets.text_encoder, "templated text tokens (text-encoder budget)"),
+                                (n_video, budgets.video, "video tokens (packed_video_token_budget)"),
+                                (c, budgets.caption, "caption tokens (packed_caption_token_budget)"),
+                                (cap.full_length, budgets.text_encoder_segment, "templated text tokens per item"),
+                                (n_video + c, budgets.joint_segment, "joint tokens (packed_joint_segment_limit)"),
+                                (c, budgets.caption_segment, "caption tokens (packed_caption_segment_limit)")):
+        if needed > limit:
+            log.warning(f"skipping {modality} item {ref.global_index}/{ref.shard_index}:{ref.sample_index}: "
+                        f"needs {needed} {what} > {limit}")
+            return None
     return Item(ref=ref, latent=latent, caption=cap, prefix_frames=prefix_frames, n_video_tokens=n_video, grid=grid,
                 modality=modality)
 

@@ -14,6 +14,7 @@ import csv
 import glob
 import io
 import json
+import logging
 import os
 import random
 from concurrent.futures import ThreadPoolExecutor
@@ -25,6 +26,8 @@ import torch
 from .items import (Budgets, CaptionCodec, Item, ItemRef, decode_latent, draw_task, finalize_item, iter_tar_samples,
                     load_latent, read_tar_sample)
 from .patching import packed_rope_tables
+
+log = logging.getLogger("pan2_b200.data")
 
 MIX_SALT = 0x51C3A7E1
 
@@ -247,7 +250,8 @@ class PackingDataset:
         text = text.encode("utf-8", "ignore").decode("utf-8")
         try:
             lat = load_latent(path)
-        except Exception:
+        except Exception as e:  # a missing or unreadable latent skips the row, as in the reference
+            log.warning(f"skipping row {ref.local_index} of csv[{ref.csv_index}]: cannot load {path!r}: {e}")
             return None
         prefix, drop = draw_task(self.seed, ref, int(lat.shape[1]), self.video_cond_prob, self.image_cond_prob,
                                  self.cfg_drop_prob)
