@@ -89,6 +89,13 @@ class PackedLoader:
         self.dev_rng = torch.Generator(device=self.device)
         self.T, self.dist, self.loc, self.scale = T, timestep_distribution, timestep_loc, timestep_scale
         self.shift, self.shift_mode, self.shift_kwargs = shift, shift_mode, dict(shift_kwargs or {})
+        # the dynamic shift reads each item's token grid; these strides turn it back into frames and
+        # pixels (Wan 2.2: 4 frames and 16 x 16 pixels per latent, times the patch; reference:
+        # train.py:1349-1358)
+        pt, ph, pw = tuple(getattr(dataset, "patch_size", (1, 2, 2)))
+        self.shift_kwargs.setdefault("frame_stride", 4 * pt)
+        self.shift_kwargs.setdefault("pixel_stride_h", 16 * ph)
+        self.shift_kwargs.setdefault("pixel_stride_w", 16 * pw)
         self._stop = threading.Event()
         self._thread = None
         self._q = None

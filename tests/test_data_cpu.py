@@ -1,5 +1,6 @@
 """Data pipeline on CPU: sample-data formats, budget packing, exact resume, batch assembly."""
 import itertools
+import math
 
 import pytest
 import torch
@@ -265,3 +266,20 @@ def test_caption_with_lone_surrogates_is_cleaned(sample_dir):
     row = dict(row, caption="a cat \ud83d sits")
     it = ds._video_item((row, ref))
     assert it is not None and it.caption.text == "a cat  sits"
+
+
+def test_dynamic_shift_sees_pixels_and_frames_of_the_token_grid(sample_dir):
+    from pan2_b200.diffusion.flow_matching import shift_timesteps
+    loader = PackedLoader(_dataset(sample_dir), device="cpu", shift_mode="dynamic")
+    assert {k: loader.shift_kwargs[k] for k in ("frame_stride", "pixel_stride_h", "pixel_stride_w")} == \
+        {"frame_stride": 4, "pixel_stride_h": 32, "pixel_stride_w": 32}
+    t = torch.tensor([300.0, 700.0])
+    # a 704 x 1280, 81-frame clip: token grid (21, 22, 40) at patch (1, 2, 2) == latent grid (21, 44, 80)
+    tok = shift_timesteps(t, 1000, mode="dynamic", latent_shapes=torch.tensor([[21.0, 22, 40]] * 2),
+                          **{k: loader.shift_kwargs[k] for k in ("frame_stride", "pixel_stride_h", "pixel_stride_w")})
+    lat = shift_timesteps(t, 1000, mode="dynamic", latent_shapes=torch.tensor([[21.0, 44, 80]] * 2))
+    assert torch.allclose(tok, lat)
+    area, frames = 704 * 1280, 81
+    s = math.exp(0.5 * ((1.15 - 0.5) / (1024 ** 2 - 256 ** 2) * (area - 256 ** 2) + 0.5 + 1.64 / 120 * (frames - 1)))
+    f = t / 1000
+    assert torch.allclose(tok, s * f / (1 + (s - 1) * f) * 1000, rtol=1e-5)
