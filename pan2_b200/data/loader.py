@@ -137,6 +137,9 @@ class PackedLoader:
         t = shift_timesteps(t, self.T, self.shift, self.shift_mode,
                             latent_shapes=torch.tensor([list(g) for g in plan.grids], dtype=torch.float32),
                             **self.shift_kwargs)
+        # rounded to the batch dtype (bf16 in bf16 runs) before the noising and the timestep
+        # embedding read it, as the reference loader does (dataset/packed_dataloader.py:370-374)
+        t = t.to(self.dtype).float()
         t_dev = t.to(dev, non_blocking=True)
         inputs, targets = [], []
         for i, item in enumerate(plan.items):

@@ -283,3 +283,13 @@ def test_dynamic_shift_sees_pixels_and_frames_of_the_token_grid(sample_dir):
     s = math.exp(0.5 * ((1.15 - 0.5) / (1024 ** 2 - 256 ** 2) * (area - 256 ** 2) + 0.5 + 1.64 / 120 * (frames - 1)))
     f = t / 1000
     assert torch.allclose(tok, s * f / (1 + (s - 1) * f) * 1000, rtol=1e-5)
+
+
+def test_timesteps_are_rounded_to_the_batch_dtype(sample_dir):
+    ds = _dataset(sample_dir, image_prob=0.0)
+    for dtype in (torch.bfloat16, torch.float32):
+        loader = PackedLoader(ds, device="cpu", dtype=dtype, seed=0, shift=3.0)
+        batch, _ = next(iter(loader))
+        loader.close()
+        t = batch["timestep"]
+        assert t.dtype == torch.float32 and torch.equal(t, t.to(dtype).float())
