@@ -30,6 +30,13 @@ mkdir -p logs
 export PYTORCH_CUDA_ALLOC_CONF=${PYTORCH_CUDA_ALLOC_CONF:-expandable_segments:True}
 export HF_HUB_OFFLINE=${HF_HUB_OFFLINE:-1}
 export TORCH_NCCL_ASYNC_ERROR_HANDLING=${TORCH_NCCL_ASYNC_ERROR_HANDLING:-1}
+# multi-node over AWS EFA (libfabric): set PAN_NET=efa, or leave it to auto-detect the EFA devices
+if [[ ${PAN_NET:-auto} == efa || ( ${PAN_NET:-auto} == auto && -d /sys/class/infiniband && \
+      -n $(ls /sys/class/infiniband 2>/dev/null | grep -m1 efa) ) ]]; then
+    export FI_PROVIDER=${FI_PROVIDER:-efa}
+    export FI_EFA_USE_DEVICE_RDMA=${FI_EFA_USE_DEVICE_RDMA:-1}
+    export FI_EFA_FORK_SAFE=${FI_EFA_FORK_SAFE:-1}
+fi
 # the CUDA extension is built in-tree once; every rank imports the same .so
 python -c "import torch, pan2_b200._C" 2>/dev/null || python setup.py build_ext --inplace
 
