@@ -30,6 +30,7 @@ from pan2_b200.ops.attention import work_items
 from pan2_b200.ops.packed import _bounds_tensor, ln_stats_of
 
 HIDDEN, HEADS, HEAD_DIM, FFN = 4096, 32, 128, 32768
+GEMM_BAND_MB = 0  # the GEMM tile-order setting restored after a --gemm-band-mb sweep
 CLIPS, CLIP_TOKENS = 5, 18992
 
 
@@ -44,15 +45,29 @@ def measured_peaks():
 
 
 class Timer:
-    """Median per-launch device time with an L2 flush between launches."""
+    """Median per-launch device time with an L2 flush between launches.  With ``sustain_s`` > 0 the
+    op first runs back to back for that long (clocks settle under the power cap).  The SM clock is
+    sampled during the timed launches (``last_clock``: median MHz and throttle reasons)."""
 
-    def __init__(self, iters: int, warmup: int):
-        self.iters, self.warmup = iters, warmup
+    def __init__(self, iters: int, warmup: int, sustain_s: float = 0.0):
+        self.iters, self.warmup, self.sustain_s = iters, warmup, sustain_s
         self.flush = torch.empty(256 << 20, dtype=torch.uint8, device="cuda")
+        self.last_clock = None
 
     def __call__(self, fn) -> float:
+        import time
+        from pan2_b200.utils.clocks import ClockSampler
         for _ in range(self.warmup):
             fn()
+        if self.sustain_s > 0:
+            torch.cuda.synchronize()
+            t0 = time.time()
+            while time.time() - t0 < self.sustain_s:
+                for _ in range(4):
+                    fn()
+                torch.cuda.synchronize()
+        sampler = ClockSampler(interval_ms=50)
+        sampler.start()
         times = []
         torch.cuda.synchronize()
         for _ in range(self.iters):
@@ -63,7 +78,18 @@ class Timer:
             e.record()
             times.append((s, e))
         torch.cuda.synchronize()
+        clk = sampler.stop(gpus=[torch.cuda.current_device()])
+        self.last_clock = {"sm_mhz": clk.get("sm_mhz"), "reasons": clk.get("reasons")}
         return statistics.median(s.elapsed_time(e) for s, e in times)
+
+    def clock_fields(self, prefix: str, ms: float) -> dict:
+        """Median SM clock of the last timing and time x clock (the clock-normalised cost)."""
+        c = self.last_clock or {}
+        mhz = c.get("sm_mhz")
+        out = {f"{prefix}sm_mhz": mhz, f"{prefix}reasons": c.get("reasons")}
+        if mhz:
+            out[f"{prefix}ms_x_ghz"] = round(ms * mhz / 1000.0, 4)
+        return out
 
 
 def gemm_cases(small: bool):
@@ -75,7 +101,7 @@ def gemm_cases(small: bool):
     return cases[:1] if small else cases
 
 
-def run_gemm(name, M, N, K, layout, timer, library, peaks):
+def run_gemm(name, M, N, K, layout, timer, library, peaks, band_mbs=(None,)):
     E = ext()
     dev = "cuda"
     a = torch.randn(K, M, device=dev, dtype=torch.bfloat16) if layout == "TN" else \
@@ -84,22 +110,34 @@ def run_gemm(name, M, N, K, layout, timer, library, peaks):
         torch.randn(K, N, device=dev, dtype=torch.bfloat16)
     out = torch.empty(M, N, device=dev, dtype=torch.float32 if layout == "TN" else torch.bfloat16)
     fn = lambda: E.gemm(a, b, out, layout != "TN", layout == "NT", None, None, False)
-    ms = timer(fn)
     fl = 2.0 * M * N * K
-    rec = dict(case=f"gemm_{name}", shape=[M, N, K], layout=layout, out_dtype=str(out.dtype).split(".")[-1],
-               ms=round(ms, 4), tflops=round(fl / ms / 1e9, 1), frac_of_peak=round(fl / ms / 1e9 / peaks[1], 3))
+    recs = []
+    for band in band_mbs:
+        if band is not None:
+            E.gemm_tuning(6, 0, int(band))
+        ms = timer(fn)
+        rec = dict(case=f"gemm_{name}", shape=[M, N, K], layout=layout, out_dtype=str(out.dtype).split(".")[-1],
+                   ms=round(ms, 4), tflops=round(fl / ms / 1e9, 1), frac_of_peak=round(fl / ms / 1e9 / peaks[1], 3))
+        if band is not None:
+            rec["band_mb"] = int(band)
+        rec.update(timer.clock_fields("", ms))
+        recs.append(rec)
+    E.gemm_tuning(6, 0, GEMM_BAND_MB)
     if library:
         ao = a.t() if layout == "TN" else a
         bo = b.t() if layout == "NT" else b
         lib_out = torch.empty(M, N, device=dev, dtype=torch.bfloat16)
         ms_l = timer(lambda: torch.matmul(ao, bo, out=lib_out))
-        rec["cublas_bf16_out_ms"] = round(ms_l, 4)
-        rec["cublas_tflops"] = round(fl / ms_l / 1e9, 1)
-    rec["error_flag"] = E.error_flag(True)
-    return rec
+        for rec in recs:
+            rec["cublas_bf16_out_ms"] = round(ms_l, 4)
+            rec["cublas_tflops"] = round(fl / ms_l / 1e9, 1)
+            rec.update(timer.clock_fields("cublas_", ms_l))
+    for rec in recs:
+        rec["error_flag"] = E.error_flag(True)
+    return recs
 
 
-def run_attention(small, timer, library, peaks, which):
+def run_attention(small, timer, library, peaks, which, fwd_variants=(None,), bwd_variants=(None,)):
     E = ext()
     lens = [8192] if small else [CLIP_TOKENS] * CLIPS
     L = sum(lens)
@@ -107,24 +145,39 @@ def run_attention(small, timer, library, peaks, which):
     scale = 1 / math.sqrt(HEAD_DIM)
     it_f, it_b = work_items(lens, 256, q.device), work_items(lens, 128, q.device)
     fl = sum(4.0 * s * s * HEAD_DIM * HEADS for s in lens)
+    default_f, default_b = E.attn_get_variant(0), E.attn_get_variant(1)
     out = []
     o, lse = E.attn_fwd(q, k, v, it_f, L, scale)
+    lib_f = lib_b = None
     if "fwd" in which:
-        ms = timer(lambda: E.attn_fwd(q, k, v, it_f, L, scale))
-        rec = dict(case="attn_fwd", segments=lens, heads=HEADS, head_dim=HEAD_DIM, ms=round(ms, 4),
-                   tflops=round(fl / ms / 1e9, 1), frac_of_peak=round(fl / ms / 1e9 / peaks[1], 3))
-        if library:
-            rec.update(_sdpa(q, lens, timer, fl, backward=False))
-        out.append(rec)
+        for var in fwd_variants:
+            E.attn_set_forward_variant(default_f if var is None else int(var))
+            ms = timer(lambda: E.attn_fwd(q, k, v, it_f, L, scale))
+            rec = dict(case="attn_fwd", segments=lens, heads=HEADS, head_dim=HEAD_DIM,
+                       variant=E.attn_get_variant(0), ms=round(ms, 4), tflops=round(fl / ms / 1e9, 1),
+                       frac_of_peak=round(fl / ms / 1e9 / peaks[1], 3))
+            rec.update(timer.clock_fields("", ms))
+            if library:
+                lib_f = lib_f or _sdpa(q, lens, timer, fl, backward=False)
+                rec.update(lib_f)
+            out.append(rec)
+        E.attn_set_forward_variant(default_f)
     if "bwd" in which:
+        o, lse = E.attn_fwd(q, k, v, it_f, L, scale)
         do = torch.randn_like(o)
-        ms = timer(lambda: E.attn_bwd(do, q, k, v, o, lse, it_b, it_b, L, scale))
         flb = 2.5 * fl  # dV, dP, dQ, dK GEMMs plus the S recompute
-        rec = dict(case="attn_bwd", segments=lens, heads=HEADS, head_dim=HEAD_DIM, ms=round(ms, 4),
-                   tflops=round(flb / ms / 1e9, 1), frac_of_peak=round(flb / ms / 1e9 / peaks[1], 3))
-        if library:
-            rec.update(_sdpa(q, lens, timer, flb, backward=True))
-        out.append(rec)
+        for var in bwd_variants:
+            E.attn_set_backward_variant(default_b if var is None else int(var))
+            ms = timer(lambda: E.attn_bwd(do, q, k, v, o, lse, it_b, it_b, L, scale))
+            rec = dict(case="attn_bwd", segments=lens, heads=HEADS, head_dim=HEAD_DIM,
+                       variant=E.attn_get_variant(1), ms=round(ms, 4), tflops=round(flb / ms / 1e9, 1),
+                       frac_of_peak=round(flb / ms / 1e9 / peaks[1], 3))
+            rec.update(timer.clock_fields("", ms))
+            if library:
+                lib_b = lib_b or _sdpa(q, lens, timer, flb, backward=True)
+                rec.update(lib_b)
+            out.append(rec)
+        E.attn_set_backward_variant(default_b)
     for r in out:
         r["error_flag"] = E.error_flag(True)
     return out
@@ -189,23 +242,28 @@ def main():
     ap.add_argument("--iters", type=int, default=10)
     ap.add_argument("--warmup", type=int, default=3)
     ap.add_argument("--no-library", action="store_true", help="skip the cuBLAS / SDPA comparisons")
-    ap.add_argument("--attn-bwd-variant", type=int, default=None,
-                    help="attention backward: 0 two passes, 1 fused single pass, 2 pipelined single pass")
+    ap.add_argument("--attn-bwd-variant", default=None,
+                    help="comma list of attention backward variants: 0 two passes, 1 fused, 2 pipelined, "
+                         "3 fused with the reordered schedule")
+    ap.add_argument("--attn-fwd-variant", default=None, help="comma list of attention forward variants (0..5)")
+    ap.add_argument("--gemm-band-mb", default=None,
+                    help="comma list of GEMM M-band budgets in MB (0 = N bands only)")
+    ap.add_argument("--sustain-s", type=float, default=0.0,
+                    help="run each op back to back this long before timing (clocks settle under the power cap)")
     args = ap.parse_args()
     pat = re.compile(args.case)
-    if args.attn_bwd_variant is not None:
-        ext().attn_set_backward_variant(args.attn_bwd_variant)
+    lst = lambda s: [int(x) for x in s.split(",")] if s else [None]
     peaks = measured_peaks()
-    timer = Timer(args.iters, args.warmup)
+    timer = Timer(args.iters, args.warmup, args.sustain_s)
     library = not args.no_library
-    recs = []
     if pat.search("gemm"):
         for c in gemm_cases(args.small):
-            recs.append(run_gemm(*c, timer=timer, library=library, peaks=peaks))
-            print(json.dumps(recs[-1]), flush=True)
+            for rec in run_gemm(*c, timer=timer, library=library, peaks=peaks, band_mbs=lst(args.gemm_band_mb)):
+                print(json.dumps(rec), flush=True)
     which = [w for w in ("fwd", "bwd") if pat.search("attn_" + w)]
     if which:
-        for r in run_attention(args.small, timer, library, peaks, which):
+        for r in run_attention(args.small, timer, library, peaks, which, lst(args.attn_fwd_variant),
+                               lst(args.attn_bwd_variant)):
             print(json.dumps(r), flush=True)
     which = [w for w in ("ln_modulate", "gate_residual") if pat.search(w)]
     if which:

@@ -115,6 +115,12 @@ __device__ __forceinline__ void fadd2(float& d0, float& d1, float a0, float a1, 
       : "=f"(d0), "=f"(d1)
       : "f"(a0), "f"(a1), "f"(b0), "f"(b1));
 }
+__device__ __forceinline__ void fmul2(float& d0, float& d1, float a0, float a1, float b0, float b1) {
+  asm("{\n\t.reg .b64 ra, rb, rd;\n\tmov.b64 ra, {%2, %3};\n\tmov.b64 rb, {%4, %5};\n\t"
+      "mul.rn.f32x2 rd, ra, rb;\n\tmov.b64 {%0, %1}, rd;\n\t}"
+      : "=f"(d0), "=f"(d1)
+      : "f"(a0), "f"(a1), "f"(b0), "f"(b1));
+}
 __device__ __forceinline__ float fmax3(float a, float b, float c) {
   float d;
   asm("max.f32 %0, %1, %2, %3;" : "=f"(d) : "f"(a), "f"(b), "f"(c));
@@ -127,16 +133,48 @@ __device__ __forceinline__ float fast_exp2(float x) {
   return y;
 }
 
+// Two 2^x on the FMA pipe with packed pair arithmetic (the split and polynomial of poly_exp2);
+// arguments below -127 are clamped (their result, < 2^-126, is below what bf16 P resolves).
+__device__ __forceinline__ void poly_exp2x2(float x0, float x1, float& r0, float& r1) {
+  x0 = fmaxf(x0, -127.f);
+  x1 = fmaxf(x1, -127.f);
+  const float magic = 12582912.f;
+  float y0, y1, j0, j1, f0, f1, p0, p1;
+  fadd2(y0, y1, x0, x1, magic, magic);
+  fadd2(j0, j1, y0, y1, -magic, -magic);
+  fadd2(f0, f1, x0, x1, -j0, -j1);
+  ffma2(p0, p1, 0.05517150138583113f, 0.05517150138583113f, f0, f1, 0.24261095811365377f, 0.24261095811365377f);
+  ffma2(p0, p1, p0, p1, f0, f1, 0.6932609941182479f, 0.6932609941182479f);
+  ffma2(p0, p1, p0, p1, f0, f1, 0.999928083295878f, 0.999928083295878f);
+  r0 = __int_as_float(__float_as_int(p0) + ((__float_as_int(y0) - __float_as_int(magic)) << 23));
+  r1 = __int_as_float(__float_as_int(p1) + ((__float_as_int(y1) - __float_as_int(magic)) << 23));
+}
+
 // ============================================================================ forward
 constexpr int FWD_THREADS = 320;
 constexpr int FWD_RING = 5;  // K/V tiles in flight (P lives in TMEM, so the smem goes to the ring)
 constexpr int FWD_SMEM = 2 * TILE_BYTES /*Q*/ + FWD_RING * TILE_BYTES + 1024 + 256;
 
-template <int PAIRED, int PACKED>
+// Forward variant bits (template argument V):
+//   1  PAIRED   two score chunks per TMEM wait (two-pass softmax only)
+//   2  PACKED   packed f32x2 FMA / add and 3-input max
+//   4  INORDER  the next score GEMM of a tile is issued right after that tile's PV GEMM: tcgen05.mma
+//               instructions of one thread execute in issue order, so S(j+1) cannot overwrite the
+//               P(j) columns before PV(j) has read them, and no completion wait sits between them
+//   8  ROWREG   the whole 128-score row is loaded once into registers (one TMEM pass for max and exp)
+//   bits 4..7   EMU: of each 32-column chunk's 16 column pairs, the last EMU pairs are exponentiated
+//               with the FMA-pipe polynomial instead of the MUFU unit (ROWREG only)
+constexpr int FWD_PAIRED = 1, FWD_PACKED = 2, FWD_INORDER = 4, FWD_ROWREG = 8;
+constexpr int fwd_variant(int flags, int emu) { return flags | (emu << 4); }
+
+template <int V>
 __global__ void __launch_bounds__(FWD_THREADS, 1)
 attn_fwd_kernel(const __grid_constant__ CUtensorMap qmap, const __grid_constant__ CUtensorMap kmap,
                 const __grid_constant__ CUtensorMap vmap, const WorkItem* __restrict__ items, int L, int H,
                 float scale_log2, __nv_bfloat16* __restrict__ out, float* __restrict__ lse, const PeerRows o_peer) {
+  constexpr bool PAIRED = V & FWD_PAIRED, PACKED = V & FWD_PACKED, INORDER = V & FWD_INORDER,
+                 ROWREG = V & FWD_ROWREG;
+  constexpr int EMU = (V >> 4) & 15;
   extern __shared__ uint8_t smem_raw[];
   uint8_t* smem = reinterpret_cast<uint8_t*>((reinterpret_cast<uintptr_t>(smem_raw) + 1023) & ~uintptr_t(1023));
   uint8_t* sQ = smem;                                 // 2 tiles
@@ -237,10 +275,13 @@ attn_fwd_kernel(const __grid_constant__ CUtensorMap qmap, const __grid_constant_
           mma_bf16_ts(tmem + 256 + x * 128, tmem + x * 128 + kk * 8, desc_mnmajor(vb, kk), id_pv, acc || kk > 0);
         mma_commit(pv_done(x));
       };
-      // S_x(j+1) overwrites the columns PV_x(j) reads P_x(j) from: wait for PV_x(j) first
+      // S_x(j+1) overwrites the columns PV_x(j) reads P_x(j) from.  INORDER relies on the in-order
+      // execution of one thread's MMAs; otherwise PV_x(j)'s completion is awaited first.
       auto next_s = [&](int x, uint32_t kb, int j) {
-        if (!(ok = mbar_wait(pv_done(x), j & 1, 29 + x))) return;
-        tc_fence_after();
+        if (!INORDER) {
+          if (!(ok = mbar_wait(pv_done(x), j & 1, 29 + x))) return;
+          tc_fence_after();
+        }
         issue_s(x, kb);
       };
       // prologue: S_A(0), S_B(0)
@@ -286,54 +327,12 @@ attn_fwd_kernel(const __grid_constant__ CUtensorMap qmap, const __grid_constant_
     const uint32_t tO = tmem + 256 + x * 128 + lane_off;
     float m_used = -INFINITY, l = 0.f;
     bool ok = true;
-    for (int j = 0; j < n_kv; ++j) {
-      if (!(ok = mbar_wait(s_full(x), j & 1, 26))) break;
-      tc_fence_after();
-      const int valid = min(BT, it.seg_len - j * BT);
-      // row maximum: PAIRED reads two chunks per TMEM wait (10 warps per CTA cap registers at 168
-      // per thread, so at most 64 scores are live at a time); otherwise one chunk per wait
-      float mx0 = -INFINITY, mx1 = -INFINITY;
-      auto max_chunk = [&](const uint32_t (&r)[32], int c0) {
-        if (valid == BT) {
-#pragma unroll
-          for (int i = 0; i < 32; i += 4) {
-            if (PACKED) {
-              mx0 = fmax3(mx0, __uint_as_float(r[i]), __uint_as_float(r[i + 1]));
-              mx1 = fmax3(mx1, __uint_as_float(r[i + 2]), __uint_as_float(r[i + 3]));
-            } else {
-              mx0 = fmaxf(fmaxf(mx0, __uint_as_float(r[i])), __uint_as_float(r[i + 1]));
-              mx1 = fmaxf(fmaxf(mx1, __uint_as_float(r[i + 2])), __uint_as_float(r[i + 3]));
-            }
-          }
-        } else {
-#pragma unroll
-          for (int i = 0; i < 32; ++i)
-            if (c0 + i < valid) mx0 = fmaxf(mx0, __uint_as_float(r[i]));
-        }
-      };
-      if (PAIRED) {
-#pragma unroll
-        for (int h2 = 0; h2 < 2; ++h2) {
-          uint32_t ra[32], rb[32];
-          tmem_ld32(tS + h2 * 64, ra);
-          tmem_ld32(tS + h2 * 64 + 32, rb);
-          tmem_ld_wait();
-          max_chunk(ra, h2 * 64);
-          max_chunk(rb, h2 * 64 + 32);
-        }
-      } else {
-#pragma unroll
-        for (int c = 0; c < 4; ++c) {
-          uint32_t r[32];
-          tmem_ld32(tS + c * 32, r);
-          tmem_ld_wait();
-          max_chunk(r, c * 32);
-        }
-      }
-      const float m_new = fmaxf(m_used, fmaxf(mx0, mx1) * scale_log2);
+    // O and l are rescaled only when the running maximum grows by more than 8 (a factor of 256);
+    // PV_x(j-1) must be complete before O is read
+    auto maybe_rescale = [&](int j, float m_new) -> bool {
       const bool grow = m_new > m_used + 8.f;
       if (j > 0) {
-        if (!(ok = mbar_wait(pv_done(x), (j - 1) & 1, 27))) break;
+        if (!mbar_wait(pv_done(x), (j - 1) & 1, 27)) return false;
         tc_fence_after();
         if (__any_sync(0xffffffffu, grow)) {
           const float alpha = grow ? fast_exp2(m_used - m_new) : 1.f;  // m_used finite here (j > 0)
@@ -351,53 +350,159 @@ attn_fwd_kernel(const __grid_constant__ CUtensorMap qmap, const __grid_constant_
         }
       }
       if (grow) m_used = m_new;
+      return true;
+    };
+    // exponentiate one 32-column chunk of scores into 16 packed bf16 P words; masked columns -> 0
+    auto exp_chunk = [&](const uint32_t (&r)[32], int c0, int valid, uint32_t (&w)[16], float& l0, float& l1) {
+#pragma unroll
+      for (int i = 0; i < 32; i += 2) {
+        float x0, x1;
+        if (PACKED) {
+          ffma2(x0, x1, __uint_as_float(r[i]), __uint_as_float(r[i + 1]), scale_log2, scale_log2, -m_used, -m_used);
+        } else {
+          x0 = fmaf(__uint_as_float(r[i]), scale_log2, -m_used);
+          x1 = fmaf(__uint_as_float(r[i + 1]), scale_log2, -m_used);
+        }
+        float p0 = fast_exp2(x0);
+        float p1 = fast_exp2(x1);
+        if (valid < BT) {
+          p0 = c0 + i < valid ? p0 : 0.f;
+          p1 = c0 + i + 1 < valid ? p1 : 0.f;
+        }
+        if (PACKED) {
+          fadd2(l0, l1, l0, l1, p0, p1);
+        } else {
+          l0 += p0;
+          l1 += p1;
+        }
+        w[i >> 1] = pack_bf16(p0, p1);
+      }
+    };
+    // the same for 16 columns (8 words, stored with the x8 TMEM shape to keep the live range short);
+    // `c0 & 31` places them in their 32-column chunk for EMU
+    auto exp_half = [&](const uint32_t* r, int c0, int valid, uint32_t (&w)[8], float& l0, float& l1) {
+#pragma unroll
+      for (int i = 0; i < 16; i += 2) {
+        float x0, x1, p0, p1;
+        ffma2(x0, x1, __uint_as_float(r[i]), __uint_as_float(r[i + 1]), scale_log2, scale_log2, -m_used, -m_used);
+        if ((((c0 & 31) + i) >> 1) >= 16 - EMU) {
+          poly_exp2x2(x0, x1, p0, p1);
+        } else {
+          p0 = fast_exp2(x0);
+          p1 = fast_exp2(x1);
+        }
+        if (valid < BT) {
+          p0 = c0 + i < valid ? p0 : 0.f;
+          p1 = c0 + i + 1 < valid ? p1 : 0.f;
+        }
+        fadd2(l0, l1, l0, l1, p0, p1);
+        w[i >> 1] = pack_bf16(p0, p1);
+      }
+    };
+    for (int j = 0; j < n_kv; ++j) {
+      if (!(ok = mbar_wait(s_full(x), j & 1, 26))) break;
+      tc_fence_after();
+      const int valid = min(BT, it.seg_len - j * BT);
       float l0 = 0.f, l1 = 0.f;
-      // P = exp2(S * scale - m) as bf16 pairs into the first 64 columns of S (a chunk's P columns
-      // were read as scores in an earlier or the same chunk)
-      auto softmax_chunk = [&](const uint32_t (&r)[32], int c) {
-        uint32_t w[16];
+      if (ROWREG) {
+        // one TMEM pass: the 128 scores of this row stay in registers for the max and the exp
+        uint32_t s[128];
 #pragma unroll
-        for (int i = 0; i < 32; i += 2) {
-          float x0, x1;
-          if (PACKED) {
-            ffma2(x0, x1, __uint_as_float(r[i]), __uint_as_float(r[i + 1]), scale_log2, scale_log2, -m_used, -m_used);
-          } else {
-            x0 = fmaf(__uint_as_float(r[i]), scale_log2, -m_used);
-            x1 = fmaf(__uint_as_float(r[i + 1]), scale_log2, -m_used);
-          }
-          float p0 = fast_exp2(x0);
-          float p1 = fast_exp2(x1);
-          if (valid < BT) {
-            p0 = c * 32 + i < valid ? p0 : 0.f;
-            p1 = c * 32 + i + 1 < valid ? p1 : 0.f;
-          }
-          if (PACKED) {
-            fadd2(l0, l1, l0, l1, p0, p1);
-          } else {
-            l0 += p0;
-            l1 += p1;
-          }
-          w[i >> 1] = pack_bf16(p0, p1);
-        }
-        tmem_st16(tS + c * 16, w);
-      };
-      if (PAIRED) {
+        for (int c = 0; c < 4; ++c) tmem_ld32(tS + c * 32, *reinterpret_cast<uint32_t(*)[32]>(&s[c * 32]));
+        tmem_ld_wait();
+        float mx[4] = {-INFINITY, -INFINITY, -INFINITY, -INFINITY};
+        if (valid == BT) {
 #pragma unroll
-        for (int h2 = 0; h2 < 2; ++h2) {
-          uint32_t ra[32], rb[32];
-          tmem_ld32(tS + h2 * 64, ra);
-          tmem_ld32(tS + h2 * 64 + 32, rb);
-          tmem_ld_wait();
-          softmax_chunk(ra, 2 * h2);
-          softmax_chunk(rb, 2 * h2 + 1);
+          for (int i = 0; i < 128; i += 8) {
+#pragma unroll
+            for (int u = 0; u < 4; ++u)
+              mx[u] = fmax3(mx[u], __uint_as_float(s[i + 2 * u]), __uint_as_float(s[i + 2 * u + 1]));
+          }
+        } else {
+#pragma unroll
+          for (int i = 0; i < 128; ++i)
+            if (i < valid) mx[i & 3] = fmaxf(mx[i & 3], __uint_as_float(s[i]));
         }
+        const float m_new = fmaxf(m_used, fmaxf(fmaxf(mx[0], mx[1]), fmaxf(mx[2], mx[3])) * scale_log2);
+        // P = exp2(S * scale - m) as bf16 pairs into the first 64 columns of S, with the maximum this
+        // tile settles on; P is written before O is rescaled, so the score registers are dead by
+        // the time the rescale needs its own
+        const float m_keep = m_used;
+        if (m_new > m_used + 8.f) m_used = m_new;
+#pragma unroll
+        for (int c = 0; c < 8; ++c) {
+          uint32_t w[8];
+          exp_half(&s[c * 16], c * 16, valid, w, l0, l1);
+          tmem_st8(tS + c * 8, w);
+        }
+        m_used = m_keep;
+        if (!(ok = maybe_rescale(j, m_new))) break;
       } else {
+        // two TMEM passes (max, then exp); PAIRED reads two chunks per TMEM wait
+        float mx0 = -INFINITY, mx1 = -INFINITY;
+        auto max_chunk = [&](const uint32_t (&r)[32], int c0) {
+          if (valid == BT) {
 #pragma unroll
-        for (int c = 0; c < 4; ++c) {
-          uint32_t r[32];
-          tmem_ld32(tS + c * 32, r);
-          tmem_ld_wait();
-          softmax_chunk(r, c);
+            for (int i = 0; i < 32; i += 4) {
+              if (PACKED) {
+                mx0 = fmax3(mx0, __uint_as_float(r[i]), __uint_as_float(r[i + 1]));
+                mx1 = fmax3(mx1, __uint_as_float(r[i + 2]), __uint_as_float(r[i + 3]));
+              } else {
+                mx0 = fmaxf(fmaxf(mx0, __uint_as_float(r[i])), __uint_as_float(r[i + 1]));
+                mx1 = fmaxf(fmaxf(mx1, __uint_as_float(r[i + 2])), __uint_as_float(r[i + 3]));
+              }
+            }
+          } else {
+#pragma unroll
+            for (int i = 0; i < 32; ++i)
+              if (c0 + i < valid) mx0 = fmaxf(mx0, __uint_as_float(r[i]));
+          }
+        };
+        if (PAIRED) {
+#pragma unroll
+          for (int h2 = 0; h2 < 2; ++h2) {
+            uint32_t ra[32], rb[32];
+            tmem_ld32(tS + h2 * 64, ra);
+            tmem_ld32(tS + h2 * 64 + 32, rb);
+            tmem_ld_wait();
+            max_chunk(ra, h2 * 64);
+            max_chunk(rb, h2 * 64 + 32);
+          }
+        } else {
+#pragma unroll
+          for (int c = 0; c < 4; ++c) {
+            uint32_t r[32];
+            tmem_ld32(tS + c * 32, r);
+            tmem_ld_wait();
+            max_chunk(r, c * 32);
+          }
+        }
+        const float m_new = fmaxf(m_used, fmaxf(mx0, mx1) * scale_log2);
+        if (!(ok = maybe_rescale(j, m_new))) break;
+        // a chunk's P columns were read as scores in an earlier or the same chunk
+        if (PAIRED) {
+#pragma unroll
+          for (int h2 = 0; h2 < 2; ++h2) {
+            uint32_t ra[32], rb[32];
+            tmem_ld32(tS + h2 * 64, ra);
+            tmem_ld32(tS + h2 * 64 + 32, rb);
+            tmem_ld_wait();
+            uint32_t wa[16], wb[16];
+            exp_chunk(ra, h2 * 64, valid, wa, l0, l1);
+            tmem_st16(tS + h2 * 32, wa);
+            exp_chunk(rb, h2 * 64 + 32, valid, wb, l0, l1);
+            tmem_st16(tS + h2 * 32 + 16, wb);
+          }
+        } else {
+#pragma unroll
+          for (int c = 0; c < 4; ++c) {
+            uint32_t r[32];
+            tmem_ld32(tS + c * 32, r);
+            tmem_ld_wait();
+            uint32_t w[16];
+            exp_chunk(r, c * 32, valid, w, l0, l1);
+            tmem_st16(tS + c * 16, w);
+          }
         }
       }
       l += l0 + l1;
@@ -707,6 +812,13 @@ constexpr int FB_STAGE = 32 * D * 4;  // 32 query rows of fp32 dQ
 constexpr int FB_SMEM = 2 * TILE_BYTES /*K, V*/ + 2 * TILE_BYTES /*Q ring*/ + TILE_BYTES /*dO*/ +
                         TILE_BYTES /*dS^T*/ + 2 * FB_STAGE + 1024 + 256 + 2 * BT * 4;
 
+// SCHED 0: dQ^T goes into the S^T columns, so the MMA thread waits for dV / dK to complete before
+// issuing it, and the next S^T waits for the dQ^T drain.  SCHED 1: dQ^T goes into the dP^T
+// columns and dK reads dS^T from shared memory; after the elementwise hand-off the MMA thread
+// issues dQ^T, dV, dK and the next S^T back to back (one thread's MMAs execute in order, so S^T(i+1)
+// cannot overwrite P^T(i) before dV(i) has read it), and only dP^T(i+1) waits for the dQ^T(i)
+// drain, which runs while dV / dK / S^T execute.  The elementwise warps use packed f32x2 math.
+template <int SCHED>
 __global__ void __launch_bounds__(FB_THREADS, 1)
 attn_bwd_fused_kernel(const __grid_constant__ CUtensorMap qmap, const __grid_constant__ CUtensorMap kmap,
                       const __grid_constant__ CUtensorMap vmap, const __grid_constant__ CUtensorMap domap,
@@ -779,6 +891,7 @@ attn_bwd_fused_kernel(const __grid_constant__ CUtensorMap qmap, const __grid_con
       const uint32_t id_kk = idesc_bf16_f32(128, 128, 0, 0);  // S^T, dP^T: both K-major over D
       const uint32_t id_tm = idesc_bf16_f32(128, 128, 0, 1);  // dV, dK: A from TMEM, B MN-major
       const uint32_t id_mm = idesc_bf16_f32(128, 128, 1, 1);  // dQ^T: A = K^T, B = dS^T, both MN-major
+      const uint32_t id_sm = idesc_bf16_f32(128, 128, 0, 1);  // dK (SCHED 1): A = dS^T K-major, B = Q MN-major
       const uint32_t k = smem_u32(sK), v = smem_u32(sV), dO = smem_u32(sdO), dS = smem_u32(sdS);
       bool ok = mbar_wait(B(0), 0, 43);
       for (int i = 0; i < n_q && ok; ++i) {
@@ -786,15 +899,38 @@ attn_bwd_fused_kernel(const __grid_constant__ CUtensorMap qmap, const __grid_con
         const uint32_t q = smem_u32(sQ + slot * TILE_BYTES);
         if (!(ok = mbar_wait(B(1 + slot), (i >> 1) & 1, 44))) break;
         if (!(ok = mbar_wait(B(5), i & 1, 45))) break;
-        if (i > 0 && !(ok = mbar_wait(B(12), (i - 1) & 1, 46))) break;  // dQ^T(i-1) drained
+        if (SCHED == 0 && i > 0 && !(ok = mbar_wait(B(12), (i - 1) & 1, 46))) break;  // dQ^T(i-1) drained
         tc_fence_after();
 #pragma unroll
         for (int kk = 0; kk < D / 16; ++kk) mma_bf16_ss(T_S, desc_kmajor(k, kk), desc_kmajor(q, kk), id_kk, kk > 0);
+        if (SCHED == 1) {
+          if (i > 0 && !(ok = mbar_wait(B(12), (i - 1) & 1, 46))) break;  // dQ^T(i-1) drained from T_DP
+          tc_fence_after();
+        }
 #pragma unroll
         for (int kk = 0; kk < D / 16; ++kk) mma_bf16_ss(T_DP, desc_kmajor(v, kk), desc_kmajor(dO, kk), id_kk, kk > 0);
         mma_commit(B(7));
-        if (!(ok = mbar_wait(B(8), i & 1, 47))) break;  // P^T, dS^T in TMEM and dS^T in smem
+        if (!(ok = mbar_wait(B(8), i & 1, 47))) break;  // P^T in TMEM and dS^T in smem
         tc_fence_after();
+        if (SCHED == 1) {
+          // dQ_i^T = K^T dS^T into the dP^T columns (the elementwise warps read them before B(8))
+#pragma unroll
+          for (int kk = 0; kk < BT / 16; ++kk)
+            mma_bf16_ss(T_DP, desc_mnmajor(k, kk), desc_mnmajor(dS, kk), id_mm, kk > 0);
+          mma_commit(B(11));
+          // dV += P^T dO_i (A from TMEM)
+#pragma unroll
+          for (int kk = 0; kk < BT / 16; ++kk)
+            mma_bf16_ts(T_DV, T_S + kk * 8, desc_mnmajor(dO, kk), id_tm, (i > 0) || (kk > 0));
+          mma_commit(B(6));  // dO slot free
+          // dK += dS^T Q_i (A = dS^T from smem, K-major over queries)
+#pragma unroll
+          for (int kk = 0; kk < BT / 16; ++kk)
+            mma_bf16_ss(T_DK, desc_kmajor(dS, kk), desc_mnmajor(q, kk), id_sm, (i > 0) || (kk > 0));
+          mma_commit(B(3 + slot));  // Q slot free
+          mma_commit(B(9));         // dS^T smem free
+          continue;
+        }
         // dV += P^T dO_i ; dK += dS^T Q_i  (K = 128 queries, 8 columns of packed bf16 per step)
 #pragma unroll
         for (int kk = 0; kk < BT / 16; ++kk)
@@ -844,6 +980,37 @@ attn_bwd_fused_kernel(const __grid_constant__ CUtensorMap qmap, const __grid_con
       if (!(ok = mbar_wait(B(7), i & 1, 49))) break;
       if (i > 0 && !(ok = mbar_wait(B(9), (i - 1) & 1, 50))) break;  // dQ^T(i-1) has read dS^T smem
       tc_fence_after();
+      if (SCHED == 1) {
+        // P^T back into TMEM (the dV operand), dS^T to smem only; packed f32x2 math
+#pragma unroll
+        for (int c = 0; c < 4; ++c) {
+          uint32_t r[32], y[32];
+          tmem_ld32(T_S + lane_off + c * 32, r);
+          tmem_ld32(T_DP + lane_off + c * 32, y);
+          tmem_ld_wait();
+          uint32_t wp[16], wd[16];
+#pragma unroll
+          for (int j = 0; j < 32; j += 2) {
+            const int cc = c * 32 + j;
+            float x0, x1, p0, p1, t0, t1, d0, d1;
+            ffma2(x0, x1, __uint_as_float(r[j]), __uint_as_float(r[j + 1]), scale_log2, scale_log2, -s_vec[0][cc],
+                  -s_vec[0][cc + 1]);
+            p0 = fast_exp2(x0);
+            p1 = fast_exp2(x1);
+            if (valid_q < BT || !row_valid) {
+              p0 = (cc < valid_q && row_valid) ? p0 : 0.f;
+              p1 = (cc + 1 < valid_q && row_valid) ? p1 : 0.f;
+            }
+            fadd2(t0, t1, __uint_as_float(y[j]), __uint_as_float(y[j + 1]), -s_vec[1][cc], -s_vec[1][cc + 1]);
+            fmul2(d0, d1, p0, p1, t0, t1);
+            wp[j >> 1] = pack_bf16(p0, p1);
+            wd[j >> 1] = pack_bf16(d0, d1);
+          }
+          // columns [16c, 16c + 16) were read in chunk c or earlier
+          tmem_st16(T_S + lane_off + c * 16, wp);
+          store_row32_swizzled(sdS, row, c * 32, wd);
+        }
+      } else {
 #pragma unroll
       for (int c = 0; c < 4; ++c) {
         uint32_t r[32], y[32];
@@ -869,6 +1036,7 @@ attn_bwd_fused_kernel(const __grid_constant__ CUtensorMap qmap, const __grid_con
         tmem_st16(T_S + lane_off + c * 16, wp);
         tmem_st16(T_DP + lane_off + c * 16, wd);
         store_row32_swizzled(sdS, row, c * 32, wd);
+      }
       }
       tmem_st_wait();
       fence_async_smem();
@@ -918,7 +1086,7 @@ attn_bwd_fused_kernel(const __grid_constant__ CUtensorMap qmap, const __grid_con
       tc_fence_after();
       uint32_t r[4][32];
 #pragma unroll
-      for (int c = 0; c < 4; ++c) tmem_ld32(T_S + lane_off + c * 32, r[c]);
+      for (int c = 0; c < 4; ++c) tmem_ld32((SCHED == 1 ? T_DP : T_S) + lane_off + c * 32, r[c]);
       tmem_ld_wait();
       tc_fence_before();
       __syncwarp();
@@ -1365,7 +1533,7 @@ const char* make_dq_map(CUtensorMap* m, const float* base, int L, int H) {
 }
 
 // Key-tile-outer backward (fused or pipelined, per g_bwd_variant) into dq_acc / dk / dv.
-int g_bwd_variant = 1;  // 2: pipelined single pass; 1: fused single pass; 0: two passes
+int g_bwd_variant = 1;  // 3: fused, reordered schedule; 2: pipelined single pass; 1: fused; 0: two passes
 
 const char* run_bwd_single_pass(const void* q, const void* k, const void* v, const void* dout, const float* lse,
                                 const float* delta, const int* items_kv, int n_items_kv, int L, int H, float scale,
@@ -1380,8 +1548,10 @@ const char* run_bwd_single_pass(const void* q, const void* k, const void* v, con
     return e;
   static bool attr_f = false, attr_p = false;
   if (!pipe && !attr_f) {
-    if (cudaFuncSetAttribute(attn_bwd_fused_kernel, cudaFuncAttributeMaxDynamicSharedMemorySize, FB_SMEM) !=
-        cudaSuccess)
+    if (cudaFuncSetAttribute(attn_bwd_fused_kernel<0>, cudaFuncAttributeMaxDynamicSharedMemorySize, FB_SMEM) !=
+            cudaSuccess ||
+        cudaFuncSetAttribute(attn_bwd_fused_kernel<1>, cudaFuncAttributeMaxDynamicSharedMemorySize, FB_SMEM) !=
+            cudaSuccess)
       return "attention: cannot set smem size (fused backward)";
     attr_f = true;
   }
@@ -1397,18 +1567,28 @@ const char* run_bwd_single_pass(const void* q, const void* k, const void* v, con
     if (pipe)
       attn_bwd_pipe_kernel<<<dim3(n_items_kv, H), FB_THREADS, PB_SMEM, s>>>(qm, km, vm, dom, dqm, it, L, H, scale, lse,
                                                                            delta, dk, dv, dk_peer, dv_peer);
+    else if (g_bwd_variant == 3)
+      attn_bwd_fused_kernel<1><<<dim3(n_items_kv, H), FB_THREADS, FB_SMEM, s>>>(qm, km, vm, dom, dqm, it, L, H, scale,
+                                                                               lse, delta, dk, dv, dk_peer, dv_peer);
     else
-      attn_bwd_fused_kernel<<<dim3(n_items_kv, H), FB_THREADS, FB_SMEM, s>>>(qm, km, vm, dom, dqm, it, L, H, scale, lse,
-                                                                            delta, dk, dv, dk_peer, dv_peer);
+      attn_bwd_fused_kernel<0><<<dim3(n_items_kv, H), FB_THREADS, FB_SMEM, s>>>(qm, km, vm, dom, dqm, it, L, H, scale,
+                                                                               lse, delta, dk, dv, dk_peer, dv_peer);
   }
   return cudaGetLastError() == cudaSuccess ? nullptr : "attention single-pass backward launch failed";
 }
-int g_fwd_variant = 3;  // forward softmax: bit 0 two score chunks per TMEM wait, bit 1 packed fp32x2 math
+// Forward kernel variant (index into the launcher's table): 0 two-pass softmax awaiting PV before
+// the next score GEMM, 1 the same with in-order MMA issue, 2 one TMEM pass with the row in
+// registers, 3..5 the same with 4 / 6 / 8 of every 16 column pairs exponentiated on the FMA pipe.
+constexpr int kFwdVariants = 6;
+int g_fwd_variant = 0;
 
 }  // namespace attn
 
-void attn_set_backward_variant(int v) { attn::g_bwd_variant = v < 0 ? 0 : (v > 2 ? 2 : v); }
-void attn_set_forward_variant(int v) { attn::g_fwd_variant = v & 3; }
+void attn_set_backward_variant(int v) { attn::g_bwd_variant = v < 0 ? 0 : (v > 3 ? 3 : v); }
+int attn_get_variant(int backward) { return backward ? attn::g_bwd_variant : attn::g_fwd_variant; }
+void attn_set_forward_variant(int v) {
+  attn::g_fwd_variant = v < 0 ? 0 : (v >= attn::kFwdVariants ? attn::kFwdVariants - 1 : v);
+}
 
 const char* launch_attn_fwd(const void* q, const void* k, const void* v, const int* items, int n_items, int L, int H,
                             int head_dim, float scale, void* out, float* lse, cudaStream_t s, const uint64_t* o_peer,
@@ -1423,10 +1603,15 @@ const char* launch_attn_fwd(const void* q, const void* k, const void* v, const i
   if ((e = make_qkv_map(&qm, q, L, H)) || (e = make_qkv_map(&km, k, L, H)) || (e = make_qkv_map(&vm, v, L, H))) return e;
   typedef void (*FwdKernel)(CUtensorMap, CUtensorMap, CUtensorMap, const WorkItem*, int, int, float, __nv_bfloat16*,
                             float*, PeerRows);
-  static const FwdKernel variants[4] = {attn_fwd_kernel<0, 0>, attn_fwd_kernel<1, 0>, attn_fwd_kernel<0, 1>,
-                                        attn_fwd_kernel<1, 1>};
-  static bool attr[4] = {};
-  const int var = g_fwd_variant & 3;
+  static const FwdKernel variants[kFwdVariants] = {
+      attn_fwd_kernel<fwd_variant(FWD_PAIRED | FWD_PACKED, 0)>,
+      attn_fwd_kernel<fwd_variant(FWD_PAIRED | FWD_PACKED | FWD_INORDER, 0)>,
+      attn_fwd_kernel<fwd_variant(FWD_PACKED | FWD_INORDER | FWD_ROWREG, 0)>,
+      attn_fwd_kernel<fwd_variant(FWD_PACKED | FWD_INORDER | FWD_ROWREG, 4)>,
+      attn_fwd_kernel<fwd_variant(FWD_PACKED | FWD_INORDER | FWD_ROWREG, 6)>,
+      attn_fwd_kernel<fwd_variant(FWD_PACKED | FWD_INORDER | FWD_ROWREG, 8)>};
+  static bool attr[kFwdVariants] = {};
+  const int var = g_fwd_variant;
   if (!attr[var]) {
     if (cudaFuncSetAttribute(variants[var], cudaFuncAttributeMaxDynamicSharedMemorySize, FWD_SMEM) != cudaSuccess)
       return "attention: cannot set smem size";

@@ -34,6 +34,7 @@ int attn_error_flag(bool reset);
 int qkv_bounds_error(bool reset);
 void attn_set_backward_variant(int v);
 void attn_set_forward_variant(int v);
+int attn_get_variant(int backward);
 void launch_sumsq(const void* x, bool fp32, size_t n, float* partial, int n_part, cudaStream_t s);
 void launch_reduce_clip(const float* partial, int n, float max_norm, float* out, cudaStream_t s);
 void launch_muon_momentum(float* buf, const void* g, bool g_fp32, const float* clip, float mu, size_t n, void* u,
@@ -717,6 +718,7 @@ PYBIND11_MODULE(TORCH_EXTENSION_NAME, m) {
   m.def("gemm_force_cta_group", &pan::gemm_force_cta_group);
   m.def("attn_set_backward_variant", &pan::attn_set_backward_variant);
   m.def("attn_set_forward_variant", &pan::attn_set_forward_variant);
+  m.def("attn_get_variant", &pan::attn_get_variant);
   m.def("gemm_tuning", &pan::gemm_tuning);
   m.def("gemm_grouped_nt", &pan::gemm_grouped_nt);
   m.def("gemm_batched", &pan::gemm_batched);

@@ -69,6 +69,7 @@ struct Params {
   int epi;
   int probe;  // timing experiments only: bit 0 skips the epilogue stores, bit 1 re-reads k-block 0
   int reduce_add;  // D += acc through TMA reduce-add stores (no read of D by the kernel)
+  int band_m;      // tile order: 0 = N bands of 8 tiles, > 0 = M bands of band_m tiles
   int accumulate;  // host-side only: folded into C = D, beta = 1
   // batched GEMMs: operand z-coordinate = batch index; D/C advance by their batch strides
   int batch;
@@ -90,13 +91,24 @@ struct TmapSet {
   CUtensorMap aux2[kMaxGroups];
 };
 
+// Tile order (per row group).  band_m == 0: bands of up to 8 N-tiles, M-tile outer within a band
+// (consecutive tiles share A; for deep K the ~74 concurrent tiles form a near-square block).
+// band_m > 0: bands of band_m M-tiles, N-tile outer, M-tile inner: the band's A rows (sized on the
+// host to stay L2-resident) are read from DRAM once, and each B tile once per band.
 __device__ __forceinline__ void tile_coords(const Params& p, int t, int& g, int& mb, int& nb) {
   t = t % p.tiles_per_batch;
   g = 0;
   while (g + 1 < p.n_groups && t >= p.tile_prefix[g + 1]) ++g;
   const int local = t - p.tile_prefix[g];
   const int mt = p.m_tiles[g], nt = p.n_tiles[g];
-  // bands of up to 8 N-tiles: consecutive tiles share the A tile, the band's B stays in L2
+  if (p.band_m > 0) {
+    const int band = local / (p.band_m * nt);
+    const int height = min(p.band_m, mt - band * p.band_m);
+    const int idx = local - band * p.band_m * nt;
+    nb = idx / height;
+    mb = band * p.band_m + idx % height;
+    return;
+  }
   const int band = local / (mt * 8);
   const int width = min(8, nt - band * 8);
   const int idx = local - band * mt * 8;
@@ -484,6 +496,9 @@ const char* make_out_map(CUtensorMap* m, const void* base, int row_end, int n, l
 int g_forced_cta_group = 0;  // 0: choose per launch; 1 / 2: force (tests, A/B timing)
 int g_pair_stages = 6;       // smem stages of the CTA-pair kernel (4 or 6)
 int g_probe = 0;             // Params::probe of every launch (timing experiments)
+// Tile order: A rows of one M band up to g_band_mb MB (0 = always N bands).  M bands are used when a
+// 128/256-row A tile is at most 4 MB (K <= 8192): then the band stays in L2 while B streams past.
+int g_band_mb = 0;
 
 int num_sms() {
   static int n = 0;
@@ -594,6 +609,12 @@ const char* launch_gemm(const GemmArgs& a, cudaStream_t stream) {
     maps.aux2[g] = maps.aux2[0];
   }
   p.tiles_per_batch = tiles;
+  p.band_m = 0;
+  const long long a_tile_bytes = (long long)tile_m * a.K * 2;
+  if (g_band_mb > 0 && a_tile_bytes <= (4ll << 20)) {
+    const long long band = ((long long)g_band_mb << 20) / a_tile_bytes;
+    p.band_m = (int)(band < 1 ? 1 : band);
+  }
   tiles *= p.batch;
   if (tiles == 0) return nullptr;
   p.probe = g_probe;
@@ -646,9 +667,10 @@ const char* launch_gemm(const GemmArgs& a, cudaStream_t stream) {
 }
 
 void gemm_force_cta_group(int cg) { gemm::g_forced_cta_group = (cg == 1 || cg == 2) ? cg : 0; }
-void gemm_tuning(int pair_stages, int probe) {
+void gemm_tuning(int pair_stages, int probe, int band_mb) {
   gemm::g_pair_stages = pair_stages == 4 ? 4 : 6;
   gemm::g_probe = probe;
+  gemm::g_band_mb = band_mb < 0 ? 0 : band_mb;
 }
 
 int gemm_error_flag(bool reset) {

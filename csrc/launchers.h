@@ -68,8 +68,9 @@ const char* launch_gemm(const GemmArgs& args, cudaStream_t s);
 int gemm_error_flag(bool reset);
 // 0: CTA pairs or single CTAs chosen per launch; 1 / 2: forced.
 void gemm_force_cta_group(int cg);
-// CTA-pair smem stages (4 or 6) and timing-probe bits (0 in normal use).
-void gemm_tuning(int pair_stages, int probe);
+// CTA-pair smem stages (4 or 6), timing-probe bits (0 in normal use) and the M-band budget in MB
+// of the tile order (0: N bands only).
+void gemm_tuning(int pair_stages, int probe, int band_mb);
 
 // ------------------------------------------------------------------ comm_ops.cu (peer memory)
 const char* launch_symm_barrier(const uint64_t* pads, int rank, int world, uint32_t epoch, int channel,
