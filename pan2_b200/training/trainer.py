@@ -236,6 +236,8 @@ class Trainer:
             dist.barrier(group=self.layout.cpu_group)
 
     def save_checkpoint(self) -> str:
+        if self.device.type == "cuda":
+            self._check_device_errors()  # never mark a checkpoint complete over incomplete kernel output
         step = self.global_step
         root = self.checkpoint_dir(step)
         if self.is_main:
@@ -324,9 +326,16 @@ class Trainer:
 
     def _check_device_errors(self) -> None:
         """Stop the run when a kernel gave up a bounded wait (a peer that never arrived, a copy
-        that never landed): its outputs are incomplete, so continuing would train on them."""
+        that never landed): its outputs are incomplete, so continuing would train on them, and a
+        checkpoint written afterwards would be marked complete over bad state.  Every rank reads its
+        flag and the ranks agree on the largest code (one small all-reduce over the host group), so
+        all of them stop together instead of the others waiting in their next collective."""
         from ..ops._ext import ext
         flag = int(ext().error_flag(True))
+        if self.world > 1:
+            t = torch.tensor([flag], dtype=torch.int64)
+            dist.all_reduce(t, op=dist.ReduceOp.MAX, group=self.layout.cpu_group)
+            flag = int(t.item())
         if flag:
             raise RuntimeError(f"device error code {flag} after step {self.global_step - 1}: a kernel stopped "
                                "waiting (peer rank gone or stalled, or a transfer that never completed)")
@@ -423,7 +432,7 @@ class Trainer:
                 with nvtx("train_step"):
                     stats = self.runner.device_step(batches, poison=self.injector.poisons_update(self.global_step))
                 stats = self.injector.after_step(self.global_step, stats)
-                if cuda and (self.global_step - 1) % max(1, cfg.log_interval) == 0:
+                if cuda:  # every step: the flag read is one small device-to-host copy
                     self._check_device_errors()
                 if meta is not None:
                     self._update_util(meta)
@@ -465,6 +474,8 @@ class Trainer:
                                 f"({self.consecutive_skipped}/{cfg.max_consecutive_skipped_steps} consecutive skips)")
                 if recover:
                     self.heartbeat.beat("recover_from_checkpoint")
+                    if cuda:
+                        self._check_device_errors()
                     self.recover()
                 elif self.global_step % cfg.save_interval == 0:
                     self.heartbeat.beat("save_checkpoint")
@@ -484,6 +495,8 @@ class Trainer:
             self.log_packing_utilization()
             if not ckpt.is_complete(self.checkpoint_dir(self.global_step)):
                 self.save_checkpoint()
+            elif cuda:
+                self._check_device_errors()
             log.info(f"Training finished at step {self.global_step}")
             if self.wandb is not None:
                 self.wandb.finish()
