@@ -30,6 +30,7 @@
 #include <cuda_runtime.h>
 #include <stdint.h>
 
+#include <atomic>
 #include <mutex>
 
 #include "common.cuh"
@@ -45,7 +46,9 @@ namespace {
 constexpr int kTileElems = 2048;  // 256 threads x 8 elements
 constexpr int kMaxDevices = 64;
 
-float* g_partials_addr[kMaxDevices] = {nullptr};
+// Device address of g_mse_partials per device, looked up once: read without the lock (acquire),
+// written under it (release).
+std::atomic<float*> g_partials_addr[kMaxDevices];
 std::mutex g_setup_mutex;
 thread_local const char* g_last_error = "no error";
 
@@ -115,18 +118,25 @@ int pan2_mse_sums_noalloc(const void* pred, const void* target, long long n, flo
     g_last_error = "pan2_mse_sums_noalloc: no current CUDA device";
     return 3;
   }
-  float* partials = g_partials_addr[dev];
+  float* partials = g_partials_addr[dev].load(std::memory_order_acquire);
   if (partials == nullptr) {
     std::lock_guard<std::mutex> lock(g_setup_mutex);
-    if (g_partials_addr[dev] == nullptr) {
+    partials = g_partials_addr[dev].load(std::memory_order_relaxed);
+    if (partials == nullptr) {
       void* ptr = nullptr;
       if (cudaGetSymbolAddress(&ptr, g_mse_partials) != cudaSuccess || ptr == nullptr) {
         g_last_error = "pan2_mse_sums_noalloc: cudaGetSymbolAddress failed for the scratch array";
         return 3;
       }
-      g_partials_addr[dev] = static_cast<float*>(ptr);
+      partials = static_cast<float*>(ptr);
+      g_partials_addr[dev].store(partials, std::memory_order_release);
     }
-    partials = g_partials_addr[dev];
+  }
+  // An error left by an earlier, unrelated launch is reported as such and left pending for its
+  // owner (peek, not get), so it is never mistaken for a failure of this call.
+  if (cudaPeekAtLastError() != cudaSuccess) {
+    g_last_error = "pan2_mse_sums_noalloc: an earlier CUDA error is pending on this thread; nothing was launched";
+    return 3;
   }
   cudaStream_t s = static_cast<cudaStream_t>(stream);
   const int n_part = (int)(tiles > 0 ? tiles : 1);  // n == 0: one CTA writes a zero partial

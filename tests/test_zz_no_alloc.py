@@ -45,6 +45,27 @@ def test_noalloc_mse_matches_allocating_path_twice():
         assert abs(out[0].item() - ref[0].item()) <= 1e-4 * abs(ref[0].item()), (trial, out, ref)
 
 
+@pytest.mark.parametrize("n", [0, 8, 2048 * 3 + 8, 16384 * 2048])
+def test_noalloc_mse_edge_sizes(n):
+    """Empty input, one partial tile, a ragged last tile and the largest size the scratch holds."""
+    from pan2_b200.ops._ext import ext
+    fn, err = _lib()
+    torch.manual_seed(n % 97)
+    pred = torch.randn(max(n, 8), device="cuda").to(torch.bfloat16)
+    tgt = torch.randn(max(n, 8), device="cuda").to(torch.bfloat16)
+    out = torch.full((2,), -1.0, device="cuda")
+    rc = fn(pred.data_ptr(), tgt.data_ptr(), n, out.data_ptr(), torch.cuda.current_stream().cuda_stream)
+    assert rc == 0, err().decode()
+    torch.cuda.synchronize()
+    if n == 0:
+        assert out.tolist() == [0.0, 0.0]
+        return
+    ref = ext().mse_fwd(pred[:n].view(n // 8, 8), tgt[:n].view(n // 8, 8), n // 8)
+    torch.cuda.synchronize()
+    assert out[1].item() == n
+    assert abs(out[0].item() - ref[0].item()) <= 1e-4 * abs(ref[0].item()), (n, out, ref)
+
+
 def test_noalloc_mse_rejects_sizes_above_the_limit():
     fn, err = _lib()
     x = torch.zeros(8, device="cuda", dtype=torch.bfloat16)
