@@ -92,7 +92,7 @@ class Timer:
         return out
 
 
-def gemm_cases(small: bool):
+def gemm_cases(small: bool, only=None):
     rows = 8192 if small else CLIPS * CLIP_TOKENS
     # (name, M, N, K, layout): NT = x @ w^T (forward), NN = dy @ w (input grad), TN = x^T @ dy (weight grad)
     cases = [("qkv_fwd", rows, 3 * HIDDEN, HIDDEN, "NT"), ("ffn_up_fwd", rows, FFN, HIDDEN, "NT"),
@@ -101,7 +101,7 @@ def gemm_cases(small: bool):
     return cases[:1] if small else cases
 
 
-def run_gemm(name, M, N, K, layout, timer, library, peaks, band_mbs=(None,)):
+def run_gemm(name, M, N, K, layout, timer, library, peaks, band_mbs=(None,), probes=(None,)):
     E = ext()
     dev = "cuda"
     a = torch.randn(K, M, device=dev, dtype=torch.bfloat16) if layout == "TN" else \
@@ -112,14 +112,15 @@ def run_gemm(name, M, N, K, layout, timer, library, peaks, band_mbs=(None,)):
     fn = lambda: E.gemm(a, b, out, layout != "TN", layout == "NT", None, None, False)
     fl = 2.0 * M * N * K
     recs = []
-    for band in band_mbs:
-        if band is not None:
-            E.gemm_tuning(6, 0, int(band))
+    for band, probe in [(b, pr) for b in band_mbs for pr in probes]:
+        E.gemm_tuning(6, int(probe or 0), GEMM_BAND_MB if band is None else int(band))
         ms = timer(fn)
         rec = dict(case=f"gemm_{name}", shape=[M, N, K], layout=layout, out_dtype=str(out.dtype).split(".")[-1],
                    ms=round(ms, 4), tflops=round(fl / ms / 1e9, 1), frac_of_peak=round(fl / ms / 1e9 / peaks[1], 3))
         if band is not None:
             rec["band_mb"] = int(band)
+        if probe:
+            rec["probe"] = int(probe)
         rec.update(timer.clock_fields("", ms))
         recs.append(rec)
     E.gemm_tuning(6, 0, GEMM_BAND_MB)
@@ -248,6 +249,8 @@ def main():
     ap.add_argument("--attn-fwd-variant", default=None, help="comma list of attention forward variants (0..5)")
     ap.add_argument("--gemm-band-mb", default=None,
                     help="comma list of GEMM M-band budgets in MB (0 = N bands only)")
+    ap.add_argument("--gemm-probe", default=None,
+                    help="comma list of GEMM probe bits (4: waits sleep between polls; timing experiments)")
     ap.add_argument("--sustain-s", type=float, default=0.0,
                     help="run each op back to back this long before timing (clocks settle under the power cap)")
     args = ap.parse_args()
@@ -258,7 +261,8 @@ def main():
     library = not args.no_library
     if pat.search("gemm"):
         for c in gemm_cases(args.small):
-            for rec in run_gemm(*c, timer=timer, library=library, peaks=peaks, band_mbs=lst(args.gemm_band_mb)):
+            for rec in run_gemm(*c, timer=timer, library=library, peaks=peaks, band_mbs=lst(args.gemm_band_mb),
+                                probes=lst(args.gemm_probe)):
                 print(json.dumps(rec), flush=True)
     which = [w for w in ("fwd", "bwd") if pat.search("attn_" + w)]
     if which:

@@ -61,6 +61,34 @@ __device__ __forceinline__ bool mbar_try_wait(uint32_t bar, uint32_t parity) {
   return ok != 0;
 }
 
+// try_wait with a suspend-time hint: the thread sleeps in hardware until the phase completes or
+// `hint_ns` elapses, instead of re-polling.
+__device__ __forceinline__ bool mbar_try_wait_hint(uint32_t bar, uint32_t parity, uint32_t hint_ns) {
+  uint32_t ok;
+  asm volatile(
+      "{\n\t.reg .pred p;\n\t"
+      "mbarrier.try_wait.parity.acquire.cta.shared::cta.b64 p, [%1], %2, %3;\n\t"
+      "selp.u32 %0, 1, 0, p;\n\t}"
+      : "=r"(ok)
+      : "r"(bar), "r"(parity), "r"(hint_ns)
+      : "memory");
+  return ok != 0;
+}
+
+// Bounded wait whose polls sleep up to `hint_ns` each (see mbar_wait for the limit and error code).
+__device__ __forceinline__ bool mbar_wait_sleep(uint32_t bar, uint32_t parity, int code, uint32_t hint_ns,
+                                                uint64_t limit_ns = 4000000000ull) {
+  if (mbar_try_wait(bar, parity)) return true;
+  const uint64_t t0 = global_timer_ns();
+  while (true) {
+    if (mbar_try_wait_hint(bar, parity, hint_ns)) return true;
+    if (global_timer_ns() - t0 > limit_ns) {
+      atomicCAS(&g_error_flag, 0, code);
+      return false;
+    }
+  }
+}
+
 // Wait for the phase with the given parity to complete.  Gives up after `limit_ns` (default 4 s),
 // sets g_error_flag to `code` and returns false; callers then unwind instead of hanging the GPU.
 __device__ __forceinline__ bool mbar_wait(uint32_t bar, uint32_t parity, int code = 1,

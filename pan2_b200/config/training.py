@@ -17,7 +17,7 @@ from dataclasses import MISSING, dataclass, field, fields
 from enum import Enum
 from typing import Any, Dict, List, Mapping, Optional
 
-from ..diffusion.flow_matching import TimestepDistribution, TimestepShiftMode
+from ..diffusion.flow_matching import NoiseDraw, ShiftRule
 
 
 class ConditioningSchema(str, Enum):
@@ -91,14 +91,13 @@ class TrainingConfig:
     max_grad_norm: float = opt(1.0, float, "Global gradient-norm clip; 0 disables.")
     # -- flow matching
     num_train_timesteps: int = opt(1000, int, "Length T of the training time axis.", cli=False)
-    snr_type: TimestepDistribution = opt(TimestepDistribution.LOGNORM, str, "Noise-level distribution.",
-                                         flags=["--flow_snr_type"], dest="flow_snr_type",
-                                         choices=[d.value for d in TimestepDistribution], convert=TimestepDistribution)
+    snr_type: NoiseDraw = opt(NoiseDraw.LOGNORM, str, "Noise-level distribution.",
+                              flags=["--flow_snr_type"], dest="flow_snr_type",
+                              choices=[d.value for d in NoiseDraw], convert=NoiseDraw)
     flow_lognorm_loc: float = opt(0.0, float, "Logit-normal mean.")
     flow_lognorm_scale: float = opt(1.0, float, "Logit-normal std.")
-    train_timestep_shift_mode: TimestepShiftMode = opt(TimestepShiftMode.FIXED, str, "fixed or dynamic shift.",
-                                                       choices=[m.value for m in TimestepShiftMode],
-                                                       convert=TimestepShiftMode)
+    train_timestep_shift_mode: ShiftRule = opt(ShiftRule.FIXED, str, "fixed or dynamic shift.",
+                                               choices=[m.value for m in ShiftRule], convert=ShiftRule)
     train_timestep_shift: float = opt(5.0, float, "Fixed-mode time shift s.")
     train_timestep_rescale_factor: float = opt(0.5, float, "Dynamic mode: exponent scale.")
     train_timestep_max_shift: float = opt(1000.0, float, "Dynamic mode: upper bound of the shift.")

@@ -1,20 +1,23 @@
-"""Classifier-free guidance controls and spatiotemporal skip guidance (STG).
+"""Guidance schedule for sampling: classifier-free guidance (CFG) windows and spatiotemporal skip
+guidance (STG).
 
-Semantics of the reference (pan/utils/inference_guidance.py:9-111):
+Behaviour matches the reference's guidance controls (pan/utils/inference_guidance.py:9-111):
 
-* a :class:`GuidancePlan` makes CFG active at step ``i`` when ``i < end_step`` and (``i >= start_step``
-  or a warmup scale above 1 is set) and ``i`` is outside the optional skip interval; elsewhere the
-  positive prediction is used alone;
-* before ``start_step`` the warmup scale replaces the guidance scale;
-* CFG is ``neg + scale * (pos - neg)`` in the prediction dtype; STG then adds
-  ``stg_scale * (pos - weak)`` in fp32 and casts back, where ``weak`` is the positive prediction of a
-  forward that skips the given blocks (text-to-video only).  The order of these operations is part of
-  the bf16 result.
+* steps are zero-based and windows end-exclusive; CFG runs at step ``i`` when ``i < end_step``, and
+  either ``i >= start_step`` or a warmup scale above 1 was given, and ``i`` is outside the optional
+  skip interval; at every other step the positive prediction is used alone;
+* steps before ``start_step`` use the warmup scale in place of the guidance scale;
+* the mix is ``neg + scale * (pos - neg)`` in the prediction dtype, then STG adds
+  ``stg_scale * (pos - weak)`` in fp32 and casts back (``weak`` comes from a forward that skips
+  some blocks).  That order of operations is part of the bf16 result, so it is kept.
+
+Here the plan is resolved once into a per-step table (:attr:`GuidancePlan.scales`: 0 for a
+positive-only step, otherwise the scale of that step), which the sampler indexes.
 """
 from __future__ import annotations
 
 import math
-from dataclasses import dataclass
+from dataclasses import dataclass, field
 from numbers import Integral, Real
 from typing import Callable, Optional, Tuple
 
@@ -23,15 +26,24 @@ import torch
 SCHEDULES = ("standard", "early_refine_2x")
 
 
-def validate_sampling_extensions(num_steps: int, timestep_schedule: str = "standard") -> None:
-    if timestep_schedule not in SCHEDULES:
-        raise ValueError(f"unknown timestep_schedule {timestep_schedule!r}")
-    if timestep_schedule == "early_refine_2x" and num_steps != 50:
-        raise ValueError("early_refine_2x requires exactly 50 inference steps")
-
-
-def _is_int(v) -> bool:
+def _whole(v) -> bool:
     return isinstance(v, Integral) and not isinstance(v, bool)
+
+
+def _real(v) -> bool:
+    return isinstance(v, Real) and not isinstance(v, bool) and math.isfinite(v)
+
+
+def _check(ok: bool, message: str) -> None:
+    if not ok:
+        raise ValueError(message)
+
+
+def validate_sampling_extensions(num_steps: int, timestep_schedule: str = "standard") -> None:
+    """The timestep schedule is known and, for ``early_refine_2x``, runs its fixed 50 steps."""
+    _check(timestep_schedule in SCHEDULES, f"timestep_schedule {timestep_schedule!r} is not one of {SCHEDULES}")
+    _check(timestep_schedule != "early_refine_2x" or num_steps == 50,
+           "the early_refine_2x schedule is defined for 50 sampling steps only")
 
 
 @dataclass(frozen=True)
@@ -42,15 +54,17 @@ class GuidancePlan:
     stg_scale: float
     skip_interval: Optional[Tuple[int, int]] = None
     warmup_scale: float = 1.0
+    # per step: None = positive only, "warmup" = warmup scale, "main" = the caller's guidance scale
+    modes: Tuple[Optional[str], ...] = field(default=(), compare=False)
+
+    def _mode(self, i: int) -> Optional[str]:
+        _check(_whole(i), f"guidance step index {i!r} is not an integer")
+        _check(0 <= i < self.num_steps, f"guidance step index {i} is not within the {self.num_steps} sampling steps")
+        return self.modes[i]
 
     def active(self, i: int) -> bool:
-        if not _is_int(i):
-            raise ValueError("step_index must be an integer")
-        if not 0 <= i < self.num_steps:
-            raise ValueError("step_index is outside the scheduler's timestep sequence")
-        in_window = i < self.end_step and (i >= self.start_step or self.warmup_scale > 1)
-        skipped = self.skip_interval is not None and self.skip_interval[0] <= i < self.skip_interval[1]
-        return in_window and not skipped
+        """Whether step ``i`` mixes the negative prediction in."""
+        return self._mode(i) is not None
 
     def scale_at(self, i: int, guidance_scale: float) -> float:
         return self.warmup_scale if i < self.start_step else guidance_scale
@@ -58,46 +72,51 @@ class GuidancePlan:
 
 def resolve_guidance_plan(num_steps: int, *, start_step: int = 0, end_step: Optional[int] = None,
                           stg_scale: float = 0.0, skip_interval=None, warmup_scale: float = 1.0) -> GuidancePlan:
-    end_step = num_steps if end_step is None else end_step
-    for name, v in (("num_steps", num_steps), ("start_step", start_step), ("end_step", end_step)):
-        if not _is_int(v):
-            raise ValueError(f"{name} must be an integer")
-    if num_steps < 1:
-        raise ValueError("num_steps must be positive")
-    if not 0 <= start_step < end_step <= num_steps:
-        raise ValueError("require 0 <= start_step < end_step <= the scheduler's step count")
+    """Check the window against the sampler's step count and tabulate the mode of every step."""
+    stop = num_steps if end_step is None else end_step
+    for label, v in (("num_steps", num_steps), ("start_step", start_step), ("end_step", stop)):
+        _check(_whole(v), f"{label} ({v!r}) is not an integer")
+    _check(num_steps >= 1, "there must be at least one sampling step")
+    _check(0 <= start_step < stop <= num_steps,
+           f"CFG window [{start_step}, {stop}) does not fit in {num_steps} sampling steps")
+    skip = None
     if skip_interval is not None:
-        if not isinstance(skip_interval, (list, tuple)) or len(skip_interval) != 2 or not all(map(_is_int, skip_interval)):
-            raise ValueError("skip_interval must be a pair of integer step indices")
-        if not 0 <= skip_interval[0] < skip_interval[1] <= num_steps:
-            raise ValueError("require 0 <= skip_interval start < end <= the scheduler's step count")
-        skip_interval = (int(skip_interval[0]), int(skip_interval[1]))
-    if not isinstance(stg_scale, Real) or isinstance(stg_scale, bool) or not math.isfinite(stg_scale) or stg_scale < 0:
-        raise ValueError("stg_scale must be finite and nonnegative")
-    if (not isinstance(warmup_scale, Real) or isinstance(warmup_scale, bool) or not math.isfinite(warmup_scale)
-            or warmup_scale < 1):
-        raise ValueError("warmup_scale must be finite and at least 1")
-    return GuidancePlan(int(num_steps), int(start_step), int(end_step), float(stg_scale), skip_interval,
-                        float(warmup_scale))
+        _check(isinstance(skip_interval, (list, tuple)) and len(skip_interval) == 2
+               and all(_whole(v) for v in skip_interval), "skip_interval takes two integer step indices")
+        a, b = int(skip_interval[0]), int(skip_interval[1])
+        _check(0 <= a < b <= num_steps, f"skip interval [{a}, {b}) does not fit in {num_steps} sampling steps")
+        skip = (a, b)
+    _check(_real(stg_scale) and stg_scale >= 0, f"stg_scale ({stg_scale!r}) must be a finite number >= 0")
+    _check(_real(warmup_scale) and warmup_scale >= 1, f"warmup_scale ({warmup_scale!r}) must be a finite number >= 1")
+    modes = []
+    for i in range(num_steps):
+        if i >= stop or (skip is not None and skip[0] <= i < skip[1]):
+            modes.append(None)
+        elif i >= start_step:
+            modes.append("main")
+        else:
+            modes.append("warmup" if warmup_scale > 1 else None)
+    return GuidancePlan(int(num_steps), int(start_step), int(stop), float(stg_scale), skip, float(warmup_scale),
+                        tuple(modes))
 
 
 def apply_guidance(negative: torch.Tensor, positive: torch.Tensor, guidance_scale: float, *, step_index: int,
                    plan: GuidancePlan, weak_predict_fn: Optional[Callable[[], torch.Tensor]] = None) -> torch.Tensor:
-    if negative.shape != positive.shape or negative.dtype != positive.dtype:
-        raise ValueError("CFG predictions must have matching shape and dtype")
-    if negative.device != positive.device or not positive.is_floating_point():
-        raise ValueError("CFG predictions must be floating tensors on the same device")
-    if (not isinstance(guidance_scale, Real) or isinstance(guidance_scale, bool) or not math.isfinite(guidance_scale)
-            or guidance_scale <= 1):
-        raise ValueError("this guidance path requires a finite guidance_scale > 1")
-    if not plan.active(step_index):
+    """The prediction used at ``step_index``; ``weak_predict_fn`` runs only when STG applies."""
+    mode = plan._mode(step_index)
+    _check(negative.shape == positive.shape and negative.dtype == positive.dtype,
+           "negative and positive predictions differ in shape or dtype")
+    _check(negative.device == positive.device and positive.is_floating_point(),
+           "negative and positive predictions must be floating-point tensors on one device")
+    _check(_real(guidance_scale) and guidance_scale > 1, f"guidance_scale ({guidance_scale!r}) must be finite and > 1")
+    if mode is None:
         return positive
-    guided = negative + plan.scale_at(step_index, guidance_scale) * (positive - negative)
-    if plan.stg_scale:
-        if weak_predict_fn is None:
-            raise ValueError("STG requires a weak positive prediction")
-        weak = weak_predict_fn()
-        if weak.shape != positive.shape or weak.dtype != positive.dtype or weak.device != positive.device:
-            raise ValueError("STG prediction must match the positive shape, dtype and device")
-        guided = (guided.float() + plan.stg_scale * (positive.float() - weak.float())).to(guided.dtype)
-    return guided
+    scale = plan.warmup_scale if mode == "warmup" else guidance_scale
+    out = negative + scale * (positive - negative)
+    if not plan.stg_scale:
+        return out
+    _check(weak_predict_fn is not None, "stg_scale > 0 needs the skip-block (weak) prediction")
+    weak = weak_predict_fn()
+    _check(weak.shape == positive.shape and weak.dtype == positive.dtype and weak.device == positive.device,
+           "the skip-block prediction differs from the positive one in shape, dtype or device")
+    return (out.float() + plan.stg_scale * (positive.float() - weak.float())).to(out.dtype)

@@ -1,186 +1,242 @@
-"""Prompt-file parsing for generation, frame counts, negative-prompt rendering and resume checks.
+"""Prompt files for generation: entry parsing, frame counts, negative prompts and resume checks.
 
-Behaviour of the reference's inference/inputs.py:1-189:
+Accepts the reference's prompt-file format and follows its rules (inference/inputs.py:1-189 of the
+reference), implemented here as a per-entry reader:
 
-* a prompt file is a JSON list of entries, or an object with exactly one of ``entries`` / ``prompts`` /
-  ``data`` holding that list;
-* an entry's task is ``task`` / ``type``, else ``i2v`` when it names a reference image (``image_path``,
-  ``image`` or ``ref_image``), else ``t2v``; its prompt is the first non-empty of ``refined_prompt``,
-  ``refined_prompts``, ``prompt``, ``caption``;
-* the frame count is ``4 * ceil(duration_sec * fps / 4) + 1`` (the counts the Wan VAE encodes), else
-  ``frames`` / ``num_target_frames``, else the fallback;
-* the output is ``<task>_<sanitised id>.mp4`` or ``relative_path``; unsafe or duplicate paths are
-  rejected; with task ``auto`` outputs are namespaced by task;
-* a structured (JSON) negative prompt has every ``time_range_sec`` rewritten to the clip's duration;
-* :func:`is_complete` skips an output only when the video and its ``_config.json`` exist and every
-  generation argument matches; a mismatch is an error (fail closed).
+* the file is a JSON list of entries, or an object holding that list under exactly one of
+  ``entries`` / ``prompts`` / ``data``;
+* an entry's task is its ``task`` / ``type`` field, else ``i2v`` when it names a reference image
+  (``image_path`` / ``image`` / ``ref_image``), else ``t2v``; its prompt is the first non-empty of
+  ``refined_prompt``, ``refined_prompts``, ``prompt``, ``caption``;
+* frames: ``4 * ceil(duration_sec * fps / 4) + 1`` (frame counts the Wan VAE encodes), else
+  ``frames`` / ``num_target_frames``, else the fallback; computed in exact rational arithmetic;
+* output: ``<task>_<sanitised id>.mp4``, else ``relative_path``, else ``<task>_<index>.mp4``; paths
+  that leave the output folder or repeat are errors; with task ``auto`` each task gets a subfolder;
+* a negative prompt that is a JSON object has every ``time_range_sec`` set to the clip's span;
+* :func:`is_complete` lets a run skip an output only when the video and its ``_config.json`` exist
+  and every generation argument matches; a finished output with other settings is an error.
 """
 from __future__ import annotations
 
 import json
+import math
 import re
-from decimal import ROUND_CEILING, Decimal, InvalidOperation
+from fractions import Fraction
 from pathlib import Path, PurePosixPath
-from typing import Dict, List
+from typing import Dict, List, Optional
 
 GUIDANCE_KEYS = ("cfg_start_step", "cfg_end_step", "stg_scale", "stg_skip_layers")
-ROUTING_ARGS = {"prompt_json", "output_dir", "prompt_shard_index", "prompt_shard_count", "skip_existing",
-                "output_path", "task", "image_root"}
+# arguments that only choose where an output goes; every other argument must match to resume
+ROUTING_ARGS = frozenset({"prompt_json", "output_dir", "prompt_shard_index", "prompt_shard_count",
+                          "skip_existing", "output_path", "task", "image_root"})
+TASKS = ("t2v", "i2v")
+IMAGE_KEYS = ("image_path", "image", "ref_image")
+PROMPT_KEYS = ("refined_prompt", "refined_prompts", "prompt", "caption")
+NEGATIVE_KEYS = ("negative_prompt", "negative_prompts", "neg_prompt")
+WRAPPER_KEYS = ("entries", "prompts", "data")
 
 
-def _positive(value, name: str, integer: bool = False) -> Decimal:
+def _exact_positive(value, what: str, whole: bool = False) -> Fraction:
+    """``value`` as an exact positive rational (a whole number when ``whole``)."""
+    problem = f"{what} must be a positive finite {'integer' if whole else 'number'}, got {value!r}"
     if isinstance(value, bool):
-        raise ValueError(f"{name} must be positive and finite")
+        raise ValueError(problem)
     try:
-        d = Decimal(str(value))
-    except (InvalidOperation, ValueError):
-        raise ValueError(f"{name} must be positive and finite") from None
-    if not d.is_finite() or d <= 0 or (integer and d != d.to_integral_value()):
-        raise ValueError(f"{name} must be positive and finite" + (" integer" if integer else ""))
-    return d
+        q = Fraction(str(value).strip())
+    except (ValueError, ZeroDivisionError):
+        raise ValueError(problem) from None
+    if q <= 0 or (whole and q.denominator != 1):
+        raise ValueError(problem)
+    return q
 
 
 def resolve_frames(entry: Dict, fps=24, fallback=121) -> int:
-    fps_d = _positive(fps, "fps")
-    fb = _positive(fallback, "video_length", integer=True)
+    rate = _exact_positive(fps, "fps")
+    default = _exact_positive(fallback, "video_length", whole=True)
     if entry.get("duration_sec") is not None:
-        dur = _positive(entry["duration_sec"], "duration_sec")
-        return int((dur * fps_d / 4).to_integral_value(rounding=ROUND_CEILING)) * 4 + 1
+        seconds = _exact_positive(entry["duration_sec"], "duration_sec")
+        return 4 * math.ceil(seconds * rate / 4) + 1
     for key in ("frames", "num_target_frames"):
         if entry.get(key) is not None:
-            return int(_positive(entry[key], key, integer=True))
-    return int(fb)
+            return int(_exact_positive(entry[key], key, whole=True))
+    return int(default)
+
+
+def _stamp_time_ranges(node, span: str):
+    if isinstance(node, list):
+        return [_stamp_time_ranges(v, span) for v in node]
+    if isinstance(node, dict):
+        return {k: span if k == "time_range_sec" else _stamp_time_ranges(v, span) for k, v in node.items()}
+    return node
 
 
 def render_negative_duration(text, video_length: int, fps=24):
+    """A structured (JSON object) negative prompt with its time ranges set to this clip's duration;
+    any other text unchanged."""
     try:
-        doc = json.loads(text)
+        parsed = json.loads(text)
     except (TypeError, json.JSONDecodeError):
         return text
-    if not isinstance(doc, dict):
+    if not isinstance(parsed, dict):
         return text
-    span = f"0 to {(int(video_length) - 1) / float(fps):g}"
-
-    def walk(node):
-        if isinstance(node, dict):
-            return {k: (span if k == "time_range_sec" else walk(v)) for k, v in node.items()}
-        if isinstance(node, list):
-            return [walk(v) for v in node]
-        return node
-
-    return json.dumps(walk(doc), ensure_ascii=False, separators=(",", ":"))
+    span = "0 to " + format((int(video_length) - 1) / float(fps), "g")
+    return json.dumps(_stamp_time_ranges(parsed, span), ensure_ascii=False, separators=(",", ":"))
 
 
-def _entries(payload):
+def _entry_list(payload) -> list:
     if isinstance(payload, dict):
-        keys = [k for k in ("entries", "prompts", "data") if k in payload]
-        if len(keys) != 1:
-            raise ValueError("a prompt wrapper object needs exactly one entries/prompts/data list")
-        payload = payload[keys[0]]
+        present = [k for k in WRAPPER_KEYS if k in payload]
+        if len(present) != 1:
+            raise ValueError(f"a prompt-file object must hold its entries under exactly one of {WRAPPER_KEYS}; "
+                             f"found {present}")
+        payload = payload[present[0]]
     if not isinstance(payload, list):
-        raise ValueError("the prompt JSON must contain a list of entries")
+        raise ValueError("a prompt file holds a list of entries")
     return payload
+
+
+def _single_alias(entry: Dict, keys, what: str, truthy: bool = True) -> Optional[str]:
+    """The one alias of ``keys`` the entry uses (all present aliases must agree)."""
+    used = [k for k in keys if (entry.get(k) if truthy else k in entry)]
+    if len({json.dumps(entry[k], sort_keys=True) for k in used}) > 1:
+        raise ValueError(f"entry gives different values for the {what} aliases {used}")
+    return used[0] if used else None
+
+
+class _EntryReader:
+    """Turns one prompt-file entry into a generation record."""
+
+    def __init__(self, entry, index: int, out_root: Path, mode: str, image_root: Optional[Path],
+                 check_images: bool):
+        if not isinstance(entry, dict):
+            raise ValueError(f"prompt entry {index} is not a JSON object")
+        self.entry, self.index, self.out_root, self.mode = entry, index, out_root, mode
+        self.image_root, self.check_images = image_root, check_images
+
+    def task(self) -> str:
+        named = {str(self.entry[k]).strip().lower() for k in ("task", "type") if self.entry.get(k)}
+        if len(named) > 1:
+            raise ValueError(f"entry {self.index}: task and type disagree ({sorted(named)})")
+        t = named.pop() if named else ("i2v" if any(self.entry.get(k) for k in IMAGE_KEYS) else "t2v")
+        if t not in TASKS:
+            raise ValueError(f"entry {self.index}: task {t!r} is not one of {TASKS}")
+        return t
+
+    def image(self, task: str) -> Optional[str]:
+        key = _single_alias(self.entry, IMAGE_KEYS, "reference image")
+        if task == "t2v":
+            if key:
+                raise ValueError(f"entry {self.index}: a text-to-video entry names a reference image ({key})")
+            return None
+        if key is None:
+            raise ValueError(f"entry {self.index}: an image-to-video entry needs one of {IMAGE_KEYS}")
+        raw = self.entry[key]
+        if not isinstance(raw, str) or not raw.strip():
+            raise ValueError(f"entry {self.index}: the reference image path is empty")
+        p = Path(raw)
+        if self.image_root is not None:
+            if p.name in ("", ".", ".."):
+                raise ValueError(f"entry {self.index}: {raw!r} has no file name to look up under image_root")
+            p = self.image_root / p.name
+        resolved = p.resolve()
+        if self.check_images and not resolved.is_file():
+            raise ValueError(f"entry {self.index}: reference image {resolved} is not a file")
+        return str(resolved)
+
+    def prompt(self, task: str) -> str:
+        text = next((self.entry[k] for k in PROMPT_KEYS if self.entry.get(k)), None)
+        if not isinstance(text, str) or not text.strip():
+            raise ValueError(f"entry {self.index} ({task}): no prompt text in any of {PROMPT_KEYS}")
+        return text
+
+    def output(self, task: str, n_before: int) -> Path:
+        ident = self.entry.get("id")
+        ident = "" if ident is None else str(ident).strip()
+        if ident:
+            safe = re.sub(r"[^A-Za-z0-9._-]+", "_", ident).strip("._-")
+            if not safe:
+                raise ValueError(f"entry {self.index}: id {ident!r} leaves no usable file name")
+            name = f"{task}_{safe}.mp4"
+        else:
+            name = str(self.entry.get("relative_path") or "").strip() or f"{task}_{n_before:04d}.mp4"
+        rel = PurePosixPath(name)
+        folder = self.out_root / task if self.mode == "auto" else self.out_root
+        target = (folder / name).resolve()
+        if (rel.is_absolute() or ".." in rel.parts or "\\" in name or rel.suffix.lower() != ".mp4"
+                or not target.is_relative_to(self.out_root)):
+            raise ValueError(f"entry {self.index}: output path {name!r} is not a .mp4 inside the output folder")
+        return target
+
+    def negative(self, frames: int, fps, default_negative: str):
+        key = _single_alias(self.entry, NEGATIVE_KEYS, "negative prompt", truthy=False)
+        if key is not None:
+            return self.entry[key]
+        return render_negative_duration(default_negative, frames, fps)
 
 
 def load_inference_inputs(path, output_dir, *, task: str = "t2v", fps=24, fallback=121, shard_index: int = 0,
                           shard_count: int = 1, default_negative: str = "", validate_images: bool = True,
                           image_root=None) -> List[Dict]:
-    if task not in ("t2v", "i2v", "auto"):
-        raise ValueError("task must be t2v, i2v or auto")
-    if type(validate_images) is not bool:
-        raise ValueError("validate_images must be a boolean")
+    """Generation records of this shard (every ``shard_count``-th record from ``shard_index``)."""
+    if task not in TASKS + ("auto",):
+        raise ValueError(f"task {task!r} is not t2v, i2v or auto")
+    if not isinstance(validate_images, bool):
+        raise ValueError("validate_images takes True or False")
+    if not (type(shard_index) is int and type(shard_count) is int and 0 <= shard_index < shard_count):
+        raise ValueError(f"prompt shard {shard_index!r} of {shard_count!r} is not a valid shard")
+    root_images = None
     if image_root is not None:
         if not str(image_root).strip():
-            raise ValueError("image_root must be a nonempty local directory path")
-        image_root = Path(image_root).resolve()
-        if validate_images and not image_root.is_dir():
-            raise ValueError(f"image_root must be an existing local directory: {image_root}")
-    if type(shard_count) is not int or type(shard_index) is not int or not 0 <= shard_index < shard_count:
-        raise ValueError("require 0 <= prompt_shard_index < prompt_shard_count")
-    root = Path(output_dir).resolve()
+            raise ValueError("image_root is empty")
+        root_images = Path(image_root).resolve()
+        if validate_images and not root_images.is_dir():
+            raise ValueError(f"image_root {root_images} is not a folder")
+    out_root = Path(output_dir).resolve()
     records: List[Dict] = []
-    seen = set()
-    for entry in _entries(json.loads(Path(path).read_text(encoding="utf-8"))):
-        if not isinstance(entry, dict):
-            raise ValueError("prompt entries must be objects")
-        declared = {str(entry[k]).strip().lower() for k in ("task", "type") if entry.get(k)}
-        if len(declared) > 1:
-            raise ValueError("conflicting task/type fields")
-        img_keys = [k for k in ("image_path", "image", "ref_image") if entry.get(k)]
-        etask = declared.pop() if declared else ("i2v" if img_keys else "t2v")
-        if etask not in ("t2v", "i2v"):
-            raise ValueError(f"unsupported task: {etask}")
-        if task != "auto" and etask != task:
+    taken = set()
+    for i, entry in enumerate(_entry_list(json.loads(Path(path).read_text(encoding="utf-8")))):
+        r = _EntryReader(entry, i, out_root, task, root_images, validate_images)
+        t = r.task()
+        if task != "auto" and t != task:
             continue
-        image_path = None
-        if etask == "i2v":
-            if not img_keys:
-                raise ValueError("an I2V entry requires image_path (or image / ref_image)")
-            if len({json.dumps(entry[k]) for k in img_keys}) > 1:
-                raise ValueError("conflicting reference image aliases")
-            image_path = entry[img_keys[0]]
-            if not isinstance(image_path, str) or not image_path.strip():
-                raise ValueError("the I2V reference image must be an existing local file")
-            if image_root is not None:
-                base = Path(image_path).name
-                if base in ("", ".", ".."):
-                    raise ValueError("the I2V reference image needs a file name for image_root remapping")
-                image_path = image_root / base
-            image_path = str(Path(image_path).resolve())
-            if validate_images and not Path(image_path).is_file():
-                raise ValueError(f"the I2V reference image must be an existing local file: {image_path}")
-        elif img_keys:
-            raise ValueError("a T2V entry cannot name a reference image")
-        prompt = next((entry[k] for k in ("refined_prompt", "refined_prompts", "prompt", "caption") if entry.get(k)),
-                      None)
-        if not isinstance(prompt, str) or not prompt.strip():
-            raise ValueError(f"{etask.upper()} entry needs a nonempty positive prompt")
-        eid = "" if entry.get("id") is None else str(entry["id"]).strip()
-        if eid:
-            name = re.sub(r"[^A-Za-z0-9._-]+", "_", eid).strip("._-")
-            if not name:
-                raise ValueError("empty output id after sanitisation")
-            relative = f"{etask}_{name}.mp4"
-        else:
-            relative = str(entry.get("relative_path") or "").strip() or f"{etask}_{len(records):04d}.mp4"
-        rel = PurePosixPath(relative)
-        base_dir = root / etask if task == "auto" else root
-        target = (base_dir / relative).resolve()
-        if (rel.is_absolute() or ".." in rel.parts or "\\" in relative or rel.suffix.lower() != ".mp4"
-                or not target.is_relative_to(root)):
-            raise ValueError(f"unsafe output path: {relative}")
-        if target in seen:
-            raise ValueError(f"duplicate output path: {relative}")
-        seen.add(target)
+        image = r.image(t)
+        prompt = r.prompt(t)
+        target = r.output(t, len(records))
+        if target in taken:
+            raise ValueError(f"entry {i}: output {target} is produced by an earlier entry too")
+        taken.add(target)
         frames = resolve_frames(entry, fps, fallback)
-        neg_keys = [k for k in ("negative_prompt", "negative_prompts", "neg_prompt") if k in entry]
-        if len({json.dumps(entry[k]) for k in neg_keys}) > 1:
-            raise ValueError("conflicting negative prompt aliases")
-        negative = entry[neg_keys[0]] if neg_keys else render_negative_duration(default_negative, frames, fps)
-        rec = dict(prompt=prompt, negative_prompt=negative, video_length=frames, output_path=str(target))
+        rec = dict(prompt=prompt, negative_prompt=r.negative(frames, fps, default_negative), video_length=frames,
+                   output_path=str(target))
         if task == "auto":
-            rec["task"] = etask
-        if etask == "i2v":
-            rec["image_path"] = image_path
+            rec["task"] = t
+        if image is not None:
+            rec["image_path"] = image
         records.append(rec)
     if not records:
-        raise ValueError(f"the prompt JSON contains no {task.upper()} entries")
+        raise ValueError(f"{path} has no entries for task {task}")
     return records[shard_index::shard_count]
 
 
 def is_complete(args) -> bool:
+    """True when this output exists with the same generation settings (skip it); False when it is
+    missing or half written (generate it); an error when it exists with other settings."""
     video = Path(args.output_path)
-    cfg = video.with_name(video.stem + "_config.json")
-    if not (video.is_file() and video.stat().st_size and cfg.is_file() and cfg.stat().st_size):
+    settings = video.with_name(video.stem + "_config.json")
+    if not all(p.is_file() and p.stat().st_size > 0 for p in (video, settings)):
         return False
     try:
-        saved = json.loads(cfg.read_text(encoding="utf-8"))["arguments"]
+        saved = json.loads(settings.read_text(encoding="utf-8"))["arguments"]
     except (OSError, ValueError, KeyError, TypeError):
         return False
     if not isinstance(saved, dict):
         return False
-    diff = [k for k, v in vars(args).items()
-            if not k.startswith("_") and k not in ROUTING_ARGS and (k not in saved or saved[k] != v)]
-    if diff:
-        raise ValueError(f"existing output settings differ for {video}: {', '.join(diff)}")
+    changed = sorted(k for k, v in vars(args).items()
+                     if not k.startswith("_") and k not in ROUTING_ARGS and saved.get(k, _MISSING) != v)
+    if changed:
+        raise ValueError(f"{video} was generated with other settings ({', '.join(changed)}); "
+                         "use another output folder or turn off skip_existing")
     return True
+
+
+_MISSING = object()
