@@ -1,9 +1,13 @@
-"""Caption encoder ("token refiner"): pre-norm self-attention blocks over the projected captions.
+"""Caption encoder (token refiner): pre-norm self-attention blocks over the projected captions.
 
-Same structure and parameter names as pan/models/transformers/modules/caption_encoder.py:30-153:
-``attn_norm`` RMSNorm(1e-5) -> bias-free fused ``qkv`` -> per-head ``q_norm``/``k_norm`` RMSNorm ->
-attention -> ``attn_out``; then ``ffn_norm`` -> SwiGLU ``w2(w3(x) * silu(w1(x)))``.  Captions run either
-packed (``cu_seqlens`` + host ``lens``) or padded (``mask`` ``[B, L]``; position 0 is always visible).
+Parameter names, shapes and creation order match the reference's caption encoder
+(pan/models/transformers/modules/caption_encoder.py:30-153), so checkpoints load and seeded
+initialisation matches: ``attn_norm`` -> bias-free fused ``qkv`` -> per-head ``q_norm`` / ``k_norm``
+-> attention -> ``attn_out``, then ``ffn_norm`` -> SwiGLU ``w2(w3(x) * silu(w1(x)))``.
+
+Captions run packed (``cu_seqlens`` and host ``lens``: the varlen tcgen05 attention) or padded
+(``mask`` ``[B, L]``; the first position of every caption stays visible so an all-padding caption
+still has a key).
 """
 from __future__ import annotations
 
@@ -19,7 +23,7 @@ from ..ops.gemm import linear
 
 
 class SwiGLUFeedForward(nn.Module):
-    """Bias-free SwiGLU: ``w2(w3(x) * silu(w1(x)))``."""
+    """Bias-free SwiGLU ``w2(w3(x) * silu(w1(x)))`` (``w1``, ``w3``, ``w2`` created in that order)."""
 
     def __init__(self, dim: int, inner_dim: int):
         super().__init__()
@@ -28,21 +32,24 @@ class SwiGLUFeedForward(nn.Module):
         self.w2 = nn.Linear(inner_dim, dim, bias=False)
 
     def forward(self, x: torch.Tensor) -> torch.Tensor:
-        gate = F.silu(linear(x, self.w1.weight))
-        return linear(linear(x, self.w3.weight) * gate, self.w2.weight)
+        value = linear(x, self.w3.weight)
+        return linear(value * F.silu(linear(x, self.w1.weight)), self.w2.weight)
 
 
-def _init_residual_output(layer: nn.Linear, zero_init: bool, init_std: Optional[float]) -> None:
-    if init_std is not None and init_std < 0:
-        raise ValueError(f"residual init std must be non-negative, got {init_std}")
-    if init_std is None and not zero_init:
+def reinit_branch_output(layer: nn.Linear, zero: bool, std: Optional[float]) -> None:
+    """Re-initialise a residual branch's output projection: normal with ``std`` when given, zero
+    when ``zero``; left as constructed otherwise.  A bias, if any, becomes zero."""
+    if std is None and not zero:
         return
-    if init_std is None:
-        nn.init.zeros_(layer.weight)
-    else:
-        nn.init.normal_(layer.weight, mean=0.0, std=init_std)
-    if layer.bias is not None:
-        nn.init.zeros_(layer.bias)
+    if std is not None and not std >= 0:
+        raise ValueError(f"residual_init_std={std} is negative")
+    with torch.no_grad():
+        if std is None:
+            layer.weight.zero_()
+        else:
+            layer.weight.normal_(0.0, std)
+        if layer.bias is not None:
+            layer.bias.zero_()
 
 
 class CaptionEncoderBlock(nn.Module):
@@ -50,47 +57,43 @@ class CaptionEncoderBlock(nn.Module):
                  eps: float = 1e-5, zero_residual_init: bool = False, residual_init_std: Optional[float] = None):
         super().__init__()
         self.heads = num_attention_heads
-        head_dim = dim // num_attention_heads
-        # attribute order = parameter / initializer order
+        d_head = dim // num_attention_heads
+        norm_or_id = (lambda: RMSNorm(d_head, eps=eps)) if qk_norm else nn.Identity
         self.attn_norm = RMSNorm(dim, eps=eps)
         self.qkv = nn.Linear(dim, 3 * dim, bias=False)
-        self.qkv.weight._muon_chunks_dim_0 = 3 * num_attention_heads
-        self.q_norm = RMSNorm(head_dim, eps=eps) if qk_norm else nn.Identity()
-        self.k_norm = RMSNorm(head_dim, eps=eps) if qk_norm else nn.Identity()
+        self.qkv.weight._muon_chunks_dim_0 = 3 * num_attention_heads  # Muon: a row block per (q|k|v, head)
+        self.q_norm = norm_or_id()
+        self.k_norm = norm_or_id()
         self.attn_out = nn.Linear(dim, dim, bias=False)
         self.ffn_norm = RMSNorm(dim, eps=eps)
         self.ffn = SwiGLUFeedForward(dim, int(dim * mlp_ratio))
-        _init_residual_output(self.attn_out, zero_residual_init, residual_init_std)
-        _init_residual_output(self.ffn.w2, zero_residual_init, residual_init_std)
-
-    def attention(self, x, mask=None, cu_seqlens=None, lens=None, max_seqlen=None):
-        q, k, v = linear(x, self.qkv.weight).chunk(3, dim=-1)
-        q, k, v = (t.unflatten(-1, (self.heads, -1)) for t in (q, k, v))
-        q = self.q_norm(q).to(v.dtype)
-        k = self.k_norm(k).to(v.dtype)
-        if cu_seqlens is None:
-            o = dense_attention(q, k, v, mask)
-        else:
-            o = varlen_attention(q, k, v, cu_seqlens, lens, max_seqlen)
-        return linear(o.flatten(-2), self.attn_out.weight)
+        for out in (self.attn_out, self.ffn.w2):
+            reinit_branch_output(out, zero_residual_init, residual_init_std)
 
     def forward(self, x, attention_mask=None, cu_seqlens=None, lens=None, max_seqlen=None):
-        if cu_seqlens is not None and attention_mask is not None:
-            raise ValueError("Pass either attention_mask (padded) or cu_seqlens (packed), not both")
-        x = x + self.attention(self.attn_norm(x), attention_mask, cu_seqlens, lens, max_seqlen)
-        x = x + self.ffn(self.ffn_norm(x))
-        return x
+        packed = cu_seqlens is not None
+        if packed and attention_mask is not None:
+            raise ValueError("a caption batch is packed (cu_seqlens) or padded (attention_mask), not both")
+        h = self.attn_norm(x)
+        q, k, v = linear(h, self.qkv.weight).unflatten(-1, (3, self.heads, -1)).unbind(-3)
+        q = self.q_norm(q).to(v.dtype)
+        k = self.k_norm(k).to(v.dtype)
+        o = varlen_attention(q, k, v, cu_seqlens, lens, max_seqlen) if packed else dense_attention(q, k, v,
+                                                                                                  attention_mask)
+        x = x + linear(o.flatten(-2), self.attn_out.weight)
+        return x + self.ffn(self.ffn_norm(x))
 
 
 class CaptionEncoder(nn.Module):
     def __init__(self, dim: int, num_attention_heads: int, num_layers: int = 4, **block_kwargs):
         super().__init__()
-        self.blocks = nn.ModuleList([CaptionEncoderBlock(dim=dim, num_attention_heads=num_attention_heads, **block_kwargs)
-                                     for _ in range(num_layers)])
+        self.blocks = nn.ModuleList(CaptionEncoderBlock(dim=dim, num_attention_heads=num_attention_heads,
+                                                        **block_kwargs) for _ in range(num_layers))
 
     def forward(self, x, mask=None, cu_seqlens=None, lens: Optional[Sequence[int]] = None, max_seqlen=None):
         if mask is not None:
-            mask = mask.bool() | (torch.arange(mask.shape[1], device=mask.device) == 0)
+            mask = mask.bool().clone()
+            mask[:, 0] = True  # every caption keeps one visible key
         for block in self.blocks:
             x = block(x, attention_mask=mask, cu_seqlens=cu_seqlens, lens=lens, max_seqlen=max_seqlen)
         return x

@@ -1,18 +1,24 @@
 """Input embeddings: the video patch embedding and the timestep encoder.
 
-Behaviour follows pan/models/transformers/modules/embeddings.py:26-127 of the reference:
+Parameter names, shapes and initialisation match the reference
+(pan/models/transformers/modules/embeddings.py:26-127) so checkpoints interchange:
 
-* ``VideoPatchEmbed`` is a stride == kernel ``Conv3d``; on the packed path the dataloader has already
-  cut samples into flat ``[C*pt*ph*pw, N, 1, 1]`` patches and the conv weight is applied as the
-  equivalent linear map (embeddings.py:51-55).  Xavier-uniform over the flattened weight, zero bias.
-* ``TimestepEncoder``: sinusoidal ``cos || sin`` embedding of ``t * exp(-ln(max_period) * i / half)``,
-  ``num_channels=256``; then ``in_proj -> SiLU -> out_proj``.  The frequency table is a persistent
-  buffer that is always rebuilt in fp32 on the CPU (embeddings.py:96-121), never trusted from a
-  low-precision copy.
+* ``VideoPatchEmbed.proj`` is a stride-equals-kernel ``Conv3d``, Xavier-uniform over its flattened
+  ``[inner_dim, C*pt*ph*pw]`` weight, zero bias.  The packed path receives patches already cut by
+  the loader (``[C*pt*ph*pw, N, 1, 1]``) and applies the conv as the equivalent linear map.
+* ``TimestepEncoder``: the sinusoidal ``cos || sin`` embedding of ``t * exp(-ln(max_period) i / half)``
+  over 256 channels, then ``in_proj -> SiLU -> out_proj``.
+
+The sinusoid frequencies must be the fp32 values computed on the CPU (a low-precision or GPU copy puts
+a phase error on the fast channels).  Here ``forward`` never reads the stored ``freqs`` buffer: it
+takes the table from :func:`sinusoid_frequencies`, cached per device.  The buffer is kept only so
+state dicts carry the reference's ``timestep_encoder.freqs`` key; hooks write the exact fp32 table
+into every state dict produced and replace whatever a loaded state dict holds there.
 """
 from __future__ import annotations
 
 import math
+from functools import lru_cache
 
 import torch
 import torch.nn as nn
@@ -20,16 +26,15 @@ import torch.nn.functional as F
 
 
 def patch_triple(patch_size) -> tuple:
-    if isinstance(patch_size, int):
-        return (patch_size, patch_size, patch_size)
-    patch_size = tuple(int(p) for p in patch_size)
-    if len(patch_size) != 3:
-        raise ValueError(f"patch_size must be an int or a (t, h, w) triple, got {patch_size}")
-    return patch_size
+    """``(t, h, w)`` patch size from an int or a 3-sequence."""
+    dims = (patch_size,) * 3 if isinstance(patch_size, int) else tuple(int(p) for p in patch_size)
+    if len(dims) != 3:
+        raise ValueError(f"patch_size {patch_size!r}: give one int or three (t, h, w)")
+    return dims
 
 
 class VideoPatchEmbed(nn.Module):
-    """Video latents -> tokens (dense ``[B,C,T,H,W]`` or packed ``[C*pt*ph*pw, N, 1, 1]`` input)."""
+    """Video latents -> tokens: dense ``[B, C, T, H, W]`` or packed ``[C*pt*ph*pw, N, 1, 1]`` input."""
 
     def __init__(self, patch_size, in_channels: int, inner_dim: int):
         super().__init__()
@@ -39,65 +44,65 @@ class VideoPatchEmbed(nn.Module):
         nn.init.zeros_(self.proj.bias)
 
     def forward(self, hidden_states: torch.Tensor, packed: bool = False) -> torch.Tensor:
-        if packed:
-            patches = hidden_states.reshape(hidden_states.shape[0], -1).transpose(0, 1)  # [N, C*pt*ph*pw]
-            return F.linear(patches, self.proj.weight.flatten(1).to(patches.dtype),
-                            self.proj.bias.to(patches.dtype))
-        out = self.proj(hidden_states)
-        return out.flatten(2).transpose(1, 2)
+        if not packed:
+            return self.proj(hidden_states).flatten(2).transpose(1, 2)
+        rows = hidden_states.flatten(1).t()  # [N, C*pt*ph*pw]
+        w = self.proj.weight.flatten(1).to(rows.dtype)
+        return F.linear(rows, w, self.proj.bias.to(rows.dtype))
 
 
-def timestep_frequencies(num_channels: int = 256, max_period: float = 10000.0) -> torch.Tensor:
-    """fp32 CPU frequency table ``exp(-ln(max_period) * i / half)`` for ``i < half``."""
-    half = num_channels // 2
-    exponent = -math.log(max_period) * torch.arange(0, half, dtype=torch.float32, device="cpu") / half
-    return torch.exp(exponent)
+@lru_cache(maxsize=32)
+def _cpu_frequencies(channels: int, max_period: float) -> torch.Tensor:
+    half = channels // 2
+    steps = torch.arange(half, dtype=torch.float32, device="cpu") * -math.log(max_period)
+    return torch.exp(steps / half)
+
+
+def sinusoid_frequencies(channels: int = 256, max_period: float = 10000.0, device=None) -> torch.Tensor:
+    """``exp(-ln(max_period) * i / half)``, ``i < half``, evaluated in fp32 on the CPU."""
+    table = _cpu_frequencies(int(channels), float(max_period))
+    return table if device is None else table.to(device)
 
 
 def timestep_embedding(timesteps: torch.Tensor, freqs: torch.Tensor) -> torch.Tensor:
-    """Sinusoidal embedding ordered ``cos`` then ``sin``."""
-    angles = timesteps[:, None].float() * freqs[None, :].to(timesteps.device)
-    return torch.cat([torch.cos(angles), torch.sin(angles)], dim=-1)
+    """``cos(t f) || sin(t f)`` for every timestep."""
+    phase = torch.outer(timesteps.float(), freqs.to(timesteps.device))
+    return torch.cat((phase.cos(), phase.sin()), dim=-1)
 
 
 class TimestepEncoder(nn.Module):
     """Timesteps -> sinusoidal embedding -> ``in_proj -> act -> out_proj``."""
 
-    def __init__(self, time_embed_dim: int, make_act, num_channels: int = 256, max_period: int = 10000):
+    def __init__(self, time_embed_dim: int, activation: str = "silu", num_channels: int = 256,
+                 max_period: int = 10000):
         super().__init__()
-        self.num_channels = num_channels
-        self.max_period = max_period
-        self.register_buffer("freqs", timestep_frequencies(num_channels, max_period))
+        from .layers import make_activation
+        self.num_channels, self.max_period = num_channels, max_period
+        self.register_buffer("freqs", sinusoid_frequencies(num_channels, max_period).clone().to(
+            torch.empty(0).device))  # the module's construction device (meta under a meta context)
         self.in_proj = nn.Linear(num_channels, time_embed_dim)
-        self.act = make_act()
+        self.act = make_activation(activation)
         self.out_proj = nn.Linear(time_embed_dim, time_embed_dim)
         nn.init.normal_(self.in_proj.weight, std=0.02)
         nn.init.normal_(self.out_proj.weight, std=0.02)
+        self._register_state_dict_hook(TimestepEncoder._exact_on_save)
+        self._register_load_state_dict_pre_hook(self._exact_on_load)
 
-    def _rebuild_freqs(self):
-        device = self.freqs.device
-        if device.type == "meta":
-            return
-        self.freqs = timestep_frequencies(self.num_channels, self.max_period).to(device)
-
-    def _apply(self, fn, recurse=True):
-        super()._apply(fn, recurse=recurse)
-        self._rebuild_freqs()
-        return self
-
-    def _load_from_state_dict(self, state_dict, prefix, local_metadata, strict,
-                              missing_keys, unexpected_keys, error_msgs):
+    @staticmethod
+    def _exact_on_save(module, state_dict, prefix, local_metadata):
         key = prefix + "freqs"
-        saved = state_dict.get(key)
-        if isinstance(saved, torch.Tensor) and saved.shape == self.freqs.shape:
-            state_dict = dict(state_dict)
-            state_dict[key] = timestep_frequencies(self.num_channels, self.max_period).to(saved.device)
-        super()._load_from_state_dict(state_dict, prefix, local_metadata, strict,
-                                      missing_keys, unexpected_keys, error_msgs)
-        self._rebuild_freqs()
+        if key in state_dict:
+            state_dict[key] = sinusoid_frequencies(module.num_channels, module.max_period, state_dict[key].device)
+        return state_dict
+
+    def _exact_on_load(self, state_dict, prefix, *args):
+        key = prefix + "freqs"
+        if isinstance(state_dict.get(key), torch.Tensor) and state_dict[key].shape == self.freqs.shape:
+            state_dict[key] = sinusoid_frequencies(self.num_channels, self.max_period, state_dict[key].device)
 
     def forward(self, timestep: torch.Tensor) -> torch.Tensor:
         from ..ops.gemm import linear
-        sample = timestep_embedding(timestep, self.freqs).to(self.in_proj.weight.dtype)
-        h = self.act(linear(sample, self.in_proj.weight, self.in_proj.bias))
+        table = sinusoid_frequencies(self.num_channels, self.max_period, timestep.device)
+        emb = timestep_embedding(timestep, table).to(self.in_proj.weight.dtype)
+        h = self.act(linear(emb, self.in_proj.weight, self.in_proj.bias))
         return linear(h, self.out_proj.weight, self.out_proj.bias)

@@ -1,56 +1,56 @@
-"""Shared building blocks: activations, RMS normalisation and adaLN conditioning.
+"""Normalisation and adaLN conditioning blocks of the MMDiT.
 
-Semantics follow pan/models/transformers/modules/layers.py:24-119 of the reference:
-
-* ``RMSNorm`` normalises in fp32, rounds back to the input dtype, and only then multiplies by the
-  learned scale (layers.py:65-72).  The bf16 rounding point is part of the trained model.
-* ``AdaLNProjection`` is ``Linear(act(emb))`` producing ``chunks * width`` values, zero-initialised
-  when ``zero_init`` (layers.py:76-99).
-* ``modulate(x, shift, scale) = x * (1 + scale) + shift`` and ``gate(x, g) = x * g`` with per-sample
-  ``[B, C]`` conditioning broadcast over tokens (layers.py:102-119).
+Parameter names and the arithmetic the checkpoints were trained with are the reference's
+(pan/models/transformers/modules/layers.py:24-119): RMS normalisation runs in fp32 and the result is
+rounded to the input dtype before the learned scale multiplies it (that rounding point is part of
+the bf16 model); the adaLN projection is ``linear(activation(embedding))`` with ``chunks * width``
+outputs, zero at initialisation so a fresh block is the identity.  The packed training path applies
+modulation and gating in fused kernels (``pan2_b200.ops.packed``), not here.
 """
 from __future__ import annotations
 
-from typing import Callable, Optional
+from typing import Optional
 
 import torch
 import torch.nn as nn
 
-_ACTIVATIONS = {
-    "gelu": nn.GELU,
-    "gelu_tanh": lambda: nn.GELU(approximate="tanh"),
-    "relu": nn.ReLU,
-    "silu": nn.SiLU,
-}
 
-
-def activation_factory(name: str) -> Callable[[], nn.Module]:
-    """Zero-argument constructor of the named activation module."""
-    if name not in _ACTIVATIONS:
-        raise ValueError(f"Unknown activation {name!r}; expected one of {sorted(_ACTIVATIONS)}")
-    return _ACTIVATIONS[name]
+def make_activation(name: str) -> nn.Module:
+    """A fresh activation module for a config name (``silu``, ``gelu``, ``gelu_tanh``, ``relu``)."""
+    if name == "silu":
+        return nn.SiLU()
+    if name == "gelu":
+        return nn.GELU()
+    if name == "gelu_tanh":
+        return nn.GELU(approximate="tanh")
+    if name == "relu":
+        return nn.ReLU()
+    raise ValueError(f"activation {name!r} is not one of silu, gelu, gelu_tanh, relu")
 
 
 def rms_norm(x: torch.Tensor, weight: Optional[torch.Tensor], eps: float) -> torch.Tensor:
-    """fp32 RMS normalisation, cast back to ``x.dtype`` before the affine scale."""
-    xf = x.float()
-    y = (xf * torch.rsqrt(xf.pow(2).mean(-1, keepdim=True) + eps)).to(x.dtype)
-    return y if weight is None else y * weight
+    """fp32 RMS normalisation, rounded to ``x.dtype`` before the (optional) scale."""
+    wide = x.to(torch.float32)
+    inv_rms = torch.rsqrt(wide.square().mean(dim=-1, keepdim=True) + eps)
+    normed = (wide * inv_rms).to(x.dtype)
+    return normed if weight is None else normed * weight
 
 
 class RMSNorm(nn.Module):
-    """RMSNorm whose normalised value is rounded to the input dtype before the scale."""
+    """RMS normalisation over the last dim with an optional learned per-channel scale ``weight``."""
 
     def __init__(self, dim: int, eps: float = 1e-6, elementwise_affine: bool = True):
         super().__init__()
-        self.dim = dim
-        self.eps = eps
-        self.elementwise_affine = elementwise_affine
-        self.weight = nn.Parameter(torch.ones(dim)) if elementwise_affine else None
+        self.dim, self.eps, self.elementwise_affine = dim, eps, elementwise_affine
+        if elementwise_affine:
+            self.weight = nn.Parameter(torch.ones(dim))
+        else:
+            self.register_parameter("weight", None)
 
     def reset_parameters(self) -> None:
         if self.weight is not None:
-            nn.init.ones_(self.weight)
+            with torch.no_grad():
+                self.weight.fill_(1.0)
 
     def forward(self, x: torch.Tensor) -> torch.Tensor:
         return rms_norm(x, self.weight, self.eps)
@@ -60,30 +60,16 @@ class RMSNorm(nn.Module):
 
 
 class AdaLNProjection(nn.Module):
-    """``linear(act(emb))`` producing ``chunks * width`` modulation values."""
+    """``chunks`` modulation vectors of width ``width`` from a conditioning embedding."""
 
-    def __init__(self, width: int, chunks: int, make_act: Callable[[], nn.Module], zero_init: bool = True):
+    def __init__(self, width: int, chunks: int, activation: str = "silu", zero_init: bool = True):
         super().__init__()
-        self.act = make_act()
+        self.act = make_activation(activation)
         self.linear = nn.Linear(width, chunks * width, bias=True)
         if zero_init:
-            nn.init.zeros_(self.linear.weight)
-            nn.init.zeros_(self.linear.bias)
+            with torch.no_grad():
+                self.linear.weight.zero_()
+                self.linear.bias.zero_()
 
     def forward(self, emb: torch.Tensor) -> torch.Tensor:
         return self.linear(self.act(emb))
-
-
-def modulate(x: torch.Tensor, shift: Optional[torch.Tensor] = None,
-             scale: Optional[torch.Tensor] = None) -> torch.Tensor:
-    """``x * (1 + scale) + shift`` with ``[B, C]`` conditioning over ``[B, L, C]`` tokens."""
-    if scale is not None:
-        x = x * (1 + scale.unsqueeze(1))
-    if shift is not None:
-        x = x + shift.unsqueeze(1)
-    return x
-
-
-def gate(x: torch.Tensor, g: Optional[torch.Tensor] = None) -> torch.Tensor:
-    """``x * g`` with a ``[B, C]`` gate broadcast over the tokens of ``[B, L, C]``."""
-    return x if g is None else x * g.unsqueeze(1)

@@ -19,14 +19,14 @@ from ..ops.packed import ln_modulate
 
 
 class OutputHead(nn.Module):
-    def __init__(self, inner_dim, patch_size, out_channels, make_act, zero_init_modulation: bool = True):
+    def __init__(self, inner_dim, patch_size, out_channels, activation: str = "silu", zero_init_modulation: bool = True):
         super().__init__()
         patch_numel = patch_size * patch_size if isinstance(patch_size, int) else math.prod(patch_size)
         self.norm = nn.LayerNorm(inner_dim, elementwise_affine=False, eps=1e-6)
         self.proj = nn.Linear(inner_dim, patch_numel * out_channels, bias=True)
         nn.init.kaiming_normal_(self.proj.weight)
         nn.init.zeros_(self.proj.bias)
-        self.modulation = AdaLNProjection(inner_dim, 2, make_act, zero_init=zero_init_modulation)
+        self.modulation = AdaLNProjection(inner_dim, 2, activation, zero_init=zero_init_modulation)
 
     def modulation_rows(self, temb: torch.Tensor):
         a = self.modulation.act(temb)

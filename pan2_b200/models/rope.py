@@ -59,7 +59,7 @@ def _grid_coords(sizes: Sequence[int]) -> list:
     n = 1
     for s in sizes:
         n *= int(s)
-    flat = torch.arange(n)
+    flat = torch.arange(n, device="cpu")
     coords, stride = [], n
     for s in sizes:
         stride //= int(s)

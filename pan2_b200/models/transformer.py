@@ -15,6 +15,7 @@ out-projection, gate+residual with ``ln_stats``, grouped GELU FFN.
 """
 from __future__ import annotations
 
+import logging
 import math
 from typing import Any, Dict, List, Optional, Sequence, Tuple
 
@@ -23,7 +24,7 @@ import torch.nn as nn
 import torch.nn.functional as F
 from einops import rearrange
 
-from .layers import RMSNorm, AdaLNProjection, activation_factory, rms_norm
+from .layers import RMSNorm, AdaLNProjection, rms_norm
 from .embeddings import TimestepEncoder, VideoPatchEmbed
 from .rope import apply_rope, rope_tables_for_grid
 from .output_head import OutputHead
@@ -36,10 +37,22 @@ from ..ops.attention import varlen_attention, dense_attention
 from ..parallel.ulysses import ulysses_attention
 from ..parallel.cp_fused import fused_cp_enabled, fused_qkv_ulysses_attention
 
+log = logging.getLogger(__name__)
+
 
 # ---------------------------------------------------------------------------------------------
 # parameter holders (same names / layout as the reference)
 # ---------------------------------------------------------------------------------------------
+
+def linear_default_init(weight: torch.Tensor, bias: Optional[torch.Tensor], fan_in: int) -> None:
+    """torch's default ``nn.Linear`` initialisation for a (slice of a) stacked weight: uniform with
+    bound ``1/sqrt(fan_in)`` (the Kaiming-uniform rule with a = sqrt(5)) for both weight and bias."""
+    nn.init.kaiming_uniform_(weight, a=math.sqrt(5))
+    if bias is not None:
+        limit = fan_in ** -0.5
+        with torch.no_grad():
+            bias.uniform_(-limit, limit)
+
 
 class GroupedQKVProj(nn.Module):
     """Video+text QKV stacked ``[2*3H, H]`` (each modality block is ``[Q|K|V]``), bias ``[2*3H]``,
@@ -61,11 +74,10 @@ class GroupedQKVProj(nn.Module):
         self.reset_parameters()
 
     def reset_parameters(self):
-        nn.init.kaiming_uniform_(self.weight, a=math.sqrt(5))
-        bound = 1 / math.sqrt(self.hidden_size)
-        nn.init.uniform_(self.bias, -bound, bound)
-        nn.init.ones_(self.q_weight)
-        nn.init.ones_(self.k_weight)
+        linear_default_init(self.weight, self.bias, self.hidden_size)
+        with torch.no_grad():
+            for w in (self.q_weight, self.k_weight):
+                w.fill_(1.0)
 
     def project(self, x: torch.Tensor, modality: str):
         """Dense path: one modality's ``q, k, v`` ``[..., H, D]`` with RMS q/k norm (no RoPE)."""
@@ -91,9 +103,7 @@ class GroupedOutProj(nn.Module):
         self.reset_parameters()
 
     def reset_parameters(self):
-        nn.init.kaiming_uniform_(self.weight, a=math.sqrt(5))
-        bound = 1 / math.sqrt(self.hidden_size)
-        nn.init.uniform_(self.bias, -bound, bound)
+        linear_default_init(self.weight, self.bias, self.hidden_size)
 
     def project(self, x: torch.Tensor, modality: str) -> torch.Tensor:
         h = self.hidden_size
@@ -122,17 +132,10 @@ class GroupedFFN(nn.Module):
         self.b_down_text = nn.Parameter(torch.empty(hidden_size))
         self.reset_parameters()
 
-    @staticmethod
-    def _reset_linear(w, b):
-        nn.init.kaiming_uniform_(w, a=math.sqrt(5))
-        bound = 1 / math.sqrt(w.shape[1])
-        nn.init.uniform_(b, -bound, bound)
-
     def reset_parameters(self):
-        self._reset_linear(self.w_up_video, self.b_up_video)
-        self._reset_linear(self.w_down_video, self.b_down_video)
-        self._reset_linear(self.w_up_text, self.b_up_text)
-        self._reset_linear(self.w_down_text, self.b_down_text)
+        p = self.params_grouped()  # (weight, bias) pairs in creation order
+        for w, b in zip(p[0::2], p[1::2]):
+            linear_default_init(w, b, w.shape[1])
 
     def params_grouped(self):
         return [self.w_up_video, self.b_up_video, self.w_down_video, self.b_down_video,
@@ -162,13 +165,12 @@ class JointAttentionBlock(nn.Module):
         self.qkv_proj = GroupedQKVProj(hidden_size, num_heads, qk_norm=normalize_qk, qk_norm_type=qk_norm_kind)
         self.out_proj = GroupedOutProj(hidden_size)
         self.pre_norm = nn.LayerNorm(hidden_size, elementwise_affine=False, eps=1e-6)
-        silu = activation_factory("silu")
-        self.modulation = AdaLNProjection(hidden_size, 6, silu, zero_init=zero_init_modulation)
+        self.modulation = AdaLNProjection(hidden_size, 6, "silu", zero_init=zero_init_modulation)
         self.norm2 = nn.LayerNorm(hidden_size, elementwise_affine=False, eps=1e-6)
         self.ffn = GroupedFFN(hidden_size, self.mlp_hidden_dim, self.text_mlp_hidden_dim, mlp_act_type=ffn_activation)
         self.text_modulation_timestep_dependent = text_modulation_timestep_dependent
         if text_modulation_timestep_dependent:
-            self.text_modulation = AdaLNProjection(hidden_size, 6, silu, zero_init=zero_init_modulation)
+            self.text_modulation = AdaLNProjection(hidden_size, 6, "silu", zero_init=zero_init_modulation)
         else:
             self.text_modulation = nn.Parameter(torch.empty(hidden_size * 6))
             if zero_init_modulation:
@@ -283,42 +285,58 @@ class TextTypeEmbedding(nn.Module):
 
 
 # legacy architecture key names -> constructor arguments (pan_transformer.py:671-720)
-_LEGACY_ARCH_KEYS = {
-    "heads_num": "num_attention_heads", "mm_single_blocks_depth": "num_layers",
-    "mlp_act_type": "ffn_activation", "text_states_dim": "text_embed_dim",
-    "rope_dim_list": "rope_axes_dim", "rope_t_interp": "rope_temporal_scale",
-    "use_cond_type_embedding": "use_text_type_embedding", "qk_norm": "normalize_qk",
-    "qk_norm_type": "qk_norm_kind", "attn_mode": "attention_backend", "use_attention_mask": "mask_text_padding",
+# Architecture keys of configs written before the reference renamed them.  Each rule is one of
+#   ("rename", new_name)          the value moves to the constructor argument new_name
+#   ("only", value)               the key had one legal value; it is checked and dropped
+#   ("ffn_ratio", target or None) legacy FFN width ratios: video / text default to mlp_width_ratio (4)
+_LEGACY_RULES: Dict[str, tuple] = {
+    "heads_num": ("rename", "num_attention_heads"),
+    "mm_single_blocks_depth": ("rename", "num_layers"),
+    "mlp_act_type": ("rename", "ffn_activation"),
+    "text_states_dim": ("rename", "text_embed_dim"),
+    "rope_dim_list": ("rename", "rope_axes_dim"),
+    "rope_t_interp": ("rename", "rope_temporal_scale"),
+    "use_cond_type_embedding": ("rename", "use_text_type_embedding"),
+    "qk_norm": ("rename", "normalize_qk"),
+    "qk_norm_type": ("rename", "qk_norm_kind"),
+    "attn_mode": ("rename", "attention_backend"),
+    "use_attention_mask": ("rename", "mask_text_padding"),
+    "mm_double_blocks_depth": ("only", 0),
+    "single_stream_block_type": ("only", "mm_joint_attn"),
+    "mlp_width_ratio": ("ffn_ratio", None),
+    "video_mlp_width_ratio": ("ffn_ratio", "mlp_ratio"),
+    "text_mlp_width_ratio": ("ffn_ratio", "context_mlp_ratio"),
 }
-_LEGACY_FIXED_KEYS = {"mm_double_blocks_depth": 0, "single_stream_block_type": "mm_joint_attn"}
-_LEGACY_WIDTH_KEYS = ("mlp_width_ratio", "video_mlp_width_ratio", "text_mlp_width_ratio")
 
 
 def translate_architecture_config(config) -> dict:
-    """Map legacy architecture key names onto constructor arguments; current names pass through."""
-    out, legacy, widths = {}, [], {}
-    config = dict(config)
-    for key, value in config.items():
-        if key in _LEGACY_FIXED_KEYS:
-            if value != _LEGACY_FIXED_KEYS[key]:
-                raise ValueError(f"{key}={value!r} is not supported (only {_LEGACY_FIXED_KEYS[key]!r})")
-            legacy.append(key)
-        elif key in _LEGACY_WIDTH_KEYS:
-            widths[key] = value
-            legacy.append(key)
-        elif key in _LEGACY_ARCH_KEYS:
-            if _LEGACY_ARCH_KEYS[key] in config:
-                raise ValueError(f"config sets both {key!r} and its new name {_LEGACY_ARCH_KEYS[key]!r}")
-            out[_LEGACY_ARCH_KEYS[key]] = value
-            legacy.append(key)
+    """Constructor arguments from an architecture config that may use the legacy key names (current
+    names pass through unchanged)."""
+    given = dict(config)
+    out = {k: v for k, v in given.items() if k not in _LEGACY_RULES}
+    ratios = {}
+    for key in (k for k in given if k in _LEGACY_RULES):
+        kind, arg = _LEGACY_RULES[key]
+        value = given[key]
+        if kind == "only":
+            if value != arg:
+                raise ValueError(f"legacy architecture key {key}={value!r}: only {arg!r} is supported")
+        elif kind == "rename":
+            if arg in given:
+                raise ValueError(f"architecture config gives both the legacy {key!r} and its current name {arg!r}")
+            out[arg] = value
         else:
-            out[key] = value
-    if widths:
-        base = widths.get("mlp_width_ratio", 4.0)
-        for old, new in (("video_mlp_width_ratio", "mlp_ratio"), ("text_mlp_width_ratio", "context_mlp_ratio")):
-            if new in config:
-                raise ValueError(f"config sets both {old!r}/mlp_width_ratio and {new!r}")
-            out[new] = base if widths.get(old) is None else widths[old]
+            ratios[key] = value
+    if ratios:
+        base = ratios.get("mlp_width_ratio", 4.0)
+        for key in ("video_mlp_width_ratio", "text_mlp_width_ratio"):
+            target = _LEGACY_RULES[key][1]
+            if target in given:
+                raise ValueError(f"architecture config gives both legacy FFN ratios and {target!r}")
+            out[target] = base if ratios.get(key) is None else ratios[key]
+    renamed = sorted(k for k in given if k in _LEGACY_RULES)
+    if renamed:
+        log.warning(f"architecture config: legacy keys {renamed} mapped to the current names")
     return out
 
 
@@ -368,14 +386,14 @@ class PanVideoDiffusionTransformer(nn.Module):
         self.patch_embed = VideoPatchEmbed(self.patch_size, in_channels, hidden_size)
         self.cap_embedder = nn.Sequential(RMSNorm(text_embed_dim, eps=1e-5), nn.Linear(text_embed_dim, hidden_size))
         self.caption_encoder = CaptionEncoder(hidden_size, num_attention_heads, num_layers=caption_encoder_layers)
-        self.timestep_encoder = TimestepEncoder(hidden_size, activation_factory("silu"))
+        self.timestep_encoder = TimestepEncoder(hidden_size, "silu")
         opts = dict(attention_backend=attention_backend, normalize_qk=normalize_qk, qk_norm_kind=qk_norm_kind,
                     ffn_activation=ffn_activation, mlp_ratio=mlp_ratio, context_mlp_ratio=context_mlp_ratio,
                     zero_init_modulation=zero_init_modulation,
                     text_modulation_timestep_dependent=text_modulation_timestep_dependent)
         self.blocks = nn.ModuleList([JointAttentionBlock(hidden_size, num_attention_heads, **opts)
                                      for _ in range(num_layers)])
-        self.output_head = OutputHead(hidden_size, self.patch_size, self.out_channels, activation_factory("silu"),
+        self.output_head = OutputHead(hidden_size, self.patch_size, self.out_channels, "silu",
                                       zero_init_modulation=zero_init_modulation)
         self.text_type_embedding = TextTypeEmbedding(hidden_size) if use_text_type_embedding else None
 
@@ -453,19 +471,26 @@ class PanVideoDiffusionTransformer(nn.Module):
 
     # ------------------------------------------------------------------ dense (inference)
     def validate_stg_layers(self, stg_skip_layers):
+        """Block indices that the skip-guidance (weak) forward leaves out, checked; () when off."""
         if stg_skip_layers is None:
             return ()
-        if not isinstance(stg_skip_layers, (list, tuple)) or not stg_skip_layers:
-            raise ValueError("stg_skip_layers must be a nonempty list/tuple of zero-based block indices.")
-        if any(type(i) is not int for i in stg_skip_layers):
-            raise ValueError("stg_skip_layers must contain integer block indices (not bool).")
-        if len(set(stg_skip_layers)) != len(stg_skip_layers):
-            raise ValueError("stg_skip_layers must not contain duplicate block indices.")
-        if any(i < 0 or i >= len(self.blocks) for i in stg_skip_layers):
-            raise ValueError(f"stg_skip_layers must be in [0, {len(self.blocks) - 1}].")
-        if self.training or torch.is_grad_enabled():
-            raise ValueError("STG requires model.eval() and torch.no_grad()/inference_mode().")
-        return tuple(stg_skip_layers)
+        layers = stg_skip_layers
+        n = len(self.blocks)
+        problems = []
+        if not isinstance(layers, (list, tuple)) or len(layers) == 0:
+            problems.append("give a non-empty list of block indices")
+        else:
+            if not all(type(i) is int for i in layers):
+                problems.append("indices must be plain ints")
+            elif len(set(layers)) < len(layers):
+                problems.append("an index repeats")
+            elif min(layers) < 0 or max(layers) >= n:
+                problems.append(f"indices must lie in 0..{n - 1}")
+        if not problems and (self.training or torch.is_grad_enabled()):
+            problems.append("skip guidance is an inference feature: call eval() and run under no_grad")
+        if problems:
+            raise ValueError(f"stg_skip_layers={stg_skip_layers!r}: " + "; ".join(problems))
+        return tuple(layers)
 
     def encode_text(self, text_states, text_mask):
         mask = text_mask if self.mask_text_padding else None

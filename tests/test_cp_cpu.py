@@ -101,7 +101,7 @@ def test_ulysses_cp_matches_single_rank(tmp_path, world, cp):
 
 def test_strided_split_partitions_tokens():
     from pan2_b200.data.cp_batch import strided_split
-    from pan2_b200.parallel.ulysses import shard_sizes, grouped_perms
+    from pan2_b200.parallel.ulysses import shard_sizes
     from pan2_b200.models.transformer import PanVideoDiffusionTransformer
     with torch.device("meta"):
         m = PanVideoDiffusionTransformer(**TINY_ARCH)
@@ -120,5 +120,4 @@ def test_strided_split_partitions_tokens():
             seen_v.append(lp.n_video)
         assert sorted(seen_t) == list(range(P.n_text))
         assert sum(seen_v) == P.n_video
-        to_full, to_grouped = grouped_perms(S, cp, "cpu")
-        assert torch.equal(to_grouped[to_full], torch.arange(S))
+        assert list(shard_sizes(S, cp)) == [len(range(r, S, cp)) for r in range(cp)]

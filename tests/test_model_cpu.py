@@ -80,6 +80,16 @@ def test_legacy_block_keys_load():
     assert torch.equal(m2.state_dict()["blocks.0.qkv_proj.weight"], sd["blocks.0.qkv_proj.weight"])
 
 
-def test_timestep_freqs_rebuilt_in_fp32():
+def test_timestep_freqs_stay_exact_fp32():
+    from pan2_b200.models.embeddings import sinusoid_frequencies, timestep_embedding
+    exact = sinusoid_frequencies(256, 10000.0)
     model = tiny_model(num_layers=1).to(torch.bfloat16)
-    assert model.timestep_encoder.freqs.dtype == torch.float32
+    sd = model.state_dict()
+    assert sd["timestep_encoder.freqs"].dtype == torch.float32 and torch.equal(sd["timestep_encoder.freqs"], exact)
+    enc = model.timestep_encoder
+    t = torch.tensor([0.0, 17.0, 999.0])
+    want = enc.out_proj(enc.act(enc.in_proj(timestep_embedding(t, exact).to(torch.bfloat16))))
+    assert torch.equal(enc(t), want)
+    sd["timestep_encoder.freqs"] = sd["timestep_encoder.freqs"].to(torch.bfloat16).float()  # a lossy copy
+    model.load_state_dict(sd)
+    assert torch.equal(model.state_dict()["timestep_encoder.freqs"], exact)
