@@ -704,46 +704,50 @@ void peer_reduce(torch::Tensor peers, int64_t world, torch::Tensor segs, torch::
 
 PYBIND11_MODULE(TORCH_EXTENSION_NAME, m) {
   m.doc() = "pan2_b200 sm_100a kernels";
-  m.def("ln_modulate_fwd", &pan::ln_modulate_fwd);
-  m.def("ln_modulate_bwd", &pan::ln_modulate_bwd);
-  m.def("gate_residual_fwd", &pan::gate_residual_fwd);
-  m.def("gate_bwd", &pan::gate_bwd);
-  m.def("simple_concat_fwd", &pan::simple_concat_fwd);
-  m.def("segment_sum", &pan::segment_sum);
-  m.def("column_sum", &pan::column_sum);
-  m.def("mse_fwd", &pan::mse_fwd);
-  m.def("mse_bwd", &pan::mse_bwd);
-  m.def("gather_rows", &pan::gather_rows);
-  m.def("gemm", &pan::gemm);
-  m.def("gemm_force_cta_group", &pan::gemm_force_cta_group);
-  m.def("attn_set_backward_variant", &pan::attn_set_backward_variant);
-  m.def("attn_set_forward_variant", &pan::attn_set_forward_variant);
-  m.def("attn_get_variant", &pan::attn_get_variant);
-  m.def("gemm_tuning", &pan::gemm_tuning);
-  m.def("gemm_grouped_nt", &pan::gemm_grouped_nt);
-  m.def("gemm_batched", &pan::gemm_batched);
-  m.def("gemm_dgelu", &pan::gemm_dgelu);
-  m.def("qkv_post_fwd", &pan::qkv_post_fwd);
-  m.def("qkv_post_bwd", &pan::qkv_post_bwd);
-  m.def("attn_fwd", &pan::attn_fwd);
-  m.def("attn_bwd", &pan::attn_bwd);
-  m.def("qkv_post_fwd_scatter", &pan::qkv_post_fwd_scatter);
-  m.def("attn_fwd_cp", &pan::attn_fwd_cp);
-  m.def("attn_bwd_cp", &pan::attn_bwd_cp);
-  m.def("sumsq_partial", &pan::sumsq_partial);
-  m.def("norm_and_clip", &pan::norm_and_clip);
-  m.def("muon_momentum", &pan::muon_momentum);
-  m.def("muon_update", &pan::muon_update);
-  m.def("muon_update_peer", &pan::muon_update_peer);
-  m.def("adamw_update", &pan::adamw_update);
-  m.def("split_master", &pan::split_master);
-  m.def("join_master", &pan::join_master);
-  m.def("ns_trace", &pan::ns_trace);
-  m.def("ns_gram_normalize", &pan::ns_gram_normalize);
-  m.def("ns_add_diag", &pan::ns_add_diag);
-  m.def("ns_scale_by_invnorm", &pan::ns_scale_by_invnorm);
-  m.def("error_flag", &pan::error_flag, py::arg("reset") = true);
-  m.def("symm_barrier", &pan::symm_barrier);
-  m.def("peer_gather", &pan::peer_gather);
-  m.def("peer_reduce", &pan::peer_reduce);
+  // Every binding releases the GIL while it runs (arguments are converted first): a launch that
+  // blocks on a full stream queue, e.g. the deferred optimizer's enqueue thread, must not stall the
+  // Python thread that enqueues the forward.  No binding touches Python objects.
+  const auto kNoGil = py::call_guard<py::gil_scoped_release>();
+  m.def("ln_modulate_fwd", &pan::ln_modulate_fwd, kNoGil);
+  m.def("ln_modulate_bwd", &pan::ln_modulate_bwd, kNoGil);
+  m.def("gate_residual_fwd", &pan::gate_residual_fwd, kNoGil);
+  m.def("gate_bwd", &pan::gate_bwd, kNoGil);
+  m.def("simple_concat_fwd", &pan::simple_concat_fwd, kNoGil);
+  m.def("segment_sum", &pan::segment_sum, kNoGil);
+  m.def("column_sum", &pan::column_sum, kNoGil);
+  m.def("mse_fwd", &pan::mse_fwd, kNoGil);
+  m.def("mse_bwd", &pan::mse_bwd, kNoGil);
+  m.def("gather_rows", &pan::gather_rows, kNoGil);
+  m.def("gemm", &pan::gemm, kNoGil);
+  m.def("gemm_force_cta_group", &pan::gemm_force_cta_group, kNoGil);
+  m.def("attn_set_backward_variant", &pan::attn_set_backward_variant, kNoGil);
+  m.def("attn_set_forward_variant", &pan::attn_set_forward_variant, kNoGil);
+  m.def("attn_get_variant", &pan::attn_get_variant, kNoGil);
+  m.def("gemm_tuning", &pan::gemm_tuning, kNoGil);
+  m.def("gemm_grouped_nt", &pan::gemm_grouped_nt, kNoGil);
+  m.def("gemm_batched", &pan::gemm_batched, kNoGil);
+  m.def("gemm_dgelu", &pan::gemm_dgelu, kNoGil);
+  m.def("qkv_post_fwd", &pan::qkv_post_fwd, kNoGil);
+  m.def("qkv_post_bwd", &pan::qkv_post_bwd, kNoGil);
+  m.def("attn_fwd", &pan::attn_fwd, kNoGil);
+  m.def("attn_bwd", &pan::attn_bwd, kNoGil);
+  m.def("qkv_post_fwd_scatter", &pan::qkv_post_fwd_scatter, kNoGil);
+  m.def("attn_fwd_cp", &pan::attn_fwd_cp, kNoGil);
+  m.def("attn_bwd_cp", &pan::attn_bwd_cp, kNoGil);
+  m.def("sumsq_partial", &pan::sumsq_partial, kNoGil);
+  m.def("norm_and_clip", &pan::norm_and_clip, kNoGil);
+  m.def("muon_momentum", &pan::muon_momentum, kNoGil);
+  m.def("muon_update", &pan::muon_update, kNoGil);
+  m.def("muon_update_peer", &pan::muon_update_peer, kNoGil);
+  m.def("adamw_update", &pan::adamw_update, kNoGil);
+  m.def("split_master", &pan::split_master, kNoGil);
+  m.def("join_master", &pan::join_master, kNoGil);
+  m.def("ns_trace", &pan::ns_trace, kNoGil);
+  m.def("ns_gram_normalize", &pan::ns_gram_normalize, kNoGil);
+  m.def("ns_add_diag", &pan::ns_add_diag, kNoGil);
+  m.def("ns_scale_by_invnorm", &pan::ns_scale_by_invnorm, kNoGil);
+  m.def("error_flag", &pan::error_flag, py::arg("reset") = true, kNoGil);
+  m.def("symm_barrier", &pan::symm_barrier, kNoGil);
+  m.def("peer_gather", &pan::peer_gather, kNoGil);
+  m.def("peer_reduce", &pan::peer_reduce, kNoGil);
 }

@@ -20,6 +20,7 @@ This is the B200 restatement of the reference trainer's model wrapping and step
 from __future__ import annotations
 
 import os
+import threading
 from dataclasses import dataclass
 from typing import Dict, List, Optional, Sequence
 
@@ -202,6 +203,8 @@ def _hbm_bytes(device) -> int:
 class TrainEngine:
     """Owns the model, its sharded units and the optimizer state; runs one training step."""
 
+    DEFER_ENQUEUE_TIMEOUT_S = 600.0  # host-side bound on waiting for the optimizer thread
+
     def __init__(self, arch: dict, device: torch.device, *, group: Optional[dist.ProcessGroup] = None,
                  seed: int = 42, optim: Optional[OptimConfig] = None, offload: str = "auto",
                  activation_bytes_estimate: int = 0, replicate_group: Optional[dist.ProcessGroup] = None):
@@ -285,8 +288,11 @@ class TrainEngine:
         self.lr_t = torch.full((1,), self.optim.lr, dtype=torch.float32, device=device)
         self.norm_clip = torch.zeros(2, dtype=torch.float32, device=device)
         # deferred (overlapped) optimizer updates with host-offloaded state and one rank
-        self.defer_optimizer = device.type == "cuda" and os.environ.get("PAN_DEFER_OPTIMIZER", "0") == "1"
+        self.defer_optimizer = device.type == "cuda" and os.environ.get("PAN_DEFER_OPTIMIZER", "1") == "1"
         self._upd_events: Dict[int, torch.cuda.Event] = {}
+        self._upd_ready: Dict[int, threading.Event] = {}
+        self._upd_thread: Optional[threading.Thread] = None
+        self._upd_error: Optional[BaseException] = None
         self._lr_used = torch.zeros(1, dtype=torch.float32, device=device)
         self._clip_used = torch.ones(1, dtype=torch.float32, device=device)
         self._lr_override = None
@@ -492,7 +498,16 @@ class TrainEngine:
         return self._lr_override if self._lr_override is not None else self.lr_t
 
     def _wait_update(self, u: Unit) -> None:
-        """Order the current stream after a deferred optimizer update of ``u`` (if one is pending)."""
+        """Order the current stream after a deferred optimizer update of ``u`` (if one is pending).
+        With the update enqueued from the optimizer thread, first wait (on the host, bounded) until
+        that thread has enqueued the unit and recorded its completion event."""
+        ready = self._upd_ready.pop(u.index, None)
+        if ready is not None and not ready.wait(timeout=self.DEFER_ENQUEUE_TIMEOUT_S):
+            raise RuntimeError(f"deferred optimizer: unit {u.index} was not enqueued within "
+                               f"{self.DEFER_ENQUEUE_TIMEOUT_S} s")
+        if self._upd_error is not None:
+            err, self._upd_error = self._upd_error, None
+            raise RuntimeError("deferred optimizer update failed on its enqueue thread") from err
         ev = self._upd_events.pop(u.index, None)
         if ev is not None:
             torch.cuda.current_stream(self.device).wait_event(ev)
@@ -501,9 +516,14 @@ class TrainEngine:
         """Wait for every deferred optimizer update (before reading weights or optimizer state)."""
         for u in self.sharded.units:
             self._wait_update(u)
+        if self._upd_thread is not None:
+            self._upd_thread.join()
+            self._upd_thread = None
 
     def optimizer_step(self) -> None:
         self.sharded.end_gathers()
+        if self._upd_thread is not None:  # a previous deferred step that no forward consumed
+            self.flush_updates()
         self.step_count += 1
         units = self.sharded.units
         if not self.offload:
@@ -514,20 +534,45 @@ class TrainEngine:
         # streamed: H2D of unit i+1 overlaps compute of unit i; D2H after compute.  Tensors that
         # the placement kept on the GPU are used in place.  With one rank the whole pipeline runs
         # on side streams and overlaps the next forward, which waits per unit (root first, then the
-        # blocks in forward order) right before it reads that unit's weights.
+        # blocks in forward order) right before it reads that unit's weights.  Its few thousand
+        # launches and PCIe-paced copies are enqueued from a host thread of their own, so the main
+        # thread goes on to enqueue the next step while this one's update streams.
         launch = torch.cuda.current_stream(self.device)
         deferred = self.defer_optimizer and self.world == 1
-        if deferred:
-            # private copies: the caller may change the learning rate right after this call
-            self._lr_used.copy_(self.lr_t)
-            self._clip_used.copy_(self.norm_clip[1:2])
-            self._opt_stream.wait_stream(launch)
-            cur = self._opt_stream
-            lr_t, clip = self._lr_used, (self._clip_used if self.optim.max_grad_norm > 0 else None)
-            units = [units[-1]] + list(units[:-1])
-        else:
-            cur = launch
-            lr_t, clip = self.lr_t, (self.norm_clip[1:2] if self.optim.max_grad_norm > 0 else None)
+        if not deferred:
+            clip = self.norm_clip[1:2] if self.optim.max_grad_norm > 0 else None
+            self._stream_update(units, launch, self.lr_t, clip)
+            return
+        # private copies: the caller may change the learning rate right after this call
+        self._lr_used.copy_(self.lr_t)
+        self._clip_used.copy_(self.norm_clip[1:2])
+        start = torch.cuda.Event()
+        start.record(launch)  # everything the update reads is enqueued on `launch` before this point
+        order = [units[-1]] + list(units[:-1])
+        self._upd_events = {}
+        self._upd_error = None
+        ready = {u.index: threading.Event() for u in order}
+        self._upd_ready = dict(ready)  # the forward pops from this copy; the thread signals `ready`
+        clip = self._clip_used if self.optim.max_grad_norm > 0 else None
+
+        def run():
+            try:
+                torch.cuda.set_device(self.device)
+                self._opt_stream.wait_event(start)
+                self._stream_update(order, self._opt_stream, self._lr_used, clip, publish=ready)
+            except BaseException as e:  # surfaced by the next _wait_update
+                self._upd_error = e
+            finally:
+                for ev in ready.values():
+                    ev.set()
+
+        self._upd_thread = threading.Thread(target=run, name="pan2-optimizer-enqueue", daemon=True)
+        self._upd_thread.start()
+
+    def _stream_update(self, units: List[Unit], cur, lr_t: torch.Tensor, clip,
+                       publish: Optional[Dict[int, threading.Event]] = None) -> None:
+        """The streamed update of ``units`` on stream ``cur``.  With ``publish`` (deferred mode) a
+        completion event is recorded per unit and ``publish[unit]`` is set once it is."""
         self._lr_override = lr_t
         staged = {}
 
@@ -579,10 +624,11 @@ class TrainEngine:
                     t.record_stream(cur)
             with torch.cuda.stream(cur):
                 self._step_unit(u, lo, st, clip)
-            if deferred:
-                ev = torch.cuda.Event()
-                ev.record(cur)
-                self._upd_events[u.index] = ev
+            if publish is not None:
+                done_u = torch.cuda.Event()
+                done_u.record(cur)
+                self._upd_events[u.index] = done_u
+                publish[u.index].set()
             if parts:
                 self._d2h.wait_stream(cur)
                 with torch.cuda.stream(self._d2h):
@@ -595,11 +641,8 @@ class TrainEngine:
                     for t in views:
                         t.record_stream(self._d2h)
         self._lr_override = None
-        if deferred:
-            # the host halves of the next step's state must be written back before they are re-read
-            cur.wait_stream(self._d2h)
-        else:
-            cur.wait_stream(self._d2h)
+        # the host halves must be written back before the next step re-reads them
+        cur.wait_stream(self._d2h)
 
     def _staging_slots(self, nbytes: int) -> List[torch.Tensor]:
         """The two device slots for streamed optimizer state (grown to ``nbytes`` each); empty when
