@@ -55,12 +55,35 @@ def parse():
     return ap.parse_args()
 
 
+REF_DIR = os.path.join(ROOT, "baseline", "_ref")
+# The reference's own entry modules on the training path (train.py builds the transformer, FA4
+# attention, quack GEMMs and the patched Muon from these), imported in this order.
+REF_MODULES = ("pan.models.transformers.pan_transformer", "pan.utils.flash_attention",
+               "pan.models.transformers.modules.mlp_ops", "pan.optim.patch_muon")
+
+
 def reference_arm(args):
-    print(json.dumps({
-        "impl": "reference", "metric": METRIC,
-        "unavailable": "the reference has no setup.py/pyproject.toml (pip cannot install it) and imports "
-                       "diffusers, flash_attn.cute (FA4) and quack>=0.6.3, none of which exist in this image",
-    }), flush=True)
+    """Runs the unmodified reference from baseline/_ref through its own modules when they import;
+    otherwise prints why not (the import error itself), as one JSON line."""
+    line = {"impl": "reference", "metric": METRIC}
+    if not os.path.isdir(os.path.join(REF_DIR, "pan")):
+        line["unavailable"] = ("baseline/_ref holds no reference source: pip refuses to install it (the project has "
+                               "no setup.py or pyproject.toml)")
+        print(json.dumps(line), flush=True)
+        return
+    import importlib
+    import sys
+    sys.path.insert(0, REF_DIR)
+    for mod in REF_MODULES:
+        try:
+            importlib.import_module(mod)
+        except Exception as err:  # the reference's hard dependencies are absent from this image
+            line["unavailable"] = f"importing the reference's {mod} fails: {type(err).__name__}: {err}"[:400]
+            print(json.dumps(line), flush=True)
+            return
+    line["unavailable"] = ("the reference's modules import, but its trainer needs its pinned stack (torch 2.12, "
+                           "flash-attn 4, quack >= 0.6.3) to run the 29B step")
+    print(json.dumps(line), flush=True)
 
 
 def main():
