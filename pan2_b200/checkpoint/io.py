@@ -1,23 +1,26 @@
-"""Sharded checkpoints of the flat-unit engine: streamed per unit, resharded on load.
+"""Checkpoints of the flat-unit engine: torch distributed checkpoint (DCP) folders, streamed per tensor,
+resharded on load.
 
-Directory layout of ``checkpoint-<step>/`` (the same folders as the reference, train.py:455-458 and
-1060-1151):
+Directory layout of ``checkpoint-<step>/`` (the reference's, train.py:455-458 and 1060-1151):
 
-* ``transformer/meta.json`` + ``transformer/<unit>.rank<r>-of-<W>.safetensors`` -- every rank writes
-  the fp32 master rows it owns of every parameter of the unit (``Shard(0)`` row ranges with
-  ``ceil(rows / W)`` rows per rank, the FSDP2 rule), keyed by the parameter's full name;
-* ``optimizer/<unit>.rank<r>-of-<W>.safetensors`` -- the same rows of ``<name>.momentum_buffer``
-  (Muon) or ``<name>.exp_avg`` / ``<name>.exp_avg_sq`` (AdamW), plus ``optimizer/meta.json``;
+* ``transformer/`` -- a DCP folder (``.metadata`` + one ``__<rank>_0.distcp`` per rank) holding every
+  parameter under its model name as fp32, each rank writing the ``Shard(0)`` rows it owns
+  (``ceil(rows / W)`` rows per rank, FSDP2's rule).  The reference's converter and loaders read it
+  as they read the reference trainer's own ``transformer/`` folder;
+* ``optimizer/`` -- a DCP folder with the same rows of ``state.<name>.momentum_buffer`` (Muon) or
+  ``state.<name>.exp_avg`` / ``state.<name>.exp_avg_sq`` (AdamW), plus ``pan2_state.json`` (step
+  count, optimizer choice);
 * ``training_state.pt`` -- ``{"lr_schedulers": {name: state}, "global_step": N}``;
 * ``dataloader/<dp_rank>.json`` -- the packing loader's cursor;
 * ``COMPLETE`` -- written by rank 0 after every rank finished; a folder without it is unreadable and
   resume falls back to the previous checkpoint (train.py:1256-1279).
 
-Units are written one at a time (device -> host -> file), so no rank ever holds more than one unit of
-host copies; there is no gather to one rank.  Loading reads, for every parameter, only the row range
-the loading rank owns, from whichever saved rank files hold it (``safe_open(...).get_slice``), so a
-checkpoint loads on any world size.  :func:`consolidate` writes a plain state dict (5 GB safetensors
-shards + index), the format warm starts, the converter and the inference pipeline read.
+Saving declares each tensor's rows to DCP and produces them only when the writer asks for them
+(:mod:`pan2_b200.checkpoint.dcp_rows`), so a rank holds one tensor's host copy at a time and there is
+no gather.  Loading requests, per unit, exactly the rows the loading rank owns, so a checkpoint loads
+on any world size.  Folders of the earlier per-rank safetensors format (``meta.json`` beside
+``<unit>.rank<r>-of-<W>.safetensors``) still load.  :func:`consolidate` writes a plain state dict
+(5 GB safetensors shards + index).
 """
 from __future__ import annotations
 
@@ -70,40 +73,49 @@ def _barrier(group):
         dist.barrier(group=group)
 
 
-def save_engine(engine, root: str, *, group=None, save_optimizer: bool = True) -> None:
-    """Every rank calls this.  Writes ``transformer/`` (and ``optimizer/``) of ``root``."""
-    from safetensors.torch import save_file
+def _slot_producer(u, s, k: int, which: str, key: Optional[str] = None, engine=None):
+    """Producer of rows ``[0, k)`` of slot ``s`` (this rank's rows) as a CPU fp32 tensor shaped like
+    the parameter: the joined fp32 master (``which == "w"``) or optimizer state ``key``."""
     from ..optim.flat_ops import join_master
+    rest = tuple(s.shape[1:]) if len(s.shape) > 1 else ()
+
+    def produce():
+        n = k * s.cols
+        if which == "w":
+            x = join_master(u.hi[s.shard_off:s.shard_off + n], u.lo[s.shard_off:s.shard_off + n])
+        else:
+            x = _state_rows(engine, u, s, key, k).reshape(-1).float()
+        return x.cpu().reshape((k,) + rest)
+    return produce
+
+
+def save_engine(engine, root: str, *, group=None, save_optimizer: bool = True) -> None:
+    """Every rank calls this (collectively over ``group``, default: the default process group).
+    Writes ``transformer/`` (and ``optimizer/``) of ``root`` as DCP folders."""
+    from .dcp_rows import RowChunk, save_row_chunks
     model_dir, optim_dir, _ = checkpoint_layout(root)
     world, rank = engine.world, engine.rank
-    os.makedirs(model_dir, exist_ok=True)
-    if save_optimizer:
-        os.makedirs(optim_dir, exist_ok=True)
+    if hasattr(engine, "flush_updates"):
+        engine.flush_updates()
     if engine.device.type == "cuda":
         torch.cuda.synchronize(engine.device)
+    no_dist = not (dist.is_initialized() and dist.get_world_size(group) > 1)
+    weights, states = [], []
     for u in engine.sharded.units:
-        x = join_master(u.hi, u.lo).cpu()
-        w, o = {}, {}
         for s in u.slots:
             a, b = rows_owned(s.rows, world, rank)
-            w[s.name] = _slot_rows(x, s, b - a).reshape(b - a, s.cols).clone()
+            shape = tuple(s.shape) if len(s.shape) > 0 else (s.rows,)
+            weights.append(RowChunk(s.name, shape, a, b - a, torch.float32, _slot_producer(u, s, b - a, "w")))
             if save_optimizer:
                 for key, label in _opt_names(engine, s):
-                    o[f"{s.name}.{label}"] = _state_rows(engine, u, s, key, b - a).float().cpu().clone()
-        save_file(w, os.path.join(model_dir, _fname(u.name, rank, world)), metadata={"format": FORMAT})
-        if save_optimizer:
-            save_file(o, os.path.join(optim_dir, _fname(u.name, rank, world)), metadata={"format": FORMAT})
-    if rank == 0:
-        meta = {"format": FORMAT, "world_size": world,
-                "units": [{"name": u.name, "params": [{"name": s.name, "shape": list(s.shape), "rows": s.rows,
-                                                       "cols": s.cols, "kind": s.kind} for s in u.slots]}
-                          for u in engine.sharded.units]}
-        with open(os.path.join(model_dir, "meta.json"), "w") as f:
-            json.dump(meta, f)
-        if save_optimizer:
-            with open(os.path.join(optim_dir, "meta.json"), "w") as f:
-                json.dump({"format": FORMAT, "world_size": world, "step": engine.step_count,
-                           "use_muon": engine.optim.use_muon}, f)
+                    states.append(RowChunk(f"state.{s.name}.{label}", shape, a, b - a, torch.float32,
+                                           _slot_producer(u, s, b - a, "state", key, engine)))
+    save_row_chunks(model_dir, weights, process_group=group, no_dist=no_dist)
+    if save_optimizer:
+        save_row_chunks(optim_dir, states, process_group=group, no_dist=no_dist)
+        if rank == 0:
+            with open(os.path.join(optim_dir, "pan2_state.json"), "w") as f:
+                json.dump({"step": engine.step_count, "use_muon": engine.optim.use_muon}, f)
 
 
 class ShardedReader:
@@ -160,18 +172,75 @@ class ShardedReader:
 def load_engine(engine, root: str, *, load_optimizer: bool = True, strict: bool = True) -> List[str]:
     """Load ``root``'s transformer (and optimizer) rows this rank owns; works across world sizes.
     Returns parameter names absent from the checkpoint (raises when ``strict``)."""
-    from ..parallel.sharded import set_master
-    from ..optim.flat_ops import join_master
+    from .dcp_rows import is_dcp_folder
     model_dir, optim_dir, _ = checkpoint_layout(root)
     if hasattr(engine, "flush_updates"):
         engine.flush_updates()
     if engine.device.type == "cuda":
         torch.cuda.synchronize(engine.device)
+    if load_optimizer and not os.path.isdir(optim_dir):
+        raise ValueError(f"{root} holds no optimizer state")
+    if is_dcp_folder(model_dir):
+        missing = _load_dcp(engine, model_dir, optim_dir if load_optimizer else None)
+    else:
+        missing = _load_safetensors_shards(engine, model_dir, optim_dir if load_optimizer else None)
+    if strict and missing:
+        raise ValueError(f"{model_dir} is missing {len(missing)} transformer tensors, e.g. {missing[:5]}")
+    return missing
+
+
+def _load_dcp(engine, model_dir: str, optim_dir: Optional[str]) -> List[str]:
+    from .dcp_rows import load_row_chunks, tensor_specs
+    from ..parallel.sharded import set_master
+    from ..optim.flat_ops import join_master
+    world, rank = engine.world, engine.rank
+    have_w = tensor_specs(model_dir)
+    have_o = tensor_specs(optim_dir) if optim_dir is not None else {}
+    missing = []
+    for u in engine.sharded.units:
+        x = join_master(u.hi, u.lo).cpu().clone()
+        want_w, want_o = {}, {}
+        for s in u.slots:
+            if s.name not in have_w:
+                missing.append(s.name)
+                continue
+            a, b = rows_owned(s.rows, world, rank)
+            want_w[s.name] = (a, torch.empty((b - a,) + tuple(have_w[s.name][0][1:]), dtype=torch.float32))
+            if optim_dir is not None:
+                for key, label in _opt_names(engine, s):
+                    name = f"state.{s.name}.{label}"
+                    if name in have_o:
+                        want_o[name] = (a, torch.empty((b - a,) + tuple(have_o[name][0][1:]), dtype=torch.float32))
+        load_row_chunks(model_dir, want_w)
+        load_row_chunks(optim_dir, want_o) if optim_dir is not None else None
+        for s in u.slots:
+            if s.name not in want_w:
+                continue
+            a, rows = want_w[s.name]
+            _slot_rows(x, s, rows.shape[0]).copy_(rows.reshape(rows.shape[0], -1))
+            for key, label in (_opt_names(engine, s) if optim_dir is not None else ()):
+                got = want_o.get(f"state.{s.name}.{label}")
+                if got is not None:
+                    dst = _state_rows(engine, u, s, key, got[1].shape[0])
+                    dst.copy_(got[1].reshape(dst.shape).to(dst.device, dst.dtype))
+        set_master(u, x.to(engine.device))
+        if world == 1:
+            engine.sharded.bind_weights(u, u.hi)
+    if optim_dir is not None:
+        meta_path = os.path.join(optim_dir, "pan2_state.json")
+        if os.path.exists(meta_path):
+            with open(meta_path) as f:
+                engine.step_count = int(json.load(f).get("step", engine.step_count))
+    return missing
+
+
+def _load_safetensors_shards(engine, model_dir: str, optim_dir: Optional[str]) -> List[str]:
+    """The earlier per-rank safetensors format (``meta.json`` + ``<unit>.rank<r>-of-<W>``)."""
+    from ..parallel.sharded import set_master
+    from ..optim.flat_ops import join_master
     wr = ShardedReader(model_dir)
-    orr = None
-    if load_optimizer:
-        if not os.path.isdir(optim_dir):
-            raise ValueError(f"{root} holds no optimizer state")
+    orr, ometa = None, {}
+    if optim_dir is not None:
         orr = ShardedReader(optim_dir, meta_folder=model_dir)
         with open(os.path.join(optim_dir, "meta.json")) as f:
             ometa = json.load(f)
@@ -194,8 +263,6 @@ def load_engine(engine, root: str, *, load_optimizer: bool = True, strict: bool 
             engine.sharded.bind_weights(u, u.hi)
     if orr is not None:
         engine.step_count = int(ometa.get("step", engine.step_count))
-    if strict and missing:
-        raise ValueError(f"{model_dir} is missing {len(missing)} transformer tensors, e.g. {missing[:5]}")
     return missing
 
 

@@ -244,7 +244,7 @@ class Trainer:
             os.makedirs(root, exist_ok=True)
             ckpt.clear_complete(root)  # a folder being rewritten (after a rollback) is incomplete until done
         self._barrier()
-        ckpt.save_engine(self.engine, root)
+        ckpt.save_engine(self.engine, root, group=self.layout.cpu_group if self.world > 1 else None)
         _, _, state_file = ckpt.checkpoint_layout(root)
         if self.is_main:
             torch.save({"lr_schedulers": {"transformer": self.runner.state_dict()}, "global_step": step,

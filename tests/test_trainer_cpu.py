@@ -100,11 +100,11 @@ def test_injected_exception_surfaces(data_dir, tmp_path):
 def test_corrupt_latest_checkpoint_falls_back(data_dir, tmp_path):
     _train(_cfg(data_dir, tmp_path / "f", max_steps=4, save_interval=2))
     tdir = tmp_path / "f" / "checkpoint-4" / "transformer"
-    shards = [f for f in os.listdir(tdir) if f.endswith(".safetensors")]
+    shards = [f for f in os.listdir(tdir) if f.endswith(".distcp")]
     assert shards
     for f in shards:
         with open(tdir / f, "wb") as fh:
-            fh.write(b"not a safetensors file")
+            fh.write(b"not a checkpoint file")
     tr, rest = _train(_cfg(data_dir, tmp_path / "f", max_steps=5, save_interval=100))
     assert [h["step"] for h in rest] == [2, 3, 4]  # resumed from checkpoint-2
 
