@@ -138,7 +138,7 @@ def run_gemm(name, M, N, K, layout, timer, library, peaks, band_mbs=(None,), pro
     return recs
 
 
-def run_attention(small, timer, library, peaks, which, fwd_variants=(None,), bwd_variants=(None,)):
+def run_attention(small, timer, library, peaks, which, fwd_variants=(None,)):
     E = ext()
     lens = [8192] if small else [CLIP_TOKENS] * CLIPS
     L = sum(lens)
@@ -146,10 +146,10 @@ def run_attention(small, timer, library, peaks, which, fwd_variants=(None,), bwd
     scale = 1 / math.sqrt(HEAD_DIM)
     it_f, it_b = work_items(lens, 256, q.device), work_items(lens, 128, q.device)
     fl = sum(4.0 * s * s * HEAD_DIM * HEADS for s in lens)
-    default_f, default_b = E.attn_get_variant(0), E.attn_get_variant(1)
+    default_f = E.attn_get_variant(0)
     out = []
     o, lse = E.attn_fwd(q, k, v, it_f, L, scale)
-    lib_f = lib_b = None
+    lib_f = None
     if "fwd" in which:
         for var in fwd_variants:
             E.attn_set_forward_variant(default_f if var is None else int(var))
@@ -167,18 +167,13 @@ def run_attention(small, timer, library, peaks, which, fwd_variants=(None,), bwd
         o, lse = E.attn_fwd(q, k, v, it_f, L, scale)
         do = torch.randn_like(o)
         flb = 2.5 * fl  # dV, dP, dQ, dK GEMMs plus the S recompute
-        for var in bwd_variants:
-            E.attn_set_backward_variant(default_b if var is None else int(var))
-            ms = timer(lambda: E.attn_bwd(do, q, k, v, o, lse, it_b, it_b, L, scale))
-            rec = dict(case="attn_bwd", segments=lens, heads=HEADS, head_dim=HEAD_DIM,
-                       variant=E.attn_get_variant(1), ms=round(ms, 4), tflops=round(flb / ms / 1e9, 1),
-                       frac_of_peak=round(flb / ms / 1e9 / peaks[1], 3))
-            rec.update(timer.clock_fields("", ms))
-            if library:
-                lib_b = lib_b or _sdpa(q, lens, timer, flb, backward=True)
-                rec.update(lib_b)
-            out.append(rec)
-        E.attn_set_backward_variant(default_b)
+        ms = timer(lambda: E.attn_bwd(do, q, k, v, o, lse, it_b, it_b, L, scale))
+        rec = dict(case="attn_bwd", segments=lens, heads=HEADS, head_dim=HEAD_DIM, ms=round(ms, 4),
+                   tflops=round(flb / ms / 1e9, 1), frac_of_peak=round(flb / ms / 1e9 / peaks[1], 3))
+        rec.update(timer.clock_fields("", ms))
+        if library:
+            rec.update(_sdpa(q, lens, timer, flb, backward=True))
+        out.append(rec)
     for r in out:
         r["error_flag"] = E.error_flag(True)
     return out
@@ -243,14 +238,14 @@ def main():
     ap.add_argument("--iters", type=int, default=10)
     ap.add_argument("--warmup", type=int, default=3)
     ap.add_argument("--no-library", action="store_true", help="skip the cuBLAS / SDPA comparisons")
-    ap.add_argument("--attn-bwd-variant", default=None,
-                    help="comma list of attention backward variants: 0 two passes, 1 fused, 2 pipelined, "
-                         "3 fused with the reordered schedule")
-    ap.add_argument("--attn-fwd-variant", default=None, help="comma list of attention forward variants (0..5)")
+    ap.add_argument("--attn-fwd-variant", default=None,
+                    help="comma list of attention forward variants (1: in-order MMA issue, the default; 0: PV "
+                         "completion awaited before the next score GEMM)")
     ap.add_argument("--gemm-band-mb", default=None,
                     help="comma list of GEMM M-band budgets in MB (0 = N bands only)")
     ap.add_argument("--gemm-probe", default=None,
-                    help="comma list of GEMM probe bits (4: waits sleep between polls; timing experiments)")
+                    help="comma list of GEMM probe bits (timing experiments: 1 skips the epilogue stores, 2 "
+                         "re-reads k-block 0)")
     ap.add_argument("--sustain-s", type=float, default=0.0,
                     help="run each op back to back this long before timing (clocks settle under the power cap)")
     args = ap.parse_args()
@@ -266,8 +261,7 @@ def main():
                 print(json.dumps(rec), flush=True)
     which = [w for w in ("fwd", "bwd") if pat.search("attn_" + w)]
     if which:
-        for r in run_attention(args.small, timer, library, peaks, which, lst(args.attn_fwd_variant),
-                               lst(args.attn_bwd_variant)):
+        for r in run_attention(args.small, timer, library, peaks, which, lst(args.attn_fwd_variant)):
             print(json.dumps(r), flush=True)
     which = [w for w in ("ln_modulate", "gate_residual") if pat.search(w)]
     if which:

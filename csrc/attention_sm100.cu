@@ -1,8 +1,11 @@
 // Variable-length non-causal attention for sm_100a (tcgen05 + TMEM + TMA), head_dim 128.
+// Replaces the reference's FlashAttention-4 varlen calls (pan/utils/flash_attention.py:18-86).
 //
-// Forward (one CTA = one head x two 128-row query tiles "A" and "B" of one segment):
-//   warp 0       TMA: Q_A, Q_B once; then K_j, V_j through a 3-slot smem ring
-//   warp 1       MMA (one lane): S_X = Q_X K_j^T into TMEM, O_X += P_X V_j from smem P
+// Forward (one CTA = one head x two 128-row query tiles "A" and "B" of one segment; 10 warps):
+//   warp 0       TMA: Q_A, Q_B once; then K_j, V_j through a 5-slot smem ring
+//   warp 1       MMA (one lane): S_X = Q_X K_j^T into TMEM; O_X += P_X V_j with P_X read from TMEM
+//                (bf16, written over the first 64 columns of S_X); the next S_X is issued right
+//                behind PV_X (one thread's MMAs execute in order)
 //   warps 2..5   softmax of tile A (one TMEM lane = one query row per thread)
 //   warps 6..9   softmax of tile B
 // The two tiles ping-pong: while one softmax group works, the tensor core runs the other tile's
@@ -10,13 +13,10 @@
 // the running max grows by more than 8 (a factor of 256), so most iterations leave O in TMEM
 // untouched.  Outputs O (bf16, [L, H, D]) and the natural-log LSE ([H, L] fp32).
 //
-// Backward is two passes of one templated kernel sharing the same skeleton:
-//   MODE_DQ  : per query tile, loop over key tiles:  S = Q K^T, dP = dO V^T,
-//              dS = P (dP - Delta),  dQ += dS K
-//   MODE_DKV : per key tile, loop over query tiles:  S^T = K Q^T, dP^T = V dO^T,
-//              dV += P^T dO,  dK += dS^T Q
-// (the FlashAttention-2 recurrences, with P recomputed from the saved LSE), so no atomics are
-// needed.  TMEM holds the two score-shaped products and up to two accumulators (4 x 128 columns).
+// Backward is one fused pass, key tiles outer (attn_bwd_fused_kernel): per 128-query tile S^T and
+// dP^T on the tensor core, P^T / dS^T by the elementwise warps (P recomputed from the saved LSE),
+// dV += P^T dO and dK += dS^T Q with P^T / dS^T as TMEM operands, dQ^T = K^T dS^T drained by four
+// warps into an fp32 accumulator through TMA reduce-add stores, which a last kernel scales to bf16.
 //
 // Smem tiles are 128 rows x 64 columns bf16 with the 128-byte swizzle, two per 128-wide operand.
 // The same bytes serve as a K-major operand (rows = M/N, e.g. K for S = Q K^T) or an MN-major one
@@ -33,7 +33,6 @@ constexpr int D = 128;
 constexpr int BT = 128;                    // rows per tile (queries or keys)
 constexpr int TILE_BYTES = BT * D * 2;     // 32 KB (two 16 KB swizzled halves)
 constexpr int HALF_BYTES = TILE_BYTES / 2;
-constexpr int RING = 3;
 constexpr float kLog2e = 1.4426950408889634f;
 constexpr float kLn2 = 0.6931471805599453f;
 
@@ -83,22 +82,6 @@ __device__ __forceinline__ void store_row32_swizzled(uint8_t* tile, int r, int c
 
 __device__ __forceinline__ void fence_async_smem() { asm volatile("fence.proxy.async.shared::cta;" ::: "memory"); }
 
-// 2^x on the FMA pipe: x = j + f with j = round(x) (float magic-number rounding) and |f| <= 1/2;
-// 2^f by a degree-3 polynomial fitted here for minimum relative error on [-1/2, 1/2] (iteratively
-// reweighted least squares; max relative error 7.5e-5, far below bf16's 3.9e-3); 2^j is added to the
-// exponent field.  Half of the softmax exponentials use this so the SFU and FMA pipes share the work.
-__device__ __forceinline__ float poly_exp2(float x) {
-  x = fmaxf(x, -127.f);
-  const float magic = 12582912.f;  // 1.5 * 2^23
-  const float y = __fadd_rn(x, magic);
-  const float j = __fsub_rn(y, magic);
-  const float f = __fsub_rn(x, j);
-  const float p = fmaf(fmaf(fmaf(0.05517150138583113f, f, 0.24261095811365377f), f, 0.6932609941182479f), f,
-                       0.999928083295878f);
-  const int ji = __float_as_int(y) - __float_as_int(magic);
-  return __int_as_float(__float_as_int(p) + (ji << 23));
-}
-
 // 2^x on the SFU (PTX ex2.approx.ftz.f32, ~2 ulp); softmax probabilities are rounded to bf16 anyway.
 // Packed fp32 pair arithmetic (one instruction for two lanes' worth of FMA / add) and a 3-input
 // max: the forward softmax is bound by instruction issue, not by the MUFU exponentials.
@@ -115,12 +98,6 @@ __device__ __forceinline__ void fadd2(float& d0, float& d1, float a0, float a1, 
       : "=f"(d0), "=f"(d1)
       : "f"(a0), "f"(a1), "f"(b0), "f"(b1));
 }
-__device__ __forceinline__ void fmul2(float& d0, float& d1, float a0, float a1, float b0, float b1) {
-  asm("{\n\t.reg .b64 ra, rb, rd;\n\tmov.b64 ra, {%2, %3};\n\tmov.b64 rb, {%4, %5};\n\t"
-      "mul.rn.f32x2 rd, ra, rb;\n\tmov.b64 {%0, %1}, rd;\n\t}"
-      : "=f"(d0), "=f"(d1)
-      : "f"(a0), "f"(a1), "f"(b0), "f"(b1));
-}
 __device__ __forceinline__ float fmax3(float a, float b, float c) {
   float d;
   asm("max.f32 %0, %1, %2, %3;" : "=f"(d) : "f"(a), "f"(b), "f"(c));
@@ -133,48 +110,20 @@ __device__ __forceinline__ float fast_exp2(float x) {
   return y;
 }
 
-// Two 2^x on the FMA pipe with packed pair arithmetic (the split and polynomial of poly_exp2);
-// arguments below -127 are clamped (their result, < 2^-126, is below what bf16 P resolves).
-__device__ __forceinline__ void poly_exp2x2(float x0, float x1, float& r0, float& r1) {
-  x0 = fmaxf(x0, -127.f);
-  x1 = fmaxf(x1, -127.f);
-  const float magic = 12582912.f;
-  float y0, y1, j0, j1, f0, f1, p0, p1;
-  fadd2(y0, y1, x0, x1, magic, magic);
-  fadd2(j0, j1, y0, y1, -magic, -magic);
-  fadd2(f0, f1, x0, x1, -j0, -j1);
-  ffma2(p0, p1, 0.05517150138583113f, 0.05517150138583113f, f0, f1, 0.24261095811365377f, 0.24261095811365377f);
-  ffma2(p0, p1, p0, p1, f0, f1, 0.6932609941182479f, 0.6932609941182479f);
-  ffma2(p0, p1, p0, p1, f0, f1, 0.999928083295878f, 0.999928083295878f);
-  r0 = __int_as_float(__float_as_int(p0) + ((__float_as_int(y0) - __float_as_int(magic)) << 23));
-  r1 = __int_as_float(__float_as_int(p1) + ((__float_as_int(y1) - __float_as_int(magic)) << 23));
-}
-
 // ============================================================================ forward
 constexpr int FWD_THREADS = 320;
 constexpr int FWD_RING = 5;  // K/V tiles in flight (P lives in TMEM, so the smem goes to the ring)
 constexpr int FWD_SMEM = 2 * TILE_BYTES /*Q*/ + FWD_RING * TILE_BYTES + 1024 + 256;
 
-// Forward variant bits (template argument V):
-//   1  PAIRED   two score chunks per TMEM wait (two-pass softmax only)
-//   2  PACKED   packed f32x2 FMA / add and 3-input max
-//   4  INORDER  the next score GEMM of a tile is issued right after that tile's PV GEMM: tcgen05.mma
-//               instructions of one thread execute in issue order, so S(j+1) cannot overwrite the
-//               P(j) columns before PV(j) has read them, and no completion wait sits between them
-//   8  ROWREG   the whole 128-score row is loaded once into registers (one TMEM pass for max and exp)
-//   bits 4..7   EMU: of each 32-column chunk's 16 column pairs, the last EMU pairs are exponentiated
-//               with the FMA-pipe polynomial instead of the MUFU unit (ROWREG only)
-constexpr int FWD_PAIRED = 1, FWD_PACKED = 2, FWD_INORDER = 4, FWD_ROWREG = 8;
-constexpr int fwd_variant(int flags, int emu) { return flags | (emu << 4); }
-
-template <int V>
+// INORDER: the next score GEMM of a tile is issued right after that tile's PV GEMM.  tcgen05.mma
+// instructions of one thread execute in issue order, so S(j+1) cannot overwrite the P(j) columns
+// before PV(j) has read them and no completion wait is needed between them (measured: ~6 % less
+// time per SM clock than awaiting PV's completion first, which the other instance does).
+template <bool INORDER>
 __global__ void __launch_bounds__(FWD_THREADS, 1)
 attn_fwd_kernel(const __grid_constant__ CUtensorMap qmap, const __grid_constant__ CUtensorMap kmap,
                 const __grid_constant__ CUtensorMap vmap, const WorkItem* __restrict__ items, int L, int H,
                 float scale_log2, __nv_bfloat16* __restrict__ out, float* __restrict__ lse, const PeerRows o_peer) {
-  constexpr bool PAIRED = V & FWD_PAIRED, PACKED = V & FWD_PACKED, INORDER = V & FWD_INORDER,
-                 ROWREG = V & FWD_ROWREG;
-  constexpr int EMU = (V >> 4) & 15;
   extern __shared__ uint8_t smem_raw[];
   uint8_t* smem = reinterpret_cast<uint8_t*>((reinterpret_cast<uintptr_t>(smem_raw) + 1023) & ~uintptr_t(1023));
   uint8_t* sQ = smem;                                 // 2 tiles
@@ -357,40 +306,9 @@ attn_fwd_kernel(const __grid_constant__ CUtensorMap qmap, const __grid_constant_
 #pragma unroll
       for (int i = 0; i < 32; i += 2) {
         float x0, x1;
-        if (PACKED) {
-          ffma2(x0, x1, __uint_as_float(r[i]), __uint_as_float(r[i + 1]), scale_log2, scale_log2, -m_used, -m_used);
-        } else {
-          x0 = fmaf(__uint_as_float(r[i]), scale_log2, -m_used);
-          x1 = fmaf(__uint_as_float(r[i + 1]), scale_log2, -m_used);
-        }
+        ffma2(x0, x1, __uint_as_float(r[i]), __uint_as_float(r[i + 1]), scale_log2, scale_log2, -m_used, -m_used);
         float p0 = fast_exp2(x0);
         float p1 = fast_exp2(x1);
-        if (valid < BT) {
-          p0 = c0 + i < valid ? p0 : 0.f;
-          p1 = c0 + i + 1 < valid ? p1 : 0.f;
-        }
-        if (PACKED) {
-          fadd2(l0, l1, l0, l1, p0, p1);
-        } else {
-          l0 += p0;
-          l1 += p1;
-        }
-        w[i >> 1] = pack_bf16(p0, p1);
-      }
-    };
-    // the same for 16 columns (8 words, stored with the x8 TMEM shape to keep the live range short);
-    // `c0 & 31` places them in their 32-column chunk for EMU
-    auto exp_half = [&](const uint32_t* r, int c0, int valid, uint32_t (&w)[8], float& l0, float& l1) {
-#pragma unroll
-      for (int i = 0; i < 16; i += 2) {
-        float x0, x1, p0, p1;
-        ffma2(x0, x1, __uint_as_float(r[i]), __uint_as_float(r[i + 1]), scale_log2, scale_log2, -m_used, -m_used);
-        if ((((c0 & 31) + i) >> 1) >= 16 - EMU) {
-          poly_exp2x2(x0, x1, p0, p1);
-        } else {
-          p0 = fast_exp2(x0);
-          p1 = fast_exp2(x1);
-        }
         if (valid < BT) {
           p0 = c0 + i < valid ? p0 : 0.f;
           p1 = c0 + i + 1 < valid ? p1 : 0.f;
@@ -404,106 +322,45 @@ attn_fwd_kernel(const __grid_constant__ CUtensorMap qmap, const __grid_constant_
       tc_fence_after();
       const int valid = min(BT, it.seg_len - j * BT);
       float l0 = 0.f, l1 = 0.f;
-      if (ROWREG) {
-        // one TMEM pass: the 128 scores of this row stay in registers for the max and the exp
-        uint32_t s[128];
-#pragma unroll
-        for (int c = 0; c < 4; ++c) tmem_ld32(tS + c * 32, *reinterpret_cast<uint32_t(*)[32]>(&s[c * 32]));
-        tmem_ld_wait();
-        float mx[4] = {-INFINITY, -INFINITY, -INFINITY, -INFINITY};
+      // two TMEM passes (max, then exp), two 32-column chunks per TMEM wait (10 warps cap registers
+      // at 168 per thread, so 64 scores are live at a time)
+      float mx0 = -INFINITY, mx1 = -INFINITY;
+      auto max_chunk = [&](const uint32_t (&r)[32], int c0) {
         if (valid == BT) {
 #pragma unroll
-          for (int i = 0; i < 128; i += 8) {
-#pragma unroll
-            for (int u = 0; u < 4; ++u)
-              mx[u] = fmax3(mx[u], __uint_as_float(s[i + 2 * u]), __uint_as_float(s[i + 2 * u + 1]));
+          for (int i = 0; i < 32; i += 4) {
+            mx0 = fmax3(mx0, __uint_as_float(r[i]), __uint_as_float(r[i + 1]));
+            mx1 = fmax3(mx1, __uint_as_float(r[i + 2]), __uint_as_float(r[i + 3]));
           }
         } else {
 #pragma unroll
-          for (int i = 0; i < 128; ++i)
-            if (i < valid) mx[i & 3] = fmaxf(mx[i & 3], __uint_as_float(s[i]));
+          for (int i = 0; i < 32; ++i)
+            if (c0 + i < valid) mx0 = fmaxf(mx0, __uint_as_float(r[i]));
         }
-        const float m_new = fmaxf(m_used, fmaxf(fmaxf(mx[0], mx[1]), fmaxf(mx[2], mx[3])) * scale_log2);
-        // P = exp2(S * scale - m) as bf16 pairs into the first 64 columns of S, with the maximum this
-        // tile settles on; P is written before O is rescaled, so the score registers are dead by
-        // the time the rescale needs its own
-        const float m_keep = m_used;
-        if (m_new > m_used + 8.f) m_used = m_new;
+      };
 #pragma unroll
-        for (int c = 0; c < 8; ++c) {
-          uint32_t w[8];
-          exp_half(&s[c * 16], c * 16, valid, w, l0, l1);
-          tmem_st8(tS + c * 8, w);
-        }
-        m_used = m_keep;
-        if (!(ok = maybe_rescale(j, m_new))) break;
-      } else {
-        // two TMEM passes (max, then exp); PAIRED reads two chunks per TMEM wait
-        float mx0 = -INFINITY, mx1 = -INFINITY;
-        auto max_chunk = [&](const uint32_t (&r)[32], int c0) {
-          if (valid == BT) {
+      for (int h2 = 0; h2 < 2; ++h2) {
+        uint32_t ra[32], rb[32];
+        tmem_ld32(tS + h2 * 64, ra);
+        tmem_ld32(tS + h2 * 64 + 32, rb);
+        tmem_ld_wait();
+        max_chunk(ra, h2 * 64);
+        max_chunk(rb, h2 * 64 + 32);
+      }
+      const float m_new = fmaxf(m_used, fmaxf(mx0, mx1) * scale_log2);
+      if (!(ok = maybe_rescale(j, m_new))) break;
+      // a chunk's P columns were read as scores in an earlier or the same chunk
 #pragma unroll
-            for (int i = 0; i < 32; i += 4) {
-              if (PACKED) {
-                mx0 = fmax3(mx0, __uint_as_float(r[i]), __uint_as_float(r[i + 1]));
-                mx1 = fmax3(mx1, __uint_as_float(r[i + 2]), __uint_as_float(r[i + 3]));
-              } else {
-                mx0 = fmaxf(fmaxf(mx0, __uint_as_float(r[i])), __uint_as_float(r[i + 1]));
-                mx1 = fmaxf(fmaxf(mx1, __uint_as_float(r[i + 2])), __uint_as_float(r[i + 3]));
-              }
-            }
-          } else {
-#pragma unroll
-            for (int i = 0; i < 32; ++i)
-              if (c0 + i < valid) mx0 = fmaxf(mx0, __uint_as_float(r[i]));
-          }
-        };
-        if (PAIRED) {
-#pragma unroll
-          for (int h2 = 0; h2 < 2; ++h2) {
-            uint32_t ra[32], rb[32];
-            tmem_ld32(tS + h2 * 64, ra);
-            tmem_ld32(tS + h2 * 64 + 32, rb);
-            tmem_ld_wait();
-            max_chunk(ra, h2 * 64);
-            max_chunk(rb, h2 * 64 + 32);
-          }
-        } else {
-#pragma unroll
-          for (int c = 0; c < 4; ++c) {
-            uint32_t r[32];
-            tmem_ld32(tS + c * 32, r);
-            tmem_ld_wait();
-            max_chunk(r, c * 32);
-          }
-        }
-        const float m_new = fmaxf(m_used, fmaxf(mx0, mx1) * scale_log2);
-        if (!(ok = maybe_rescale(j, m_new))) break;
-        // a chunk's P columns were read as scores in an earlier or the same chunk
-        if (PAIRED) {
-#pragma unroll
-          for (int h2 = 0; h2 < 2; ++h2) {
-            uint32_t ra[32], rb[32];
-            tmem_ld32(tS + h2 * 64, ra);
-            tmem_ld32(tS + h2 * 64 + 32, rb);
-            tmem_ld_wait();
-            uint32_t wa[16], wb[16];
-            exp_chunk(ra, h2 * 64, valid, wa, l0, l1);
-            tmem_st16(tS + h2 * 32, wa);
-            exp_chunk(rb, h2 * 64 + 32, valid, wb, l0, l1);
-            tmem_st16(tS + h2 * 32 + 16, wb);
-          }
-        } else {
-#pragma unroll
-          for (int c = 0; c < 4; ++c) {
-            uint32_t r[32];
-            tmem_ld32(tS + c * 32, r);
-            tmem_ld_wait();
-            uint32_t w[16];
-            exp_chunk(r, c * 32, valid, w, l0, l1);
-            tmem_st16(tS + c * 16, w);
-          }
-        }
+      for (int h2 = 0; h2 < 2; ++h2) {
+        uint32_t ra[32], rb[32];
+        tmem_ld32(tS + h2 * 64, ra);
+        tmem_ld32(tS + h2 * 64 + 32, rb);
+        tmem_ld_wait();
+        uint32_t wa[16], wb[16];
+        exp_chunk(ra, h2 * 64, valid, wa, l0, l1);
+        tmem_st16(tS + h2 * 32, wa);
+        exp_chunk(rb, h2 * 64 + 32, valid, wb, l0, l1);
+        tmem_st16(tS + h2 * 32 + 16, wb);
       }
       l += l0 + l1;
       tmem_st_wait();
@@ -547,255 +404,6 @@ attn_fwd_kernel(const __grid_constant__ CUtensorMap qmap, const __grid_constant_
   }
 }
 
-// ============================================================================ backward
-enum { MODE_DQ = 0, MODE_DKV = 1 };
-constexpr int BWD_THREADS = 192;  // warp 0 TMA, warp 1 MMA, warps 2..5 elementwise + epilogue
-constexpr int BWD_SMEM = 2 * TILE_BYTES /*outer*/ + RING * TILE_BYTES + 2 * TILE_BYTES /*P, dS*/ + 1024 + 256 +
-                         2 * BT * 4 /*per-column LSE, Delta*/;
-
-// Outer tile (resident): DQ -> (Q, dO) of a query tile; DKV -> (K, V) of a key tile.
-// Inner tiles (streamed): DQ -> (K_j, V_j); DKV -> (Q_i, dO_i).
-// X = outer0 * inner0^T (S or S^T), Y = outer1 * inner1^T (dP or dP^T).
-template <int MODE>
-__global__ void __launch_bounds__(BWD_THREADS, 1)
-attn_bwd_kernel(const __grid_constant__ CUtensorMap qmap, const __grid_constant__ CUtensorMap kmap,
-                const __grid_constant__ CUtensorMap vmap, const __grid_constant__ CUtensorMap domap,
-                const WorkItem* __restrict__ items, int L, int H, float scale, const float* __restrict__ lse,
-                const float* __restrict__ delta, __nv_bfloat16* __restrict__ out0, __nv_bfloat16* __restrict__ out1) {
-  extern __shared__ uint8_t smem_raw[];
-  uint8_t* smem = reinterpret_cast<uint8_t*>((reinterpret_cast<uintptr_t>(smem_raw) + 1023) & ~uintptr_t(1023));
-  uint8_t* sOuter = smem;                       // 2 tiles
-  uint8_t* sIn = sOuter + 2 * TILE_BYTES;       // RING tiles
-  uint8_t* sP = sIn + RING * TILE_BYTES;        // P (or P^T)
-  uint8_t* sdS = sP + TILE_BYTES;               // dS (or dS^T)
-  uint64_t* bars = reinterpret_cast<uint64_t*>(sdS + TILE_BYTES);
-  // bars: outer_full, in_full[3], in_empty[3], xy_full, p_ready, ds_ready, mma_done
-  uint32_t* tmem_slot = reinterpret_cast<uint32_t*>(bars + 12);
-  // DKV: LSE and Delta of the current query tile (per column)
-  float (*s_vec)[BT] = reinterpret_cast<float (*)[BT]>(reinterpret_cast<uint8_t*>(bars) + 256);
-  volatile int& s_abort = *reinterpret_cast<volatile int*>(bars + 13);
-
-  const WorkItem it = items[blockIdx.x];
-  const int h = blockIdx.y;
-  const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
-  const int n_in = (it.seg_len + BT - 1) / BT;
-  const float scale_log2 = scale * kLog2e;
-
-  const uint32_t outer_full = smem_u32(bars + 0);
-  auto in_full = [&](int s) { return smem_u32(bars + 1 + s); };
-  auto in_empty = [&](int s) { return smem_u32(bars + 4 + s); };
-  const uint32_t xy_full = smem_u32(bars + 7);
-  const uint32_t p_ready = smem_u32(bars + 8);
-  const uint32_t ds_ready = smem_u32(bars + 9);
-  const uint32_t mma_done = smem_u32(bars + 10);
-
-  if (threadIdx.x == 0) {
-    s_abort = 0;
-    mbar_init(outer_full, 1);
-    for (int s = 0; s < RING; ++s) {
-      mbar_init(in_full(s), 1);
-      mbar_init(in_empty(s), 1);
-    }
-    mbar_init(xy_full, 1);
-    mbar_init(p_ready, 4);
-    mbar_init(ds_ready, 4);
-    mbar_init(mma_done, 1);
-    fence_barrier_init();
-  }
-  if (warp == 1) {
-    tmem_alloc(smem_u32(tmem_slot), 512);
-    tmem_relinquish();
-  }
-  tc_fence_before();
-  __syncthreads();
-  tc_fence_after();
-  const uint32_t tmem = *tmem_slot;  // X 0, Y 128, ACC1 256, ACC2 384
-  const int col = h * D;
-  const CUtensorMap* outer_map0 = MODE == MODE_DQ ? &qmap : &kmap;
-  const CUtensorMap* outer_map1 = MODE == MODE_DQ ? &domap : &vmap;
-  const CUtensorMap* in_map0 = MODE == MODE_DQ ? &kmap : &qmap;
-  const CUtensorMap* in_map1 = MODE == MODE_DQ ? &vmap : &domap;
-
-  if (warp == 0) {
-    if (lane == 0) {
-      const int r0 = it.seg_start + it.tile_start;
-      mbar_expect_tx(outer_full, 2 * TILE_BYTES);
-      for (int x = 0; x < 2; ++x) {
-        const uint32_t dst = smem_u32(sOuter + x * TILE_BYTES);
-        const CUtensorMap* m = x == 0 ? outer_map0 : outer_map1;
-        tma_load_2d(dst, m, outer_full, col, r0);
-        tma_load_2d(dst + HALF_BYTES, m, outer_full, col + 64, r0);
-      }
-      int n = 0;
-      for (int j = 0; j < n_in && !s_abort; ++j) {
-        for (int w = 0; w < 2; ++w, ++n) {
-          const int slot = n % RING;
-          if (!mbar_wait(in_empty(slot), ((n / RING) & 1) ^ 1, 31)) { s_abort = 1; break; }
-          const uint32_t fb = in_full(slot);
-          mbar_expect_tx(fb, TILE_BYTES);
-          const uint32_t dst = smem_u32(sIn + slot * TILE_BYTES);
-          const CUtensorMap* m = w == 0 ? in_map0 : in_map1;
-          const int row = it.seg_start + j * BT;
-          tma_load_2d(dst, m, fb, col, row);
-          tma_load_2d(dst + HALF_BYTES, m, fb, col + 64, row);
-        }
-      }
-    }
-  } else if (warp == 1) {
-    if (lane == 0) {
-      const uint32_t id_kk = idesc_bf16_f32(128, 128, 0, 0);  // X, Y: both operands K-major (over D)
-      const uint32_t id_km = idesc_bf16_f32(128, 128, 0, 1);  // acc += P/dS (K-major) * T (MN-major)
-      bool ok = mbar_wait(outer_full, 0, 32);
-      tc_fence_after();
-      const uint32_t o0 = smem_u32(sOuter), o1 = smem_u32(sOuter + TILE_BYTES);
-      const uint32_t pb = smem_u32(sP), db = smem_u32(sdS);
-      int n = 0;
-      for (int j = 0; j < n_in && ok; ++j) {
-        const int s0 = n % RING, s1 = (n + 1) % RING;
-        if (!(ok = mbar_wait(in_full(s0), (n / RING) & 1, 33))) break;
-        if (!(ok = mbar_wait(in_full(s1), ((n + 1) / RING) & 1, 33))) break;
-        tc_fence_after();
-        const uint32_t i0 = smem_u32(sIn + s0 * TILE_BYTES), i1 = smem_u32(sIn + s1 * TILE_BYTES);
-        // previous iteration's accumulate GEMMs must have read P/dS before they are rewritten;
-        // the elementwise warps wait on mma_done before writing, so X/Y may be issued now.
-#pragma unroll
-        for (int kk = 0; kk < D / 16; ++kk) mma_bf16_ss(tmem + 0, desc_kmajor(o0, kk), desc_kmajor(i0, kk), id_kk, kk > 0);
-#pragma unroll
-        for (int kk = 0; kk < D / 16; ++kk) mma_bf16_ss(tmem + 128, desc_kmajor(o1, kk), desc_kmajor(i1, kk), id_kk, kk > 0);
-        mma_commit(xy_full);
-        if (MODE == MODE_DKV) {
-          // dV += P^T dO_i   (dO_i = inner1 as MN-major B)
-          if (!(ok = mbar_wait(p_ready, j & 1, 34))) break;
-          tc_fence_after();
-#pragma unroll
-          for (int kk = 0; kk < BT / 16; ++kk)
-            mma_bf16_ss(tmem + 256, desc_kmajor(pb, kk), desc_mnmajor(i1, kk), id_km, j > 0 || kk > 0);
-        }
-        if (!(ok = mbar_wait(ds_ready, j & 1, 35))) break;
-        tc_fence_after();
-        if (MODE == MODE_DQ) {
-          // dQ += dS K_j   (K_j = inner0 as MN-major B)
-#pragma unroll
-          for (int kk = 0; kk < BT / 16; ++kk)
-            mma_bf16_ss(tmem + 256, desc_kmajor(db, kk), desc_mnmajor(i0, kk), id_km, j > 0 || kk > 0);
-        } else {
-          // dK += dS^T Q_i  (Q_i = inner0 as MN-major B)
-#pragma unroll
-          for (int kk = 0; kk < BT / 16; ++kk)
-            mma_bf16_ss(tmem + 384, desc_kmajor(db, kk), desc_mnmajor(i0, kk), id_km, j > 0 || kk > 0);
-        }
-        mma_commit(mma_done);
-        mma_commit(in_empty(s0));
-        mma_commit(in_empty(s1));
-        n += 2;
-      }
-      if (!ok) s_abort = 1;
-    }
-  } else {
-    // ------------------------------------------------------------ elementwise + epilogue
-    const int quarter = warp & 3;
-    const int row = quarter * 32 + lane;  // row of the outer tile
-    const uint32_t lane_off = (uint32_t)(quarter * 32) << 16;
-    const int orow = it.tile_start + row;  // row within the segment
-    const bool row_valid = orow < it.seg_len;
-    float row_lse = 0.f, row_delta = 0.f;
-    if (MODE == MODE_DQ && row_valid) {
-      row_lse = lse[(size_t)h * L + it.seg_start + orow] * kLog2e;
-      row_delta = delta[(size_t)h * L + it.seg_start + orow];
-    }
-    const int tid = threadIdx.x - 64;
-    bool ok = true;
-    for (int j = 0; j < n_in; ++j) {
-      const int valid_cols = min(BT, it.seg_len - j * BT);
-      if (MODE == MODE_DKV) {
-        // per-column (query) LSE and Delta of inner tile j; previous readers are done once
-        // mma_done(j-1) has been observed below
-        if (j > 0) {
-          if (!(ok = mbar_wait(mma_done, (j - 1) & 1, 36))) break;
-        }
-        asm volatile("bar.sync 1, 128;" ::: "memory");
-        if (tid < BT) {
-          const int qi = j * BT + tid;
-          s_vec[0][tid] = qi < it.seg_len ? lse[(size_t)h * L + it.seg_start + qi] * kLog2e : 0.f;
-          s_vec[1][tid] = qi < it.seg_len ? delta[(size_t)h * L + it.seg_start + qi] : 0.f;
-        }
-        asm volatile("bar.sync 1, 128;" ::: "memory");
-      } else if (j > 0) {
-        if (!(ok = mbar_wait(mma_done, (j - 1) & 1, 36))) break;
-      }
-      if (!(ok = mbar_wait(xy_full, j & 1, 37))) break;
-      tc_fence_after();
-      // P = exp2(X * scale*log2e - lse*log2e); masked columns / rows -> 0
-#pragma unroll
-      for (int c = 0; c < 4; ++c) {
-        uint32_t r[32], y[32];
-        tmem_ld32(tmem + lane_off + c * 32, r);
-        tmem_ld32(tmem + 128 + lane_off + c * 32, y);
-        tmem_ld_wait();
-        uint32_t wp[16], wd[16];
-#pragma unroll
-        for (int i = 0; i < 32; i += 2) {
-          float pv[2], dsv[2];
-#pragma unroll
-          for (int e = 0; e < 2; ++e) {
-            const int cc = c * 32 + i + e;
-            const bool ok_col = cc < valid_cols && row_valid;
-            const float lse2 = MODE == MODE_DQ ? row_lse : s_vec[0][cc];
-            const float dl = MODE == MODE_DQ ? row_delta : s_vec[1][cc];
-            const float p = ok_col ? exp2f(__uint_as_float(r[i + e]) * scale_log2 - lse2) : 0.f;
-            pv[e] = p;
-            dsv[e] = p * (__uint_as_float(y[i + e]) - dl);
-          }
-          wp[i >> 1] = pack_bf16(pv[0], pv[1]);
-          wd[i >> 1] = pack_bf16(dsv[0], dsv[1]);
-        }
-        if (MODE == MODE_DKV) store_row32_swizzled(sP, row, c * 32, wp);
-        store_row32_swizzled(sdS, row, c * 32, wd);
-      }
-      fence_async_smem();
-      tc_fence_before();
-      __syncwarp();
-      if (lane == 0) {
-        if (MODE == MODE_DKV) mbar_arrive(p_ready);
-        mbar_arrive(ds_ready);
-      }
-    }
-    if (ok && n_in > 0 && mbar_wait(mma_done, (n_in - 1) & 1, 38)) {
-      tc_fence_after();
-      const size_t grow = (size_t)(it.seg_start + orow) * H + h;
-      // DQ: out0 = dQ * scale.  DKV: out0 = dK * scale (ACC2), out1 = dV (ACC1).
-      for (int which = 0; which < (MODE == MODE_DQ ? 1 : 2); ++which) {
-        const uint32_t tacc = tmem + (MODE == MODE_DQ ? 256 : (which == 0 ? 384 : 256)) + lane_off;
-        const float mul = (which == 0) ? scale : 1.f;
-        __nv_bfloat16* dst = (which == 0 ? out0 : out1) + grow * D;
-#pragma unroll
-        for (int c = 0; c < 4; ++c) {
-          uint32_t r[32];
-          tmem_ld32(tacc + c * 32, r);
-          tmem_ld_wait();
-          if (row_valid) {
-#pragma unroll
-            for (int v = 0; v < 4; ++v) {
-              float o[8];
-#pragma unroll
-              for (int i = 0; i < 8; ++i) o[i] = __uint_as_float(r[v * 8 + i]) * mul;
-              store8(dst + c * 32 + v * 8, o);
-            }
-          }
-        }
-      }
-    } else {
-      s_abort = 1;
-    }
-  }
-  tc_fence_before();
-  __syncthreads();
-  if (warp == 1) {
-    tc_fence_after();
-    tmem_dealloc(tmem, 512);
-  }
-}
-
 // ============================================================================ fused backward
 // One pass, key tiles outer (one CTA = one head x 128 keys of one segment), query tiles inner:
 //   S^T  = K Q_i^T,  dP^T = V dO_i^T                        (tcgen05, operands in smem)
@@ -812,13 +420,6 @@ constexpr int FB_STAGE = 32 * D * 4;  // 32 query rows of fp32 dQ
 constexpr int FB_SMEM = 2 * TILE_BYTES /*K, V*/ + 2 * TILE_BYTES /*Q ring*/ + TILE_BYTES /*dO*/ +
                         TILE_BYTES /*dS^T*/ + 2 * FB_STAGE + 1024 + 256 + 2 * BT * 4;
 
-// SCHED 0: dQ^T goes into the S^T columns, so the MMA thread waits for dV / dK to complete before
-// issuing it, and the next S^T waits for the dQ^T drain.  SCHED 1: dQ^T goes into the dP^T
-// columns and dK reads dS^T from shared memory; after the elementwise hand-off the MMA thread
-// issues dQ^T, dV, dK and the next S^T back to back (one thread's MMAs execute in order, so S^T(i+1)
-// cannot overwrite P^T(i) before dV(i) has read it), and only dP^T(i+1) waits for the dQ^T(i)
-// drain, which runs while dV / dK / S^T execute.  The elementwise warps use packed f32x2 math.
-template <int SCHED>
 __global__ void __launch_bounds__(FB_THREADS, 1)
 attn_bwd_fused_kernel(const __grid_constant__ CUtensorMap qmap, const __grid_constant__ CUtensorMap kmap,
                       const __grid_constant__ CUtensorMap vmap, const __grid_constant__ CUtensorMap domap,
@@ -891,7 +492,6 @@ attn_bwd_fused_kernel(const __grid_constant__ CUtensorMap qmap, const __grid_con
       const uint32_t id_kk = idesc_bf16_f32(128, 128, 0, 0);  // S^T, dP^T: both K-major over D
       const uint32_t id_tm = idesc_bf16_f32(128, 128, 0, 1);  // dV, dK: A from TMEM, B MN-major
       const uint32_t id_mm = idesc_bf16_f32(128, 128, 1, 1);  // dQ^T: A = K^T, B = dS^T, both MN-major
-      const uint32_t id_sm = idesc_bf16_f32(128, 128, 0, 1);  // dK (SCHED 1): A = dS^T K-major, B = Q MN-major
       const uint32_t k = smem_u32(sK), v = smem_u32(sV), dO = smem_u32(sdO), dS = smem_u32(sdS);
       bool ok = mbar_wait(B(0), 0, 43);
       for (int i = 0; i < n_q && ok; ++i) {
@@ -899,38 +499,15 @@ attn_bwd_fused_kernel(const __grid_constant__ CUtensorMap qmap, const __grid_con
         const uint32_t q = smem_u32(sQ + slot * TILE_BYTES);
         if (!(ok = mbar_wait(B(1 + slot), (i >> 1) & 1, 44))) break;
         if (!(ok = mbar_wait(B(5), i & 1, 45))) break;
-        if (SCHED == 0 && i > 0 && !(ok = mbar_wait(B(12), (i - 1) & 1, 46))) break;  // dQ^T(i-1) drained
+        if (i > 0 && !(ok = mbar_wait(B(12), (i - 1) & 1, 46))) break;  // dQ^T(i-1) drained
         tc_fence_after();
 #pragma unroll
         for (int kk = 0; kk < D / 16; ++kk) mma_bf16_ss(T_S, desc_kmajor(k, kk), desc_kmajor(q, kk), id_kk, kk > 0);
-        if (SCHED == 1) {
-          if (i > 0 && !(ok = mbar_wait(B(12), (i - 1) & 1, 46))) break;  // dQ^T(i-1) drained from T_DP
-          tc_fence_after();
-        }
 #pragma unroll
         for (int kk = 0; kk < D / 16; ++kk) mma_bf16_ss(T_DP, desc_kmajor(v, kk), desc_kmajor(dO, kk), id_kk, kk > 0);
         mma_commit(B(7));
-        if (!(ok = mbar_wait(B(8), i & 1, 47))) break;  // P^T in TMEM and dS^T in smem
+        if (!(ok = mbar_wait(B(8), i & 1, 47))) break;  // P^T, dS^T in TMEM and dS^T in smem
         tc_fence_after();
-        if (SCHED == 1) {
-          // dQ_i^T = K^T dS^T into the dP^T columns (the elementwise warps read them before B(8))
-#pragma unroll
-          for (int kk = 0; kk < BT / 16; ++kk)
-            mma_bf16_ss(T_DP, desc_mnmajor(k, kk), desc_mnmajor(dS, kk), id_mm, kk > 0);
-          mma_commit(B(11));
-          // dV += P^T dO_i (A from TMEM)
-#pragma unroll
-          for (int kk = 0; kk < BT / 16; ++kk)
-            mma_bf16_ts(T_DV, T_S + kk * 8, desc_mnmajor(dO, kk), id_tm, (i > 0) || (kk > 0));
-          mma_commit(B(6));  // dO slot free
-          // dK += dS^T Q_i (A = dS^T from smem, K-major over queries)
-#pragma unroll
-          for (int kk = 0; kk < BT / 16; ++kk)
-            mma_bf16_ss(T_DK, desc_kmajor(dS, kk), desc_mnmajor(q, kk), id_sm, (i > 0) || (kk > 0));
-          mma_commit(B(3 + slot));  // Q slot free
-          mma_commit(B(9));         // dS^T smem free
-          continue;
-        }
         // dV += P^T dO_i ; dK += dS^T Q_i  (K = 128 queries, 8 columns of packed bf16 per step)
 #pragma unroll
         for (int kk = 0; kk < BT / 16; ++kk)
@@ -980,37 +557,6 @@ attn_bwd_fused_kernel(const __grid_constant__ CUtensorMap qmap, const __grid_con
       if (!(ok = mbar_wait(B(7), i & 1, 49))) break;
       if (i > 0 && !(ok = mbar_wait(B(9), (i - 1) & 1, 50))) break;  // dQ^T(i-1) has read dS^T smem
       tc_fence_after();
-      if (SCHED == 1) {
-        // P^T back into TMEM (the dV operand), dS^T to smem only; packed f32x2 math
-#pragma unroll
-        for (int c = 0; c < 4; ++c) {
-          uint32_t r[32], y[32];
-          tmem_ld32(T_S + lane_off + c * 32, r);
-          tmem_ld32(T_DP + lane_off + c * 32, y);
-          tmem_ld_wait();
-          uint32_t wp[16], wd[16];
-#pragma unroll
-          for (int j = 0; j < 32; j += 2) {
-            const int cc = c * 32 + j;
-            float x0, x1, p0, p1, t0, t1, d0, d1;
-            ffma2(x0, x1, __uint_as_float(r[j]), __uint_as_float(r[j + 1]), scale_log2, scale_log2, -s_vec[0][cc],
-                  -s_vec[0][cc + 1]);
-            p0 = fast_exp2(x0);
-            p1 = fast_exp2(x1);
-            if (valid_q < BT || !row_valid) {
-              p0 = (cc < valid_q && row_valid) ? p0 : 0.f;
-              p1 = (cc + 1 < valid_q && row_valid) ? p1 : 0.f;
-            }
-            fadd2(t0, t1, __uint_as_float(y[j]), __uint_as_float(y[j + 1]), -s_vec[1][cc], -s_vec[1][cc + 1]);
-            fmul2(d0, d1, p0, p1, t0, t1);
-            wp[j >> 1] = pack_bf16(p0, p1);
-            wd[j >> 1] = pack_bf16(d0, d1);
-          }
-          // columns [16c, 16c + 16) were read in chunk c or earlier
-          tmem_st16(T_S + lane_off + c * 16, wp);
-          store_row32_swizzled(sdS, row, c * 32, wd);
-        }
-      } else {
 #pragma unroll
       for (int c = 0; c < 4; ++c) {
         uint32_t r[32], y[32];
@@ -1036,7 +582,6 @@ attn_bwd_fused_kernel(const __grid_constant__ CUtensorMap qmap, const __grid_con
         tmem_st16(T_S + lane_off + c * 16, wp);
         tmem_st16(T_DP + lane_off + c * 16, wd);
         store_row32_swizzled(sdS, row, c * 32, wd);
-      }
       }
       tmem_st_wait();
       fence_async_smem();
@@ -1086,7 +631,7 @@ attn_bwd_fused_kernel(const __grid_constant__ CUtensorMap qmap, const __grid_con
       tc_fence_after();
       uint32_t r[4][32];
 #pragma unroll
-      for (int c = 0; c < 4; ++c) tmem_ld32((SCHED == 1 ? T_DP : T_S) + lane_off + c * 32, r[c]);
+      for (int c = 0; c < 4; ++c) tmem_ld32(T_S + lane_off + c * 32, r[c]);
       tmem_ld_wait();
       tc_fence_before();
       __syncwarp();
@@ -1102,310 +647,6 @@ attn_bwd_fused_kernel(const __grid_constant__ CUtensorMap qmap, const __grid_con
         asm volatile("bar.sync 2, 128;" ::: "memory");
         if (qt == 0) {
           tma_reduce_add_2d(&dqmap, smem_u32(st), col, it.seg_start + i * BT + c * 32);
-          bulk_commit();
-        }
-        ++n_used;
-      }
-    }
-    if (qt == 0) bulk_wait_all();
-  }
-  tc_fence_before();
-  __syncthreads();
-  if (warp == 1) {
-    tc_fence_after();
-    tmem_dealloc(tmem, 512);
-  }
-}
-
-// ---------------------------------------------------------------------------------------------
-// Pipelined fused backward.  Same recurrences as attn_bwd_fused_kernel, but each key tile walks
-// 64-query sub-tiles with TWO TMEM buffer sets, so the tensor core works on one sub-tile while the
-// elementwise warps and the dQ drain work on the other:
-//   buffer b (128 columns): S^T (64 cols; later P^T in its first 32, later dQ^T in all 64) and
-//                           dP^T (64 cols; later dS^T in its first 32);  dV, dK: 256 columns.
-// The MMA thread schedules from readiness instead of a fixed order: it issues a sub-tile's
-// S^T / dP^T as soon as a buffer is free (its previous dQ^T drained) and its Q / dO are loaded, and
-// a sub-tile's dV / dK / dQ^T as soon as its P^T / dS^T are written.  Q and dO sub-tiles arrive
-// through a 3-slot ring.  Barriers (index): kv_full 0, slot_full 1-3, slot_empty 4-6, s_full 7-8,
-// ds_ready 9-10, pv_done 11-12, dq_full 13-14, dq_drained 15-16, dsm_free 17-18, all_done 19.
-constexpr int BQ = 64;                          // queries per sub-tile
-constexpr int SUB_BYTES = BQ * D * 2;           // 16 KB: two [64 x 64] swizzled halves
-constexpr int SUB_HALF = SUB_BYTES / 2;
-constexpr int PB_SLOTS = 3;
-constexpr int PB_DS = BT * BQ * 2;              // dS^T [128 keys][64 queries] bf16
-constexpr int PB_STAGE = 32 * D * 4;            // 32 query rows of fp32 dQ
-constexpr int PB_SMEM = 2 * TILE_BYTES + PB_SLOTS * 2 * SUB_BYTES + 2 * PB_DS + 2 * PB_STAGE + 1024 + 256 +
-                        2 * BQ * 4;
-
-// K-major descriptor of a [64 rows, 128 cols] sub-tile at k-step kk (two 8 KB halves)
-__device__ __forceinline__ uint64_t desc_kmajor64(uint32_t base, int kk) {
-  return smem_desc_sw128(base + (kk >> 2) * SUB_HALF + (kk & 3) * 32, 16, 1024);
-}
-// the same sub-tile as an MN-major operand whose reduction dim is its 64 rows
-__device__ __forceinline__ uint64_t desc_mnmajor64(uint32_t base, int kk) {
-  return smem_desc_sw128(base + kk * 2048, SUB_HALF, 1024);
-}
-
-__global__ void __launch_bounds__(FB_THREADS, 1)
-attn_bwd_pipe_kernel(const __grid_constant__ CUtensorMap qmap, const __grid_constant__ CUtensorMap kmap,
-                     const __grid_constant__ CUtensorMap vmap, const __grid_constant__ CUtensorMap domap,
-                     const __grid_constant__ CUtensorMap dqmap, const WorkItem* __restrict__ items, int L, int H,
-                     float scale, const float* __restrict__ lse, const float* __restrict__ delta,
-                     __nv_bfloat16* __restrict__ dk_out, __nv_bfloat16* __restrict__ dv_out, const PeerRows dk_peer,
-                     const PeerRows dv_peer) {
-  extern __shared__ uint8_t smem_raw[];
-  uint8_t* smem = reinterpret_cast<uint8_t*>((reinterpret_cast<uintptr_t>(smem_raw) + 1023) & ~uintptr_t(1023));
-  uint8_t* sK = smem;
-  uint8_t* sV = sK + TILE_BYTES;
-  uint8_t* sQ = sV + TILE_BYTES;                 // PB_SLOTS sub-tiles
-  uint8_t* sdO = sQ + PB_SLOTS * SUB_BYTES;      // PB_SLOTS sub-tiles
-  uint8_t* sdS = sdO + PB_SLOTS * SUB_BYTES;     // 2 x dS^T
-  uint8_t* sStage = sdS + 2 * PB_DS;             // 2 x [32 q][128 d] fp32
-  uint64_t* bars = reinterpret_cast<uint64_t*>(sStage + 2 * PB_STAGE);
-  uint32_t* tmem_slot = reinterpret_cast<uint32_t*>(bars + 20);
-  volatile int& s_abort = *reinterpret_cast<volatile int*>(bars + 21);
-  float (*s_vec)[BQ] = reinterpret_cast<float (*)[BQ]>(reinterpret_cast<uint8_t*>(bars) + 256);
-
-  const WorkItem it = items[blockIdx.x];
-  const int h = blockIdx.y;
-  const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
-  const int n_q = (it.seg_len + BQ - 1) / BQ;
-  const float scale_log2 = scale * kLog2e;
-  auto B = [&](int i) { return smem_u32(bars + i); };
-  auto slot_full = [&](int s) { return B(1 + s); };
-  auto slot_empty = [&](int s) { return B(4 + s); };
-  auto s_full = [&](int b) { return B(7 + b); };
-  auto ds_ready = [&](int b) { return B(9 + b); };
-  auto pv_done = [&](int b) { return B(11 + b); };
-  auto dq_full = [&](int b) { return B(13 + b); };
-  auto dq_drained = [&](int b) { return B(15 + b); };
-  auto dsm_free = [&](int b) { return B(17 + b); };
-
-  if (threadIdx.x == 0) {
-    s_abort = 0;
-    for (int i = 0; i < 20; ++i) {
-      const bool four = (i == 9 || i == 10 || i == 15 || i == 16);  // arrivals of 4 warps
-      mbar_init(B(i), four ? 4 : 1);
-    }
-    fence_barrier_init();
-  }
-  if (warp == 1) {
-    tmem_alloc(smem_u32(tmem_slot), 512);
-    tmem_relinquish();
-  }
-  tc_fence_before();
-  __syncthreads();
-  tc_fence_after();
-  const uint32_t tmem = *tmem_slot;
-  auto T_S = [&](int b) { return tmem + b * 128; };
-  auto T_DP = [&](int b) { return tmem + b * 128 + 64; };
-  const uint32_t T_DV = tmem + 256, T_DK = tmem + 384;
-  const int col = h * D;
-
-  if (warp == 0) {
-    if (lane == 0) {
-      const int r0 = it.seg_start + it.tile_start;
-      mbar_expect_tx(B(0), 2 * TILE_BYTES);
-      tma_load_2d(smem_u32(sK), &kmap, B(0), col, r0);
-      tma_load_2d(smem_u32(sK) + HALF_BYTES, &kmap, B(0), col + 64, r0);
-      tma_load_2d(smem_u32(sV), &vmap, B(0), col, r0);
-      tma_load_2d(smem_u32(sV) + HALF_BYTES, &vmap, B(0), col + 64, r0);
-      for (int j = 0; j < n_q && !s_abort; ++j) {
-        const int sl = j % PB_SLOTS;
-        const int row = it.seg_start + j * BQ;
-        if (!mbar_wait(slot_empty(sl), ((j / PB_SLOTS) & 1) ^ 1, 61)) { s_abort = 1; break; }
-        mbar_expect_tx(slot_full(sl), 2 * SUB_BYTES);
-        const uint32_t q = smem_u32(sQ + sl * SUB_BYTES), o = smem_u32(sdO + sl * SUB_BYTES);
-        tma_load_2d(q, &qmap, slot_full(sl), col, row);
-        tma_load_2d(q + SUB_HALF, &qmap, slot_full(sl), col + 64, row);
-        tma_load_2d(o, &domap, slot_full(sl), col, row);
-        tma_load_2d(o + SUB_HALF, &domap, slot_full(sl), col + 64, row);
-      }
-    }
-  } else if (warp == 1) {
-    if (lane == 0) {
-      const uint32_t id_kk = idesc_bf16_f32(128, BQ, 0, 0);   // S^T, dP^T: K-major over D
-      const uint32_t id_tm = idesc_bf16_f32(128, 128, 0, 1);  // dV, dK: A from TMEM, B MN-major
-      const uint32_t id_mm = idesc_bf16_f32(128, BQ, 1, 1);   // dQ^T: A = K^T, B = dS^T, both MN-major
-      const uint32_t k = smem_u32(sK), v = smem_u32(sV);
-      bool ok = mbar_wait(B(0), 0, 62);
-      int ns = 0, ng = 0;  // next sub-tile for S^T / dP^T, next for the gradients
-      uint64_t t_last = global_timer_ns();
-      while (ok && ng < n_q) {
-        bool progress = false;
-        if (ns < n_q && ns - ng < 2) {
-          const int b = ns & 1, sl = ns % PB_SLOTS;
-          if ((ns < 2 || mbar_try_wait(dq_drained(b), ((ns - 2) >> 1) & 1)) &&
-              mbar_try_wait(slot_full(sl), (ns / PB_SLOTS) & 1)) {
-            tc_fence_after();
-            const uint32_t q = smem_u32(sQ + sl * SUB_BYTES), o = smem_u32(sdO + sl * SUB_BYTES);
-#pragma unroll
-            for (int kk = 0; kk < D / 16; ++kk)
-              mma_bf16_ss(T_S(b), desc_kmajor(k, kk), desc_kmajor64(q, kk), id_kk, kk > 0);
-#pragma unroll
-            for (int kk = 0; kk < D / 16; ++kk)
-              mma_bf16_ss(T_DP(b), desc_kmajor(v, kk), desc_kmajor64(o, kk), id_kk, kk > 0);
-            mma_commit(s_full(b));
-            ++ns;
-            progress = true;
-          }
-        }
-        if (!progress && ng < ns && mbar_try_wait(ds_ready(ng & 1), (ng >> 1) & 1)) {
-          const int b = ng & 1, sl = ng % PB_SLOTS;
-          tc_fence_after();
-          const uint32_t q = smem_u32(sQ + sl * SUB_BYTES), o = smem_u32(sdO + sl * SUB_BYTES);
-          // dV += P^T dO ; dK += dS^T Q  (K = 64 queries)
-#pragma unroll
-          for (int kk = 0; kk < BQ / 16; ++kk)
-            mma_bf16_ts(T_DV, T_S(b) + kk * 8, desc_mnmajor64(o, kk), id_tm, (ng > 0) || (kk > 0));
-#pragma unroll
-          for (int kk = 0; kk < BQ / 16; ++kk)
-            mma_bf16_ts(T_DK, T_DP(b) + kk * 8, desc_mnmajor64(q, kk), id_tm, (ng > 0) || (kk > 0));
-          mma_commit(slot_empty(sl));
-          mma_commit(pv_done(b));
-          // dQ^T overwrites the columns P^T is read from: wait until dV has consumed them
-          if (!(ok = mbar_wait(pv_done(b), (ng >> 1) & 1, 63))) break;
-          tc_fence_after();
-          const uint32_t ds = smem_u32(sdS + b * PB_DS);
-#pragma unroll
-          for (int kk = 0; kk < BT / 16; ++kk)
-            mma_bf16_ss(T_S(b), desc_mnmajor(k, kk), smem_desc_sw128(ds + kk * 2048, SUB_HALF, 1024), id_mm, kk > 0);
-          mma_commit(dq_full(b));
-          mma_commit(dsm_free(b));
-          ++ng;
-          progress = true;
-        }
-        if (progress) {
-          t_last = global_timer_ns();
-        } else if (global_timer_ns() - t_last > 4000000000ull) {
-          atomicCAS(&g_error_flag, 0, 64);
-          ok = false;
-        }
-      }
-      mma_commit(B(19));
-      if (!ok) s_abort = 1;
-    }
-  } else if (warp < 6) {
-    // ------------------------------------------------ E warps: P^T and dS^T (lane = key row)
-    const int quarter = warp & 3;
-    const int row = quarter * 32 + lane;
-    const uint32_t lane_off = (uint32_t)(quarter * 32) << 16;
-    const bool row_valid = it.tile_start + row < it.seg_len;
-    const int tid = threadIdx.x - 64;
-    bool ok = true;
-    auto fetch = [&](int i, float& lv, float& dv) {  // one sub-tile ahead, as in the fused kernel
-      const int qi = i * BQ + tid;
-      const bool in = tid < BQ && i < n_q && qi < it.seg_len;
-      lv = in ? lse[(size_t)h * L + it.seg_start + qi] * kLog2e : 0.f;
-      dv = in ? delta[(size_t)h * L + it.seg_start + qi] : 0.f;
-    };
-    float next_l, next_d;
-    fetch(0, next_l, next_d);
-    for (int i = 0; i < n_q; ++i) {
-      const int b = i & 1;
-      const int valid_q = min(BQ, it.seg_len - i * BQ);
-      asm volatile("bar.sync 1, 128;" ::: "memory");
-      if (tid < BQ) {
-        s_vec[0][tid] = next_l;
-        s_vec[1][tid] = next_d;
-      }
-      asm volatile("bar.sync 1, 128;" ::: "memory");
-      fetch(i + 1, next_l, next_d);
-      if (!(ok = mbar_wait(s_full(b), (i >> 1) & 1, 65))) break;
-      if (i >= 2 && !(ok = mbar_wait(dsm_free(b), ((i - 2) >> 1) & 1, 66))) break;  // dQ^T(i-2) read sdS[b]
-      tc_fence_after();
-      uint8_t* dsb = sdS + b * PB_DS;
-#pragma unroll
-      for (int c = 0; c < 2; ++c) {
-        uint32_t r[32], y[32];
-        tmem_ld32(T_S(b) + lane_off + c * 32, r);
-        tmem_ld32(T_DP(b) + lane_off + c * 32, y);
-        tmem_ld_wait();
-        uint32_t wp[16], wd[16];
-#pragma unroll
-        for (int j = 0; j < 32; j += 2) {
-          float pv[2], dsv[2];
-#pragma unroll
-          for (int e = 0; e < 2; ++e) {
-            const int cc = c * 32 + j + e;
-            const bool on = cc < valid_q && row_valid;
-            const float p = on ? fast_exp2(__uint_as_float(r[j + e]) * scale_log2 - s_vec[0][cc]) : 0.f;
-            pv[e] = p;
-            dsv[e] = p * (__uint_as_float(y[j + e]) - s_vec[1][cc]);
-          }
-          wp[j >> 1] = pack_bf16(pv[0], pv[1]);
-          wd[j >> 1] = pack_bf16(dsv[0], dsv[1]);
-        }
-        // packed columns [16c, 16c + 16) lie in score columns already read
-        tmem_st16(T_S(b) + lane_off + c * 16, wp);
-        tmem_st16(T_DP(b) + lane_off + c * 16, wd);
-        store_row32_swizzled(dsb, row, c * 32, wd);
-      }
-      tmem_st_wait();
-      fence_async_smem();
-      tc_fence_before();
-      __syncwarp();
-      if (lane == 0) mbar_arrive(ds_ready(b));
-    }
-    // dV, dK rows of this key tile
-    if (ok && n_q > 0 && mbar_wait(B(19), 0, 67)) {
-      tc_fence_after();
-      const int g = it.seg_start + it.tile_start + row;
-      const size_t grow = (size_t)g * H + h;
-      for (int which = 0; which < 2; ++which) {
-        const uint32_t tacc = (which == 0 ? T_DK : T_DV) + lane_off;
-        const float mul = which == 0 ? scale : 1.f;
-        const PeerRows& pr = which == 0 ? dk_peer : dv_peer;
-        __nv_bfloat16* dst = pr.base ? (row_valid ? peer_row(pr, g, h) : nullptr)
-                                     : (which == 0 ? dk_out : dv_out) + grow * D;
-#pragma unroll
-        for (int c = 0; c < 4; ++c) {
-          uint32_t r[32];
-          tmem_ld32(tacc + c * 32, r);
-          tmem_ld_wait();
-          if (row_valid) {
-#pragma unroll
-            for (int vv = 0; vv < 4; ++vv) {
-              float o[8];
-#pragma unroll
-              for (int e = 0; e < 8; ++e) o[e] = __uint_as_float(r[vv * 8 + e]) * mul;
-              store8(dst + c * 32 + vv * 8, o);
-            }
-          }
-        }
-      }
-    } else {
-      s_abort = 1;
-    }
-  } else {
-    // ------------------------------------------------ Q warps: dQ^T -> fp32 reduce-add (lane = d)
-    const int quarter = warp & 3;
-    const int d = quarter * 32 + lane;
-    const uint32_t lane_off = (uint32_t)(quarter * 32) << 16;
-    const int qt = threadIdx.x - 192;  // 0..127
-    int n_used = 0;
-    for (int i = 0; i < n_q; ++i) {
-      const int b = i & 1;
-      if (!mbar_wait(dq_full(b), (i >> 1) & 1, 68)) { s_abort = 1; break; }
-      tc_fence_after();
-      uint32_t r[2][32];
-#pragma unroll
-      for (int c = 0; c < 2; ++c) tmem_ld32(T_S(b) + lane_off + c * 32, r[c]);
-      tmem_ld_wait();
-      tc_fence_before();
-      __syncwarp();
-      if (lane == 0) mbar_arrive(dq_drained(b));  // buffer b may be reused
-#pragma unroll
-      for (int c = 0; c < 2; ++c) {
-        float* st = reinterpret_cast<float*>(sStage + (n_used & 1) * PB_STAGE);
-        if (n_used >= 2 && qt == 0) bulk_wait_read<1>();
-        asm volatile("bar.sync 2, 128;" ::: "memory");
-#pragma unroll
-        for (int qq = 0; qq < 32; ++qq) st[qq * D + d] = __uint_as_float(r[c][qq]);
-        fence_async_shared();
-        asm volatile("bar.sync 2, 128;" ::: "memory");
-        if (qt == 0) {
-          tma_reduce_add_2d(&dqmap, smem_u32(st), col, it.seg_start + i * BQ + c * 32);
           bulk_commit();
         }
         ++n_used;
@@ -1532,63 +773,38 @@ const char* make_dq_map(CUtensorMap* m, const float* base, int L, int H) {
   return r == CUDA_SUCCESS ? nullptr : "cuTensorMapEncodeTiled failed (dq accumulator)";
 }
 
-// Key-tile-outer backward (fused or pipelined, per g_bwd_variant) into dq_acc / dk / dv.
-int g_bwd_variant = 1;  // 3: fused, reordered schedule; 2: pipelined single pass; 1: fused; 0: two passes
-
+// Key-tile-outer fused backward into dq_acc / dk / dv.
 const char* run_bwd_single_pass(const void* q, const void* k, const void* v, const void* dout, const float* lse,
                                 const float* delta, const int* items_kv, int n_items_kv, int L, int H, float scale,
                                 float* dq_acc, __nv_bfloat16* dk, __nv_bfloat16* dv, const PeerRows& dk_peer,
                                 const PeerRows& dv_peer, cudaStream_t s) {
-  const bool pipe = g_bwd_variant == 2;
-  const int qrows = pipe ? BQ : BT;
   CUtensorMap qm, km, vm, dom, dqm;
   const char* e;
-  if ((e = make_qkv_map(&qm, q, L, H, qrows)) || (e = make_qkv_map(&km, k, L, H)) || (e = make_qkv_map(&vm, v, L, H)) ||
-      (e = make_qkv_map(&dom, dout, L, H, qrows)) || (e = make_dq_map(&dqm, dq_acc, L, H)))
+  if ((e = make_qkv_map(&qm, q, L, H)) || (e = make_qkv_map(&km, k, L, H)) || (e = make_qkv_map(&vm, v, L, H)) ||
+      (e = make_qkv_map(&dom, dout, L, H)) || (e = make_dq_map(&dqm, dq_acc, L, H)))
     return e;
-  static bool attr_f = false, attr_p = false;
-  if (!pipe && !attr_f) {
-    if (cudaFuncSetAttribute(attn_bwd_fused_kernel<0>, cudaFuncAttributeMaxDynamicSharedMemorySize, FB_SMEM) !=
-            cudaSuccess ||
-        cudaFuncSetAttribute(attn_bwd_fused_kernel<1>, cudaFuncAttributeMaxDynamicSharedMemorySize, FB_SMEM) !=
-            cudaSuccess)
-      return "attention: cannot set smem size (fused backward)";
-    attr_f = true;
-  }
-  if (pipe && !attr_p) {
-    if (cudaFuncSetAttribute(attn_bwd_pipe_kernel, cudaFuncAttributeMaxDynamicSharedMemorySize, PB_SMEM) !=
+  static bool attr = false;
+  if (!attr) {
+    if (cudaFuncSetAttribute(attn_bwd_fused_kernel, cudaFuncAttributeMaxDynamicSharedMemorySize, FB_SMEM) !=
         cudaSuccess)
-      return "attention: cannot set smem size (pipelined backward)";
-    attr_p = true;
+      return "attention: cannot set smem size (fused backward)";
+    attr = true;
   }
   if (cudaMemsetAsync(dq_acc, 0, (size_t)L * H * D * sizeof(float), s) != cudaSuccess) return "dq memset failed";
-  if (n_items_kv > 0) {
-    const WorkItem* it = reinterpret_cast<const WorkItem*>(items_kv);
-    if (pipe)
-      attn_bwd_pipe_kernel<<<dim3(n_items_kv, H), FB_THREADS, PB_SMEM, s>>>(qm, km, vm, dom, dqm, it, L, H, scale, lse,
-                                                                           delta, dk, dv, dk_peer, dv_peer);
-    else if (g_bwd_variant == 3)
-      attn_bwd_fused_kernel<1><<<dim3(n_items_kv, H), FB_THREADS, FB_SMEM, s>>>(qm, km, vm, dom, dqm, it, L, H, scale,
-                                                                               lse, delta, dk, dv, dk_peer, dv_peer);
-    else
-      attn_bwd_fused_kernel<0><<<dim3(n_items_kv, H), FB_THREADS, FB_SMEM, s>>>(qm, km, vm, dom, dqm, it, L, H, scale,
-                                                                               lse, delta, dk, dv, dk_peer, dv_peer);
-  }
-  return cudaGetLastError() == cudaSuccess ? nullptr : "attention single-pass backward launch failed";
+  if (n_items_kv > 0)
+    attn_bwd_fused_kernel<<<dim3(n_items_kv, H), FB_THREADS, FB_SMEM, s>>>(
+        qm, km, vm, dom, dqm, reinterpret_cast<const WorkItem*>(items_kv), L, H, scale, lse, delta, dk, dv, dk_peer,
+        dv_peer);
+  return cudaGetLastError() == cudaSuccess ? nullptr : "attention backward launch failed";
 }
-// Forward kernel variant (index into the launcher's table): 0 two-pass softmax awaiting PV before
-// the next score GEMM, 1 the same with in-order MMA issue, 2 one TMEM pass with the row in
-// registers, 3..5 the same with 4 / 6 / 8 of every 16 column pairs exponentiated on the FMA pipe.
-constexpr int kFwdVariants = 6;
-int g_fwd_variant = 0;
+
+// Forward kernel: 1 = in-order MMA issue (default), 0 = PV completion awaited before the next score GEMM.
+int g_fwd_inorder = 1;
 
 }  // namespace attn
 
-void attn_set_backward_variant(int v) { attn::g_bwd_variant = v < 0 ? 0 : (v > 3 ? 3 : v); }
-int attn_get_variant(int backward) { return backward ? attn::g_bwd_variant : attn::g_fwd_variant; }
-void attn_set_forward_variant(int v) {
-  attn::g_fwd_variant = v < 0 ? 0 : (v >= attn::kFwdVariants ? attn::kFwdVariants - 1 : v);
-}
+void attn_set_forward_variant(int v) { attn::g_fwd_inorder = v ? 1 : 0; }
+int attn_get_variant(int backward) { return backward ? 0 : attn::g_fwd_inorder; }
 
 const char* launch_attn_fwd(const void* q, const void* k, const void* v, const int* items, int n_items, int L, int H,
                             int head_dim, float scale, void* out, float* lse, cudaStream_t s, const uint64_t* o_peer,
@@ -1603,15 +819,9 @@ const char* launch_attn_fwd(const void* q, const void* k, const void* v, const i
   if ((e = make_qkv_map(&qm, q, L, H)) || (e = make_qkv_map(&km, k, L, H)) || (e = make_qkv_map(&vm, v, L, H))) return e;
   typedef void (*FwdKernel)(CUtensorMap, CUtensorMap, CUtensorMap, const WorkItem*, int, int, float, __nv_bfloat16*,
                             float*, PeerRows);
-  static const FwdKernel variants[kFwdVariants] = {
-      attn_fwd_kernel<fwd_variant(FWD_PAIRED | FWD_PACKED, 0)>,
-      attn_fwd_kernel<fwd_variant(FWD_PAIRED | FWD_PACKED | FWD_INORDER, 0)>,
-      attn_fwd_kernel<fwd_variant(FWD_PACKED | FWD_INORDER | FWD_ROWREG, 0)>,
-      attn_fwd_kernel<fwd_variant(FWD_PACKED | FWD_INORDER | FWD_ROWREG, 4)>,
-      attn_fwd_kernel<fwd_variant(FWD_PACKED | FWD_INORDER | FWD_ROWREG, 6)>,
-      attn_fwd_kernel<fwd_variant(FWD_PACKED | FWD_INORDER | FWD_ROWREG, 8)>};
-  static bool attr[kFwdVariants] = {};
-  const int var = g_fwd_variant;
+  static const FwdKernel variants[2] = {attn_fwd_kernel<false>, attn_fwd_kernel<true>};
+  static bool attr[2] = {};
+  const int var = g_fwd_inorder;
   if (!attr[var]) {
     if (cudaFuncSetAttribute(variants[var], cudaFuncAttributeMaxDynamicSharedMemorySize, FWD_SMEM) != cudaSuccess)
       return "attention: cannot set smem size";
@@ -1633,38 +843,15 @@ const char* launch_attn_bwd(const void* q, const void* k, const void* v, const v
   const int warps = L * H;
   attn_bwd_delta_kernel<<<(warps * 32 + 255) / 256, 256, 0, s>>>((const __nv_bfloat16*)o,
                                                                  (const __nv_bfloat16*)dout, L, H, delta);
-  CUtensorMap qm, km, vm, dom;
+  if (dq_acc == nullptr) return "attention backward: an fp32 dQ accumulator is required";
   const char* e;
-  if ((e = make_qkv_map(&qm, q, L, H)) || (e = make_qkv_map(&km, k, L, H)) || (e = make_qkv_map(&vm, v, L, H)) ||
-      (e = make_qkv_map(&dom, dout, L, H)))
+  if ((e = run_bwd_single_pass(q, k, v, dout, lse, delta, items_kv, n_items_kv, L, H, scale, dq_acc,
+                               (__nv_bfloat16*)dk, (__nv_bfloat16*)dv, PeerRows{nullptr, 1, 0, H},
+                               PeerRows{nullptr, 1, 0, H}, s)))
     return e;
-  if (g_bwd_variant >= 1 && dq_acc != nullptr) {
-    if ((e = run_bwd_single_pass(q, k, v, dout, lse, delta, items_kv, n_items_kv, L, H, scale, dq_acc,
-                                 (__nv_bfloat16*)dk, (__nv_bfloat16*)dv, PeerRows{nullptr, 1, 0, H},
-                                 PeerRows{nullptr, 1, 0, H}, s)))
-      return e;
-    const size_t n8 = (size_t)L * H * D / 8;
-    attn_dq_convert_kernel<<<(unsigned)((n8 + 255) / 256), 256, 0, s>>>(dq_acc, n8, scale, (__nv_bfloat16*)dq,
-                                                                         PeerRows{nullptr, 1, 0, H}, H, L);
-    return cudaGetLastError() == cudaSuccess ? nullptr : "attention fused backward launch failed";
-  }
-  static bool attr = false;
-  if (!attr) {
-    if (cudaFuncSetAttribute(attn_bwd_kernel<MODE_DQ>, cudaFuncAttributeMaxDynamicSharedMemorySize, BWD_SMEM) !=
-            cudaSuccess ||
-        cudaFuncSetAttribute(attn_bwd_kernel<MODE_DKV>, cudaFuncAttributeMaxDynamicSharedMemorySize, BWD_SMEM) !=
-            cudaSuccess)
-      return "attention: cannot set smem size";
-    attr = true;
-  }
-  if (n_items_q > 0)
-    attn_bwd_kernel<MODE_DQ><<<dim3(n_items_q, H), BWD_THREADS, BWD_SMEM, s>>>(
-        qm, km, vm, dom, reinterpret_cast<const WorkItem*>(items_q), L, H, scale, lse, delta, (__nv_bfloat16*)dq,
-        nullptr);
-  if (n_items_kv > 0)
-    attn_bwd_kernel<MODE_DKV><<<dim3(n_items_kv, H), BWD_THREADS, BWD_SMEM, s>>>(
-        qm, km, vm, dom, reinterpret_cast<const WorkItem*>(items_kv), L, H, scale, lse, delta, (__nv_bfloat16*)dk,
-        (__nv_bfloat16*)dv);
+  const size_t n8 = (size_t)L * H * D / 8;
+  attn_dq_convert_kernel<<<(unsigned)((n8 + 255) / 256), 256, 0, s>>>(dq_acc, n8, scale, (__nv_bfloat16*)dq,
+                                                                       PeerRows{nullptr, 1, 0, H}, H, L);
   return cudaGetLastError() == cudaSuccess ? nullptr : "attention backward launch failed";
 }
 

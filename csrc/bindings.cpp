@@ -32,7 +32,6 @@ const char* launch_attn_bwd(const void* q, const void* k, const void* v, const v
                             float* dq_acc, cudaStream_t s);
 int attn_error_flag(bool reset);
 int qkv_bounds_error(bool reset);
-void attn_set_backward_variant(int v);
 void attn_set_forward_variant(int v);
 int attn_get_variant(int backward);
 void launch_sumsq(const void* x, bool fp32, size_t n, float* partial, int n_part, cudaStream_t s);
@@ -720,7 +719,6 @@ PYBIND11_MODULE(TORCH_EXTENSION_NAME, m) {
   m.def("gather_rows", &pan::gather_rows, kNoGil);
   m.def("gemm", &pan::gemm, kNoGil);
   m.def("gemm_force_cta_group", &pan::gemm_force_cta_group, kNoGil);
-  m.def("attn_set_backward_variant", &pan::attn_set_backward_variant, kNoGil);
   m.def("attn_set_forward_variant", &pan::attn_set_forward_variant, kNoGil);
   m.def("attn_get_variant", &pan::attn_get_variant, kNoGil);
   m.def("gemm_tuning", &pan::gemm_tuning, kNoGil);

@@ -67,8 +67,7 @@ struct Params {
   __nv_bfloat16* aux2;    // DGELU: GELU(pre) out
   long long ldaux2;
   int epi;
-  int probe;  // timing experiments only: bit 0 skips the epilogue stores, bit 1 re-reads k-block 0,
-              // bit 2 makes the waits sleep (suspend-time hint) between polls
+  int probe;  // timing experiments only: bit 0 skips the epilogue stores, bit 1 re-reads k-block 0
   int reduce_add;  // D += acc through TMA reduce-add stores (no read of D by the kernel)
   int band_m;      // tile order: 0 = N bands of 8 tiles, > 0 = M bands of band_m tiles
   int accumulate;  // host-side only: folded into C = D, beta = 1
@@ -150,9 +149,6 @@ gemm_kernel(const __grid_constant__ Params p, const __grid_constant__ TmapSet ma
   const int tile0 = CG == 2 ? (int)cluster_id_x() : (int)blockIdx.x;
   const int tile_step = CG == 2 ? (int)nclusters_x() : (int)gridDim.x;
 
-  auto gwait = [&](uint32_t bar, uint32_t parity, int code) {
-    return (p.probe & 4) ? mbar_wait_sleep(bar, parity, code, 1000000u) : mbar_wait(bar, parity, code);
-  };
   auto full_bar = [&](int s) { return smem_u32(bars + s); };
   auto empty_bar = [&](int s) { return smem_u32(bars + STAGES + s); };
   auto tfull_bar = [&](int a) { return smem_u32(bars + 2 * STAGES + a); };
@@ -200,7 +196,7 @@ gemm_kernel(const __grid_constant__ Params p, const __grid_constant__ TmapSet ma
         const int z = t / p.tiles_per_batch;
         const int k_blocks = p.k_blocks[g];
         for (int kb = 0; kb < k_blocks && !s_abort; ++kb) {
-          if (!gwait(empty_bar(stage), phase ^ 1, 11)) { s_abort = 1; break; }
+          if (!mbar_wait(empty_bar(stage), phase ^ 1, 11)) { s_abort = 1; break; }
           // CG 2: both CTAs' bytes complete on the leader's full barrier
           const uint32_t fb = CG == 2 ? mapa_shared(full_bar(stage), 0) : full_bar(stage);
           if (crank == 0) mbar_expect_tx(full_bar(stage), CG * (A_STAGE + B_STAGE));
@@ -240,7 +236,7 @@ gemm_kernel(const __grid_constant__ Params p, const __grid_constant__ TmapSet ma
       int acc = 0;
       uint32_t acc_phase = 0;
       for (int t = tile0; t < total_tiles && !s_abort; t += tile_step) {
-        if (!gwait(tempty_bar(acc), acc_phase ^ 1, 12)) { s_abort = 1; break; }
+        if (!mbar_wait(tempty_bar(acc), acc_phase ^ 1, 12)) { s_abort = 1; break; }
         tc_fence_after();
         int g, mb, nb;
         tile_coords(p, t, g, mb, nb);
@@ -248,7 +244,7 @@ gemm_kernel(const __grid_constant__ Params p, const __grid_constant__ TmapSet ma
         const uint32_t d_tmem = tmem_base + acc * BN;
         bool ok = true;
         for (int kb = 0; kb < k_blocks; ++kb) {
-          if (!gwait(full_bar(stage), phase, 13)) { ok = false; break; }
+          if (!mbar_wait(full_bar(stage), phase, 13)) { ok = false; break; }
           tc_fence_after();
           const uint32_t sa = smem_u32(smem_a + stage * A_STAGE);
           const uint32_t sb = smem_u32(smem_b + stage * B_STAGE);
@@ -361,7 +357,7 @@ gemm_kernel(const __grid_constant__ Params p, const __grid_constant__ TmapSet ma
     int acc = 0;
     uint32_t acc_phase = 0;
     for (int t = tile0; t < total_tiles && !s_abort; t += tile_step) {
-      if (!gwait(tfull_bar(acc), acc_phase, 14)) { s_abort = 1; break; }
+      if (!mbar_wait(tfull_bar(acc), acc_phase, 14)) { s_abort = 1; break; }
       tc_fence_after();
       int g, mb, nb;
       tile_coords(p, t, g, mb, nb);

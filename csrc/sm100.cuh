@@ -61,34 +61,6 @@ __device__ __forceinline__ bool mbar_try_wait(uint32_t bar, uint32_t parity) {
   return ok != 0;
 }
 
-// try_wait with a suspend-time hint: the thread sleeps in hardware until the phase completes or
-// `hint_ns` elapses, instead of re-polling.
-__device__ __forceinline__ bool mbar_try_wait_hint(uint32_t bar, uint32_t parity, uint32_t hint_ns) {
-  uint32_t ok;
-  asm volatile(
-      "{\n\t.reg .pred p;\n\t"
-      "mbarrier.try_wait.parity.acquire.cta.shared::cta.b64 p, [%1], %2, %3;\n\t"
-      "selp.u32 %0, 1, 0, p;\n\t}"
-      : "=r"(ok)
-      : "r"(bar), "r"(parity), "r"(hint_ns)
-      : "memory");
-  return ok != 0;
-}
-
-// Bounded wait whose polls sleep up to `hint_ns` each (see mbar_wait for the limit and error code).
-__device__ __forceinline__ bool mbar_wait_sleep(uint32_t bar, uint32_t parity, int code, uint32_t hint_ns,
-                                                uint64_t limit_ns = 4000000000ull) {
-  if (mbar_try_wait(bar, parity)) return true;
-  const uint64_t t0 = global_timer_ns();
-  while (true) {
-    if (mbar_try_wait_hint(bar, parity, hint_ns)) return true;
-    if (global_timer_ns() - t0 > limit_ns) {
-      atomicCAS(&g_error_flag, 0, code);
-      return false;
-    }
-  }
-}
-
 // Wait for the phase with the given parity to complete.  Gives up after `limit_ns` (default 4 s),
 // sets g_error_flag to `code` and returns false; callers then unwind instead of hanging the GPU.
 __device__ __forceinline__ bool mbar_wait(uint32_t bar, uint32_t parity, int code = 1,
@@ -224,12 +196,6 @@ __device__ __forceinline__ void tmem_st16(uint32_t taddr, const uint32_t (&r)[16
           taddr),
       "r"(r[0]), "r"(r[1]), "r"(r[2]), "r"(r[3]), "r"(r[4]), "r"(r[5]), "r"(r[6]), "r"(r[7]), "r"(r[8]), "r"(r[9]),
       "r"(r[10]), "r"(r[11]), "r"(r[12]), "r"(r[13]), "r"(r[14]), "r"(r[15]));
-}
-
-// 32 lanes x 8 columns store.
-__device__ __forceinline__ void tmem_st8(uint32_t taddr, const uint32_t (&r)[8]) {
-  asm volatile("tcgen05.st.sync.aligned.32x32b.x8.b32 [%0], {%1,%2,%3,%4,%5,%6,%7,%8};" ::"r"(taddr), "r"(r[0]),
-               "r"(r[1]), "r"(r[2]), "r"(r[3]), "r"(r[4]), "r"(r[5]), "r"(r[6]), "r"(r[7]));
 }
 
 __device__ __forceinline__ void tmem_ld_wait() { asm volatile("tcgen05.wait::ld.sync.aligned;" ::: "memory"); }

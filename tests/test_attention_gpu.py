@@ -20,24 +20,14 @@ def ref_attention(q, k, v, lens, scale):
     return out, lse
 
 
-# (forward variant, backward variant); None keeps the library default
-VARIANTS = [(None, None), (1, 3), (2, 3), (5, 3), (0, 2), (0, 0)]
-
-
-@pytest.fixture(params=VARIANTS, ids=["default", "fwd1_bwd3", "fwd2_bwd3", "fwd5_bwd3", "pipelined_bwd",
-                                      "two_pass_bwd"])
+@pytest.fixture(params=[1, 0], ids=["inorder_fwd", "awaiting_fwd"])
 def variants(request):
     from pan2_b200.ops._ext import ext
     E = ext()
-    saved = (E.attn_get_variant(0), E.attn_get_variant(1))
-    f, b = request.param
-    if f is not None:
-        E.attn_set_forward_variant(f)
-    if b is not None:
-        E.attn_set_backward_variant(b)
+    saved = E.attn_get_variant(0)
+    E.attn_set_forward_variant(request.param)
     yield request.param
-    E.attn_set_forward_variant(saved[0])
-    E.attn_set_backward_variant(saved[1])
+    E.attn_set_forward_variant(saved)
 
 
 @pytest.mark.parametrize("lens", [[128], [300, 129, 1000, 64], [2048, 5, 700]])
