@@ -52,6 +52,8 @@ def parse():
                          "clip (~107k tokens) with Ulysses CP over all ranks; sft: mixed images + videos of "
                          "random lengths filling the SFT budget, CP=2")
     ap.add_argument("--cp", type=int, default=None, help="context-parallel size (longctx: all ranks, sft: 2)")
+    ap.add_argument("--no-parity", action="store_true",
+                    help="skip the small-model check of the fused peer-memory paths against NCCL (N > 1)")
     return ap.parse_args()
 
 
@@ -126,6 +128,12 @@ def main():
         import datetime
         dist.init_process_group("nccl", timeout=datetime.timedelta(seconds=900), device_id=device)
         group = dist.group.WORLD
+
+    parity = None
+    if world > 1 and not args.no_parity:
+        # every fused collective path against its NCCL baseline on a small model, before the timed job
+        from pan2_b200.utils.parity import fused_path_parity
+        parity = fused_path_parity(device, group, rank, layout, cp)
 
     with open(args.config) as f:
         cfg = yaml.safe_load(f)
@@ -246,6 +254,7 @@ def main():
                     "h2d_bytes_per_step": h2d, "d2h_bytes_per_step": 8,
                     "api": "pan2_b200.training.step.StepRunner (inputs copied from pinned host memory)"},
             "gpu_launches": launches["total"],
+            "parity_fused_vs_nccl": parity,
             "clocks": clocks,
             "loss": metrics["loss"],
             "grad_norm": metrics["grad_norm"],
