@@ -26,36 +26,61 @@ __device__ __forceinline__ void load_bounds(const int* __restrict__ bounds, int 
 }
 
 // y = LN(x) * (1 + scale[seg]) + shift[seg]; padding rows -> 0.
-__global__ void ln_modulate_fwd_kernel(const __nv_bfloat16* __restrict__ x, const float* __restrict__ stats,
-                                       const __nv_bfloat16* __restrict__ shift,
-                                       const __nv_bfloat16* __restrict__ scale, const int* __restrict__ bounds,
-                                       int n_seg, int L, int C, __nv_bfloat16* __restrict__ y) {
+// A CTA owns a 2048-column slab (8 columns per thread, one 16-byte vector) and a run of
+// consecutive rows.  Consecutive rows almost always share a segment, so each thread keeps its
+// columns of shift and (1 + scale) in registers and reloads them only when the segment changes;
+// per row a thread then reads 16 bytes of x and writes 16 bytes of y (plus the row's two
+// statistics, one broadcast load per warp), which keeps the kernel on DRAM bandwidth rather than on
+// L1 re-reads of the modulation rows.  Rows are processed ROWS at a time so several loads are in
+// flight per thread.
+constexpr int LNM_COLS = 2048;
+constexpr int LNM_ROWS = 4;
+__global__ void __launch_bounds__(256) ln_modulate_fwd_kernel(
+    const __nv_bfloat16* __restrict__ x, const float* __restrict__ stats, const __nv_bfloat16* __restrict__ shift,
+    const __nv_bfloat16* __restrict__ scale, const int* __restrict__ bounds, int n_seg, int L, int C,
+    int rows_per_cta, __nv_bfloat16* __restrict__ y) {
   __shared__ int sb[kMaxSeg + 1];
   load_bounds(bounds, n_seg, sb);
-  const int lane = threadIdx.x & 31;
-  const int warps = blockDim.x >> 5;
-  for (int row = blockIdx.x * warps + (threadIdx.x >> 5); row < L; row += gridDim.x * warps) {
-    const int seg = find_segment(sb, n_seg, row);
-    __nv_bfloat16* yr = y + (size_t)row * C;
-    if (seg < 0) {
-      float z[8] = {0, 0, 0, 0, 0, 0, 0, 0};
-      for (int c = lane * 8; c < C; c += 256) store8(yr + c, z);
-      continue;
-    }
-    const float s0 = stats[2 * row], s1 = stats[2 * row + 1];
-    const float mean = s0 / C;
-    const float rstd = rsqrtf(fmaxf(s1 / C - mean * mean, 0.f) + kLnEps);
-    const __nv_bfloat16* xr = x + (size_t)row * C;
-    const __nv_bfloat16* sh = shift + (size_t)seg * C;
-    const __nv_bfloat16* sc = scale + (size_t)seg * C;
-    for (int c = lane * 8; c < C; c += 256) {
-      float xv[8], hv[8], sv[8], o[8];
-      load8(xr + c, xv);
-      load8(sh + c, hv);
-      load8(sc + c, sv);
+  const int c = blockIdx.x * LNM_COLS + threadIdx.x * 8;
+  if (c >= C) return;
+  const int r0 = blockIdx.y * rows_per_cta;
+  const int r1 = min(L, r0 + rows_per_cta);
+  int seg = -2, seg_end = -1;  // segment of the cached modulation columns; its last row + 1
+  float hv[8], sv1[8];
+  const float inv_c = 1.f / C;
+  for (int row = r0; row < r1; row += LNM_ROWS) {
+    float xv[LNM_ROWS][8];
 #pragma unroll
-      for (int i = 0; i < 8; ++i) o[i] = (xv[i] - mean) * rstd * (1.f + sv[i]) + hv[i];
-      store8(yr + c, o);
+    for (int k = 0; k < LNM_ROWS; ++k)
+      if (row + k < r1) load8(x + (size_t)(row + k) * C + c, xv[k]);
+#pragma unroll
+    for (int k = 0; k < LNM_ROWS; ++k) {
+      const int r = row + k;
+      if (r >= r1) break;
+      float o[8];
+      if (r >= seg_end) {
+        seg = find_segment(sb, n_seg, r);
+        if (seg >= 0) {
+          seg_end = sb[seg + 1];
+          load8(shift + (size_t)seg * C + c, hv);
+          load8(scale + (size_t)seg * C + c, sv1);
+#pragma unroll
+          for (int i = 0; i < 8; ++i) sv1[i] += 1.f;
+        } else {
+          seg_end = r < sb[0] ? sb[0] : L;  // the next row that can be inside a segment
+        }
+      }
+      if (seg < 0) {
+#pragma unroll
+        for (int i = 0; i < 8; ++i) o[i] = 0.f;
+      } else {
+        const float2 st = *reinterpret_cast<const float2*>(stats + 2 * (size_t)r);
+        const float mean = st.x * inv_c;
+        const float rstd = rsqrtf(fmaxf(st.y * inv_c - mean * mean, 0.f) + kLnEps);
+#pragma unroll
+        for (int i = 0; i < 8; ++i) o[i] = (xv[k][i] - mean) * rstd * sv1[i] + hv[i];
+      }
+      store8(y + (size_t)r * C + c, o);
     }
   }
 }
@@ -392,8 +417,15 @@ void column_reduce(const void* g, const void* x, const float* stats, const int* 
 
 void launch_ln_modulate_fwd(const void* x, const float* stats, const void* shift, const void* scale,
                             const int* bounds, int n_seg, int L, int C, void* y, cudaStream_t s) {
-  ln_modulate_fwd_kernel<<<row_grid(L), 256, 0, s>>>(CBF(x), stats, CBF(shift), CBF(scale), bounds, n_seg, L, C,
-                                                     BF(y));
+  if (L <= 0) return;
+  const int slabs = (C + LNM_COLS - 1) / LNM_COLS;
+  // about four CTAs per SM in total, rows split evenly (a multiple of the unroll)
+  const int chunks = (592 + slabs - 1) / slabs;
+  int rows = (L + chunks - 1) / chunks;
+  rows = (rows + LNM_ROWS - 1) / LNM_ROWS * LNM_ROWS;
+  const dim3 grid(slabs, (L + rows - 1) / rows);
+  ln_modulate_fwd_kernel<<<grid, 256, 0, s>>>(CBF(x), stats, CBF(shift), CBF(scale), bounds, n_seg, L, C, rows,
+                                              BF(y));
 }
 
 void launch_ln_modulate_bwd(const void* g, const void* x, const float* stats, const void* scale, const int* bounds,
