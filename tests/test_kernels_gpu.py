@@ -211,3 +211,27 @@ def test_qkv_project_matches_reference():
         assert_close(a.cpu(), r, 2e-2, n)
     for a, r, n in zip(gc, gr, ["dx", "dw", "db", "dqw", "dkw"]):
         assert_close(a.cpu(), r, 3e-2, n)
+
+
+def test_ln_modulate_forward_wide_rows_many_segments():
+    """Bench-width rows (C = 4096, two column slabs), several segments per CTA row run, padding
+    rows at the end: equal to the fp32 formula."""
+    from pan2_b200.ops._ext import ext
+    from pan2_b200.ops.packed import _bounds_tensor, ln_stats_of
+    torch.manual_seed(3)
+    L, C = 5003, 4096
+    bounds = [0, 7, 1500, 1501, 3333, 4990]
+    x = (torch.randn(L, C, device="cuda") * 1.5 + 0.3).to(torch.bfloat16)
+    stats = ln_stats_of(x)
+    shift = (torch.randn(5, C, device="cuda") * 0.1).to(torch.bfloat16)
+    scale = (torch.randn(5, C, device="cuda") * 0.1).to(torch.bfloat16)
+    y = ext().ln_modulate_fwd(x, stats, shift, scale, _bounds_tensor(bounds, x.device), 5)
+    xf = x.float()
+    mean = stats[:, 0:1] / C
+    rstd = torch.rsqrt((stats[:, 1:2] / C - mean * mean).clamp_min(0) + 1e-6)
+    ref = torch.zeros(L, C, device="cuda")
+    for s in range(5):
+        a, b = bounds[s], bounds[s + 1]
+        ref[a:b] = (xf[a:b] - mean[a:b]) * rstd[a:b] * (1 + scale[s].float()) + shift[s].float()
+    assert (y.float() - ref).abs().max().item() < 3e-2
+    assert y[bounds[-1]:].abs().max().item() == 0
