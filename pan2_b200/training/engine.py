@@ -555,9 +555,11 @@ class TrainEngine:
         self._upd_ready = dict(ready)  # the forward pops from this copy; the thread signals `ready`
         clip = self._clip_used if self.optim.max_grad_norm > 0 else None
 
+        dev_index = self.device.index if self.device.index is not None else torch.cuda.current_device()
+
         def run():
             try:
-                torch.cuda.set_device(self.device)
+                torch.cuda.set_device(dev_index)
                 self._opt_stream.wait_event(start)
                 self._stream_update(order, self._opt_stream, self._lr_used, clip, publish=ready)
             except BaseException as e:  # surfaced by the next _wait_update
