@@ -34,8 +34,9 @@ __device__ __forceinline__ void load_bounds(const int* __restrict__ bounds, int 
 // L1 re-reads of the modulation rows.  Rows are processed ROWS at a time so several loads are in
 // flight per thread.
 constexpr int LNM_COLS = 2048;
-constexpr int LNM_ROWS = 4;
-__global__ void __launch_bounds__(256) ln_modulate_fwd_kernel(
+constexpr int LNM_ROWS = 8;       // rows in flight per thread (raw 16-byte vectors, 128 bytes)
+constexpr int LNM_CTAS_PER_SM = 3;
+__global__ void __launch_bounds__(256, LNM_CTAS_PER_SM) ln_modulate_fwd_kernel(
     const __nv_bfloat16* __restrict__ x, const float* __restrict__ stats, const __nv_bfloat16* __restrict__ shift,
     const __nv_bfloat16* __restrict__ scale, const int* __restrict__ bounds, int n_seg, int L, int C,
     int rows_per_cta, __nv_bfloat16* __restrict__ y) {
@@ -45,19 +46,18 @@ __global__ void __launch_bounds__(256) ln_modulate_fwd_kernel(
   if (c >= C) return;
   const int r0 = blockIdx.y * rows_per_cta;
   const int r1 = min(L, r0 + rows_per_cta);
-  int seg = -2, seg_end = -1;  // segment of the cached modulation columns; its last row + 1
+  int seg = -2, seg_end = -1;  // segment of the cached modulation columns; first row past it
   float hv[8], sv1[8];
   const float inv_c = 1.f / C;
   for (int row = r0; row < r1; row += LNM_ROWS) {
-    float xv[LNM_ROWS][8];
+    uint4 raw[LNM_ROWS];
 #pragma unroll
     for (int k = 0; k < LNM_ROWS; ++k)
-      if (row + k < r1) load8(x + (size_t)(row + k) * C + c, xv[k]);
+      raw[k] = row + k < r1 ? *reinterpret_cast<const uint4*>(x + (size_t)(row + k) * C + c) : make_uint4(0, 0, 0, 0);
 #pragma unroll
     for (int k = 0; k < LNM_ROWS; ++k) {
       const int r = row + k;
       if (r >= r1) break;
-      float o[8];
       if (r >= seg_end) {
         seg = find_segment(sb, n_seg, r);
         if (seg >= 0) {
@@ -70,6 +70,7 @@ __global__ void __launch_bounds__(256) ln_modulate_fwd_kernel(
           seg_end = r < sb[0] ? sb[0] : L;  // the next row that can be inside a segment
         }
       }
+      float o[8];
       if (seg < 0) {
 #pragma unroll
         for (int i = 0; i < 8; ++i) o[i] = 0.f;
@@ -77,8 +78,13 @@ __global__ void __launch_bounds__(256) ln_modulate_fwd_kernel(
         const float2 st = *reinterpret_cast<const float2*>(stats + 2 * (size_t)r);
         const float mean = st.x * inv_c;
         const float rstd = rsqrtf(fmaxf(st.y * inv_c - mean * mean, 0.f) + kLnEps);
+        const __nv_bfloat162* h2 = reinterpret_cast<const __nv_bfloat162*>(&raw[k]);
 #pragma unroll
-        for (int i = 0; i < 8; ++i) o[i] = (xv[k][i] - mean) * rstd * sv1[i] + hv[i];
+        for (int i = 0; i < 4; ++i) {
+          const float2 xv = __bfloat1622float2(h2[i]);
+          o[2 * i] = (xv.x - mean) * rstd * sv1[2 * i] + hv[2 * i];
+          o[2 * i + 1] = (xv.y - mean) * rstd * sv1[2 * i + 1] + hv[2 * i + 1];
+        }
       }
       store8(y + (size_t)r * C + c, o);
     }
@@ -419,8 +425,14 @@ void launch_ln_modulate_fwd(const void* x, const float* stats, const void* shift
                             const int* bounds, int n_seg, int L, int C, void* y, cudaStream_t s) {
   if (L <= 0) return;
   const int slabs = (C + LNM_COLS - 1) / LNM_COLS;
-  // about four CTAs per SM in total, rows split evenly (a multiple of the unroll)
-  const int chunks = (592 + slabs - 1) / slabs;
+  // one wave: LNM_CTAS_PER_SM CTAs per SM in total, rows split evenly (a multiple of the unroll)
+  static int sms = 0;
+  if (sms == 0) {
+    int dev = 0;
+    cudaGetDevice(&dev);
+    cudaDeviceGetAttribute(&sms, cudaDevAttrMultiProcessorCount, dev);
+  }
+  const int chunks = (sms * LNM_CTAS_PER_SM + slabs - 1) / slabs;
   int rows = (L + chunks - 1) / chunks;
   rows = (rows + LNM_ROWS - 1) / LNM_ROWS * LNM_ROWS;
   const dim3 grid(slabs, (L + rows - 1) / rows);
