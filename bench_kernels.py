@@ -231,9 +231,55 @@ def run_elementwise(small, timer, peaks, which):
     return out
 
 
+def _ns_library(G, coeffs=(3.4445, -4.7750, 2.0315), steps=5, eps=1e-7, reset=2):
+    """The same Gram Newton-Schulz recurrence on cuBLAS (torch bf16 batched matmuls, fp32 Gram of
+    the input): the library baseline of the fused-kernel chain."""
+    a, b, c = coeffs
+    X = G.transpose(-1, -2) if G.shape[-2] > G.shape[-1] else G
+    R32 = torch.matmul(X.float(), X.float().transpose(-1, -2))
+    n2 = torch.diagonal(R32, dim1=-2, dim2=-1).sum(-1).clamp(min=eps * eps).view(-1, 1, 1)
+    R = (R32 / n2).to(torch.bfloat16)
+    eye = torch.eye(R.shape[-1], device=G.device, dtype=torch.bfloat16)
+    Q, first = None, True
+    for i in range(steps):
+        if i == reset and Q is not None:
+            if first:
+                Q = (Q / n2.sqrt()).to(torch.bfloat16)
+                first = False
+            X = torch.matmul(Q, X)
+            R = torch.matmul(X, X.transpose(-1, -2))
+            Q = None
+        Z = c * torch.matmul(R, R) + b * R
+        Q = a * eye + Z if Q is None else torch.matmul(Q, Z) + a * Q
+        if i < steps - 1 and (i + 1) != reset:
+            RZ = torch.matmul(R, Z) + a * R
+            R = torch.matmul(Z, RZ) + a * RZ
+    if first:
+        Q = (Q / n2.sqrt()).to(torch.bfloat16)
+    return torch.matmul(Q, X)
+
+
+def run_muon_ns(timer, library):
+    """Gram Newton-Schulz of the 29B block's Muon matrices: the QKV weight as its 192 per-head row
+    chunks and the video FFN up-projection (orthogonalised through its 4096-row side)."""
+    from pan2_b200.optim.muon import gram_newton_schulz
+    out = []
+    for name, shape in (("qkv_chunks", (192, 128, 4096)), ("ffn_up_video", (1, 32768, 4096)),
+                        ("out_proj_chunks", (2, 4096, 4096))):
+        G = torch.randn(*shape, device="cuda").to(torch.bfloat16)
+        ms = timer(lambda: gram_newton_schulz(G))
+        rec = dict(case=f"muon_ns_{name}", shape=list(shape), ms=round(ms, 4))
+        if library:
+            ms_l = timer(lambda: _ns_library(G))
+            rec["library_bmm_ms"] = round(ms_l, 4)
+        out.append(rec)
+    return out
+
+
 def main():
     ap = argparse.ArgumentParser(description=__doc__.splitlines()[0])
-    ap.add_argument("--case", default=".*", help="regex over gemm, attn_fwd, attn_bwd, ln_modulate, gate_residual")
+    ap.add_argument("--case", default=".*",
+                    help="regex over gemm, attn_fwd, attn_bwd, ln_modulate, gate_residual, muon_ns")
     ap.add_argument("--small", action="store_true", help="one small case per kernel (operands still above L2)")
     ap.add_argument("--iters", type=int, default=10)
     ap.add_argument("--warmup", type=int, default=3)
@@ -266,6 +312,9 @@ def main():
     which = [w for w in ("ln_modulate", "gate_residual") if pat.search(w)]
     if which:
         for r in run_elementwise(args.small, timer, peaks, which):
+            print(json.dumps(r), flush=True)
+    if pat.search("muon_ns"):
+        for r in run_muon_ns(timer, library):
             print(json.dumps(r), flush=True)
     print(json.dumps({"peaks": {"hbm_gbs": peaks[0], "bf16_tflops": peaks[1], "source": peaks[2]}}))
 
