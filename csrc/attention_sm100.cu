@@ -415,10 +415,17 @@ attn_fwd_kernel(const __grid_constant__ CUtensorMap qmap, const __grid_constant_
 // two-pass form needs seven and two exponentials).  TMEM: S^T/P^T/dQ^T 0..127, dP^T/dS^T 128..255,
 // dV 256..383, dK 384..511.  Warps: 0 TMA, 1 MMA, 2..5 E, 6..9 Q.  dQ accumulates in an fp32
 // buffer that a final kernel scales into bf16.
-constexpr int FB_THREADS = 320;
+// Warps: 0 TMA, 1 MMA, 2..5 and 10..13 elementwise (E) on query columns 0..63 and 64..127 of the
+// same key rows (two E warps per SM sub-partition, so one computes while the other waits on TMEM),
+// 6..9 dQ drain.  An E group's packed P^T / dS^T land in TMEM columns [64 g, 64 g + 32) of S^T /
+// dP^T, which only its own group reads as scores, so the groups never wait on each other; the MMA
+// reads query step kk (16 queries) at column 64 (kk / 4) + 8 (kk % 4).
+constexpr int FB_THREADS = 448;
 constexpr int FB_STAGE = 32 * D * 4;  // 32 query rows of fp32 dQ
 constexpr int FB_SMEM = 2 * TILE_BYTES /*K, V*/ + 2 * TILE_BYTES /*Q ring*/ + TILE_BYTES /*dO*/ +
                         TILE_BYTES /*dS^T*/ + 2 * FB_STAGE + 1024 + 256 + 2 * BT * 4;
+
+__device__ __forceinline__ uint32_t packed_col(int kk) { return (uint32_t)(64 * (kk >> 2) + 8 * (kk & 3)); }
 
 __global__ void __launch_bounds__(FB_THREADS, 1)
 attn_bwd_fused_kernel(const __grid_constant__ CUtensorMap qmap, const __grid_constant__ CUtensorMap kmap,
@@ -451,7 +458,7 @@ attn_bwd_fused_kernel(const __grid_constant__ CUtensorMap qmap, const __grid_con
 
   if (threadIdx.x == 0) {
     s_abort = 0;
-    for (int i = 0; i < 14; ++i) mbar_init(B(i), (i == 8 || i == 12) ? 4 : 1);  // ds_ready / dq_drained: 4 warps
+    for (int i = 0; i < 14; ++i) mbar_init(B(i), i == 8 ? 8 : (i == 12 ? 4 : 1));  // ds_ready: 8 E warps, dq_drained: 4
     fence_barrier_init();
   }
   if (warp == 1) {
@@ -511,11 +518,11 @@ attn_bwd_fused_kernel(const __grid_constant__ CUtensorMap qmap, const __grid_con
         // dV += P^T dO_i ; dK += dS^T Q_i  (K = 128 queries, 8 columns of packed bf16 per step)
 #pragma unroll
         for (int kk = 0; kk < BT / 16; ++kk)
-          mma_bf16_ts(T_DV, T_S + kk * 8, desc_mnmajor(dO, kk), id_tm, (i > 0) || (kk > 0));
+          mma_bf16_ts(T_DV, T_S + packed_col(kk), desc_mnmajor(dO, kk), id_tm, (i > 0) || (kk > 0));
         mma_commit(B(6));  // dO slot free
 #pragma unroll
         for (int kk = 0; kk < BT / 16; ++kk)
-          mma_bf16_ts(T_DK, T_DP + kk * 8, desc_mnmajor(q, kk), id_tm, (i > 0) || (kk > 0));
+          mma_bf16_ts(T_DK, T_DP + packed_col(kk), desc_mnmajor(q, kk), id_tm, (i > 0) || (kk > 0));
         mma_commit(B(3 + slot));  // Q slot free
         mma_commit(B(10));
         if (!(ok = mbar_wait(B(10), i & 1, 48))) break;  // P^T read before dQ^T overwrites its columns
@@ -529,19 +536,20 @@ attn_bwd_fused_kernel(const __grid_constant__ CUtensorMap qmap, const __grid_con
       mma_commit(B(13));
       if (!ok) s_abort = 1;
     }
-  } else if (warp < 6) {
+  } else if (warp < 6 || warp >= 10) {
     // ------------------------------------------------ E warps: P^T and dS^T (lane = key row)
     const int quarter = warp & 3;
+    const int grp = warp >= 10 ? 1 : 0;  // query columns [64 grp, 64 grp + 64)
     const int row = quarter * 32 + lane;
     const uint32_t lane_off = (uint32_t)(quarter * 32) << 16;
     const bool row_valid = it.tile_start + row < it.seg_len;
-    const int tid = threadIdx.x - 64;
+    const int tid = grp == 0 ? threadIdx.x - 64 : -1;  // group 0 stages the per-query LSE / Delta
     bool ok = true;
     // LSE / Delta of query tile i are loaded from global memory one tile ahead (registers), so their
     // latency overlaps the previous tile's work instead of stalling every tile
     auto fetch = [&](int i, float& lv, float& dv) {
       const int qi = i * BT + tid;
-      const bool in = i < n_q && qi < it.seg_len;
+      const bool in = tid >= 0 && i < n_q && qi < it.seg_len;
       lv = in ? lse[(size_t)h * L + it.seg_start + qi] * kLog2e : 0.f;
       dv = in ? delta[(size_t)h * L + it.seg_start + qi] : 0.f;
     };
@@ -549,16 +557,19 @@ attn_bwd_fused_kernel(const __grid_constant__ CUtensorMap qmap, const __grid_con
     fetch(0, next_l, next_d);
     for (int i = 0; i < n_q; ++i) {
       const int valid_q = min(BT, it.seg_len - i * BT);
-      asm volatile("bar.sync 1, 128;" ::: "memory");
-      s_vec[0][tid] = next_l;
-      s_vec[1][tid] = next_d;
-      asm volatile("bar.sync 1, 128;" ::: "memory");
+      asm volatile("bar.sync 1, 256;" ::: "memory");
+      if (tid >= 0) {
+        s_vec[0][tid] = next_l;
+        s_vec[1][tid] = next_d;
+      }
+      asm volatile("bar.sync 1, 256;" ::: "memory");
       fetch(i + 1, next_l, next_d);
       if (!(ok = mbar_wait(B(7), i & 1, 49))) break;
       if (i > 0 && !(ok = mbar_wait(B(9), (i - 1) & 1, 50))) break;  // dQ^T(i-1) has read dS^T smem
       tc_fence_after();
 #pragma unroll
-      for (int c = 0; c < 4; ++c) {
+      for (int cg = 0; cg < 2; ++cg) {
+        const int c = 2 * grp + cg;  // 32-column chunk of the 128 query columns
         uint32_t r[32], y[32];
         tmem_ld32(T_S + lane_off + c * 32, r);
         tmem_ld32(T_DP + lane_off + c * 32, y);
@@ -578,9 +589,9 @@ attn_bwd_fused_kernel(const __grid_constant__ CUtensorMap qmap, const __grid_con
           wp[j >> 1] = pack_bf16(pv[0], pv[1]);
           wd[j >> 1] = pack_bf16(dsv[0], dsv[1]);
         }
-        // columns [16c, 16c + 16) were read in chunk c or earlier
-        tmem_st16(T_S + lane_off + c * 16, wp);
-        tmem_st16(T_DP + lane_off + c * 16, wd);
+        // packed columns [64 grp + 16 cg, +16) of this group's score columns, read in chunk cg or earlier
+        tmem_st16(T_S + lane_off + 64 * grp + 16 * cg, wp);
+        tmem_st16(T_DP + lane_off + 64 * grp + 16 * cg, wd);
         store_row32_swizzled(sdS, row, c * 32, wd);
       }
       tmem_st_wait();
@@ -601,7 +612,8 @@ attn_bwd_fused_kernel(const __grid_constant__ CUtensorMap qmap, const __grid_con
         __nv_bfloat16* dst = pr.base ? (row_valid ? peer_row(pr, g, h) : nullptr)
                                      : (which == 0 ? dk_out : dv_out) + grow * D;
 #pragma unroll
-        for (int c = 0; c < 4; ++c) {
+        for (int cg = 0; cg < 2; ++cg) {
+          const int c = 2 * grp + cg;
           uint32_t r[32];
           tmem_ld32(tacc + c * 32, r);
           tmem_ld_wait();
@@ -629,27 +641,34 @@ attn_bwd_fused_kernel(const __grid_constant__ CUtensorMap qmap, const __grid_con
     for (int i = 0; i < n_q; ++i) {
       if (!mbar_wait(B(11), i & 1, 52)) { s_abort = 1; break; }
       tc_fence_after();
-      uint32_t r[4][32];
+      // two halves of 64 query columns (the 14-warp CTA caps registers at 128 per thread)
 #pragma unroll
-      for (int c = 0; c < 4; ++c) tmem_ld32(T_S + lane_off + c * 32, r[c]);
-      tmem_ld_wait();
-      tc_fence_before();
-      __syncwarp();
-      if (lane == 0) mbar_arrive(B(12));  // the S^T columns may be rewritten
-#pragma unroll
-      for (int c = 0; c < 4; ++c) {
-        float* st = reinterpret_cast<float*>(sStage + (n_used & 1) * FB_STAGE);
-        if (n_used >= 2 && qt == 0) bulk_wait_read<1>();
-        asm volatile("bar.sync 2, 128;" ::: "memory");
-#pragma unroll
-        for (int qq = 0; qq < 32; ++qq) st[qq * D + d] = __uint_as_float(r[c][qq]);
-        fence_async_shared();
-        asm volatile("bar.sync 2, 128;" ::: "memory");
-        if (qt == 0) {
-          tma_reduce_add_2d(&dqmap, smem_u32(st), col, it.seg_start + i * BT + c * 32);
-          bulk_commit();
+      for (int hf = 0; hf < 2; ++hf) {
+        uint32_t r[2][32];
+        tmem_ld32(T_S + lane_off + hf * 64, r[0]);
+        tmem_ld32(T_S + lane_off + hf * 64 + 32, r[1]);
+        tmem_ld_wait();
+        if (hf == 1) {
+          tc_fence_before();
+          __syncwarp();
+          if (lane == 0) mbar_arrive(B(12));  // the S^T columns may be rewritten
         }
-        ++n_used;
+#pragma unroll
+        for (int c2 = 0; c2 < 2; ++c2) {
+          const int c = 2 * hf + c2;
+          float* st = reinterpret_cast<float*>(sStage + (n_used & 1) * FB_STAGE);
+          if (n_used >= 2 && qt == 0) bulk_wait_read<1>();
+          asm volatile("bar.sync 2, 128;" ::: "memory");
+#pragma unroll
+          for (int qq = 0; qq < 32; ++qq) st[qq * D + d] = __uint_as_float(r[c2][qq]);
+          fence_async_shared();
+          asm volatile("bar.sync 2, 128;" ::: "memory");
+          if (qt == 0) {
+            tma_reduce_add_2d(&dqmap, smem_u32(st), col, it.seg_start + i * BT + c * 32);
+            bulk_commit();
+          }
+          ++n_used;
+        }
       }
     }
     if (qt == 0) bulk_wait_all();
