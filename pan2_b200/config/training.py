@@ -40,7 +40,7 @@ def str_to_bool(v) -> bool:
         return True
     if s in ("0", "false", "f", "no", "n", "off"):
         return False
-    raise argparse.ArgumentTypeError(f"expected a boolean, got {v!r}")
+    raise argparse.ArgumentTypeError(f"{v!r} is not a boolean (true/false, yes/no, 1/0)")
 
 
 def parse_json_object(raw, name: str) -> Optional[Dict[str, Any]]:
@@ -54,9 +54,9 @@ def parse_json_object(raw, name: str) -> Optional[Dict[str, Any]]:
     try:
         obj = json.loads(text)
     except json.JSONDecodeError as exc:
-        raise ValueError(f"--{name} must be a JSON object or a path to one: {exc}") from exc
+        raise ValueError(f"--{name}: neither a JSON object nor a readable JSON file ({exc})") from exc
     if not isinstance(obj, dict):
-        raise ValueError(f"--{name} must be a JSON object")
+        raise ValueError(f"--{name} holds JSON that is not an object")
     return obj
 
 
@@ -165,39 +165,39 @@ class TrainingConfig:
     def check(self) -> None:
         """Reject inconsistent settings with an error naming the option."""
         if not self.legacy_eager_mode:
-            raise ValueError("legacy_eager_mode must remain true")
+            raise ValueError("legacy_eager_mode=false is not supported: this trainer always runs eagerly")
         if self.warmup_steps < 0:
-            raise ValueError("--warmup_steps must be >= 0")
+            raise ValueError(f"warmup_steps={self.warmup_steps} is negative")
         if self.lr_decay_steps is not None and self.lr_decay_steps < 0:
-            raise ValueError("--lr_decay_steps must be >= 0 when set")
+            raise ValueError(f"lr_decay_steps={self.lr_decay_steps} is negative")
         for name in ("lr_warmup_start_ratio", "lr_decay_floor_ratio"):
             v = getattr(self, name)
             if not math.isfinite(v) or not 0.0 <= v <= 1.0:
-                raise ValueError(f"--{name} must be finite and in [0, 1]")
+                raise ValueError(f"{name}={v!r} is not a finite value between 0 and 1")
         if self.anomaly_detection_warmup_steps < 0:
-            raise ValueError("--anomaly_detection_warmup_steps must be >= 0")
+            raise ValueError("anomaly_detection_warmup_steps cannot be negative")
         if not (math.isfinite(self.image_cond_prob) and math.isfinite(self.video_cond_prob)):
-            raise ValueError("Require finite image_cond_prob and video_cond_prob")
+            raise ValueError("image_cond_prob and video_cond_prob must be finite numbers")
         if self.image_cond_prob < 0 or self.video_cond_prob < 0 or self.image_cond_prob + self.video_cond_prob > 1:
-            raise ValueError("Require 0 <= image_cond_prob, video_cond_prob and their sum <= 1")
+            raise ValueError("image_cond_prob and video_cond_prob are probabilities of exclusive tasks: each >= 0, together <= 1")
         if not (math.isfinite(self.flow_lognorm_loc) and math.isfinite(self.flow_lognorm_scale)):
-            raise ValueError("Require finite flow_lognorm_loc and flow_lognorm_scale")
+            raise ValueError("flow_lognorm_loc and flow_lognorm_scale must be finite numbers")
         if self.flow_lognorm_scale <= 0:
-            raise ValueError("Require flow_lognorm_scale > 0")
+            raise ValueError("flow_lognorm_scale (the logit-normal std) must be positive")
         if self.train_timestep_shift <= 0:
-            raise ValueError("Require train_timestep_shift > 0")
+            raise ValueError("train_timestep_shift must be positive")
         if self.train_timestep_rescale_factor < 0:
-            raise ValueError("Require train_timestep_rescale_factor >= 0")
+            raise ValueError("train_timestep_rescale_factor cannot be negative")
         if self.train_timestep_max_shift <= 0:
-            raise ValueError("Require train_timestep_max_shift > 0")
+            raise ValueError("train_timestep_max_shift must be positive")
         if self.pretrained_transformer_path and not self.load_transformer_weights:
-            raise ValueError("pretrained_transformer_path is set but load_transformer_weights is false")
+            raise ValueError("a pretrained_transformer_path is given while load_transformer_weights is off; set one consistently with the other")
         if self.load_transformer_weights and not self.pretrained_transformer_path:
-            raise ValueError("--load_transformer_weights true requires --pretrained_transformer_path")
+            raise ValueError("load_transformer_weights is on but no pretrained_transformer_path is given")
         if self.load_transformer_weights and not os.path.exists(self.pretrained_transformer_path):
-            raise FileNotFoundError(f"--pretrained_transformer_path not found: {self.pretrained_transformer_path}")
+            raise FileNotFoundError(f"pretrained_transformer_path {self.pretrained_transformer_path} does not exist")
         if self.gradient_accumulation_steps < 1:
-            raise ValueError("--gradient_accumulation_steps must be >= 1")
+            raise ValueError("gradient_accumulation_steps must be at least 1")
 
 
 def _cli_fields():
@@ -237,7 +237,7 @@ def load_yaml_defaults(path: str, parser: argparse.ArgumentParser) -> Dict[str, 
     if obj is None:
         return {}
     if not isinstance(obj, Mapping):
-        raise ValueError(f"Training config {path} must be a YAML mapping")
+        raise ValueError(f"{path}: the training config must be a YAML mapping of sections")
     actions = {a.dest: a for a in parser._actions if a.dest not in ("help", argparse.SUPPRESS)}
     out: Dict[str, Any] = {}
 

@@ -108,14 +108,14 @@ def read_training_config(args) -> None:
         return
     import yaml
     if not os.path.isfile(args.training_config):
-        raise ValueError(f"--training_config not found: {args.training_config}")
+        raise ValueError(f"training config {args.training_config} does not exist")
     with open(args.training_config, encoding="utf-8") as f:
         doc = yaml.safe_load(f) or {}
     model, data = doc.get("model") or {}, doc.get("data") or {}
     if not isinstance(model, dict) or not isinstance(data, dict):
-        raise ValueError(f"'model' and 'data' in {args.training_config} must be mappings")
+        raise ValueError(f"{args.training_config}: the model and data sections must be YAML mappings")
     if model.get("single_stream_block_type", "mm_joint_attn") != "mm_joint_attn":
-        raise ValueError("model.single_stream_block_type must be mm_joint_attn")
+        raise ValueError("only joint-attention blocks exist here: model.single_stream_block_type must be mm_joint_attn")
     arch = dict(model.get("transformer_config_overrides") or {})
     if model.get("zero_init_modulation") is not None:
         arch["zero_init_modulation"] = model["zero_init_modulation"]
@@ -136,29 +136,29 @@ def architecture(overrides) -> dict:
 
 def prepare_jobs(args, task: str) -> List[argparse.Namespace]:
     if args.image_root is not None and not args.prompt_json:
-        raise ValueError("--image_root requires --prompt_json")
+        raise ValueError("--image_root remaps the images of a prompt file: give --prompt_json too")
     if task == "auto" and not args.prompt_json:
-        raise ValueError("--task auto requires --prompt_json")
+        raise ValueError("--task auto reads each entry's task from a prompt file: give --prompt_json")
     if args.prompt_json:
         if args.output_path or not args.output_dir or args.image_path:
-            raise ValueError("--prompt_json requires --output_dir; put reference images in the JSON, not --image_path")
+            raise ValueError("a prompt file writes one video per entry under --output_dir; reference images belong in its entries, not in --image_path")
         recs = load_inference_inputs(args.prompt_json, args.output_dir, task=task, fps=args.fps, fallback=args.video_length,
                                      shard_index=0 if task == "auto" else args.prompt_shard_index,
                                      shard_count=1 if task == "auto" else args.prompt_shard_count,
                                      default_negative=args.negative_prompt, image_root=args.image_root)
         if task == "auto":
             if args.stg_scale != 0 and any(r["task"] == "i2v" for r in recs):
-                raise ValueError("STG supports T2V only; the auto collection contains I2V entries")
+                raise ValueError("skip-layer guidance is text-to-video only, and this prompt file has image-to-video entries")
             recs = recs[args.prompt_shard_index::args.prompt_shard_count]
     else:
         if args.output_dir or (args.prompt_shard_index, args.prompt_shard_count) != (0, 1):
-            raise ValueError("--output_dir and prompt sharding require --prompt_json")
+            raise ValueError("--output_dir and --prompt_shard_* apply to prompt files: give --prompt_json")
         prompts = args.prompt if isinstance(args.prompt, list) else [args.prompt]
         refs = args.image_path if task == "i2v" else None
         if task == "i2v" and not refs:
-            raise ValueError("I2V requires --image_path (or per-entry images with --prompt_json)")
+            raise ValueError("image-to-video needs a reference image: --image_path, or per-entry images in --prompt_json")
         if refs is not None and len(refs) != len(prompts):
-            raise ValueError("the reference count must match the --prompt count")
+            raise ValueError("give one reference image per --prompt")
         recs = []
         for i, pr in enumerate(prompts):
             out = args.output_path
@@ -225,7 +225,7 @@ def dit_bytes(arch: dict, dtype) -> int:
 def generate(args, sp_group=None, sp_rank: int = 0) -> List[str]:
     task = "i2v" if args.image_path else (args.task or "t2v")
     if args.task is not None and task != args.task:
-        raise ValueError("--task conflicts with the supplied reference image")
+        raise ValueError("--task t2v was given together with a reference image")
     jobs = prepare_jobs(args, task)
     if not jobs:
         _log("no pending prompts in this shard")
@@ -332,28 +332,28 @@ def build_arg_parser() -> argparse.ArgumentParser:
 def check_args(args, argv) -> None:
     validate_sampling_extensions(args.num_inference_steps or 50, args.timestep_schedule)
     if not 0 <= args.first_step_velocity_scale <= 1:
-        raise ValueError("--first_step_velocity_scale must be in [0, 1]")
+        raise ValueError("--first_step_velocity_scale is a factor between 0 and 1")
     if not 1.0 <= args.cfg_warmup_scale < float("inf"):
-        raise ValueError("--cfg_warmup_scale must be finite and at least 1")
+        raise ValueError("--cfg_warmup_scale must be a finite number no smaller than 1")
     if args.stg_scale == 0 and not any(a == "--stg_skip_layers" or a.startswith("--stg_skip_layers=") for a in argv):
         args.stg_skip_layers = None
     if args.skip_existing and (not args.save_settings or any(getattr(args, k) is None for k in
                                                             ("num_inference_steps", "flow_shift", "guidance_scale"))):
-        raise ValueError("--skip_existing requires saved settings and explicit steps / shift / CFG")
+        raise ValueError("--skip_existing compares saved settings, so --num_inference_steps, --flow_shift and --guidance_scale must be given explicitly")
     if args.skip_existing and not (args.output_path or args.output_dir):
-        raise ValueError("--skip_existing requires a stable --output_path or --output_dir")
+        raise ValueError("--skip_existing needs a fixed --output_path or --output_dir to look for finished videos")
     if args.video_crf is not None and not 0 <= args.video_crf <= 51:
-        raise ValueError("--video_crf must be within [0, 51]")
+        raise ValueError(f"--video_crf {args.video_crf} is outside the encoder's 0..51 range")
     if args.negative_prompt_file:
         if args.negative_prompt:
-            raise ValueError("--negative_prompt and --negative_prompt_file are mutually exclusive")
+            raise ValueError("give the negative prompt once: --negative_prompt or --negative_prompt_file")
         with open(args.negative_prompt_file, encoding="utf-8") as f:
             args.negative_prompt = f.read().strip()
     read_training_config(args)
     if isinstance(args.image_path, list) and len(args.image_path) == 1 and args.image_path[0].strip().lower() == "none":
         args.image_path = None
     if args.video_height <= 0 or args.video_width <= 0 or args.fps <= 0:
-        raise ValueError("--video_height, --video_width and --fps must be positive")
+        raise ValueError("--video_height, --video_width and --fps take positive values")
     for k, v in (("num_inference_steps", 50), ("flow_shift", 5.0), ("guidance_scale", 4.0)):
         if getattr(args, k) is None and not args.skip_existing:
             setattr(args, k, v)
