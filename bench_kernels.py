@@ -286,8 +286,7 @@ def main():
     ap.add_argument("--no-library", action="store_true", help="skip the cuBLAS / SDPA comparisons")
     ap.add_argument("--attn-fwd-variant", default=None,
                     help="comma list of attention forward variants (1: in-order MMA issue, the default; 0: PV "
-                         "completion awaited before the next score GEMM; 2: in-order with two softmax warps per "
-                         "TMEM lane quarter and tile)")
+                         "completion awaited before the next score GEMM)")
     ap.add_argument("--gemm-band-mb", default=None,
                     help="comma list of GEMM M-band budgets in MB (0 = N bands only)")
     ap.add_argument("--gemm-probe", default=None,

@@ -110,39 +110,25 @@ __device__ __forceinline__ float fast_exp2(float x) {
   return y;
 }
 
-// TMEM column of K step kk (16 keys / queries = 8 packed bf16 columns) of a P-like operand written by
-// two column groups: group g's packed columns sit at [64 g, 64 g + 32), inside its own score columns.
-__device__ __forceinline__ uint32_t packed_col(int kk) { return (uint32_t)(64 * (kk >> 2) + 8 * (kk & 3)); }
-
 // ============================================================================ forward
-// GROUPS = 1: one softmax warp per TMEM lane quarter and tile (10 warps).  GROUPS = 2: two warps per
-// lane quarter and tile, each owning 64 of the 128 key columns (18 warps): the row maximum is
-// combined through shared memory (one named barrier per tile and KV step), P lands in each
-// group's own score columns, and the row sum is combined once at the end.
-template <int GROUPS>
-struct FwdShape {
-  static constexpr int THREADS = 64 + 256 * GROUPS;
-  static constexpr int RING = GROUPS == 1 ? 5 : 4;  // K/V tiles in flight (P lives in TMEM)
-  static constexpr int XCH = GROUPS == 1 ? 0 : 2 * 2 * BT * 4;  // [tile][group][row] partial maxima
-  static constexpr int SMEM = 2 * TILE_BYTES /*Q*/ + RING * TILE_BYTES + 1024 + 256 + XCH;
-};
+constexpr int FWD_THREADS = 320;
+constexpr int FWD_RING = 5;  // K/V tiles in flight (P lives in TMEM, so the smem goes to the ring)
+constexpr int FWD_SMEM = 2 * TILE_BYTES /*Q*/ + FWD_RING * TILE_BYTES + 1024 + 256;
 
 // INORDER: the next score GEMM of a tile is issued right after that tile's PV GEMM.  tcgen05.mma
 // instructions of one thread execute in issue order, so S(j+1) cannot overwrite the P(j) columns
 // before PV(j) has read them and no completion wait is needed between them (measured: ~6 % less
 // time per SM clock than awaiting PV's completion first, which the other instance does).
-template <bool INORDER, int GROUPS>
-__global__ void __launch_bounds__(FwdShape<GROUPS>::THREADS, 1)
+template <bool INORDER>
+__global__ void __launch_bounds__(FWD_THREADS, 1)
 attn_fwd_kernel(const __grid_constant__ CUtensorMap qmap, const __grid_constant__ CUtensorMap kmap,
                 const __grid_constant__ CUtensorMap vmap, const WorkItem* __restrict__ items, int L, int H,
                 float scale_log2, __nv_bfloat16* __restrict__ out, float* __restrict__ lse, const PeerRows o_peer) {
-  constexpr int FWD_RING = FwdShape<GROUPS>::RING;
   extern __shared__ uint8_t smem_raw[];
   uint8_t* smem = reinterpret_cast<uint8_t*>((reinterpret_cast<uintptr_t>(smem_raw) + 1023) & ~uintptr_t(1023));
   uint8_t* sQ = smem;                                 // 2 tiles
   uint8_t* sKV = sQ + 2 * TILE_BYTES;                 // FWD_RING tiles
   uint64_t* bars = reinterpret_cast<uint64_t*>(sKV + FWD_RING * TILE_BYTES);
-  float* xch = reinterpret_cast<float*>(reinterpret_cast<uint8_t*>(bars) + 256);  // GROUPS == 2 only
   // bars: q_full, kv_full[R], kv_empty[R], s_full[2], p_ready[2], pv_done[2]
   constexpr int RB = 1 + 2 * FWD_RING;
   uint32_t* tmem_slot = reinterpret_cast<uint32_t*>(bars + RB + 6);
@@ -169,7 +155,7 @@ attn_fwd_kernel(const __grid_constant__ CUtensorMap qmap, const __grid_constant_
     }
     for (int x = 0; x < 2; ++x) {
       mbar_init(s_full(x), 1);
-      mbar_init(p_ready(x), 4 * GROUPS);
+      mbar_init(p_ready(x), 4);
       mbar_init(pv_done(x), 1);
     }
     fence_barrier_init();
@@ -235,8 +221,7 @@ attn_fwd_kernel(const __grid_constant__ CUtensorMap qmap, const __grid_constant_
       auto issue_pv = [&](int x, uint32_t vb, bool acc) {
 #pragma unroll
         for (int kk = 0; kk < BT / 16; ++kk)
-          mma_bf16_ts(tmem + 256 + x * 128, tmem + x * 128 + (GROUPS == 2 ? packed_col(kk) : kk * 8),
-                      desc_mnmajor(vb, kk), id_pv, acc || kk > 0);
+          mma_bf16_ts(tmem + 256 + x * 128, tmem + x * 128 + kk * 8, desc_mnmajor(vb, kk), id_pv, acc || kk > 0);
         mma_commit(pv_done(x));
       };
       // S_x(j+1) overwrites the columns PV_x(j) reads P_x(j) from.  INORDER relies on the in-order
@@ -283,9 +268,7 @@ attn_fwd_kernel(const __grid_constant__ CUtensorMap qmap, const __grid_constant_
     }
   } else {
     // ------------------------------------------------------------ softmax groups
-    const int x = (warp - 2) / (4 * GROUPS);                 // 0 = tile A, 1 = tile B
-    const int g = GROUPS == 2 ? ((warp - 2) >> 2) & 1 : 0;   // key-column group
-    const int h2_begin = GROUPS == 2 ? g : 0, h2_end = GROUPS == 2 ? g + 1 : 2;  // 64-column halves owned
+    const int x = (warp - 2) >> 2;           // 0 = tile A, 1 = tile B
     const int quarter = warp & 3;            // TMEM lane quarter of this warp
     const int row = quarter * 32 + lane;     // query row within the tile
     const uint32_t lane_off = (uint32_t)(quarter * 32) << 16;
@@ -303,7 +286,7 @@ attn_fwd_kernel(const __grid_constant__ CUtensorMap qmap, const __grid_constant_
         if (__any_sync(0xffffffffu, grow)) {
           const float alpha = grow ? fast_exp2(m_used - m_new) : 1.f;  // m_used finite here (j > 0)
 #pragma unroll
-          for (int c = 2 * h2_begin; c < 2 * h2_end; ++c) {
+          for (int c = 0; c < 4; ++c) {
             uint32_t o[32];
             tmem_ld32(tO + c * 32, o);
             tmem_ld_wait();
@@ -334,9 +317,6 @@ attn_fwd_kernel(const __grid_constant__ CUtensorMap qmap, const __grid_constant_
         w[i >> 1] = pack_bf16(p0, p1);
       }
     };
-    // Every warp of a tile runs all n_kv iterations and meets the tile's named barrier in each (and
-    // once after the loop), also after a bounded wait gave up (ok == false: the work is skipped), so a
-    // timeout can never leave a partner warp waiting at the barrier.
     for (int j = 0; j < n_kv; ++j) {
       if (ok) {
         ok = mbar_wait(s_full(x), j & 1, 26);
@@ -362,7 +342,7 @@ attn_fwd_kernel(const __grid_constant__ CUtensorMap qmap, const __grid_constant_
       };
       if (ok) {
 #pragma unroll
-        for (int h2 = h2_begin; h2 < h2_end; ++h2) {
+        for (int h2 = 0; h2 < 2; ++h2) {
           uint32_t ra[32], rb[32];
           tmem_ld32(tS + h2 * 64, ra);
           tmem_ld32(tS + h2 * 64 + 32, rb);
@@ -371,24 +351,19 @@ attn_fwd_kernel(const __grid_constant__ CUtensorMap qmap, const __grid_constant_
           max_chunk(rb, h2 * 64 + 32);
         }
       }
-      float mx = fmaxf(mx0, mx1);
-      if (GROUPS == 2) {  // combine with the other column group of these rows
-        xch[(x * 2 + g) * BT + row] = mx;
-        asm volatile("bar.sync %0, 256;" ::"r"(1 + x) : "memory");
-        mx = fmaxf(mx, xch[(x * 2 + (g ^ 1)) * BT + row]);
-      }
-      if (!ok) continue;
+      const float mx = fmaxf(mx0, mx1);
+      if (!ok) break;
       const float m_new = fmaxf(m_used, mx * scale_log2);
-      if (!(ok = maybe_rescale(j, m_new))) continue;
+      if (!(ok = maybe_rescale(j, m_new))) break;
       // a chunk's P columns were read as scores in an earlier or the same chunk
 #pragma unroll
-      for (int h2 = h2_begin; h2 < h2_end; ++h2) {
+      for (int h2 = 0; h2 < 2; ++h2) {
         uint32_t ra[32], rb[32];
         tmem_ld32(tS + h2 * 64, ra);
         tmem_ld32(tS + h2 * 64 + 32, rb);
         tmem_ld_wait();
         uint32_t wa[16], wb[16];
-        const int pc = (GROUPS == 2 ? 64 : 32) * h2;  // packed P columns of this half
+        const int pc = 32 * h2;  // packed P columns of this half
         exp_chunk(ra, h2 * 64, valid, wa, l0, l1);
         tmem_st16(tS + pc, wa);
         exp_chunk(rb, h2 * 64 + 32, valid, wb, l0, l1);
@@ -400,11 +375,6 @@ attn_fwd_kernel(const __grid_constant__ CUtensorMap qmap, const __grid_constant_
       __syncwarp();
       if (lane == 0) mbar_arrive(p_ready(x));
     }
-    if (GROUPS == 2) {  // the row sum over both column groups (every warp of the tile reaches this point)
-      xch[(x * 2 + g) * BT + row] = l;
-      asm volatile("bar.sync %0, 256;" ::"r"(1 + x) : "memory");
-      l += xch[(x * 2 + (g ^ 1)) * BT + row];
-    }
     if (ok && n_kv > 0 && mbar_wait(pv_done(x), (n_kv - 1) & 1, 28)) {
       tc_fence_after();
       const int qrow = it.tile_start + x * BT + row;
@@ -413,7 +383,7 @@ attn_fwd_kernel(const __grid_constant__ CUtensorMap qmap, const __grid_constant_
       __nv_bfloat16* dst = out + ((size_t)(it.seg_start + qrow) * H + h) * D;
       __nv_bfloat16* pdst = (store && o_peer.base) ? peer_row(o_peer, it.seg_start + qrow, h) : nullptr;
 #pragma unroll
-      for (int c = 2 * h2_begin; c < 2 * h2_end; ++c) {
+      for (int c = 0; c < 4; ++c) {
         uint32_t r[32];
         tmem_ld32(tO + c * 32, r);
         tmem_ld_wait();
@@ -428,7 +398,7 @@ attn_fwd_kernel(const __grid_constant__ CUtensorMap qmap, const __grid_constant_
           }
         }
       }
-      if (store && g == 0) lse[(size_t)h * L + it.seg_start + qrow] = (m_used + log2f(l)) * kLn2;
+      if (store) lse[(size_t)h * L + it.seg_start + qrow] = (m_used + log2f(l)) * kLn2;
     } else {
       s_abort = 1;
     }
@@ -452,12 +422,7 @@ attn_fwd_kernel(const __grid_constant__ CUtensorMap qmap, const __grid_constant_
 // two-pass form needs seven and two exponentials).  TMEM: S^T/P^T/dQ^T 0..127, dP^T/dS^T 128..255,
 // dV 256..383, dK 384..511.  Warps: 0 TMA, 1 MMA, 2..5 E, 6..9 Q.  dQ accumulates in an fp32
 // buffer that a final kernel scales into bf16.
-// Warps: 0 TMA, 1 MMA, 2..5 and 10..13 elementwise (E) on query columns 0..63 and 64..127 of the
-// same key rows (two E warps per SM sub-partition, so one computes while the other waits on TMEM),
-// 6..9 dQ drain.  An E group's packed P^T / dS^T land in TMEM columns [64 g, 64 g + 32) of S^T /
-// dP^T, which only its own group reads as scores, so the groups never wait on each other; the MMA
-// reads query step kk (16 queries) at column 64 (kk / 4) + 8 (kk % 4).
-constexpr int FB_THREADS = 448;
+constexpr int FB_THREADS = 320;
 constexpr int FB_STAGE = 32 * D * 4;  // 32 query rows of fp32 dQ
 constexpr int FB_SMEM = 2 * TILE_BYTES /*K, V*/ + 2 * TILE_BYTES /*Q ring*/ + TILE_BYTES /*dO*/ +
                         TILE_BYTES /*dS^T*/ + 2 * FB_STAGE + 1024 + 256 + 2 * BT * 4;
@@ -493,7 +458,7 @@ attn_bwd_fused_kernel(const __grid_constant__ CUtensorMap qmap, const __grid_con
 
   if (threadIdx.x == 0) {
     s_abort = 0;
-    for (int i = 0; i < 14; ++i) mbar_init(B(i), i == 8 ? 8 : (i == 12 ? 4 : 1));  // ds_ready: 8 E warps, dq_drained: 4
+    for (int i = 0; i < 14; ++i) mbar_init(B(i), (i == 8 || i == 12) ? 4 : 1);  // ds_ready / dq_drained: 4 warps
     fence_barrier_init();
   }
   if (warp == 1) {
@@ -553,11 +518,11 @@ attn_bwd_fused_kernel(const __grid_constant__ CUtensorMap qmap, const __grid_con
         // dV += P^T dO_i ; dK += dS^T Q_i  (K = 128 queries, 8 columns of packed bf16 per step)
 #pragma unroll
         for (int kk = 0; kk < BT / 16; ++kk)
-          mma_bf16_ts(T_DV, T_S + packed_col(kk), desc_mnmajor(dO, kk), id_tm, (i > 0) || (kk > 0));
+          mma_bf16_ts(T_DV, T_S + kk * 8, desc_mnmajor(dO, kk), id_tm, (i > 0) || (kk > 0));
         mma_commit(B(6));  // dO slot free
 #pragma unroll
         for (int kk = 0; kk < BT / 16; ++kk)
-          mma_bf16_ts(T_DK, T_DP + packed_col(kk), desc_mnmajor(q, kk), id_tm, (i > 0) || (kk > 0));
+          mma_bf16_ts(T_DK, T_DP + kk * 8, desc_mnmajor(q, kk), id_tm, (i > 0) || (kk > 0));
         mma_commit(B(3 + slot));  // Q slot free
         mma_commit(B(10));
         if (!(ok = mbar_wait(B(10), i & 1, 48))) break;  // P^T read before dQ^T overwrites its columns
@@ -571,20 +536,19 @@ attn_bwd_fused_kernel(const __grid_constant__ CUtensorMap qmap, const __grid_con
       mma_commit(B(13));
       if (!ok) s_abort = 1;
     }
-  } else if (warp < 6 || warp >= 10) {
+  } else if (warp < 6) {
     // ------------------------------------------------ E warps: P^T and dS^T (lane = key row)
     const int quarter = warp & 3;
-    const int grp = warp >= 10 ? 1 : 0;  // query columns [64 grp, 64 grp + 64)
     const int row = quarter * 32 + lane;
     const uint32_t lane_off = (uint32_t)(quarter * 32) << 16;
     const bool row_valid = it.tile_start + row < it.seg_len;
-    const int tid = grp == 0 ? threadIdx.x - 64 : -1;  // group 0 stages the per-query LSE / Delta
+    const int tid = threadIdx.x - 64;
     bool ok = true;
     // LSE / Delta of query tile i are loaded from global memory one tile ahead (registers), so their
     // latency overlaps the previous tile's work instead of stalling every tile
     auto fetch = [&](int i, float& lv, float& dv) {
       const int qi = i * BT + tid;
-      const bool in = tid >= 0 && i < n_q && qi < it.seg_len;
+      const bool in = i < n_q && qi < it.seg_len;
       lv = in ? lse[(size_t)h * L + it.seg_start + qi] * kLog2e : 0.f;
       dv = in ? delta[(size_t)h * L + it.seg_start + qi] : 0.f;
     };
@@ -592,12 +556,10 @@ attn_bwd_fused_kernel(const __grid_constant__ CUtensorMap qmap, const __grid_con
     fetch(0, next_l, next_d);
     for (int i = 0; i < n_q; ++i) {
       const int valid_q = min(BT, it.seg_len - i * BT);
-      asm volatile("bar.sync 1, 256;" ::: "memory");
-      if (tid >= 0) {
-        s_vec[0][tid] = next_l;
-        s_vec[1][tid] = next_d;
-      }
-      asm volatile("bar.sync 1, 256;" ::: "memory");
+      asm volatile("bar.sync 1, 128;" ::: "memory");
+      s_vec[0][tid] = next_l;
+      s_vec[1][tid] = next_d;
+      asm volatile("bar.sync 1, 128;" ::: "memory");
       fetch(i + 1, next_l, next_d);
       // no break between the named barriers: after a bounded wait gave up the warp keeps meeting
       // them (skipping its work), so its group partners never wait on it forever
@@ -606,8 +568,7 @@ attn_bwd_fused_kernel(const __grid_constant__ CUtensorMap qmap, const __grid_con
       if (!ok) continue;
       tc_fence_after();
 #pragma unroll
-      for (int cg = 0; cg < 2; ++cg) {
-        const int c = 2 * grp + cg;  // 32-column chunk of the 128 query columns
+      for (int c = 0; c < 4; ++c) {
         uint32_t r[32], y[32];
         tmem_ld32(T_S + lane_off + c * 32, r);
         tmem_ld32(T_DP + lane_off + c * 32, y);
@@ -627,9 +588,9 @@ attn_bwd_fused_kernel(const __grid_constant__ CUtensorMap qmap, const __grid_con
           wp[j >> 1] = pack_bf16(pv[0], pv[1]);
           wd[j >> 1] = pack_bf16(dsv[0], dsv[1]);
         }
-        // packed columns [64 grp + 16 cg, +16) of this group's score columns, read in chunk cg or earlier
-        tmem_st16(T_S + lane_off + 64 * grp + 16 * cg, wp);
-        tmem_st16(T_DP + lane_off + 64 * grp + 16 * cg, wd);
+        // columns [16c, 16c + 16) were read in chunk c or earlier
+        tmem_st16(T_S + lane_off + c * 16, wp);
+        tmem_st16(T_DP + lane_off + c * 16, wd);
         store_row32_swizzled(sdS, row, c * 32, wd);
       }
       tmem_st_wait();
@@ -650,8 +611,7 @@ attn_bwd_fused_kernel(const __grid_constant__ CUtensorMap qmap, const __grid_con
         __nv_bfloat16* dst = pr.base ? (row_valid ? peer_row(pr, g, h) : nullptr)
                                      : (which == 0 ? dk_out : dv_out) + grow * D;
 #pragma unroll
-        for (int cg = 0; cg < 2; ++cg) {
-          const int c = 2 * grp + cg;
+        for (int c = 0; c < 4; ++c) {
           uint32_t r[32];
           tmem_ld32(tacc + c * 32, r);
           tmem_ld_wait();
@@ -682,38 +642,29 @@ attn_bwd_fused_kernel(const __grid_constant__ CUtensorMap qmap, const __grid_con
     for (int i = 0; i < n_q; ++i) {
       if (ok && !(ok = mbar_wait(B(11), i & 1, 52))) s_abort = 1;
       if (ok) tc_fence_after();
-      // two halves of 64 query columns (the 14-warp CTA caps registers at 128 per thread)
+      uint32_t r[4][32];
+      if (ok) {
 #pragma unroll
-      for (int hf = 0; hf < 2; ++hf) {
-        uint32_t r[2][32];
+        for (int c = 0; c < 4; ++c) tmem_ld32(T_S + lane_off + c * 32, r[c]);
+        tmem_ld_wait();
+        tc_fence_before();
+        __syncwarp();
+        if (lane == 0) mbar_arrive(B(12));  // the S^T columns may be rewritten
+      }
+#pragma unroll
+      for (int c = 0; c < 4; ++c) {
+        float* st = reinterpret_cast<float*>(sStage + (n_used & 1) * FB_STAGE);
+        if (n_used >= 2 && qt == 0) bulk_wait_read<1>();
+        asm volatile("bar.sync 2, 128;" ::: "memory");
         if (ok) {
-          tmem_ld32(T_S + lane_off + hf * 64, r[0]);
-          tmem_ld32(T_S + lane_off + hf * 64 + 32, r[1]);
-          tmem_ld_wait();
-          if (hf == 1) {
-            tc_fence_before();
-            __syncwarp();
-            if (lane == 0) mbar_arrive(B(12));  // the S^T columns may be rewritten
-          }
-        }
 #pragma unroll
-        for (int c2 = 0; c2 < 2; ++c2) {
-          const int c = 2 * hf + c2;
-          float* st = reinterpret_cast<float*>(sStage + (n_used & 1) * FB_STAGE);
-          if (n_used >= 2 && qt == 0) bulk_wait_read<1>();
-          asm volatile("bar.sync 2, 128;" ::: "memory");
-          if (ok) {
-#pragma unroll
-            for (int qq = 0; qq < 32; ++qq) st[qq * D + d] = __uint_as_float(r[c2][qq]);
-          }
-          fence_async_shared();
-          asm volatile("bar.sync 2, 128;" ::: "memory");
-          if (qt == 0 && ok) {
-            tma_reduce_add_2d(&dqmap, smem_u32(st), col, it.seg_start + i * BT + c * 32);
-          }
-          if (qt == 0) bulk_commit();
-          ++n_used;
+          for (int qq = 0; qq < 32; ++qq) st[qq * D + d] = __uint_as_float(r[c][qq]);
         }
+        fence_async_shared();
+        asm volatile("bar.sync 2, 128;" ::: "memory");
+        if (qt == 0 && ok) tma_reduce_add_2d(&dqmap, smem_u32(st), col, it.seg_start + i * BT + c * 32);
+        if (qt == 0) bulk_commit();
+        ++n_used;
       }
     }
     if (qt == 0) bulk_wait_all();
@@ -862,13 +813,12 @@ const char* run_bwd_single_pass(const void* q, const void* k, const void* v, con
   return cudaGetLastError() == cudaSuccess ? nullptr : "attention backward launch failed";
 }
 
-// Forward kernel: 1 = in-order MMA issue (default), 0 = PV completion awaited before the next score
-// GEMM, 2 = in-order with two softmax warps per lane quarter and tile.
+// Forward kernel: 1 = in-order MMA issue (default), 0 = PV completion awaited before the next score GEMM.
 int g_fwd_inorder = 1;
 
 }  // namespace attn
 
-void attn_set_forward_variant(int v) { attn::g_fwd_inorder = v < 0 ? 0 : (v > 2 ? 2 : v); }
+void attn_set_forward_variant(int v) { attn::g_fwd_inorder = v ? 1 : 0; }
 int attn_get_variant(int backward) { return backward ? 0 : attn::g_fwd_inorder; }
 
 const char* launch_attn_fwd(const void* q, const void* k, const void* v, const int* items, int n_items, int L, int H,
@@ -884,20 +834,17 @@ const char* launch_attn_fwd(const void* q, const void* k, const void* v, const i
   if ((e = make_qkv_map(&qm, q, L, H)) || (e = make_qkv_map(&km, k, L, H)) || (e = make_qkv_map(&vm, v, L, H))) return e;
   typedef void (*FwdKernel)(CUtensorMap, CUtensorMap, CUtensorMap, const WorkItem*, int, int, float, __nv_bfloat16*,
                             float*, PeerRows);
-  static const FwdKernel variants[3] = {attn_fwd_kernel<false, 1>, attn_fwd_kernel<true, 1>,
-                                        attn_fwd_kernel<true, 2>};
-  static const int threads[3] = {FwdShape<1>::THREADS, FwdShape<1>::THREADS, FwdShape<2>::THREADS};
-  static const int smem[3] = {FwdShape<1>::SMEM, FwdShape<1>::SMEM, FwdShape<2>::SMEM};
-  static bool attr[3] = {};
+  static const FwdKernel variants[2] = {attn_fwd_kernel<false>, attn_fwd_kernel<true>};
+  static bool attr[2] = {};
   const int var = g_fwd_inorder;
   if (!attr[var]) {
-    if (cudaFuncSetAttribute(variants[var], cudaFuncAttributeMaxDynamicSharedMemorySize, smem[var]) != cudaSuccess)
+    if (cudaFuncSetAttribute(variants[var], cudaFuncAttributeMaxDynamicSharedMemorySize, FWD_SMEM) != cudaSuccess)
       return "attention: cannot set smem size";
     attr[var] = true;
   }
   dim3 grid(n_items, H);
   auto kern = variants[var];
-  kern<<<grid, threads[var], smem[var], s>>>(qm, km, vm, reinterpret_cast<const WorkItem*>(items), L, H, scale * kLog2e,
+  kern<<<grid, FWD_THREADS, FWD_SMEM, s>>>(qm, km, vm, reinterpret_cast<const WorkItem*>(items), L, H, scale * kLog2e,
                                            (__nv_bfloat16*)out, lse, opr);
   return cudaGetLastError() == cudaSuccess ? nullptr : "attention forward launch failed";
 }
