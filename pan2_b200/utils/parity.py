@@ -1,7 +1,8 @@
 """Multi-GPU correctness check of the fused peer-memory paths against their NCCL baselines.
 
 Runs inside an already initialised job (every rank calls it) on a small model of the real block
-structure (2 joint blocks, hidden 512, 4 heads of 128): one training step with each path switched on
+structure (2 joint blocks, 4 heads of 128, or as many as context parallelism needs): one training
+step with each path switched on
 and off, the others held fixed, and reports the largest relative differences:
 
 * ``fsdp_peer``: parameter gather + gradient reduce-scatter over peer memory (``PAN_PEER_COMM``)
@@ -47,11 +48,17 @@ def _rel(a, b) -> float:
     return num / (den + 1e-30)
 
 
+def small_arch(cp: int = 1) -> dict:
+    """The small model, with as many 128-wide heads as Ulysses needs (a multiple of ``cp``, at least 4)."""
+    heads = -(-max(4, cp) // cp) * cp
+    return dict(SMALL_ARCH, num_attention_heads=heads, hidden_size=heads * 128)
+
+
 def _one_step(device, group, rank: int, layout=None, cp: int = 1) -> Dict:
     from ..data.synthetic import batch_to_device, synthetic_packed_batch
     from ..ops._ext import ext
     from ..training.engine import OptimConfig, TrainEngine
-    eng = TrainEngine(SMALL_ARCH, device, group=group, seed=7, optim=OptimConfig(lr=1e-3), offload="off")
+    eng = TrainEngine(small_arch(cp), device, group=group, seed=7, optim=OptimConfig(lr=1e-3), offload="off")
     if cp > 1:
         from ..data.cp_batch import broadcast_and_split
         eng.set_context_parallel(layout.cp_group, cp, layout.cp_rank)
