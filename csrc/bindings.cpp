@@ -648,8 +648,18 @@ void ns_trace(torch::Tensor R, torch::Tensor out) {
   launch_trace(R.data_ptr<float>(), R.size(0), R.size(1), out.data_ptr<float>(), stream());
   check_launch(nullptr, "ns_trace");
 }
+// The two per-element passes below move 16-byte vectors: contiguous [B, M, M] with M * M % 8 == 0
+static void check_gram_batch(const torch::Tensor& t, torch::ScalarType dt, const char* what) {
+  TORCH_CHECK(t.scalar_type() == dt && t.dim() == 3 && t.is_contiguous() && t.size(1) == t.size(2), what,
+              " must be a contiguous [B, M, M] tensor of the expected dtype");
+  TORCH_CHECK((t.size(1) * t.size(2)) % 8 == 0, what, ": M * M must be a multiple of 8");
+  TORCH_CHECK((reinterpret_cast<uintptr_t>(t.data_ptr()) & 15) == 0, what, " must be 16-byte aligned");
+}
 void ns_gram_normalize(torch::Tensor R, torch::Tensor norm2, double eps, torch::Tensor Rn) {
   const at::cuda::CUDAGuard guard(R.device());
+  check_gram_batch(R, torch::kFloat32, "R");
+  check_gram_batch(Rn, torch::kBFloat16, "Rn");
+  TORCH_CHECK(Rn.sizes() == R.sizes() && norm2.numel() == R.size(0), "Rn / norm2 do not match R");
   launch_gram_normalize(R.data_ptr<float>(), norm2.data_ptr<float>(), R.size(0), R.size(1), (float)eps, Rn.data_ptr(),
                         stream());
   check_launch(nullptr, "ns_gram_normalize");
@@ -661,6 +671,8 @@ void ns_add_diag(torch::Tensor Z, double a) {
 }
 void ns_scale_by_invnorm(torch::Tensor Q, torch::Tensor norm2, double eps) {
   const at::cuda::CUDAGuard guard(Q.device());
+  check_gram_batch(Q, torch::kBFloat16, "Q");
+  TORCH_CHECK(norm2.numel() == Q.size(0), "norm2 does not match Q");
   launch_scale_by_invnorm(Q.data_ptr(), norm2.data_ptr<float>(), Q.size(0), Q.size(1), (float)eps, stream());
   check_launch(nullptr, "ns_scale_by_invnorm");
 }

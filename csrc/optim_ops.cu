@@ -183,14 +183,26 @@ __global__ void trace_kernel(const float* __restrict__ R, int M, long long bstri
   }
 }
 
-// Rn[b] = bf16(R[b] / max(norm2[b], eps^2));   Q-initialisation helper: Q = Z + a*I (in place on Z)
+// Rn[b] = bf16(R[b] / max(norm2[b], eps^2)).  `M * M` is a multiple of 8 (M of the Gram matrices
+// is a multiple of 8), so each thread moves 32 bytes of fp32 in and one 16-byte bf16 vector out; the
+// grid's y dimension walks the batch and x fills the SMs.
 __global__ void gram_normalize_kernel(const float* __restrict__ R, const float* __restrict__ norm2, int M,
                                       float eps, __nv_bfloat16* __restrict__ Rn) {
   const int b = blockIdx.y;
   const float s = 1.f / fmaxf(norm2[b], eps * eps);
   const size_t off = (size_t)b * M * M;
-  for (int i = blockIdx.x * blockDim.x + threadIdx.x; i < M * M; i += gridDim.x * blockDim.x)
-    Rn[off + i] = __float2bfloat16_rn(R[off + i] * s);
+  const size_t n8 = (size_t)M * M / 8;
+  const float4* src = reinterpret_cast<const float4*>(R + off);
+  uint4* dst = reinterpret_cast<uint4*>(Rn + off);
+  for (size_t i = (size_t)blockIdx.x * blockDim.x + threadIdx.x; i < n8; i += (size_t)gridDim.x * blockDim.x) {
+    const float4 a = src[2 * i], c = src[2 * i + 1];
+    uint4 o;
+    o.x = pack_bf16(a.x * s, a.y * s);
+    o.y = pack_bf16(a.z * s, a.w * s);
+    o.z = pack_bf16(c.x * s, c.y * s);
+    o.w = pack_bf16(c.z * s, c.w * s);
+    dst[i] = o;
+  }
 }
 
 __global__ void add_diag_kernel(__nv_bfloat16* __restrict__ Z, int M, float a) {
@@ -201,14 +213,30 @@ __global__ void add_diag_kernel(__nv_bfloat16* __restrict__ Z, int M, float a) {
   }
 }
 
-// Q[b] *= 1 / sqrt(max(norm2[b], eps^2))
+// Q[b] *= 1 / sqrt(max(norm2[b], eps^2)), eight bf16 per 16-byte access (M * M % 8 == 0)
 __global__ void scale_by_invnorm_kernel(__nv_bfloat16* __restrict__ Q, const float* __restrict__ norm2, int M,
                                         float eps) {
   const int b = blockIdx.y;
   const float s = rsqrtf(fmaxf(norm2[b], eps * eps));
-  const size_t off = (size_t)b * M * M;
-  for (int i = blockIdx.x * blockDim.x + threadIdx.x; i < M * M; i += gridDim.x * blockDim.x)
-    Q[off + i] = __float2bfloat16_rn(__bfloat162float(Q[off + i]) * s);
+  uint4* q = reinterpret_cast<uint4*>(Q + (size_t)b * M * M);
+  const size_t n8 = (size_t)M * M / 8;
+  for (size_t i = (size_t)blockIdx.x * blockDim.x + threadIdx.x; i < n8; i += (size_t)gridDim.x * blockDim.x) {
+    uint4 v = q[i];
+    uint32_t* w = reinterpret_cast<uint32_t*>(&v);
+#pragma unroll
+    for (int j = 0; j < 4; ++j) {
+      const float2 f = __bfloat1622float2(*reinterpret_cast<const __nv_bfloat162*>(&w[j]));
+      w[j] = pack_bf16(f.x * s, f.y * s);
+    }
+    q[i] = v;
+  }
+}
+
+// CTAs along x for a batched per-matrix pass of n8 16-byte vectors: about 16 CTAs per SM in total
+inline dim3 batched_grid(int batch, size_t n8) {
+  size_t per = (148 * 16 + batch - 1) / batch;
+  size_t need = (n8 + 255) / 256;
+  return dim3((unsigned)(need < per ? (need > 0 ? need : 1) : per), batch);
 }
 
 inline int grid_for(size_t n) {
@@ -267,16 +295,14 @@ void launch_trace(const float* R, int batch, int M, float* out, cudaStream_t s) 
   trace_kernel<<<batch, 256, 0, s>>>(R, M, (long long)M * M, out);
 }
 void launch_gram_normalize(const float* R, const float* norm2, int batch, int M, float eps, void* Rn, cudaStream_t s) {
-  dim3 grid((M * M + 255) / 256 < 64 ? (M * M + 255) / 256 : 64, batch);
-  gram_normalize_kernel<<<grid, 256, 0, s>>>(R, norm2, M, eps, (__nv_bfloat16*)Rn);
+  gram_normalize_kernel<<<batched_grid(batch, (size_t)M * M / 8), 256, 0, s>>>(R, norm2, M, eps, (__nv_bfloat16*)Rn);
 }
 void launch_add_diag(void* Z, int batch, int M, float a, cudaStream_t s) {
   dim3 grid((M + 255) / 256, batch);
   add_diag_kernel<<<grid, 256, 0, s>>>((__nv_bfloat16*)Z, M, a);
 }
 void launch_scale_by_invnorm(void* Q, const float* norm2, int batch, int M, float eps, cudaStream_t s) {
-  dim3 grid((M * M + 255) / 256 < 64 ? (M * M + 255) / 256 : 64, batch);
-  scale_by_invnorm_kernel<<<grid, 256, 0, s>>>((__nv_bfloat16*)Q, norm2, M, eps);
+  scale_by_invnorm_kernel<<<batched_grid(batch, (size_t)M * M / 8), 256, 0, s>>>((__nv_bfloat16*)Q, norm2, M, eps);
 }
 
 }  // namespace pan

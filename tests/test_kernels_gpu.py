@@ -235,3 +235,26 @@ def test_ln_modulate_forward_wide_rows_many_segments():
         ref[a:b] = (xf[a:b] - mean[a:b]) * rstd[a:b] * (1 + scale[s].float()) + shift[s].float()
     assert (y.float() - ref).abs().max().item() < 3e-2
     assert y[bounds[-1]:].abs().max().item() == 0
+
+
+@pytest.mark.parametrize("B,M", [(1, 5120), (3, 200), (4, 36)])
+def test_newton_schulz_normalise_and_rescale(B, M):
+    """The two per-element Newton-Schulz passes equal the fp32 formulas rounded once to bf16:
+    Rn = bf16(R / max(tr R, eps^2)) and Q <- bf16(Q / sqrt(max(tr R, eps^2)))."""
+    E = ext()
+    torch.manual_seed(B * M)
+    eps = 1e-7
+    R = torch.randn(B, M, M, device="cuda")
+    norm2 = torch.empty(B, device="cuda")
+    E.ns_trace(R, norm2)
+    ref_n2 = torch.diagonal(R, dim1=-2, dim2=-1).sum(-1)
+    assert torch.allclose(norm2, ref_n2, rtol=1e-4, atol=1e-3)
+    norm2.abs_()
+    Rn = torch.empty(B, M, M, device="cuda", dtype=torch.bfloat16)
+    E.ns_gram_normalize(R, norm2, eps, Rn)
+    den = norm2.clamp_min(eps * eps).view(-1, 1, 1)
+    assert torch.equal(Rn, (R * (1.0 / den)).to(torch.bfloat16))
+    Q = bf(B, M, M)
+    want = (Q.float() * torch.rsqrt(den)).to(torch.bfloat16)
+    E.ns_scale_by_invnorm(Q, norm2, eps)
+    assert (Q.float() - want.float()).abs().max().item() <= 2 ** -7 * want.float().abs().max().item()
