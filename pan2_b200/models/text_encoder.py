@@ -8,6 +8,12 @@ caption as the user turn, the assistant turn opened); Qwen encodes the whole tem
 only the rows after the user-turn header (``prefix_len`` tokens, measured once from the tokenizer)
 reach the DiT.  An empty caption becomes one space, so the user turn is never empty.
 
+A batch of captions is encoded as ONE packed sequence (:class:`~pan2_b200.models.qwen_packed.
+PackedQwenForward`: per-caption positions, causal attention within each caption, the GatedDeltaNet
+convolution and recurrence restarted at every caption start), so no GEMM of the 9B encoder spends
+work on padding rows -- the reference's packed encode (``dataset/packed_dataloader.py:225-244``).
+A model without Qwen3.5's layer structure falls back to a right-padded batch with an attention mask.
+
 The model and tokenizer come from a Hugging Face id or a local folder (``transformers``); they can
 also be injected (tests, other checkpoints).  :class:`QwenCaptionCodec` is the training loader's
 interface (:class:`~pan2_b200.data.items.CaptionCodec`) and also serves generation through
@@ -22,6 +28,7 @@ import torch
 import torch.nn as nn
 
 from ..data.items import Caption, CaptionCodec
+from .qwen_packed import PackedQwenForward
 
 DEFAULT_TEXT_ENCODER = "Qwen/Qwen3.5-9B"
 SYSTEM_PROMPT = "You are a helpful assistant. Generate the video with the following instructions."
@@ -72,6 +79,7 @@ class QwenCaptionCodec(CaptionCodec):
         self.max_caption_tokens = int(max_caption_tokens)
         self._prefix: Optional[int] = None
         self.embed_dim = embed_dim or int(getattr(getattr(self.model, "config", None), "hidden_size", 4096))
+        self._packed = PackedQwenForward(self.model) if PackedQwenForward.supports(self.model) else None
 
     def to(self, device) -> "QwenCaptionCodec":
         """Move the language model (generation offloading parks it on the CPU between prompts)."""
@@ -105,8 +113,27 @@ class QwenCaptionCodec(CaptionCodec):
                        cropped_length=int(ids.numel()) - self.prefix_len, token_ids=ids)
 
     # ---- features
+    def _model_device(self):
+        return next(self.model.parameters()).device
+
     @torch.no_grad()
-    def _forward(self, captions: Sequence[Caption], device) -> Tuple[torch.Tensor, torch.Tensor]:
+    def _caption_rows(self, captions: Sequence[Caption]) -> Tuple[torch.Tensor, list]:
+        """Hidden states of every caption's cropped span, packed in order (on the model's device),
+        and the span lengths."""
+        if self._packed is None:
+            hidden, _ = self._padded(captions, self._model_device())
+            rows = [hidden[i, :c.cropped_length] for i, c in enumerate(captions)]
+            return torch.cat(rows, 0), [c.cropped_length for c in captions]
+        lengths = [int(c.full_length) for c in captions]
+        hidden = self._packed(torch.cat([c.token_ids.view(-1)[:n] for c, n in zip(captions, lengths)]), lengths)
+        rows, a = [], 0
+        for c, n in zip(captions, lengths):
+            rows.append(hidden[a + c.prefix_len:a + n])
+            a += n
+        return torch.cat(rows, 0), [c.cropped_length for c in captions]
+
+    @torch.no_grad()
+    def _padded(self, captions: Sequence[Caption], device) -> Tuple[torch.Tensor, torch.Tensor]:
         pad = self.tokenizer.pad_token_id if self.tokenizer.pad_token_id is not None else self.tokenizer.eos_token_id
         L = max(c.full_length for c in captions)
         ids = torch.full((len(captions), L), pad, dtype=torch.long)
@@ -114,7 +141,7 @@ class QwenCaptionCodec(CaptionCodec):
         for i, c in enumerate(captions):
             ids[i, :c.full_length] = c.token_ids
             mask[i, :c.full_length] = 1
-        dev = next(self.model.parameters()).device
+        dev = self._model_device()
         hidden = self.model(input_ids=ids.to(dev), attention_mask=mask.to(dev), use_cache=False).last_hidden_state
         p = self.prefix_len
         return hidden[:, p:].to(device), mask[:, p:].to(device)
@@ -122,14 +149,24 @@ class QwenCaptionCodec(CaptionCodec):
     def embed(self, captions: Sequence[Caption], device) -> torch.Tensor:
         if not captions:
             return torch.zeros(0, self.embed_dim, device=device)
-        hidden, mask = self._forward(captions, device)
-        return torch.cat([hidden[i, :c.cropped_length] for i, c in enumerate(captions)], 0)
+        rows, _ = self._caption_rows(captions)
+        return rows.to(device)
 
     def encode(self, texts, device=None) -> Tuple[torch.Tensor, torch.Tensor]:
         """Generation: ``(embeds [B, L, D], mask [B, L])`` of the caption spans, right-padded."""
         texts = [texts] if isinstance(texts, str) else list(texts)
         caps = [self.tokenize(t, self.max_caption_tokens) for t in texts]
-        return self._forward(caps, device if device is not None else next(self.model.parameters()).device)
+        device = device if device is not None else self._model_device()
+        rows, lengths = self._caption_rows(caps)
+        L = max(lengths)
+        out = rows.new_zeros(len(caps), L, rows.shape[-1])
+        mask = torch.zeros(len(caps), L, dtype=torch.long)
+        a = 0
+        for i, n in enumerate(lengths):
+            out[i, :n] = rows[a:a + n]
+            mask[i, :n] = 1
+            a += n
+        return out.to(device), mask.to(device)
 
 
 class HashTextEncoder:

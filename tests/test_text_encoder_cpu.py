@@ -1,6 +1,14 @@
-"""Caption codec logic (chat template, prefix crop, truncation, padding) with an injected
-character-level tokenizer and a toy language model: the Qwen weights are not needed to check which
-token rows reach the DiT."""
+"""Caption codec logic and the packed Qwen3.5 encode.
+
+* chat template, prefix crop, truncation and padding, with an injected character-level tokenizer and
+  a toy language model (the Qwen weights are not needed to check which token rows reach the DiT);
+* with a tiny random Qwen3.5 from transformers: the gated delta rule over a packed,
+  caption-restarted chunk grid equals the token-by-token recurrence of its definition; the packed
+  forward of several captions equals the Hugging Face model run on each caption alone (captions
+  shorter than, equal to and longer than one 64-token chunk); ``embed`` / ``encode`` agree on the
+  packed and the right-padded paths.
+"""
+import pytest
 import torch
 import torch.nn as nn
 
@@ -64,3 +72,94 @@ def test_prefix_crop_truncation_and_padding():
     assert emb[short.cropped_length, 0].item() == 2 + ord("x")
     e, m = codec.encode(["a red fox", "x" * 200])
     assert e.shape[0] == 2 and m[0].sum().item() == short.cropped_length and m[1].sum().item() == 40
+
+
+def _qwen_modules():
+    transformers = pytest.importorskip("transformers")
+    mq = pytest.importorskip("transformers.models.qwen3_5.modeling_qwen3_5")
+    return transformers, mq
+
+
+LENGTHS = [5, 70, 130, 1, 64, 3]
+
+
+def tiny_qwen(seed=0):
+    transformers, mq = _qwen_modules()
+    torch.manual_seed(seed)
+    cfg = transformers.Qwen3_5TextConfig(
+        vocab_size=512, hidden_size=64, intermediate_size=128, num_hidden_layers=4, num_attention_heads=4,
+        num_key_value_heads=2, head_dim=16, linear_num_value_heads=4, linear_num_key_heads=2,
+        linear_key_head_dim=16, linear_value_head_dim=8, linear_conv_kernel_dim=4,
+        layer_types=["linear_attention", "full_attention", "linear_attention", "full_attention"])
+    cfg._attn_implementation = "sdpa"
+    m = mq.Qwen3_5TextModel(cfg).eval()
+    with torch.no_grad():
+        for p in m.parameters():
+            p.add_(torch.randn_like(p) * 0.2)
+    return m
+
+
+def _recurrence(q, k, v, beta, g):
+    """Token-by-token gated delta rule of one caption: q, k [T, H, dk], v [T, H, dv], beta, g [T, H]."""
+    T, H, dk = q.shape
+    q = torch.nn.functional.normalize(q, dim=-1, eps=1e-3) * dk ** -0.5
+    k = torch.nn.functional.normalize(k, dim=-1, eps=1e-3)
+    S = torch.zeros(H, dk, v.shape[-1], dtype=torch.float64)
+    out = []
+    for t in range(T):
+        S = S * torch.exp(g[t]).view(H, 1, 1)
+        pred = torch.einsum("hk,hkv->hv", k[t], S)
+        S = S + torch.einsum("hk,hv->hkv", k[t], beta[t].view(H, 1) * (v[t] - pred))
+        out.append(torch.einsum("hk,hkv->hv", q[t], S))
+    return torch.stack(out)
+
+
+def test_chunked_delta_rule_equals_the_recurrence():
+    from pan2_b200.models.qwen_packed import _layout, gated_delta_rule_packed
+    torch.manual_seed(1)
+    lens = [3, 64, 65, 150]
+    T, H, dk, dv = sum(lens), 3, 8, 5
+    q, k = torch.randn(T, H, dk, dtype=torch.float64), torch.randn(T, H, dk, dtype=torch.float64)
+    v = torch.randn(T, H, dv, dtype=torch.float64)
+    beta = torch.rand(T, H, dtype=torch.float64)
+    g = -torch.rand(T, H, dtype=torch.float64) * 0.3
+    got = gated_delta_rule_packed(q, k, v, beta, g, _layout(lens, 64, "cpu"))
+    a = 0
+    for n in lens:
+        ref = _recurrence(q[a:a + n], k[a:a + n], v[a:a + n], beta[a:a + n], g[a:a + n])
+        assert (got[a:a + n].double() - ref).abs().max() < 1e-4 * ref.abs().max(), n
+        a += n
+
+
+def test_packed_forward_equals_each_caption_alone():
+    from pan2_b200.models.qwen_packed import PackedQwenForward
+    m = tiny_qwen()
+    ids = [torch.randint(0, 512, (n,)) for n in LENGTHS]
+    packed = PackedQwenForward(m)(torch.cat(ids), LENGTHS)
+    a = 0
+    for n, i in zip(LENGTHS, ids):
+        with torch.no_grad():
+            ref = m(input_ids=i[None], use_cache=False).last_hidden_state[0]
+        assert (packed[a:a + n] - ref).abs().max() < 1e-4 * ref.abs().max(), n
+        a += n
+
+
+def test_codec_packed_and_padded_paths_agree():
+    m = tiny_qwen(2)
+    codec = QwenCaptionCodec(model=m, tokenizer=CharTokenizer(), max_caption_tokens=90, embed_dim=64)
+    assert codec._packed is not None
+    texts = ["a red fox", "", "the camera pans slowly over a wide river valley at dawn, mist rising " * 2, "x"]
+    caps = [codec.tokenize(t, 90) for t in texts]
+    rows = codec.embed(caps, "cpu")
+    assert rows.shape == (sum(c.cropped_length for c in caps), 64)
+    a = 0
+    for c in caps:
+        with torch.no_grad():
+            ref = m(input_ids=c.token_ids[None], use_cache=False).last_hidden_state[0, c.prefix_len:]
+        assert (rows[a:a + c.cropped_length] - ref).abs().max() < 1e-4 * ref.abs().max()
+        a += c.cropped_length
+    emb, mask = codec.encode(texts, device="cpu")
+    codec._packed = None
+    emb_pad, mask_pad = codec.encode(texts, device="cpu")
+    assert torch.equal(mask, mask_pad)
+    assert (emb - emb_pad).abs().max() < 1e-4 * emb_pad.abs().max()
