@@ -1,7 +1,7 @@
 """Fused peer-memory collectives against their NCCL baselines, as fractions of the NVLink roofline.
 
     torchrun --nnodes=1 --nproc-per-node N --master-addr 127.0.0.1 --master-port P bench_comm.py \
-        [--path gather|reduce|muon|ulysses|all] [--iters K] [--warmup W]
+        [--path gather|adaln|reduce|muon|ulysses|all] [--iters K] [--warmup W]
 
 One rank per GPU of one node (N = 2, 4 or 8).  The units are the 29B model's (one joint block of
 config/pretrain_29B_720p.yaml plus the root unit), built by the training engine itself, so every
@@ -10,6 +10,10 @@ number times the code path a training step runs:
 * ``gather`` (path a): one block's FSDP parameter all-gather fused with the shard -> natural-layout
   unpack (``peer_gather``: each rank pulls its peers' bf16 ``hi`` rows out of symmetric memory)
   against NCCL ``all_gather_into_tensor`` followed by the unpack copies;
+* ``adaln`` (path a, fused into the consuming op): the forward's AdaLN modulation of one block,
+  ``a [5, H] @ W^T + b`` with ``W [6H, H]`` read row by row from the owning peers inside the
+  projection kernel (``peer_gemv``, ``PAN_PEER_ADALN=1``), against gathering ``W`` (``peer_gather`` of
+  that slot) and projecting the local copy with the GEMM;
 * ``reduce`` (path b): one block's gradient reduce-scatter fused with the bf16 -> fp32 cast
   (device barrier + ``peer_reduce``) against the pack-with-cast copies + NCCL ``reduce_scatter_tensor``;
 * ``muon`` (path d): the optimizer step with the distributed Muon exchange through peer memory
@@ -18,7 +22,7 @@ number times the code path a training step runs:
   ranks, the all-to-alls folded into ``qkv_post`` / attention (``PAN_CP_FUSED=1``) against NCCL
   all-to-alls (``PAN_CP_FUSED=0``), on one 5 s 720p clip (18,480 + 512 tokens).
 
-Roofline (gather, reduce): the bytes that must cross NVLink into each GPU divided by the measured
+Roofline (gather, adaln, reduce): the bytes that must cross NVLink into each GPU divided by the measured
 peer-copy bandwidth, 770 GB/s per direction (900 nominal); the compute of these two paths (an
 unpack, a cast and a sum) is far below its memory time, so the link time is the bound.  For muon
 and ulysses the line reports the A/B step times and the link time of the exchanged bytes.
@@ -42,7 +46,7 @@ LINK_GBS = 770.0  # measured peer copy, per direction per GPU
 
 def parse():
     ap = argparse.ArgumentParser()
-    ap.add_argument("--path", default="all", choices=("gather", "reduce", "muon", "ulysses", "all"))
+    ap.add_argument("--path", default="all", choices=("gather", "adaln", "reduce", "muon", "ulysses", "all"))
     ap.add_argument("--iters", type=int, default=10)
     ap.add_argument("--warmup", type=int, default=3)
     ap.add_argument("--config", default=os.path.join(ROOT, "config", "pretrain_29B_720p.yaml"))
@@ -91,6 +95,7 @@ def bench_gather_reduce(args, arch, device, rank, world, paths):
     from pan2_b200.parallel.sharded import pack_rows, unpack_rows
     from pan2_b200.training.engine import OptimConfig, TrainEngine
     os.environ["PAN_PEER_COMM"] = "1"
+    os.environ["PAN_PEER_ADALN"] = "1" if "adaln" in paths else "0"
     eng = TrainEngine(arch, device, group=dist.group.WORLD, seed=3, optim=OptimConfig(lr=1e-4), offload="off")
     sh = eng.sharded
     if not eng.peer_comm:
@@ -123,6 +128,41 @@ def bench_gather_reduce(args, arch, device, rank, world, paths):
                      "peer_ms": round(t_peer, 4), "nccl_ms": round(t_nccl, 4),
                      "roofline_ms": round(roof_ms, 4), "peer_of_roofline": round(roof_ms / t_peer, 3),
                      "nccl_of_roofline": round(roof_ms / t_nccl, 3), "equal": bool(torch.equal(full_p, full_n))})
+    if "adaln" in paths and u.index in sh.adaln:
+        from pan2_b200.ops.gemm import linear
+        from pan2_b200.parallel.symm import GatherPlan
+        proj, bias_slot = sh.adaln[u.index]
+        w = proj.slot
+        full = torch.empty(u.numel_full, dtype=bf, device=device)
+        sh.gather_plans[u.index].run(sh.hi_mem, full)  # bias (and, for the reference result, W)
+        bias = u.slot_full(full, bias_slot)
+        from types import SimpleNamespace
+        hi_off = proj.w_off - w.shard_off  # the unit's element offset in the hi buffer
+        w_plan = GatherPlan(SimpleNamespace(slots=[w]), world, hi_off, device)  # gathers W alone
+        gen = torch.Generator(device=device).manual_seed(5)
+        a = torch.randn(5, w.cols, generator=gen, device=device).to(bf)
+        y_p = torch.empty(5, w.rows, dtype=bf, device=device)
+
+        def fused():
+            proj.run(sh.hi_mem, a, bias, y_p)
+
+        def gathered():
+            w_plan.run(sh.hi_mem, full)
+            return linear(a, u.slot_full(full, w), bias)
+
+        t_fused = _timed(fused, args.iters, args.warmup, device)
+        t_gath = _timed(gathered, args.iters, args.warmup, device)
+        y_g = gathered()
+        rel = ((y_p.float() - y_g.float()).abs().max() / y_g.float().abs().max().clamp_min(1e-30)).item()
+        w_bytes = w.rows * w.cols * 2
+        link_bytes = (world - 1) / world * w_bytes
+        roof_ms = link_bytes / (LINK_GBS * 1e9) * 1e3
+        _emit(rank, {"path": "a: AdaLN projection reading the weight from the peers (peer_gemv)", "n_gpus": world,
+                     "unit": "blocks.0.modulation.linear", "weight_shape": [w.rows, w.cols], "weight_bytes": w_bytes,
+                     "link_bytes_per_gpu": int(link_bytes), "fused_ms": round(t_fused, 4),
+                     "gather_then_gemm_ms": round(t_gath, 4), "roofline_ms": round(roof_ms, 4),
+                     "fused_of_roofline": round(roof_ms / t_fused, 3),
+                     "gather_then_gemm_of_roofline": round(roof_ms / t_gath, 3), "max_rel_diff": rel})
     if "reduce" in paths:
         slot = 1
         g = sh.grad_mem.view(slot * sh.slot_elems * 2, u.numel_full, bf)
@@ -244,11 +284,11 @@ def main():
     device = torch.device("cuda", local)
     torch.cuda.set_device(device)
     arch = _arch(args.config)
-    paths = ("gather", "reduce", "muon", "ulysses") if args.path == "all" else (args.path,)
+    paths = ("gather", "adaln", "reduce", "muon", "ulysses") if args.path == "all" else (args.path,)
     from pan2_b200.parallel.layout import init_process_group
     init_process_group(300.0, "cpu:gloo,cuda:nccl")
     try:
-        if "gather" in paths or "reduce" in paths:
+        if "gather" in paths or "reduce" in paths or "adaln" in paths:
             bench_gather_reduce(args, arch, device, rank, world, paths)
         if "muon" in paths:
             bench_muon(args, arch, device, rank, world)

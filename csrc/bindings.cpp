@@ -711,6 +711,32 @@ void peer_reduce(torch::Tensor peers, int64_t world, torch::Tensor segs, torch::
                "peer_reduce");
 }
 
+// y [k, N] = a [k, K] @ W^T + bias, W row-sharded over the peers (rows_per_rank rows each, at element
+// offset w_off of every peer's buffer)
+void peer_gemv(torch::Tensor peers, int64_t w_off, int64_t rows_per_rank, torch::Tensor a,
+               c10::optional<torch::Tensor> bias, torch::Tensor y) {
+  const at::cuda::CUDAGuard guard(a.device());
+  TORCH_CHECK(a.scalar_type() == torch::kBFloat16 && a.dim() == 2 && a.is_contiguous(), "peer_gemv: a must be bf16 [k, K]");
+  TORCH_CHECK(y.scalar_type() == torch::kBFloat16 && y.dim() == 2 && y.is_contiguous() && y.size(0) == a.size(0),
+              "peer_gemv: y must be bf16 [k, N]");
+  TORCH_CHECK((reinterpret_cast<uintptr_t>(a.data_ptr()) & 15) == 0, "peer_gemv: a must be 16-byte aligned");
+  TORCH_CHECK(peers.scalar_type() == torch::kInt64 && peers.is_cuda(), "peer_gemv: peers must be a device int64 array");
+  TORCH_CHECK(rows_per_rank > 0 && (y.size(1) + rows_per_rank - 1) / rows_per_rank <= peers.numel(),
+              "peer_gemv: the rows do not fit the ranks");
+  const void* b = nullptr;
+  if (bias.has_value() && bias->defined()) {
+    TORCH_CHECK(bias->scalar_type() == torch::kBFloat16 && bias->numel() == y.size(1) && bias->is_contiguous(),
+                "peer_gemv: bias must be bf16 [N]");
+    b = bias->data_ptr();
+  }
+  int dev = a.device().index(), sms = 0;
+  cudaDeviceGetAttribute(&sms, cudaDevAttrMultiProcessorCount, dev);
+  check_launch(launch_peer_gemv(reinterpret_cast<const uint64_t*>(peers.data_ptr<int64_t>()), w_off, (int)rows_per_rank,
+                                (int)y.size(1), (int)a.size(1), (int)a.size(0), a.data_ptr(), b, y.data_ptr(), sms,
+                                stream()),
+               "peer_gemv");
+}
+
 }  // namespace pan
 
 PYBIND11_MODULE(TORCH_EXTENSION_NAME, m) {
@@ -760,4 +786,5 @@ PYBIND11_MODULE(TORCH_EXTENSION_NAME, m) {
   m.def("symm_barrier", &pan::symm_barrier, kNoGil);
   m.def("peer_gather", &pan::peer_gather, kNoGil);
   m.def("peer_reduce", &pan::peer_reduce, kNoGil);
+  m.def("peer_gemv", &pan::peer_gemv, kNoGil);
 }

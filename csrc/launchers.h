@@ -79,6 +79,8 @@ const char* launch_peer_gather(const uint64_t* peers, const void* segs, const in
                                int n_seg, long long total, void* out, cudaStream_t s);
 const char* launch_peer_reduce(const uint64_t* peers, int world, const void* segs, const long long* prefix, int n_seg,
                                long long total, float scale, float* out, cudaStream_t s);
+const char* launch_peer_gemv(const uint64_t* peers, long long w_off, int rows_per_rank, int N, int K, int k,
+                             const void* a, const void* bias, void* y, int n_sms, cudaStream_t s);
 int comm_error_flag(bool reset);
 
 }  // namespace pan

@@ -188,21 +188,24 @@ class JointAttentionBlock(nn.Module):
         super()._load_from_state_dict(state_dict, prefix, local_metadata, strict, missing_keys,
                                       unexpected_keys, error_msgs)
 
-    def modulation_rows(self, vec: torch.Tensor) -> torch.Tensor:
-        """``[k+1, 6H]``: one row per video sample then the shared text row."""
-        a = self.modulation.act(vec)
-        video_mod = linear(a, self.modulation.linear.weight, self.modulation.linear.bias)
+    def modulation_rows(self, vec: torch.Tensor, video_mod: Optional[torch.Tensor] = None) -> torch.Tensor:
+        """``[k+1, 6H]``: one row per video sample then the shared text row.  ``video_mod`` supplies
+        the video rows when they were computed elsewhere (the peer-memory AdaLN projection)."""
+        if video_mod is None:
+            a = self.modulation.act(vec)
+            video_mod = linear(a, self.modulation.linear.weight, self.modulation.linear.bias)
         text_mod = self.text_modulation.unsqueeze(0).to(video_mod.dtype)
         return torch.cat([video_mod, text_mod], dim=0)
 
     def forward_packed(self, x: torch.Tensor, ln_stats: torch.Tensor, vec: torch.Tensor,
-                       meta: PackedSequenceParams, attn_fn=None) -> Tuple[torch.Tensor, torch.Tensor]:
+                       meta: PackedSequenceParams, attn_fn=None,
+                       video_mod: Optional[torch.Tensor] = None) -> Tuple[torch.Tensor, torch.Tensor]:
         """Packed training forward over the concat layout; returns ``(x, ln_stats)``."""
         if self.text_modulation_timestep_dependent:
             raise ValueError("packed JointAttentionBlock assumes timestep-independent text modulation")
         bounds = meta.concat_bounds
         bt = getattr(meta, "_bounds_dev", None)
-        mods = self.modulation_rows(vec).to(x.dtype)
+        mods = self.modulation_rows(vec, video_mod).to(x.dtype)
         shift1, scale1, gate1, shift2, scale2, gate2 = mods.chunk(6, dim=-1)
         x_mod = P.ln_modulate(x, ln_stats, shift1, scale1, bounds, bt)
         mm_bounds = [0, meta.n_video, meta.n_active]

@@ -71,6 +71,8 @@ class Unit:
     state: Dict[str, torch.Tensor] = field(default_factory=dict)  # optimizer state (flat shard layout)
     gather_event: Optional[torch.cuda.Event] = None
     grad_slot: int = 0                          # peer mode: gradient ring slot of the current backward
+    adaln_rows: Optional[torch.Tensor] = None   # peer AdaLN: the forward's modulation rows [k, 6H]
+    partial_gather: bool = False                # full_hi lacks the AdaLN weight (forward-only gather)
 
     def slot_full(self, buf: torch.Tensor, s: ParamSlot) -> torch.Tensor:
         return buf[s.full_off:s.full_off + s.numel].view(s.shape)
@@ -173,6 +175,11 @@ class ShardedModel:
         self._slot_last: Dict[int, int] = {}   # slot -> index of the reduction that last read it
         self._latest: Optional[Tuple[int, torch.cuda.Event]] = None  # last reduction barrier passed
         self._begin_event: Optional[torch.cuda.Event] = None
+        # peer AdaLN (enable_peer_memory(peer_adaln=True)): per block unit, the modulation weight is
+        # left out of the forward's gather and read from the peers by the projection kernel itself
+        self.adaln: Dict[int, tuple] = {}   # unit index -> (PeerProjection, bias slot)
+        self.adaln_on = False               # this step's forward uses it (set by the engine)
+        self.adaln_input: Optional[torch.Tensor] = None  # act(vec) [k, H] bf16, once known
 
     # ---------------------------------------------------------------- parameter views
     def bind_weights(self, u: Unit, full: Optional[torch.Tensor]) -> None:
@@ -187,10 +194,12 @@ class ShardedModel:
     # ---------------------------------------------------------------- peer memory
     GRAD_SLOTS = 4  # slot 0: the root unit's gradient (alive for the whole backward); 1..3: block ring
 
-    def enable_peer_memory(self) -> bool:
+    def enable_peer_memory(self, peer_adaln: bool = False) -> bool:
         """Move ``hi`` shards into symmetric memory and set up the fused gather / reduce plans.
-        Returns False (NCCL collectives stay in use) when peer memory is unavailable."""
-        from .symm import GatherPlan, PeerMemory, ReducePlan, peer_memory_available
+        Returns False (NCCL collectives stay in use) when peer memory is unavailable.  With
+        ``peer_adaln`` every block's AdaLN modulation weight is also set up for the fused
+        projection (:meth:`adaln_projection`)."""
+        from .symm import GatherPlan, PeerMemory, PeerProjection, ReducePlan, peer_memory_available
         if self.world == 1 or self.replicate_group is not None or not peer_memory_available(self.group, self.device):
             return False
         offs, total = [], 0
@@ -205,6 +214,16 @@ class ShardedModel:
         self.slot_elems = _align(max(u.numel_full for u in self.units), 128)
         self.grad_mem = PeerMemory(self.GRAD_SLOTS * self.slot_elems * 2, self.group, self.device)
         self.gather_plans = [GatherPlan(u, self.world, off, self.device) for u, off in zip(self.units, offs)]
+        self.gather_plans_fwd = list(self.gather_plans)
+        if peer_adaln:
+            for u, off in zip(self.units, offs):
+                lin = getattr(getattr(u.module, "modulation", None), "linear", None)
+                w = next((x for x in u.slots if lin is not None and x.module is lin and x.attr == "weight"), None)
+                b = next((x for x in u.slots if lin is not None and x.module is lin and x.attr == "bias"), None)
+                if w is None or len(w.shape) != 2:
+                    continue
+                self.adaln[u.index] = (PeerProjection(w, off), b)
+                self.gather_plans_fwd[u.index] = GatherPlan(u, self.world, off, self.device, skip=[w])
         self.reduce_plans = [ReducePlan(u, self.rank, self.world, self.device) for u in self.units]
         self.slot_ptrs = [self.grad_mem.peer_ptrs(j * self.slot_elems * 2) for j in range(self.GRAD_SLOTS)]
         torch.cuda.synchronize(self.device)
@@ -237,33 +256,71 @@ class ShardedModel:
         return ext().error_flag(False)
 
     # ---------------------------------------------------------------- all-gather
-    def gather(self, u: Unit, stream: Optional[torch.cuda.Stream] = None) -> None:
-        """Make ``u.full_hi`` hold the unit's full bf16 weights and bind the module to it."""
+    def gather(self, u: Unit, stream: Optional[torch.cuda.Stream] = None, forward: bool = False) -> None:
+        """Make ``u.full_hi`` hold the unit's full bf16 weights and bind the module to it.  With
+        ``forward`` and the peer AdaLN path on, the modulation weight is not gathered; its rows of
+        this step's modulation are computed from the peers instead (``take_adaln_rows``)."""
         if self.world == 1:
             u.full_hi = u.hi
             self.bind_weights(u, u.full_hi)
             return
         if u.full_hi is None:
-            self.prefetch(u)
+            self.prefetch(u, forward=forward)
+        elif u.partial_gather and not forward:
+            raise RuntimeError(f"unit {u.index}: forward-only gather reused outside the forward")
+        if u.partial_gather and u.adaln_rows is None:
+            self._adaln_projection(u)
         if u.gather_event is not None:
             torch.cuda.current_stream(self.device).wait_event(u.gather_event)
             u.gather_event = None
         self.bind_weights(u, u.full_hi)
 
-    def prefetch(self, u: Unit) -> None:
+    def _fused_adaln(self, u: Unit, forward: bool) -> bool:
+        return forward and self.peer and self.adaln_on and u.index in self.adaln
+
+    def _adaln_projection(self, u: Unit) -> None:
+        """Issue the peer AdaLN projection of ``u`` on the communication stream (after the unit's
+        gather, which brings the bias) and move the unit's gather event behind it."""
+        if self.adaln_input is None:
+            raise RuntimeError("peer AdaLN: the conditioning rows are not set")
+        proj, bias_slot = self.adaln[u.index]
+        a = self.adaln_input
+        out = torch.empty(a.shape[0], proj.slot.rows, dtype=torch.bfloat16, device=self.device)
+        self.comm_stream.wait_stream(torch.cuda.current_stream(self.device))
+        with torch.cuda.stream(self.comm_stream):
+            if u.gather_event is not None:
+                self.comm_stream.wait_event(u.gather_event)
+            bias = u.slot_full(u.full_hi, bias_slot) if bias_slot is not None else None
+            proj.run(self.hi_mem, a, bias, out)
+            ev = torch.cuda.Event()
+            ev.record(self.comm_stream)
+        out.record_stream(self.comm_stream)
+        a.record_stream(self.comm_stream)
+        u.gather_event = ev
+        u.adaln_rows = out
+
+    def take_adaln_rows(self, u: Unit) -> Optional[torch.Tensor]:
+        rows, u.adaln_rows = u.adaln_rows, None
+        return rows
+
+    def prefetch(self, u: Unit, forward: bool = False) -> None:
         """Start the all-gather of ``u`` on the communication stream (no-op if in flight/done)."""
         if self.world == 1 or u.full_hi is not None:
             return
         if self.peer:
+            fused = self._fused_adaln(u, forward)
             full = torch.empty(u.numel_full, dtype=torch.bfloat16, device=self.device)
             self.comm_stream.wait_stream(torch.cuda.current_stream(self.device))
             with torch.cuda.stream(self.comm_stream):
-                self.gather_plans[u.index].run(self.hi_mem, full)
+                (self.gather_plans_fwd if fused else self.gather_plans)[u.index].run(self.hi_mem, full)
                 ev = torch.cuda.Event()
                 ev.record(self.comm_stream)
             full.record_stream(self.comm_stream)
             u.gather_event = ev
             u.full_hi = full
+            u.partial_gather = fused
+            if fused and self.adaln_input is not None:
+                self._adaln_projection(u)
             return
         packed = torch.empty(self.world * u.numel_shard, dtype=torch.bfloat16, device=self.device)
         full = torch.empty(u.numel_full, dtype=torch.bfloat16, device=self.device)
@@ -292,6 +349,8 @@ class ShardedModel:
         if self.world == 1:
             return
         u.full_hi = None
+        u.adaln_rows = None
+        u.partial_gather = False
         self.bind_weights(u, None)
 
     # ---------------------------------------------------------------- gradients

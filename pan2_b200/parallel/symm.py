@@ -10,7 +10,10 @@ any rank's memory directly:
 * :class:`GatherPlan` -- the FSDP all-gather of one unit fused with the unpack: rank ``r`` pulls row
   range ``r`` of every parameter from peer ``r``'s ``hi`` shard into the natural full layout;
 * :class:`ReducePlan` -- the gradient reduce-scatter of one unit fused with the bf16 -> fp32 cast and
-  scale: each rank sums its row range of every parameter across all peers' bf16 gradients.
+  scale: each rank sums its row range of every parameter across all peers' bf16 gradients;
+* :class:`PeerProjection` -- the all-gather fused into the consuming projection for a skinny
+  activation (the AdaLN modulation: k <= 8 conditioning rows against a 6H x H weight): the weight
+  is read once, row by row from the rank that owns it, and never materialised locally.
 
 Plans are lists of contiguous element runs computed once per unit on the host (the row-sharded
 layout makes every parameter's rank slice one run in both layouts).
@@ -90,11 +93,15 @@ def _pack(segs: List[Tuple[int, int, int]], peers: Optional[List[int]], device):
 
 
 class GatherPlan:
-    """Unit all-gather: ``full[natural]`` <- every peer's ``hi`` shard rows (peer memory reads)."""
+    """Unit all-gather: ``full[natural]`` <- every peer's ``hi`` shard rows (peer memory reads).
+    Slots in ``skip`` are left out (their region of ``full`` stays unwritten)."""
 
-    def __init__(self, unit, world: int, hi_offset_elems: int, device):
+    def __init__(self, unit, world: int, hi_offset_elems: int, device, skip=()):
         segs, peers = [], []
+        skip = {id(s) for s in skip}
         for s in unit.slots:
+            if id(s) in skip:
+                continue
             for r in range(world):
                 a = min(s.rows, r * s.shard_rows)
                 b = min(s.rows, a + s.shard_rows)
@@ -123,3 +130,17 @@ class ReducePlan:
 
     def run(self, peer_grad_ptrs: torch.Tensor, out: torch.Tensor, scale: float = 1.0) -> None:
         ext().peer_reduce(peer_grad_ptrs, self.world, self.segs, self.prefix, self.total, scale, out)
+
+
+class PeerProjection:
+    """``y [k, N] = a [k, K] @ W^T + b`` for a weight slot ``W`` of a sharded unit, reading every row
+    of ``W`` from its owner's ``hi`` shard (peer memory) inside the projection kernel."""
+
+    def __init__(self, slot, hi_offset_elems: int):
+        self.slot = slot
+        self.w_off = hi_offset_elems + slot.shard_off
+        if self.w_off % 8 or slot.cols % 8:
+            raise ValueError("peer projection needs 16-byte aligned weight rows")
+
+    def run(self, pm: PeerMemory, a: torch.Tensor, bias: Optional[torch.Tensor], out: torch.Tensor) -> None:
+        ext().peer_gemv(pm.peers, self.w_off, self.slot.shard_rows, a, bias, out)

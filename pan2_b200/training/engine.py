@@ -91,12 +91,14 @@ class BlockCheckpoint(torch.autograd.Function):
         engine._wait_update(u)
         if idx > 0:
             engine._wait_update(sm.units[idx - 1])  # its gradient buffer receives this block's checkpoint
-        sm.gather(u)
+        sm.gather(u, forward=True)
         if idx + 1 < engine.n_blocks:
-            sm.prefetch(sm.units[idx + 1])
+            sm.prefetch(sm.units[idx + 1], forward=True)
         blk = engine.model.blocks[idx]
+        video_mod = sm.take_adaln_rows(u)
         with torch.no_grad():
-            y, st = blk.forward_packed(x, ln_stats, vec, engine.meta, attn_fn=engine._attention_keeper(idx))
+            y, st = blk.forward_packed(x, ln_stats, vec, engine.meta, attn_fn=engine._attention_keeper(idx),
+                                       video_mod=video_mod)
         sm.release(u)
         ctx.engine, ctx.idx = engine, idx
         stash = engine.stash_checkpoint(idx, x, ln_stats)
@@ -272,7 +274,10 @@ class TrainEngine:
         # gathers / gradient reductions as peer-memory kernels when the shard group is one node
         self.peer_comm = False
         if self.world > 1 and device.type == "cuda" and os.environ.get("PAN_PEER_COMM", "1") != "0":
-            self.peer_comm = self.sharded.enable_peer_memory()
+            # PAN_PEER_ADALN=1: the forward reads each block's AdaLN weight from the peers inside the
+            # modulation projection instead of gathering it (parameter all-gather fused into the op)
+            self.peer_comm = self.sharded.enable_peer_memory(
+                peer_adaln=os.environ.get("PAN_PEER_ADALN", "0") == "1")
         self._muon_pm = None  # peer-mapped exchange / result regions of distributed Muon
         self._muon_layouts: Dict[int, dict] = {}
         self.stash_in_grads = self.world == 1
@@ -435,11 +440,17 @@ class TrainEngine:
         root = sm.units[-1]
         self._wait_update(root)
         sm.begin_gathers()
+        # peer AdaLN path: only with recomputed blocks (their backward gathers every weight) and at
+        # most 8 conditioning rows (the projection kernel's limit)
+        sm.adaln_on = bool(sm.adaln) and self.recompute_blocks and int(batch["timestep"].shape[0]) <= 8
+        sm.adaln_input = None
         sm.gather(root)
         if self.n_blocks:
-            sm.prefetch(sm.units[0])
+            sm.prefetch(sm.units[0], forward=True)
         sm.attach_grads(root, zero=not self.accumulating)
         x, ln_stats, vec = model.embed_packed(batch["hidden_states"], batch["timestep"], batch["text_states"], meta)
+        if sm.adaln_on:
+            sm.adaln_input = model.blocks[0].modulation.act(vec.detach()).to(torch.bfloat16).contiguous()
         self._kept_attn = {}
         block_fn = BlockCheckpoint if self.recompute_blocks else BlockKeepGraph
         for i in range(self.n_blocks):

@@ -9,11 +9,15 @@ and off, the others held fixed, and reports the largest relative differences:
   against NCCL all-gather / reduce-scatter -- loss, gradient shards, update;
 * ``muon_peer``: distributed Muon's exchange over peer memory (``PAN_PEER_MUON``) against the NCCL
   all-to-all -- the optimizer's change of every parameter;
+* ``adaln_peer``: the forward's AdaLN modulation projected straight from the peers' weight shards
+  (``PAN_PEER_ADALN``) against the gathered weight -- loss, gradient shards, and the update as a
+  relative RMS (the projection rounds differently from the GEMM, so AdamW's sign-like first step
+  flips a few noise-level elements);
 * ``cp_fused`` (context-parallel jobs): Ulysses all-to-alls folded into the kernels
   (``PAN_CP_FUSED``) against NCCL ``all_to_all_single`` -- loss and gradient shards.
 
 Differences are max |a - b| / max |a| over all tensors (fp32 reduction order differs between the
-paths, so small nonzero values are expected).
+paths, so small nonzero values are expected), except the ``_rms`` entries (||a - b|| / ||a||).
 """
 from __future__ import annotations
 
@@ -48,6 +52,15 @@ def _rel(a, b) -> float:
     return num / (den + 1e-30)
 
 
+def _rel_rms(a, b) -> float:
+    """||a - b|| / ||a|| over all tensors.  For an optimizer update after inputs that differ by
+    rounding: AdamW's first step is about lr * sign(g), so a few elements whose gradients are pure
+    rounding noise change by up to 2 lr (a max-norm of 1-2), while the update as a whole agrees."""
+    num = sum(float((x.float() - y.float()).pow(2).sum()) for x, y in zip(a, b))
+    den = sum(float(x.float().pow(2).sum()) for x in a)
+    return (num / (den + 1e-30)) ** 0.5
+
+
 def small_arch(cp: int = 1) -> dict:
     """The small model, with as many 128-wide heads as Ulysses needs (a multiple of ``cp``, at least 4)."""
     heads = -(-max(4, cp) // cp) * cp
@@ -76,7 +89,7 @@ def _one_step(device, group, rank: int, layout=None, cp: int = 1) -> Dict:
     delta = [u.hi.float() - h for u, h in zip(eng.sharded.units, hi0)]
     torch.cuda.synchronize(device)
     out = dict(loss=torch.tensor([float(loss)]), grads=grads, delta=delta, err=int(ext().error_flag(True)),
-               peer=bool(eng.peer_comm))
+               peer=bool(eng.peer_comm), adaln=bool(eng.sharded.adaln))
     del eng
     torch.cuda.empty_cache()
     return out
@@ -87,18 +100,24 @@ def fused_path_parity(device, group, rank: int, layout=None, cp: int = 1) -> Dic
     import torch.distributed as dist
     res: Dict[str, Optional[float]] = {}
     if cp == 1:
-        with _env(PAN_PEER_COMM=1, PAN_PEER_MUON=1):
+        with _env(PAN_PEER_COMM=1, PAN_PEER_MUON=1, PAN_PEER_ADALN=0):
             peer = _one_step(device, group, rank)
-        with _env(PAN_PEER_COMM=0):
+        with _env(PAN_PEER_COMM=0, PAN_PEER_ADALN=0):
             base = _one_step(device, group, rank)
-        with _env(PAN_PEER_COMM=1, PAN_PEER_MUON=0):
+        with _env(PAN_PEER_COMM=1, PAN_PEER_MUON=0, PAN_PEER_ADALN=0):
             muon_nccl = _one_step(device, group, rank)
+        with _env(PAN_PEER_COMM=1, PAN_PEER_MUON=1, PAN_PEER_ADALN=1):
+            adaln = _one_step(device, group, rank)
         res["fsdp_peer_active"] = float(peer["peer"])
         res["fsdp_peer_loss"] = _rel([peer["loss"]], [base["loss"]])
         res["fsdp_peer_grads"] = _rel(peer["grads"], base["grads"])
         res["fsdp_peer_update"] = _rel(peer["delta"], base["delta"])
         res["muon_peer_update"] = _rel(peer["delta"], muon_nccl["delta"])
-        errs = peer["err"] | base["err"] | muon_nccl["err"]
+        res["adaln_peer_active"] = float(adaln["adaln"])
+        res["adaln_peer_loss"] = _rel([adaln["loss"]], [peer["loss"]])
+        res["adaln_peer_grads"] = _rel(adaln["grads"], peer["grads"])
+        res["adaln_peer_update_rms"] = _rel_rms(adaln["delta"], peer["delta"])
+        errs = peer["err"] | base["err"] | muon_nccl["err"] | adaln["err"]
     else:
         with _env(PAN_CP_FUSED=1):
             fused = _one_step(device, group, rank, layout, cp)

@@ -1,5 +1,7 @@
 """Peer-memory collectives on 2+ B200s of one node: the fused gather / reduce-scatter engine path
-equals the NCCL path, and a barrier whose peer never arrives returns with an error code."""
+equals the NCCL path, the forward's peer AdaLN projection equals the gathered-weight projection, and
+a barrier whose peer never arrives returns with an error code.  The projection kernel's arithmetic
+is also checked on one GPU, with the "peers" being local buffers."""
 import os
 import socket
 
@@ -39,11 +41,13 @@ def _engine_step(rank, world, port, path):
     from pan2_b200.ops._ext import ext
     from pan2_b200.training.engine import OptimConfig, TrainEngine
     out = {}
-    for mode in ("0", "1"):
-        os.environ["PAN_PEER_COMM"] = mode
+    for mode in ("0", "1", "adaln"):
+        os.environ["PAN_PEER_COMM"] = "0" if mode == "0" else "1"
+        os.environ["PAN_PEER_ADALN"] = "1" if mode == "adaln" else "0"
         eng = TrainEngine(ARCH, torch.device("cuda", rank), group=dist.group.WORLD, seed=7,
                           optim=OptimConfig(lr=1e-3), offload="off")
-        assert eng.peer_comm == (mode == "1")
+        assert eng.peer_comm == (mode != "0")
+        assert bool(eng.sharded.adaln) == (mode == "adaln")
         batch = batch_to_device(synthetic_packed_batch(2, (3, 16, 16), 40, rope_axes=(32, 48, 48), seed=rank), "cuda")
         hi0 = [u.hi.float().clone() for u in eng.sharded.units]
         loss = eng.forward_backward(batch)
@@ -113,6 +117,13 @@ def test_peer_memory_engine_matches_nccl(tmp_path):
     for da, db in zip(a["delta"], b["delta"]):
         assert (da - db).abs().max().item() <= 5e-2 * (da.abs().max().item() + 1e-12)
     assert abs(a["loss2"] - b["loss2"]) < 1e-3 * abs(a["loss2"])
+    # the forward's modulation rows from the peer projection (accumulation order differs from the GEMM)
+    c = r["adaln"]
+    assert c["err"] == 0
+    assert abs(c["loss"] - b["loss"]) < 1e-3 * abs(b["loss"])
+    for gb, gc in zip(b["grads"], c["grads"]):
+        assert (gb - gc).abs().max().item() <= 3e-2 * (gb.abs().max().item() + 1e-12)
+    assert abs(c["loss2"] - b["loss2"]) < 2e-3 * abs(b["loss2"])
 
 
 @pytest.mark.skipif(torch.cuda.device_count() < 2, reason="needs two GPUs of one node")
@@ -120,3 +131,30 @@ def test_barrier_times_out_with_error_code(tmp_path):
     r = _spawn(_barrier_timeout, 2, str(tmp_path / "b.pt"))
     assert r["ok_first"]
     assert r["err"] == 101  # rank 0 gave up waiting for peer 1
+
+
+@pytest.mark.parametrize("k,N,K,ranks", [(5, 3072, 512, 2), (8, 1000, 256, 3), (1, 30720, 5120, 8)])
+def test_peer_projection_kernel_matches_fp32(k, N, K, ranks):
+    """y = a W^T + b with W's row shards in separate buffers (as on separate ranks) at an offset."""
+    from pan2_b200.ops._ext import ext
+    torch.manual_seed(k * N)
+    W = (torch.randn(N, K, device="cuda") * 0.05).to(torch.bfloat16)
+    a = torch.randn(k, K, device="cuda").to(torch.bfloat16)
+    b = torch.randn(N, device="cuda").to(torch.bfloat16)
+    rows = -(-N // ranks)
+    off = 8 * 37
+    bufs = []
+    for r in range(ranks):
+        buf = torch.zeros(off + rows * K, device="cuda", dtype=torch.bfloat16)
+        part = W[r * rows:(r + 1) * rows]
+        buf[off:off + part.numel()] = part.reshape(-1)
+        bufs.append(buf)
+    peers = torch.tensor([t.data_ptr() for t in bufs], dtype=torch.int64, device="cuda")
+    y = torch.empty(k, N, device="cuda", dtype=torch.bfloat16)
+    ext().peer_gemv(peers, off, rows, a, b, y)
+    ref = a.float() @ W.float().t() + b.float()
+    err = (y.float() - ref).abs().max().item()
+    assert err <= 1e-2 * ref.abs().max().item(), err
+    y2 = torch.empty_like(y)
+    ext().peer_gemv(peers, off, rows, a, None, y2)
+    assert (y2.float() - (ref - b.float())).abs().max().item() <= 1e-2 * ref.abs().max().item()

@@ -1,5 +1,10 @@
-"""Packed Qwen3.5 caption encoding on a B200 (bf16, tiny random model): equal to each caption
-encoded alone by the Hugging Face model, within bf16 rounding."""
+"""Packed Qwen3.5 caption encoding on a B200 (tiny random model).
+
+fp32: the packed encode equals each caption encoded alone by the Hugging Face model.  bf16: the
+random toy model amplifies rounding (the Hugging Face bf16 forward itself moves far from fp32), so
+the packed bf16 encode is held to the Hugging Face bf16 forward's own distance from fp32."""
+import copy
+
 import pytest
 import torch
 
@@ -7,16 +12,24 @@ pytestmark = pytest.mark.gpu
 pytest.importorskip("transformers.models.qwen3_5.modeling_qwen3_5")
 
 
-def test_packed_bf16_forward_matches_each_caption_alone():
+def test_packed_forward_matches_each_caption_alone_on_cuda():
     from test_text_encoder_cpu import LENGTHS, tiny_qwen
     from pan2_b200.models.qwen_packed import PackedQwenForward
-    m = tiny_qwen(3).to("cuda", torch.bfloat16)
+    m32 = tiny_qwen(3).cuda()
+    m16 = copy.deepcopy(m32).to(torch.bfloat16)
+    torch.manual_seed(0)
     ids = [torch.randint(0, 512, (n,)) for n in LENGTHS]
-    packed = PackedQwenForward(m)(torch.cat(ids).cuda(), LENGTHS).float()
+    flat = torch.cat(ids).cuda()
+    p32 = PackedQwenForward(m32)(flat, LENGTHS).float()
+    p16 = PackedQwenForward(m16)(flat, LENGTHS).float()
     a = 0
     for n, i in zip(LENGTHS, ids):
         with torch.no_grad():
-            ref = m(input_ids=i[None].cuda(), use_cache=False).last_hidden_state[0].float()
-        err = (packed[a:a + n] - ref).abs().max().item()
-        assert err < 5e-2 * ref.abs().max().item(), (n, err)
+            r32 = m32(input_ids=i[None].cuda(), use_cache=False).last_hidden_state[0].float()
+            r16 = m16(input_ids=i[None].cuda(), use_cache=False).last_hidden_state[0].float()
+        scale = r32.abs().max().item()
+        assert (p32[a:a + n] - r32).abs().max().item() < 1e-3 * scale, n
+        err_packed = (p16[a:a + n] - r32).abs().max().item()
+        err_hf = (r16 - r32).abs().max().item()
+        assert err_packed <= 1.5 * err_hf + 1e-2 * scale, (n, err_packed, err_hf)
         a += n
