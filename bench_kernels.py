@@ -232,11 +232,12 @@ def run_elementwise(small, timer, peaks, which):
 
 
 def _ns_library(G, coeffs=(3.4445, -4.7750, 2.0315), steps=5, eps=1e-7, reset=2):
-    """The same Gram Newton-Schulz recurrence on cuBLAS (torch bf16 batched matmuls, fp32 Gram of
-    the input): the library baseline of the fused-kernel chain."""
+    """The same Gram Newton-Schulz recurrence on cuBLAS (torch bf16 batched matmuls; the Gram of the
+    input from bf16 operands with an fp32 result, as the fused Gram kernel forms it): the library
+    baseline of the tcgen05 chain."""
     a, b, c = coeffs
     X = G.transpose(-1, -2) if G.shape[-2] > G.shape[-1] else G
-    R32 = torch.matmul(X.float(), X.float().transpose(-1, -2))
+    R32 = torch.bmm(X, X.transpose(-1, -2), out_dtype=torch.float32)
     n2 = torch.diagonal(R32, dim1=-2, dim2=-1).sum(-1).clamp(min=eps * eps).view(-1, 1, 1)
     R = (R32 / n2).to(torch.bfloat16)
     eye = torch.eye(R.shape[-1], device=G.device, dtype=torch.bfloat16)
