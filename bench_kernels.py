@@ -101,7 +101,7 @@ def gemm_cases(small: bool, only=None):
     return cases[:1] if small else cases
 
 
-def run_gemm(name, M, N, K, layout, timer, library, peaks, band_mbs=(None,), probes=(None,)):
+def run_gemm(name, M, N, K, layout, timer, library, peaks, band_mbs=(None,), probes=(None,), band_ns=(None,)):
     E = ext()
     dev = "cuda"
     a = torch.randn(K, M, device=dev, dtype=torch.bfloat16) if layout == "TN" else \
@@ -112,8 +112,8 @@ def run_gemm(name, M, N, K, layout, timer, library, peaks, band_mbs=(None,), pro
     fn = lambda: E.gemm(a, b, out, layout != "TN", layout == "NT", None, None, False)
     fl = 2.0 * M * N * K
     recs = []
-    for band, probe in [(b, pr) for b in band_mbs for pr in probes]:
-        E.gemm_tuning(6, int(probe or 0), GEMM_BAND_MB if band is None else int(band))
+    for band, probe, bn in [(b, pr, w) for b in band_mbs for pr in probes for w in band_ns]:
+        E.gemm_tuning(6, int(probe or 0), GEMM_BAND_MB if band is None else int(band), int(bn or 0))
         ms = timer(fn)
         rec = dict(case=f"gemm_{name}", shape=[M, N, K], layout=layout, out_dtype=str(out.dtype).split(".")[-1],
                    ms=round(ms, 4), tflops=round(fl / ms / 1e9, 1), frac_of_peak=round(fl / ms / 1e9 / peaks[1], 3))
@@ -121,9 +121,11 @@ def run_gemm(name, M, N, K, layout, timer, library, peaks, band_mbs=(None,), pro
             rec["band_mb"] = int(band)
         if probe:
             rec["probe"] = int(probe)
+        if bn:
+            rec["band_n"] = int(bn)
         rec.update(timer.clock_fields("", ms))
         recs.append(rec)
-    E.gemm_tuning(6, 0, GEMM_BAND_MB)
+    E.gemm_tuning(6, 0, GEMM_BAND_MB, 0)
     if library:
         ao = a.t() if layout == "TN" else a
         bo = b.t() if layout == "NT" else b
@@ -290,6 +292,8 @@ def main():
                          "completion awaited before the next score GEMM)")
     ap.add_argument("--gemm-band-mb", default=None,
                     help="comma list of GEMM M-band budgets in MB (0 = N bands only)")
+    ap.add_argument("--gemm-band-n", default=None,
+                    help="comma list of GEMM N-band widths in tiles (0 = the default of 8)")
     ap.add_argument("--gemm-probe", default=None,
                     help="comma list of GEMM probe bits (timing experiments: 1 skips the epilogue stores, 2 "
                          "re-reads k-block 0)")
@@ -304,7 +308,7 @@ def main():
     if pat.search("gemm"):
         for c in gemm_cases(args.small):
             for rec in run_gemm(*c, timer=timer, library=library, peaks=peaks, band_mbs=lst(args.gemm_band_mb),
-                                probes=lst(args.gemm_probe)):
+                                probes=lst(args.gemm_probe), band_ns=lst(args.gemm_band_n)):
                 print(json.dumps(rec), flush=True)
     which = [w for w in ("fwd", "bwd") if pat.search("attn_" + w)]
     if which:

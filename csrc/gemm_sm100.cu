@@ -69,7 +69,8 @@ struct Params {
   int epi;
   int probe;  // timing experiments only: bit 0 skips the epilogue stores, bit 1 re-reads k-block 0
   int reduce_add;  // D += acc through TMA reduce-add stores (no read of D by the kernel)
-  int band_m;      // tile order: 0 = N bands of 8 tiles, > 0 = M bands of band_m tiles
+  int band_m;      // tile order: 0 = N bands of band_n tiles, > 0 = M bands of band_m tiles
+  int band_n;      // width of an N band in tiles (band_m == 0)
   int accumulate;  // host-side only: folded into C = D, beta = 1
   // batched GEMMs: operand z-coordinate = batch index; D/C advance by their batch strides
   int batch;
@@ -91,7 +92,7 @@ struct TmapSet {
   CUtensorMap aux2[kMaxGroups];
 };
 
-// Tile order (per row group).  band_m == 0: bands of up to 8 N-tiles, M-tile outer within a band
+// Tile order (per row group).  band_m == 0: bands of up to band_n N-tiles, M-tile outer within a band
 // (consecutive tiles share A; for deep K the ~74 concurrent tiles form a near-square block).
 // band_m > 0: bands of band_m M-tiles, N-tile outer, M-tile inner: the band's A rows (sized on the
 // host to stay L2-resident) are read from DRAM once, and each B tile once per band.
@@ -109,11 +110,12 @@ __device__ __forceinline__ void tile_coords(const Params& p, int t, int& g, int&
     mb = band * p.band_m + idx % height;
     return;
   }
-  const int band = local / (mt * 8);
-  const int width = min(8, nt - band * 8);
-  const int idx = local - band * mt * 8;
+  const int bw = p.band_n;
+  const int band = local / (mt * bw);
+  const int width = min(bw, nt - band * bw);
+  const int idx = local - band * mt * bw;
   mb = idx / width;
-  nb = band * 8 + idx % width;
+  nb = band * bw + idx % width;
 }
 
 __device__ __forceinline__ float gelu_tanh(float x) {
@@ -499,6 +501,9 @@ int g_probe = 0;             // Params::probe of every launch (timing experiment
 // Tile order: A rows of one M band up to g_band_mb MB (0 = always N bands).  M bands are used when a
 // 128/256-row A tile is at most 4 MB (K <= 8192): then the band stays in L2 while B streams past.
 int g_band_mb = 0;
+// N-band width in tiles (0: 8).  A is re-read once per band, and the band's B tiles stay in L2
+// while the M tiles stream past, so wider bands trade L2 room for fewer A passes.
+int g_band_n = 0;
 
 int num_sms() {
   static int n = 0;
@@ -610,6 +615,7 @@ const char* launch_gemm(const GemmArgs& a, cudaStream_t stream) {
   }
   p.tiles_per_batch = tiles;
   p.band_m = 0;
+  p.band_n = g_band_n > 0 ? g_band_n : 8;
   const long long a_tile_bytes = (long long)tile_m * a.K * 2;
   if (g_band_mb > 0 && a_tile_bytes <= (4ll << 20)) {
     const long long band = ((long long)g_band_mb << 20) / a_tile_bytes;
@@ -667,10 +673,11 @@ const char* launch_gemm(const GemmArgs& a, cudaStream_t stream) {
 }
 
 void gemm_force_cta_group(int cg) { gemm::g_forced_cta_group = (cg == 1 || cg == 2) ? cg : 0; }
-void gemm_tuning(int pair_stages, int probe, int band_mb) {
+void gemm_tuning(int pair_stages, int probe, int band_mb, int band_n) {
   gemm::g_pair_stages = pair_stages == 4 ? 4 : 6;
   gemm::g_probe = probe;
   gemm::g_band_mb = band_mb < 0 ? 0 : band_mb;
+  gemm::g_band_n = band_n < 0 ? 0 : band_n;
 }
 
 int gemm_error_flag(bool reset) {

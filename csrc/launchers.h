@@ -70,7 +70,7 @@ int gemm_error_flag(bool reset);
 void gemm_force_cta_group(int cg);
 // CTA-pair smem stages (4 or 6), timing-probe bits (0 in normal use) and the M-band budget in MB
 // of the tile order (0: N bands only).
-void gemm_tuning(int pair_stages, int probe, int band_mb);
+void gemm_tuning(int pair_stages, int probe, int band_mb, int band_n);
 
 // ------------------------------------------------------------------ comm_ops.cu (peer memory)
 const char* launch_symm_barrier(const uint64_t* pads, int rank, int world, uint32_t epoch, int channel,
