@@ -501,9 +501,14 @@ int g_probe = 0;             // Params::probe of every launch (timing experiment
 // Tile order: A rows of one M band up to g_band_mb MB (0 = always N bands).  M bands are used when a
 // 128/256-row A tile is at most 4 MB (K <= 8192): then the band stays in L2 while B streams past.
 int g_band_mb = 0;
-// N-band width in tiles (0: 8).  A is re-read once per band, and the band's B tiles stay in L2
-// while the M tiles stream past, so wider bands trade L2 room for fewer A passes.
+// N-band width in tiles (0: by shape).  A is re-read once per band, and the band's B tiles stay in
+// L2 while the M tiles stream past, so wider bands trade L2 room for fewer A passes.  Measured on
+// the 29B shapes (94,960 rows): 16-tile bands cut the FFN up-projection and its input gradient
+// (N = 32768, K = 4096) by 6-8 % and let the clock settle higher under the power cap (less DRAM
+// traffic); the QKV projection (N = 12288) ran 12 % slower with them and the deep-K shapes
+// (K >= 32768) were flat, so those keep 8.
 int g_band_n = 0;
+inline int band_n_for(int K, int max_n_tiles) { return (K <= 8192 && max_n_tiles >= 64) ? 16 : 8; }
 
 int num_sms() {
   static int n = 0;
@@ -615,7 +620,9 @@ const char* launch_gemm(const GemmArgs& a, cudaStream_t stream) {
   }
   p.tiles_per_batch = tiles;
   p.band_m = 0;
-  p.band_n = g_band_n > 0 ? g_band_n : 8;
+  int max_nt = 0;
+  for (int g = 0; g < G; ++g) max_nt = p.n_tiles[g] > max_nt ? p.n_tiles[g] : max_nt;
+  p.band_n = g_band_n > 0 ? g_band_n : band_n_for(a.K, max_nt);
   const long long a_tile_bytes = (long long)tile_m * a.K * 2;
   if (g_band_mb > 0 && a_tile_bytes <= (4ll << 20)) {
     const long long band = ((long long)g_band_mb << 20) / a_tile_bytes;

@@ -39,7 +39,7 @@ def cta_group(request):
 
 
 @pytest.mark.parametrize("M,N,K", [(128, 256, 64), (300, 200, 136), (1024, 768, 512), (77, 4096, 256),
-                                   (2304, 2048, 1024)])
+                                   (2304, 2048, 1024), (1100, 16640, 256)])  # last: 16-tile N bands
 def test_gemm_nt(M, N, K, cta_group):
     a, b = bf(M, K), bf(N, K)
     bias = bf(N)
@@ -49,7 +49,8 @@ def test_gemm_nt(M, N, K, cta_group):
     assert_close(out, ref, 1e-2, "nt")
 
 
-@pytest.mark.parametrize("M,N,K", [(256, 128, 256), (300, 200, 136), (512, 1024, 768), (1300, 1536, 512)])
+@pytest.mark.parametrize("M,N,K", [(256, 128, 256), (300, 200, 136), (512, 1024, 768), (1300, 1536, 512),
+                                   (700, 16640, 128)])
 def test_gemm_nn(M, N, K, cta_group):
     a, b = bf(M, K), bf(K, N)
     out = torch.empty(M, N, device="cuda", dtype=torch.bfloat16)

@@ -12,7 +12,17 @@ pytestmark = pytest.mark.gpu
 pytest.importorskip("transformers.models.qwen3_5.modeling_qwen3_5")
 
 
-def test_packed_forward_matches_each_caption_alone_on_cuda():
+@pytest.fixture
+def exact_fp32():
+    """fp32 references without TF32 (cuDNN convolutions default to it)."""
+    old = torch.backends.cuda.matmul.allow_tf32, torch.backends.cudnn.allow_tf32
+    torch.backends.cuda.matmul.allow_tf32 = False
+    torch.backends.cudnn.allow_tf32 = False
+    yield
+    torch.backends.cuda.matmul.allow_tf32, torch.backends.cudnn.allow_tf32 = old
+
+
+def test_packed_forward_matches_each_caption_alone_on_cuda(exact_fp32):
     from test_text_encoder_cpu import LENGTHS, tiny_qwen
     from pan2_b200.models.qwen_packed import PackedQwenForward
     m32 = tiny_qwen(3).cuda()
