@@ -83,7 +83,9 @@ def _qwen_modules():
 LENGTHS = [5, 70, 130, 1, 64, 3]
 
 
-def tiny_qwen(seed=0):
+def tiny_qwen(seed=0, noise=0.2):
+    """A 4-layer Qwen3.5 (3:1 linear / full attention like the 9B) with random weights; ``noise``
+    scales the perturbation (0.2 makes rounding grow fast through the layers, 0.02 keeps it tame)."""
     transformers, mq = _qwen_modules()
     torch.manual_seed(seed)
     cfg = transformers.Qwen3_5TextConfig(
@@ -95,7 +97,7 @@ def tiny_qwen(seed=0):
     m = mq.Qwen3_5TextModel(cfg).eval()
     with torch.no_grad():
         for p in m.parameters():
-            p.add_(torch.randn_like(p) * 0.2)
+            p.add_(torch.randn_like(p) * noise)
     return m
 
 
