@@ -92,12 +92,15 @@ class Timer:
         return out
 
 
-def gemm_cases(small: bool, only=None):
-    rows = 8192 if small else CLIPS * CLIP_TOKENS
+def gemm_cases(small: bool, only=None, rows=None):
+    """The step's GEMM shapes; ``only`` keeps the named ones, ``rows`` overrides the token rows."""
+    rows = rows or (8192 if small else CLIPS * CLIP_TOKENS)
     # (name, M, N, K, layout): NT = x @ w^T (forward), NN = dy @ w (input grad), TN = x^T @ dy (weight grad)
     cases = [("qkv_fwd", rows, 3 * HIDDEN, HIDDEN, "NT"), ("ffn_up_fwd", rows, FFN, HIDDEN, "NT"),
              ("ffn_down_fwd", rows, HIDDEN, FFN, "NT"), ("ffn_down_dgrad", rows, FFN, HIDDEN, "NN"),
              ("ffn_up_wgrad", FFN, HIDDEN, rows, "TN")]
+    if only:
+        return [c for c in cases if c[0] in only]
     return cases[:1] if small else cases
 
 
@@ -292,6 +295,9 @@ def main():
                          "completion awaited before the next score GEMM)")
     ap.add_argument("--gemm-band-mb", default=None,
                     help="comma list of GEMM M-band budgets in MB (0 = N bands only)")
+    ap.add_argument("--gemm-shape", default=None,
+                    help="comma list of GEMM cases to run (qkv_fwd, ffn_up_fwd, ffn_down_fwd, ffn_down_dgrad, ffn_up_wgrad)")
+    ap.add_argument("--rows", type=int, default=None, help="token rows of the GEMM cases (default: the step's)")
     ap.add_argument("--gemm-band-n", default=None,
                     help="comma list of GEMM N-band widths in tiles (0 = the default of 8)")
     ap.add_argument("--gemm-probe", default=None,
@@ -306,7 +312,8 @@ def main():
     timer = Timer(args.iters, args.warmup, args.sustain_s)
     library = not args.no_library
     if pat.search("gemm"):
-        for c in gemm_cases(args.small):
+        only = args.gemm_shape.split(",") if args.gemm_shape else None
+        for c in gemm_cases(args.small, only, args.rows):
             for rec in run_gemm(*c, timer=timer, library=library, peaks=peaks, band_mbs=lst(args.gemm_band_mb),
                                 probes=lst(args.gemm_probe), band_ns=lst(args.gemm_band_n)):
                 print(json.dumps(rec), flush=True)
