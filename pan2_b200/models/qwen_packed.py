@@ -204,7 +204,7 @@ class PackedQwenForward:
         o = gated_delta_rule_packed(q, k, v, beta, g, lay, self.chunk).to(x.dtype)
         # gated RMS norm over each head's value features: norm first, then the SiLU gate
         of = o.float()
-        eps = float(getattr(la.norm, "variance_epsilon", la.layer_norm_epsilon))
+        eps = float(getattr(la.norm, "variance_epsilon", getattr(la.norm, "eps", la.layer_norm_epsilon)))
         of = of * torch.rsqrt(of.pow(2).mean(-1, keepdim=True) + eps)
         o = la.norm.weight * of.to(x.dtype)
         o = (o * F.silu(z.float())).to(x.dtype)

@@ -95,6 +95,18 @@ def tiny_qwen(seed=0, noise=0.2):
         layer_types=["linear_attention", "full_attention", "linear_attention", "full_attention"])
     cfg._attn_implementation = "sdpa"
     m = mq.Qwen3_5TextModel(cfg).eval()
+    # the reference runs Hugging Face's own PyTorch implementations: where flash-linear-attention
+    # is importable (a GPU machine), its Triton gated norm and delta-rule kernels would replace them
+    for layer in m.layers:
+        la = getattr(layer, "linear_attn", None)
+        if la is None:
+            continue
+        norm = mq.Qwen3_5RMSNormGated(la.head_v_dim, eps=la.layer_norm_epsilon)
+        with torch.no_grad():
+            norm.weight.copy_(la.norm.weight.detach().cpu())
+        la.norm = norm
+        la.chunk_gated_delta_rule = mq.torch_chunk_gated_delta_rule
+        la.causal_conv1d_fn = None
     with torch.no_grad():
         for p in m.parameters():
             p.add_(torch.randn_like(p) * noise)
