@@ -39,7 +39,7 @@ WORKLOAD_METRICS = {
 def parse():
     ap = argparse.ArgumentParser()
     ap.add_argument("--gpus", type=int, default=1)
-    ap.add_argument("--steps", type=int, default=2)
+    ap.add_argument("--steps", type=int, default=3)
     ap.add_argument("--warmup", type=int, default=3)
     ap.add_argument("--impl", default="ours", choices=("ours", "reference"))
     ap.add_argument("--config", default=os.path.join(ROOT, "config", "pretrain_29B_720p.yaml"))
@@ -185,6 +185,7 @@ def main():
 
     for _ in range(args.warmup):
         runner.train_step(batch)
+    engine.flush_updates()  # the timed region holds exactly K optimizer updates
     torch.cuda.synchronize()
     if world > 1:
         dist.barrier()

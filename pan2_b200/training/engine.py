@@ -19,6 +19,7 @@ This is the B200 restatement of the reference trainer's model wrapping and step
 """
 from __future__ import annotations
 
+import math
 import os
 import threading
 from dataclasses import dataclass
@@ -209,7 +210,8 @@ class TrainEngine:
 
     def __init__(self, arch: dict, device: torch.device, *, group: Optional[dist.ProcessGroup] = None,
                  seed: int = 42, optim: Optional[OptimConfig] = None, offload: str = "auto",
-                 activation_bytes_estimate: int = 0, replicate_group: Optional[dist.ProcessGroup] = None):
+                 activation_bytes_estimate: int = 0, replicate_group: Optional[dist.ProcessGroup] = None,
+                 offload_gpu_bytes: Optional[int] = None):
         self.device = device
         self.group = group
         self.replicate_group = replicate_group
@@ -238,6 +240,8 @@ class TrainEngine:
         if self.offload and device.type == "cuda":
             resident = total * 2 / self.world + (total * 2 if self.world == 1 else total * 4 / self.world)
             self._gpu_budget = int(_hbm_bytes(device) - resident - activation_bytes_estimate - 8e9)
+            if offload_gpu_bytes is not None:
+                self._gpu_budget = int(offload_gpu_bytes)
             from ..optim.muon import use_muon_for
             n_muon = sum(p.numel() for n, p in model.named_parameters()
                          if self.optim.use_muon and use_muon_for(n, tuple(p.shape)))
@@ -248,12 +252,24 @@ class TrainEngine:
                 raise MemoryError(
                     f"offloaded optimizer state needs {self.host_bytes_planned / 1e9:.0f} GB of pinned host memory per "
                     f"rank but only {avail / 1e9:.0f} GB are available on this host")
+        # Offloadable state (lo halves, optimizer state) takes the GPU budget in the order the next
+        # step's forward needs the units, each unit whole: the root first (with deferred updates its
+        # update gates the embedding that starts every forward), then the blocks in forward order;
+        # the rest lives in pinned host memory and streams.  The root is built last, so its share
+        # is set aside now.
+        self._soff: Dict[int, int] = {}
+        root_reserve = 0
+        if self.offload and device.type == "cuda":
+            root_reserve = min(max(self._gpu_budget, 0), self._offloadable_bytes(
+                [(n, tuple(p.shape)) for n, p in model.named_parameters() if not n.startswith("blocks.")]))
+            self._gpu_budget -= root_reserve
         for i in range(self.n_blocks):
             torch.manual_seed(seed * 1000003 + i)
             with torch.device(device):
                 blk = JointAttentionBlock(model.hidden_size, model.num_attention_heads, **blk_opts)
             model.blocks[i] = blk
             units.append(self._materialise(i, f"blocks.{i}", blk, f"blocks.{i}."))
+            self._alloc_unit_state(units[-1])
         torch.manual_seed(seed * 1000003 + self.n_blocks)
         with torch.device(device):
             small = PanVideoDiffusionTransformer(**{**arch, "num_layers": 0})
@@ -261,7 +277,9 @@ class TrainEngine:
             if name != "blocks":
                 setattr(model, name, child)
         root = _Root(model)
+        self._gpu_budget += root_reserve
         units.append(self._materialise(self.n_blocks, "root", root, ""))
+        self._alloc_unit_state(units[-1])
         self.model = model
         self.sharded = ShardedModel(units, group, device, self.offload, replicate_group)
         self.sharded.before_read = self.flush_updates
@@ -270,7 +288,6 @@ class TrainEngine:
                 self.sharded.bind_weights(u, u.hi)
             else:
                 self.sharded.bind_weights(u, None)
-        self._alloc_optimizer_state()
         # gathers / gradient reductions as peer-memory kernels when the shard group is one node
         self.peer_comm = False
         if self.world > 1 and device.type == "cuda" and os.environ.get("PAN_PEER_COMM", "1") != "0":
@@ -353,23 +370,31 @@ class TrainEngine:
             return torch.zeros(n, dtype=dtype, device=self.device)
         return torch.zeros(n, dtype=dtype, pin_memory=True)
 
-    def _alloc_optimizer_state(self) -> None:
+    def _offloadable_bytes(self, params) -> int:
+        """Upper bound of the lo halves and optimizer state of ``params`` (name, shape) on this rank."""
+        from ..optim.muon import use_muon_for
+        total = 0
+        for name, shape in params:
+            rows = shape[0] if shape else 1
+            n = -(-rows // self.world) * (int(math.prod(shape[1:])) if len(shape) >= 2 else 1) + 8
+            muon = self.optim.use_muon and use_muon_for(name, shape)
+            total += n * (2 + (4 if muon else 8))
+        return total + (1 << 20)
+
+    def _alloc_unit_state(self, u: Unit) -> None:
         """Compact per-unit state: Muon momentum for Muon slots, AdamW (m, v) for the others."""
-        pin = self.offload
-        self._soff = {}
-        for u in self.sharded.units:
-            mo = ao = 0
-            for s in u.slots:
-                n = s.shard_rows * s.cols
-                if self._is_muon(s):
-                    self._soff[id(s)] = mo
-                    mo += n
-                else:
-                    self._soff[id(s)] = ao
-                    ao += n
-            u.state["mom"] = self._state_tensor(mo, torch.float32) if mo else None
-            u.state["m"] = self._state_tensor(ao, torch.float32) if ao else None
-            u.state["v"] = self._state_tensor(ao, torch.float32) if ao else None
+        mo = ao = 0
+        for s in u.slots:
+            n = s.shard_rows * s.cols
+            if self._is_muon(s):
+                self._soff[id(s)] = mo
+                mo += n
+            else:
+                self._soff[id(s)] = ao
+                ao += n
+        u.state["mom"] = self._state_tensor(mo, torch.float32) if mo else None
+        u.state["m"] = self._state_tensor(ao, torch.float32) if ao else None
+        u.state["v"] = self._state_tensor(ao, torch.float32) if ao else None
 
     def _is_muon(self, s) -> bool:
         return self.optim.use_muon and s.kind == "muon"

@@ -112,6 +112,49 @@ def test_deferred_offloaded_optimizer_matches_synchronous():
         assert torch.equal(a, c)
 
 
+def _unit_state_bytes(u):
+    ts = [u.lo] + [t for t in u.state.values() if t is not None]
+    return sum(t.numel() * t.element_size() for t in ts)
+
+
+def test_offloaded_state_placed_in_forward_order():
+    """A GPU budget for part of the offloadable state gives the root unit and then the first blocks
+    their lo halves and optimizer state on the GPU, whole; the last block streams from the host; the
+    overlapped updates over that mixed placement equal the synchronous ones."""
+    from pan2_b200.training.engine import TrainEngine, OptimConfig
+    from pan2_b200.models.transformer import PanVideoDiffusionTransformer
+    with torch.device("meta"):
+        shape_model = PanVideoDiffusionTransformer(**ARCH)
+    batch, _ = tiny_batch(shape_model)
+    b = _dev(batch)
+    probe = TrainEngine(ARCH, torch.device("cuda"), seed=5, optim=OptimConfig(lr=1e-3), offload="on",
+                        offload_gpu_bytes=0)
+    units = probe.sharded.units
+    budget = _unit_state_bytes(units[-1]) + _unit_state_bytes(units[0]) + (4 << 20)  # slack of the root estimate
+    del probe
+    res = {}
+    for defer in (False, True):
+        eng = TrainEngine(ARCH, torch.device("cuda"), seed=5, optim=OptimConfig(lr=1e-3), offload="on",
+                          offload_gpu_bytes=budget)
+        us = eng.sharded.units
+        on_gpu = lambda u: [t.is_cuda for t in [u.lo] + [t for t in u.state.values() if t is not None]]
+        assert all(on_gpu(us[-1])) and all(on_gpu(us[0]))      # root, then block 0
+        assert not any(on_gpu(us[-2]))                          # the last block streams
+        eng.defer_optimizer = defer
+        losses = []
+        for step in range(3):
+            losses.append(eng.forward_backward(b).item())
+            eng.grad_norm()
+            eng.optimizer_step()
+        eng.flush_updates()
+        torch.cuda.synchronize()
+        res[defer] = (losses, [u.hi.float().cpu().clone() for u in us])
+        del eng
+    assert res[False][0] == res[True][0]
+    for a, c in zip(res[False][1], res[True][1]):
+        assert torch.equal(a, c)
+
+
 @pytest.mark.parametrize("mode", ["keep_attention", "no_recompute"])
 def test_checkpointing_modes_give_the_recompute_gradients(mode):
     """Kept-attention checkpointing (the recompute skips the attention forward) and no activation
