@@ -173,13 +173,24 @@ def linear(x: torch.Tensor, w: torch.Tensor, b: Optional[torch.Tensor] = None) -
     return F.linear(x, w.to(x.dtype), None if b is None else b.to(x.dtype))
 
 
+def _rows_outside_zeroed(t: torch.Tensor, bounds: Sequence[int]) -> torch.Tensor:
+    """``t`` (fresh, uninitialised) with the rows outside ``[bounds[0], bounds[-1])`` zeroed; the
+    grouped GEMMs write every row inside the bounds."""
+    if bounds[0] > 0:
+        t[:bounds[0]].zero_()
+    if bounds[-1] < t.shape[0]:
+        t[bounds[-1]:].zero_()
+    return t
+
+
 class _GroupedLinearCUDA(torch.autograd.Function):
     @staticmethod
     def forward(ctx, x, w, b, bounds):
         G = len(bounds) - 1
         wc = w.to(torch.bfloat16).contiguous()
         bc = b.to(torch.bfloat16).contiguous()
-        out = torch.zeros(x.shape[0], wc.shape[1], dtype=torch.bfloat16, device=x.device)
+        out = _rows_outside_zeroed(torch.empty(x.shape[0], wc.shape[1], dtype=torch.bfloat16, device=x.device),
+                                   bounds)
         grouped_mm_nt(x, wc, bounds, out, bias=bc)
         ctx.save_for_backward(x, wc)
         ctx.bounds = list(bounds)
@@ -191,7 +202,7 @@ class _GroupedLinearCUDA(torch.autograd.Function):
         x, wc = ctx.saved_tensors
         bounds = ctx.bounds
         gy = gy.contiguous()
-        gx = torch.zeros_like(x)
+        gx = _rows_outside_zeroed(torch.empty_like(x), bounds)
         gw = torch.zeros(wc.shape, dtype=torch.float32, device=x.device)
         for g in range(len(bounds) - 1):
             r0, r1 = bounds[g], bounds[g + 1]
@@ -244,7 +255,7 @@ class _GroupedFFNCUDA(torch.autograd.Function):
         L = x.shape[0]
         hidden = max(w.shape[0] for w in wu)
         pre = torch.empty(L, hidden, dtype=torch.bfloat16, device=x.device)
-        out = torch.zeros(L, wd[0].shape[0], dtype=torch.bfloat16, device=x.device)
+        out = _rows_outside_zeroed(torch.empty(L, wd[0].shape[0], dtype=torch.bfloat16, device=x.device), bounds)
         E = ext()
         for g in range(G):
             hid = wu[g].shape[0]
@@ -264,7 +275,7 @@ class _GroupedFFNCUDA(torch.autograd.Function):
         x, pre = saved[0], saved[1]
         wu, wd = saved[2:2 + G], saved[2 + G:2 + 2 * G]
         gy = gy.contiguous()
-        gx = torch.zeros_like(x)
+        gx = _rows_outside_zeroed(torch.empty_like(x), bounds)
         grads = []
         E = ext()
         dev = x.device
