@@ -179,13 +179,13 @@ def load_engine(engine, root: str, *, load_optimizer: bool = True, strict: bool 
     if engine.device.type == "cuda":
         torch.cuda.synchronize(engine.device)
     if load_optimizer and not os.path.isdir(optim_dir):
-        raise ValueError(f"{root} holds no optimizer state")
+        raise ValueError(f"no optimizer state found under {root}")
     if is_dcp_folder(model_dir):
         missing = _load_dcp(engine, model_dir, optim_dir if load_optimizer else None)
     else:
         missing = _load_safetensors_shards(engine, model_dir, optim_dir if load_optimizer else None)
     if strict and missing:
-        raise ValueError(f"{model_dir} is missing {len(missing)} transformer tensors, e.g. {missing[:5]}")
+        raise ValueError(f"{len(missing)} transformer tensors absent from {model_dir} (first: {missing[:5]})")
     return missing
 
 
@@ -443,7 +443,7 @@ def load_plain_into_engine(engine, path: str, strict: bool = True) -> List[str]:
         if world == 1:
             engine.sharded.bind_weights(u, u.hi)
     if strict and missing:
-        raise ValueError(f"{path} is missing {len(missing)} transformer tensors, e.g. {missing[:5]}")
+        raise ValueError(f"{len(missing)} transformer tensors absent from {path} (first: {missing[:5]})")
     return missing
 
 

@@ -251,12 +251,12 @@ def load_yaml_defaults(path: str, parser: argparse.ArgumentParser) -> Dict[str, 
                 continue
             if key in actions:
                 if key in out:
-                    raise ValueError(f"Duplicate training config key {key!r}; second occurrence at {'.'.join(here)}")
+                    raise ValueError(f"training config sets {key!r} twice (again at {'.'.join(here)})")
                 out[key] = value
             elif isinstance(value, Mapping):
                 visit(value, here)
             else:
-                raise ValueError(f"Unknown training config key {'.'.join(here)!r}")
+                raise ValueError(f"training config key {'.'.join(here)!r} is not an option")
 
     visit(obj)
     for key, value in list(out.items()):

@@ -63,7 +63,7 @@ def local_params(P: PackedSequenceParams, cp: int, rank: int, group, device) -> 
     vrows, trows, lv, lc = shard_rows(vlen, clen, cp, rank)
     S = sum(vlen) + sum(clen)
     if sum(lv) == 0:
-        raise ValueError(f"cp shard {rank} of a {S}-token batch holds no video tokens (cp={cp}); use a smaller cp_size")
+        raise ValueError(f"with cp={cp}, context-parallel rank {rank} gets no video token of the {S}-token batch; lower cp_size")
     s_local = sum(lv) + sum(lc)
     idx_v = torch.tensor(vrows, dtype=torch.long, device=device)
     idx_t = torch.tensor(trows, dtype=torch.long, device=device)

@@ -36,7 +36,7 @@ def placeholder_video_caption(index: int, seconds: float) -> str:
     doc = {"video_style": "Placeholder", "lighting": "Placeholder", "perspective_view": "Placeholder",
            "subjects_lifecycle": [{"subject_id": "<|Subject1|>", "display_name": f"Placeholder subject {index}",
                                    "subject_attribute": "Placeholder"}],
-           "init_frame_visual_description": f"Synthetic sample {index}; the latent is random noise.",
+           "init_frame_visual_description": f"Synthetic sample {index} (random-noise latent).",
            "events": events, "quality": "Placeholder"}
     return json.dumps(doc, indent=2)
 

@@ -51,7 +51,7 @@ class FlowEulerScheduler:
         v = float(timestep) if not torch.is_tensor(timestep) else float(timestep.detach().cpu())
         hits = (self._host_t == v).nonzero().view(-1).tolist()
         if not hits:
-            raise ValueError(f"timestep {timestep} is not in scheduler.timesteps; call set_timesteps() first")
+            raise ValueError(f"no step of the current schedule has timestep {timestep} (was set_timesteps() called?)")
         return hits[1] if len(hits) > 1 else hits[0]
 
     def coefficient(self, timestep) -> float:
@@ -78,7 +78,7 @@ def apply_timestep_schedule(sched: FlowEulerScheduler, name: str) -> torch.Tenso
     ok = (s.ndim == 1 and s.numel() == 51 and sched.timesteps.numel() == 50 and bool(torch.isfinite(s).all())
           and bool((s[:-1] > s[1:]).all()) and abs(float(s[0]) - 1.0) < 1e-6 and abs(float(s[-1])) < 1e-6)
     if not ok:
-        raise ValueError("early_refine_2x requires a descending 50-step sigma grid from 1 to 0")
+        raise ValueError("the early_refine_2x grid is defined only for 50 sigmas falling from 1 to 0")
     keep = torch.ones(51, dtype=torch.bool)
     keep[15] = False
     keep[25] = False

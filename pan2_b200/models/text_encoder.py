@@ -46,7 +46,7 @@ def load_qwen_language_model(path: str = DEFAULT_TEXT_ENCODER, hidden_state_skip
     from transformers import AutoConfig, AutoModelForImageTextToText
     skip = int(hidden_state_skip_layer)
     if skip < 0:
-        raise ValueError(f"hidden_state_skip_layer must be >= 0, got {skip}")
+        raise ValueError(f"cannot drop a negative number of decoder layers ({skip})")
     cfg = AutoConfig.from_pretrained(path)
     tcfg = getattr(cfg, "text_config", cfg)
     if skip >= tcfg.num_hidden_layers:

@@ -364,7 +364,7 @@ class PanVideoDiffusionTransformer(nn.Module):
         super().__init__()
         head_dim, leftover = divmod(hidden_size, num_attention_heads)
         if leftover:
-            raise ValueError(f"hidden_size {hidden_size} is not a multiple of num_attention_heads {num_attention_heads}")
+            raise ValueError(f"{num_attention_heads} attention heads do not split a hidden size of {hidden_size} evenly")
         if len(rope_axes_dim) != 3 or sum(rope_axes_dim) != head_dim:
             raise ValueError(f"rope_axes_dim {rope_axes_dim} needs three entries summing to the head dim {head_dim}")
         self.config = dict(patch_size=list(patch_size), in_channels=in_channels, out_channels=out_channels,

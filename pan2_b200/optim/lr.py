@@ -18,7 +18,7 @@ LR_SCHEDULER_TYPES = ("constant_with_warmup", "linear_decay", "cosine_decay")
 def make_lr_lambda(scheduler_type: str, warmup_steps: int, decay_steps: Optional[int], max_steps: int,
                    warmup_start_ratio: float, decay_floor_ratio: float) -> Callable[[int], float]:
     if scheduler_type not in LR_SCHEDULER_TYPES:
-        raise ValueError(f"Unknown lr_scheduler_type={scheduler_type!r}; expected one of {LR_SCHEDULER_TYPES}")
+        raise ValueError(f"learning-rate schedule {scheduler_type!r} is not one of {LR_SCHEDULER_TYPES}")
     eff_decay = decay_steps if decay_steps is not None else max(max_steps - warmup_steps, 0)
 
     def lr_lambda(step: int) -> float:

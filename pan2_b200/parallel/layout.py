@@ -79,7 +79,7 @@ def init_parallel_layout(cp: int = 1, hybrid_shard: bool = False, timeout_s: flo
     init_process_group(timeout_s, backend)
     world, rank = dist.get_world_size(), dist.get_rank()
     if world % cp:
-        raise ValueError(f"cp_size={cp} must evenly divide the number of ranks ({world})")
+        raise ValueError(f"{world} ranks cannot be split into context-parallel groups of {cp}")
     dp = world // cp
     # (dp, cp) mesh, cp fastest: ranks [d*cp, (d+1)*cp) form one cp group
     cp_groups = [list(range(d * cp, (d + 1) * cp)) for d in range(dp)]

@@ -41,11 +41,11 @@ def latent_grid(num_frames: int, height: int, width: int, patch_size) -> Tuple[i
     if height <= 0 or width <= 0:
         raise ValueError(f"height and width must be positive, got {height}x{width}")
     if height % WAN22_SPATIAL_STRIDE or width % WAN22_SPATIAL_STRIDE:
-        raise ValueError(f"{height}x{width} is not a multiple of the VAE stride {WAN22_SPATIAL_STRIDE}")
+        raise ValueError(f"height and width ({height}x{width}) must both divide by {WAN22_SPATIAL_STRIDE}, the VAE's spatial stride")
     rows, cols = height // WAN22_SPATIAL_STRIDE, width // WAN22_SPATIAL_STRIDE
     ph, pw = tuple(patch_size)[-2:]
     if rows % ph or cols % pw:
-        raise ValueError(f"latent {rows}x{cols} of a {height}x{width} video is not a multiple of the patch {(ph, pw)}")
+        raise ValueError(f"the {rows}x{cols} latent of a {height}x{width} video does not tile into {(ph, pw)} patches")
     grid = ((num_frames - 1) // WAN22_TEMPORAL_STRIDE + 1, rows, cols)
     if min(grid) <= 0:
         raise ValueError(f"empty latent grid {grid} for {num_frames} frames at {height}x{width}")
@@ -201,7 +201,7 @@ class PanVideoPipeline:
             if src.dim() == 4:
                 src = src.unsqueeze(0)
             if src.shape[0] not in (1, B):
-                raise ValueError(f"reference latents have batch {src.shape[0]}, expected 1 or {B}")
+                raise ValueError(f"{src.shape[0]} reference latents for {B} prompts (give one, or one per prompt)")
             k = min(int(src.shape[2]), T)
             cond[:, :WAN22_LATENT_CHANNELS, :k] = src[:, :, :k].expand(B, -1, -1, -1, -1)
             cond[:, WAN22_LATENT_CHANNELS, :k] = 1.0
@@ -226,7 +226,7 @@ class PanVideoPipeline:
         steps = d["num_inference_steps"] if num_inference_steps is None else num_inference_steps
         i2v = reference_image is not None or reference_latents is not None
         if not isinstance(i2v_skip_first_latent_cfg, bool):
-            raise ValueError("i2v_skip_first_latent_cfg must be a boolean")
+            raise ValueError("i2v_skip_first_latent_cfg takes True or False")
         if type(first_step_velocity_scale) not in (int, float) or not 0 <= first_step_velocity_scale <= 1:
             raise ValueError("first_step_velocity_scale must be finite and in [0, 1]")
         validate_sampling_extensions(steps, timestep_schedule)
@@ -239,7 +239,7 @@ class PanVideoPipeline:
             if stg_scale != 0 and i2v:
                 raise ValueError("STG supports T2V only")
         if stg_scale == 0 and stg_skip_layers is not None:
-            raise ValueError("stg_skip_layers requires stg_scale > 0")
+            raise ValueError("stg_skip_layers has no effect unless stg_scale is positive")
         use_cfg = guidance_scale > 1
 
         # ---- text
@@ -389,5 +389,5 @@ def load_transformer_weights(model, path: str, strict: bool = True) -> List[str]
             missing.append(k)
     missing = [m for m in missing if not m.endswith("freqs")]
     if strict and missing:
-        raise ValueError(f"{path} is missing {len(missing)} transformer tensors, e.g. {missing[:5]}")
+        raise ValueError(f"{len(missing)} transformer tensors absent from {path} (first: {missing[:5]})")
     return missing

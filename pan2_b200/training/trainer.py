@@ -108,8 +108,8 @@ def architecture_from_config(cfg: TrainingConfig) -> dict:
                 "out_channels": WAN22_LATENT_CHANNELS}
     for key, want in expected.items():
         if key in over and int(over[key]) != want:
-            raise ValueError(f"{schema} conditioning with Wan 2.2 latents expects "
-                             f"transformer_config_overrides.{key}={want}, got {over[key]}")
+            raise ValueError(f"transformer_config_overrides.{key}={over[key]} does not fit {schema} "
+                             f"conditioning of Wan 2.2 latents, which needs {want}")
     arch = dict(ARCH_DEFAULTS)
     arch.update(over)
     arch.update(expected)
@@ -176,9 +176,9 @@ class Trainer:
         cfg, L = self.cfg, self.layout
         csvs = sorted(expand_csv_paths(cfg.packed_dataloader_meta_csv_path or []))
         if len(csvs) < L.dp_size:
-            msg = (f"{len(csvs)} CSV file(s) in packed_dataloader_meta_csv_path for {L.dp_size} data-parallel ranks: "
-                   f"every rank needs at least one CSV, so {L.dp_size - len(csvs)} rank(s) would get none. Split the "
-                   f"metadata into at least {L.dp_size} CSVs, or use fewer ranks / a larger cp_size.")
+            msg = (f"{L.dp_size} data-parallel ranks read whole CSV files, but packed_dataloader_meta_csv_path "
+                   f"lists only {len(csvs)}: {L.dp_size - len(csvs)} rank(s) would have no data.  Provide at least "
+                   f"{L.dp_size} CSV files, or run fewer data-parallel ranks (fewer GPUs or a larger cp_size).")
             raise ValueError(msg)
         csvs = csvs[L.dp_rank::L.dp_size]
         tars: List[str] = []
@@ -279,8 +279,8 @@ class Trainer:
         if load_dataloader_state:
             p = os.path.join(root, "dataloader", f"{self.layout.dp_rank}.json")
             if not os.path.exists(p):
-                raise ValueError(f"checkpoint {root} has no dataloader state for dp_rank {self.layout.dp_rank} ({p}); "
-                                 "it was written with a different data-parallel size")
+                raise ValueError(f"{p} does not exist: {root} was saved by a run with a different number of "
+                                 f"data-parallel ranks than this one (rank {self.layout.dp_rank})")
             self.resume_dataloader_state = DataloaderState.from_json(Path(p).read_text())
             if not self.cfg.resume_video_csv:
                 self.resume_dataloader_state = self.resume_dataloader_state.reset_video_stream()
@@ -396,7 +396,7 @@ class Trainer:
             if resumed is None:
                 self.warm_start(cfg.pretrained_transformer_path)
             else:
-                log.info(f"{cfg.output_dir} already has checkpoints; resumed {resumed} instead of warm starting")
+                log.info(f"resumed from {resumed}: {cfg.output_dir} holds checkpoints, so the warm start is skipped")
         self._barrier()
         if self.is_main:
             log.info(f"Training for {cfg.max_steps} steps: batch_size={cfg.batch_size} (packed batches are sized "
@@ -456,9 +456,9 @@ class Trainer:
                 if stats["step_skipped"]:
                     self.consecutive_skipped += 1
                     self.total_skipped += 1
-                    log.warning(f"Skipped optimizer step at step {self.global_step}: non-finite update "
-                                f"(loss={stats['loss']}, grad_norm={stats['grad_norm']}); "
-                                f"{self.consecutive_skipped} consecutive, {self.total_skipped} total")
+                    log.warning(f"step {self.global_step}: update not applied, loss {stats['loss']} / grad norm "
+                                f"{stats['grad_norm']} not finite ({self.consecutive_skipped} in a row, "
+                                f"{self.total_skipped} so far)")
                 else:
                     self.consecutive_skipped = 0
                 self.global_step += 1

@@ -151,7 +151,7 @@ def test_conditioning_schema_sets_and_checks_the_channel_widths(data_dir, tmp_pa
     assert (ch["in_channels"], ch["out_channels"]) == (97, 48)
     bad = _cfg(data_dir, tmp_path / "s", conditioning_schema="channel_concat",
                transformer_config_overrides=json.dumps(dict(TINY_OVERRIDES, in_channels=48)))
-    with pytest.raises(ValueError, match="in_channels=97"):
+    with pytest.raises(ValueError, match="in_channels=48 does not fit"):
         architecture_from_config(bad)
     with pytest.raises(ValueError, match="not divisible by the transformer patch size"):
         _train(_cfg(data_dir, tmp_path / "s", video_width=208, max_steps=1))  # 13 latent columns, patch 2
