@@ -210,6 +210,8 @@ class _HostArena:
         if self.size > 0 and int(torch.cuda.cudart().cudaHostRegister(ptr, self.size, 0)) == 0:
             self.registered = True
             weakref.finalize(self, _host_unregister, ptr)
+        else:
+            self.buf = None  # registration refused: the state falls back to pinned allocations
 
     def take(self, n: int, dtype) -> Optional[torch.Tensor]:
         nbytes = n * torch.empty(0, dtype=dtype).element_size()
