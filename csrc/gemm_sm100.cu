@@ -7,7 +7,11 @@
 // Up to four row groups share A and K but carry their own B / bias / width (the video and text
 // weights of the per-modality projections run in one launch).
 //
-// CTA = 192 threads, one CTA per SM, tiles of 128 x 256 x 64 with a 4-stage smem ring:
+// CTA = 192 threads, one CTA per SM (persistent: each CTA, or CTA pair, walks tiles t, t + grid, ...),
+// tiles of 128 x 256 x 64 with a 4-stage smem ring, or for large problems 256 x 256 per CTA pair
+// (cta_group::2, 6 stages; see Cfg below).  Tile order: bands of N tiles (8 wide, 16 for wide
+// shallow-K launches) with the M tile outer inside a band, so a band's B tiles stay in L2 while A
+// streams past (tile_coords; band_n_for picks the width):
 //   warp 0      TMA producer (one lane): A/B tiles -> smem, completion on `full[s]`
 //   warp 1      MMA issuer (one lane): 4 x tcgen05.mma 128x256x16 per stage, commit -> `empty[s]`;
 //               owns the TMEM allocation (2 accumulators x 256 fp32 columns = 512 columns)
