@@ -8,7 +8,8 @@
 // mean = s0 / C, var = s1 / C - mean^2.
 //
 // Layout of the work: one warp owns one row (memory-bound, no shared-memory reductions); lanes
-// stride the row in 16-byte vectors so a warp reads 512 contiguous bytes per step.  Column
+// stride the row in 16-byte vectors so a warp reads 512 contiguous bytes per step.  The LN-modulate
+// forward instead gives each CTA a 2048-column slab and a run of rows (see its kernel).  Column
 // reductions over rows (modulation/gate gradients, bias sums) use 256-thread CTAs that own 2048
 // columns and a chunk of rows and flush fp32 partials with atomics at segment ends.
 #include "common.cuh"
