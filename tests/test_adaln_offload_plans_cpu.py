@@ -5,7 +5,10 @@
 * the engine's estimate of the root unit's offloadable bytes bounds what the root really allocates,
   so the budget set aside for it covers it;
 * the grouped GEMM helpers zero exactly the rows outside the groups;
-* the packed caption layout handles empty batches and captions of whole chunks.
+* the packed caption layout handles empty batches and captions of whole chunks;
+* the host arena of the offloaded state hands out 256-byte aligned, zeroed views, declines what does
+  not fit (the caller falls back to pinned blocks), unregisters on release, and hands out nothing
+  when the driver refuses the registration (a stand-in for the CUDA runtime calls; no GPU here).
 """
 import pytest
 import torch
@@ -91,3 +94,48 @@ def test_packed_caption_layout_edges():
     assert lay.pos.tolist()[:3] == [0, 1, 2] and lay.pos.tolist()[64] == 0
     empty = _layout([], 64, "cpu")
     assert empty.n_chunks == 0 and empty.grid_valid.numel() == 0
+
+
+class _FakeCudart:
+    """Stand-in for the driver's host registration (no GPU here): records the calls."""
+
+    def __init__(self, rc=0):
+        self.rc, self.registered, self.unregistered = rc, [], []
+
+    def cudaHostRegister(self, ptr, size, flags):
+        self.registered.append((ptr, size))
+        return self.rc
+
+    def cudaHostUnregister(self, ptr):
+        self.unregistered.append(ptr)
+        return 0
+
+
+def test_host_arena_carves_aligned_zeroed_views(monkeypatch):
+    import gc
+    from pan2_b200.training import engine as E
+    fake = _FakeCudart()
+    monkeypatch.setattr(E.torch.cuda, "cudart", lambda: fake)
+    arena = E._HostArena(1 << 16)
+    assert arena.registered and fake.registered == [(arena.buf.data_ptr(), 1 << 16)]
+    arena.buf.fill_(7)
+    a = arena.take(10, torch.int16)
+    b = arena.take(100, torch.float32)
+    assert a.dtype == torch.int16 and b.dtype == torch.float32
+    assert (a.data_ptr() - arena.buf.data_ptr()) % 256 == 0 and (b.data_ptr() - arena.buf.data_ptr()) % 256 == 0
+    assert b.data_ptr() >= a.data_ptr() + 20
+    assert a.abs().sum() == 0 and b.abs().sum() == 0
+    assert arena.take(1 << 16, torch.uint8) is None  # does not fit: the caller falls back
+    ptr = arena.buf.data_ptr()
+    del arena
+    gc.collect()
+    assert fake.unregistered == [ptr]
+
+
+def test_host_arena_refused_registration_hands_out_nothing(monkeypatch):
+    from pan2_b200.training import engine as E
+    fake = _FakeCudart(rc=1)
+    monkeypatch.setattr(E.torch.cuda, "cudart", lambda: fake)
+    arena = E._HostArena(4096)
+    assert not arena.registered and arena.buf is None
+    assert arena.take(4, torch.float32) is None
